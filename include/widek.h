@@ -1,0 +1,142 @@
+/*
+ * widek.h — C-ABI of libwidek, the sm_100a kernels behind wide_compiler's
+ * N-first wide primitives.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a device pointer on the CUDA device that is current
+ *     for the calling thread; `stream` is a cudaStream_t (NULL = legacy
+ *     default stream). Work is enqueued asynchronously on that stream.
+ *   - The library never allocates device memory on these paths; the caller
+ *     owns every buffer.
+ *   - Tensors are dense and row-major ("contiguous") unless a stride
+ *     argument says otherwise. `n` is always the number of fused models and
+ *     every N-first tensor is laid out [n, ...].
+ *   - dtype is one of WIDEK_F32 / WIDEK_BF16 / WIDEK_F16; arithmetic is
+ *     carried out in fp32 whatever the storage type.
+ *   - Return value: WIDEK_OK (0) or a negative WIDEK_ERR_* code. The message
+ *     of the last failure on the calling thread is available through
+ *     widek_last_error(). Nothing traps on the device: kernels that give up
+ *     on a bounded wait record a code that widek_device_error() returns.
+ *   - Entry points are re-entrant and may be called from several host
+ *     threads on different streams.
+ *
+ * Each function cites the reference (WideCompiler v0.6.0, Python) call site
+ * whose torch arithmetic it replaces, as path:line inside that project.
+ */
+#ifndef WIDEK_H_
+#define WIDEK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WIDEK_API __attribute__((visibility("default")))
+#else
+#define WIDEK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WIDEK_OK 0
+#define WIDEK_ERR_INVALID -1      /* bad shape, dtype, pointer or alignment */
+#define WIDEK_ERR_UNSUPPORTED -2  /* valid request this build does not serve */
+#define WIDEK_ERR_CUDA -3         /* a CUDA runtime call or launch failed */
+#define WIDEK_ERR_TIMEOUT -4      /* a bounded device-side wait ran out */
+
+#define WIDEK_F32 0
+#define WIDEK_BF16 1
+#define WIDEK_F16 2
+
+#define WIDEK_ACT_NONE 0
+#define WIDEK_ACT_RELU 1
+#define WIDEK_ACT_GELU 2 /* exact erf form, torch.nn.functional.gelu default */
+
+/* ---- library state ---------------------------------------------------- */
+
+/* ABI version (major*100 + minor). */
+WIDEK_API int widek_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len). Returns the code of that error (0 if none). */
+WIDEK_API int widek_last_error(char* buf, size_t len);
+
+/* Synchronizes the current device, returns the device-side error word in
+ * *code (0 = none) and clears it. Returns WIDEK_OK or WIDEK_ERR_CUDA. */
+WIDEK_API int widek_device_error(int* code);
+
+/* ---- WideLinear -------------------------------------------------------- */
+
+/* y[i] = act(x[i] @ w[i]^T + bias[i]) for every model i in [0, n).
+ *   x: [n, m, k], w: [n, o, k], bias: [n, o] or NULL, y: [n, m, o].
+ * bf16/f16 with k % 8 == 0 and 16-byte aligned pointers run on the tcgen05
+ * tensor-core kernel; every other case runs the CUDA-core kernel (fp32
+ * FFMA, used for fp32 so results match fp32 arithmetic with TF32 off).
+ * Replaces: wide_compiler/core/primitives/wide_linear.py:165
+ *           (einsum 'noi,nbi->nbo') and :168 (bias add). */
+WIDEK_API int widek_linear_fwd(const void* x, const void* w, const void* bias, void* y,
+                     int64_t n, int64_t m, int64_t k, int64_t o,
+                     int dtype, int act, void* stream);
+
+/* Same contraction forced onto the CUDA-core kernel (any dtype/alignment).
+ * Replaces the same call site; exposed for testing and small problems. */
+WIDEK_API int widek_linear_fwd_simt(const void* x, const void* w, const void* bias, void* y,
+                          int64_t n, int64_t m, int64_t k, int64_t o,
+                          int dtype, int act, void* stream);
+
+/* ---- WideLayerNorm ----------------------------------------------------- */
+
+/* Per-row LayerNorm over the last dim d with per-model affine:
+ *   x, y: [n, rows_per_model, d]; w, b: [n, d] (flat [n*d] in the module).
+ * Biased variance, statistics in fp32.
+ * Replaces: wide_compiler/core/primitives/wide_layernorm.py:62-65. */
+WIDEK_API int widek_layernorm_fwd(const void* x, const void* w, const void* b, void* y,
+                        int64_t n, int64_t rows_per_model, int64_t d,
+                        double eps, int dtype, void* stream);
+
+/* ---- layout boundary (pack / unpack) ----------------------------------- */
+
+/* dst[j, i, :] = src[i, j, :] for src [a, b, inner_bytes] (bytes).
+ * N-first [N, B, R] <-> channel-packed [B, N, R] in both directions.
+ * Replaces: wide_compiler/core/traced_wide.py:463-469 (unpack view +
+ * first-stage copy) and :531-532 (pack movedim+reshape). */
+WIDEK_API int widek_swap01(const void* src, void* dst, int64_t a, int64_t b,
+                 int64_t inner_bytes, void* stream);
+
+/* Stacks n separate [b, inner_bytes] buffers into dst [b, n, inner_bytes].
+ * srcs is a HOST array of n device pointers.
+ * Replaces: wide_compiler/core/ensemble_util.py:45 (torch.stack(dim=1)). */
+WIDEK_API int widek_pack(const void* const* srcs, int64_t n, void* dst, int64_t b,
+               int64_t inner_bytes, void* stream);
+
+/* ---- elementwise glue --------------------------------------------------- */
+
+#define WIDEK_UNARY_RELU 0
+#define WIDEK_UNARY_GELU 1
+#define WIDEK_UNARY_SIGMOID 2
+#define WIDEK_UNARY_TANH 3
+#define WIDEK_UNARY_SILU 4
+
+#define WIDEK_BINARY_ADD 0
+#define WIDEK_BINARY_MUL 1
+#define WIDEK_BINARY_SUB 2
+#define WIDEK_BINARY_DIV 3
+
+/* y = op(x) over numel elements.
+ * Replaces: wide_compiler/core/traced_wide.py:174-186 (FunctionalOp on
+ * F.relu / F.gelu / torch.sigmoid / torch.tanh / F.silu). */
+WIDEK_API int widek_unary(const void* x, void* y, int64_t numel, int op, int dtype,
+                void* stream);
+
+/* y = a op b over numel elements (same shape, dense).
+ * Replaces: wide_compiler/core/traced_wide.py:189-211 (BinaryOp add / mul /
+ * sub / div). */
+WIDEK_API int widek_binary(const void* a, const void* b, void* y, int64_t numel, int op,
+                 int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WIDEK_H_ */

@@ -1,0 +1,118 @@
+// CUDA-core grouped GEMM: y[i] = act(x[i] @ w[i]^T + bias[i]) for every model.
+//
+// Serves fp32 WideLinear (fp32 FFMA, so results keep fp32 products: the
+// reference's tolerance is defined with TF32 off) and any bf16/f16 problem the
+// tensor-core kernel cannot take (k not a multiple of 8, unaligned pointers).
+// Classic shared-memory tiling: a CTA computes a BM x BN output tile of one
+// model; each thread owns a TM x TN register tile.
+#include "common.cuh"
+
+namespace widek {
+namespace {
+
+template <typename T, int BM, int BN, int BK, int TM, int TN>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    gemm_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
+                     T* __restrict__ y, int M, int K, int O, int act) {
+    constexpr int NT = (BM / TM) * (BN / TN);
+    __shared__ float As[BK][BM + 4];
+    __shared__ float Bs[BK][BN + 4];
+    const int model = blockIdx.z;
+    const int m0 = blockIdx.y * BM;
+    const int o0 = blockIdx.x * BN;
+    x += (int64_t)model * M * K;
+    w += (int64_t)model * O * K;
+    y += (int64_t)model * M * O;
+    const int tid = threadIdx.x;
+    const int tx = tid % (BN / TN);
+    const int ty = tid / (BN / TN);
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+    for (int k0 = 0; k0 < K; k0 += BK) {
+        for (int i = tid; i < BM * BK; i += NT) {
+            const int r = i / BK, c = i % BK;
+            const int gm = m0 + r, gk = k0 + c;
+            As[c][r] = (gm < M && gk < K) ? to_f<T>(x[(int64_t)gm * K + gk]) : 0.f;
+        }
+        for (int i = tid; i < BN * BK; i += NT) {
+            const int r = i / BK, c = i % BK;
+            const int go = o0 + r, gk = k0 + c;
+            Bs[c][r] = (go < O && gk < K) ? to_f<T>(w[(int64_t)go * K + gk]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            float a[TM], b[TN];
+#pragma unroll
+            for (int i = 0; i < TM; ++i) a[i] = As[kk][ty * TM + i];
+#pragma unroll
+            for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tx * TN + j];
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int gm = m0 + ty * TM + i;
+        if (gm >= M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            const int go = o0 + tx * TN + j;
+            if (go >= O) continue;
+            float v = acc[i][j];
+            if (bias) v += to_f<T>(bias[(int64_t)model * O + go]);
+            y[(int64_t)gm * O + go] = from_f<T>(apply_act(v, act));
+        }
+    }
+}
+
+struct SimtLaunch {
+    const void *x, *w, *b;
+    void* y;
+    int64_t n, m, k, o;
+    int act;
+    cudaStream_t st;
+
+    template <typename T>
+    int run() {
+        if (n > 65535) return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): n=%lld > 65535", (long long)n);
+        if (m > 0x7fffffff || k > 0x7fffffff || o > 0x7fffffff)
+            return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): dimension exceeds int32");
+        const T* xp = static_cast<const T*>(x);
+        const T* wp = static_cast<const T*>(w);
+        const T* bp = static_cast<const T*>(b);
+        T* yp = static_cast<T*>(y);
+        if (m <= 32) {
+            dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 31) / 32), (unsigned)n);
+            gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act);
+        } else {
+            dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)n);
+            if (grid.y > 65535) return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): m too large");
+            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act);
+        }
+        return check_launch("widek_linear_fwd_simt");
+    }
+};
+
+}  // namespace
+}  // namespace widek
+
+extern "C" int widek_linear_fwd_simt(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m,
+                                     int64_t k, int64_t o, int dtype, int act, void* stream) {
+    using namespace widek;
+    if (n < 0 || m < 0 || k < 0 || o < 0) return set_error(WIDEK_ERR_INVALID, "linear: negative size");
+    if (act < WIDEK_ACT_NONE || act > WIDEK_ACT_GELU) return set_error(WIDEK_ERR_INVALID, "linear: bad activation %d", act);
+    if (n == 0 || m == 0 || o == 0) return WIDEK_OK;
+    if (!x && k > 0) return set_error(WIDEK_ERR_INVALID, "linear: null x");
+    if (!y) return set_error(WIDEK_ERR_INVALID, "linear: null y");
+    SimtLaunch L{x, w, bias, y, n, m, k, o, act, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}

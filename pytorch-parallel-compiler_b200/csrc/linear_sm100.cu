@@ -1,0 +1,321 @@
+// WideLinear forward on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+//   y[i] = act(x[i] @ w[i]^T + bias[i]),  x: [n, m, k], w: [n, o, k], y: [n, m, o]
+//
+// Design (one persistent CTA per SM, warp-specialised, 192 threads):
+//   warp 0      TMA producer: streams 128x64 tiles of x and BNx64 tiles of w
+//               (K-major, 128-byte swizzle) into a STAGES-deep smem ring.
+//               3-D tensor maps [n][rows][k] keep every tile inside one model
+//               (rows past m or o read as zero). w is streamed once
+//               (L2 evict-first), x is re-read by every column tile of its
+//               model (L2 evict-last).
+//   warp 1      allocates TMEM (2 x BN fp32 columns: a double-buffered
+//               accumulator); one elected thread issues tcgen05.mma
+//               (M=128, N=BN, K=16 per instruction) and tcgen05.commit to
+//               release smem stages and to publish finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld the 128 x BN accumulator (one row per
+//               thread), add the bias, apply the activation, convert, store.
+//               Runs while the MMA warp fills the other accumulator.
+// Tiles are ordered (model, column tile, row tile) with the row tile fastest,
+// so the CTAs that share a w tile run at the same time and w crosses HBM once.
+//
+// fp32 (and anything the tensor-core path cannot take) goes to the CUDA-core
+// kernel in gemm_simt.cu, so fp32 results keep fp32 products (TF32 off).
+#include "sm100_ptx.cuh"
+
+namespace widek {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+    static constexpr uint32_t A_BYTES = BM * BK * 2;
+    static constexpr uint32_t B_BYTES = BN * BK * 2;
+    static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
+    static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4 + 1) + 16;
+    static constexpr uint32_t TOTAL = 1024 + RING + BAR_BYTES;  // 1024: alignment slack
+};
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                     const T* __restrict__ bias, T* __restrict__ y, int n_models, int M, int K, int O, int act,
+                     int vec_store, int* err) {
+    using S = GemmSmem<BN, STAGES>;
+    constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+    constexpr uint32_t TMEM_COLS = 2 * BN;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * S::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;   // [2]
+    uint64_t* tempty = tfull + 2;       // [2]
+    uint64_t* done = tempty + 2;        // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int mt_count = (M + BM - 1) / BM;
+    const int nt_count = (O + BN - 1) / BN;
+    const int kb_count = (K + BK - 1) / BK;
+    const int tiles = n_models * mt_count * nt_count;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4 * 32);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------
+        // TMA producer
+        // ------------------------------------------------------------------
+        const uint64_t pol_x = l2_policy_evict_last();
+        const uint64_t pol_w = l2_policy_evict_first();
+        int s = 0;
+        uint32_t ph = 0;
+        int issued = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int mt = tile % mt_count;
+            const int rest = tile / mt_count;
+            const int nt = rest % nt_count;
+            const int model = rest / nt_count;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
+                    tma_load_3d(sA + s * S::A_BYTES, &tm_x, &full[s], kb * BK, mt * BM, model, pol_x);
+                    tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, nt * BN, model, pol_w);
+                }
+                __syncwarp();
+                ++issued;
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            // Let copies already in flight land before the CTA's smem is released.
+            const int inflight = issued < STAGES ? issued : STAGES;
+            for (int j = 1; j <= inflight; ++j) {
+                const int idx = issued - j;
+                const volatile int never = 0;
+                mbar_wait(&full[idx % STAGES], (uint32_t)((idx / STAGES) & 1), &never);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------
+        // MMA issuer (one elected thread issues, the warp tracks phases)
+        // ------------------------------------------------------------------
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * BN;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a0 = smem_addr(sA + s * S::A_BYTES);
+                    const uint32_t b0 = smem_addr(sB + s * S::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        // 16 elements = 32 bytes further along the swizzled row.
+                        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), IDESC,
+                                    (kb | k) != 0);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                __syncwarp();
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+            if (!ok) break;
+            if (lane == 0) umma_commit(&tfull[acc]);
+            __syncwarp();
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+        }
+        // Drain: every MMA this thread issued completes before TMEM is freed.
+        if (lane == 0) umma_commit(done);
+        __syncwarp();
+        const volatile int never = 0;
+        mbar_wait(done, 0, &never);
+    } else {
+        // ------------------------------------------------------------------
+        // Epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+        // ------------------------------------------------------------------
+        const int q = warp & 3;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int mt = tile % mt_count;
+            const int rest = tile / mt_count;
+            const int nt = rest % nt_count;
+            const int model = rest / nt_count;
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const int row = mt * BM + q * 32 + lane;
+            const bool row_ok = row < M;
+            T* yrow = y + ((int64_t)model * M + (row_ok ? row : 0)) * O;
+            const T* brow = bias ? bias + (int64_t)model * O : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                const int col0 = nt * BN + c;
+                if (col0 >= O) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c) + ((uint32_t)(q * 32) << 16), r);
+                tmem_ld_wait();
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                if (brow) {
+                    if (col0 + 32 <= O) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] += to_f<T>(brow[col0 + j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < O) v[j] += to_f<T>(brow[col0 + j]);
+                    }
+                }
+                if (act != WIDEK_ACT_NONE) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], act);
+                }
+                if (row_ok) {
+                    if (vec_store && col0 + 32 <= O) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) store16<T>(yrow + col0 + j, v + j);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < O) yrow[col0 + j] = from_f<T>(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+template <typename T>
+CUtensorMapDataType tmap_dtype();
+template <>
+CUtensorMapDataType tmap_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <>
+CUtensorMapDataType tmap_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+
+template <typename T, int BN, int STAGES>
+int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
+              cudaStream_t st) {
+    using S = GemmSmem<BN, STAGES>;
+    CUtensorMap tx, tw;
+    {
+        const uint64_t dims[3] = {(uint64_t)k, (uint64_t)m, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)m * k * 2};
+        const uint32_t box[3] = {BK, BM, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dtype<T>(), 3, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[3] = {(uint64_t)k, (uint64_t)o, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)o * k * 2};
+        const uint32_t box[3] = {BK, BN, 1};
+        int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    auto kern = linear_tc_kernel<T, BN, STAGES>;
+    static bool attr_done[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "linear: cannot reserve %u bytes of shared memory", S::TOTAL);
+        attr_done[dev] = true;
+    }
+    const int64_t tiles = n * ((m + BM - 1) / BM) * ((o + BN - 1) / BN);
+    const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
+    const int vec_store = (o % 8 == 0) && aligned16(y);
+    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
+                                           device_error_ptr());
+    return check_launch("widek_linear_fwd (tcgen05)");
+}
+
+template <typename T>
+int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
+              cudaStream_t st) {
+    if (o > 128) return launch_tc<T, 256, 4>(x, w, bias, y, n, m, k, o, act, st);
+    if (o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, st);
+    return launch_tc<T, 64, 8>(x, w, bias, y, n, m, k, o, act, st);
+}
+
+}  // namespace
+}  // namespace widek
+
+extern "C" int widek_linear_fwd(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m,
+                                int64_t k, int64_t o, int dtype, int act, void* stream) {
+    using namespace widek;
+    if (n < 0 || m < 0 || k < 0 || o < 0)
+        return set_error(WIDEK_ERR_INVALID, "linear: negative size");
+    if (act < WIDEK_ACT_NONE || act > WIDEK_ACT_GELU) return set_error(WIDEK_ERR_INVALID, "linear: bad activation %d", act);
+    if (n == 0 || m == 0 || o == 0) return WIDEK_OK;
+    const bool tc_ok = (dtype == WIDEK_BF16 || dtype == WIDEK_F16) && k > 0 && (k % 8 == 0) && aligned16(x) &&
+                       aligned16(w) && n <= 0x7fffffff && m <= 0x7fffffff && k <= 0x7fffffff &&
+                       o <= 0x7fffffff && n * ((m + 127) / 128) * ((o + 63) / 64) <= 0x7fffffff;
+    if (!tc_ok) return widek_linear_fwd_simt(x, w, bias, y, n, m, k, o, dtype, act, stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (dtype == WIDEK_BF16)
+        return linear_tc<__nv_bfloat16>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w,
+                                        (const __nv_bfloat16*)bias, (__nv_bfloat16*)y, n, m, k, o, act, st);
+    return linear_tc<__half>((const __half*)x, (const __half*)w, (const __half*)bias, (__half*)y, n, m, k, o, act,
+                             st);
+}

@@ -1,0 +1,143 @@
+"""Loader for libwidek.so, the sm_100a kernels behind every wide primitive.
+
+The library is a plain C-ABI shared object (``include/widek.h``); it is bound
+with ctypes so that no torch C++ extension has to be compiled against a
+particular torch build. Arguments are raw device pointers, sizes, dtype codes
+and the current CUDA stream.
+
+There is no fallback: if the library is missing or fails to load, every
+primitive forward raises. Build it with
+``python pytorch-parallel-compiler_b200/csrc/build.py`` (or
+``__graft_entry__.build()``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("WIDEK_LIB", os.path.join(_HERE, "_lib", "libwidek.so"))
+
+WIDEK_OK = 0
+WIDEK_ERR_INVALID = -1
+WIDEK_ERR_UNSUPPORTED = -2
+WIDEK_ERR_CUDA = -3
+WIDEK_ERR_TIMEOUT = -4
+
+F32, BF16, F16 = 0, 1, 2
+ACT_NONE, ACT_RELU, ACT_GELU = 0, 1, 2
+
+_DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_dbl = ctypes.c_double
+
+# name -> argtypes (restype is always c_int). Mirrors include/widek.h.
+SIGNATURES = {
+    "widek_version": [],
+    "widek_last_error": [ctypes.c_char_p, ctypes.c_size_t],
+    "widek_device_error": [ctypes.POINTER(ctypes.c_int)],
+    "widek_linear_fwd": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
+    "widek_linear_fwd_simt": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
+    "widek_layernorm_fwd": [_c_void_p] * 4 + [_i64] * 3 + [_dbl, _int, _c_void_p],
+    "widek_swap01": [_c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p],
+    "widek_pack": [ctypes.POINTER(_c_void_p), _i64, _c_void_p, _i64, _i64, _c_void_p],
+    "widek_unary": [_c_void_p, _c_void_p, _i64, _int, _int, _c_void_p],
+    "widek_binary": [_c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _c_void_p],
+}
+
+
+class WideKernelError(RuntimeError):
+    """A libwidek entry point reported a failure."""
+
+
+_lib: Optional[ctypes.CDLL] = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Loads libwidek.so once and binds every declared entry point."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"wide_compiler: native kernel library not found at {LIB_PATH}. "
+                "Build it with `python pytorch-parallel-compiler_b200/csrc/build.py`; "
+                "there is no non-CUDA implementation of the wide primitives.")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def lib() -> ctypes.CDLL:
+    return _lib if _lib is not None else load()
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    lib().widek_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc == WIDEK_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc in (WIDEK_ERR_INVALID, WIDEK_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise WideKernelError(msg)
+
+
+def device_error() -> int:
+    """Synchronizes, returns and clears the device-side error word."""
+    code = ctypes.c_int(0)
+    check(lib().widek_device_error(ctypes.byref(code)), "widek_device_error")
+    return code.value
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"wide_compiler kernels support float32/bfloat16/float16, got {t.dtype}") from None
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(*tensors: Optional[torch.Tensor], what: str) -> torch.device:
+    """Every tensor must be a CUDA tensor on one device; returns that device."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                f"{what}: wide_compiler runs the wide primitives only on CUDA (sm_100a) tensors; "
+                f"got a tensor on {t.device}. Move the module and its inputs to a B200 GPU.")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{what}: tensors on different devices ({dev} and {t.device})")
+    if dev is None:
+        raise RuntimeError(f"{what}: no tensor arguments")
+    return dev

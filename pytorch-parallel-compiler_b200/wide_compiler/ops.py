@@ -1,0 +1,156 @@
+"""Tensor-level wrappers over the libwidek C-ABI.
+
+Each function validates its tensors (CUDA, one device, supported dtype),
+makes them dense, allocates the output with torch's caching allocator, and
+launches the kernel on torch's current stream. These are the only places the
+wide primitives reach device code; nothing here computes on the host.
+"""
+from __future__ import annotations
+
+import contextlib
+import math
+from typing import List, Optional, Sequence
+
+import ctypes
+import torch
+from torch import Tensor
+
+from . import _native as N
+
+ACT_NONE, ACT_RELU, ACT_GELU = N.ACT_NONE, N.ACT_RELU, N.ACT_GELU
+
+UNARY_CODES = {"relu": 0, "gelu": 1, "sigmoid": 2, "tanh": 3, "silu": 4}
+BINARY_CODES = {"add": 0, "mul": 1, "sub": 2, "div": 3}
+
+
+def _guard(dev: torch.device):
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
+
+
+def _dense(t: Tensor) -> Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _same_dtype(what: str, ref: Tensor, *others: Optional[Tensor]) -> None:
+    for o in others:
+        if o is not None and o.dtype != ref.dtype:
+            raise TypeError(f"{what}: dtype mismatch ({ref.dtype} vs {o.dtype})")
+
+
+# ---------------------------------------------------------------------------
+# WideLinear
+# ---------------------------------------------------------------------------
+
+def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NONE,
+           force_simt: bool = False) -> Tensor:
+    """y[i] = act(x[i] @ weight[i]^T + bias[i]).
+
+    x: [N, ..., K] (any batch dims), weight: [N, O, K], bias: [N, O] or None.
+    Returns [N, ..., O].
+    """
+    dev = N.require_cuda(x, weight, bias, what="WideLinear")
+    _same_dtype("WideLinear", weight, x, bias)
+    n, o, k = weight.shape
+    if x.shape[0] != n or x.shape[-1] != k:
+        raise ValueError(f"WideLinear: input {tuple(x.shape)} does not match weight {tuple(weight.shape)}")
+    batch = x.shape[1:-1]
+    xd = _dense(x)
+    m = math.prod(batch)
+    wd = _dense(weight)
+    bd = _dense(bias) if bias is not None else None
+    y = torch.empty((n, *batch, o), device=dev, dtype=weight.dtype)
+    fn = N.lib().widek_linear_fwd_simt if force_simt else N.lib().widek_linear_fwd
+    with _guard(dev):
+        rc = fn(xd.data_ptr(), wd.data_ptr(), N.ptr(bd), y.data_ptr(), n, m, k, o,
+                N.dtype_code(weight), act, N.stream_ptr(dev))
+    N.check(rc, "widek_linear_fwd")
+    return y
+
+
+# ---------------------------------------------------------------------------
+# WideLayerNorm
+# ---------------------------------------------------------------------------
+
+def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: float) -> Tensor:
+    """LayerNorm over the last dim with per-model affine (weight/bias flat [n*d])."""
+    dev = N.require_cuda(x, weight, bias, what="WideLayerNorm")
+    _same_dtype("WideLayerNorm", x, weight, bias)
+    if x.shape[0] != n or x.shape[-1] != d:
+        raise ValueError(f"WideLayerNorm: input {tuple(x.shape)} is not [N={n}, ..., D={d}]")
+    xd = _dense(x)
+    rows = xd.numel() // (n * d) if n * d > 0 else 0
+    y = torch.empty_like(xd)
+    with _guard(dev):
+        rc = N.lib().widek_layernorm_fwd(xd.data_ptr(), _dense(weight).data_ptr(), _dense(bias).data_ptr(),
+                                         y.data_ptr(), n, rows, d, float(eps), N.dtype_code(x),
+                                         N.stream_ptr(dev))
+    N.check(rc, "widek_layernorm_fwd")
+    return y
+
+
+# ---------------------------------------------------------------------------
+# Layout boundary
+# ---------------------------------------------------------------------------
+
+def swap01(x: Tensor) -> Tensor:
+    """[A, B, *rest] -> [B, A, *rest] as one dense copy (rows of prod(rest))."""
+    dev = N.require_cuda(x, what="swap01")
+    xd = _dense(x)
+    a, b = xd.shape[0], xd.shape[1]
+    rest = xd.shape[2:]
+    y = torch.empty((b, a, *rest), device=dev, dtype=x.dtype)
+    inner = xd.numel() // max(1, a * b) * xd.element_size() if a * b > 0 else 0
+    with _guard(dev):
+        rc = N.lib().widek_swap01(xd.data_ptr(), y.data_ptr(), a, b, inner, N.stream_ptr(dev))
+    N.check(rc, "widek_swap01")
+    return y
+
+
+def pack(inputs: Sequence[Tensor]) -> Tensor:
+    """Stacks N tensors [B, *F] into [B, N, *F] (one kernel, N source pointers)."""
+    dev = N.require_cuda(*inputs, what="pack")
+    t0 = inputs[0]
+    for t in inputs[1:]:
+        if t.shape != t0.shape or t.dtype != t0.dtype:
+            raise ValueError("pack: all inputs must share shape and dtype")
+    dense = [_dense(t) for t in inputs]
+    b = t0.shape[0]
+    n = len(dense)
+    out = torch.empty((b, n, *t0.shape[1:]), device=dev, dtype=t0.dtype)
+    inner = (t0.numel() // b) * t0.element_size() if b > 0 else 0
+    arr = (ctypes.c_void_p * n)(*[t.data_ptr() for t in dense])
+    with _guard(dev):
+        rc = N.lib().widek_pack(arr, n, out.data_ptr(), b, inner, N.stream_ptr(dev))
+    N.check(rc, "widek_pack")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Elementwise glue
+# ---------------------------------------------------------------------------
+
+def unary(x: Tensor, op: str) -> Tensor:
+    dev = N.require_cuda(x, what=f"unary {op}")
+    xd = _dense(x)
+    y = torch.empty_like(xd)
+    with _guard(dev):
+        rc = N.lib().widek_unary(xd.data_ptr(), y.data_ptr(), xd.numel(), UNARY_CODES[op], N.dtype_code(x),
+                                 N.stream_ptr(dev))
+    N.check(rc, f"widek_unary({op})")
+    return y
+
+
+def binary(a: Tensor, b: Tensor, op: str) -> Tensor:
+    dev = N.require_cuda(a, b, what=f"binary {op}")
+    _same_dtype(f"binary {op}", a, b)
+    if a.shape != b.shape:
+        raise ValueError(f"binary {op}: shapes differ ({tuple(a.shape)} vs {tuple(b.shape)})")
+    ad, bd = _dense(a), _dense(b)
+    y = torch.empty_like(ad)
+    with _guard(dev):
+        rc = N.lib().widek_binary(ad.data_ptr(), bd.data_ptr(), y.data_ptr(), ad.numel(), BINARY_CODES[op],
+                                  N.dtype_code(a), N.stream_ptr(dev))
+    N.check(rc, f"widek_binary({op})")
+    return y

@@ -1,0 +1,179 @@
+"""Host-side logic that needs no GPU: package surface, registry, config,
+parameter layouts (state_dict compatibility with the reference fixtures),
+FX graph construction, and the loud failure on non-CUDA tensors."""
+import dataclasses
+
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import wide_compiler as wc
+from conftest import golden_names, load_golden
+from wide_compiler.core import primitives as P
+
+
+REFERENCE_ALL = ['compile', 'WideBuilder', 'pack', 'unpack', 'WideConfig', 'get_default_config',
+                 'set_default_config', 'register', 'unregister', 'get_registry', 'list_registered',
+                 'TracedWideModel', 'FunctionalOp', 'BinaryOp', 'print_trace', 'pack_inputs', 'unpack_outputs',
+                 'WideLinear', 'WideConv1d', 'WideConv2d', 'WideConv3d', 'WideBatchNorm1d', 'WideBatchNorm2d',
+                 'WideLayerNorm', 'WideGroupNorm', 'WideInstanceNorm1d', 'WideInstanceNorm2d', 'WideEmbedding',
+                 'WideAttention', 'WideGRU', 'WideLSTM']
+
+
+def test_public_surface_matches_reference():
+    for name in REFERENCE_ALL:
+        assert hasattr(wc, name), name
+    assert wc.benchmark_primitive is None
+
+
+def test_registry_has_all_builtins_and_api():
+    assert set(wc.list_registered()) == set(P.BUILTIN_PRIMITIVES)
+    reg = wc.get_registry()
+    assert reg.get_class('Linear') is wc.WideLinear
+    assert 'GRU' in reg
+
+    class NoFrom(nn.Module):
+        pass
+
+    with pytest.raises(TypeError):
+        wc.register('Bogus', NoFrom)
+
+    @wc.register('MyThing')
+    class WideThing(nn.Module):
+        @classmethod
+        def from_modules(cls, modules):
+            return cls()
+
+    assert reg.build([nn.Identity()]) is None
+    assert 'MyThing' in wc.list_registered()
+    wc.unregister('MyThing')
+    assert 'MyThing' not in wc.list_registered()
+
+
+def test_config_presets_and_debug_field():
+    c = wc.WideConfig()
+    assert c.debug is False
+    d = wc.WideConfig.debug()
+    assert d.debug is True and d.validate is True and d.compile is False
+    assert dataclasses.replace(c, debug=True).debug is True
+    with pytest.raises(ValueError):
+        wc.WideConfig(compile_mode='bogus')
+    assert wc.WideConfig.fast().compile is True
+
+
+def _build_from_state(g):
+    k, m, s = g['kind'], g['meta'], g['state']
+    if k == 'linear':
+        mod = wc.WideLinear(m['n'], m['in'], m['out'], bias=m['bias'])
+    elif k == 'layernorm':
+        mod = wc.WideLayerNorm(m['n'], m['d'], m['eps'])
+    elif k == 'batchnorm':
+        cls = wc.WideBatchNorm2d if m['dims'] == 5 else wc.WideBatchNorm1d
+        mod = cls(m['n'], m['c'])
+    elif k == 'groupnorm':
+        mod = wc.WideGroupNorm(m['n'], m['groups'], m['c'], affine=m['affine'])
+    elif k == 'instancenorm':
+        cls = wc.WideInstanceNorm2d if m['dims'] == 5 else wc.WideInstanceNorm1d
+        mod = cls(m['n'], m['c'], affine=m['affine'])
+    elif k == 'embedding':
+        mod = wc.WideEmbedding(m['n'], m['v'], m['d'])
+    elif k == 'conv':
+        if m['dims'] == 2:
+            mod = wc.WideConv2d(m['n'], m['cin'], m['cout'], m['k'], m['s'], m['p'], m['d'], bias=m['bias'],
+                                strategy='grouped')
+        elif m['dims'] == 1:
+            mod = wc.WideConv1d(m['n'], m['cin'], m['cout'], m['k'], m['s'], m['p'], m['d'], bias=m['bias'],
+                                strategy=P.Conv1dStrategy.GROUPED)
+        else:
+            mod = wc.WideConv3d(m['n'], m['cin'], m['cout'], m['k'], m['s'], m['p'], m['d'], bias=m['bias'])
+    elif k == 'attention':
+        mod = wc.WideAttention(m['n'], m['d'], m['heads'])
+    elif k == 'gru':
+        mod = wc.WideGRU(m['n'], m['i'], m['h'])
+    elif k == 'lstm':
+        mod = wc.WideLSTM(m['n'], m['i'], m['h'])
+    else:
+        return None
+    mod.load_state_dict(s, strict=True)
+    return mod
+
+
+@pytest.mark.parametrize("name", [n for n in golden_names() if not n.startswith('traced')])
+def test_reference_state_dict_loads_strictly(name):
+    """Parameter names/shapes match the reference: its state_dict loads with strict=True."""
+    assert _build_from_state(load_golden(name)) is not None
+
+
+def test_from_modules_layouts():
+    lin = [nn.Linear(6, 10) for _ in range(3)]
+    w = wc.WideLinear.from_modules(lin)
+    assert w.weight.shape == (3, 10, 6)
+    torch.testing.assert_close(w.weight[1], lin[1].weight)
+    lstms = [nn.LSTM(4, 5, batch_first=True) for _ in range(3)]
+    wl = wc.WideLSTM.from_modules(lstms)
+    assert wl.weight_ih.shape == (60, 12)
+    bih, bhh = wl._blocks()
+    torch.testing.assert_close(bih[2], lstms[2].weight_ih_l0)
+    torch.testing.assert_close(bhh[0], lstms[0].weight_hh_l0)
+    assert float(wl.weight_hh[0:20, 5:15].abs().sum()) == 0.0
+    mha = [nn.MultiheadAttention(8, 2, batch_first=True) for _ in range(2)]
+    wa = wc.WideAttention.from_modules(mha)
+    torch.testing.assert_close(wa.kv_weight[1], mha[1].in_proj_weight[8:])
+    wqkv, bqkv = wa._fused_qkv()
+    torch.testing.assert_close(wqkv[0], mha[0].in_proj_weight)
+
+
+def test_lstm_block_cache_invalidates_on_update():
+    wl = wc.WideLSTM(2, 3, 4)
+    a, _ = wl._blocks()
+    with torch.no_grad():
+        wl.weight_ih[0, 0] += 1.0
+    b, _ = wl._blocks()
+    assert float(b[0, 0, 0] - a[0, 0, 0]) == pytest.approx(1.0)
+
+
+class _MLP(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.fc1 = nn.Linear(8, 16)
+        self.fc2 = nn.Linear(16, 8)
+
+    def forward(self, x):
+        return self.fc2(F.relu(self.fc1(x)))
+
+
+def test_traced_model_structure_cpu():
+    models = [_MLP() for _ in range(4)]
+    wide = wc.TracedWideModel.from_models(models, torch.randn(2, 8))
+    kinds = [type(wide.stages[k]).__name__ for k in wide.stages]
+    assert kinds == ['WideLinear', 'FunctionalOp', 'WideLinear']
+    assert wide.stages['relu'].unary == 'relu'
+    assert 'Total:' in wide.summary()
+
+
+def test_compile_argument_errors():
+    with pytest.raises(ValueError):
+        wc.compile(_MLP(), torch.randn(2, 8))          # n missing
+    with pytest.raises(ValueError):
+        wc.compile([], torch.randn(2, 8))
+    with pytest.raises(ValueError):
+        wc.compile([_MLP()], None)
+
+
+def test_cpu_tensors_fail_loudly():
+    w = wc.WideLinear(2, 4, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        w(torch.randn(2, 3, 4))
+    ln = wc.WideLayerNorm(2, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ln(torch.randn(2, 3, 4))
+
+
+def test_unpack_outputs_views_and_errors():
+    out = torch.arange(2 * 12).view(2, 12).float()
+    parts = wc.unpack(out, 3)
+    assert len(parts) == 3 and parts[1].shape == (2, 4)
+    assert parts[1].data_ptr() == out.data_ptr() + 4 * 4
+    with pytest.raises(ValueError):
+        wc.unpack(out, 5)

@@ -1,0 +1,93 @@
+"""The oracle (oracle/wide_oracle.py) against the golden fixtures produced by
+running the reference implementation itself (tests/golden/make_golden.py).
+This pins the oracle that the GPU parity tests then use at larger sizes."""
+import pytest
+import torch
+
+from conftest import golden_names, load_golden
+from oracle import wide_oracle as O
+
+TOL = dict(rtol=1e-5, atol=1e-5)
+
+
+def _close(a, b, **tol):
+    torch.testing.assert_close(a.to(torch.float64), b.to(torch.float64), **(tol or TOL))
+
+
+def oracle_eval(g):
+    """Runs the oracle for one fixture; returns {output name: tensor}."""
+    k, m, s, inp = g['kind'], g['meta'], g['state'], g['inputs']
+    if k == 'linear':
+        return {'y': O.linear(inp['x'], s['weight'], s.get('bias'))}
+    if k == 'layernorm':
+        return {'y': O.layernorm(inp['x'], s['weight'], s['bias'], m['n'], m['d'], m['eps'])}
+    if k == 'batchnorm':
+        y, rm, rv = O.batchnorm(inp['x'], m['n'], m['c'], s['op.weight'], s['op.bias'], s['op.running_mean'],
+                                s['op.running_var'], use_batch_stats=m['train'])
+        out = {'y': y}
+        if m['train']:
+            out.update(running_mean=rm, running_var=rv)
+        return out
+    if k == 'groupnorm':
+        return {'y': O.groupnorm(inp['x'], m['n'], m['groups'], s.get('norm.weight'), s.get('norm.bias'), 1e-5)}
+    if k == 'instancenorm':
+        return {'y': O.groupnorm(inp['x'], m['n'], m['c'], s.get('norm.weight'), s.get('norm.bias'), 1e-5)}
+    if k == 'embedding':
+        return {'y': O.embedding(inp['idx'], s['weight'])}
+    if k == 'conv':
+        pre = {1: 'op', 2: 'grouped_conv', 3: 'conv'}[m['dims']]
+        nd = m['dims']
+        return {'y': O.conv_nd(inp['x'], s[f'{pre}.weight'], s.get(f'{pre}.bias'), m['n'], (m['s'],) * nd,
+                               (m['p'],) * nd, (m['d'],) * nd)}
+    if k == 'attention':
+        q = inp['q']
+        kk = inp['k'] if inp['k'] is not None else q
+        v = inp['v'] if inp['v'] is not None else kk
+        return {'y': O.attention(q, kk, v, s['q_weight'], s['kv_weight'], s.get('q_bias'), s.get('kv_bias'),
+                                 s['out_weight'], s.get('out_bias'), m['heads'], inp['mask'], m['causal'])}
+    if k == 'gru':
+        y, hn = O.gru(inp['x'], inp['h0'], s['weight_ih'], s['weight_hh'], s.get('bias_ih'), s.get('bias_hh'))
+        return {'y': y, 'h_n': hn}
+    if k == 'lstm':
+        n = m['n']
+        wih, whh = O.lstm_blocks(s['weight_ih'], s['weight_hh'], n)
+        bih = s['bias_ih'].view(n, -1) if 'bias_ih' in s else None
+        bhh = s['bias_hh'].view(n, -1) if 'bias_hh' in s else None
+        y, (hn, cn) = O.lstm(inp['x'], inp['h0'], inp['c0'], wih, whh, bih, bhh)
+        return {'y': y, 'h_n': hn, 'c_n': cn}
+    if k == 'traced':
+        n = m['n']
+        if m['model'] == 'MLP':
+            st = lambda key: torch.stack([s[f'm{i}.{key}'] for i in range(n)])
+            return {'y': O.mlp2(inp['packed'], n, st('fc1.weight'), st('fc1.bias'), st('fc2.weight'),
+                                st('fc2.bias'))}
+        if m['model'] == 'ResBlock':
+            cat = lambda key: torch.cat([s[f'm{i}.{key}'] for i in range(n)])
+            bn = lambda p: {f: cat(f'{p}.{f}') for f in ('weight', 'bias', 'running_mean', 'running_var')}
+            x = O.packed_to_nfirst(inp['packed'], n)
+            y = O.resblock(x, n, cat('conv1.weight'), cat('conv1.bias'), bn('bn1'), cat('conv2.weight'),
+                           cat('conv2.bias'), bn('bn2'))
+            return {'y': O.nfirst_to_packed(y)}
+    raise KeyError(k)
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_oracle_matches_reference_fixture(name):
+    g = load_golden(name)
+    got = oracle_eval(g)
+    for key, val in got.items():
+        _close(val, g['outputs'][key])
+
+
+def test_fixture_set_covers_every_primitive():
+    kinds = {load_golden(n)['kind'] for n in golden_names()}
+    assert {'linear', 'layernorm', 'batchnorm', 'groupnorm', 'instancenorm', 'embedding', 'conv', 'attention',
+            'gru', 'lstm', 'traced'} <= kinds
+
+
+def test_pack_roundtrip_oracle():
+    g = load_golden('traced_mlp')
+    packed = O.pack_inputs(g['inputs']['inputs'])
+    torch.testing.assert_close(packed, g['inputs']['packed'])
+    nf = O.packed_to_nfirst(packed, g['meta']['n'])
+    torch.testing.assert_close(O.nfirst_to_packed(nf), packed)
