@@ -45,13 +45,21 @@ METRIC = "wide-forward samples/s (N·B/s) at 1/2/4/8 B200; % of TC/HBM roofline"
 N_MODELS, B_ROWS, IN_F, OUT_F = 64, 256, 1024, 4096
 DTYPE = torch.bfloat16
 ELEM = 2
-# Compulsory HBM bytes per launch: W + x + y + bias, each touched once.
-ALG_BYTES = ELEM * (N_MODELS * OUT_F * IN_F + N_MODELS * B_ROWS * IN_F + N_MODELS * B_ROWS * OUT_F
-                    + N_MODELS * OUT_F)
-ALG_FLOPS = 2 * N_MODELS * B_ROWS * IN_F * OUT_F
+
+
+def alg_bytes(n):
+    """Compulsory HBM bytes per launch: W + x + y + bias, each touched once."""
+    return ELEM * (n * OUT_F * IN_F + n * B_ROWS * IN_F + n * B_ROWS * OUT_F + n * OUT_F)
+
+
+def alg_flops(n):
+    return 2 * n * B_ROWS * IN_F * OUT_F
+
+
+ALG_BYTES = alg_bytes(N_MODELS)
 # DRAM traffic (read + write bytes) per launch of linear_tc_kernel measured by
-# ncu; see profiles/linear_tc_cfg2.md (None until captured).
-NCU_TRAFFIC_BYTES = None
+# ncu on a 16-model capture scaled to 64 models; see profiles/linear_tc_cfg2.md.
+NCU_TRAFFIC_BYTES = 593_080_000  # 148.27 MB for 16 models x 64/16
 
 
 def peaks():
@@ -278,7 +286,7 @@ def run_b200(args):
     if rank == 0:
         samples = N_MODELS * B_ROWS * world
         peak, peak_kind = peaks()
-        achieved = ALG_BYTES / (ms * 1e-3) / 1e9
+        achieved = alg_bytes(N_MODELS) / (ms * 1e-3) / 1e9
         line = {
             "metric": METRIC,
             "value": samples / (ms_max * 1e-3),
@@ -307,8 +315,8 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_BYTES,
-                         "algorithmic_bytes": ALG_BYTES,
-                         "tflops": ALG_FLOPS / (ms * 1e-3) / 1e12},
+                         "algorithmic_bytes": alg_bytes(N_MODELS),
+                         "tflops": alg_flops(N_MODELS) / (ms * 1e-3) / 1e12},
             "clocks": clk,
             "device_error": dev_err,
         }
@@ -322,6 +330,7 @@ def run_b200(args):
 
 
 def main():
+    global N_MODELS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -331,9 +340,12 @@ def main():
     ap.add_argument("--gather", action="store_true", help="include the optional output all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--models", type=int, default=N_MODELS,
+                    help="models per GPU (default: the cfg2 value 64; smaller only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    N_MODELS = args.models
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -135,6 +135,60 @@ WIDEK_API int widek_unary(const void* x, void* y, int64_t numel, int op, int dty
 WIDEK_API int widek_binary(const void* a, const void* b, void* y, int64_t numel, int op,
                  int dtype, void* stream);
 
+/* ---- WideBatchNorm1d / WideBatchNorm2d ---------------------------------- */
+
+/* Normalization with given statistics (eval mode, running stats):
+ *   x, y: [n, batch, c, l] (l = spatial size, 1 for [n, batch, c]);
+ *   weight, bias (nullable), mean, var: flat [n*c].
+ * y = (x - mean) / sqrt(var + eps) * weight + bias per (model, channel).
+ * Replaces: wide_compiler/core/primitives/wide_batchnorm_2d.py:53-72 and
+ *           wide_batchnorm_1d.py:53-73 (permute copies + nn.BatchNorm(N*C)). */
+WIDEK_API int widek_batchnorm_fwd(const void* x, void* y, const void* weight, const void* bias,
+                                  const void* mean, const void* var, int64_t n, int64_t batch,
+                                  int64_t c, int64_t l, double eps, int dtype, void* stream);
+
+/* Bytes of workspace widek_batchnorm_train_fwd needs for this shape on the
+ * current device (fp64 partial sums). */
+WIDEK_API size_t widek_batchnorm_train_workspace(int64_t n, int64_t batch, int64_t c, int64_t l);
+
+/* Training-mode normalization with batch statistics per (model, channel)
+ * over batch*l elements; updates running_mean / running_var in place
+ * (momentum; unbiased variance) when given, writes save_mean / save_invstd
+ * (fp32 [n*c], nullable). `workspace` is caller-provided device memory of at
+ * least widek_batchnorm_train_workspace() bytes.
+ * Replaces: the same call sites in training mode (nn.BatchNorm batch
+ * statistics and running-stat update). */
+WIDEK_API int widek_batchnorm_train_fwd(const void* x, void* y, const void* weight, const void* bias,
+                                        void* running_mean, void* running_var, float* save_mean,
+                                        float* save_invstd, void* workspace, size_t workspace_bytes,
+                                        int64_t n, int64_t batch, int64_t c, int64_t l,
+                                        double momentum, double eps, int dtype, void* stream);
+
+/* ---- WideGroupNorm / WideInstanceNorm1d/2d -------------------------------- */
+
+/* Statistics per (model, sample, group) over the group's (c/groups)*l
+ * elements, per-channel affine (weight/bias flat [n*c], nullable).
+ *   x, y: [n, batch, c, l]. row_mean / row_var (fp32 [n*batch*groups],
+ * nullable together) receive each group's mean and biased variance.
+ * InstanceNorm is groups == c.
+ * Replaces: wide_compiler/core/primitives/wide_groupnorm.py:90-117 and
+ *           wide_instancenorm.py:89-108, :222-240. */
+WIDEK_API int widek_groupnorm_fwd(const void* x, void* y, const void* weight, const void* bias,
+                                  float* row_mean, float* row_var, int64_t n, int64_t batch,
+                                  int64_t c, int64_t l, int64_t groups, double eps, int dtype,
+                                  void* stream);
+
+/* ---- WideEmbedding ------------------------------------------------------ */
+
+/* out[i, j, :] = weight[i, idx[j], :] for every model i; idx: int64 [num_idx]
+ * shared by all models; weight: [n, v, d]; out: [n, num_idx, d]. Negative
+ * indices wrap once; indices outside [-v, v) give a zero row and set the
+ * device error word.
+ * Replaces: wide_compiler/core/primitives/wide_embedding.py:85-99
+ *           (weight[:, idx]). */
+WIDEK_API int widek_embedding_fwd(const int64_t* idx, const void* weight, void* out, int64_t n,
+                                  int64_t num_idx, int64_t v, int64_t d, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

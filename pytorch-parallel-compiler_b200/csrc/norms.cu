@@ -1,0 +1,489 @@
+// Wide BatchNorm / GroupNorm / InstanceNorm forwards and the wide embedding
+// gather, all on the N-first layout (no channel-packing copies).
+//
+// Layout: x, y are [n, batch, c, l] (l = product of spatial dims, 1 for
+// [n, batch, c]); per-channel tensors (weight, bias, running stats) are flat
+// [n * c], channel index n_i * c + c_i, exactly the inner nn.BatchNorm(N*C) /
+// nn.GroupNorm(N*G, N*C) parameter order of the reference.
+#include "common.cuh"
+
+namespace widek {
+namespace {
+
+// ---------------------------------------------------------------------------
+// BatchNorm with given statistics (eval mode): y = x * scale + shift per
+// channel. One pass; 16-byte vectors when rows (length l) allow.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void bn_scale_shift(int64_t ch, const T* w, const T* b, const T* mean, const T* var,
+                                               float eps, float& scale, float& shift) {
+    const float m = to_f<T>(mean[ch]);
+    const float r = rsqrtf(to_f<T>(var[ch]) + eps);
+    const float g = w ? to_f<T>(w[ch]) : 1.f;
+    const float bb = b ? to_f<T>(b[ch]) : 0.f;
+    scale = g * r;
+    shift = bb - m * scale;
+}
+
+template <typename T, bool VEC>
+__global__ void bn_eval_kernel(const T* __restrict__ x, T* __restrict__ y, const T* __restrict__ w,
+                               const T* __restrict__ b, const T* __restrict__ rm, const T* __restrict__ rv,
+                               int64_t total, int64_t batch, int64_t c, int64_t l, float eps) {
+    constexpr int V = VEC ? 16 / sizeof(T) : 1;
+    const int64_t nvec = total / V;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+        const int64_t e = i * V;
+        const int64_t row = e / l;                 // (n, b, c) row
+        const int64_t ci = row % c;
+        const int64_t ni = row / (batch * c);
+        float sc, sh;
+        bn_scale_shift<T>(ni * c + ci, w, b, rm, rv, eps, sc, sh);
+        if (VEC) {
+            float v[V];
+            load16<T>(x + e, v);
+#pragma unroll
+            for (int j = 0; j < V; ++j) v[j] = v[j] * sc + sh;
+            store16<T>(y + e, v);
+        } else {
+            y[e] = from_f<T>(to_f<T>(x[e]) * sc + sh);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// BatchNorm with batch statistics (train mode), two launches:
+//   1. partial sums: grid (channels, chunks); each CTA reduces one chunk of the
+//      channel's batch*l elements to (sum, sum of squares) of x - shift, with
+//      the channel's first element as shift, into the workspace (fp64).
+//   2. finalize + normalize: grid (channels, chunks); each CTA combines its
+//      channel's partials, normalizes its chunk; CTA 0 of a channel updates
+//      the running statistics and writes the saved mean / inverse std.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T chan_elem(const T* x, int64_t ni, int64_t ci, int64_t j, int64_t batch, int64_t c,
+                                       int64_t l) {
+    const int64_t bi = j / l;
+    const int64_t li = j - bi * l;
+    return x[((ni * batch + bi) * c + ci) * l + li];
+}
+
+template <int NT>
+__device__ __forceinline__ void block_sum2(double& a, double& b) {
+    __shared__ double sa[NT / 32], sb[NT / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { sa[w] = a; sb[w] = b; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double ta = 0, tb = 0;
+        for (int i = 0; i < NT / 32; ++i) { ta += sa[i]; tb += sb[i]; }
+        sa[0] = ta;
+        sb[0] = tb;
+    }
+    __syncthreads();
+    a = sa[0];
+    b = sb[0];
+}
+
+constexpr int kBnThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kBnThreads) bn_partial_kernel(const T* __restrict__ x, double* __restrict__ ws,
+                                                                int64_t batch, int64_t c, int64_t l, int chunks) {
+    const int64_t ch = blockIdx.x;
+    const int k = blockIdx.y;
+    const int64_t ni = ch / c, ci = ch % c;
+    const int64_t cnt = batch * l;
+    const int64_t per = (cnt + chunks - 1) / chunks;
+    const int64_t j0 = (int64_t)k * per;
+    const int64_t j1 = j0 + per < cnt ? j0 + per : cnt;
+    const float shift = to_f<T>(chan_elem(x, ni, ci, 0, batch, c, l));
+    float s1 = 0.f, s2 = 0.f;
+    for (int64_t j = j0 + threadIdx.x; j < j1; j += kBnThreads) {
+        const float d = to_f<T>(chan_elem(x, ni, ci, j, batch, c, l)) - shift;
+        s1 += d;
+        s2 += d * d;
+    }
+    double a = s1, b = s2;
+    block_sum2<kBnThreads>(a, b);
+    if (threadIdx.x == 0) {
+        ws[(ch * chunks + k) * 2 + 0] = a;
+        ws[(ch * chunks + k) * 2 + 1] = b;
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kBnThreads) bn_apply_kernel(
+    const T* __restrict__ x, T* __restrict__ y, const T* __restrict__ w, const T* __restrict__ b,
+    T* __restrict__ rm, T* __restrict__ rv, float* __restrict__ save_mean, float* __restrict__ save_invstd,
+    const double* __restrict__ ws, int64_t batch, int64_t c, int64_t l, int chunks, float momentum, float eps) {
+    const int64_t ch = blockIdx.x;
+    const int k = blockIdx.y;
+    const int64_t ni = ch / c, ci = ch % c;
+    const int64_t cnt = batch * l;
+    double s1 = 0, s2 = 0;
+    for (int i = 0; i < chunks; ++i) {
+        s1 += ws[(ch * chunks + i) * 2 + 0];
+        s2 += ws[(ch * chunks + i) * 2 + 1];
+    }
+    const double shift = (double)to_f<T>(chan_elem(x, ni, ci, 0, batch, c, l));
+    const double dm = s1 / (double)cnt;
+    double var = s2 / (double)cnt - dm * dm;
+    if (var < 0) var = 0;
+    const float mean = (float)(shift + dm);
+    const float invstd = (float)(1.0 / sqrt(var + (double)eps));
+    const float g = w ? to_f<T>(w[ch]) : 1.f;
+    const float bb = b ? to_f<T>(b[ch]) : 0.f;
+    const float sc = g * invstd;
+    const float sh = bb - mean * sc;
+    const int64_t per = (cnt + chunks - 1) / chunks;
+    const int64_t j0 = (int64_t)k * per;
+    const int64_t j1 = j0 + per < cnt ? j0 + per : cnt;
+    for (int64_t j = j0 + threadIdx.x; j < j1; j += kBnThreads) {
+        const int64_t bi = j / l;
+        const int64_t li = j - bi * l;
+        const int64_t off = ((ni * batch + bi) * c + ci) * l + li;
+        y[off] = from_f<T>(to_f<T>(x[off]) * sc + sh);
+    }
+    if (k == 0 && threadIdx.x == 0) {
+        if (rm) rm[ch] = from_f<T>((1.f - momentum) * to_f<T>(rm[ch]) + momentum * mean);
+        if (rv) {
+            const double unbiased = cnt > 1 ? var * (double)cnt / (double)(cnt - 1) : var;
+            rv[ch] = from_f<T>((1.f - momentum) * to_f<T>(rv[ch]) + momentum * (float)unbiased);
+        }
+        if (save_mean) save_mean[ch] = mean;
+        if (save_invstd) save_invstd[ch] = invstd;
+    }
+}
+
+int bn_chunks(int64_t channels, int64_t cnt, int sms) {
+    const int64_t want_ctas = 4LL * sms;
+    int64_t ch = (want_ctas + channels - 1) / channels;
+    const int64_t by_size = (cnt + 4095) / 4096;
+    if (ch > by_size) ch = by_size;
+    if (ch > 64) ch = 64;
+    if (ch < 1) ch = 1;
+    return (int)ch;
+}
+
+// ---------------------------------------------------------------------------
+// GroupNorm: statistics per (n, b, group) over the group's contiguous
+// (c / groups) * l elements; per-channel affine. One CTA per group row; the row
+// is held in registers when it fits (exact two-pass mean / variance), otherwise
+// it is streamed three times (sum, squared deviations, normalize).
+// InstanceNorm is the same kernel with groups == c.
+// ---------------------------------------------------------------------------
+constexpr int kGnThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGnThreads / 32; ++i) t += red[i];
+    __syncthreads();
+    return t;
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kGnThreads) gn_reg_kernel(
+    const T* __restrict__ x, T* __restrict__ y, const T* __restrict__ w, const T* __restrict__ b,
+    float* __restrict__ out_mean, float* __restrict__ out_var, int64_t batch, int64_t c, int64_t l, int groups,
+    float eps) {
+    constexpr int V = 16 / sizeof(T);
+    __shared__ float red[kGnThreads / 32];
+    const int64_t row = blockIdx.x;                  // ((n * batch) + b) * groups + g
+    const int64_t cg = c / groups;
+    const int64_t len = cg * l;
+    const int64_t nvec = len / V;
+    const T* xr = x + row * len;
+    T* yr = y + row * len;
+    float v[VPT][V];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int64_t vi = threadIdx.x + (int64_t)i * kGnThreads;
+        if (vi < nvec) {
+            load16<T>(xr + vi * V, v[i]);
+#pragma unroll
+            for (int j = 0; j < V; ++j) s += v[i][j];
+        }
+    }
+    const float mean = block_sum<T>(s, red) / (float)len;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int64_t vi = threadIdx.x + (int64_t)i * kGnThreads;
+        if (vi < nvec) {
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const float d = v[i][j] - mean;
+                q += d * d;
+            }
+        }
+    }
+    const float var = block_sum<T>(q, red) / (float)len;
+    const float rstd = rsqrtf(var + eps);
+    if (threadIdx.x == 0 && out_mean) {
+        out_mean[row] = mean;
+        out_var[row] = var;
+    }
+    const int64_t g = row % groups;
+    const int64_t n_i = row / groups / batch;
+    const int64_t ch0 = n_i * c + g * cg;            // first flat channel of this group
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int64_t vi = threadIdx.x + (int64_t)i * kGnThreads;
+        if (vi < nvec) {
+            const int64_t ch = ch0 + (vi * V) / l;   // a vector never straddles channels (l % V == 0)
+            const float ga = w ? to_f<T>(w[ch]) * rstd : rstd;
+            const float be = b ? to_f<T>(b[ch]) : 0.f;
+            float o[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) o[j] = (v[i][j] - mean) * ga + be;
+            store16<T>(yr + vi * V, o);
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGnThreads) gn_stream_kernel(
+    const T* __restrict__ x, T* __restrict__ y, const T* __restrict__ w, const T* __restrict__ b,
+    float* __restrict__ out_mean, float* __restrict__ out_var, int64_t batch, int64_t c, int64_t l, int groups,
+    float eps) {
+    __shared__ float red[kGnThreads / 32];
+    const int64_t row = blockIdx.x;
+    const int64_t cg = c / groups;
+    const int64_t len = cg * l;
+    const T* xr = x + row * len;
+    T* yr = y + row * len;
+    float s = 0.f;
+    for (int64_t e = threadIdx.x; e < len; e += kGnThreads) s += to_f<T>(xr[e]);
+    const float mean = block_sum<T>(s, red) / (float)len;
+    float q = 0.f;
+    for (int64_t e = threadIdx.x; e < len; e += kGnThreads) {
+        const float d = to_f<T>(xr[e]) - mean;
+        q += d * d;
+    }
+    const float var = block_sum<T>(q, red) / (float)len;
+    const float rstd = rsqrtf(var + eps);
+    if (threadIdx.x == 0 && out_mean) {
+        out_mean[row] = mean;
+        out_var[row] = var;
+    }
+    const int64_t g = row % groups;
+    const int64_t ch0 = (row / groups / batch) * c + g * cg;
+    for (int64_t e = threadIdx.x; e < len; e += kGnThreads) {
+        const int64_t ch = ch0 + e / l;
+        const float ga = w ? to_f<T>(w[ch]) * rstd : rstd;
+        const float be = b ? to_f<T>(b[ch]) : 0.f;
+        yr[e] = from_f<T>((to_f<T>(xr[e]) - mean) * ga + be);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Embedding: out[i, j, :] = weight[i, idx[j], :] for every model i, with one
+// shared index tensor. Negative indices wrap once (Python indexing, as the
+// reference's weight[:, idx]); indices outside [-v, v) produce a zero row and
+// set the device error word.
+// ---------------------------------------------------------------------------
+template <typename U>
+__global__ void embedding_kernel(const int64_t* __restrict__ idx, const U* __restrict__ wt, U* __restrict__ out,
+                                 int64_t n, int64_t nidx, int64_t v, int64_t row_units, int* err) {
+    const int64_t total = n * nidx * row_units;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int64_t r = t / row_units;
+        const int64_t u = t - r * row_units;
+        const int64_t mi = r / nidx;
+        const int64_t j = r - mi * nidx;
+        int64_t k = idx[j];
+        if (k < 0) k += v;
+        if (k < 0 || k >= v) {
+            if (u == 0) raise_device_error(err, DEV_ERR_INDEX);
+            out[t] = U{};
+            continue;
+        }
+        out[t] = wt[(mi * v + k) * row_units + u];
+    }
+}
+
+unsigned grid_for(int64_t items, int threads) {
+    const int64_t want = (items + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count(current_device()) * 8;
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, cap));
+}
+
+struct BnEval {
+    const void *x, *w, *b, *rm, *rv;
+    void* y;
+    int64_t n, batch, c, l;
+    float eps;
+    cudaStream_t st;
+    template <typename T>
+    int run() {
+        constexpr int V = 16 / sizeof(T);
+        const int64_t total = n * batch * c * l;
+        const bool vec = (l % V == 0) && aligned16(x) && aligned16(y);
+        const auto* xp = static_cast<const T*>(x);
+        auto* yp = static_cast<T*>(y);
+        if (vec)
+            bn_eval_kernel<T, true><<<grid_for(total / V, 256), 256, 0, st>>>(
+                xp, yp, (const T*)w, (const T*)b, (const T*)rm, (const T*)rv, total, batch, c, l, eps);
+        else
+            bn_eval_kernel<T, false><<<grid_for(total, 256), 256, 0, st>>>(
+                xp, yp, (const T*)w, (const T*)b, (const T*)rm, (const T*)rv, total, batch, c, l, eps);
+        return check_launch("widek_batchnorm_fwd");
+    }
+};
+
+struct BnTrain {
+    const void *x, *w, *b;
+    void *y, *rm, *rv;
+    float *save_mean, *save_invstd;
+    void* ws;
+    size_t ws_bytes;
+    int64_t n, batch, c, l;
+    float momentum, eps;
+    cudaStream_t st;
+    template <typename T>
+    int run() {
+        const int64_t channels = n * c;
+        const int64_t cnt = batch * l;
+        const int chunks = bn_chunks(channels, cnt, sm_count(current_device()));
+        const size_t need = (size_t)channels * chunks * 2 * sizeof(double);
+        if (!ws || ws_bytes < need)
+            return set_error(WIDEK_ERR_INVALID, "batchnorm train: workspace of %zu bytes needed, %zu given", need,
+                             ws_bytes);
+        if (channels > 0x7fffffff) return set_error(WIDEK_ERR_UNSUPPORTED, "batchnorm: too many channels");
+        dim3 grid((unsigned)channels, (unsigned)chunks);
+        bn_partial_kernel<T><<<grid, kBnThreads, 0, st>>>(static_cast<const T*>(x), static_cast<double*>(ws),
+                                                           batch, c, l, chunks);
+        int rc = check_launch("widek_batchnorm_train_fwd (partials)");
+        if (rc) return rc;
+        bn_apply_kernel<T><<<grid, kBnThreads, 0, st>>>(
+            static_cast<const T*>(x), static_cast<T*>(y), (const T*)w, (const T*)b, (T*)rm, (T*)rv, save_mean,
+            save_invstd, static_cast<const double*>(ws), batch, c, l, chunks, momentum, eps);
+        return check_launch("widek_batchnorm_train_fwd (apply)");
+    }
+};
+
+struct GnLaunch {
+    const void *x, *w, *b;
+    void* y;
+    float *out_mean, *out_var;
+    int64_t n, batch, c, l;
+    int groups;
+    float eps;
+    cudaStream_t st;
+    template <typename T>
+    int run() {
+        constexpr int V = 16 / sizeof(T);
+        const int64_t rows = n * batch * groups;
+        const int64_t len = (c / groups) * l;
+        if (rows > 0x7fffffff) return set_error(WIDEK_ERR_UNSUPPORTED, "groupnorm: too many rows");
+        const bool vec = (l % V == 0) && aligned16(x) && aligned16(y);
+        const int64_t vpt = (len / V + kGnThreads - 1) / kGnThreads;
+        const auto* xp = static_cast<const T*>(x);
+        auto* yp = static_cast<T*>(y);
+        const T* wp = static_cast<const T*>(w);
+        const T* bp = static_cast<const T*>(b);
+        const unsigned grid = (unsigned)rows;
+        if (vec && vpt <= 1)
+            gn_reg_kernel<T, 1><<<grid, kGnThreads, 0, st>>>(xp, yp, wp, bp, out_mean, out_var, batch, c, l, groups, eps);
+        else if (vec && vpt <= 2)
+            gn_reg_kernel<T, 2><<<grid, kGnThreads, 0, st>>>(xp, yp, wp, bp, out_mean, out_var, batch, c, l, groups, eps);
+        else if (vec && vpt <= 4)
+            gn_reg_kernel<T, 4><<<grid, kGnThreads, 0, st>>>(xp, yp, wp, bp, out_mean, out_var, batch, c, l, groups, eps);
+        else if (vec && vpt <= 8)
+            gn_reg_kernel<T, 8><<<grid, kGnThreads, 0, st>>>(xp, yp, wp, bp, out_mean, out_var, batch, c, l, groups, eps);
+        else
+            gn_stream_kernel<T><<<grid, kGnThreads, 0, st>>>(xp, yp, wp, bp, out_mean, out_var, batch, c, l, groups, eps);
+        return check_launch("widek_groupnorm_fwd");
+    }
+};
+
+}  // namespace
+}  // namespace widek
+
+extern "C" {
+
+int widek_batchnorm_fwd(const void* x, void* y, const void* weight, const void* bias, const void* mean,
+                        const void* var, int64_t n, int64_t batch, int64_t c, int64_t l, double eps, int dtype,
+                        void* stream) {
+    using namespace widek;
+    if (n < 0 || batch < 0 || c < 0 || l < 0) return set_error(WIDEK_ERR_INVALID, "batchnorm: negative size");
+    if (n * batch * c * l == 0) return WIDEK_OK;
+    if (!x || !y || !mean || !var) return set_error(WIDEK_ERR_INVALID, "batchnorm: null pointer");
+    BnEval L{x, weight, bias, mean, var, y, n, batch, c, l, (float)eps, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+size_t widek_batchnorm_train_workspace(int64_t n, int64_t batch, int64_t c, int64_t l) {
+    using namespace widek;
+    if (n <= 0 || batch <= 0 || c <= 0 || l <= 0) return 0;
+    const int chunks = bn_chunks(n * c, batch * l, sm_count(current_device()));
+    return (size_t)(n * c) * chunks * 2 * sizeof(double);
+}
+
+int widek_batchnorm_train_fwd(const void* x, void* y, const void* weight, const void* bias, void* running_mean,
+                              void* running_var, float* save_mean, float* save_invstd, void* workspace,
+                              size_t workspace_bytes, int64_t n, int64_t batch, int64_t c, int64_t l,
+                              double momentum, double eps, int dtype, void* stream) {
+    using namespace widek;
+    if (n < 0 || batch < 0 || c < 0 || l < 0) return set_error(WIDEK_ERR_INVALID, "batchnorm: negative size");
+    if (n * batch * c * l == 0) return WIDEK_OK;
+    if (!x || !y) return set_error(WIDEK_ERR_INVALID, "batchnorm: null pointer");
+    BnTrain L{x, weight, bias, y, running_mean, running_var, save_mean, save_invstd, workspace, workspace_bytes,
+              n, batch, c, l, (float)momentum, (float)eps, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+int widek_groupnorm_fwd(const void* x, void* y, const void* weight, const void* bias, float* row_mean,
+                        float* row_var, int64_t n, int64_t batch, int64_t c, int64_t l, int64_t groups, double eps,
+                        int dtype, void* stream) {
+    using namespace widek;
+    if (n < 0 || batch < 0 || c < 0 || l < 0 || groups <= 0 || (c % groups) != 0)
+        return set_error(WIDEK_ERR_INVALID, "groupnorm: bad sizes (c=%lld groups=%lld)", (long long)c,
+                         (long long)groups);
+    if (n * batch * c * l == 0) return WIDEK_OK;
+    if (!x || !y) return set_error(WIDEK_ERR_INVALID, "groupnorm: null pointer");
+    if ((row_mean == nullptr) != (row_var == nullptr))
+        return set_error(WIDEK_ERR_INVALID, "groupnorm: row_mean and row_var go together");
+    GnLaunch L{x, weight, bias, y, row_mean, row_var, n, batch, c, l, (int)groups, (float)eps, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+int widek_embedding_fwd(const int64_t* idx, const void* weight, void* out, int64_t n, int64_t num_idx, int64_t v,
+                        int64_t d, int dtype, void* stream) {
+    using namespace widek;
+    if (n < 0 || num_idx < 0 || v < 0 || d < 0) return set_error(WIDEK_ERR_INVALID, "embedding: negative size");
+    const size_t es = dtype_size(dtype);
+    if (!es) return set_error(WIDEK_ERR_INVALID, "embedding: unknown dtype %d", dtype);
+    if (n * num_idx * d == 0) return WIDEK_OK;
+    if (!idx || !weight || !out) return set_error(WIDEK_ERR_INVALID, "embedding: null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t row_bytes = d * (int64_t)es;
+    int* err = device_error_ptr();
+    if (row_bytes % 16 == 0 && aligned16(weight) && aligned16(out)) {
+        const int64_t ru = row_bytes / 16;
+        embedding_kernel<uint4><<<grid_for(n * num_idx * ru, 256), 256, 0, st>>>(
+            idx, static_cast<const uint4*>(weight), static_cast<uint4*>(out), n, num_idx, v, ru, err);
+    } else if (es == 4) {
+        embedding_kernel<uint32_t><<<grid_for(n * num_idx * d, 256), 256, 0, st>>>(
+            idx, static_cast<const uint32_t*>(weight), static_cast<uint32_t*>(out), n, num_idx, v, d, err);
+    } else {
+        embedding_kernel<uint16_t><<<grid_for(n * num_idx * d, 256), 256, 0, st>>>(
+            idx, static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), n, num_idx, v, d, err);
+    }
+    return check_launch("widek_embedding_fwd");
+}
+
+}  // extern "C"

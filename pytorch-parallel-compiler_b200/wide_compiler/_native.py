@@ -50,7 +50,13 @@ SIGNATURES = {
     "widek_pack": [ctypes.POINTER(_c_void_p), _i64, _c_void_p, _i64, _i64, _c_void_p],
     "widek_unary": [_c_void_p, _c_void_p, _i64, _int, _int, _c_void_p],
     "widek_binary": [_c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _c_void_p],
+    "widek_batchnorm_fwd": [_c_void_p] * 6 + [_i64] * 4 + [_dbl, _int, _c_void_p],
+    "widek_batchnorm_train_workspace": [_i64] * 4,
+    "widek_batchnorm_train_fwd": [_c_void_p] * 9 + [ctypes.c_size_t] + [_i64] * 4 + [_dbl, _dbl, _int, _c_void_p],
+    "widek_groupnorm_fwd": [_c_void_p] * 6 + [_i64] * 5 + [_dbl, _int, _c_void_p],
+    "widek_embedding_fwd": [_c_void_p] * 3 + [_i64] * 4 + [_int, _c_void_p],
 }
+RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t}
 
 
 class WideKernelError(RuntimeError):
@@ -78,7 +84,7 @@ def load() -> ctypes.CDLL:
         for name, argtypes in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         _lib = lib
         return lib
 

@@ -154,3 +154,103 @@ def binary(a: Tensor, b: Tensor, op: str) -> Tensor:
                                   N.dtype_code(a), N.stream_ptr(dev))
     N.check(rc, f"widek_binary({op})")
     return y
+
+
+# ---------------------------------------------------------------------------
+# Norms
+# ---------------------------------------------------------------------------
+
+def _nbcl(x: Tensor, n: int, c: int, what: str):
+    if x.dim() < 3 or x.shape[0] != n or x.shape[2] != c:
+        raise ValueError(f"{what}: input {tuple(x.shape)} is not [N={n}, B, C={c}, ...]")
+    return x.shape[1], math.prod(x.shape[3:])
+
+
+def batchnorm(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias: Optional[Tensor],
+              running_mean: Optional[Tensor], running_var: Optional[Tensor], use_batch_stats: bool,
+              update_running: bool, momentum: float, eps: float) -> Tensor:
+    """Per-(model, channel) batch normalization on [N, B, C, *S]; weight, bias
+    and running stats flat [N*C]. With use_batch_stats the running stats (if
+    update_running) are updated in place."""
+    dev = N.require_cuda(x, weight, bias, running_mean, running_var, what="WideBatchNorm")
+    _same_dtype("WideBatchNorm", x, weight, bias, running_mean, running_var)
+    batch, l = _nbcl(x, n, c, "WideBatchNorm")
+    xd = _dense(x)
+    y = torch.empty_like(xd)
+    code = N.dtype_code(x)
+    with _guard(dev):
+        if not use_batch_stats:
+            if running_mean is None or running_var is None:
+                raise ValueError("WideBatchNorm: eval mode needs running statistics")
+            rc = N.lib().widek_batchnorm_fwd(xd.data_ptr(), y.data_ptr(), N.ptr(weight), N.ptr(bias),
+                                             running_mean.data_ptr(), running_var.data_ptr(), n, batch, c, l,
+                                             float(eps), code, N.stream_ptr(dev))
+            N.check(rc, "widek_batchnorm_fwd")
+            return y
+        ws_bytes = N.lib().widek_batchnorm_train_workspace(n, batch, c, l)
+        ws = torch.empty(max(int(ws_bytes), 16), dtype=torch.uint8, device=dev)
+        rm = running_mean if update_running else None
+        rv = running_var if update_running else None
+        rc = N.lib().widek_batchnorm_train_fwd(xd.data_ptr(), y.data_ptr(), N.ptr(weight), N.ptr(bias), N.ptr(rm),
+                                               N.ptr(rv), None, None, ws.data_ptr(), ws.numel(), n, batch, c, l,
+                                               float(momentum), float(eps), code, N.stream_ptr(dev))
+    N.check(rc, "widek_batchnorm_train_fwd")
+    return y
+
+
+def groupnorm(x: Tensor, n: int, groups: int, weight: Optional[Tensor], bias: Optional[Tensor], eps: float,
+              row_stats: bool = False):
+    """GroupNorm on [N, B, C, *S] with statistics per (model, sample, group).
+    With row_stats also returns fp32 (mean, biased var) of shape [N, B, groups]."""
+    dev = N.require_cuda(x, weight, bias, what="WideGroupNorm")
+    _same_dtype("WideGroupNorm", x, weight, bias)
+    if x.dim() < 3 or x.shape[0] != n:
+        raise ValueError(f"WideGroupNorm: input {tuple(x.shape)} is not [N={n}, B, C, ...]")
+    batch, c = x.shape[1], x.shape[2]
+    l = math.prod(x.shape[3:])
+    xd = _dense(x)
+    y = torch.empty_like(xd)
+    mean = var = None
+    if row_stats:
+        mean = torch.empty(n, batch, groups, device=dev, dtype=torch.float32)
+        var = torch.empty_like(mean)
+    with _guard(dev):
+        rc = N.lib().widek_groupnorm_fwd(xd.data_ptr(), y.data_ptr(), N.ptr(weight), N.ptr(bias), N.ptr(mean),
+                                         N.ptr(var), n, batch, c, l, groups, float(eps), N.dtype_code(x),
+                                         N.stream_ptr(dev))
+    N.check(rc, "widek_groupnorm_fwd")
+    return (y, mean, var) if row_stats else y
+
+
+def instancenorm_train(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias: Optional[Tensor],
+                       running_mean: Tensor, running_var: Tensor, momentum: float, eps: float) -> Tensor:
+    """InstanceNorm in training mode with tracked running stats: instance
+    statistics for the output; running stats move toward the batch average of
+    the instance mean / unbiased variance (torch.nn.InstanceNorm semantics)."""
+    y, mean, var = groupnorm(x, n, c, weight, bias, eps, row_stats=True)
+    l = math.prod(x.shape[3:])
+    unbiased = var * (l / max(l - 1, 1))
+    with torch.no_grad():
+        running_mean.mul_(1 - momentum).add_(mean.mean(dim=1).reshape(-1).to(running_mean.dtype), alpha=momentum)
+        running_var.mul_(1 - momentum).add_(unbiased.mean(dim=1).reshape(-1).to(running_var.dtype), alpha=momentum)
+    return y
+
+
+# ---------------------------------------------------------------------------
+# Embedding
+# ---------------------------------------------------------------------------
+
+def embedding(idx: Tensor, weight: Tensor) -> Tensor:
+    """[N, V, D] tables, shared integer indices of any shape -> [N, *idx.shape, D]."""
+    dev = N.require_cuda(idx, weight, what="WideEmbedding")
+    if idx.dtype not in (torch.int64, torch.int32, torch.int16, torch.int8, torch.uint8):
+        raise TypeError(f"WideEmbedding: indices must be integers, got {idx.dtype}")
+    ii = _dense(idx.to(torch.int64))
+    n, v, d = weight.shape
+    wd = _dense(weight)
+    out = torch.empty((n, *idx.shape, d), device=dev, dtype=weight.dtype)
+    with _guard(dev):
+        rc = N.lib().widek_embedding_fwd(ii.data_ptr(), wd.data_ptr(), out.data_ptr(), n, ii.numel(), v, d,
+                                         N.dtype_code(weight), N.stream_ptr(dev))
+    N.check(rc, "widek_embedding_fwd")
+    return out

@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "widek.h")
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"WIDEK_API\s+int\s+(widek_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"WIDEK_API\s+(?:int|size_t)\s+(widek_\w+)\s*\(", text)))
 
 
 def test_header_declares_entry_points():
