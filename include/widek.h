@@ -189,6 +189,33 @@ WIDEK_API int widek_groupnorm_fwd(const void* x, void* y, const void* weight, co
 WIDEK_API int widek_embedding_fwd(const int64_t* idx, const void* weight, void* out, int64_t n,
                                   int64_t num_idx, int64_t v, int64_t d, int dtype, void* stream);
 
+/* ---- WideGRU / WideLSTM --------------------------------------------------- */
+
+/* GRU recurrence over `steps` time steps in one launch (gate order r, z, n):
+ *   gates_x: [n, batch, steps, 3*hidden] = x @ W_ih^T + b_ih for every step
+ *            (computed beforehand with widek_linear_fwd);
+ *   w_hh: [n, 3*hidden, hidden]; b_hh: [n, 3*hidden] or NULL;
+ *   h0: [n, batch, hidden] or NULL (zeros);
+ *   out: [n, batch, steps, hidden]; h_n: [n, batch, hidden].
+ * One thread-block cluster per model keeps W_hh on chip across all steps.
+ * Replaces: wide_compiler/core/primitives/wide_gru.py:181-213 (per-step
+ * einsum, bias, chunk, sigmoid/tanh, blend, stack). */
+WIDEK_API int widek_gru_recurrence(const void* gates_x, const void* w_hh, const void* b_hh,
+                                   const void* h0, void* out, void* h_n, int64_t n,
+                                   int64_t batch, int64_t steps, int64_t hidden, int dtype,
+                                   void* stream);
+
+/* LSTM recurrence (gate order i, f, g, o) with the same conventions:
+ *   gates_x: [n, batch, steps, 4*hidden]; w_hh: [n, 4*hidden, hidden] (the
+ *   diagonal blocks of the block-diagonal module parameter); b_hh:
+ *   [n, 4*hidden] or NULL; h0, c0: [n, batch, hidden] or NULL;
+ *   out: [n, batch, steps, hidden]; h_n, c_n: [n, batch, hidden].
+ * Replaces: wide_compiler/core/primitives/wide_lstm.py:184-234. */
+WIDEK_API int widek_lstm_recurrence(const void* gates_x, const void* w_hh, const void* b_hh,
+                                    const void* h0, const void* c0, void* out, void* h_n,
+                                    void* c_n, int64_t n, int64_t batch, int64_t steps,
+                                    int64_t hidden, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -254,3 +254,63 @@ def embedding(idx: Tensor, weight: Tensor) -> Tensor:
                                          N.dtype_code(weight), N.stream_ptr(dev))
     N.check(rc, "widek_embedding_fwd")
     return out
+
+
+# ---------------------------------------------------------------------------
+# Recurrent layers
+# ---------------------------------------------------------------------------
+
+def _rnn_common(x: Tensor, w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor], gates: int, what: str):
+    if x.dim() != 4:
+        raise ValueError(f"{what}: input must be [N, B, T, I], got {tuple(x.shape)}")
+    n, batch, steps, i = x.shape
+    if w_ih.shape[0] != n or w_ih.shape[2] != i:
+        raise ValueError(f"{what}: weight_ih {tuple(w_ih.shape)} does not match input {tuple(x.shape)}")
+    hidden = w_hh.shape[2]
+    if w_hh.shape != (n, gates * hidden, hidden):
+        raise ValueError(f"{what}: weight_hh {tuple(w_hh.shape)} is not [N, {gates}H, H]")
+    # Input projection for all steps at once: [N, B, T, G*H] (bias b_ih fused).
+    gx = linear(x, w_ih, b_ih) if steps > 0 else None
+    return n, batch, steps, hidden, gx
+
+
+def gru(x: Tensor, h0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor],
+        b_hh: Optional[Tensor]):
+    """WideGRU forward: returns (out [N, B, T, H], h_n [N, B, H])."""
+    dev = N.require_cuda(x, h0, w_ih, w_hh, b_ih, b_hh, what="WideGRU")
+    _same_dtype("WideGRU", w_ih, x, h0, w_hh, b_ih, b_hh)
+    n, batch, steps, hidden, gx = _rnn_common(x, w_ih, w_hh, b_ih, 3, "WideGRU")
+    if h0 is not None and tuple(h0.shape) != (n, batch, hidden):
+        raise ValueError(f"WideGRU: h_0 must be [N, B, H] = {(n, batch, hidden)}, got {tuple(h0.shape)}")
+    out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
+    hn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
+    h0d = _dense(h0) if h0 is not None else None
+    with _guard(dev):
+        rc = N.lib().widek_gru_recurrence(N.ptr(gx), _dense(w_hh).data_ptr(), N.ptr(_dense(b_hh) if b_hh is not None else None),
+                                          N.ptr(h0d), out.data_ptr(), hn.data_ptr(), n, batch, steps, hidden,
+                                          N.dtype_code(x), N.stream_ptr(dev))
+    N.check(rc, "widek_gru_recurrence")
+    return out, hn
+
+
+def lstm(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor,
+         b_ih: Optional[Tensor], b_hh: Optional[Tensor]):
+    """WideLSTM forward on dense diagonal blocks: returns (out, (h_n, c_n))."""
+    dev = N.require_cuda(x, h0, c0, w_ih, w_hh, b_ih, b_hh, what="WideLSTM")
+    _same_dtype("WideLSTM", w_ih, x, h0, c0, w_hh, b_ih, b_hh)
+    n, batch, steps, hidden, gx = _rnn_common(x, w_ih, w_hh, b_ih, 4, "WideLSTM")
+    for name, t in (("h_0", h0), ("c_0", c0)):
+        if t is not None and tuple(t.shape) != (n, batch, hidden):
+            raise ValueError(f"WideLSTM: {name} must be [N, B, H] = {(n, batch, hidden)}, got {tuple(t.shape)}")
+    out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
+    hn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
+    cn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
+    with _guard(dev):
+        rc = N.lib().widek_lstm_recurrence(N.ptr(gx), _dense(w_hh).data_ptr(),
+                                           N.ptr(_dense(b_hh) if b_hh is not None else None),
+                                           N.ptr(_dense(h0) if h0 is not None else None),
+                                           N.ptr(_dense(c0) if c0 is not None else None), out.data_ptr(),
+                                           hn.data_ptr(), cn.data_ptr(), n, batch, steps, hidden, N.dtype_code(x),
+                                           N.stream_ptr(dev))
+    N.check(rc, "widek_lstm_recurrence")
+    return out, (hn, cn)

@@ -1,0 +1,108 @@
+"""GPU parity: WideGRU / WideLSTM persistent recurrence kernels against the
+reference fixtures and the oracle (fp32 contract: rtol 1e-3 / atol 1e-4)."""
+import pytest
+import torch
+
+import wide_compiler as wc
+from wide_compiler import ops
+from conftest import golden_names, load_golden
+from gpu_util import assert_fp32_close, assert_lowp_close, no_device_error
+from oracle import wide_oracle as O
+from test_api_host import _build_from_state
+
+pytestmark = pytest.mark.gpu
+DEV = 'cuda'
+
+
+@pytest.mark.parametrize("name", golden_names('gru') + golden_names('lstm'))
+def test_rnn_golden(name):
+    g = load_golden(name)
+    mod = _build_from_state(g).to(DEV)
+    inp = g['inputs']
+    x = inp['x'].to(DEV)
+    if g['kind'] == 'gru':
+        h0 = inp['h0'].to(DEV) if inp['h0'] is not None else None
+        y, hn = mod(x, h0)
+        assert_fp32_close(y, g['outputs']['y'])
+        assert_fp32_close(hn, g['outputs']['h_n'])
+    else:
+        hx = (inp['h0'].to(DEV), inp['c0'].to(DEV)) if inp['h0'] is not None else None
+        y, (hn, cn) = mod(x, hx)
+        assert_fp32_close(y, g['outputs']['y'])
+        assert_fp32_close(hn, g['outputs']['h_n'])
+        assert_fp32_close(cn, g['outputs']['c_n'])
+
+
+def _rnn_params(n, i, h, gates, dtype, seed):
+    gen = torch.Generator().manual_seed(seed)
+    s = 1.0 / h ** 0.5
+    u = lambda *shape: ((torch.rand(*shape, generator=gen) * 2 - 1) * s).to(dtype)
+    return u(n, gates * h, i), u(n, gates * h, h), u(n, gates * h), u(n, gates * h)
+
+
+@pytest.mark.parametrize("n,b,t,i,h", [(32, 4, 32, 64, 128), (3, 16, 7, 20, 256), (2, 3, 5, 8, 24), (1, 1, 1, 4, 8)])
+def test_gru_random_fp32(n, b, t, i, h):
+    wih, whh, bih, bhh = _rnn_params(n, i, h, 3, torch.float32, n + h)
+    x = torch.randn(n, b, t, i)
+    h0 = torch.randn(n, b, h) * 0.5
+    y, hn = ops.gru(x.to(DEV), h0.to(DEV), wih.to(DEV), whh.to(DEV), bih.to(DEV), bhh.to(DEV))
+    ry, rh = O.gru(x, h0, wih, whh, bih, bhh)
+    assert_fp32_close(y, ry)
+    assert_fp32_close(hn, rh)
+    no_device_error()
+
+
+@pytest.mark.parametrize("n,b,t,i,h", [(32, 4, 32, 64, 128), (2, 8, 6, 16, 512), (3, 5, 4, 12, 40), (2, 40, 3, 8, 64)])
+def test_lstm_random_fp32(n, b, t, i, h):
+    wih, whh, bih, bhh = _rnn_params(n, i, h, 4, torch.float32, n * 7 + h)
+    x = torch.randn(n, b, t, i)
+    h0, c0 = torch.randn(n, b, h) * 0.5, torch.randn(n, b, h) * 0.5
+    y, (hn, cn) = ops.lstm(x.to(DEV), h0.to(DEV), c0.to(DEV), wih.to(DEV), whh.to(DEV), bih.to(DEV), bhh.to(DEV))
+    ry, (rh, rc) = O.lstm(x, h0, c0, wih, whh, bih, bhh)
+    assert_fp32_close(y, ry)
+    assert_fp32_close(hn, rh)
+    assert_fp32_close(cn, rc)
+    no_device_error()
+
+
+def test_rnn_bf16_and_no_bias():
+    n, b, t, i, h = 4, 4, 16, 32, 128
+    wih, whh, _, _ = _rnn_params(n, i, h, 3, torch.bfloat16, 5)
+    x = torch.randn(n, b, t, i).to(torch.bfloat16)
+    y, hn = ops.gru(x.to(DEV), None, wih.to(DEV), whh.to(DEV), None, None)
+    ry, rh = O.gru(x, None, wih, whh, None, None)
+    assert_lowp_close(y, ry)
+    wih, whh, bih, bhh = _rnn_params(n, i, h, 4, torch.bfloat16, 6)
+    y, (hn, cn) = ops.lstm(x.to(DEV), None, None, wih.to(DEV), whh.to(DEV), bih.to(DEV), bhh.to(DEV))
+    ry, (rh, rc) = O.lstm(x, None, None, wih, whh, bih, bhh)
+    assert_lowp_close(y, ry)
+    assert_lowp_close(cn, rc)
+
+
+def test_rnn_modules_from_torch_cfg4():
+    """BASELINE cfg4 through the public modules built from nn.GRU / nn.LSTM."""
+    torch.manual_seed(0)
+    grus = [torch.nn.GRU(64, 128, batch_first=True) for _ in range(32)]
+    lstms = [torch.nn.LSTM(64, 128, batch_first=True) for _ in range(32)]
+    x = torch.randn(32, 4, 32, 64)
+    wg = wc.WideGRU.from_modules(grus).to(DEV)
+    wl = wc.WideLSTM.from_modules(lstms).to(DEV)
+    y, hn = wg(x.to(DEV))
+    for k in (0, 13, 31):
+        ry, rh = grus[k](x[k])
+        assert_fp32_close(y[k], ry.detach())
+        assert_fp32_close(hn[k], rh[0].detach())
+    y, (hn, cn) = wl(x.to(DEV))
+    for k in (0, 31):
+        ry, (rh, rc) = lstms[k](x[k])
+        assert_fp32_close(y[k], ry.detach())
+        assert_fp32_close(cn[k], rc[0].detach())
+
+
+def test_rnn_zero_steps():
+    wih, whh, bih, bhh = _rnn_params(2, 4, 8, 3, torch.float32, 1)
+    h0 = torch.randn(2, 3, 8)
+    y, hn = ops.gru(torch.empty(2, 3, 0, 4, device=DEV), h0.to(DEV), wih.to(DEV), whh.to(DEV), bih.to(DEV),
+                    bhh.to(DEV))
+    assert y.shape == (2, 3, 0, 8)
+    torch.testing.assert_close(hn.cpu(), h0)
