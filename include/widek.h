@@ -216,6 +216,30 @@ WIDEK_API int widek_lstm_recurrence(const void* gates_x, const void* w_hh, const
                                     void* c_n, int64_t n, int64_t batch, int64_t steps,
                                     int64_t hidden, int dtype, void* stream);
 
+/* ---- WideAttention -------------------------------------------------------- */
+
+#define WIDEK_MASK_NONE 0
+#define WIDEK_MASK_BOOL 1       /* uint8, nonzero = attend */
+#define WIDEK_MASK_ADD 2        /* additive, same dtype as q */
+#define WIDEK_MASK_ADD_F32 3    /* additive, fp32 */
+
+/* Scaled dot-product attention core for nb*heads independent heads:
+ *   q: rows [nb, tq] with row stride q_row_stride elements, head h at
+ *      columns [h*head_dim, (h+1)*head_dim); k, v likewise with tk rows;
+ *   o: [nb, tq] rows of o_row_stride elements, head h at h*head_dim.
+ * softmax(q k^T * scale [+ mask]) v per head; causal = key index <= query
+ * index (top-left aligned). mask (nullable) is addressed as
+ * mask[b*s0 + h*s1 + i*s2 + j*s3] with mask_strides = {s0, s1, s2, s3}
+ * (0 for broadcast dims). Rows with no attended key produce zeros.
+ * Replaces: wide_compiler/core/primitives/wide_attention.py:217-231
+ * (head split copies, F.scaled_dot_product_attention, head merge). */
+WIDEK_API int widek_attention_fwd(const void* q, const void* k, const void* v, void* o,
+                                  int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+                                  int64_t o_row_stride, int64_t nb, int64_t heads, int64_t tq,
+                                  int64_t tk, int64_t head_dim, int causal, const void* mask,
+                                  int mask_kind, const int64_t* mask_strides, double scale,
+                                  int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

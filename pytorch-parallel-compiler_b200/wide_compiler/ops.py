@@ -314,3 +314,81 @@ def lstm(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], w_ih: Tensor, w_
                                            N.stream_ptr(dev))
     N.check(rc, "widek_lstm_recurrence")
     return out, (hn, cn)
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+
+def attention_core(q: Tensor, k: Tensor, v: Tensor, nb: int, heads: int, tq: int, tk: int, head_dim: int,
+                   q_stride: int, k_stride: int, v_stride: int, out: Tensor, causal: bool,
+                   attn_mask: Optional[Tensor]) -> Tensor:
+    """softmax(q k^T / sqrt(head_dim) [+mask]) v over nb*heads heads, reading
+    q/k/v through row strides (elements; the tensors passed are the base
+    views) and writing ``out`` rows of heads*head_dim elements."""
+    dev = out.device
+    kind, mptr, strides = 0, None, None
+    keep_alive = None
+    if attn_mask is not None:
+        m = attn_mask.to(dev)
+        if m.dtype == torch.bool:
+            m = m.view(torch.uint8)
+            kind = 1
+        elif m.dtype == q.dtype:
+            kind = 2
+        else:
+            m = m.to(torch.float32)
+            kind = 3
+        try:
+            m4 = torch.broadcast_to(m, (nb, heads, tq, tk))
+        except RuntimeError:
+            raise ValueError(f"WideAttention: attn_mask of shape {tuple(attn_mask.shape)} does not broadcast to "
+                             f"[N*B={nb}, heads={heads}, Tq={tq}, Tk={tk}]") from None
+        keep_alive = m4
+        mptr = m4.data_ptr()
+        strides = (ctypes.c_int64 * 4)(*m4.stride())
+    with _guard(dev):
+        rc = N.lib().widek_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), q_stride,
+                                         k_stride, v_stride, heads * head_dim, nb, heads, tq, tk, head_dim,
+                                         1 if causal else 0, mptr, kind, strides, 1.0 / math.sqrt(head_dim),
+                                         N.dtype_code(out), N.stream_ptr(dev))
+    del keep_alive
+    N.check(rc, "widek_attention_fwd")
+    return out
+
+
+def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool) -> Tensor:
+    """WideAttention forward on N-first [N, B, T, D] tensors (see the module)."""
+    dev = N.require_cuda(query, key, value, mod.q_weight, what="WideAttention")
+    _same_dtype("WideAttention", mod.q_weight, query, key, value)
+    if is_causal and attn_mask is not None:
+        raise RuntimeError("WideAttention: an explicit attn_mask cannot be combined with is_causal=True "
+                           "(same rule as scaled_dot_product_attention)")
+    n, d, heads = mod.n, mod.d_model, mod.n_heads
+    dh = d // heads
+    if query.dim() != 4 or query.shape[0] != n or query.shape[3] != d:
+        raise ValueError(f"WideAttention: query must be [N={n}, B, T, D={d}], got {tuple(query.shape)}")
+    _, b, tq, _ = query.shape
+    tk = key.shape[2]
+    if key.shape[:2] != (n, b) or value.shape[:3] != key.shape[:3]:
+        raise ValueError("WideAttention: key/value shapes do not match the query")
+    if key is query and value is query:
+        w, bias = mod._fused_qkv()
+        qkv = linear(query, w, bias)                       # [N, B, T, 3D]
+        flat = qkv.view(-1)
+        q_t, k_t, v_t = flat, flat[d:], flat[2 * d:]
+        sq = sk = sv = 3 * d
+    elif value is key:
+        q_t = linear(query, mod.q_weight, mod.q_bias).view(-1)
+        kv = linear(key, mod.kv_weight, mod.kv_bias).view(-1)   # [N, B, Tk, 2D]
+        k_t, v_t = kv, kv[d:]
+        sq, sk, sv = d, 2 * d, 2 * d
+    else:
+        kb = mod.kv_bias
+        q_t = linear(query, mod.q_weight, mod.q_bias).view(-1)
+        k_t = linear(key, mod.kv_weight[:, :d], None if kb is None else kb[:, :d]).view(-1)
+        v_t = linear(value, mod.kv_weight[:, d:], None if kb is None else kb[:, d:]).view(-1)
+        sq = sk = sv = d
+    o = torch.empty(n, b, tq, d, device=dev, dtype=query.dtype)
+    attention_core(q_t, k_t, v_t, n * b, heads, tq, tk, dh, sq, sk, sv, o, is_causal, attn_mask)
+    return linear(o, mod.out_weight, mod.out_bias)
