@@ -190,7 +190,8 @@ def attention(query: Tensor, key: Tensor, value: Tensor, q_weight: Tensor, kv_we
         keep = torch.ones(tq, tk, dtype=torch.bool).tril()
         s = s.masked_fill(~keep, float('-inf'))
     if attn_mask is not None:
-        m = attn_mask.to('cpu')
+        # SDPA broadcasts the mask against [N*B, heads, tq, tk].
+        m = torch.broadcast_to(attn_mask.to('cpu'), (n * b, n_heads, tq, tk)).reshape(n, b, n_heads, tq, tk)
         if m.dtype == torch.bool:
             s = s.masked_fill(~m, float('-inf'))
         else:

@@ -57,7 +57,7 @@ SIGNATURES = {
     "widek_embedding_fwd": [_c_void_p] * 3 + [_i64] * 4 + [_int, _c_void_p],
     "widek_gru_recurrence": [_c_void_p] * 6 + [_i64] * 4 + [_int, _c_void_p],
     "widek_lstm_recurrence": [_c_void_p] * 8 + [_i64] * 4 + [_int, _c_void_p],
-    "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 10 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
+    "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
 }
 RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t}

@@ -55,3 +55,19 @@ def test_zero_sized_calls_are_noops():
     lib = N.load()
     assert lib.widek_linear_fwd(None, None, None, None, 0, 4, 4, 4, N.BF16, 0, None) == 0
     assert lib.widek_swap01(None, None, 0, 3, 16, None) == 0
+
+
+def _header_param_counts():
+    text = open(HEADER).read()
+    out = {}
+    for m in re.finditer(r"WIDEK_API\s+(?:int|size_t)\s+(widek_\w+)\s*\(([^)]*)\)", text, re.S):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else len(params.split(","))
+    return out
+
+
+def test_binding_argument_counts_match_header():
+    from wide_compiler import _native
+    counts = _header_param_counts()
+    for name, argtypes in _native.SIGNATURES.items():
+        assert len(argtypes) == counts[name], f"{name}: binding has {len(argtypes)} args, header {counts[name]}"
