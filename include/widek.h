@@ -164,6 +164,27 @@ WIDEK_API int widek_batchnorm_train_fwd(const void* x, void* y, const void* weig
                                         int64_t n, int64_t batch, int64_t c, int64_t l,
                                         double momentum, double eps, int dtype, void* stream);
 
+/* Allocation-free variant of widek_batchnorm_train_fwd for callers that
+ * cannot allocate device memory (a runtime that owns all device memory in
+ * its own fixed pool, a latency-critical path that must not risk cudaMalloc's
+ * implicit synchronization, an FFI caller with no allocator). This entry
+ * point has no counterpart in the reference.
+ * Same arguments and results as widek_batchnorm_train_fwd minus the
+ * workspace: the fp64 partial sums live in a fixed 1 MiB device array inside
+ * the library (held on every GPU that loads it until exit), so at most
+ * 65536 channels (n*c) are accepted; larger requests return
+ * WIDEK_ERR_INVALID. The first call on a device resolves that array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race and
+ * must be serialized by the caller. Nothing in the array has to start at zero
+ * (every slot is written before it is read). Allocates nothing. */
+WIDEK_API int widek_batchnorm_train_fwd_noalloc(const void* x, void* y, const void* weight,
+                                                const void* bias, void* running_mean,
+                                                void* running_var, float* save_mean,
+                                                float* save_invstd, int64_t n, int64_t batch,
+                                                int64_t c, int64_t l, double momentum, double eps,
+                                                int dtype, void* stream);
+
 /* ---- WideGroupNorm / WideInstanceNorm1d/2d -------------------------------- */
 
 /* Statistics per (model, sample, group) over the group's (c/groups)*l

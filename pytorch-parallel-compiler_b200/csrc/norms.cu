@@ -5,6 +5,8 @@
 // [n, batch, c]); per-channel tensors (weight, bias, running stats) are flat
 // [n * c], channel index n_i * c + c_i, exactly the inner nn.BatchNorm(N*C) /
 // nn.GroupNorm(N*G, N*C) parameter order of the reference.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace widek {
@@ -487,3 +489,104 @@ int widek_embedding_fwd(const int64_t* idx, const void* weight, void* out, int64
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the training-mode BatchNorm.
+//
+// Some callers cannot call cudaMalloc at all: a serving runtime that owns all
+// device memory through its own fixed-budget pool, a latency-critical path
+// that must not risk cudaMalloc's implicit device synchronization or its
+// failure, or a thin FFI binding that has no access to any allocator. For
+// them widek_batchnorm_train_fwd_noalloc keeps the split reduction's scratch
+// (fp64 partial sums per channel and chunk) in the fixed-size array below
+// instead of a caller workspace. Every GPU that loads this library holds the
+// array (kNoAllocScratchDoubles doubles = 1 MiB) until the process exits.
+//
+// The name g_bn_noalloc_scratch is a host-side stand-in in host code, not a
+// device address: its device address is resolved with cudaGetSymbolAddress
+// once per device (with that device current) on the first call on that
+// device, and that address is what the kernels receive.
+//
+// Every call shares the array, so calls whose work overlaps on the GPU (two
+// streams, or two host threads) race on it and must be serialized by the
+// caller. Nothing in it needs to start at zero: the partial-sum kernel writes
+// every slot it uses before the apply kernel reads it, so the contents left by
+// the previous call are never read.
+// ---------------------------------------------------------------------------
+namespace widek {
+namespace {
+
+constexpr int64_t kNoAllocScratchDoubles = int64_t(1) << 17;   // 1 MiB of fp64
+
+static __device__ __align__(256) double g_bn_noalloc_scratch[kNoAllocScratchDoubles];
+
+std::mutex g_noalloc_mutex;
+double* g_noalloc_scratch_ptr[64] = {nullptr};
+
+// Device address of the scratch array for the current device (set-up on the
+// first call per device).
+int noalloc_scratch(double** out) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64) return set_error(WIDEK_ERR_UNSUPPORTED, "noalloc: device index %d", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+    if (!g_noalloc_scratch_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_bn_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(WIDEK_ERR_CUDA, "noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        g_noalloc_scratch_ptr[dev] = static_cast<double*>(p);
+    }
+    *out = g_noalloc_scratch_ptr[dev];
+    return WIDEK_OK;
+}
+
+struct BnTrainNoAlloc {
+    const void *x, *w, *b;
+    void *y, *rm, *rv;
+    float *save_mean, *save_invstd;
+    double* scratch;
+    int64_t n, batch, c, l;
+    float momentum, eps;
+    cudaStream_t st;
+    template <typename T>
+    int run() {
+        const int64_t channels = n * c;
+        const int64_t cnt = batch * l;
+        int chunks = bn_chunks(channels, cnt, sm_count(current_device()));
+        const int64_t fit = kNoAllocScratchDoubles / (2 * channels);   // >= 1 (checked by the caller)
+        if (chunks > fit) chunks = (int)fit;
+        dim3 grid((unsigned)channels, (unsigned)chunks);
+        bn_partial_kernel<T><<<grid, kBnThreads, 0, st>>>(static_cast<const T*>(x), scratch, batch, c, l, chunks);
+        int rc = check_launch("widek_batchnorm_train_fwd_noalloc (partials)");
+        if (rc) return rc;
+        bn_apply_kernel<T><<<grid, kBnThreads, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(y), (const T*)w,
+                                                         (const T*)b, (T*)rm, (T*)rv, save_mean, save_invstd, scratch,
+                                                         batch, c, l, chunks, momentum, eps);
+        return check_launch("widek_batchnorm_train_fwd_noalloc (apply)");
+    }
+};
+
+}  // namespace
+}  // namespace widek
+
+extern "C" int widek_batchnorm_train_fwd_noalloc(const void* x, void* y, const void* weight, const void* bias,
+                                                 void* running_mean, void* running_var, float* save_mean,
+                                                 float* save_invstd, int64_t n, int64_t batch, int64_t c,
+                                                 int64_t l, double momentum, double eps, int dtype,
+                                                 void* stream) {
+    using namespace widek;
+    if (n < 0 || batch < 0 || c < 0 || l < 0) return set_error(WIDEK_ERR_INVALID, "batchnorm noalloc: negative size");
+    if (n * c > kNoAllocScratchDoubles / 2)
+        return set_error(WIDEK_ERR_INVALID,
+                         "batchnorm noalloc: %lld channels (n*c) exceed the fixed scratch limit of %lld channels; "
+                         "use widek_batchnorm_train_fwd with a workspace",
+                         (long long)(n * c), (long long)(kNoAllocScratchDoubles / 2));
+    if (n * batch * c * l == 0) return WIDEK_OK;
+    if (!x || !y) return set_error(WIDEK_ERR_INVALID, "batchnorm noalloc: null pointer");
+    double* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    BnTrainNoAlloc L{x, weight, bias, y, running_mean, running_var, save_mean, save_invstd, scratch,
+                     n, batch, c, l, (float)momentum, (float)eps, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}

@@ -53,6 +53,7 @@ SIGNATURES = {
     "widek_batchnorm_fwd": [_c_void_p] * 6 + [_i64] * 4 + [_dbl, _int, _c_void_p],
     "widek_batchnorm_train_workspace": [_i64] * 4,
     "widek_batchnorm_train_fwd": [_c_void_p] * 9 + [ctypes.c_size_t] + [_i64] * 4 + [_dbl, _dbl, _int, _c_void_p],
+    "widek_batchnorm_train_fwd_noalloc": [_c_void_p] * 8 + [_i64] * 4 + [_dbl, _dbl, _int, _c_void_p],
     "widek_groupnorm_fwd": [_c_void_p] * 6 + [_i64] * 5 + [_dbl, _int, _c_void_p],
     "widek_embedding_fwd": [_c_void_p] * 3 + [_i64] * 4 + [_int, _c_void_p],
     "widek_gru_recurrence": [_c_void_p] * 6 + [_i64] * 4 + [_int, _c_void_p],
