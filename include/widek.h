@@ -237,6 +237,38 @@ WIDEK_API int widek_lstm_recurrence(const void* gates_x, const void* w_hh, const
                                     void* c_n, int64_t n, int64_t batch, int64_t steps,
                                     int64_t hidden, int dtype, void* stream);
 
+/* ---- WideConv1d / WideConv2d / WideConv3d -------------------------------- */
+
+/* Repacks conv weights [rows][cin][taps] -> [rows][taps][cin] (rows = n*cout,
+ * taps = kd*kh*kw) for the tensor-core path; elem_bytes 2 or 4. */
+WIDEK_API int widek_conv_pack_weight(const void* w, void* w_packed, int64_t rows, int64_t cin,
+                                     int64_t taps, int64_t elem_bytes, void* stream);
+
+/* Bytes of the channels-last staging workspace widek_conv_fwd uses on the
+ * tensor-core path (n*batch*cin*d*h*w elements). */
+WIDEK_API size_t widek_conv_workspace(int64_t n, int64_t batch, int64_t cin, int64_t d, int64_t h,
+                                      int64_t w, int dtype);
+
+/* One independent convolution per model on the N-first layout:
+ *   x: [n, batch, cin, d, h, w] (d = 1 for 2-D; d = h = 1 for 1-D);
+ *   w: [n*cout, cin, kd, kh, kw]; y: [n, batch, cout, od, oh, ow].
+ * geom = 22 int64: n, batch, cin, cout, d, h, w, kd, kh, kw, sd, sh, sw,
+ *        pd, ph, pw, dd, dh, dw, od, oh, ow (stride s, padding p, dilation d).
+ * Epilogue per output element of channel c of model i (ch = i*cout + c):
+ *   v = acc + bias[ch]; v *= scale[ch]; v += shift[ch];
+ *   residual_first ? v = act(v + residual) : v = act(v) + residual
+ * (each term skipped when its pointer is NULL).
+ * bf16/f16 2-D/1-D convs with stride 1, cin % 64 == 0 and cout % 16 == 0 run
+ * on the tcgen05 implicit-GEMM kernel when w_packed (from
+ * widek_conv_pack_weight) and a workspace of widek_conv_workspace() bytes
+ * are given; everything else runs a CUDA-core direct convolution.
+ * Replaces: wide_compiler/core/primitives/wide_conv2d.py:169-194 (permute
+ * copies + grouped F.conv2d), wide_conv1d.py:118-135, wide_conv3d.py:102-125. */
+WIDEK_API int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const void* bias,
+                             const void* scale, const void* shift, const void* residual, void* y,
+                             void* workspace, size_t workspace_bytes, const int64_t* geom, int act,
+                             int residual_first, int dtype, void* stream);
+
 /* ---- WideAttention -------------------------------------------------------- */
 
 #define WIDEK_MASK_NONE 0

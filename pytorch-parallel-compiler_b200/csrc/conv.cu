@@ -1,0 +1,497 @@
+// Wide convolutions (1-D / 2-D / 3-D, one independent conv per model) on the
+// N-first layout x [n, batch, cin, *spatial] -> y [n, batch, cout, *spatial'].
+//
+// Tensor-core path (bf16/f16, 2-D or 1-D, stride 1, cin % 64 == 0,
+// cout % 16 == 0): implicit GEMM on tcgen05.
+//   * the input is staged channels-last ([n*batch][h][w][cin], a caller
+//     workspace) by one tiled transpose kernel, so that for a fixed filter tap
+//     (kh, kw) the 64 input channels of an output pixel are one contiguous
+//     128-byte row;
+//   * the weights are pre-packed [n][cout][kh][kw][cin] (K-major with
+//     k = (kh, kw, cin)) by widek_conv_pack_weight;
+//   * a 128-pixel M tile is TH x TW output pixels (TW = row width rounded up
+//     to a power of two, TH = 128 / TW). K-block (kh, kw, 64 channels) of A is
+//     ONE TMA box {64, TW, TH, 1} of the channels-last input at coordinates
+//     (c0, wo0 - pad + kw*dil, ho0 - pad + kh*dil, image): the innermost
+//     coordinate stays 64-aligned, and out-of-range (padding) pixels are
+//     zero-filled by the TMA unit;
+//   * warp-specialised persistent kernel as the linear one (TMA warp, MMA
+//     warp, 4 epilogue warps, double-buffered TMEM accumulator); the epilogue
+//     writes NCHW directly (for a fixed output channel a warp stores 32
+//     consecutive pixels) and can fuse bias, a per-channel scale/shift
+//     (folded BatchNorm), an activation and a residual add.
+// CUDA-core path (everything else, including fp32): direct convolution, one
+// output element per thread, fp32 accumulation.
+#include "sm100_ptx.cuh"
+
+namespace widek {
+namespace {
+
+using namespace sm100;
+
+// ---------------------------------------------------------------------------
+// Layout helpers
+// ---------------------------------------------------------------------------
+// [nb][c][p] -> [nb][p][c], 32x32 tiles through shared memory.
+template <typename T>
+__global__ void nchw_to_nhwc_kernel(const T* __restrict__ src, T* __restrict__ dst, int64_t nb, int c, int64_t p) {
+    __shared__ T tile[32][33];
+    const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
+    const int64_t p0 = (int64_t)blockIdx.x * 32;
+    const int c0 = blockIdx.y * 32;
+    for (int64_t img = blockIdx.z; img < nb; img += gridDim.z) {
+        const T* s = src + img * c * p;
+        T* d = dst + img * c * p;
+        for (int r = ty; r < 32; r += 8) {
+            const int cc = c0 + r;
+            const int64_t pp = p0 + tx;
+            if (cc < c && pp < p) tile[r][tx] = s[(int64_t)cc * p + pp];
+        }
+        __syncthreads();
+        for (int r = ty; r < 32; r += 8) {
+            const int64_t pp = p0 + r;
+            const int cc = c0 + tx;
+            if (cc < c && pp < p) d[pp * c + cc] = tile[tx][r];
+        }
+        __syncthreads();
+    }
+}
+
+// w [rows][cin][taps] -> wp [rows][taps][cin]
+template <typename U>
+__global__ void pack_weight_kernel(const U* __restrict__ w, U* __restrict__ wp, int64_t rows, int64_t cin,
+                                   int64_t taps) {
+    const int64_t total = rows * cin * taps;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t r = i / (cin * taps);
+        const int64_t rem = i - r * cin * taps;
+        const int64_t t = rem / cin;
+        const int64_t ci = rem - t * cin;
+        wp[i] = w[(r * cin + ci) * taps + t];
+    }
+}
+
+unsigned grid_cap(int64_t items, int threads) {
+    const int64_t want = (items + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count(current_device()) * 8;
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, cap));
+}
+
+struct ConvGeom {
+    int n, batch, cin, cout;
+    int d, h, w;          // input spatial (d = 1 for 2-D, h = d = 1 for 1-D)
+    int kd, kh, kw;
+    int sd, sh, sw;
+    int pd, ph, pw;
+    int dd, dh, dw;
+    int od, oh, ow;       // output spatial
+};
+
+struct ConvEpi {
+    const void* bias;     // [n*cout] or null
+    const void* scale;    // [n*cout] or null (per-channel multiplier after bias)
+    const void* shift;    // [n*cout] or null
+    const void* residual; // same layout as y, or null
+    int act;              // WIDEK_ACT_*
+    int residual_first;   // 1: add the residual before the activation
+};
+
+template <typename T>
+__device__ __forceinline__ float conv_epilogue(float v, int64_t ch, int64_t yoff, const ConvEpi& e) {
+    if (e.bias) v += to_f<T>(static_cast<const T*>(e.bias)[ch]);
+    if (e.scale) v *= to_f<T>(static_cast<const T*>(e.scale)[ch]);
+    if (e.shift) v += to_f<T>(static_cast<const T*>(e.shift)[ch]);
+    if (e.residual && e.residual_first) v += to_f<T>(static_cast<const T*>(e.residual)[yoff]);
+    v = apply_act(v, e.act);
+    if (e.residual && !e.residual_first) v += to_f<T>(static_cast<const T*>(e.residual)[yoff]);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core direct convolution
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void conv_direct_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, ConvGeom g,
+                                   ConvEpi e) {
+    const int64_t osp = (int64_t)g.od * g.oh * g.ow;
+    const int64_t total = (int64_t)g.n * g.batch * g.cout * osp;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t isp = (int64_t)g.d * g.h * g.w;
+    const int taps = g.kd * g.kh * g.kw;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        int64_t r = i;
+        const int ox = (int)(r % g.ow); r /= g.ow;
+        const int oy = (int)(r % g.oh); r /= g.oh;
+        const int oz = (int)(r % g.od); r /= g.od;
+        const int co = (int)(r % g.cout); r /= g.cout;
+        const int64_t img = r;                       // n_i * batch + b
+        const int64_t ni = img / g.batch;
+        const T* xi = x + img * g.cin * isp;
+        const T* wr = w + (ni * g.cout + co) * (int64_t)g.cin * taps;
+        float acc = 0.f;
+        for (int ci = 0; ci < g.cin; ++ci) {
+            const T* xc = xi + (int64_t)ci * isp;
+            const T* wc = wr + (int64_t)ci * taps;
+            for (int a = 0; a < g.kd; ++a) {
+                const int iz = oz * g.sd - g.pd + a * g.dd;
+                if (iz < 0 || iz >= g.d) continue;
+                for (int bb = 0; bb < g.kh; ++bb) {
+                    const int iy = oy * g.sh - g.ph + bb * g.dh;
+                    if (iy < 0 || iy >= g.h) continue;
+                    for (int cc = 0; cc < g.kw; ++cc) {
+                        const int ix = ox * g.sw - g.pw + cc * g.dw;
+                        if (ix < 0 || ix >= g.w) continue;
+                        acc = fmaf(to_f<T>(xc[((int64_t)iz * g.h + iy) * g.w + ix]),
+                                   to_f<T>(wc[(a * g.kh + bb) * g.kw + cc]), acc);
+                    }
+                }
+            }
+        }
+        y[i] = from_f<T>(conv_epilogue<T>(acc, ni * g.cout + co, i, e));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 implicit GEMM (2-D / 1-D, stride 1)
+// ---------------------------------------------------------------------------
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct ConvSmem {
+    static constexpr uint32_t A_BYTES = BM * BK * 2;
+    static constexpr uint32_t B_BYTES = BN * BK * 2;
+    static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
+    static constexpr uint32_t TOTAL = 1024 + RING + 8 * (2 * STAGES + 5) + 16;
+};
+
+struct ConvTcGeom {
+    int n, batch, cout, ho, wo, th, tw, tiles_h, tiles_w, nt_count;
+    int kh, kw, cblocks, ph, pw, dh, dw;
+};
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   T* __restrict__ y, ConvTcGeom g, ConvEpi e, int* err) {
+    using S = ConvSmem<BN, STAGES>;
+    constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+    constexpr uint32_t TMEM_COLS = 2 * BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * S::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt_count = g.tiles_h * g.tiles_w;
+    const int kb_count = g.kh * g.kw * g.cblocks;
+    const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * mt_count;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 4 * 32); }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0 && lane == 0) { tma_prefetch_desc(&tm_x); tma_prefetch_desc(&tm_w); }
+    if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // tile -> (model, n-tile, image-in-batch, m-tile); m-tile fastest.
+    auto decode = [&](int64_t tile, int& model, int& nt, int& b, int& mt) {
+        mt = (int)(tile % mt_count); tile /= mt_count;
+        b = (int)(tile % g.batch); tile /= g.batch;
+        nt = (int)(tile % g.nt_count);
+        model = (int)(tile / g.nt_count);
+    };
+
+    if (warp == 0) {
+        const uint64_t pol_x = l2_policy_evict_first();
+        const uint64_t pol_w = l2_policy_evict_last();
+        int s = 0, issued = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            int model, nt, b, mt;
+            decode(tile, model, nt, b, mt);
+            const int ho0 = (mt / g.tiles_w) * g.th;
+            const int wo0 = (mt % g.tiles_w) * g.tw;
+            const int img = model * g.batch + b;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                const int cb = kb % g.cblocks;
+                const int tap = kb / g.cblocks;
+                const int ky = tap / g.kw, kx = tap % g.kw;
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
+                    tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], cb * BK, wo0 - g.pw + kx * g.dw,
+                                ho0 - g.ph + ky * g.dh, img, pol_x);
+                    tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, nt * BN, model, pol_w);
+                }
+                __syncwarp();
+                ++issued;
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+            const int inflight = issued < STAGES ? issued : STAGES;
+            for (int j = 1; j <= inflight; ++j) {
+                const int idx = issued - j;
+                const volatile int never = 0;
+                mbar_wait(&full[idx % STAGES], (uint32_t)((idx / STAGES) & 1), &never);
+            }
+        }
+    } else if (warp == 1) {
+        int s = 0, local = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * BN;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a0 = smem_addr(sA + s * S::A_BYTES);
+                    const uint32_t b0 = smem_addr(sB + s * S::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), IDESC,
+                                    (kb | k) != 0);
+                    umma_commit(&empty[s]);
+                }
+                __syncwarp();
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+            if (!ok) break;
+            if (lane == 0) umma_commit(&tfull[acc]);
+            __syncwarp();
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+        }
+        if (lane == 0) umma_commit(done);
+        __syncwarp();
+        const volatile int never = 0;
+        mbar_wait(done, 0, &never);
+    } else {
+        const int q = warp & 3;
+        const int64_t osp = (int64_t)g.ho * g.wo;
+        int local = 0;
+        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            int model, nt, b, mt;
+            decode(tile, model, nt, b, mt);
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const int r = q * 32 + lane;                 // pixel within the tile
+            const int ho = (mt / g.tiles_w) * g.th + r / g.tw;
+            const int wo = (mt % g.tiles_w) * g.tw + r % g.tw;
+            const bool pix_ok = ho < g.ho && wo < g.wo;
+            const int64_t img = (int64_t)model * g.batch + b;
+            const int64_t pix = (int64_t)ho * g.wo + wo;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                const int co0 = nt * BN + c;
+                if (co0 >= g.cout) break;    // warp-uniform
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c) + ((uint32_t)(q * 32) << 16), v);
+                tmem_ld_wait();
+                if (pix_ok) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int co = co0 + j;
+                        if (co < g.cout) {
+                            const int64_t yoff = (img * g.cout + co) * osp + pix;
+                            const float val = conv_epilogue<T>(__uint_as_float(v[j]), (int64_t)model * g.cout + co,
+                                                               yoff, e);
+                            y[yoff] = from_f<T>(val);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+template <typename T>
+CUtensorMapDataType tmap_dt() {
+    return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+template <typename T, int BN, int STAGES>
+int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const ConvEpi& e, cudaStream_t st) {
+    using S = ConvSmem<BN, STAGES>;
+    ConvTcGeom g{};
+    g.n = cg.n; g.batch = cg.batch; g.cout = cg.cout; g.ho = cg.oh; g.wo = cg.ow;
+    int tw = 1;
+    while (tw < cg.ow && tw < BM) tw <<= 1;
+    g.tw = tw;
+    g.th = BM / tw;
+    g.tiles_h = (cg.oh + g.th - 1) / g.th;
+    g.tiles_w = (cg.ow + g.tw - 1) / g.tw;
+    g.nt_count = (cg.cout + BN - 1) / BN;
+    g.kh = cg.kh; g.kw = cg.kw; g.cblocks = cg.cin / BK;
+    g.ph = cg.ph; g.pw = cg.pw; g.dh = cg.dh; g.dw = cg.dw;
+    const int64_t nb = (int64_t)cg.n * cg.batch;
+    CUtensorMap tx, tw_map;
+    {
+        const uint64_t dims[4] = {(uint64_t)cg.cin, (uint64_t)cg.w, (uint64_t)cg.h, (uint64_t)nb};
+        const uint64_t strides[3] = {(uint64_t)cg.cin * 2, (uint64_t)cg.w * cg.cin * 2,
+                                     (uint64_t)cg.h * cg.w * cg.cin * 2};
+        const uint32_t box[4] = {BK, (uint32_t)g.tw, (uint32_t)g.th, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dt<T>(), 4, x_nhwc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t k = (uint64_t)cg.kh * cg.kw * cg.cin;
+        const uint64_t dims[3] = {k, (uint64_t)cg.cout, (uint64_t)cg.n};
+        const uint64_t strides[2] = {k * 2, (uint64_t)cg.cout * k * 2};
+        const uint32_t box[3] = {BK, BN, 1};
+        int rc = encode_tmap_tiled(&tw_map, tmap_dt<T>(), 3, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    auto kern = conv_tc_kernel<T, BN, STAGES>;
+    static bool attr_done[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "conv: cannot reserve %u bytes of shared memory", S::TOTAL);
+        attr_done[dev] = true;
+    }
+    const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * g.tiles_h * g.tiles_w;
+    const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
+    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw_map, y, g, e, device_error_ptr());
+    return check_launch("widek_conv_fwd (tcgen05)");
+}
+
+bool tc_eligible(const ConvGeom& g, int dtype) {
+    return (dtype == WIDEK_BF16 || dtype == WIDEK_F16) && g.d == 1 && g.kd == 1 && g.sh == 1 && g.sw == 1 &&
+           g.cin % 64 == 0 && g.cout % 16 == 0 && g.cout <= 4096 && g.h <= 65536 && g.w <= 65536;
+}
+
+struct ConvLaunch {
+    const void *x, *w, *wp;
+    void *y, *ws;
+    size_t ws_bytes;
+    ConvGeom g;
+    ConvEpi e;
+    int dtype;
+    cudaStream_t st;
+    template <typename T>
+    int run() {
+        if (wp && tc_eligible(g, dtype)) {
+            if constexpr (!std::is_same<T, float>::value) {
+                const int64_t nb = (int64_t)g.n * g.batch;
+                const size_t need = (size_t)nb * g.cin * g.h * g.w * sizeof(T);
+                if (ws && ws_bytes >= need && aligned16(ws) && aligned16(wp)) {
+                    const int64_t p = (int64_t)g.h * g.w;
+                    dim3 grid((unsigned)((p + 31) / 32), (unsigned)((g.cin + 31) / 32),
+                              (unsigned)std::min<int64_t>(nb, 65535));
+                    nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(static_cast<const T*>(x),
+                                                                         static_cast<T*>(ws), nb, g.cin, p);
+                    int rc = check_launch("widek_conv_fwd (nhwc staging)");
+                    if (rc) return rc;
+                    const T* xs = static_cast<const T*>(ws);
+                    const T* wpp = static_cast<const T*>(wp);
+                    T* yp = static_cast<T*>(y);
+                    if (g.cout <= 64) return launch_conv_tc<T, 64, 8>(xs, wpp, yp, g, e, st);
+                    if (g.cout <= 128) return launch_conv_tc<T, 128, 6>(xs, wpp, yp, g, e, st);
+                    return launch_conv_tc<T, 256, 4>(xs, wpp, yp, g, e, st);
+                }
+            }
+        }
+        const int64_t total = (int64_t)g.n * g.batch * g.cout * g.od * g.oh * g.ow;
+        conv_direct_kernel<T><<<grid_cap(total, 256), 256, 0, st>>>(static_cast<const T*>(x),
+                                                                    static_cast<const T*>(w), static_cast<T*>(y),
+                                                                    g, e);
+        return check_launch("widek_conv_fwd (direct)");
+    }
+};
+
+}  // namespace
+}  // namespace widek
+
+extern "C" {
+
+int widek_conv_pack_weight(const void* w, void* wp, int64_t rows, int64_t cin, int64_t taps, int64_t elem_bytes,
+                           void* stream) {
+    using namespace widek;
+    if (rows < 0 || cin < 0 || taps < 0) return set_error(WIDEK_ERR_INVALID, "conv_pack_weight: negative size");
+    if (rows * cin * taps == 0) return WIDEK_OK;
+    if (!w || !wp) return set_error(WIDEK_ERR_INVALID, "conv_pack_weight: null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t total = rows * cin * taps;
+    if (elem_bytes == 2)
+        pack_weight_kernel<uint16_t><<<grid_cap(total, 256), 256, 0, st>>>(
+            static_cast<const uint16_t*>(w), static_cast<uint16_t*>(wp), rows, cin, taps);
+    else if (elem_bytes == 4)
+        pack_weight_kernel<uint32_t><<<grid_cap(total, 256), 256, 0, st>>>(
+            static_cast<const uint32_t*>(w), static_cast<uint32_t*>(wp), rows, cin, taps);
+    else
+        return set_error(WIDEK_ERR_INVALID, "conv_pack_weight: element size %lld", (long long)elem_bytes);
+    return check_launch("widek_conv_pack_weight");
+}
+
+size_t widek_conv_workspace(int64_t n, int64_t batch, int64_t cin, int64_t d, int64_t h, int64_t w, int dtype) {
+    return (size_t)(n * batch * cin * d * h * w) * widek::dtype_size(dtype);
+}
+
+int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const void* bias, const void* scale,
+                   const void* shift, const void* residual, void* y, void* workspace, size_t workspace_bytes,
+                   const int64_t* geom, int act, int residual_first, int dtype, void* stream) {
+    using namespace widek;
+    if (!geom) return set_error(WIDEK_ERR_INVALID, "conv: null geometry");
+    ConvGeom g{};
+    int* f = &g.n;
+    for (int i = 0; i < 22; ++i) {
+        if (geom[i] < 0 || geom[i] > 0x7fffffff) return set_error(WIDEK_ERR_INVALID, "conv: geometry[%d] out of range", i);
+        f[i] = (int)geom[i];
+    }
+    if (g.kd < 1 || g.kh < 1 || g.kw < 1 || g.sd < 1 || g.sh < 1 || g.sw < 1 || g.dd < 1 || g.dh < 1 || g.dw < 1)
+        return set_error(WIDEK_ERR_INVALID, "conv: kernel/stride/dilation must be >= 1");
+    auto outsz = [](int in, int p, int d, int k, int s) { return (in + 2 * p - d * (k - 1) - 1) / s + 1; };
+    if (g.od != outsz(g.d, g.pd, g.dd, g.kd, g.sd) || g.oh != outsz(g.h, g.ph, g.dh, g.kh, g.sh) ||
+        g.ow != outsz(g.w, g.pw, g.dw, g.kw, g.sw))
+        return set_error(WIDEK_ERR_INVALID, "conv: output size does not match input/kernel/stride/padding");
+    if (act < WIDEK_ACT_NONE || act > WIDEK_ACT_GELU) return set_error(WIDEK_ERR_INVALID, "conv: bad activation");
+    if ((int64_t)g.n * g.batch * g.cout * g.od * g.oh * g.ow == 0) return WIDEK_OK;
+    if (!x || !w || !y) return set_error(WIDEK_ERR_INVALID, "conv: null pointer");
+    ConvEpi e{bias, scale, shift, residual, act, residual_first};
+    ConvLaunch L{x, w, w_packed, y, workspace, workspace_bytes, g, e, dtype, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+}  // extern "C"

@@ -392,3 +392,72 @@ def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optiona
     o = torch.empty(n, b, tq, d, device=dev, dtype=query.dtype)
     attention_core(q_t, k_t, v_t, n * b, heads, tq, tk, dh, sq, sk, sv, o, is_causal, attn_mask)
     return linear(o, mod.out_weight, mod.out_bias)
+
+
+# ---------------------------------------------------------------------------
+# Convolutions
+# ---------------------------------------------------------------------------
+
+def _packed_weight(weight: Tensor, rows: int, cin: int, taps: int, dev) -> Tensor:
+    """[rows, cin, taps] -> [rows, taps, cin] for the tensor-core conv, cached
+    on the weight tensor object and rebuilt when its version, storage or dtype
+    changes."""
+    key = (weight._version, weight.data_ptr(), weight.dtype, tuple(weight.shape))
+    hit = getattr(weight, '_widek_packed', None)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    wd = _dense(weight.detach())
+    wp = torch.empty(rows, taps, cin, device=dev, dtype=weight.dtype)
+    with _guard(dev):
+        rc = N.lib().widek_conv_pack_weight(wd.data_ptr(), wp.data_ptr(), rows, cin, taps, wd.element_size(),
+                                            N.stream_ptr(dev))
+    N.check(rc, "widek_conv_pack_weight")
+    try:
+        weight._widek_packed = (key, wp)
+    except (AttributeError, RuntimeError):
+        pass
+    return wp
+
+
+def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, padding, dilation,
+            scale: Optional[Tensor] = None, shift: Optional[Tensor] = None, residual: Optional[Tensor] = None,
+            act: int = ACT_NONE, residual_first: bool = False) -> Tensor:
+    """N independent convolutions on x [N, B, Cin, *S] (1-3 spatial dims) with
+    weight [N*Cout, Cin, *K]; returns [N, B, Cout, *S']. Optional fused
+    epilogue: per-channel scale/shift ([N*Cout]), activation, residual."""
+    dev = N.require_cuda(x, weight, bias, scale, shift, residual, what="WideConv")
+    _same_dtype("WideConv", weight, x, bias, scale, shift, residual)
+    nd = x.dim() - 3
+    if nd not in (1, 2, 3) or weight.dim() != nd + 2:
+        raise ValueError(f"WideConv: input {tuple(x.shape)} / weight {tuple(weight.shape)} rank mismatch")
+    nn_, batch, cin = x.shape[:3]
+    if nn_ != n or weight.shape[0] % n != 0 or weight.shape[1] != cin:
+        raise ValueError(f"WideConv: input {tuple(x.shape)} does not match weight {tuple(weight.shape)} for N={n}")
+    cout = weight.shape[0] // n
+    pad3 = lambda v, fill: (fill,) * (3 - nd) + tuple(v)
+    sp = pad3(x.shape[3:], 1)
+    ks = pad3(weight.shape[2:], 1)
+    st = pad3(stride, 1)
+    pd = pad3(padding, 0)
+    dl = pad3(dilation, 1)
+    out_sp = tuple((sp[i] + 2 * pd[i] - dl[i] * (ks[i] - 1) - 1) // st[i] + 1 for i in range(3))
+    if min(out_sp) <= 0:
+        raise ValueError(f"WideConv: output size {out_sp} is not positive")
+    y = torch.empty((n, batch, cout, *out_sp[3 - nd:]), device=dev, dtype=x.dtype)
+    xd = _dense(x)
+    geom = (ctypes.c_int64 * 22)(n, batch, cin, cout, *sp, *ks, *st, *pd, *dl, *out_sp)
+    wp = ws = None
+    tc = (x.dtype in (torch.bfloat16, torch.float16) and nd in (1, 2) and st == (1, 1, 1) and cin % 64 == 0
+          and cout % 16 == 0)
+    if tc:
+        taps = ks[0] * ks[1] * ks[2]
+        wp = _packed_weight(weight, n * cout, cin, taps, dev)
+        ws = torch.empty(int(N.lib().widek_conv_workspace(n, batch, cin, *sp, N.dtype_code(x))) // x.element_size(),
+                         device=dev, dtype=x.dtype)
+    with _guard(dev):
+        rc = N.lib().widek_conv_fwd(xd.data_ptr(), _dense(weight).data_ptr(), N.ptr(wp), N.ptr(bias), N.ptr(scale),
+                                    N.ptr(shift), N.ptr(_dense(residual) if residual is not None else None),
+                                    y.data_ptr(), N.ptr(ws), 0 if ws is None else ws.numel() * ws.element_size(),
+                                    geom, act, 1 if residual_first else 0, N.dtype_code(x), N.stream_ptr(dev))
+    N.check(rc, "widek_conv_fwd")
+    return y
