@@ -1,28 +1,32 @@
 """Benchmark of the wide forward path on B200 (one JSON line on rank 0).
 
-Workload (the headline config that fits one GPU):
-WideLinear, N=64 models per GPU, in=1024, out=4096, B=256 rows per model,
-bf16 weights/activations (W ~ N(0, 1/1024), bias zeros, x ~ N(0, 1)), fp32
-accumulation. A step is one wide forward over the whole batch: one launch of
-the tcgen05 grouped-GEMM kernel (bias fused in its epilogue).
+Default workload (the headline config that fits one
+GPU): WideLinear, N=64 models per GPU, in=1024, out=4096, B=256 rows per
+model, bf16 weights/activations (W ~ N(0, 1/1024), bias zeros, x ~ N(0, 1)),
+fp32 accumulation. A step is one wide forward over the whole batch: one
+launch of the tcgen05 grouped-GEMM kernel (bias fused in its epilogue).
 
   value   samples/s = N*B*world / t_step, t_step from CUDA events over K
           back-to-back steps with inputs resident in HBM (705 MB touched per
           step, far above the 126 MB L2, so no flush is needed); max over ranks.
-  e2e     same metric through the public API (``WideLinear.__call__``) with
-          the step's input copied host->device from pinned memory and the
-          output copied device->host inside the timed region.
-  roofline  HBM-bound (arithmetic intensity 195 FLOP/B < ridge): algorithmic
-          bytes per launch / mean launch time vs the measured HBM copy peak.
-  cpu_baseline  the reference's arithmetic (einsum + bias, bf16) on the host
-          cores, on a bounded sample (a few models per timed step).
+  e2e     same metric through the public API (the module's __call__) with the
+          step's input copied host->device from pinned memory and the output
+          copied device->host inside the timed region.
+  roofline  dominant kernel's algorithmic bytes (or FLOPs) per launch / mean
+          launch time (CUDA events on the launching stream) vs the measured
+          peak in MEASURED_PEAKS.json.
+  cpu_baseline  the reference's arithmetic (its torch op sequence in the
+          config dtype) on the host cores, on a bounded sample.
 
-Multi-GPU (torchrun, one process per GPU, NCCL): each rank runs its own 64
+Other BASELINE configs (``--workload cfg1|cfg3|cfg4gru|cfg4lstm|cfg5``) print
+the same line for that config; ``--graph`` replays the step from a CUDA graph.
+
+Multi-GPU (torchrun, one process per GPU, NCCL): each rank runs its own set of
 models (weak scaling; the N models are independent, no collective is on the
 data path). ``--gather`` adds the optional output all-gather to every step.
 
 ``--impl reference`` times the reference's CPU implementation of the path
-(the oracle port of its torch arithmetic) on rank 0 only.
+(the oracle's restatement of its torch op sequence) on rank 0 only.
 """
 from __future__ import annotations
 
@@ -40,35 +44,24 @@ sys.path.insert(0, os.path.join(ROOT, "pytorch-parallel-compiler_b200"))
 sys.path.insert(0, ROOT)
 
 import torch  # noqa: E402
+import torch.nn as nn  # noqa: E402
+import torch.nn.functional as F  # noqa: E402
 
 METRIC = "wide-forward samples/s (N·B/s) at 1/2/4/8 B200; % of TC/HBM roofline"
-N_MODELS, B_ROWS, IN_F, OUT_F = 64, 256, 1024, 4096
-DTYPE = torch.bfloat16
-ELEM = 2
 
-
-def alg_bytes(n):
-    """Compulsory HBM bytes per launch: W + x + y + bias, each touched once."""
-    return ELEM * (n * OUT_F * IN_F + n * B_ROWS * IN_F + n * B_ROWS * OUT_F + n * OUT_F)
-
-
-def alg_flops(n):
-    return 2 * n * B_ROWS * IN_F * OUT_F
-
-
-ALG_BYTES = alg_bytes(N_MODELS)
 # DRAM traffic (read + write bytes) per launch of linear_tc_kernel measured by
 # ncu on a 16-model capture scaled to 64 models; see profiles/linear_tc_cfg2.md.
-NCU_TRAFFIC_BYTES = 593_080_000  # 148.27 MB for 16 models x 64/16
+NCU_TRAFFIC_BYTES_CFG2 = 593_080_000
 
 
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return {"hbm": float(p["hbm_gbs"]), "tensor_burst": float(p["bf16_tflops"]),
+                "tensor_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "kind": "measured"}
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm": 6650.0, "tensor_burst": 1590.0, "tensor_sustained": 1400.0, "kind": "fallback"}
 
 
 class ClockSampler:
@@ -132,76 +125,371 @@ def dist_env():
     return world, rank, local
 
 
-def make_workload(dev, seed):
-    g = torch.Generator(device=dev).manual_seed(seed)
-    import wide_compiler as wc
-    lin = wc.WideLinear(N_MODELS, IN_F, OUT_F, bias=True)
-    with torch.no_grad():
-        w = (torch.randn(N_MODELS, OUT_F, IN_F, device=dev, generator=g) / (IN_F ** 0.5)).to(DTYPE)
-        lin = lin.to(dev, DTYPE)
-        lin.weight.copy_(w)
-        lin.bias.zero_()
-    x = torch.randn(N_MODELS, B_ROWS, IN_F, device=dev, generator=g).to(DTYPE)
-    return lin, x
-
-
-def cpu_baseline_sample(seconds: float = 10.0):
-    """The reference's arithmetic for this path (wide_linear.py:165-168: einsum
-    'noi,nbi->nbo' then + bias, in the config dtype) on the host cores, on a
-    bounded sample of models; returns samples/s and what was sampled."""
-    from oracle import wide_oracle as O
-    threads = len(os.sched_getaffinity(0))
-    torch.set_num_threads(threads)
-    n_s = 2
-    g = torch.Generator().manual_seed(0)
-    w = (torch.randn(n_s, OUT_F, IN_F, generator=g) / 32).to(DTYPE)
-    b = torch.zeros(n_s, OUT_F, dtype=DTYPE)
-    x = torch.randn(n_s, B_ROWS, IN_F, generator=g).to(DTYPE)
-    O.linear_ref_dtype(x, w, b)  # warm-up
+def _timed_cpu(fn, seconds):
+    fn()
     t0 = time.perf_counter()
     reps = 0
     while True:
-        O.linear_ref_dtype(x, w, b)
+        fn()
         reps += 1
         el = time.perf_counter() - t0
         if el >= seconds:
-            break
-    value = reps * n_s * B_ROWS / el
-    return {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} reps x {n_s} of the {N_MODELS} models (B={B_ROWS}, {IN_F}->{OUT_F}, bf16) "
-                      f"in {el:.1f} s, torch CPU einsum+bias"}
+            return reps, el
 
+
+# ---------------------------------------------------------------------------
+# Workloads
+# ---------------------------------------------------------------------------
+
+class Workload:
+    """One BASELINE config: builds the wide module and resident inputs on a
+    device, knows its per-step samples, algorithmic work and roofline."""
+    name = ""
+    dtype = "bf16"
+    bound = "hbm"            # roofline of the dominant kernel(s)
+    peak_key = "hbm"
+    launches_per_step = 1
+
+    def forward(self, x):
+        return self.module(x)
+
+    def traffic(self):
+        return None
+
+
+class LinearCfg2(Workload):
+    name = "cfg2"
+
+    def __init__(self, n=64, b=256, i=1024, o=4096):
+        self.n, self.b, self.i, self.o = n, b, i, o
+
+    def samples(self):
+        return self.n * self.b
+
+    def alg_bytes(self):
+        return 2 * (self.n * self.o * self.i + self.n * self.b * self.i + self.n * self.b * self.o + self.n * self.o)
+
+    def alg_flops(self):
+        return 2 * self.n * self.b * self.i * self.o
+
+    def traffic(self):
+        return int(NCU_TRAFFIC_BYTES_CFG2 * self.n / 64)
+
+    def config(self):
+        return {"workload": f"WideLinear cfg2: N={self.n} models/GPU, in={self.i}, out={self.o}, B={self.b}, "
+                            f"bf16, fp32 accumulate, bias fused",
+                "models_per_gpu": self.n, "rows_per_model": self.b, "in_features": self.i,
+                "out_features": self.o, "l2": "inputs larger than L2 (705 MB touched per step), no flush"}
+
+    def setup(self, dev, seed):
+        import wide_compiler as wc
+        g = torch.Generator(device=dev).manual_seed(seed)
+        lin = wc.WideLinear(self.n, self.i, self.o, bias=True).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(self.n, self.o, self.i, device=dev, generator=g) / self.i ** 0.5)
+            lin.bias.zero_()
+        self.module = lin
+        self.x = torch.randn(self.n, self.b, self.i, device=dev, generator=g).to(torch.bfloat16)
+
+    def cpu_sample(self, seconds):
+        from oracle import wide_oracle as O
+        n_s = 2
+        g = torch.Generator().manual_seed(0)
+        w = (torch.randn(n_s, self.o, self.i, generator=g) / 32).to(torch.bfloat16)
+        b = torch.zeros(n_s, self.o, dtype=torch.bfloat16)
+        x = torch.randn(n_s, self.b, self.i, generator=g).to(torch.bfloat16)
+        reps, el = _timed_cpu(lambda: O.linear_ref_dtype(x, w, b), seconds)
+        return reps * n_s * self.b / el, (f"{reps} reps x {n_s} of the {self.n} models (B={self.b}, "
+                                          f"{self.i}->{self.o}, bf16) in {el:.1f} s, torch CPU einsum+bias")
+
+
+class _MLP(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.fc1 = nn.Linear(64, 128)
+        self.fc2 = nn.Linear(128, 64)
+
+    def forward(self, x):
+        return self.fc2(F.relu(self.fc1(x)))
+
+
+class MlpCfg1(Workload):
+    name = "cfg1"
+    dtype = "fp32"
+    launches_per_step = 5
+
+    def __init__(self, n=100, b=32):
+        self.n, self.b = n, b
+
+    def samples(self):
+        return self.n * self.b
+
+    def alg_flops(self):
+        return 2 * self.n * self.b * (64 * 128 + 128 * 64)
+
+    def alg_bytes(self):
+        # whole-model compulsory bytes: x, W1, b1, W2, b2, y (fp32)
+        return 4 * self.n * (self.b * 64 + 128 * 64 + 128 + 64 * 128 + 64 + self.b * 64)
+
+    def config(self):
+        return {"workload": f"cfg1 TracedWideModel of N={self.n} MLPs (Linear 64->128, ReLU, Linear 128->64), "
+                            f"fp32, B={self.b}, packed input [{self.b}, {self.n * 64}]",
+                "l2": "small working set (8 MB) stays in L2 between steps"}
+
+    def setup(self, dev, seed):
+        import wide_compiler as wc
+        torch.manual_seed(seed)
+        models = [_MLP().to(dev) for _ in range(self.n)]
+        self.module = wc.compile(models, torch.randn(self.b, 64, device=dev))
+        self.x = torch.randn(self.b, self.n * 64, device=dev)
+
+    def cpu_sample(self, seconds):
+        from oracle import wide_oracle as O
+        g = torch.Generator().manual_seed(0)
+        w1 = torch.randn(self.n, 128, 64, generator=g) / 8
+        b1 = torch.zeros(self.n, 128)
+        w2 = torch.randn(self.n, 64, 128, generator=g) / 11
+        b2 = torch.zeros(self.n, 64)
+        x = torch.randn(self.b, self.n * 64, generator=g)
+
+        def run():
+            xn = x.view(self.b, self.n, 64).movedim(1, 0).contiguous()
+            y = O.mlp2_ref_dtype(xn, w1, b1, w2, b2)
+            return y.movedim(0, 1).reshape(self.b, -1)
+        reps, el = _timed_cpu(run, seconds)
+        return reps * self.samples() / el, f"{reps} full cfg1 forwards in {el:.1f} s (fp32, torch CPU)"
+
+
+class _ResBlock(nn.Module):
+    def __init__(self, c=64):
+        super().__init__()
+        self.conv1 = nn.Conv2d(c, c, 3, padding=1)
+        self.bn1 = nn.BatchNorm2d(c)
+        self.conv2 = nn.Conv2d(c, c, 3, padding=1)
+        self.bn2 = nn.BatchNorm2d(c)
+
+    def forward(self, x):
+        h = F.relu(self.bn1(self.conv1(x)))
+        return self.bn2(self.conv2(h)) + x
+
+
+class ResBlockCfg3(Workload):
+    name = "cfg3"
+    bound = "tensor"
+    peak_key = "tensor_sustained"
+    launches_per_step = 9
+
+    def __init__(self, n=100, b=32, c=64, hw=32):
+        self.n, self.b, self.c, self.hw = n, b, c, hw
+
+    def samples(self):
+        return self.n * self.b
+
+    def alg_flops(self):
+        return 2 * 2 * self.n * self.b * self.hw * self.hw * self.c * self.c * 9
+
+    def alg_bytes(self):
+        return 2 * 2 * self.n * self.b * self.c * self.hw * self.hw   # fused block: x in, y out (bf16)
+
+    def config(self):
+        return {"workload": f"cfg3 TracedWideModel of N={self.n} ResBlocks (Conv3x3 {self.c}->{self.c} pad 1, BN "
+                            f"eval, ReLU, Conv3x3, BN, + identity), B={self.b}, {self.hw}x{self.hw}, bf16",
+                "l2": "inputs larger than L2 (419 MB activation per step), no flush"}
+
+    def setup(self, dev, seed):
+        import wide_compiler as wc
+        torch.manual_seed(seed)
+        models = []
+        for _ in range(self.n):
+            m = _ResBlock(self.c)
+            with torch.no_grad():
+                for bn in (m.bn1, m.bn2):
+                    bn.running_mean.normal_(0, 1)
+                    bn.running_var.uniform_(0.5, 2.0)
+                    bn.weight.uniform_(0.5, 1.5)
+                    bn.bias.normal_(0, 0.1)
+            models.append(m.to(dev, torch.bfloat16).eval())
+        self.module = wc.compile(models, torch.randn(2, self.c, self.hw, self.hw, device=dev,
+                                                     dtype=torch.bfloat16)).eval()
+        self.x = torch.randn(self.b, self.n * self.c, self.hw, self.hw, device=dev).to(torch.bfloat16)
+
+    def cpu_sample(self, seconds):
+        from oracle import wide_oracle as O
+        n_s, c = 1, self.c
+        g = torch.Generator().manual_seed(0)
+        bf = torch.bfloat16
+
+        def mk(*s, sc=1.0):
+            return (torch.randn(*s, generator=g) * sc).to(bf)
+
+        def bn():
+            return {'running_mean': mk(n_s * c), 'running_var': (torch.rand(n_s * c, generator=g) + 0.5).to(bf),
+                    'weight': (torch.rand(n_s * c, generator=g) + 0.5).to(bf), 'bias': mk(n_s * c, sc=0.1)}
+        c1w, c2w = mk(n_s * c, c, 3, 3, sc=1 / 24), mk(n_s * c, c, 3, 3, sc=1 / 24)
+        c1b, c2b = mk(n_s * c, sc=0.1), mk(n_s * c, sc=0.1)
+        bn1, bn2 = bn(), bn()
+        x = mk(n_s, self.b, c, self.hw, self.hw)
+        reps, el = _timed_cpu(lambda: O.resblock_ref_dtype(x, c1w, c1b, bn1, c2w, c2b, bn2), seconds)
+        return reps * n_s * self.b / el, (f"{reps} reps x {n_s} of the {self.n} ResBlocks (B={self.b}, bf16) in "
+                                          f"{el:.1f} s, torch CPU grouped conv + BN")
+
+
+class RnnCfg4(Workload):
+    dtype = "fp32"
+    launches_per_step = 2
+
+    def __init__(self, kind, n=32, b=4, t=32, i=64, h=128):
+        self.kind, self.n, self.b, self.t, self.i, self.h = kind, n, b, t, i, h
+        self.name = f"cfg4{kind}"
+        self.g = 3 if kind == "gru" else 4
+
+    def samples(self):
+        return self.n * self.b
+
+    def alg_flops(self):
+        return 2 * self.n * self.b * self.t * self.g * self.h * (self.i + self.h)
+
+    def alg_bytes(self):
+        return 4 * self.n * (self.b * self.t * (self.i + self.h) + self.g * self.h * (self.i + self.h)
+                             + 2 * self.g * self.h)
+
+    def config(self):
+        return {"workload": f"cfg4 Wide{self.kind.upper()} N={self.n}, input {self.i}, hidden {self.h}, B={self.b}, "
+                            f"T={self.t}, fp32 (TF32 off)",
+                "l2": "small working set stays in L2 between steps"}
+
+    def setup(self, dev, seed):
+        import wide_compiler as wc
+        torch.manual_seed(seed)
+        cls = nn.GRU if self.kind == "gru" else nn.LSTM
+        mods = [cls(self.i, self.h, batch_first=True) for _ in range(self.n)]
+        wcls = wc.WideGRU if self.kind == "gru" else wc.WideLSTM
+        self.module = wcls.from_modules(mods).to(dev)
+        self.x = torch.randn(self.n, self.b, self.t, self.i, device=dev)
+
+    def forward(self, x):
+        return self.module(x)[0]
+
+    def cpu_sample(self, seconds):
+        from oracle import wide_oracle as O
+        g = torch.Generator().manual_seed(0)
+        s = 1 / self.h ** 0.5
+
+        def u(*shape):
+            return (torch.rand(*shape, generator=g) * 2 - 1) * s
+        wih, whh = u(self.n, self.g * self.h, self.i), u(self.n, self.g * self.h, self.h)
+        bih, bhh = u(self.n, self.g * self.h), u(self.n, self.g * self.h)
+        x = torch.randn(self.n, self.b, self.t, self.i, generator=g)
+        fn = O.gru_ref_dtype if self.kind == "gru" else O.lstm_ref_dtype
+        reps, el = _timed_cpu(lambda: fn(x, wih, whh, bih, bhh), seconds)
+        return reps * self.samples() / el, f"{reps} full cfg4 {self.kind} forwards in {el:.1f} s (fp32, torch CPU)"
+
+
+class AttnCfg5(Workload):
+    name = "cfg5"
+    bound = "tensor"
+    peak_key = "tensor_sustained"
+    launches_per_step = 4
+
+    def __init__(self, n=16, b=8, t=1024, d=512, heads=8):
+        self.n, self.b, self.t, self.d, self.heads = n, b, t, d, heads
+
+    def samples(self):
+        return self.n * self.b
+
+    def alg_flops(self):
+        proj = 2 * self.n * self.b * self.t * self.d * self.d * 4
+        core = 2 * 2 * self.n * self.b * self.heads * (self.t * self.t // 2) * (self.d // self.heads)
+        return proj + core
+
+    def alg_bytes(self):
+        act = self.n * self.b * self.t * self.d * 2
+        return act * 2 + 4 * self.n * self.d * self.d * 2 + act * 2     # x, y, weights, LN read + write
+
+    def config(self):
+        return {"workload": f"cfg5 WideAttention N={self.n}, d_model={self.d}, {self.heads} heads, causal, "
+                            f"B={self.b}, T={self.t}, bf16, followed by WideLayerNorm({self.d})",
+                "l2": "inputs larger than L2 (134 MB activation, ~0.5 GB of intermediates per step), no flush"}
+
+    def setup(self, dev, seed):
+        import wide_compiler as wc
+        torch.manual_seed(seed)
+        a = wc.WideAttention(self.n, self.d, self.heads)
+        with torch.no_grad():
+            for p in (a.q_weight, a.kv_weight, a.out_weight):
+                p.normal_(0, 0.02)
+            a.q_bias.zero_()
+            a.kv_bias.zero_()
+            a.out_bias.zero_()
+        self.attn = a.to(dev, torch.bfloat16).eval()
+        self.ln = wc.WideLayerNorm(self.n, self.d).to(dev, torch.bfloat16)
+        self.module = self.attn
+        self.x = torch.randn(self.n, self.b, self.t, self.d, device=dev).to(torch.bfloat16)
+
+    def forward(self, x):
+        return self.ln(self.attn(x, is_causal=True))
+
+    def cpu_sample(self, seconds):
+        from oracle import wide_oracle as O
+        n_s = 1
+        g = torch.Generator().manual_seed(0)
+        bf = torch.bfloat16
+        wq = (torch.randn(n_s, self.d, self.d, generator=g) * 0.02).to(bf)
+        wkv = (torch.randn(n_s, 2 * self.d, self.d, generator=g) * 0.02).to(bf)
+        wo = (torch.randn(n_s, self.d, self.d, generator=g) * 0.02).to(bf)
+        lw, lb = torch.ones(n_s * self.d, dtype=bf), torch.zeros(n_s * self.d, dtype=bf)
+        x = torch.randn(n_s, self.b, self.t, self.d, generator=g).to(bf)
+        reps, el = _timed_cpu(lambda: O.attention_ln_ref_dtype(x, wq, wkv, wo, self.heads, lw, lb), seconds)
+        return reps * n_s * self.b / el, (f"{reps} reps x {n_s} of the {self.n} models (B={self.b}, T={self.t}, "
+                                          f"bf16) in {el:.1f} s, torch CPU einsum + SDPA + LN")
+
+
+def make_workload(name, models=None):
+    if name == "cfg2":
+        return LinearCfg2(n=models or 64)
+    if name == "cfg1":
+        return MlpCfg1()
+    if name == "cfg3":
+        return ResBlockCfg3()
+    if name == "cfg4gru":
+        return RnnCfg4("gru")
+    if name == "cfg4lstm":
+        return RnnCfg4("lstm")
+    if name == "cfg5":
+        return AttnCfg5()
+    raise ValueError(name)
+
+
+# ---------------------------------------------------------------------------
+# Arms
+# ---------------------------------------------------------------------------
 
 def run_reference(args):
+    """The reference's CPU path for the chosen workload, rank 0 only; each
+    step is one bounded sample of the workload."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    from oracle import wide_oracle as O
+    wl = make_workload(args.workload, args.models)
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    n_s = 1
-    g = torch.Generator().manual_seed(0)
-    w = (torch.randn(N_MODELS, OUT_F, IN_F, generator=g) / 32).to(DTYPE)
-    b = torch.zeros(N_MODELS, OUT_F, dtype=DTYPE)
-    x = torch.randn(N_MODELS, B_ROWS, IN_F, generator=g).to(DTYPE)
-    for s in range(args.warmup):
-        i = s % N_MODELS
-        O.linear_ref_dtype(x[i:i + n_s], w[i:i + n_s], b[i:i + n_s])
+    per_step_s = max(0.0, args.ref_step_seconds)
+    for _ in range(args.warmup):
+        wl.cpu_sample(per_step_s)
+    vals, desc = [], ""
     t0 = time.perf_counter()
-    for s in range(args.steps):
-        i = s % N_MODELS
-        O.linear_ref_dtype(x[i:i + n_s], w[i:i + n_s], b[i:i + n_s])
+    for _ in range(args.steps):
+        v, desc = wl.cpu_sample(per_step_s)
+        vals.append(v)
     el = time.perf_counter() - t0
-    value = args.steps * n_s * B_ROWS / el
+    value = statistics.median(vals)
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * el / max(args.steps, 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"WideLinear cfg2 sample: {n_s} of {N_MODELS} models per step, B={B_ROWS}, "
-                               f"{IN_F}->{OUT_F}, bf16 (reference arithmetic on host CPU)"},
-        "impl": "reference",
+        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+        "config": wl.config(), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-                         "sample": f"{n_s} model x {B_ROWS} rows per step, {args.steps} steps"},
+                         "sample": f"median over steps; last step: {desc}"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -215,20 +503,22 @@ def run_b200(args):
     pg = False
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = True
-    from wide_compiler import _native, ops
+    from wide_compiler import _native
     _native.load()
-    lin, x = make_workload(dev, seed=1234 + rank)
-    out_gather = None
-    if args.gather and world > 1:
-        out_gather = torch.empty(world * N_MODELS, B_ROWS, OUT_F, device=dev, dtype=DTYPE)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    wl = make_workload(args.workload, args.models)
+    wl.setup(dev, seed=1234 + rank)
+    x = wl.x
+    gather = args.gather and world > 1
 
     def step():
-        y = ops.linear(x, lin.weight, lin.bias)
-        if out_gather is not None:
-            torch.distributed.all_gather_into_tensor(out_gather, y)
+        y = wl.forward(x)
+        if gather:
+            from wide_compiler import parallel
+            parallel.gather_outputs(y, y.shape[0] * world)
         return y
 
     def barrier():
@@ -236,18 +526,31 @@ def run_b200(args):
             torch.distributed.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
+    run = step
+    graph = None
+    if args.graph:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        run = graph.replay
+
     clocks = ClockSampler(local)
     clocks.start()
-    # Warm-up (untimed); also spins clocks up before the timed region.
     for _ in range(max(args.warmup, 3)):
-        step()
+        run()
     barrier()
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        run()
     e1.record(stream)
     barrier()
     ms = e0.elapsed_time(e1) / args.steps
@@ -257,21 +560,23 @@ def run_b200(args):
     ms_max = float(t.item())
 
     # End to end through the public API: pinned host input -> device ->
-    # WideLinear forward -> host output, every step.
+    # forward -> host output, every step.
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     x_host = x.cpu().pin_memory()
-    y_host = torch.empty(N_MODELS, B_ROWS, OUT_F, dtype=DTYPE).pin_memory()
+    y0 = wl.forward(x)
+    y_host = torch.empty(y0.shape, dtype=y0.dtype).pin_memory()
     x_dev = torch.empty_like(x)
     for _ in range(2):
         x_dev.copy_(x_host, non_blocking=True)
-        y_host.copy_(lin(x_dev), non_blocking=True)
+        y_host.copy_(wl.forward(x_dev), non_blocking=True)
     barrier()
     e0.record(stream)
     for _ in range(e2e_steps):
         x_dev.copy_(x_host, non_blocking=True)
-        y = lin(x_dev)
-        if out_gather is not None:
-            torch.distributed.all_gather_into_tensor(out_gather, y)
+        y = wl.forward(x_dev)
+        if gather:
+            from wide_compiler import parallel
+            parallel.gather_outputs(y, y.shape[0] * world)
         y_host.copy_(y, non_blocking=True)
     e1.record(stream)
     barrier()
@@ -282,46 +587,45 @@ def run_b200(args):
     ms_e2e = float(t2.item())
     clk = clocks.stop()
     dev_err = _native.device_error()
+    del graph
 
     if rank == 0:
-        samples = N_MODELS * B_ROWS * world
-        peak, peak_kind = peaks()
-        achieved = alg_bytes(N_MODELS) / (ms * 1e-3) / 1e9
+        samples = wl.samples() * world
+        pk = peaks()
+        if wl.bound == "hbm":
+            achieved = wl.alg_bytes() / (ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
+                    "frac": achieved / pk["hbm"], "peak_kind": f"{pk['kind']} HBM copy",
+                    "traffic": wl.traffic(), "algorithmic_bytes": wl.alg_bytes(),
+                    "tflops": wl.alg_flops() / (ms * 1e-3) / 1e12}
+        else:
+            achieved = wl.alg_flops() / (ms * 1e-3) / 1e12
+            peak = pk[wl.peak_key]
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "peak_kind": f"{pk['kind']} bf16 dense ({wl.peak_key})",
+                    "traffic": wl.traffic(), "algorithmic_flops": wl.alg_flops(),
+                    "gbs": wl.alg_bytes() / (ms * 1e-3) / 1e9}
+        cfg = wl.config()
+        cfg["gather"] = bool(gather)
+        cfg["cuda_graph"] = bool(args.graph)
         line = {
-            "metric": METRIC,
-            "value": samples / (ms_max * 1e-3),
-            "unit": "samples/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms_max,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic",
-            "config": {
-                "workload": f"WideLinear cfg2: N={N_MODELS} models/GPU, in={IN_F}, out={OUT_F}, B={B_ROWS}, "
-                            f"bf16, fp32 accumulate, bias fused",
-                "models_per_gpu": N_MODELS, "rows_per_model": B_ROWS, "in_features": IN_F,
-                "out_features": OUT_F, "l2": "inputs larger than L2 (705 MB touched per step), no flush",
-                "gather": bool(out_gather is not None),
-            },
+            "metric": METRIC, "value": samples / (ms_max * 1e-3), "unit": "samples/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic", "config": cfg,
             "e2e": {"value": samples / (ms_e2e * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
                     "steps": e2e_steps, "ms_per_step": ms_e2e},
-            "gpu_launches": args.steps,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_BYTES,
-                         "algorithmic_bytes": alg_bytes(N_MODELS),
-                         "tflops": alg_flops(N_MODELS) / (ms * 1e-3) / 1e12},
+            "gpu_launches": args.steps * wl.launches_per_step,
+            "roofline": roof,
             "clocks": clk,
             "device_error": dev_err,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
+            torch.set_num_threads(len(os.sched_getaffinity(0)))
+            v, desc = wl.cpu_sample(args.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": torch.get_num_threads(),
+                                    "kind": "port", "sample": desc}
         print(json.dumps(line), flush=True)
     if pg:
         torch.distributed.barrier(device_ids=[local])
@@ -330,22 +634,24 @@ def run_b200(args):
 
 
 def main():
-    global N_MODELS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4gru", "cfg4lstm", "cfg5"])
+    ap.add_argument("--models", type=int, default=None,
+                    help="cfg2 models per GPU (default 64; smaller only for profiling captures)")
     ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--graph", action="store_true", help="replay each step from a CUDA graph")
     ap.add_argument("--gather", action="store_true", help="include the optional output all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=0.02,
+                    help="reference arm: minimum CPU time of one step's bounded sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--models", type=int, default=N_MODELS,
-                    help="models per GPU (default: the cfg2 value 64; smaller only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    N_MODELS = args.models
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -323,3 +323,84 @@ def linear_ref_dtype(x: Tensor, weight: Tensor, bias: Optional[Tensor]) -> Tenso
     if bias is not None:
         out = out + bias.unsqueeze(1)
     return out
+
+
+# ---------------------------------------------------------------------------
+# The reference's own op sequences in the storage dtype, for timing the
+# reference's CPU path in bench.py (not parity checkers).
+# ---------------------------------------------------------------------------
+def mlp2_ref_dtype(x_nfirst: Tensor, w1, b1, w2, b2) -> Tensor:
+    """TracedWideModel MLP stages: WideLinear (einsum + bias), F.relu, WideLinear."""
+    return linear_ref_dtype(torch.relu(linear_ref_dtype(x_nfirst, w1, b1)), w2, b2)
+
+
+def resblock_ref_dtype(x: Tensor, c1w, c1b, bn1, c2w, c2b, bn2) -> Tensor:
+    """WideConv2d (permute + grouped conv, wide_conv2d.py:169-194),
+    WideBatchNorm2d eval (wide_batchnorm_2d.py:53-72), ReLU, conv, BN, + x."""
+    n, b, c, h, w = x.shape
+
+    def conv(t, wt, bs):
+        p = t.permute(1, 0, 2, 3, 4).reshape(b, n * c, h, w)
+        o = F.conv2d(p, wt, bs, padding=1, groups=n)
+        return o.view(b, n, c, h, w).permute(1, 0, 2, 3, 4).contiguous()
+
+    def bn(t, prm):
+        p = t.permute(1, 0, 2, 3, 4).reshape(b, n * c, h, w)
+        o = F.batch_norm(p, prm['running_mean'], prm['running_var'], prm['weight'], prm['bias'], False, 0.0, 1e-5)
+        return o.view(b, n, c, h, w).permute(1, 0, 2, 3, 4).contiguous()
+
+    hdn = torch.relu(bn(conv(x, c1w, c1b), bn1))
+    return bn(conv(hdn, c2w, c2b), bn2) + x
+
+
+def gru_ref_dtype(x, w_ih, w_hh, b_ih, b_hh):
+    """wide_gru.py:148-213 op sequence in the input dtype."""
+    n, b, t, _ = x.shape
+    hsz = w_hh.shape[2]
+    gx = torch.einsum('nbti,ngi->nbtg', x, w_ih) + b_ih.view(n, 1, 1, -1)
+    h = torch.zeros(n, b, hsz, dtype=x.dtype)
+    outs = []
+    for s in range(t):
+        gh = torch.einsum('nbh,ngh->nbg', h, w_hh) + b_hh.view(n, 1, -1)
+        xr, xz, xn = gx[:, :, s].chunk(3, dim=-1)
+        hr, hz, hn = gh.chunk(3, dim=-1)
+        r = torch.sigmoid(xr + hr)
+        z = torch.sigmoid(xz + hz)
+        h = (1 - z) * torch.tanh(xn + r * hn) + z * h
+        outs.append(h)
+    return torch.stack(outs, dim=2), h
+
+
+def lstm_ref_dtype(x, w_ih, w_hh, b_ih, b_hh):
+    """wide_lstm.py:158-234 op sequence (diagonal blocks) in the input dtype."""
+    n, b, t, _ = x.shape
+    hsz = w_hh.shape[2]
+    gx = torch.einsum('nbti,ngi->nbtg', x, w_ih) + b_ih.view(n, 1, 1, -1)
+    h = torch.zeros(n, b, hsz, dtype=x.dtype)
+    c = torch.zeros(n, b, hsz, dtype=x.dtype)
+    outs = []
+    for s in range(t):
+        g = gx[:, :, s] + torch.einsum('nbh,ngh->nbg', h, w_hh) + b_hh.view(n, 1, -1)
+        i_, f_, g_, o_ = g.chunk(4, dim=-1)
+        c = torch.sigmoid(f_) * c + torch.sigmoid(i_) * torch.tanh(g_)
+        h = torch.sigmoid(o_) * torch.tanh(c)
+        outs.append(h)
+    return torch.stack(outs, dim=2), (h, c)
+
+
+def attention_ln_ref_dtype(x, q_weight, kv_weight, out_weight, heads, ln_w, ln_b, eps=1e-5):
+    """wide_attention.py:178-238 (einsum projections, head split,
+    F.scaled_dot_product_attention causal, merge, out projection) followed by
+    wide_layernorm.py:41-67, in the input dtype (biases are zero in cfg5)."""
+    n, b, t, d = x.shape
+    dh = d // heads
+    q = torch.einsum('nbtd,nod->nbto', x, q_weight)
+    k = torch.einsum('nbtd,nod->nbto', x, kv_weight[:, :d])
+    v = torch.einsum('nbtd,nod->nbto', x, kv_weight[:, d:])
+    sp = lambda u: u.view(n, b, t, heads, dh).permute(0, 1, 3, 2, 4).reshape(n * b, heads, t, dh)
+    o = F.scaled_dot_product_attention(sp(q), sp(k), sp(v), is_causal=True)
+    o = o.view(n, b, heads, t, dh).permute(0, 1, 3, 2, 4).reshape(n, b, t, d)
+    y = torch.einsum('nbtd,nod->nbto', o, out_weight)
+    mean = y.mean(dim=-1, keepdim=True)
+    var = y.var(dim=-1, unbiased=False, keepdim=True)
+    return (y - mean) / torch.sqrt(var + eps) * ln_w.view(n, 1, 1, d) + ln_b.view(n, 1, 1, d)
