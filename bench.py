@@ -507,6 +507,7 @@ def run_b200(args):
         pg = True
     from wide_compiler import _native
     _native.load()
+    _native.check(_native.lib().widek_linear_set_variant(args.linear_variant), "widek_linear_set_variant")
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     wl = make_workload(args.workload, args.models)
@@ -608,6 +609,7 @@ def run_b200(args):
         cfg = wl.config()
         cfg["gather"] = bool(gather)
         cfg["cuda_graph"] = bool(args.graph)
+        cfg["linear_variant"] = "CTA-pair tiles" if args.linear_variant == 2 else "single-CTA tiles"
         line = {
             "metric": METRIC, "value": samples / (ms_max * 1e-3), "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
@@ -649,6 +651,8 @@ def main():
     ap.add_argument("--ref-step-seconds", type=float, default=0.02,
                     help="reference arm: minimum CPU time of one step's bounded sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--linear-variant", type=int, default=0,
+                    help="tensor-core GEMM tiling: 0 auto (single-CTA), 1 single-CTA tiles, 2 CTA-pair tiles")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -85,6 +85,13 @@ WIDEK_API int widek_linear_fwd_simt(const void* x, const void* w, const void* bi
                           int64_t n, int64_t m, int64_t k, int64_t o,
                           int dtype, int act, void* stream);
 
+/* Selects the tensor-core tiling of widek_linear_fwd for this process:
+ * 0 = automatic (single-CTA 128xBN tiles), 1 = single-CTA tiles,
+ * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128.
+ * A measurement knob (process-wide, not synchronized with running calls).
+ * No counterpart in the reference. */
+WIDEK_API int widek_linear_set_variant(int variant);
+
 /* ---- WideLayerNorm ----------------------------------------------------- */
 
 /* Per-row LayerNorm over the last dim d with per-model affine:

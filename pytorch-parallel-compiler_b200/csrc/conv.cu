@@ -22,6 +22,8 @@
 //     (folded BatchNorm), an activation and a residual add.
 // CUDA-core path (everything else, including fp32): direct convolution, one
 // output element per thread, fp32 accumulation.
+#include <cstring>
+
 #include "sm100_ptx.cuh"
 
 namespace widek {
@@ -32,7 +34,7 @@ using namespace sm100;
 // ---------------------------------------------------------------------------
 // Layout helpers
 // ---------------------------------------------------------------------------
-// [nb][c][p] -> [nb][p][c], 32x32 tiles through shared memory.
+// [nb][c][p] -> [nb][p][c], 32x32 tiles through shared memory (any c, p).
 template <typename T>
 __global__ void nchw_to_nhwc_kernel(const T* __restrict__ src, T* __restrict__ dst, int64_t nb, int c, int64_t p) {
     __shared__ T tile[32][33];
@@ -52,6 +54,55 @@ __global__ void nchw_to_nhwc_kernel(const T* __restrict__ src, T* __restrict__ d
             const int64_t pp = p0 + r;
             const int cc = c0 + tx;
             if (cc < c && pp < p) d[pp * c + cc] = tile[tx][r];
+        }
+        __syncthreads();
+    }
+}
+
+// 16-bit [nb][c][p] -> [nb][p][c] for c % 64 == 0 and p % 64 == 0: 64x64
+// tiles, 16-byte loads along p and 16-byte stores along c. `packed_b` > 0
+// means the source is the channel-packed [b][n][c][p] layout (image
+// img = n * packed_b + b), so the unpack of a TracedWideModel input is fused.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_vec_kernel(const uint16_t* __restrict__ src,
+                                                               uint16_t* __restrict__ dst, int64_t nb, int c,
+                                                               int64_t p, int64_t packed_b, int64_t packed_n) {
+    __shared__ uint16_t tile[64][64 + 2];
+    const int t = threadIdx.x;
+    const int64_t tiles_p = p / 64, tiles_c = c / 64;
+    const int64_t total = nb * tiles_c * tiles_p;
+    for (int64_t job = blockIdx.x; job < total; job += gridDim.x) {
+        const int64_t tp = job % tiles_p;
+        const int64_t rest = job / tiles_p;
+        const int64_t tc = rest % tiles_c;
+        const int64_t img = rest / tiles_c;
+        int64_t src_img = img;
+        if (packed_b > 0) {
+            const int64_t n_i = img / packed_b, b_i = img % packed_b;
+            src_img = b_i * packed_n + n_i;
+        }
+        const uint16_t* s = src + (src_img * c + tc * 64) * p + tp * 64;
+        uint16_t* d = dst + (img * p + tp * 64) * c + tc * 64;
+        // load: 64 channel rows x 8 chunks of 8 pixels
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int chunk = t + 256 * i;
+            const int row = chunk >> 3, col = (chunk & 7) * 8;
+            const uint4 v = *reinterpret_cast<const uint4*>(s + (int64_t)row * p + col);
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tile[row][col + j] = e[j];
+        }
+        __syncthreads();
+        // store: 64 pixel rows x 8 chunks of 8 channels
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int chunk = t + 256 * i;
+            const int pix = chunk >> 3, ch = (chunk & 7) * 8;
+            uint4 v;
+            uint16_t* e = reinterpret_cast<uint16_t*>(&v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) e[j] = tile[ch + j][pix];
+            *reinterpret_cast<uint4*>(d + (int64_t)pix * c + ch) = v;
         }
         __syncthreads();
     }
@@ -164,18 +215,32 @@ struct ConvSmem {
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
-    static constexpr uint32_t TOTAL = 1024 + RING + 8 * (2 * STAGES + 5) + 16;
+    static constexpr uint32_t STAGE_OUT = BM * BN * 2;   // output tile staged for the TMA store
+    static constexpr uint32_t BARS = 8 * (2 * STAGES + 5) + 16;
+    static constexpr uint32_t TOTAL = 1024 + RING + STAGE_OUT + BARS;
 };
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct ConvTcGeom {
     int n, batch, cout, ho, wo, th, tw, tiles_h, tiles_w, nt_count;
     int kh, kw, cblocks, ph, pw, dh, dw;
 };
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool TMA_STORE>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                   T* __restrict__ y, ConvTcGeom g, ConvEpi e, int* err) {
+                   const __grid_constant__ CUtensorMap tm_y, T* __restrict__ y, ConvTcGeom g, ConvEpi e, int* err) {
     using S = ConvSmem<BN, STAGES>;
     constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
     constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -183,7 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * S::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING);
+    T* sOut = reinterpret_cast<T*>(smem + S::RING);      // [BN][BM] output tile (TMA store source)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::STAGE_OUT);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -203,7 +269,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         mbar_init_fence();
     }
-    if (warp == 0 && lane == 0) { tma_prefetch_desc(&tm_x); tma_prefetch_desc(&tm_w); }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+        if (TMA_STORE) tma_prefetch_desc(&tm_y);
+    }
     if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
@@ -294,8 +364,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const volatile int never = 0;
         mbar_wait(done, 0, &never);
     } else {
+        // Epilogue: warps 2..5, TMEM lane quarter q = warp % 4 (pixels
+        // q*32 .. q*32+31 of the tile). Per 32-channel chunk, lane j fetches
+        // the per-channel parameters of channel co0 + j once; the values are
+        // broadcast with shuffles.
         const int q = warp & 3;
+        const int ep_tid = threadIdx.x - 64;            // 0..127
         const int64_t osp = (int64_t)g.ho * g.wo;
+        const T* bias = static_cast<const T*>(e.bias);
+        const T* scale = static_cast<const T*>(e.scale);
+        const T* shift = static_cast<const T*>(e.shift);
+        const T* res = static_cast<const T*>(e.residual);
         int local = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             int model, nt, b, mt;
@@ -309,34 +388,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const int r = q * 32 + lane;                 // pixel within the tile
-            const int ho = (mt / g.tiles_w) * g.th + r / g.tw;
-            const int wo = (mt % g.tiles_w) * g.tw + r % g.tw;
+            const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
+            const int ho = ho0 + r / g.tw;
+            const int wo = wo0 + r % g.tw;
             const bool pix_ok = ho < g.ho && wo < g.wo;
             const int64_t img = (int64_t)model * g.batch + b;
             const int64_t pix = (int64_t)ho * g.wo + wo;
+            if (TMA_STORE) {
+                // the previous tile's store must have finished reading sOut
+                if (ep_tid == 0) bulk_wait_read0();
+                epi_bar_sync();
+            }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 const int co0 = nt * BN + c;
                 if (co0 >= g.cout) break;    // warp-uniform
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c) + ((uint32_t)(q * 32) << 16), v);
+                const int my_co = co0 + lane;
+                const int64_t my_ch = (int64_t)model * g.cout + (my_co < g.cout ? my_co : 0);
+                const float pb = bias ? to_f<T>(bias[my_ch]) : 0.f;
+                const float ps = scale ? to_f<T>(scale[my_ch]) : 1.f;
+                const float pt = shift ? to_f<T>(shift[my_ch]) : 0.f;
                 tmem_ld_wait();
-                if (pix_ok) {
+                const int64_t ybase = (img * g.cout + co0) * osp + pix;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int co = co0 + j;
-                        if (co < g.cout) {
-                            const int64_t yoff = (img * g.cout + co) * osp + pix;
-                            const float val = conv_epilogue<T>(__uint_as_float(v[j]), (int64_t)model * g.cout + co,
-                                                               yoff, e);
-                            y[yoff] = from_f<T>(val);
-                        }
+                for (int j = 0; j < 32; ++j) {
+                    float val = (__uint_as_float(v[j]) + __shfl_sync(0xffffffffu, pb, j)) *
+                                    __shfl_sync(0xffffffffu, ps, j) +
+                                __shfl_sync(0xffffffffu, pt, j);
+                    const bool ok = pix_ok && co0 + j < g.cout;
+                    if (res && e.residual_first && ok) val += to_f<T>(res[ybase + (int64_t)j * osp]);
+                    val = apply_act(val, e.act);
+                    if (res && !e.residual_first && ok) val += to_f<T>(res[ybase + (int64_t)j * osp]);
+                    if (TMA_STORE) {
+                        sOut[(c + j) * BM + r] = from_f<T>(val);
+                    } else if (ok) {
+                        y[ybase + (int64_t)j * osp] = from_f<T>(val);
                     }
                 }
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+            if (TMA_STORE) {
+                fence_proxy_async_smem();
+                epi_bar_sync();
+                if (ep_tid == 0) {
+                    const int cvalid = g.cout - nt * BN;
+                    if (cvalid >= BN) {
+                        tma_store_4d(&tm_y, sOut, wo0, ho0, nt * BN, (int)img);
+                    }
+                    bulk_commit();
+                }
+            }
         }
+        if (TMA_STORE && ep_tid == 0) bulk_wait0();
     }
     tc_fence_before();
     __syncthreads();
@@ -351,7 +457,7 @@ CUtensorMapDataType tmap_dt() {
     return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool TMA_STORE>
 int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const ConvEpi& e, cudaStream_t st) {
     using S = ConvSmem<BN, STAGES>;
     ConvTcGeom g{};
@@ -383,7 +489,18 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
         int rc = encode_tmap_tiled(&tw_map, tmap_dt<T>(), 3, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    auto kern = conv_tc_kernel<T, BN, STAGES>;
+    CUtensorMap ty_map;
+    memset(&ty_map, 0, sizeof(ty_map));
+    if (TMA_STORE) {
+        // NCHW output per image: dims {W, H, C, image}; box = one tile of BN channels
+        const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)nb};
+        const uint64_t strides[3] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2,
+                                     (uint64_t)cg.cout * cg.oh * cg.ow * 2};
+        const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, (uint32_t)BN, 1};
+        int rc = encode_tmap_tiled(&ty_map, tmap_dt<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
+    auto kern = conv_tc_kernel<T, BN, STAGES, TMA_STORE>;
     static bool attr_done[64] = {false};
     const int dev = current_device();
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
@@ -393,7 +510,7 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
     }
     const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * g.tiles_h * g.tiles_w;
     const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
-    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw_map, y, g, e, device_error_ptr());
+    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw_map, ty_map, y, g, e, device_error_ptr());
     return check_launch("widek_conv_fwd (tcgen05)");
 }
 
@@ -409,6 +526,7 @@ struct ConvLaunch {
     ConvGeom g;
     ConvEpi e;
     int dtype;
+    int64_t packed_b;     // > 0: x is channel-packed [batch][n][cin][...] (tensor-core path only)
     cudaStream_t st;
     template <typename T>
     int run() {
@@ -418,18 +536,38 @@ struct ConvLaunch {
                 const size_t need = (size_t)nb * g.cin * g.h * g.w * sizeof(T);
                 if (ws && ws_bytes >= need && aligned16(ws) && aligned16(wp)) {
                     const int64_t p = (int64_t)g.h * g.w;
-                    dim3 grid((unsigned)((p + 31) / 32), (unsigned)((g.cin + 31) / 32),
-                              (unsigned)std::min<int64_t>(nb, 65535));
-                    nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(static_cast<const T*>(x),
-                                                                         static_cast<T*>(ws), nb, g.cin, p);
+                    if (p % 64 == 0 && aligned16(x)) {
+                        const int64_t jobs = nb * (g.cin / 64) * (p / 64);
+                        const int blocks = (int)std::min<int64_t>(jobs, (int64_t)sm_count(current_device()) * 8);
+                        nchw_to_nhwc_vec_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint16_t*>(x),
+                                                                        static_cast<uint16_t*>(ws), nb, g.cin, p,
+                                                                        packed_b, g.n);
+                    } else {
+                        dim3 grid((unsigned)((p + 31) / 32), (unsigned)((g.cin + 31) / 32),
+                                  (unsigned)std::min<int64_t>(nb, 65535));
+                        nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(static_cast<const T*>(x),
+                                                                             static_cast<T*>(ws), nb, g.cin, p);
+                    }
                     int rc = check_launch("widek_conv_fwd (nhwc staging)");
                     if (rc) return rc;
                     const T* xs = static_cast<const T*>(ws);
                     const T* wpp = static_cast<const T*>(wp);
                     T* yp = static_cast<T*>(y);
-                    if (g.cout <= 64) return launch_conv_tc<T, 64, 8>(xs, wpp, yp, g, e, st);
-                    if (g.cout <= 128) return launch_conv_tc<T, 128, 6>(xs, wpp, yp, g, e, st);
-                    return launch_conv_tc<T, 256, 4>(xs, wpp, yp, g, e, st);
+                    // TMA store of the output tile: box width = tile width (>= 8 elements,
+                    // 16-byte multiple), rows 16-byte aligned, whole BN-channel tiles.
+                    int tw = 1;
+                    while (tw < g.ow && tw < BM) tw <<= 1;
+                    const bool store_ok = tw >= 8 && g.ow % 8 == 0 && aligned16(yp);
+                    if (g.cout <= 64) {
+                        if (store_ok && g.cout == 64) return launch_conv_tc<T, 64, 8, true>(xs, wpp, yp, g, e, st);
+                        return launch_conv_tc<T, 64, 8, false>(xs, wpp, yp, g, e, st);
+                    }
+                    if (g.cout <= 128) {
+                        if (store_ok && g.cout % 128 == 0) return launch_conv_tc<T, 128, 6, true>(xs, wpp, yp, g, e, st);
+                        return launch_conv_tc<T, 128, 6, false>(xs, wpp, yp, g, e, st);
+                    }
+                    if (store_ok && g.cout % 256 == 0) return launch_conv_tc<T, 256, 3, true>(xs, wpp, yp, g, e, st);
+                    return launch_conv_tc<T, 256, 3, false>(xs, wpp, yp, g, e, st);
                 }
             }
         }
@@ -490,7 +628,7 @@ int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const voi
     if ((int64_t)g.n * g.batch * g.cout * g.od * g.oh * g.ow == 0) return WIDEK_OK;
     if (!x || !w || !y) return set_error(WIDEK_ERR_INVALID, "conv: null pointer");
     ConvEpi e{bias, scale, shift, residual, act, residual_first};
-    ConvLaunch L{x, w, w_packed, y, workspace, workspace_bytes, g, e, dtype, (cudaStream_t)stream};
+    ConvLaunch L{x, w, w_packed, y, workspace, workspace_bytes, g, e, dtype, 0, (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
 }
 

@@ -248,6 +248,224 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a cluster of 2 CTAs on 2 SMs computes a
+// 256 x 256 tile. CTA r loads rows [r*128, r*128+128) of the x tile and rows
+// [r*128, r*128+128) of the w tile (32 KB per stage per SM instead of 48 KB,
+// so 6 stages fit); the leader (r = 0) issues M=256, N=256 MMAs that read
+// both CTAs' shared memory and write each CTA's 128 accumulator rows into its
+// own TMEM. Both CTAs' TMA loads count their bytes on the leader's "full"
+// barrier; the leader's commits arrive on the "empty" / "tmem full" barriers
+// of both CTAs (multicast commit); each CTA's epilogue releases the
+// accumulator on the leader's "tmem empty" barrier (remote arrive).
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+
+struct PairSmem {
+    static constexpr uint32_t A_BYTES = 128 * BK * 2;
+    static constexpr uint32_t B_BYTES = 128 * BK * 2;
+    static constexpr uint32_t RING = kPairStages * (A_BYTES + B_BYTES);
+    static constexpr uint32_t TOTAL = 1024 + RING + 8 * (2 * kPairStages + 5) + 16;
+};
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    linear_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                          const T* __restrict__ bias, T* __restrict__ y, int n_models, int M, int K, int O, int act,
+                          int vec_store, int* err) {
+    using S = PairSmem;
+    constexpr int BN2 = 256;                 // N per pair tile (and per CTA accumulator)
+    constexpr uint32_t IDESC = idesc_f16(256, BN2, std::is_same<T, __nv_bfloat16>::value);
+    constexpr uint32_t TMEM_COLS = 2 * BN2;
+    constexpr int STAGES = kPairStages;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * S::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int mt_count = (M + 255) / 256;
+    const int nt_count = (O + BN2 - 1) / BN2;
+    const int kb_count = (K + BK - 1) / BK;
+    const int tiles = n_models * mt_count * nt_count;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * 4 * 32);   // both CTAs' epilogue threads
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();                      // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // TMA producer (both CTAs); bytes land on the leader's full barrier.
+        const uint64_t pol_x = l2_policy_evict_last();
+        const uint64_t pol_w = l2_policy_evict_first();
+        int s = 0, issued = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int tile = pair; tile < tiles && ok; tile += npairs) {
+            const int mt = tile % mt_count;
+            const int rest = tile / mt_count;
+            const int nt = rest % nt_count;
+            const int model = rest / nt_count;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (S::A_BYTES + S::B_BYTES));
+                    const uint32_t leader_full = map_to_rank(smem_addr(&full[s]), 0);
+                    tma_load_3d_pair(sA + s * S::A_BYTES, &tm_x, leader_full, kb * BK, mt * 256 + rank * 128, model,
+                                     pol_x);
+                    tma_load_3d_pair(sB + s * S::B_BYTES, &tm_w, leader_full, kb * BK, nt * BN2 + rank * 128, model,
+                                     pol_w);
+                }
+                __syncwarp();
+                ++issued;
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            // This CTA's copies count on the leader's barrier; give them time
+            // to land (bounded) before the CTA's shared memory is released.
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 1000000ull) { }
+        }
+    } else if (warp == 1) {
+        if (rank == 0) {
+            // MMA issuer (leader only)
+            int s = 0, local = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += npairs, ++local) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN2;
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a0 = smem_addr(sA + s * S::A_BYTES);
+                        const uint32_t b0 = smem_addr(sB + s * S::B_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k)
+                            umma_f16_ss_pair(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32),
+                                             IDESC, (kb | k) != 0);
+                        umma_commit_pair_multicast(&empty[s], 0x3);
+                    }
+                    __syncwarp();
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                if (lane == 0) umma_commit_pair_multicast(&tfull[acc], 0x3);
+                __syncwarp();
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            }
+            if (lane == 0) umma_commit_pair_multicast(done, 0x1);
+            __syncwarp();
+            const volatile int never = 0;
+            mbar_wait(done, 0, &never);
+        }
+    } else {
+        // Epilogue: warps 2..5 of each CTA own TMEM lane quarters (warp % 4).
+        const int q = warp & 3;
+        const uint32_t leader_tempty0 = map_to_rank(smem_addr(&tempty[0]), 0);
+        int local = 0;
+        for (int tile = pair; tile < tiles; tile += npairs, ++local) {
+            const int mt = tile % mt_count;
+            const int rest = tile / mt_count;
+            const int nt = rest % nt_count;
+            const int model = rest / nt_count;
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const int row = mt * 256 + (int)rank * 128 + q * 32 + lane;
+            const bool row_ok = row < M;
+            T* yrow = y + ((int64_t)model * M + (row_ok ? row : 0)) * O;
+            const T* brow = bias ? bias + (int64_t)model * O : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < BN2; c += 32) {
+                const int col0 = nt * BN2 + c;
+                if (col0 >= O) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN2 + c) + ((uint32_t)(q * 32) << 16), r);
+                tmem_ld_wait();
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                if (brow) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (col0 + j < O) v[j] += to_f<T>(brow[col0 + j]);
+                }
+                if (act != WIDEK_ACT_NONE) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], act);
+                }
+                if (row_ok) {
+                    if (vec_store && col0 + 32 <= O) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) store16<T>(yrow + col0 + j, v + j);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < O) yrow[col0 + j] = from_f<T>(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_remote(leader_tempty0 + acc * 8);
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync_all();                      // no CTA leaves while its pair may still touch its smem / TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
 template <typename T>
 CUtensorMapDataType tmap_dtype();
 template <>
@@ -291,8 +509,50 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
 }
 
 template <typename T>
+int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
+                   cudaStream_t st) {
+    using S = PairSmem;
+    CUtensorMap tx, tw;
+    {
+        const uint64_t dims[3] = {(uint64_t)k, (uint64_t)m, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)m * k * 2};
+        const uint32_t box[3] = {BK, 128, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dtype<T>(), 3, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[3] = {(uint64_t)k, (uint64_t)o, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)o * k * 2};
+        const uint32_t box[3] = {BK, 128, 1};
+        int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    auto kern = linear_tc_pair_kernel<T>;
+    static bool attr_done[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "linear: cannot reserve %u bytes of shared memory", S::TOTAL);
+        attr_done[dev] = true;
+    }
+    const int64_t tiles = n * ((m + 255) / 256) * ((o + 255) / 256);
+    const int pairs = (int)std::min<int64_t>(tiles, sm_count(dev) / 2);
+    const int vec_store = (o % 8 == 0) && aligned16(y);
+    kern<<<2 * pairs, kThreads, S::TOTAL, st>>>(tx, tw, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
+                                                device_error_ptr());
+    return check_launch("widek_linear_fwd (tcgen05 pair)");
+}
+
+// Kernel selection (set with widek_linear_set_variant, for measurements):
+// 0 = automatic (single-CTA tiles; they measured faster than CTA pairs on the
+// cfg2 shape), 1 = single-CTA tiles, 2 = CTA-pair tiles whenever legal.
+int g_linear_variant = 0;
+
+template <typename T>
 int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
               cudaStream_t st) {
+    const bool pair_ok = o > 128 && m > 128;
+    if (pair_ok && g_linear_variant == 2) return launch_tc_pair<T>(x, w, bias, y, n, m, k, o, act, st);
     if (o > 128) return launch_tc<T, 256, 4>(x, w, bias, y, n, m, k, o, act, st);
     if (o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, st);
     return launch_tc<T, 64, 8>(x, w, bias, y, n, m, k, o, act, st);
@@ -300,6 +560,12 @@ int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
 
 }  // namespace
 }  // namespace widek
+
+extern "C" int widek_linear_set_variant(int variant) {
+    if (variant < 0 || variant > 2) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
+    widek::g_linear_variant = variant;
+    return WIDEK_OK;
+}
 
 extern "C" int widek_linear_fwd(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m,
                                 int64_t k, int64_t o, int dtype, int act, void* stream) {

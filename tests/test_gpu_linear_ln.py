@@ -188,3 +188,24 @@ def test_traced_mlp_golden():
     out = wide(g['inputs']['packed'].to(DEV))
     assert_fp32_close(out, g['outputs']['y'])
     no_device_error()
+
+
+@pytest.mark.parametrize("n,m,k,o", [(2, 256, 1024, 512), (3, 300, 200, 264), (1, 129, 64, 136), (4, 512, 256, 1024)])
+def test_linear_pair_tiles_match_single_cta(n, m, k, o):
+    """CTA-pair (cta_group::2) tiles vs single-CTA tiles vs the oracle."""
+    from wide_compiler import _native
+    x, w, b = _rand_linear(n, m, k, o, torch.bfloat16, seed=m + o)
+    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+    lib = _native.lib()
+    try:
+        _native.check(lib.widek_linear_set_variant(1), "variant")
+        y1 = ops.linear(xd, wd, bd)
+        _native.check(lib.widek_linear_set_variant(2), "variant")
+        y2 = ops.linear(xd, wd, bd)
+    finally:
+        lib.widek_linear_set_variant(0)
+    ref = O.linear(x, w, b)
+    assert_lowp_close(y1, ref)
+    assert_lowp_close(y2, ref)
+    torch.testing.assert_close(y1.float(), y2.float(), rtol=1e-2, atol=1e-2)
+    no_device_error()
