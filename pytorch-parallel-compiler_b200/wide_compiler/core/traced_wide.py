@@ -194,6 +194,19 @@ class WideStage:
     num_inputs: int = 1
 
 
+def _bn_fold(bn: nn.Module):
+    """Eval-mode BatchNorm as a per-channel scale/shift (fp32):
+    scale = w / sqrt(running_var + eps), shift = b - running_mean * scale."""
+    rv = bn.running_var.float()
+    scale = torch.rsqrt(rv + bn.eps)
+    if bn.weight is not None:
+        scale = scale * bn.weight.float()
+    shift = -bn.running_mean.float() * scale
+    if bn.bias is not None:
+        shift = shift + bn.bias.float()
+    return scale, shift
+
+
 def _get_nested_attr(obj: Any, path: str) -> Any:
     for part in path.split('.'):
         obj = getattr(obj, part)
@@ -242,6 +255,10 @@ class TracedWideModel(nn.Module):
         self._input_name: str = 'x'
         self._output_name: str = ''
         self._attr_names: List[str] = []
+        # Cross-stage fusion (Linear+act, Conv+BN[+act|+residual[+act]]);
+        # the plan is built on the first forward.
+        self.fuse: bool = True
+        self._fusion: Optional[Dict[str, Any]] = None
 
     @classmethod
     def from_models(cls, models: List[nn.Module], sample_input: Tensor) -> 'TracedWideModel':
@@ -341,21 +358,148 @@ class TracedWideModel(nn.Module):
         n, b, c = out.shape[0], out.shape[1], out.shape[2]
         return ops.swap01(out).reshape(b, n * c, *out.shape[3:])
 
+    # -- cross-stage fusion ----------------------------------------------------
+
+    def _consumers(self) -> Dict[str, List[str]]:
+        cons: Dict[str, List[str]] = {}
+        for name in self._execution_order:
+            refs = list(self._node_args.get(name, ())) + list(self._node_kwargs.get(name, {}).values())
+            for a in refs:
+                if isinstance(a, str):
+                    cons.setdefault(a, []).append(name)
+        cons.setdefault(self._output_name, []).append('<output>')
+        return cons
+
+    def _build_fusion_plan(self) -> Dict[str, Any]:
+        """Groups of single-consumer chains executed as one kernel:
+        Linear -> act; Conv -> BatchNorm(eval) [-> act | -> add(residual) [-> act]].
+        Returns {last_node: group} and the set of nodes folded into groups."""
+        from ..ops import ACT_GELU, ACT_RELU
+        cons = self._consumers()
+        acts = {'relu': ACT_RELU, 'gelu': ACT_GELU}
+        groups: Dict[str, Dict[str, Any]] = {}
+        folded = set()
+
+        def only_consumer(name):
+            c = cons.get(name, [])
+            return c[0] if len(c) == 1 and c[0] in self.stage_info and c[0] not in folded else None
+
+        def op_of(name):
+            return self.stages[name.replace('.', '_')]
+
+        def unary_act(name):
+            o = op_of(name)
+            if isinstance(o, FunctionalOp) and o.unary in acts and len(self._node_args[name]) == 1 \
+                    and o._plain(self._node_kwargs.get(name, {})):
+                return acts[o.unary]
+            return None
+
+        for name in self._execution_order:
+            if name not in self.stage_info or name in folded:
+                continue
+            op = op_of(name)
+            if isinstance(op, WideLinear) and len(self._node_args[name]) == 1:
+                nxt = only_consumer(name)
+                if nxt is not None and unary_act(nxt) is not None:
+                    groups[nxt] = {'kind': 'linear', 'nodes': [name, nxt], 'head': name, 'act': unary_act(nxt)}
+                    folded.update([name])
+                continue
+            if isinstance(op, (WideConv1d, WideConv2d)) and len(self._node_args[name]) == 1:
+                bn = only_consumer(name)
+                if bn is None or not isinstance(op_of(bn), (WideBatchNorm1d, WideBatchNorm2d)):
+                    continue
+                g = {'kind': 'conv', 'nodes': [name, bn], 'head': name, 'bn': bn, 'act': 0,
+                     'residual': None, 'residual_first': False}
+                tail = bn
+                nxt = only_consumer(bn)
+                if nxt is not None and unary_act(nxt) is not None:
+                    g['act'] = unary_act(nxt)
+                    g['nodes'].append(nxt)
+                    tail = nxt
+                elif nxt is not None and isinstance(op_of(nxt), BinaryOp) and op_of(nxt).op == 'add' \
+                        and not self._node_kwargs.get(nxt):
+                    a0, a1 = self._node_args[nxt]
+                    other = a1 if a0 == bn else a0
+                    if isinstance(other, str) and other != bn:
+                        g['residual'] = other
+                        g['nodes'].append(nxt)
+                        tail = nxt
+                        after = only_consumer(nxt)
+                        if after is not None and unary_act(after) is not None:
+                            g['act'] = unary_act(after)
+                            g['residual_first'] = True
+                            g['nodes'].append(after)
+                            tail = after
+                groups[tail] = g
+                folded.update(g['nodes'][:-1])
+        return {'groups': groups, 'folded': folded}
+
+    def _run_group(self, g: Dict[str, Any], values: Dict[str, Any]):
+        """Executes a fused group; returns None when it cannot run fused
+        (e.g. BatchNorm in training mode), in which case the nodes run one by one."""
+        from .. import ops
+        head = g['head']
+        x = values.get(self._node_args[head][0])
+        if not isinstance(x, Tensor) or not x.is_cuda:
+            return None
+        op = self.stages[head.replace('.', '_')]
+        if g['kind'] == 'linear':
+            return ops.linear(x, op.weight, op.bias, act=g['act'])
+        bn_mod = self.stages[g['bn'].replace('.', '_')].op
+        if bn_mod.training or bn_mod.running_mean is None or bn_mod.running_var is None:
+            return None
+        res = values.get(g['residual']) if g['residual'] is not None else None
+        if g['residual'] is not None and not isinstance(res, Tensor):
+            return None
+        scale, shift = _bn_fold(bn_mod)
+        if isinstance(op, WideConv2d):
+            w, b = op.grouped_conv.weight, op.grouped_conv.bias
+            st, pd, dl = op.stride, op.padding, op.dilation
+        else:
+            w, b = op._params()
+            st, pd, dl = (op.stride,), (op.padding,), (op.dilation,)
+        if res is not None and (res.dtype != x.dtype or res.device != x.device):
+            return None
+        y = ops.conv_nd(x, w, b, op.n, st, pd, dl, scale=scale.to(x.dtype), shift=shift.to(x.dtype),
+                        residual=res, act=g['act'], residual_first=g['residual_first'])
+        if res is not None and y.shape != res.shape:
+            return None
+        return y
+
     def _run_stages(self, x: Tensor) -> Any:
+        if self._fusion is None:
+            self._fusion = self._build_fusion_plan() if self.fuse else {'groups': {}, 'folded': set()}
+        groups, folded = self._fusion['groups'], self._fusion['folded']
         values: Dict[str, Any] = {self._input_name: x}
         for name in self._attr_names:
             buf = f"_attr_{name.replace('.', '_')}"
             if hasattr(self, buf):
                 values[name] = getattr(self, buf)
+        pending = []                      # folded nodes whose group fell back to node-by-node
         for name in self._execution_order:
             if name in self._attr_names or name not in self.stage_info:
                 continue
-            op = self.stages[name.replace('.', '_')]
-            args = [values[a] if isinstance(a, str) and a in values else a for a in self._node_args[name]]
-            kwargs = {k: (values[v] if isinstance(v, str) and v in values else v)
-                      for k, v in self._node_kwargs.get(name, {}).items()}
-            values[name] = op(*args, **kwargs)
+            if name in folded:
+                pending.append(name)
+                continue
+            if name in groups:
+                y = self._run_group(groups[name], values)
+                if y is not None:
+                    values[name] = y
+                    pending = [p for p in pending if p not in groups[name]['nodes']]
+                    continue
+                for p_name in groups[name]['nodes'][:-1]:
+                    values[p_name] = self._run_node(p_name, values)
+                pending = [p for p in pending if p not in groups[name]['nodes']]
+            values[name] = self._run_node(name, values)
         return values[self._output_name]
+
+    def _run_node(self, name: str, values: Dict[str, Any]) -> Any:
+        op = self.stages[name.replace('.', '_')]
+        args = [values[a] if isinstance(a, str) and a in values else a for a in self._node_args[name]]
+        kwargs = {k: (values[v] if isinstance(v, str) and v in values else v)
+                  for k, v in self._node_kwargs.get(name, {}).items()}
+        return op(*args, **kwargs)
 
     def forward(self, x: Tensor) -> Tensor:
         out = self._run_stages(self._unpack(x))

@@ -177,3 +177,32 @@ def test_unpack_outputs_views_and_errors():
     assert parts[1].data_ptr() == out.data_ptr() + 4 * 4
     with pytest.raises(ValueError):
         wc.unpack(out, 5)
+
+
+class _ResBlockT(nn.Module):
+    def __init__(self, c=4, post_relu=False):
+        super().__init__()
+        self.post_relu = post_relu
+        self.conv1 = nn.Conv2d(c, c, 3, padding=1)
+        self.bn1 = nn.BatchNorm2d(c)
+        self.conv2 = nn.Conv2d(c, c, 3, padding=1)
+        self.bn2 = nn.BatchNorm2d(c)
+
+    def forward(self, x):
+        h = F.relu(self.bn1(self.conv1(x)))
+        y = self.bn2(self.conv2(h)) + x
+        return F.relu(y) if self.post_relu else y
+
+
+def test_fusion_plan_structure():
+    mlp = wc.TracedWideModel.from_models([_MLP() for _ in range(3)], torch.randn(2, 8))
+    plan = mlp._build_fusion_plan()
+    assert list(plan['groups']) == ['relu'] and plan['groups']['relu']['kind'] == 'linear'
+    rb = wc.TracedWideModel.from_models([_ResBlockT() for _ in range(2)], torch.randn(1, 4, 6, 6))
+    plan = rb._build_fusion_plan()
+    kinds = {k: (g['kind'], g['act'], g['residual']) for k, g in plan['groups'].items()}
+    assert kinds['relu'] == ('conv', 1, None)
+    assert kinds['add'] == ('conv', 0, 'x')
+    rb2 = wc.TracedWideModel.from_models([_ResBlockT(post_relu=True) for _ in range(2)], torch.randn(1, 4, 6, 6))
+    g = rb2._build_fusion_plan()['groups']
+    assert g['relu_1']['residual'] == 'x' and g['relu_1']['residual_first'] and g['relu_1']['act'] == 1

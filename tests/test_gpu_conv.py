@@ -138,3 +138,60 @@ def test_traced_resblock_golden():
     wide = wc.compile(models, torch.randn(2, 4, 6, 6, device=DEV)).eval()
     out = wide(g['inputs']['packed'].to(DEV))
     assert_fp32_close(out, g['outputs']['y'])
+
+
+class _RB(torch.nn.Module):
+    def __init__(self, c, post_relu):
+        super().__init__()
+        self.post_relu = post_relu
+        self.conv1 = torch.nn.Conv2d(c, c, 3, padding=1)
+        self.bn1 = torch.nn.BatchNorm2d(c)
+        self.conv2 = torch.nn.Conv2d(c, c, 3, padding=1)
+        self.bn2 = torch.nn.BatchNorm2d(c)
+
+    def forward(self, x):
+        h = torch.nn.functional.relu(self.bn1(self.conv1(x)))
+        y = self.bn2(self.conv2(h)) + x
+        return torch.nn.functional.relu(y) if self.post_relu else y
+
+
+@pytest.mark.parametrize("post_relu", [False, True])
+def test_traced_resblock_fused_matches_unfused_bf16(post_relu):
+    torch.manual_seed(2)
+    n, c = 3, 64
+    models = []
+    for _ in range(n):
+        m = _RB(c, post_relu)
+        with torch.no_grad():
+            for bn in (m.bn1, m.bn2):
+                bn.running_mean.normal_(0, 1)
+                bn.running_var.uniform_(0.5, 2.0)
+                bn.weight.uniform_(0.5, 1.5)
+                bn.bias.normal_(0, 0.1)
+        models.append(m.to(DEV, torch.bfloat16).eval())
+    wide = wc.compile(models, torch.randn(2, c, 16, 16, device=DEV, dtype=torch.bfloat16)).eval()
+    x = torch.randn(2, n * c, 16, 16, device=DEV).to(torch.bfloat16)
+    y_fused = wide(x)
+    assert wide._fusion['groups'], "expected fused groups"
+    wide.fuse = False
+    wide._fusion = None
+    y_plain = wide(x)
+    assert_lowp_close(y_fused, y_plain.double())
+    # and against the per-model torch modules in fp32
+    xs = wc.unpack(x, n)
+    ref = torch.cat([models[i].float()(xs[i].float()) for i in range(n)], dim=1)
+    assert_lowp_close(y_fused, ref.double(), rtol=5e-2)
+
+
+def test_traced_fusion_falls_back_in_training_mode():
+    torch.manual_seed(3)
+    models = [_RB(8, False).to(DEV) for _ in range(2)]
+    wide = wc.compile(models, torch.randn(2, 8, 6, 6, device=DEV))
+    wide.train()
+    x = torch.randn(4, 16, 6, 6, device=DEV)
+    y = wide(x)          # BatchNorm in training mode: groups run node by node
+    for m in models:
+        m.train()
+    xs = wc.unpack(x, 2)
+    ref = torch.cat([models[i](xs[i]) for i in range(2)], dim=1)
+    assert_fp32_close(y, ref.detach())
