@@ -87,7 +87,8 @@ WIDEK_API int widek_linear_fwd_simt(const void* x, const void* w, const void* bi
 
 /* Selects the tensor-core tiling of widek_linear_fwd for this process:
  * 0 = automatic (single-CTA 128xBN tiles), 1 = single-CTA tiles,
- * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128.
+ * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128,
+ * 3 = single-CTA 128x128 tiles (6-stage ring), 4 = as 1 without L2 hints.
  * A measurement knob (process-wide, not synchronized with running calls).
  * No counterpart in the reference. */
 WIDEK_API int widek_linear_set_variant(int variant);

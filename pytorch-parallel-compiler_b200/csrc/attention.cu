@@ -145,8 +145,14 @@ __global__ void __launch_bounds__(32 * kSimtRows) attn_simt_kernel(AttnArgs a) {
 // ---------------------------------------------------------------------------
 // Tensor-core kernel (bf16 / f16, dh = 64 or 128)
 // ---------------------------------------------------------------------------
-constexpr int kBM = 64;      // query rows per CTA (16 per warp)
-constexpr int kBN = 64;      // keys per tile
+constexpr int kBN = 64;      // keys per tile (query rows per CTA: 16 per warp)
+
+// 2^x on the special-function unit (the scores are already in the log2 domain).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -210,11 +216,11 @@ __device__ __forceinline__ int swz(int r, int c) {
     return r * D + ((c ^ (r & 7)) << 3);
 }
 
-template <typename T, int D>
+template <typename T, int D, int NT>
 __device__ __forceinline__ void load_tile(T* dst, const T* src, int64_t stride, int row0, int rows_valid,
                                           int nrows) {
     constexpr int CPR = D / 8;   // 16-byte chunks per row
-    for (int i = threadIdx.x; i < nrows * CPR; i += 128) {
+    for (int i = threadIdx.x; i < nrows * CPR; i += NT) {
         const int r = i / CPR, c = i % CPR;
         const bool ok = r < rows_valid;
         const T* s = ok ? src + (int64_t)(row0 + r) * stride + c * 8 : src;
@@ -222,8 +228,10 @@ __device__ __forceinline__ void load_tile(T* dst, const T* src, int64_t stride, 
     }
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
+template <typename T, int D, int NW>
+__global__ void __launch_bounds__(NW * 32) attn_mma_kernel(AttnArgs a) {
+    constexpr int kBM = 16 * NW;
+    constexpr int NT = 32 * NW;
     extern __shared__ __align__(128) uint8_t smraw[];
     T* Qs = reinterpret_cast<T*>(smraw);                 // [kBM][D]
     T* Ks = Qs + kBM * D;                                // [2][kBN][D]
@@ -241,10 +249,10 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
     if (a.causal) kend = min(kend, min(q0 + kBM, a.tq));
     const int ntiles = (kend + kBN - 1) / kBN;
 
-    load_tile<T, D>(Qs, qp, a.sq, q0, min(kBM, a.tq - q0), kBM);
+    load_tile<T, D, NT>(Qs, qp, a.sq, q0, min(kBM, a.tq - q0), kBM);
     if (ntiles > 0) {
-        load_tile<T, D>(Ks, kp, a.sk, 0, min(kBN, a.tk), kBN);
-        load_tile<T, D>(Vs, vp, a.sv, 0, min(kBN, a.tk), kBN);
+        load_tile<T, D, NT>(Ks, kp, a.sk, 0, min(kBN, a.tk), kBN);
+        load_tile<T, D, NT>(Vs, vp, a.sv, 0, min(kBN, a.tk), kBN);
     }
     cp_async_commit();
 
@@ -261,8 +269,8 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
         const int buf = it & 1;
         if (it + 1 < ntiles) {
             const int k1 = (it + 1) * kBN;
-            load_tile<T, D>(Ks + (buf ^ 1) * kBN * D, kp, a.sk, k1, min(kBN, a.tk - k1), kBN);
-            load_tile<T, D>(Vs + (buf ^ 1) * kBN * D, vp, a.sv, k1, min(kBN, a.tk - k1), kBN);
+            load_tile<T, D, NT>(Ks + (buf ^ 1) * kBN * D, kp, a.sk, k1, min(kBN, a.tk - k1), kBN);
+            load_tile<T, D, NT>(Vs + (buf ^ 1) * kBN * D, vp, a.sv, k1, min(kBN, a.tk - k1), kBN);
         }
         cp_async_commit();
         cp_async_wait<1>();
@@ -278,6 +286,16 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
         }
         const T* Kt = Ks + buf * kBN * D;
         const T* Vt = Vs + buf * kBN * D;
+        const int kbase = it * kBN;
+        const int wrow0 = q0 + warp * 16;                  // this warp's first query row
+        // Causal: a tile entirely after this warp's last row contributes nothing.
+        if (a.causal && kbase > wrow0 + 15) {
+            __syncthreads();
+            continue;
+        }
+        // Per-element masking only where it can change something.
+        const bool need_mask = a.mask_kind != 0 || kbase + kBN > a.tk || wrow0 + 15 >= a.tq ||
+                               (a.causal && kbase + kBN - 1 > wrow0);
         // S = Q K^T : 16 x 64 per warp (8 n-tiles of 8 keys)
         float s[kBN / 8][4];
 #pragma unroll
@@ -298,22 +316,32 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
             }
         }
         // scale (log2 domain), masks, online softmax
-        const int kbase = it * kBN;
         float tmax[2] = {-INFINITY, -INFINITY};
+        if (need_mask) {
 #pragma unroll
-        for (int j = 0; j < kBN / 8; ++j) {
+            for (int j = 0; j < kBN / 8; ++j) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = qr0 + (e >> 1) * 8;
-                const int kj = kbase + j * 8 + 2 * tq4 + (e & 1);
-                float val = s[j][e] * sl2;
-                bool keep = kj < a.tk && row < a.tq;
-                if (keep && (a.causal || a.mask_kind)) {
-                    const float add = mask_value<T>(a, b, h, row, kj, keep);
-                    val += add * 1.4426950408889634f;
+                for (int e = 0; e < 4; ++e) {
+                    const int row = qr0 + (e >> 1) * 8;
+                    const int kj = kbase + j * 8 + 2 * tq4 + (e & 1);
+                    float val = s[j][e] * sl2;
+                    bool keep = kj < a.tk && row < a.tq;
+                    if (keep && (a.causal || a.mask_kind)) {
+                        const float add = mask_value<T>(a, b, h, row, kj, keep);
+                        val += add * 1.4426950408889634f;
+                    }
+                    s[j][e] = keep ? val : -INFINITY;
+                    tmax[e >> 1] = fmaxf(tmax[e >> 1], s[j][e]);
                 }
-                s[j][e] = keep ? val : -INFINITY;
-                tmax[e >> 1] = fmaxf(tmax[e >> 1], s[j][e]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kBN / 8; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    s[j][e] *= sl2;
+                    tmax[e >> 1] = fmaxf(tmax[e >> 1], s[j][e]);
+                }
             }
         }
         float alpha[2];
@@ -322,7 +350,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
             tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
             tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
             const float mnew = fmaxf(mrow[r], tmax[r]);
-            alpha[r] = (mnew == -INFINITY) ? 1.f : exp2f(mrow[r] - mnew);
+            alpha[r] = (mnew == -INFINITY) ? 1.f : fast_exp2(mrow[r] - mnew);
             mrow[r] = mnew;
         }
         float psum[2] = {0.f, 0.f};
@@ -333,7 +361,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnArgs a) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float mr = mrow[e >> 1];
-                p[e] = (s[j][e] == -INFINITY) ? 0.f : exp2f(s[j][e] - mr);
+                p[e] = (s[j][e] == -INFINITY) ? 0.f : fast_exp2(s[j][e] - mr);
                 psum[e >> 1] += p[e];
             }
             // C fragment of n-tile j -> half of the A fragment for k-step j/2
@@ -399,14 +427,26 @@ int launch_attn(AttnArgs a, cudaStream_t st) {
     if (mma_ok) {
         if constexpr (!std::is_same<T, float>::value) {
             const int D = a.dh;
-            const size_t smem = (size_t)(kBM * D + 4 * kBN * D) * sizeof(T);
-            dim3 grid((unsigned)((a.tq + kBM - 1) / kBM), (unsigned)(a.nb * a.heads));
-            if (D == 64) {
-                auto k = attn_mma_kernel<T, 64>;
+            // 8 warps (128 query rows) per CTA share each K/V tile; short
+            // sequences use 4 warps so that more CTAs run.
+            const int nw = a.tq >= 256 ? 8 : 4;
+            const int bm = 16 * nw;
+            const size_t smem = (size_t)(bm * D + 4 * kBN * D) * sizeof(T);
+            dim3 grid((unsigned)((a.tq + bm - 1) / bm), (unsigned)(a.nb * a.heads));
+            if (D == 64 && nw == 8) {
+                auto k = attn_mma_kernel<T, 64, 8>;
+                cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                k<<<grid, 256, smem, st>>>(a);
+            } else if (D == 64) {
+                auto k = attn_mma_kernel<T, 64, 4>;
                 cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
                 k<<<grid, 128, smem, st>>>(a);
+            } else if (nw == 8) {
+                auto k = attn_mma_kernel<T, 128, 8>;
+                cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                k<<<grid, 256, smem, st>>>(a);
             } else {
-                auto k = attn_mma_kernel<T, 128>;
+                auto k = attn_mma_kernel<T, 128, 4>;
                 cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
                 k<<<grid, 128, smem, st>>>(a);
             }

@@ -210,14 +210,15 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool RES_TMA = false>
 struct ConvSmem {
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
     static constexpr uint32_t STAGE_OUT = BM * BN * 2;   // output tile staged for the TMA store
-    static constexpr uint32_t BARS = 8 * (2 * STAGES + 5) + 16;
-    static constexpr uint32_t TOTAL = 1024 + RING + STAGE_OUT + BARS;
+    static constexpr uint32_t STAGE_RES = RES_TMA ? BM * BN * 2 : 0;   // residual tile (TMA load)
+    static constexpr uint32_t BARS = 8 * (2 * STAGES + 6) + 16;
+    static constexpr uint32_t TOTAL = 1024 + RING + STAGE_OUT + STAGE_RES + BARS;
 };
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
@@ -237,11 +238,12 @@ struct ConvTcGeom {
     int kh, kw, cblocks, ph, pw, dh, dw;
 };
 
-template <typename T, int BN, int STAGES, bool TMA_STORE>
+template <typename T, int BN, int STAGES, bool TMA_STORE, bool RES_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                   const __grid_constant__ CUtensorMap tm_y, T* __restrict__ y, ConvTcGeom g, ConvEpi e, int* err) {
-    using S = ConvSmem<BN, STAGES>;
+                   const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
+                   T* __restrict__ y, ConvTcGeom g, ConvEpi e, int* err) {
+    using S = ConvSmem<BN, STAGES, RES_TMA>;
     constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
     constexpr uint32_t TMEM_COLS = 2 * BN;
     extern __shared__ uint8_t smem_raw[];
@@ -249,12 +251,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * S::A_BYTES;
     T* sOut = reinterpret_cast<T*>(smem + S::RING);      // [BN][BM] output tile (TMA store source)
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::STAGE_OUT);
+    T* sRes = reinterpret_cast<T*>(smem + S::RING + S::STAGE_OUT);   // [BN][BM] residual tile
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::STAGE_OUT + S::STAGE_RES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* done = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* res_bar = done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -266,6 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 4 * 32); }
         mbar_init(done, 1);
+        mbar_init(res_bar, 1);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -273,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_x);
         tma_prefetch_desc(&tm_w);
         if (TMA_STORE) tma_prefetch_desc(&tm_y);
+        if (RES_TMA) tma_prefetch_desc(&tm_r);
     }
     if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
     tc_fence_before();
@@ -381,12 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             decode(tile, model, nt, b, mt);
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
-                *abort_flag = 1;
-                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
-                break;
-            }
-            tc_fence_after();
             const int r = q * 32 + lane;                 // pixel within the tile
             const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
             const int ho = ho0 + r / g.tw;
@@ -395,9 +395,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t img = (int64_t)model * g.batch + b;
             const int64_t pix = (int64_t)ho * g.wo + wo;
             if (TMA_STORE) {
-                // the previous tile's store must have finished reading sOut
+                // The previous tile's store must have finished reading sOut and
+                // every thread must be done with the previous sRes; then the
+                // residual tile is requested so that it lands while this tile's
+                // MMAs finish.
                 if (ep_tid == 0) bulk_wait_read0();
                 epi_bar_sync();
+                if (RES_TMA && ep_tid == 0) {
+                    mbar_arrive_expect_tx(res_bar, S::STAGE_RES);
+                    tma_load_4d(sRes, &tm_r, res_bar, wo0, ho0, nt * BN, (int)img, l2_policy_evict_first());
+                }
+            }
+            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            if (RES_TMA && !mbar_wait(res_bar, (uint32_t)(local & 1), abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+                break;
             }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -412,15 +430,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float pt = shift ? to_f<T>(shift[my_ch]) : 0.f;
                 tmem_ld_wait();
                 const int64_t ybase = (img * g.cout + co0) * osp + pix;
+                // residual values of this chunk: from the TMA-staged tile, or
+                // 32 independent loads issued before any use
+                float rv[32];
+                if (res) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (RES_TMA) {
+                            rv[j] = to_f<T>(sRes[(c + j) * BM + r]);
+                        } else {
+                            const bool ok = pix_ok && co0 + j < g.cout;
+                            rv[j] = ok ? to_f<T>(res[ybase + (int64_t)j * osp]) : 0.f;
+                        }
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     float val = (__uint_as_float(v[j]) + __shfl_sync(0xffffffffu, pb, j)) *
                                     __shfl_sync(0xffffffffu, ps, j) +
                                 __shfl_sync(0xffffffffu, pt, j);
                     const bool ok = pix_ok && co0 + j < g.cout;
-                    if (res && e.residual_first && ok) val += to_f<T>(res[ybase + (int64_t)j * osp]);
+                    if (res && e.residual_first) val += rv[j];
                     val = apply_act(val, e.act);
-                    if (res && !e.residual_first && ok) val += to_f<T>(res[ybase + (int64_t)j * osp]);
+                    if (res && !e.residual_first) val += rv[j];
                     if (TMA_STORE) {
                         sOut[(c + j) * BM + r] = from_f<T>(val);
                     } else if (ok) {
@@ -457,9 +489,9 @@ CUtensorMapDataType tmap_dt() {
     return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-template <typename T, int BN, int STAGES, bool TMA_STORE>
+template <typename T, int BN, int STAGES, bool TMA_STORE, bool RES_TMA = false>
 int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const ConvEpi& e, cudaStream_t st) {
-    using S = ConvSmem<BN, STAGES>;
+    using S = ConvSmem<BN, STAGES, RES_TMA>;
     ConvTcGeom g{};
     g.n = cg.n; g.batch = cg.batch; g.cout = cg.cout; g.ho = cg.oh; g.wo = cg.ow;
     int tw = 1;
@@ -500,7 +532,18 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
         int rc = encode_tmap_tiled(&ty_map, tmap_dt<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
-    auto kern = conv_tc_kernel<T, BN, STAGES, TMA_STORE>;
+    CUtensorMap tr_map;
+    memset(&tr_map, 0, sizeof(tr_map));
+    if (RES_TMA) {
+        const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)nb};
+        const uint64_t strides[3] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2,
+                                     (uint64_t)cg.cout * cg.oh * cg.ow * 2};
+        const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, (uint32_t)BN, 1};
+        int rc = encode_tmap_tiled(&tr_map, tmap_dt<T>(), 4, e.residual, dims, strides, box,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
+    auto kern = conv_tc_kernel<T, BN, STAGES, TMA_STORE, RES_TMA>;
     static bool attr_done[64] = {false};
     const int dev = current_device();
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
@@ -510,7 +553,7 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
     }
     const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * g.tiles_h * g.tiles_w;
     const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
-    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw_map, ty_map, y, g, e, device_error_ptr());
+    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw_map, ty_map, tr_map, y, g, e, device_error_ptr());
     return check_launch("widek_conv_fwd (tcgen05)");
 }
 
@@ -558,11 +601,15 @@ struct ConvLaunch {
                     int tw = 1;
                     while (tw < g.ow && tw < BM) tw <<= 1;
                     const bool store_ok = tw >= 8 && g.ow % 8 == 0 && aligned16(yp);
+                    const bool res_tma = store_ok && e.residual && aligned16(e.residual);
                     if (g.cout <= 64) {
+                        if (res_tma && g.cout == 64) return launch_conv_tc<T, 64, 8, true, true>(xs, wpp, yp, g, e, st);
                         if (store_ok && g.cout == 64) return launch_conv_tc<T, 64, 8, true>(xs, wpp, yp, g, e, st);
                         return launch_conv_tc<T, 64, 8, false>(xs, wpp, yp, g, e, st);
                     }
                     if (g.cout <= 128) {
+                        if (res_tma && g.cout % 128 == 0)
+                            return launch_conv_tc<T, 128, 5, true, true>(xs, wpp, yp, g, e, st);
                         if (store_ok && g.cout % 128 == 0) return launch_conv_tc<T, 128, 6, true>(xs, wpp, yp, g, e, st);
                         return launch_conv_tc<T, 128, 6, false>(xs, wpp, yp, g, e, st);
                     }

@@ -45,7 +45,7 @@ template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                      const T* __restrict__ bias, T* __restrict__ y, int n_models, int M, int K, int O, int act,
-                     int vec_store, int* err) {
+                     int vec_store, int l2_hints, int* err) {
     using S = GemmSmem<BN, STAGES>;
     constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
     constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------------
         // TMA producer
         // ------------------------------------------------------------------
-        const uint64_t pol_x = l2_policy_evict_last();
-        const uint64_t pol_w = l2_policy_evict_first();
+        const uint64_t pol_x = l2_hints ? l2_policy_evict_last() : l2_policy_evict_normal();
+        const uint64_t pol_w = l2_hints ? l2_policy_evict_first() : l2_policy_evict_normal();
         int s = 0;
         uint32_t ph = 0;
         int issued = 0;
@@ -466,6 +466,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+// Kernel selection (set with widek_linear_set_variant, for measurements):
+// 0 = automatic (single-CTA tiles; they measured faster than CTA pairs on the
+// cfg2 shape), 1 = single-CTA tiles, 2 = CTA-pair tiles whenever legal,
+// 3 = single-CTA 128x128 tiles with a 6-stage ring, 4 = as 1 without L2 hints.
+int g_linear_variant = 0;
+
 template <typename T>
 CUtensorMapDataType tmap_dtype();
 template <>
@@ -504,7 +510,7 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
     const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
     const int vec_store = (o % 8 == 0) && aligned16(y);
     kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
-                                           device_error_ptr());
+                                           g_linear_variant == 4 ? 0 : 1, device_error_ptr());
     return check_launch("widek_linear_fwd (tcgen05)");
 }
 
@@ -543,16 +549,13 @@ int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64
     return check_launch("widek_linear_fwd (tcgen05 pair)");
 }
 
-// Kernel selection (set with widek_linear_set_variant, for measurements):
-// 0 = automatic (single-CTA tiles; they measured faster than CTA pairs on the
-// cfg2 shape), 1 = single-CTA tiles, 2 = CTA-pair tiles whenever legal.
-int g_linear_variant = 0;
 
 template <typename T>
 int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
               cudaStream_t st) {
     const bool pair_ok = o > 128 && m > 128;
     if (pair_ok && g_linear_variant == 2) return launch_tc_pair<T>(x, w, bias, y, n, m, k, o, act, st);
+    if (g_linear_variant == 3 && o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, st);
     if (o > 128) return launch_tc<T, 256, 4>(x, w, bias, y, n, m, k, o, act, st);
     if (o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, st);
     return launch_tc<T, 64, 8>(x, w, bias, y, n, m, k, o, act, st);
@@ -562,7 +565,7 @@ int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
 }  // namespace widek
 
 extern "C" int widek_linear_set_variant(int variant) {
-    if (variant < 0 || variant > 2) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
+    if (variant < 0 || variant > 4) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
     widek::g_linear_variant = variant;
     return WIDEK_OK;
 }
