@@ -160,6 +160,12 @@ class Workload:
 class LinearCfg2(Workload):
     name = "cfg2"
 
+    def torch_reference_step(self):
+        """The reference's own GPU op sequence (wide_linear.py:162-171:
+        einsum 'noi,nbi->nbo' + bias, cuBLAS through torch) on the same inputs."""
+        w, b, x = self.module.weight, self.module.bias, self.x
+        return lambda: torch.einsum('noi,nbi->nbo', w, x) + b.unsqueeze(1)
+
     def __init__(self, n=64, b=256, i=1024, o=4096):
         self.n, self.b, self.i, self.o = n, b, i, o
 
@@ -279,6 +285,25 @@ class ResBlockCfg3(Workload):
     peak_key = "tensor_sustained"
     launches_per_step = 9
 
+    def torch_reference_step(self):
+        """The reference's GPU op sequence for this graph (wide_conv2d.py:169-194
+        permute + grouped conv, wide_batchnorm_2d.py:53-72 permute + BN,
+        F.relu, + identity) with the same parameters, through torch (cuDNN)."""
+        n, c, hw = self.n, self.c, self.hw
+        st = self.module.stages
+        conv1, bn1, conv2, bn2 = st['conv1'].grouped_conv, st['bn1'].op, st['conv2'].grouped_conv, st['bn2'].op
+        x = self.x                                    # packed [B, N*C, H, W]
+
+        def run():
+            b = x.shape[0]
+            h = F.batch_norm(F.conv2d(x, conv1.weight, conv1.bias, padding=1, groups=n), bn1.running_mean,
+                             bn1.running_var, bn1.weight, bn1.bias, False, 0.0, bn1.eps)
+            h = F.relu(h)
+            y = F.batch_norm(F.conv2d(h, conv2.weight, conv2.bias, padding=1, groups=n), bn2.running_mean,
+                             bn2.running_var, bn2.weight, bn2.bias, False, 0.0, bn2.eps)
+            return y + x
+        return run
+
     def __init__(self, n=100, b=32, c=64, hw=32):
         self.n, self.b, self.c, self.hw = n, b, c, hw
 
@@ -390,6 +415,27 @@ class AttnCfg5(Workload):
     bound = "tensor"
     peak_key = "tensor_sustained"
     launches_per_step = 4
+
+    def torch_reference_step(self):
+        """The reference's GPU op sequence (wide_attention.py:178-238 einsum
+        projections, head split, SDPA causal, merge, out projection;
+        wide_layernorm.py:41-67) with the same parameters, through torch."""
+        a, ln, x = self.attn, self.ln, self.x
+        n, d, hd = self.n, self.d, self.heads
+
+        def run():
+            _, b, t, _ = x.shape
+            q = torch.einsum('nbtd,nod->nbto', x, a.q_weight) + a.q_bias.view(n, 1, 1, d)
+            k = torch.einsum('nbtd,nod->nbto', x, a.kv_weight[:, :d]) + a.kv_bias[:, :d].view(n, 1, 1, d)
+            v = torch.einsum('nbtd,nod->nbto', x, a.kv_weight[:, d:]) + a.kv_bias[:, d:].view(n, 1, 1, d)
+            sp = lambda u: u.view(n, b, t, hd, d // hd).permute(0, 1, 3, 2, 4).reshape(n * b, hd, t, d // hd)
+            o = F.scaled_dot_product_attention(sp(q), sp(k), sp(v), is_causal=True)
+            o = o.view(n, b, hd, t, d // hd).permute(0, 1, 3, 2, 4).reshape(n, b, t, d)
+            y = torch.einsum('nbtd,nod->nbto', o, a.out_weight) + a.out_bias.view(n, 1, 1, d)
+            mean = y.mean(dim=-1, keepdim=True)
+            var = y.var(dim=-1, unbiased=False, keepdim=True)
+            return (y - mean) / torch.sqrt(var + ln.eps) * ln.weight.view(n, 1, 1, d) + ln.bias.view(n, 1, 1, d)
+        return run
 
     def __init__(self, n=16, b=8, t=1024, d=512, heads=8):
         self.n, self.b, self.t, self.d, self.heads = n, b, t, d, heads
@@ -623,6 +669,22 @@ def run_b200(args):
             "clocks": clk,
             "device_error": dev_err,
         }
+        if world == 1 and hasattr(wl, "torch_reference_step"):
+            # Extra column: the reference's torch GPU path (library kernels), same device, same inputs.
+            fn = wl.torch_reference_step()
+            with torch.no_grad():
+                for _ in range(5):
+                    fn()
+                torch.cuda.synchronize(dev)
+                e0.record(stream)
+                for _ in range(args.steps):
+                    fn()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+            tms = e0.elapsed_time(e1) / args.steps
+            line["torch_gpu_reference"] = {"ms_per_step": tms, "value": wl.samples() / (tms * 1e-3),
+                                           "unit": "samples/s",
+                                           "note": "reference op sequence on this GPU via torch (cuBLAS/cuDNN/SDPA)"}
         if world == 1 and not args.no_cpu_baseline:
             torch.set_num_threads(len(os.sched_getaffinity(0)))
             v, desc = wl.cpu_sample(args.cpu_seconds)

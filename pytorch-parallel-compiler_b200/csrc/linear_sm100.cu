@@ -21,6 +21,8 @@
 //
 // fp32 (and anything the tensor-core path cannot take) goes to the CUDA-core
 // kernel in gemm_simt.cu, so fp32 results keep fp32 products (TF32 off).
+#include <cstring>
+
 #include "sm100_ptx.cuh"
 
 namespace widek {
@@ -32,21 +34,36 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool TMA_STORE = false>
 struct GemmSmem {
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
+    // Output staging for the TMA store: two buffers of 128 rows x 32 columns.
+    static constexpr uint32_t OUT_CHUNK = BM * 32 * 2;
+    static constexpr uint32_t OUT_BYTES = TMA_STORE ? 2 * OUT_CHUNK : 0;
     static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4 + 1) + 16;
-    static constexpr uint32_t TOTAL = 1024 + RING + BAR_BYTES;  // 1024: alignment slack
+    static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + BAR_BYTES;  // 1024: alignment slack
 };
 
-template <typename T, int BN, int STAGES>
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <typename T, int BN, int STAGES, bool TMA_STORE>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                     const T* __restrict__ bias, T* __restrict__ y, int n_models, int M, int K, int O, int act,
-                     int vec_store, int l2_hints, int* err) {
-    using S = GemmSmem<BN, STAGES>;
+                     const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias, T* __restrict__ y,
+                     int n_models, int M, int K, int O, int act, int vec_store, int l2_hints, int* err) {
+    using S = GemmSmem<BN, STAGES, TMA_STORE>;
     constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
     constexpr uint32_t TMEM_COLS = 2 * BN;
 
@@ -54,7 +71,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * S::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING);
+    uint8_t* sOut = smem + S::RING;     // [2][128 rows][64 B], 64-byte swizzled (TMA store source)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::OUT_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;   // [2]
     uint64_t* tempty = tfull + 2;       // [2]
@@ -85,6 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tm_x);
         tma_prefetch_desc(&tm_w);
+        if (TMA_STORE) tma_prefetch_desc(&tm_y);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
@@ -179,10 +198,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(done, 0, &never);
     } else {
         // ------------------------------------------------------------------
-        // Epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+        // Epilogue: warps 2..5 own TMEM lane quarters (warp % 4). Per
+        // 32-column chunk: lane j fetches bias[col0 + j] once (broadcast by
+        // shuffles); with TMA_STORE the chunk (128 rows x 64 B) is staged in
+        // shared memory (64-byte swizzle, double-buffered) and written by one
+        // TMA store, so the SM issues full-line writes instead of 16-byte
+        // pieces scattered over 32 rows per instruction.
         // ------------------------------------------------------------------
         const int q = warp & 3;
+        const int ep_tid = threadIdx.x - 64;
         int local = 0;
+        int oc = 0;                               // chunks stored so far (buffer parity)
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int mt = tile % mt_count;
             const int rest = tile / mt_count;
@@ -196,7 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int row = mt * BM + q * 32 + lane;
+            const int rloc = q * 32 + lane;
+            const int row = mt * BM + rloc;
             const bool row_ok = row < M;
             T* yrow = y + ((int64_t)model * M + (row_ok ? row : 0)) * O;
             const T* brow = bias ? bias + (int64_t)model * O : nullptr;
@@ -206,25 +233,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (col0 >= O) break;  // warp-uniform
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c) + ((uint32_t)(q * 32) << 16), r);
+                const float my_bias = (brow && col0 + lane < O) ? to_f<T>(brow[col0 + lane]) : 0.f;
                 tmem_ld_wait();
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                if (brow) {
-                    if (col0 + 32 <= O) {
+                for (int j = 0; j < 32; ++j)
+                    v[j] = apply_act(__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j), act);
+                if (TMA_STORE) {
+                    uint8_t* buf = sOut + (oc & 1) * S::OUT_CHUNK;
+                    if (ep_tid == 0) bulk_wait_read1();       // the store that used this buffer has read it
+                    epi_bar_sync();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] += to_f<T>(brow[col0 + j]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < O) v[j] += to_f<T>(brow[col0 + j]);
+                    for (int j = 0; j < 4; ++j) {
+                        const int phys = j ^ ((rloc >> 1) & 3);
+                        store16<T>(reinterpret_cast<T*>(buf + rloc * 64 + phys * 16), v + 8 * j);
                     }
-                }
-                if (act != WIDEK_ACT_NONE) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], act);
-                }
-                if (row_ok) {
+                    fence_proxy_async_smem();
+                    epi_bar_sync();
+                    if (ep_tid == 0) {
+                        tma_store_3d(&tm_y, buf, col0, mt * BM, model);
+                        bulk_commit();
+                    }
+                    ++oc;
+                } else if (row_ok) {
                     if (vec_store && col0 + 32 <= O) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 8) store16<T>(yrow + col0 + j, v + j);
@@ -238,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
         }
+        if (TMA_STORE && ep_tid == 0) bulk_wait0();
     }
 
     tc_fence_before();
@@ -479,10 +511,10 @@ CUtensorMapDataType tmap_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE
 template <>
 CUtensorMapDataType tmap_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool TMA_STORE = false>
 int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
               cudaStream_t st) {
-    using S = GemmSmem<BN, STAGES>;
+    using S = GemmSmem<BN, STAGES, TMA_STORE>;
     CUtensorMap tx, tw;
     {
         const uint64_t dims[3] = {(uint64_t)k, (uint64_t)m, (uint64_t)n};
@@ -498,7 +530,16 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
         int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    auto kern = linear_tc_kernel<T, BN, STAGES>;
+    CUtensorMap ty;
+    memset(&ty, 0, sizeof(ty));
+    if (TMA_STORE) {
+        const uint64_t dims[3] = {(uint64_t)o, (uint64_t)m, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)o * 2, (uint64_t)m * o * 2};
+        const uint32_t box[3] = {32, BM, 1};
+        int rc = encode_tmap_tiled(&ty, tmap_dtype<T>(), 3, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
+    }
+    auto kern = linear_tc_kernel<T, BN, STAGES, TMA_STORE>;
     static bool attr_done[64] = {false};
     const int dev = current_device();
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
@@ -509,7 +550,7 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
     const int64_t tiles = n * ((m + BM - 1) / BM) * ((o + BN - 1) / BN);
     const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
     const int vec_store = (o % 8 == 0) && aligned16(y);
-    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
+    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw, ty, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
                                            g_linear_variant == 4 ? 0 : 1, device_error_ptr());
     return check_launch("widek_linear_fwd (tcgen05)");
 }
@@ -556,6 +597,14 @@ int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
     const bool pair_ok = o > 128 && m > 128;
     if (pair_ok && g_linear_variant == 2) return launch_tc_pair<T>(x, w, bias, y, n, m, k, o, act, st);
     if (g_linear_variant == 3 && o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, st);
+    // Output through shared memory + TMA store when the output rows are
+    // 16-byte aligned (o % 8 == 0); variant 5 keeps direct stores.
+    const bool store_ok = (o % 8 == 0) && aligned16(y) && g_linear_variant != 5;
+    if (store_ok) {
+        if (o > 128) return launch_tc<T, 256, 4, true>(x, w, bias, y, n, m, k, o, act, st);
+        if (o > 64) return launch_tc<T, 128, 6, true>(x, w, bias, y, n, m, k, o, act, st);
+        return launch_tc<T, 64, 8, true>(x, w, bias, y, n, m, k, o, act, st);
+    }
     if (o > 128) return launch_tc<T, 256, 4>(x, w, bias, y, n, m, k, o, act, st);
     if (o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, st);
     return launch_tc<T, 64, 8>(x, w, bias, y, n, m, k, o, act, st);
@@ -565,7 +614,7 @@ int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
 }  // namespace widek
 
 extern "C" int widek_linear_set_variant(int variant) {
-    if (variant < 0 || variant > 4) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
+    if (variant < 0 || variant > 5) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
     widek::g_linear_variant = variant;
     return WIDEK_OK;
 }
