@@ -301,6 +301,13 @@ WIDEK_API int widek_attention_fwd(const void* q, const void* k, const void* v, v
                                   int mask_kind, const int64_t* mask_strides, double scale,
                                   int dtype, void* stream);
 
+/* Kernel choice for widek_attention_fwd: 0 = tcgen05/TMEM flash kernel
+ * where it applies (bf16/f16, head_dim 64, no explicit mask), else the
+ * warp-level MMA or CUDA-core kernels (default); 1 = never the tcgen05
+ * kernel. Process-wide; for tests and measurements. No reference
+ * counterpart (the reference has a single torch SDPA call). */
+WIDEK_API int widek_attention_set_variant(int variant);
+
 #ifdef __cplusplus
 }
 #endif

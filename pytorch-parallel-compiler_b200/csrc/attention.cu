@@ -7,33 +7,22 @@
 // h*dh), so no head-split copies exist; the output is written directly as
 // [n, b, tq, D] (head h at columns h*dh) for the output projection.
 //
-// bf16/f16 with dh in {64, 128}: tensor-core kernel (m16n8k16 MMA, 64 query
-// rows per CTA, 64-key tiles double-buffered with cp.async, XOR-swizzled
-// shared memory for conflict-free ldmatrix). fp32 and other head sizes: a
-// CUDA-core kernel (one warp per query row, fp32 FFMA).
+// bf16/f16, dh = 64, no explicit mask: the tcgen05/TMEM kernel of
+// attention_sm100.cu. Other bf16/f16 calls with dh in {64, 128}: a warp-level
+// tensor-core kernel here (m16n8k16 MMA, 64 or 128 query rows per CTA,
+// 64-key tiles double-buffered with cp.async, XOR-swizzled shared memory for
+// conflict-free ldmatrix). fp32 and other head sizes: a CUDA-core kernel (one
+// warp per query row, fp32 FFMA).
 //
 // Masking: causal (key index <= query index, top-left aligned as
 // torch.nn.functional.scaled_dot_product_attention), and/or an explicit mask
 // broadcast to [n*b, heads, tq, tk] through element strides: boolean (true =
 // attend) or additive (added to the scaled scores). Rows with no attended key
 // produce zeros.
-#include "common.cuh"
+#include "attention.cuh"
 
 namespace widek {
 namespace {
-
-struct AttnArgs {
-    const void* q;
-    const void* k;
-    const void* v;
-    void* o;
-    const void* mask;            // nullable
-    int64_t sq, sk, sv, so;      // row strides (elements) of q, k, v, o
-    int64_t ms_b, ms_h, ms_q, ms_k;  // mask strides (elements) over [nb, h, tq, tk]
-    int nb, heads, tq, tk, dh;
-    int causal, mask_kind;       // mask_kind: 0 none, 1 bool (uint8), 2 additive (same dtype as q), 3 additive fp32
-    float scale;
-};
 
 template <typename T>
 __device__ __forceinline__ float mask_value(const AttnArgs& a, int64_t bh_b, int h, int qi, int kj, bool& keep) {
@@ -417,8 +406,14 @@ __global__ void __launch_bounds__(NW * 32) attn_mma_kernel(AttnArgs a) {
     }
 }
 
+int g_attn_variant = 0;
+
 template <typename T>
 int launch_attn(AttnArgs a, cudaStream_t st) {
+    if (a.nb * (int64_t)a.heads > 0 && g_attn_variant == 0) {
+        const int rc = launch_attn_tc<T>(a, st);
+        if (rc != WIDEK_ERR_UNSUPPORTED) return rc;
+    }
     const bool mma_ok = !std::is_same<T, float>::value && (a.dh == 64 || a.dh == 128) &&
                         (a.sq % 8 == 0) && (a.sk % 8 == 0) && (a.sv % 8 == 0) && (a.so % 2 == 0) &&
                         aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
@@ -484,7 +479,16 @@ struct AttnLaunch {
 };
 
 }  // namespace
+
+int attn_variant() { return g_attn_variant; }
+
 }  // namespace widek
+
+extern "C" int widek_attention_set_variant(int variant) {
+    if (variant < 0 || variant > 1) return widek::set_error(WIDEK_ERR_INVALID, "attention: unknown variant %d", variant);
+    widek::g_attn_variant = variant;
+    return WIDEK_OK;
+}
 
 extern "C" int widek_attention_fwd(const void* q, const void* k, const void* v, void* o, int64_t q_row_stride,
                                    int64_t k_row_stride, int64_t v_row_stride, int64_t o_row_stride, int64_t nb,
