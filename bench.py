@@ -554,6 +554,7 @@ def run_b200(args):
     from wide_compiler import _native
     _native.load()
     _native.check(_native.lib().widek_linear_set_variant(args.linear_variant), "widek_linear_set_variant")
+    _native.check(_native.lib().widek_attention_set_variant(args.attn_variant), "widek_attention_set_variant")
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     wl = make_workload(args.workload, args.models)
@@ -656,6 +657,10 @@ def run_b200(args):
         cfg["gather"] = bool(gather)
         cfg["cuda_graph"] = bool(args.graph)
         cfg["linear_variant"] = "CTA-pair tiles" if args.linear_variant == 2 else "single-CTA tiles"
+        if args.workload == "cfg5":
+            cfg["attention_variant"] = ("warp-level MMA" if args.attn_variant == 1 else
+                                        "tcgen05/TMEM" + (f", {args.attn_variant - 10}/4 exp2 pairs on FMA"
+                                                          if args.attn_variant >= 10 else ""))
         line = {
             "metric": METRIC, "value": samples / (ms_max * 1e-3), "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
@@ -715,6 +720,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--linear-variant", type=int, default=0,
                     help="tensor-core GEMM tiling: 0 auto (single-CTA), 1 single-CTA tiles, 2 CTA-pair tiles")
+    ap.add_argument("--attn-variant", type=int, default=0,
+                    help="attention core: 0 tcgen05/TMEM kernel (default exponential split), 1 warp-level MMA "
+                         "kernel, 10/11/12 tcgen05 with 0/1/2 of every 4 exponential pairs on the FMA pipe")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -304,8 +304,11 @@ WIDEK_API int widek_attention_fwd(const void* q, const void* k, const void* v, v
 /* Kernel choice for widek_attention_fwd: 0 = tcgen05/TMEM flash kernel
  * where it applies (bf16/f16, head_dim 64, no explicit mask), else the
  * warp-level MMA or CUDA-core kernels (default); 1 = never the tcgen05
- * kernel. Process-wide; for tests and measurements. No reference
- * counterpart (the reference has a single torch SDPA call). */
+ * kernel; 10 + k (k = 0, 1, 2) = as 0, with k of every 4 column pairs of
+ * exponentials computed by an FMA-pipe polynomial instead of the
+ * special-function unit (0 and 1 reset k to its default, 1).
+ * Process-wide; for tests and measurements. No reference counterpart (the
+ * reference has a single torch SDPA call). */
 WIDEK_API int widek_attention_set_variant(int variant);
 
 #ifdef __cplusplus

@@ -407,6 +407,7 @@ __global__ void __launch_bounds__(NW * 32) attn_mma_kernel(AttnArgs a) {
 }
 
 int g_attn_variant = 0;
+int g_attn_poly_pairs = 1;
 
 template <typename T>
 int launch_attn(AttnArgs a, cudaStream_t st) {
@@ -481,13 +482,22 @@ struct AttnLaunch {
 }  // namespace
 
 int attn_variant() { return g_attn_variant; }
+int attn_poly_pairs() { return g_attn_poly_pairs; }
 
 }  // namespace widek
 
 extern "C" int widek_attention_set_variant(int variant) {
-    if (variant < 0 || variant > 1) return widek::set_error(WIDEK_ERR_INVALID, "attention: unknown variant %d", variant);
-    widek::g_attn_variant = variant;
-    return WIDEK_OK;
+    if (variant == 0 || variant == 1) {
+        widek::g_attn_variant = variant;
+        widek::g_attn_poly_pairs = 1;
+        return WIDEK_OK;
+    }
+    if (variant >= 10 && variant <= 12) {
+        widek::g_attn_variant = 0;
+        widek::g_attn_poly_pairs = variant - 10;
+        return WIDEK_OK;
+    }
+    return widek::set_error(WIDEK_ERR_INVALID, "attention: unknown variant %d", variant);
 }
 
 extern "C" int widek_attention_fwd(const void* q, const void* k, const void* v, void* o, int64_t q_row_stride,

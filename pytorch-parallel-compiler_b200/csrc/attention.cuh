@@ -28,5 +28,8 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st);
 
 // 0: tcgen05 kernel where it applies (default); 1: warp-level MMA kernel.
 int attn_variant();
+// Column pairs out of every 4 whose exponentials the tcgen05 kernel computes
+// with the FMA-pipe polynomial instead of ex2.approx (0..2).
+int attn_poly_pairs();
 
 }  // namespace widek

@@ -2,31 +2,47 @@
 //
 // One CTA computes 256 query rows of one head as two 128-row tiles (Q0, Q1)
 // that take turns on the tensor core while the other tile's softmax runs on
-// the CUDA cores. 320 threads, warp-specialised:
+// the CUDA cores. 352 threads, warp-specialised:
 //   warps 0..3  softmax for Q0, warps 4..7 softmax for Q1: thread = one query
 //               row = one TMEM lane (warp % 4 selects the lane quarter).
 //   warp 8      TMA producer: Q0/Q1 once, then 128-key tiles of K and V
-//               through a 3-stage ring (128-byte swizzle, read in place from
-//               the projection output through 3-D maps [nb][t][columns]).
-//   warp 9      allocates TMEM and issues the MMAs from one elected thread:
+//               through two 2-stage rings (128-byte swizzle, read in place
+//               from the projection output through 3-D maps [nb][t][columns]);
+//               K of tile j+1 is fetched before V of tile j.
+//   warps 9, 10 issue the MMAs of tile 0 / tile 1 from one elected thread
+//               each (warp 9 also allocates TMEM):
 //                 S_i = Q_i K_j^T   (M=128, N=128, K=64)  -> TMEM, fp32
 //                 O_i += P_i V_j    (M=128, N=64,  K=128) -> TMEM, fp32
+//               S_i(j+1) is issued as soon as the softmax has read S_i(j),
+//               so the next scores are ready when the softmax needs them;
+//               with one issuing warp per tile neither tile's pipeline waits
+//               for the other's softmax.
 //               P_i (bf16/f16) is written by the softmax warps into shared
-//               memory in the K-major 128-byte-swizzled layout; V is used as
-//               an MN-major operand straight from its TMA tile.
+//               memory (two buffers per tile) in the K-major 128-byte-swizzled
+//               layout; V is used as an MN-major operand straight from its
+//               TMA tile.
 // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384).
 //
-// Online softmax (log2 domain, scale folded into one FMA before ex2): each
-// thread owns a whole row, so row max and row sum need no shuffles. The
-// running max is only moved (and O rescaled in TMEM) when the new tile's max
-// exceeds it by more than 2^8; otherwise P entries up to 256 are kept, which
-// the fp32 accumulators absorb, and the final division by the row sum
-// cancels the stale scale.
+// Online softmax (log2 domain, scale folded into one FMA before the
+// exponential): each thread owns a whole row, so row max and row sum need no
+// shuffles; both are computed as trees of independent partial results with
+// the 2-wide fp32 instructions of sm_100. The running max is only moved (and
+// O rescaled in TMEM) when the new tile's max exceeds it by more than 2^8;
+// otherwise P entries up to 256 are kept, which the fp32 accumulators absorb,
+// and the final division by the row sum cancels the stale scale. Because of
+// that, the softmax normally never waits for the previous P V product: with
+// two P buffers it only needs the product from two tiles back.
 //
-// Causal (top-left aligned): Q0 stops one key tile before Q1; per-element
-// masking only on tiles that cross the diagonal or the end of the keys. The
-// output is normalised, staged in shared memory (the tile's P buffer, free by
-// then) and written by one TMA store per warp (rows past tq are clipped).
+// Exponentials: ex2.approx on the special-function unit, and for NPOLY of
+// every 4 column pairs a polynomial on the FMA pipe (rint range reduction,
+// 2^f on [-1/2, 1/2] by a degree-3 fit with 7.5e-5 relative error, made by
+// fit_exp2_poly.py), which spreads the work over both pipes.
+//
+// Causal (top-left aligned): Q0 stops one key tile before Q1; on tiles that
+// cross the diagonal, 32-key chunks that no row of a warp attends are not
+// exponentiated. The output is normalised, staged in
+// shared memory (a P buffer, free by then) and written by one TMA store per
+// warp (rows past tq are clipped).
 //
 // Every wait is bounded; on a timeout the CTA records DEV_ERR_ATTN_TIMEOUT,
 // stops issuing, lets its copies and MMAs in flight finish and frees TMEM.
@@ -46,10 +62,9 @@ using namespace sm100;
 constexpr int kQT = 128;        // query rows per tile
 constexpr int kKT = 128;        // keys per tile
 constexpr int kHD = 64;         // head dim
-constexpr int kStages = 3;
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kTmaWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;    // and 10: one MMA warp per query tile
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;
 
@@ -57,20 +72,50 @@ struct Smem {
     static constexpr uint32_t Q_BYTES = kQT * kHD * 2;      // 16 KB
     static constexpr uint32_t KV_BYTES = kKT * kHD * 2;     // 16 KB
     static constexpr uint32_t P_BYTES = kQT * kKT * 2;      // 32 KB: two 64-key halves of 16 KB
-    static constexpr uint32_t OFF_Q = 0;
-    static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;
-    static constexpr uint32_t OFF_V = OFF_K + kStages * KV_BYTES;
-    static constexpr uint32_t OFF_P = OFF_V + kStages * KV_BYTES;
-    static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
-    // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], o_full[2], done
-    static constexpr uint32_t NBAR = 1 + 3 * kStages + 8 + 1;
+    static constexpr uint32_t OFF_Q = 0;                    // [2 tiles]
+    static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;  // [2 stages]
+    static constexpr uint32_t OFF_V = OFF_K + 2 * KV_BYTES; // [2 stages]
+    static constexpr uint32_t OFF_P = OFF_V + 2 * KV_BYTES; // [2 tiles][2 buffers]
+    static constexpr uint32_t OFF_BAR = OFF_P + 4 * P_BYTES;
+    // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full[2], o_full[2][2], done[2]
+    static constexpr uint32_t NBAR = 1 + 8 + 6 + 4 + 2;
     static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NBAR * 8 + 16;
 };
+static_assert(Smem::TOTAL <= 232448, "attention smem over the per-CTA limit");
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x for two values on the FMA/ALU pipes. x = n + f with n = rint(x) (by
+// adding and subtracting 1.5 * 2^23), 2^f from a degree-3 polynomial on
+// [-1/2, 1/2], times 2^n built in the exponent field. x is clamped at -127,
+// where 2^n is built as exactly +0, so masked scores (-inf) give exactly 0;
+// results are never negative. Valid for x <= 127.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    constexpr float kMagic = 12582912.f;   // 1.5 * 2^23
+    x.x = fmaxf(x.x, -127.f);
+    x.y = fmaxf(x.y, -127.f);
+    const float2 t = __fadd2_rn(x, make_float2(kMagic, kMagic));
+    const float2 n = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+    const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(make_float2(0.0551716648f, 0.0551716648f), f, make_float2(0.242611125f, 0.242611125f));
+    p = __ffma2_rn(p, f, make_float2(0.693260968f, 0.693260968f));
+    p = __ffma2_rn(p, f, make_float2(0.999928057f, 0.999928057f));
+    // The low bits of t hold n (two's complement): (n << 23) + bits(1.0f) is
+    // the float 2^n for n >= -126 and +0 for n = -127 (the 1.5 * 2^23 part of
+    // t shifts out).
+    const float2 two_n = make_float2(__int_as_float((__float_as_int(t.x) << 23) + 0x3F800000),
+                                     __int_as_float((__float_as_int(t.y) << 23) + 0x3F800000));
+    return __fmul2_rn(p, two_n);
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
 
 template <typename T>
@@ -84,6 +129,14 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// 32 lanes x 32 columns of fp32 into v[0..31] of each thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr, r);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
 }
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -124,22 +177,22 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, c
 }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Writes 64 packed pairs (128 values of one row) into a K-major, 128-byte
-// swizzled [128 rows][128 columns] tile: two 64-column halves of 16 KB, row r
-// at r*128 bytes within a half, 16-byte unit u stored at unit u ^ (r % 8).
-__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, const uint32_t (&pk)[64]) {
+// S = Q K^T for one 128-row tile: 4 MMAs over the 64-wide head dim.
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_q, uint32_t a_k, uint32_t idesc) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    for (int kk = 0; kk < kHD / 16; ++kk)
+        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a_q + kk * 32), sdesc_kmajor_sw128(a_k + kk * 32), idesc, kk != 0);
+}
+// O (+)= P V: 8 MMAs over the 128 keys; P K-major in two 64-key halves,
+// V MN-major with 16 key rows (2 KB) per MMA.
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t a_p, uint32_t a_v, uint32_t idesc, bool accum) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int base = half * 32 + u * 4;
-            uint4 v = make_uint4(pk[base], pk[base + 1], pk[base + 2], pk[base + 3]);
-            *reinterpret_cast<uint4*>(tile + half * 16384 + r * 128 + ((u ^ (r & 7)) << 4)) = v;
-        }
-    }
+    for (int kk = 0; kk < kKT / 16; ++kk)
+        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a_p + (kk >> 2) * 16384 + (kk & 3) * 32),
+                    sdesc_mnmajor_sw128(a_v + kk * 16 * 128), idesc, accum || kk != 0);
 }
 
-template <typename T>
+template <typename T, int NPOLY>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o, int heads,
@@ -155,15 +208,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sV = smem + Smem::OFF_V;
     uint8_t* sP = smem + Smem::OFF_P;
     uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + Smem::OFF_BAR);
-    uint64_t* k_full = q_full + 1;
-    uint64_t* v_full = k_full + kStages;
-    uint64_t* kv_empty = v_full + kStages;
-    uint64_t* s_full = kv_empty + kStages;   // [2]
-    uint64_t* s_free = s_full + 2;           // [2]
-    uint64_t* p_full = s_free + 2;           // [2]
-    uint64_t* o_full = p_full + 2;           // [2]
-    uint64_t* done = o_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* k_full = q_full + 1;      // [2]
+    uint64_t* k_empty = k_full + 2;     // [2]
+    uint64_t* v_full = k_empty + 2;     // [2]
+    uint64_t* v_empty = v_full + 2;     // [2]
+    uint64_t* s_full = v_empty + 2;     // [2 tiles]
+    uint64_t* s_free = s_full + 2;      // [2 tiles]
+    uint64_t* p_full = s_free + 2;      // [2 tiles]
+    uint64_t* o_full = p_full + 2;      // [2 tiles][2 P buffers]
+    uint64_t* done = o_full + 4;        // [2 MMA warps]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -187,18 +241,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < 2; ++s) {
             mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 2);
             mbar_init(&v_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&v_empty[s], 2);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], 128);
             mbar_init(&p_full[i], 128);
-            mbar_init(&o_full[i], 1);
+            mbar_init(&o_full[2 * i], 1);
+            mbar_init(&o_full[2 * i + 1], 1);
         }
-        mbar_init(done, 1);
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -219,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kTmaWarp) {
         // ------------------------------------------------------------------
-        // TMA producer
+        // TMA producer: Q0/Q1, then K(0), and per tile j: K(j+1), V(j).
         // ------------------------------------------------------------------
         const uint64_t pol = l2_policy_evict_normal();
         const int col = h * kHD;
@@ -231,20 +288,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (rows[i] > 0) tma_load_3d(sQ + i * Smem::Q_BYTES, &tm_q, q_full, col, q0 + i * kQT, b, pol);
         }
         __syncwarp();
-        int issued = 0;
+        int k_issued = 0, v_issued = 0;
         bool ok = true;
-        for (int j = 0; j < nmax; ++j) {
-            const int s = j % kStages;
-            const uint32_t ph = (uint32_t)((j / kStages) & 1);
-            if (!mbar_wait_warp(&kv_empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&k_full[s], Smem::KV_BYTES);
-                tma_load_3d(sK + s * Smem::KV_BYTES, &tm_k, &k_full[s], col, j * kKT, b, pol);
-                mbar_arrive_expect_tx(&v_full[s], Smem::KV_BYTES);
-                tma_load_3d(sV + s * Smem::KV_BYTES, &tm_v, &v_full[s], col, j * kKT, b, pol);
+        for (int step = 0; step <= nmax && ok; ++step) {
+            // step 0 loads K(0); step j+1 loads K(j+1) (if any) and V(j).
+            const int jk = step;
+            if (jk < nmax) {
+                const int s = jk & 1;
+                if (!mbar_wait_warp(&k_empty[s], (uint32_t)(((jk >> 1) & 1) ^ 1), abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&k_full[s], Smem::KV_BYTES);
+                    tma_load_3d(sK + s * Smem::KV_BYTES, &tm_k, &k_full[s], col, jk * kKT, b, pol);
+                }
+                __syncwarp();
+                ++k_issued;
             }
-            __syncwarp();
-            ++issued;
+            const int jv = step - 1;
+            if (jv >= 0) {
+                const int s = jv & 1;
+                if (!mbar_wait_warp(&v_empty[s], (uint32_t)(((jv >> 1) & 1) ^ 1), abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&v_full[s], Smem::KV_BYTES);
+                    tma_load_3d(sV + s * Smem::KV_BYTES, &tm_v, &v_full[s], col, jv * kKT, b, pol);
+                }
+                __syncwarp();
+                ++v_issued;
+            }
         }
         if (!ok) {
             *abort_flag = 1;
@@ -254,74 +323,72 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Copies still in flight land before the CTA's smem is released.
             const volatile int never = 0;
             mbar_wait(q_full, 0, &never);
-            const int inflight = issued < kStages ? issued : kStages;
-            for (int t = 1; t <= inflight; ++t) {
-                const int idx = issued - t;
-                const uint32_t ph = (uint32_t)((idx / kStages) & 1);
-                mbar_wait(&k_full[idx % kStages], ph, &never);
-                mbar_wait(&v_full[idx % kStages], ph, &never);
+            for (int t = 1; t <= 2; ++t) {
+                const int jk = k_issued - t, jv = v_issued - t;
+                if (jk >= 0) mbar_wait(&k_full[jk & 1], (uint32_t)((jk >> 1) & 1), &never);
+                if (jv >= 0) mbar_wait(&v_full[jv & 1], (uint32_t)((jv >> 1) & 1), &never);
             }
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp >= kMmaWarp) {
         // ------------------------------------------------------------------
-        // MMA issuer
+        // MMA issuers: warp 9 + i serves query tile i, so that each tile's
+        // S(j+1) follows its own softmax without waiting for the other
+        // tile. Both warps commit every K/V stage (count-2 "empty"
+        // barriers), also the stages their tile no longer needs; each waits
+        // for a stage's "full" barrier before committing its "empty" one,
+        // so that its arrival always lands on the phase of that load.
         // ------------------------------------------------------------------
+        const int i = warp - kMmaWarp;
+        const int n = ntile[i];
+        const uint32_t aQ = smem_addr(sQ) + i * Smem::Q_BYTES, aK = smem_addr(sK), aV = smem_addr(sV);
+        const uint32_t aP = smem_addr(sP) + 2 * i * Smem::P_BYTES;
+        const uint32_t dS = tmem_base + i * kKT, dO = tmem_base + 2 * kKT + i * kHD;
         bool ok = mbar_wait_warp(q_full, 0, abort_flag);
-        const uint32_t aQ = smem_addr(sQ), aK = smem_addr(sK), aV = smem_addr(sV), aP = smem_addr(sP);
-        auto issue_s = [&](int i, int s) {
-            const uint32_t a0 = aQ + i * Smem::Q_BYTES, b0 = aK + s * Smem::KV_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < kHD / 16; ++kk)
-                umma_f16_ss(tmem_base + i * kKT, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32),
-                            IDESC_S, kk != 0);
-            umma_commit(&s_full[i]);
-        };
-        auto issue_pv = [&](int i, int s, int j) {
-            const uint32_t a0 = aP + i * Smem::P_BYTES, b0 = aV + s * Smem::KV_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < kKT / 16; ++kk)
-                umma_f16_ss(tmem_base + 2 * kKT + i * kHD,
-                            sdesc_kmajor_sw128(a0 + (kk >> 2) * 16384 + (kk & 3) * 32),
-                            sdesc_mnmajor_sw128(b0 + kk * 16 * 128), IDESC_PV, (j | kk) != 0);
-            umma_commit(&o_full[i]);
-        };
         if (ok && nmax > 0) {
             ok = mbar_wait_warp(&k_full[0], 0, abort_flag);
             if (ok) {
                 tc_fence_after();
-                if (lane == 0)
-                    for (int i = 0; i < 2; ++i)
-                        if (ntile[i] > 0) issue_s(i, 0);
+                if (lane == 0) {
+                    if (n > 0) {
+                        issue_qk(dS, aQ, aK, IDESC_S);
+                        umma_commit(&s_full[i]);
+                    }
+                    umma_commit(&k_empty[0]);
+                }
                 __syncwarp();
             }
         }
         for (int j = 0; j < nmax && ok; ++j) {
-            const int s = j % kStages;
-            const uint32_t ph = (uint32_t)((j / kStages) & 1);
-            const int s1 = (j + 1) % kStages;
-            const uint32_t ph1 = (uint32_t)(((j + 1) / kStages) & 1);
-            bool k1_ready = false, v_ready = false;
-            for (int i = 0; i < 2 && ok; ++i) {
-                if (j + 1 < ntile[i]) {
-                    // Next S of this tile as soon as its softmax has read the current one.
-                    if (!k1_ready) { ok = mbar_wait_warp(&k_full[s1], ph1, abort_flag); k1_ready = true; }
-                    if (ok) ok = mbar_wait_warp(&s_free[i], (uint32_t)(j & 1), abort_flag);
+            const int s1 = (j + 1) & 1;
+            const int sv = j & 1;
+            if (j + 1 < nmax) {
+                ok = mbar_wait_warp(&k_full[s1], (uint32_t)(((j + 1) >> 1) & 1), abort_flag);
+                if (!ok) break;
+                if (j + 1 < n) {
+                    // Next S as soon as the softmax has read the current one.
+                    ok = mbar_wait_warp(&s_free[i], (uint32_t)(j & 1), abort_flag);
                     if (!ok) break;
                     tc_fence_after();
-                    if (lane == 0) issue_s(i, s1);
-                    __syncwarp();
+                    if (lane == 0) {
+                        issue_qk(dS, aQ, aK + s1 * Smem::KV_BYTES, IDESC_S);
+                        umma_commit(&s_full[i]);
+                    }
                 }
-                if (j < ntile[i]) {
-                    if (!v_ready) { ok = mbar_wait_warp(&v_full[s], ph, abort_flag); v_ready = true; }
-                    if (ok) ok = mbar_wait_warp(&p_full[i], (uint32_t)(j & 1), abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (lane == 0) issue_pv(i, s, j);
-                    __syncwarp();
+                if (lane == 0) umma_commit(&k_empty[s1]);
+                __syncwarp();
+            }
+            ok = mbar_wait_warp(&v_full[sv], (uint32_t)((j >> 1) & 1), abort_flag);
+            if (!ok) break;
+            if (j < n) {
+                ok = mbar_wait_warp(&p_full[i], (uint32_t)(j & 1), abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    issue_pv(dO, aP + (j & 1) * Smem::P_BYTES, aV + sv * Smem::KV_BYTES, IDESC_PV, j > 0);
+                    umma_commit(&o_full[2 * i + (j & 1)]);
                 }
             }
-            if (!ok) break;
-            if (lane == 0) umma_commit(&kv_empty[s]);
+            if (lane == 0) umma_commit(&v_empty[sv]);
             __syncwarp();
         }
         if (!ok) {
@@ -329,10 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             raise_device_error(err, DEV_ERR_ATTN_TIMEOUT);
         }
         // Every MMA issued by this thread completes before TMEM is freed.
-        if (lane == 0) umma_commit(done);
+        if (lane == 0) umma_commit(&done[i]);
         __syncwarp();
         const volatile int never = 0;
-        mbar_wait(done, 0, &never);
+        mbar_wait(&done[i], 0, &never);
     } else {
         // ------------------------------------------------------------------
         // Softmax: warps 4i..4i+3 own query tile i, one row per thread.
@@ -345,37 +412,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
         const uint32_t tS = tmem_base + lane_off + i * kKT;
         const uint32_t tO = tmem_base + lane_off + 2 * kKT + i * kHD;
-        uint8_t* myP = sP + i * Smem::P_BYTES;
+        uint8_t* myP = sP + 2 * i * Smem::P_BYTES;
         const int n = ntile[i];
+        const float2 sl2x2 = make_float2(sl2, sl2);
         float m_used = -INFINITY;   // running max, log2 domain (scaled)
-        float l = 0.f;
+        float2 lsum[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) lsum[e] = make_float2(0.f, 0.f);
         bool ok = true;
         for (int j = 0; j < n; ++j) {
             if (!mbar_wait_warp(&s_full[i], (uint32_t)(j & 1), abort_flag)) { ok = false; break; }
             tc_fence_after();
-            uint32_t su[kKT];
+            const int kbase = j * kKT;
+            // Keys of this tile attended by at least one row of the warp.
+            int kvalid = min(kKT, tk - kbase);
+            if (causal) kvalid = min(kvalid, wrow0 + 32 - kbase);
+            const int nch = (max(kvalid, 0) + 31) >> 5;   // 32-key chunks to process (warp-uniform)
+            // All four chunks are read (a conditional read costs registers);
+            // the chunks no row attends are skipped below.
+            float s[kKT];
 #pragma unroll
-            for (int c = 0; c < kKT; c += 32)
-                tmem_ld_32x32b_x32(tS + c, *reinterpret_cast<uint32_t(*)[32]>(su + c));
+            for (int cc = 0; cc < 4; ++cc) tmem_ld32(tS + cc * 32, s + cc * 32);
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&s_free[i]);
 
-            const int kbase = j * kKT;
             const bool need_mask = (kbase + kKT > tk) || (causal && kbase + kKT - 1 > wrow0);
-            float s[kKT];
-#pragma unroll
-            for (int c = 0; c < kKT; ++c) s[c] = __uint_as_float(su[c]);
             if (need_mask) {
                 const int lim = causal ? min(tk - kbase, qrow - kbase + 1) : tk - kbase;
 #pragma unroll
                 for (int c = 0; c < kKT; ++c)
                     if (c >= lim) s[c] = -INFINITY;
             }
-            float mx = s[0];
+            // Row max: four independent 3-input max chains per chunk.
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 1; c < kKT; ++c) mx = fmaxf(mx, s[c]);
-            const float m_tile = mx * sl2;
+            for (int cc = 0; cc < 4; ++cc) {
+                if (cc < nch) {
+#pragma unroll
+                    for (int c = cc * 32; c < cc * 32 + 32; c += 8) {
+                        mx4[0] = max3(mx4[0], s[c], s[c + 1]);
+                        mx4[1] = max3(mx4[1], s[c + 2], s[c + 3]);
+                        mx4[2] = max3(mx4[2], s[c + 4], s[c + 5]);
+                        mx4[3] = max3(mx4[3], s[c + 6], s[c + 7]);
+                    }
+                }
+            }
+            const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
             const float m_new = fmaxf(m_used, m_tile);
             const bool rescale = m_new > m_used + kRescaleLog2;
             float alpha = 1.f;
@@ -383,35 +466,73 @@ __global__ void __launch_bounds__(kThreads, 1)
                 alpha = ex2(m_used - m_new);
                 m_used = m_new;
             }
-            l *= alpha;
             const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+            const float2 negm2 = make_float2(neg_m, neg_m);
+            const float2 alpha2 = make_float2(alpha, alpha);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) lsum[e] = __fmul2_rn(lsum[e], alpha2);
             uint32_t pk[kKT / 2];
 #pragma unroll
-            for (int c = 0; c < kKT; c += 2) {
-                const float p0 = ex2(fmaf(s[c], sl2, neg_m));
-                const float p1 = ex2(fmaf(s[c + 1], sl2, neg_m));
-                l += p0 + p1;
-                pk[c / 2] = pack2<T>(p0, p1);
-            }
-            if (j > 0) {
-                // P_i(j-1) V has finished: the P buffer is free and O holds
-                // the sum through tile j-1.
-                if (!mbar_wait_warp(&o_full[i], (uint32_t)((j - 1) & 1), abort_flag)) { ok = false; break; }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+            for (int cc = 0; cc < 4; ++cc) {
+                if (cc < nch) {
 #pragma unroll
-                    for (int c = 0; c < kHD; c += 32) {
-                        uint32_t o[32];
-                        tmem_ld_32x32b_x32(tO + c, o);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st_32x32b_x32(tO + c, o);
+                    for (int c = cc * 32; c < cc * 32 + 32; c += 2) {
+                        const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sl2x2, negm2);
+                        float2 p;
+                        if (((c >> 1) & 3) < NPOLY) {
+                            p = exp2_poly2(x);
+                        } else {
+                            p.x = ex2(x.x);
+                            p.y = ex2(x.y);
+                        }
+                        lsum[(c >> 1) & 3] = __fadd2_rn(lsum[(c >> 1) & 3], p);
+                        pk[c >> 1] = pack2<T>(p.x, p.y);
                     }
-                    tmem_st_wait();
+                } else {
+#pragma unroll
+                    for (int c = cc * 32; c < cc * 32 + 32; c += 2) pk[c >> 1] = 0u;
                 }
             }
-            store_row_sw128(myP, r, pk);
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                // O must be rescaled before P_i(j) V joins it: wait for
+                // P_i(j-1) V, then scale the row in TMEM.
+                if (!mbar_wait_warp(&o_full[2 * i + ((j - 1) & 1)], (uint32_t)(((j - 1) >> 1) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < kHD; c += 32) {
+                    uint32_t o[32];
+                    tmem_ld_32x32b_x32(tO + c, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
+                                                    alpha2);
+                        o[e] = __float_as_uint(v.x);
+                        o[e + 1] = __float_as_uint(v.y);
+                    }
+                    tmem_st_32x32b_x32(tO + c, o);
+                }
+                tmem_st_wait();
+            }
+            // P buffer j%2 was last read by P_i(j-2) V.
+            if (j >= 2 &&
+                !mbar_wait_warp(&o_full[2 * i + (j & 1)], (uint32_t)(((j - 2) >> 1) & 1), abort_flag)) {
+                ok = false;
+                break;
+            }
+            uint8_t* pb = myP + (j & 1) * Smem::P_BYTES;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int base = half * 32 + u * 4;
+                    *reinterpret_cast<uint4*>(pb + half * 16384 + r * 128 + ((u ^ (r & 7)) << 4)) =
+                        make_uint4(pk[base], pk[base + 1], pk[base + 2], pk[base + 3]);
+                }
+            }
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_full[i]);
@@ -422,28 +543,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ok is warp-uniform here (every wait above is), and so is rows[i].
         if (ok && rows[i] > 0 && n > 0) {
-            if (!mbar_wait_warp(&o_full[i], (uint32_t)((n - 1) & 1), abort_flag)) {
+            const int jl = n - 1;
+            if (!mbar_wait_warp(&o_full[2 * i + (jl & 1)], (uint32_t)((jl >> 1) & 1), abort_flag)) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_ATTN_TIMEOUT);
             } else if (wrow0 < tq) {
                 tc_fence_after();
-                uint32_t ou[kHD];
-#pragma unroll
-                for (int c = 0; c < kHD; c += 32)
-                    tmem_ld_32x32b_x32(tO + c, *reinterpret_cast<uint32_t(*)[32]>(ou + c));
+                float o[kHD];
+                tmem_ld32(tO, o);
+                tmem_ld32(tO + 32, o + 32);
                 tmem_ld_wait();
+                const float2 l2 = __fadd2_rn(__fadd2_rn(lsum[0], lsum[1]), __fadd2_rn(lsum[2], lsum[3]));
+                const float l = l2.x + l2.y;
                 const float inv = l > 0.f ? 1.f / l : 0.f;
                 // Stage this warp's 32 rows x 64 columns in its own 4 KB slice
-                // of the P buffer (128-byte swizzle, as the TMA store reads it)
-                // and write them with one TMA store; rows past tq are clipped.
-                uint8_t* stage = myP + qd * 32 * 128;
+                // of the last P buffer (128-byte swizzle, as the TMA store
+                // reads it) and write them with one TMA store; rows past tq
+                // are clipped.
+                uint8_t* stage = myP + (jl & 1) * Smem::P_BYTES + qd * 32 * 128;
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int c = u * 8 + e * 2;
-                        w[e] = pack2<T>(__uint_as_float(ou[c]) * inv, __uint_as_float(ou[c + 1]) * inv);
+                        w[e] = pack2<T>(o[c] * inv, o[c + 1] * inv);
                     }
                     *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
                         make_uint4(w[0], w[1], w[2], w[3]);
@@ -485,6 +609,24 @@ int rows_map(CUtensorMap* m, const void* base, int64_t stride, int t, int nb, in
     return encode_tmap_tiled(m, tmap_dtype<T>(), 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+template <typename T, int NPOLY>
+int launch_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& o,
+              const AttnArgs& a, int64_t blocks, cudaStream_t st) {
+    auto kern = attn_tc_kernel<T, NPOLY>;
+    static bool attr_done[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem::TOTAL) !=
+            cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "attention: cannot reserve %u bytes of shared memory", Smem::TOTAL);
+        attr_done[dev] = true;
+    }
+    const float sl2 = a.scale * 1.4426950408889634f;
+    kern<<<(unsigned)blocks, kThreads, Smem::TOTAL, st>>>(q, k, v, o, a.heads, a.tq, a.tk, a.causal, sl2,
+                                                          device_error_ptr());
+    return check_launch("widek_attention_fwd (tcgen05)");
+}
+
 }  // namespace
 
 template <typename T>
@@ -493,11 +635,11 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st) {
         return WIDEK_ERR_UNSUPPORTED;
     } else {
         const int64_t width = (int64_t)a.heads * kHD;
-        const bool fits = a.dh == kHD && a.mask_kind == 0 && a.scale > 0.f && a.tk >= 0 &&
+        const bool fits = a.dh == kHD && a.mask_kind == 0 && a.scale > 0.f && a.tk > 0 &&
                           a.sq % 8 == 0 && a.sk % 8 == 0 && a.sv % 8 == 0 && a.so % 8 == 0 &&
                           a.sq >= width && a.sk >= width && a.sv >= width && a.so >= width &&
                           aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.o);
-        if (!fits || a.tk == 0) return WIDEK_ERR_UNSUPPORTED;
+        if (!fits) return WIDEK_ERR_UNSUPPORTED;
         const int64_t nqb = (a.tq + 2 * kQT - 1) / (2 * kQT);
         const int64_t blocks = nqb * a.nb * (int64_t)a.heads;
         if (blocks > 0x7fffffff) return WIDEK_ERR_UNSUPPORTED;
@@ -507,19 +649,11 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st) {
         if (!rc) rc = rows_map<T>(&tv_, a.v, a.sv, a.tk, a.nb, a.heads, kKT);
         if (!rc) rc = rows_map<T>(&to_, a.o, a.so, a.tq, a.nb, a.heads, 32);
         if (rc) return rc;
-        auto kern = attn_tc_kernel<T>;
-        static bool attr_done[64] = {false};
-        const int dev = current_device();
-        if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem::TOTAL) !=
-                cudaSuccess)
-                return set_error(WIDEK_ERR_CUDA, "attention: cannot reserve %u bytes of shared memory", Smem::TOTAL);
-            attr_done[dev] = true;
+        switch (attn_poly_pairs()) {
+            case 0: return launch_tc<T, 0>(tq_, tk_, tv_, to_, a, blocks, st);
+            case 2: return launch_tc<T, 2>(tq_, tk_, tv_, to_, a, blocks, st);
+            default: return launch_tc<T, 1>(tq_, tk_, tv_, to_, a, blocks, st);
         }
-        const float sl2 = a.scale * 1.4426950408889634f;
-        kern<<<(unsigned)blocks, kThreads, Smem::TOTAL, st>>>(tq_, tk_, tv_, to_, a.heads, a.tq, a.tk, a.causal,
-                                                              sl2, device_error_ptr());
-        return check_launch("widek_attention_fwd (tcgen05)");
     }
 }
 
