@@ -6,22 +6,22 @@
 //   warps 0..3  softmax for Q0, warps 4..7 softmax for Q1: thread = one query
 //               row = one TMEM lane (warp % 4 selects the lane quarter).
 //   warp 8      TMA producer: Q0/Q1 once, then 128-key tiles of K and V
-//               through two 2-stage rings (128-byte swizzle, read in place
+//               through two 3-stage rings (128-byte swizzle, read in place
 //               from the projection output through 3-D maps [nb][t][columns]);
 //               K of tile j+1 is fetched before V of tile j.
 //   warps 9, 10 issue the MMAs of tile 0 / tile 1 from one elected thread
 //               each (warp 9 also allocates TMEM):
-//                 S_i = Q_i K_j^T   (M=128, N=128, K=64)  -> TMEM, fp32
-//                 O_i += P_i V_j    (M=128, N=64,  K=128) -> TMEM, fp32
+//                 S_i = Q_i K_j^T   (M=128, N=128, K=64), A and B in smem
+//                 O_i += P_i V_j    (M=128, N=64,  K=128), A (P) in TMEM,
+//                                   B (V) in smem as an MN-major operand
 //               S_i(j+1) is issued as soon as the softmax has read S_i(j),
 //               so the next scores are ready when the softmax needs them;
 //               with one issuing warp per tile neither tile's pipeline waits
 //               for the other's softmax.
-//               P_i (bf16/f16) is written by the softmax warps into shared
-//               memory (two buffers per tile) in the K-major 128-byte-swizzled
-//               layout; V is used as an MN-major operand straight from its
-//               TMA tile.
-// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384).
+// TMEM columns (512): S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384),
+// P0 [384,448), P1 [448,512) (P: bf16/f16 pairs, one row per lane).
+// Keeping P in TMEM spares shared memory the P stores and the MMA's P reads,
+// which on B200 share the 128 B/clk per SM that the S MMAs need.
 //
 // Online softmax (log2 domain, scale folded into one FMA before the
 // exponential): each thread owns a whole row, so row max and row sum need no
@@ -29,9 +29,7 @@
 // the 2-wide fp32 instructions of sm_100. The running max is only moved (and
 // O rescaled in TMEM) when the new tile's max exceeds it by more than 2^8;
 // otherwise P entries up to 256 are kept, which the fp32 accumulators absorb,
-// and the final division by the row sum cancels the stale scale. Because of
-// that, the softmax normally never waits for the previous P V product: with
-// two P buffers it only needs the product from two tiles back.
+// and the final division by the row sum cancels the stale scale.
 //
 // Exponentials: ex2.approx on the special-function unit, and for NPOLY of
 // every 4 column pairs a polynomial on the FMA pipe (rint range reduction,
@@ -40,9 +38,9 @@
 //
 // Causal (top-left aligned): Q0 stops one key tile before Q1; on tiles that
 // cross the diagonal, 32-key chunks that no row of a warp attends are not
-// exponentiated. The output is normalised, staged in
-// shared memory (a P buffer, free by then) and written by one TMA store per
-// warp (rows past tq are clipped).
+// exponentiated. The output is normalised, staged in shared memory (the
+// tile's Q buffer, free once its last MMA is done) and written by one TMA
+// store per warp (rows past tq are clipped).
 //
 // Every wait is bounded; on a timeout the CTA records DEV_ERR_ATTN_TIMEOUT,
 // stops issuing, lets its copies and MMAs in flight finish and frees TMEM.
@@ -68,17 +66,17 @@ constexpr int kMmaWarp = 9;    // and 10: one MMA warp per query tile
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;
 
+constexpr int kStages = 3;      // K ring and V ring depth
+
 struct Smem {
     static constexpr uint32_t Q_BYTES = kQT * kHD * 2;      // 16 KB
     static constexpr uint32_t KV_BYTES = kKT * kHD * 2;     // 16 KB
-    static constexpr uint32_t P_BYTES = kQT * kKT * 2;      // 32 KB: two 64-key halves of 16 KB
     static constexpr uint32_t OFF_Q = 0;                    // [2 tiles]
-    static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;  // [2 stages]
-    static constexpr uint32_t OFF_V = OFF_K + 2 * KV_BYTES; // [2 stages]
-    static constexpr uint32_t OFF_P = OFF_V + 2 * KV_BYTES; // [2 tiles][2 buffers]
-    static constexpr uint32_t OFF_BAR = OFF_P + 4 * P_BYTES;
-    // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full[2], o_full[2][2], done[2]
-    static constexpr uint32_t NBAR = 1 + 8 + 6 + 4 + 2;
+    static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;  // [kStages]
+    static constexpr uint32_t OFF_V = OFF_K + kStages * KV_BYTES;
+    static constexpr uint32_t OFF_BAR = OFF_V + kStages * KV_BYTES;
+    // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2], p_full[2], o_full[2], done[2]
+    static constexpr uint32_t NBAR = 1 + 4 * kStages + 10;
     static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NBAR * 8 + 16;
 };
 static_assert(Smem::TOTAL <= 232448, "attention smem over the per-CTA limit");
@@ -183,13 +181,21 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_q, uint32_t
     for (int kk = 0; kk < kHD / 16; ++kk)
         umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a_q + kk * 32), sdesc_kmajor_sw128(a_k + kk * 32), idesc, kk != 0);
 }
-// O (+)= P V: 8 MMAs over the 128 keys; P K-major in two 64-key halves,
-// V MN-major with 16 key rows (2 KB) per MMA.
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t a_p, uint32_t a_v, uint32_t idesc, bool accum) {
+// O (+)= P V: 8 MMAs over the 128 keys; P from TMEM (8 columns of packed
+// pairs per 16 keys), V MN-major with 16 key rows (2 KB) per MMA.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t t_p, uint32_t a_v, uint32_t idesc, bool accum) {
 #pragma unroll
     for (int kk = 0; kk < kKT / 16; ++kk)
-        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a_p + (kk >> 2) * 16384 + (kk & 3) * 32),
-                    sdesc_mnmajor_sw128(a_v + kk * 16 * 128), idesc, accum || kk != 0);
+        umma_f16_ts(d_tmem, t_p + kk * 8, sdesc_mnmajor_sw128(a_v + kk * 16 * 128), idesc, accum || kk != 0);
 }
 
 template <typename T, int NPOLY>
@@ -206,17 +212,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sQ = smem + Smem::OFF_Q;
     uint8_t* sK = smem + Smem::OFF_K;
     uint8_t* sV = smem + Smem::OFF_V;
-    uint8_t* sP = smem + Smem::OFF_P;
     uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + Smem::OFF_BAR);
-    uint64_t* k_full = q_full + 1;      // [2]
-    uint64_t* k_empty = k_full + 2;     // [2]
-    uint64_t* v_full = k_empty + 2;     // [2]
-    uint64_t* v_empty = v_full + 2;     // [2]
-    uint64_t* s_full = v_empty + 2;     // [2 tiles]
-    uint64_t* s_free = s_full + 2;      // [2 tiles]
-    uint64_t* p_full = s_free + 2;      // [2 tiles]
-    uint64_t* o_full = p_full + 2;      // [2 tiles][2 P buffers]
-    uint64_t* done = o_full + 4;        // [2 MMA warps]
+    uint64_t* k_full = q_full + 1;            // [kStages]
+    uint64_t* k_empty = k_full + kStages;     // [kStages]
+    uint64_t* v_full = k_empty + kStages;     // [kStages]
+    uint64_t* v_empty = v_full + kStages;     // [kStages]
+    uint64_t* s_full = v_empty + kStages;     // [2 tiles]
+    uint64_t* s_free = s_full + 2;            // [2 tiles]
+    uint64_t* p_full = s_free + 2;            // [2 tiles]
+    uint64_t* o_full = p_full + 2;            // [2 tiles]
+    uint64_t* done = o_full + 2;              // [2 MMA warps]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 2);
             mbar_init(&v_full[s], 1);
@@ -251,11 +256,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], 128);
             mbar_init(&p_full[i], 128);
-            mbar_init(&o_full[2 * i], 1);
-            mbar_init(&o_full[2 * i + 1], 1);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&done[i], 1);
         }
-        mbar_init(&done[0], 1);
-        mbar_init(&done[1], 1);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -294,8 +297,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // step 0 loads K(0); step j+1 loads K(j+1) (if any) and V(j).
             const int jk = step;
             if (jk < nmax) {
-                const int s = jk & 1;
-                if (!mbar_wait_warp(&k_empty[s], (uint32_t)(((jk >> 1) & 1) ^ 1), abort_flag)) { ok = false; break; }
+                const int s = jk % kStages;
+                if (!mbar_wait_warp(&k_empty[s], (uint32_t)(((jk / kStages) & 1) ^ 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&k_full[s], Smem::KV_BYTES);
                     tma_load_3d(sK + s * Smem::KV_BYTES, &tm_k, &k_full[s], col, jk * kKT, b, pol);
@@ -305,8 +311,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const int jv = step - 1;
             if (jv >= 0) {
-                const int s = jv & 1;
-                if (!mbar_wait_warp(&v_empty[s], (uint32_t)(((jv >> 1) & 1) ^ 1), abort_flag)) { ok = false; break; }
+                const int s = jv % kStages;
+                if (!mbar_wait_warp(&v_empty[s], (uint32_t)(((jv / kStages) & 1) ^ 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&v_full[s], Smem::KV_BYTES);
                     tma_load_3d(sV + s * Smem::KV_BYTES, &tm_v, &v_full[s], col, jv * kKT, b, pol);
@@ -323,10 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Copies still in flight land before the CTA's smem is released.
             const volatile int never = 0;
             mbar_wait(q_full, 0, &never);
-            for (int t = 1; t <= 2; ++t) {
+            for (int t = 1; t <= kStages; ++t) {
                 const int jk = k_issued - t, jv = v_issued - t;
-                if (jk >= 0) mbar_wait(&k_full[jk & 1], (uint32_t)((jk >> 1) & 1), &never);
-                if (jv >= 0) mbar_wait(&v_full[jv & 1], (uint32_t)((jv >> 1) & 1), &never);
+                if (jk >= 0) mbar_wait(&k_full[jk % kStages], (uint32_t)((jk / kStages) & 1), &never);
+                if (jv >= 0) mbar_wait(&v_full[jv % kStages], (uint32_t)((jv / kStages) & 1), &never);
             }
         }
     } else if (warp >= kMmaWarp) {
@@ -341,8 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = warp - kMmaWarp;
         const int n = ntile[i];
         const uint32_t aQ = smem_addr(sQ) + i * Smem::Q_BYTES, aK = smem_addr(sK), aV = smem_addr(sV);
-        const uint32_t aP = smem_addr(sP) + 2 * i * Smem::P_BYTES;
         const uint32_t dS = tmem_base + i * kKT, dO = tmem_base + 2 * kKT + i * kHD;
+        const uint32_t tP = tmem_base + 2 * kKT + 2 * kHD + i * (kKT / 2);
         bool ok = mbar_wait_warp(q_full, 0, abort_flag);
         if (ok && nmax > 0) {
             ok = mbar_wait_warp(&k_full[0], 0, abort_flag);
@@ -359,10 +368,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         for (int j = 0; j < nmax && ok; ++j) {
-            const int s1 = (j + 1) & 1;
-            const int sv = j & 1;
+            const int s1 = (j + 1) % kStages;
+            const int sv = j % kStages;
             if (j + 1 < nmax) {
-                ok = mbar_wait_warp(&k_full[s1], (uint32_t)(((j + 1) >> 1) & 1), abort_flag);
+                ok = mbar_wait_warp(&k_full[s1], (uint32_t)(((j + 1) / kStages) & 1), abort_flag);
                 if (!ok) break;
                 if (j + 1 < n) {
                     // Next S as soon as the softmax has read the current one.
@@ -377,15 +386,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) umma_commit(&k_empty[s1]);
                 __syncwarp();
             }
-            ok = mbar_wait_warp(&v_full[sv], (uint32_t)((j >> 1) & 1), abort_flag);
+            ok = mbar_wait_warp(&v_full[sv], (uint32_t)((j / kStages) & 1), abort_flag);
             if (!ok) break;
             if (j < n) {
                 ok = mbar_wait_warp(&p_full[i], (uint32_t)(j & 1), abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 if (lane == 0) {
-                    issue_pv(dO, aP + (j & 1) * Smem::P_BYTES, aV + sv * Smem::KV_BYTES, IDESC_PV, j > 0);
-                    umma_commit(&o_full[2 * i + (j & 1)]);
+                    issue_pv(dO, tP, aV + sv * Smem::KV_BYTES, IDESC_PV, j > 0);
+                    umma_commit(&o_full[i]);
                 }
             }
             if (lane == 0) umma_commit(&v_empty[sv]);
@@ -412,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
         const uint32_t tS = tmem_base + lane_off + i * kKT;
         const uint32_t tO = tmem_base + lane_off + 2 * kKT + i * kHD;
-        uint8_t* myP = sP + 2 * i * Smem::P_BYTES;
+        const uint32_t tP = tmem_base + lane_off + 2 * kKT + 2 * kHD + i * (kKT / 2);
         const int n = ntile[i];
         const float2 sl2x2 = make_float2(sl2, sl2);
         float m_used = -INFINITY;   // running max, log2 domain (scaled)
@@ -493,47 +502,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int c = cc * 32; c < cc * 32 + 32; c += 2) pk[c >> 1] = 0u;
                 }
             }
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                // O must be rescaled before P_i(j) V joins it: wait for
-                // P_i(j-1) V, then scale the row in TMEM.
-                if (!mbar_wait_warp(&o_full[2 * i + ((j - 1) & 1)], (uint32_t)(((j - 1) >> 1) & 1), abort_flag)) {
+            if (j > 0) {
+                // P_i(j-1) V has finished: P's TMEM columns are free and O
+                // holds the sum through tile j-1 (rescaled here if needed
+                // before P_i(j) V joins it).
+                if (!mbar_wait_warp(&o_full[i], (uint32_t)((j - 1) & 1), abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-                for (int c = 0; c < kHD; c += 32) {
-                    uint32_t o[32];
-                    tmem_ld_32x32b_x32(tO + c, o);
-                    tmem_ld_wait();
+                    for (int c = 0; c < kHD; c += 32) {
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(tO + c, o);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
-                                                    alpha2);
-                        o[e] = __float_as_uint(v.x);
-                        o[e + 1] = __float_as_uint(v.y);
+                        for (int e = 0; e < 32; e += 2) {
+                            const float2 v = __fmul2_rn(
+                                make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), alpha2);
+                            o[e] = __float_as_uint(v.x);
+                            o[e + 1] = __float_as_uint(v.y);
+                        }
+                        tmem_st_32x32b_x32(tO + c, o);
                     }
-                    tmem_st_32x32b_x32(tO + c, o);
-                }
-                tmem_st_wait();
-            }
-            // P buffer j%2 was last read by P_i(j-2) V.
-            if (j >= 2 &&
-                !mbar_wait_warp(&o_full[2 * i + (j & 1)], (uint32_t)(((j - 2) >> 1) & 1), abort_flag)) {
-                ok = false;
-                break;
-            }
-            uint8_t* pb = myP + (j & 1) * Smem::P_BYTES;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int base = half * 32 + u * 4;
-                    *reinterpret_cast<uint4*>(pb + half * 16384 + r * 128 + ((u ^ (r & 7)) << 4)) =
-                        make_uint4(pk[base], pk[base + 1], pk[base + 2], pk[base + 3]);
                 }
             }
-            fence_proxy_async_smem();
+            tmem_st_32x32b_x32(tP, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+            tmem_st_32x32b_x32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
+            tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_full[i]);
         }
@@ -543,8 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ok is warp-uniform here (every wait above is), and so is rows[i].
         if (ok && rows[i] > 0 && n > 0) {
-            const int jl = n - 1;
-            if (!mbar_wait_warp(&o_full[2 * i + (jl & 1)], (uint32_t)((jl >> 1) & 1), abort_flag)) {
+            if (!mbar_wait_warp(&o_full[i], (uint32_t)((n - 1) & 1), abort_flag)) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_ATTN_TIMEOUT);
             } else if (wrow0 < tq) {
@@ -557,10 +553,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float l = l2.x + l2.y;
                 const float inv = l > 0.f ? 1.f / l : 0.f;
                 // Stage this warp's 32 rows x 64 columns in its own 4 KB slice
-                // of the last P buffer (128-byte swizzle, as the TMA store
-                // reads it) and write them with one TMA store; rows past tq
+                // of the tile's Q buffer (every MMA that read it is done:
+                // o_full follows them), 128-byte swizzled as the TMA store
+                // reads it, and write them with one TMA store; rows past tq
                 // are clipped.
-                uint8_t* stage = myP + (jl & 1) * Smem::P_BYTES + qd * 32 * 128;
+                uint8_t* stage = sQ + i * Smem::Q_BYTES + qd * 32 * 128;
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     uint32_t w[4];
