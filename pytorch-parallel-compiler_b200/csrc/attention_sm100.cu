@@ -1,12 +1,16 @@
 // Flash-attention core on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// One CTA computes 256 query rows of one head as two 128-row tiles (Q0, Q1)
+// A work item is 256 query rows of one head, as two 128-row tiles (Q0, Q1)
 // that take turns on the tensor core while the other tile's softmax runs on
-// the CUDA cores. 352 threads, warp-specialised:
+// the CUDA cores. With at least as many heads as SMs the kernel is
+// persistent: one CTA per SM loops over items, and the next item's Q load
+// and first S = Q K^T overlap the current item's last softmax and output
+// (Q is double-buffered; O's TMEM columns are handed back by the epilogue).
+// 352 threads, warp-specialised:
 //   warps 0..3  softmax for Q0, warps 4..7 softmax for Q1: thread = one query
 //               row = one TMEM lane (warp % 4 selects the lane quarter).
-//   warp 8      TMA producer: Q0/Q1 once, then 128-key tiles of K and V
-//               through two 3-stage rings (128-byte swizzle, read in place
+//   warp 8      TMA producer: Q0/Q1 per item, then 128-key tiles of K and
+//               V through two 3-stage rings (128-byte swizzle, read in place
 //               from the projection output through 3-D maps [nb][t][columns]);
 //               K of tile j+1 is fetched before V of tile j.
 //   warps 9, 10 issue the MMAs of tile 0 / tile 1 from one elected thread
@@ -38,9 +42,8 @@
 //
 // Causal (top-left aligned): Q0 stops one key tile before Q1; on tiles that
 // cross the diagonal, 32-key chunks that no row of a warp attends are not
-// exponentiated. The output is normalised, staged in shared memory (the
-// tile's Q buffer, free once its last MMA is done) and written by one TMA
-// store per warp (rows past tq are clipped).
+// exponentiated. The output is normalised, staged in shared memory and
+// written by one TMA store per warp (rows past tq are clipped).
 //
 // Every wait is bounded; on a timeout the CTA records DEV_ERR_ATTN_TIMEOUT,
 // stops issuing, lets its copies and MMAs in flight finish and frees TMEM.
@@ -71,12 +74,14 @@ constexpr int kStages = 3;      // K ring and V ring depth
 struct Smem {
     static constexpr uint32_t Q_BYTES = kQT * kHD * 2;      // 16 KB
     static constexpr uint32_t KV_BYTES = kKT * kHD * 2;     // 16 KB
-    static constexpr uint32_t OFF_Q = 0;                    // [2 tiles]
-    static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;  // [kStages]
+    static constexpr uint32_t OFF_Q = 0;                    // [2 item buffers][2 tiles]
+    static constexpr uint32_t OFF_K = OFF_Q + 4 * Q_BYTES;  // [kStages]
     static constexpr uint32_t OFF_V = OFF_K + kStages * KV_BYTES;
-    static constexpr uint32_t OFF_BAR = OFF_V + kStages * KV_BYTES;
-    // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2], p_full[2], o_full[2], done[2]
-    static constexpr uint32_t NBAR = 1 + 4 * kStages + 10;
+    static constexpr uint32_t OFF_OUT = OFF_V + kStages * KV_BYTES;   // [2 tiles] output staging
+    static constexpr uint32_t OFF_BAR = OFF_OUT + 2 * Q_BYTES;
+    // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[S], v_empty[S],
+    // s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], done[2]
+    static constexpr uint32_t NBAR = 4 + 4 * kStages + 12;
     static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NBAR * 8 + 16;
 };
 static_assert(Smem::TOTAL <= 232448, "attention smem over the per-CTA limit");
@@ -198,22 +203,43 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t t_p, uint32_t
         umma_f16_ts(d_tmem, t_p + kk * 8, sdesc_mnmajor_sw128(a_v + kk * 16 * 128), idesc, accum || kk != 0);
 }
 
+// Work item w of the launch -> (batch*head index, query block of 256 rows).
+// One item per CTA (persist = 0): the query blocks of a head are adjacent,
+// the one with the most keys first. Persistent (gridDim.x = G CTAs, each
+// taking items blockIdx.x + k*G): round k covers G consecutive heads at one
+// query-block class, classes from most keys to fewest, so all CTAs of a
+// round do the same amount of work and the G heads' K/V stay in L2 over
+// the nqb rounds that revisit them.
+__device__ __forceinline__ void item_of(int w, int nqb, int persist, int& bh, int& qb) {
+    if (!persist) {
+        bh = w / nqb;
+        qb = nqb - 1 - w % nqb;
+        return;
+    }
+    const int G = (int)gridDim.x;
+    const int k = w / G, c = w % G;
+    bh = (k / nqb) * G + c;
+    qb = nqb - 1 - k % nqb;
+}
+
 template <typename T, int NPOLY>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o, int heads,
-                   int tq, int tk, int causal, float sl2, int* err) {
+                   int nbh, int items, int persist, int tq, int tk, int causal, float sl2, int* err) {
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr uint32_t IDESC_S = idesc_f16(kQT, kKT, kBf16);
     constexpr uint32_t IDESC_PV = idesc_f16(kQT, kHD, kBf16) | (1u << 16);   // B (V) MN-major
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem + Smem::OFF_Q;
+    uint8_t* sQ = smem + Smem::OFF_Q;       // [item buffer][tile]
     uint8_t* sK = smem + Smem::OFF_K;
     uint8_t* sV = smem + Smem::OFF_V;
-    uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + Smem::OFF_BAR);
-    uint64_t* k_full = q_full + 1;            // [kStages]
+    uint8_t* sOut = smem + Smem::OFF_OUT;   // [tile]
+    uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + Smem::OFF_BAR);   // [2 item buffers]
+    uint64_t* q_empty = q_full + 2;           // [2 item buffers]
+    uint64_t* k_full = q_empty + 2;           // [kStages]
     uint64_t* k_empty = k_full + kStages;     // [kStages]
     uint64_t* v_full = k_empty + kStages;     // [kStages]
     uint64_t* v_empty = v_full + kStages;     // [kStages]
@@ -221,31 +247,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* s_free = s_full + 2;            // [2 tiles]
     uint64_t* p_full = s_free + 2;            // [2 tiles]
     uint64_t* o_full = p_full + 2;            // [2 tiles]
-    uint64_t* done = o_full + 2;              // [2 MMA warps]
+    uint64_t* o_free = o_full + 2;            // [2 tiles]
+    uint64_t* done = o_free + 2;              // [2 MMA warps]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-
-    // Work item: CTAs of one head are adjacent (they share K/V through L2);
-    // within a head the query blocks with the most keys start first.
     const int nqb = (tq + 2 * kQT - 1) / (2 * kQT);
-    const int bh = blockIdx.x / nqb;
-    const int qb = nqb - 1 - (int)(blockIdx.x % nqb);
-    const int b = bh / heads, h = bh % heads;
-    const int q0 = qb * 2 * kQT;
-    int rows[2], ntile[2];
+
+    // Per-item geometry, identical in every role: query rows and key tiles
+    // of the two query tiles.
+    auto geometry = [&](int qb, int (&rows)[2], int (&ntile)[2]) {
+        const int q0 = qb * 2 * kQT;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        rows[i] = max(0, min(kQT, tq - (q0 + i * kQT)));
-        const int klim = causal ? min(tk, q0 + i * kQT + rows[i]) : tk;
-        ntile[i] = rows[i] > 0 ? (klim + kKT - 1) / kKT : 0;
-    }
-    const int nmax = max(ntile[0], ntile[1]);
+        for (int i = 0; i < 2; ++i) {
+            rows[i] = max(0, min(kQT, tq - (q0 + i * kQT)));
+            const int klim = causal ? min(tk, q0 + i * kQT + rows[i]) : tk;
+            ntile[i] = rows[i] > 0 ? (klim + kKT - 1) / kKT : 0;
+        }
+    };
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int u = 0; u < 2; ++u) {
+            mbar_init(&q_full[u], 1);
+            mbar_init(&q_empty[u], 2);
+        }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 2);
@@ -257,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s_free[i], 128);
             mbar_init(&p_full[i], 128);
             mbar_init(&o_full[i], 1);
+            mbar_init(&o_free[i], 128);
             mbar_init(&done[i], 1);
         }
         *abort_flag = 0;
@@ -279,49 +307,61 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kTmaWarp) {
         // ------------------------------------------------------------------
-        // TMA producer: Q0/Q1, then K(0), and per tile j: K(j+1), V(j).
+        // TMA producer. Per item: Q0/Q1 into item buffer u % 2 (once the
+        // item two back has released it), then K(0), and per key tile j:
+        // K(j+1), V(j). The K and V rings run on across items.
         // ------------------------------------------------------------------
         const uint64_t pol = l2_policy_evict_normal();
-        const int col = h * kHD;
-        if (lane == 0) {
-            uint32_t qbytes = 0;
-            for (int i = 0; i < 2; ++i) qbytes += rows[i] > 0 ? Smem::Q_BYTES : 0;
-            mbar_arrive_expect_tx(q_full, qbytes);
-            for (int i = 0; i < 2; ++i)
-                if (rows[i] > 0) tma_load_3d(sQ + i * Smem::Q_BYTES, &tm_q, q_full, col, q0 + i * kQT, b, pol);
-        }
-        __syncwarp();
-        int k_issued = 0, v_issued = 0;
+        int kc = 0, vc = 0, u = 0;      // K loads, V loads, items (running)
         bool ok = true;
-        for (int step = 0; step <= nmax && ok; ++step) {
-            // step 0 loads K(0); step j+1 loads K(j+1) (if any) and V(j).
-            const int jk = step;
-            if (jk < nmax) {
-                const int s = jk % kStages;
-                if (!mbar_wait_warp(&k_empty[s], (uint32_t)(((jk / kStages) & 1) ^ 1), abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&k_full[s], Smem::KV_BYTES);
-                    tma_load_3d(sK + s * Smem::KV_BYTES, &tm_k, &k_full[s], col, jk * kKT, b, pol);
-                }
-                __syncwarp();
-                ++k_issued;
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+            int bh, qb;
+            item_of(w, nqb, persist, bh, qb);
+            if (bh >= nbh) continue;
+            const int b = bh / heads, col = (bh % heads) * kHD, q0 = qb * 2 * kQT;
+            int rows[2], ntile[2];
+            geometry(qb, rows, ntile);
+            const int nmax = max(ntile[0], ntile[1]);
+            const int qs = u & 1;
+            if (!mbar_wait_warp(&q_empty[qs], (uint32_t)(((u >> 1) & 1) ^ 1), abort_flag)) { ok = false; break; }
+            if (lane == 0) {
+                uint32_t qbytes = 0;
+                for (int i = 0; i < 2; ++i) qbytes += rows[i] > 0 ? Smem::Q_BYTES : 0;
+                mbar_arrive_expect_tx(&q_full[qs], qbytes);
+                for (int i = 0; i < 2; ++i)
+                    if (rows[i] > 0)
+                        tma_load_3d(sQ + (2 * qs + i) * Smem::Q_BYTES, &tm_q, &q_full[qs], col, q0 + i * kQT, b, pol);
             }
-            const int jv = step - 1;
-            if (jv >= 0) {
-                const int s = jv % kStages;
-                if (!mbar_wait_warp(&v_empty[s], (uint32_t)(((jv / kStages) & 1) ^ 1), abort_flag)) {
-                    ok = false;
-                    break;
+            __syncwarp();
+            ++u;
+            for (int step = 0; step <= nmax && ok; ++step) {
+                // step 0 loads K(0); step j+1 loads K(j+1) (if any) and V(j).
+                if (step < nmax) {
+                    const int s = kc % kStages;
+                    if (!mbar_wait_warp(&k_empty[s], (uint32_t)(((kc / kStages) & 1) ^ 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&k_full[s], Smem::KV_BYTES);
+                        tma_load_3d(sK + s * Smem::KV_BYTES, &tm_k, &k_full[s], col, step * kKT, b, pol);
+                    }
+                    __syncwarp();
+                    ++kc;
                 }
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&v_full[s], Smem::KV_BYTES);
-                    tma_load_3d(sV + s * Smem::KV_BYTES, &tm_v, &v_full[s], col, jv * kKT, b, pol);
+                if (step >= 1) {
+                    const int s = vc % kStages;
+                    if (!mbar_wait_warp(&v_empty[s], (uint32_t)(((vc / kStages) & 1) ^ 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&v_full[s], Smem::KV_BYTES);
+                        tma_load_3d(sV + s * Smem::KV_BYTES, &tm_v, &v_full[s], col, (step - 1) * kKT, b, pol);
+                    }
+                    __syncwarp();
+                    ++vc;
                 }
-                __syncwarp();
-                ++v_issued;
             }
         }
         if (!ok) {
@@ -331,9 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok || *abort_flag) {
             // Copies still in flight land before the CTA's smem is released.
             const volatile int never = 0;
-            mbar_wait(q_full, 0, &never);
+            for (int t = 1; t <= 2; ++t)
+                if (u - t >= 0) mbar_wait(&q_full[(u - t) & 1], (uint32_t)(((u - t) >> 1) & 1), &never);
             for (int t = 1; t <= kStages; ++t) {
-                const int jk = k_issued - t, jv = v_issued - t;
+                const int jk = kc - t, jv = vc - t;
                 if (jk >= 0) mbar_wait(&k_full[jk % kStages], (uint32_t)((jk / kStages) & 1), &never);
                 if (jv >= 0) mbar_wait(&v_full[jv % kStages], (uint32_t)((jv / kStages) & 1), &never);
             }
@@ -342,63 +383,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------------
         // MMA issuers: warp 9 + i serves query tile i, so that each tile's
         // S(j+1) follows its own softmax without waiting for the other
-        // tile. Both warps commit every K/V stage (count-2 "empty"
-        // barriers), also the stages their tile no longer needs; each waits
-        // for a stage's "full" barrier before committing its "empty" one,
+        // tile. Both warps commit every K/V stage and Q buffer (count-2
+        // "empty" barriers), also those their tile does not use; each waits
+        // for a buffer's "full" barrier before committing its "empty" one,
         // so that its arrival always lands on the phase of that load.
+        // The first S of an item only needs the previous S read (s_free), so
+        // it overlaps the previous item's last softmax and epilogue; its
+        // first P V (which overwrites O) waits for that epilogue (o_free).
         // ------------------------------------------------------------------
         const int i = warp - kMmaWarp;
-        const int n = ntile[i];
-        const uint32_t aQ = smem_addr(sQ) + i * Smem::Q_BYTES, aK = smem_addr(sK), aV = smem_addr(sV);
+        const uint32_t aK = smem_addr(sK), aV = smem_addr(sV);
         const uint32_t dS = tmem_base + i * kKT, dO = tmem_base + 2 * kKT + i * kHD;
         const uint32_t tP = tmem_base + 2 * kKT + 2 * kHD + i * (kKT / 2);
-        bool ok = mbar_wait_warp(q_full, 0, abort_flag);
-        if (ok && nmax > 0) {
-            ok = mbar_wait_warp(&k_full[0], 0, abort_flag);
-            if (ok) {
-                tc_fence_after();
-                if (lane == 0) {
-                    if (n > 0) {
-                        issue_qk(dS, aQ, aK, IDESC_S);
-                        umma_commit(&s_full[i]);
-                    }
-                    umma_commit(&k_empty[0]);
-                }
-                __syncwarp();
-            }
-        }
-        for (int j = 0; j < nmax && ok; ++j) {
-            const int s1 = (j + 1) % kStages;
-            const int sv = j % kStages;
-            if (j + 1 < nmax) {
-                ok = mbar_wait_warp(&k_full[s1], (uint32_t)(((j + 1) / kStages) & 1), abort_flag);
-                if (!ok) break;
-                if (j + 1 < n) {
-                    // Next S as soon as the softmax has read the current one.
-                    ok = mbar_wait_warp(&s_free[i], (uint32_t)(j & 1), abort_flag);
+        int kc = 0, vc = 0, u = 0;      // running K tiles, V tiles, items
+        int g = 0;                      // running S/P/O tile index of this query tile
+        int ue = 0;                     // items of this query tile with output (epilogues)
+        bool ok = true;
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+            int bh, qb;
+            item_of(w, nqb, persist, bh, qb);
+            if (bh >= nbh) continue;
+            int rows[2], ntile[2];
+            geometry(qb, rows, ntile);
+            const int n = ntile[i];
+            const int nmax = max(ntile[0], ntile[1]);
+            const int qs = u & 1;
+            const uint32_t aQ = smem_addr(sQ) + (2 * qs + i) * Smem::Q_BYTES;
+            ok = mbar_wait_warp(&q_full[qs], (uint32_t)((u >> 1) & 1), abort_flag);
+            for (int j = -1; j < nmax && ok; ++j) {
+                // S(j+1) of this tile, then P V for tile j.
+                if (j + 1 < nmax) {
+                    const int s1 = kc % kStages;
+                    ok = mbar_wait_warp(&k_full[s1], (uint32_t)((kc / kStages) & 1), abort_flag);
                     if (!ok) break;
-                    tc_fence_after();
-                    if (lane == 0) {
-                        issue_qk(dS, aQ, aK + s1 * Smem::KV_BYTES, IDESC_S);
-                        umma_commit(&s_full[i]);
+                    if (j + 1 < n) {
+                        const int t = g + j + 1;   // running index of this S
+                        if (t > 0) ok = mbar_wait_warp(&s_free[i], (uint32_t)((t - 1) & 1), abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        if (lane == 0) {
+                            issue_qk(dS, aQ, aK + s1 * Smem::KV_BYTES, IDESC_S);
+                            umma_commit(&s_full[i]);
+                        }
                     }
+                    if (lane == 0) umma_commit(&k_empty[s1]);
+                    __syncwarp();
+                    ++kc;
                 }
-                if (lane == 0) umma_commit(&k_empty[s1]);
-                __syncwarp();
+                if (j >= 0) {
+                    const int sv = vc % kStages;
+                    ok = mbar_wait_warp(&v_full[sv], (uint32_t)((vc / kStages) & 1), abort_flag);
+                    if (!ok) break;
+                    if (j < n) {
+                        if (j == 0 && ue > 0)
+                            ok = mbar_wait_warp(&o_free[i], (uint32_t)((ue - 1) & 1), abort_flag);
+                        if (ok) ok = mbar_wait_warp(&p_full[i], (uint32_t)((g + j) & 1), abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        if (lane == 0) {
+                            issue_pv(dO, tP, aV + sv * Smem::KV_BYTES, IDESC_PV, j > 0);
+                            umma_commit(&o_full[i]);
+                        }
+                    }
+                    if (lane == 0) umma_commit(&v_empty[sv]);
+                    __syncwarp();
+                    ++vc;
+                }
             }
-            ok = mbar_wait_warp(&v_full[sv], (uint32_t)((j / kStages) & 1), abort_flag);
             if (!ok) break;
-            if (j < n) {
-                ok = mbar_wait_warp(&p_full[i], (uint32_t)(j & 1), abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                if (lane == 0) {
-                    issue_pv(dO, tP, aV + sv * Smem::KV_BYTES, IDESC_PV, j > 0);
-                    umma_commit(&o_full[i]);
-                }
-            }
-            if (lane == 0) umma_commit(&v_empty[sv]);
+            // Q buffer qs is free once this warp's MMAs of the item are done.
+            if (lane == 0) umma_commit(&q_empty[qs]);
             __syncwarp();
+            ++u;
+            if (n > 0) {
+                g += n;
+                ++ue;
+            }
         }
         if (!ok) {
             *abort_flag = 1;
@@ -416,169 +476,186 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = warp >> 2;
         const int qd = warp & 3;
         const int r = qd * 32 + lane;                 // row within the tile = TMEM lane
-        const int qrow = q0 + i * kQT + r;
-        const int wrow0 = q0 + i * kQT + qd * 32;     // first row of this warp
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
         const uint32_t tS = tmem_base + lane_off + i * kKT;
         const uint32_t tO = tmem_base + lane_off + 2 * kKT + i * kHD;
         const uint32_t tP = tmem_base + lane_off + 2 * kKT + 2 * kHD + i * (kKT / 2);
-        const int n = ntile[i];
+        uint8_t* stage = sOut + i * Smem::Q_BYTES + qd * 32 * 128;   // this warp's 32 output rows
         const float2 sl2x2 = make_float2(sl2, sl2);
-        float m_used = -INFINITY;   // running max, log2 domain (scaled)
-        float2 lsum[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) lsum[e] = make_float2(0.f, 0.f);
+        int g = 0;                      // running S/P/O tile index of this query tile
         bool ok = true;
-        for (int j = 0; j < n; ++j) {
-            if (!mbar_wait_warp(&s_full[i], (uint32_t)(j & 1), abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const int kbase = j * kKT;
-            // Keys of this tile attended by at least one row of the warp.
-            int kvalid = min(kKT, tk - kbase);
-            if (causal) kvalid = min(kvalid, wrow0 + 32 - kbase);
-            const int nch = (max(kvalid, 0) + 31) >> 5;   // 32-key chunks to process (warp-uniform)
-            // All four chunks are read (a conditional read costs registers);
-            // the chunks no row attends are skipped below.
-            float s[kKT];
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+            int bh, qb;
+            item_of(w, nqb, persist, bh, qb);
+            if (bh >= nbh) continue;
+            int rows[2], ntile[2];
+            geometry(qb, rows, ntile);
+            const int n = ntile[i];
+            if (n == 0) continue;
+            const int q0 = qb * 2 * kQT;
+            const int qrow = q0 + i * kQT + r;
+            const int wrow0 = q0 + i * kQT + qd * 32;     // first row of this warp
+            float m_used = -INFINITY;   // running max, log2 domain (scaled)
+            float2 lsum[4];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) tmem_ld32(tS + cc * 32, s + cc * 32);
+            for (int e = 0; e < 4; ++e) lsum[e] = make_float2(0.f, 0.f);
+            for (int j = 0; j < n; ++j) {
+                const int t = g + j;
+                if (!mbar_wait_warp(&s_full[i], (uint32_t)(t & 1), abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const int kbase = j * kKT;
+                // Keys of this tile attended by at least one row of the warp.
+                int kvalid = min(kKT, tk - kbase);
+                if (causal) kvalid = min(kvalid, wrow0 + 32 - kbase);
+                const int nch = (max(kvalid, 0) + 31) >> 5;   // 32-key chunks to process (warp-uniform)
+                // All four chunks are read (a conditional read costs
+                // registers); the chunks no row attends are skipped below.
+                float s[kKT];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) tmem_ld32(tS + cc * 32, s + cc * 32);
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(&s_free[i]);
+
+                const bool need_mask = (kbase + kKT > tk) || (causal && kbase + kKT - 1 > wrow0);
+                if (need_mask) {
+                    const int lim = causal ? min(tk - kbase, qrow - kbase + 1) : tk - kbase;
+#pragma unroll
+                    for (int c = 0; c < kKT; ++c)
+                        if (c >= lim) s[c] = -INFINITY;
+                }
+                // Row max: four independent 3-input max chains per chunk.
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    if (cc < nch) {
+#pragma unroll
+                        for (int c = cc * 32; c < cc * 32 + 32; c += 8) {
+                            mx4[0] = max3(mx4[0], s[c], s[c + 1]);
+                            mx4[1] = max3(mx4[1], s[c + 2], s[c + 3]);
+                            mx4[2] = max3(mx4[2], s[c + 4], s[c + 5]);
+                            mx4[3] = max3(mx4[3], s[c + 6], s[c + 7]);
+                        }
+                    }
+                }
+                const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+                const float m_new = fmaxf(m_used, m_tile);
+                const bool rescale = m_new > m_used + kRescaleLog2;
+                float alpha = 1.f;
+                if (rescale) {
+                    alpha = ex2(m_used - m_new);
+                    m_used = m_new;
+                }
+                const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+                const float2 negm2 = make_float2(neg_m, neg_m);
+                const float2 alpha2 = make_float2(alpha, alpha);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) lsum[e] = __fmul2_rn(lsum[e], alpha2);
+                uint32_t pk[kKT / 2];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    if (cc < nch) {
+#pragma unroll
+                        for (int c = cc * 32; c < cc * 32 + 32; c += 2) {
+                            const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sl2x2, negm2);
+                            float2 p;
+                            if (((c >> 1) & 3) < NPOLY) {
+                                p = exp2_poly2(x);
+                            } else {
+                                p.x = ex2(x.x);
+                                p.y = ex2(x.y);
+                            }
+                            lsum[(c >> 1) & 3] = __fadd2_rn(lsum[(c >> 1) & 3], p);
+                            pk[c >> 1] = pack2<T>(p.x, p.y);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = cc * 32; c < cc * 32 + 32; c += 2) pk[c >> 1] = 0u;
+                    }
+                }
+                if (j > 0) {
+                    // P_i(j-1) V has finished: P's TMEM columns are free and
+                    // O holds the sum through tile j-1 (rescaled here if
+                    // needed before P_i(j) V joins it). For j = 0 the previous
+                    // item's epilogue already waited for its last P V.
+                    if (!mbar_wait_warp(&o_full[i], (uint32_t)((t - 1) & 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                        for (int c = 0; c < kHD; c += 32) {
+                            uint32_t o[32];
+                            tmem_ld_32x32b_x32(tO + c, o);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int e = 0; e < 32; e += 2) {
+                                const float2 v = __fmul2_rn(
+                                    make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), alpha2);
+                                o[e] = __float_as_uint(v.x);
+                                o[e + 1] = __float_as_uint(v.y);
+                            }
+                            tmem_st_32x32b_x32(tO + c, o);
+                        }
+                    }
+                }
+                tmem_st_32x32b_x32(tP, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+                tmem_st_32x32b_x32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&p_full[i]);
+            }
+            if (!ok) break;
+            // Epilogue: O after the item's last P V; O's columns are handed
+            // back (o_free) as soon as they are in registers.
+            if (!mbar_wait_warp(&o_full[i], (uint32_t)((g + n - 1) & 1), abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float o[kHD];
+            tmem_ld32(tO, o);
+            tmem_ld32(tO + 32, o + 32);
             tmem_ld_wait();
             tc_fence_before();
-            mbar_arrive(&s_free[i]);
-
-            const bool need_mask = (kbase + kKT > tk) || (causal && kbase + kKT - 1 > wrow0);
-            if (need_mask) {
-                const int lim = causal ? min(tk - kbase, qrow - kbase + 1) : tk - kbase;
+            mbar_arrive(&o_free[i]);
+            g += n;
+            if (wrow0 < tq) {
+                const float2 l2 = __fadd2_rn(__fadd2_rn(lsum[0], lsum[1]), __fadd2_rn(lsum[2], lsum[3]));
+                const float l = l2.x + l2.y;
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                // This warp's 32 rows x 64 columns, 128-byte swizzled as the
+                // TMA store reads them, once the previous store has read the
+                // staging slice; rows past tq are clipped by the store.
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
 #pragma unroll
-                for (int c = 0; c < kKT; ++c)
-                    if (c >= lim) s[c] = -INFINITY;
-            }
-            // Row max: four independent 3-input max chains per chunk.
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                for (int u8 = 0; u8 < 8; ++u8) {
+                    uint32_t wv[4];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                if (cc < nch) {
-#pragma unroll
-                    for (int c = cc * 32; c < cc * 32 + 32; c += 8) {
-                        mx4[0] = max3(mx4[0], s[c], s[c + 1]);
-                        mx4[1] = max3(mx4[1], s[c + 2], s[c + 3]);
-                        mx4[2] = max3(mx4[2], s[c + 4], s[c + 5]);
-                        mx4[3] = max3(mx4[3], s[c + 6], s[c + 7]);
+                    for (int e = 0; e < 4; ++e) {
+                        const int c = u8 * 8 + e * 2;
+                        wv[e] = pack2<T>(o[c] * inv, o[c + 1] * inv);
                     }
+                    *reinterpret_cast<uint4*>(stage + lane * 128 + ((u8 ^ (lane & 7)) << 4)) =
+                        make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
-            }
-            const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-            const float m_new = fmaxf(m_used, m_tile);
-            const bool rescale = m_new > m_used + kRescaleLog2;
-            float alpha = 1.f;
-            if (rescale) {
-                alpha = ex2(m_used - m_new);
-                m_used = m_new;
-            }
-            const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-            const float2 negm2 = make_float2(neg_m, neg_m);
-            const float2 alpha2 = make_float2(alpha, alpha);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) lsum[e] = __fmul2_rn(lsum[e], alpha2);
-            uint32_t pk[kKT / 2];
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                if (cc < nch) {
-#pragma unroll
-                    for (int c = cc * 32; c < cc * 32 + 32; c += 2) {
-                        const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sl2x2, negm2);
-                        float2 p;
-                        if (((c >> 1) & 3) < NPOLY) {
-                            p = exp2_poly2(x);
-                        } else {
-                            p.x = ex2(x.x);
-                            p.y = ex2(x.y);
-                        }
-                        lsum[(c >> 1) & 3] = __fadd2_rn(lsum[(c >> 1) & 3], p);
-                        pk[c >> 1] = pack2<T>(p.x, p.y);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = cc * 32; c < cc * 32 + 32; c += 2) pk[c >> 1] = 0u;
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&tm_o, stage, (bh % heads) * kHD, wrow0, bh / heads);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
+                __syncwarp();
             }
-            if (j > 0) {
-                // P_i(j-1) V has finished: P's TMEM columns are free and O
-                // holds the sum through tile j-1 (rescaled here if needed
-                // before P_i(j) V joins it).
-                if (!mbar_wait_warp(&o_full[i], (uint32_t)((j - 1) & 1), abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-                    for (int c = 0; c < kHD; c += 32) {
-                        uint32_t o[32];
-                        tmem_ld_32x32b_x32(tO + c, o);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2) {
-                            const float2 v = __fmul2_rn(
-                                make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), alpha2);
-                            o[e] = __float_as_uint(v.x);
-                            o[e + 1] = __float_as_uint(v.y);
-                        }
-                        tmem_st_32x32b_x32(tO + c, o);
-                    }
-                }
-            }
-            tmem_st_32x32b_x32(tP, *reinterpret_cast<const uint32_t(*)[32]>(pk));
-            tmem_st_32x32b_x32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(&p_full[i]);
         }
         if (!ok) {
             *abort_flag = 1;
             raise_device_error(err, DEV_ERR_ATTN_TIMEOUT);
         }
-        // ok is warp-uniform here (every wait above is), and so is rows[i].
-        if (ok && rows[i] > 0 && n > 0) {
-            if (!mbar_wait_warp(&o_full[i], (uint32_t)((n - 1) & 1), abort_flag)) {
-                *abort_flag = 1;
-                raise_device_error(err, DEV_ERR_ATTN_TIMEOUT);
-            } else if (wrow0 < tq) {
-                tc_fence_after();
-                float o[kHD];
-                tmem_ld32(tO, o);
-                tmem_ld32(tO + 32, o + 32);
-                tmem_ld_wait();
-                const float2 l2 = __fadd2_rn(__fadd2_rn(lsum[0], lsum[1]), __fadd2_rn(lsum[2], lsum[3]));
-                const float l = l2.x + l2.y;
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                // Stage this warp's 32 rows x 64 columns in its own 4 KB slice
-                // of the tile's Q buffer (every MMA that read it is done:
-                // o_full follows them), 128-byte swizzled as the TMA store
-                // reads it, and write them with one TMA store; rows past tq
-                // are clipped.
-                uint8_t* stage = sQ + i * Smem::Q_BYTES + qd * 32 * 128;
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int c = u * 8 + e * 2;
-                        w[e] = pack2<T>(o[c] * inv, o[c + 1] * inv);
-                    }
-                    *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    tma_store_3d(&tm_o, stage, h * kHD, wrow0, b);
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-                }
-                __syncwarp();
-            }
-        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -608,7 +685,7 @@ int rows_map(CUtensorMap* m, const void* base, int64_t stride, int t, int nb, in
 
 template <typename T, int NPOLY>
 int launch_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& o,
-              const AttnArgs& a, int64_t blocks, cudaStream_t st) {
+              const AttnArgs& a, cudaStream_t st) {
     auto kern = attn_tc_kernel<T, NPOLY>;
     static bool attr_done[64] = {false};
     const int dev = current_device();
@@ -618,9 +695,26 @@ int launch_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, 
             return set_error(WIDEK_ERR_CUDA, "attention: cannot reserve %u bytes of shared memory", Smem::TOTAL);
         attr_done[dev] = true;
     }
+    // Persistent (one CTA per SM looping over items) when there are at
+    // least as many heads as SMs; otherwise one item per CTA.
+    const int64_t nbh = (int64_t)a.nb * a.heads;
+    const int64_t nqb = (a.tq + 2 * kQT - 1) / (2 * kQT);
+    const int sms = sm_count(dev);
+    int64_t grid, items;
+    int persist;
+    if (sms > 0 && nbh >= sms) {
+        persist = 1;
+        grid = sms;
+        items = (nbh + sms - 1) / sms * nqb * sms;
+    } else {
+        persist = 0;
+        items = nbh * nqb;
+        grid = items;
+    }
+    if (items > 0x7fffffff || nbh > 0x7fffffff) return WIDEK_ERR_UNSUPPORTED;
     const float sl2 = a.scale * 1.4426950408889634f;
-    kern<<<(unsigned)blocks, kThreads, Smem::TOTAL, st>>>(q, k, v, o, a.heads, a.tq, a.tk, a.causal, sl2,
-                                                          device_error_ptr());
+    kern<<<(unsigned)grid, kThreads, Smem::TOTAL, st>>>(q, k, v, o, a.heads, (int)nbh, (int)items, persist, a.tq,
+                                                        a.tk, a.causal, sl2, device_error_ptr());
     return check_launch("widek_attention_fwd (tcgen05)");
 }
 
@@ -637,9 +731,6 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st) {
                           a.sq >= width && a.sk >= width && a.sv >= width && a.so >= width &&
                           aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.o);
         if (!fits) return WIDEK_ERR_UNSUPPORTED;
-        const int64_t nqb = (a.tq + 2 * kQT - 1) / (2 * kQT);
-        const int64_t blocks = nqb * a.nb * (int64_t)a.heads;
-        if (blocks > 0x7fffffff) return WIDEK_ERR_UNSUPPORTED;
         CUtensorMap tq_, tk_, tv_, to_;
         int rc = rows_map<T>(&tq_, a.q, a.sq, a.tq, a.nb, a.heads, kQT);
         if (!rc) rc = rows_map<T>(&tk_, a.k, a.sk, a.tk, a.nb, a.heads, kKT);
@@ -647,9 +738,9 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st) {
         if (!rc) rc = rows_map<T>(&to_, a.o, a.so, a.tq, a.nb, a.heads, 32);
         if (rc) return rc;
         switch (attn_poly_pairs()) {
-            case 0: return launch_tc<T, 0>(tq_, tk_, tv_, to_, a, blocks, st);
-            case 2: return launch_tc<T, 2>(tq_, tk_, tv_, to_, a, blocks, st);
-            default: return launch_tc<T, 1>(tq_, tk_, tv_, to_, a, blocks, st);
+            case 0: return launch_tc<T, 0>(tq_, tk_, tv_, to_, a, st);
+            case 2: return launch_tc<T, 2>(tq_, tk_, tv_, to_, a, st);
+            default: return launch_tc<T, 1>(tq_, tk_, tv_, to_, a, st);
         }
     }
 }

@@ -112,6 +112,25 @@ def test_core_variants_agree_cfg5_shape():
     no_device_error()
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("variant", [0, 10])
+def test_core_persistent_rounds(causal, variant):
+    """At least as many heads as SMs: one CTA per SM loops over work items
+    (query blocks of 256 rows, heaviest first per round); 160 heads leave the
+    last round partly empty and T=600 gives three query blocks, the last one
+    ragged, so items of different sizes follow each other on a CTA."""
+    out, ref = _run(20, 8, 600, 600, causal, torch.bfloat16, variant, seed=21)
+    assert_lowp_close(out, ref)
+    no_device_error()
+
+
+def test_core_persistent_cross_lengths():
+    """Persistent mode with tq != tk (keys past the causal diagonal)."""
+    out, ref = _run(19, 8, 300, 520, True, torch.bfloat16, 0, seed=22)
+    assert_lowp_close(out, ref)
+    no_device_error()
+
+
 def test_core_large_head_count_grid():
     """More than 65535 (batch x head) pairs: the tcgen05 kernel's flat grid."""
     nb, heads, t = 8200, 8, 8
