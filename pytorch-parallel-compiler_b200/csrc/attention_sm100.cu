@@ -2,10 +2,10 @@
 //
 // A work item is 256 query rows of one head, as two 128-row tiles (Q0, Q1)
 // that take turns on the tensor core while the other tile's softmax runs on
-// the CUDA cores. With at least as many heads as SMs the kernel is
-// persistent: one CTA per SM loops over items, and the next item's Q load
-// and first S = Q K^T overlap the current item's last softmax and output
-// (Q is double-buffered; O's TMEM columns are handed back by the epilogue).
+// the CUDA cores. The kernel is persistent: at most one CTA per SM loops over
+// items, and the next item's Q load and first S = Q K^T overlap the current
+// item's last softmax and output (Q is double-buffered; O's TMEM columns are
+// handed back by the epilogue).
 // 352 threads, warp-specialised:
 //   warps 0..3  softmax for Q0, warps 4..7 softmax for Q1: thread = one query
 //               row = one TMEM lane (warp % 4 selects the lane quarter).
@@ -50,7 +50,9 @@
 //
 // Replaces the scaled_dot_product_attention call of
 // wide_compiler/core/primitives/wide_attention.py:217-231 for head_dim 64.
+#include <algorithm>
 #include <cstring>
+#include <numeric>
 
 #include "attention.cuh"
 #include "sm100_ptx.cuh"
@@ -203,30 +205,22 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t t_p, uint32_t
         umma_f16_ts(d_tmem, t_p + kk * 8, sdesc_mnmajor_sw128(a_v + kk * 16 * 128), idesc, accum || kk != 0);
 }
 
-// Work item w of the launch -> (batch*head index, query block of 256 rows).
-// One item per CTA (persist = 0): the query blocks of a head are adjacent,
-// the one with the most keys first. Persistent (gridDim.x = G CTAs, each
-// taking items blockIdx.x + k*G): round k covers G consecutive heads at one
-// query-block class, classes from most keys to fewest, so all CTAs of a
-// round do the same amount of work and the G heads' K/V stay in L2 over
-// the nqb rounds that revisit them.
-__device__ __forceinline__ void item_of(int w, int nqb, int persist, int& bh, int& qb) {
-    if (!persist) {
-        bh = w / nqb;
-        qb = nqb - 1 - w % nqb;
-        return;
-    }
-    const int G = (int)gridDim.x;
-    const int k = w / G, c = w % G;
-    bh = (k / nqb) * G + c;
-    qb = nqb - 1 - k % nqb;
+// Work item w -> (batch*head index, query block of 256 rows): the query
+// blocks of a head are adjacent (they share K/V through L2), the one with the
+// most keys first. CTAs take items blockIdx.x, + gridDim.x, ...; the host
+// picks a grid size coprime to the number of query blocks, so that each CTA
+// cycles through all query-block classes (balanced work) while the items in
+// flight at any time cover few heads (L2 reuse of their K/V).
+__device__ __forceinline__ void item_of(int w, int nqb, int& bh, int& qb) {
+    bh = w / nqb;
+    qb = nqb - 1 - w % nqb;
 }
 
 template <typename T, int NPOLY>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o, int heads,
-                   int nbh, int items, int persist, int tq, int tk, int causal, float sl2, int* err) {
+                   int items, int tq, int tk, int causal, float sl2, int* err) {
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr uint32_t IDESC_S = idesc_f16(kQT, kKT, kBf16);
     constexpr uint32_t IDESC_PV = idesc_f16(kQT, kHD, kBf16) | (1u << 16);   // B (V) MN-major
@@ -316,8 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
             int bh, qb;
-            item_of(w, nqb, persist, bh, qb);
-            if (bh >= nbh) continue;
+            item_of(w, nqb, bh, qb);
             const int b = bh / heads, col = (bh % heads) * kHD, q0 = qb * 2 * kQT;
             int rows[2], ntile[2];
             geometry(qb, rows, ntile);
@@ -401,8 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
             int bh, qb;
-            item_of(w, nqb, persist, bh, qb);
-            if (bh >= nbh) continue;
+            item_of(w, nqb, bh, qb);
             int rows[2], ntile[2];
             geometry(qb, rows, ntile);
             const int n = ntile[i];
@@ -486,8 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
             int bh, qb;
-            item_of(w, nqb, persist, bh, qb);
-            if (bh >= nbh) continue;
+            item_of(w, nqb, bh, qb);
             int rows[2], ntile[2];
             geometry(qb, rows, ntile);
             const int n = ntile[i];
@@ -695,26 +686,18 @@ int launch_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, 
             return set_error(WIDEK_ERR_CUDA, "attention: cannot reserve %u bytes of shared memory", Smem::TOTAL);
         attr_done[dev] = true;
     }
-    // Persistent (one CTA per SM looping over items) when there are at
-    // least as many heads as SMs; otherwise one item per CTA.
+    // Persistent: at most one CTA per SM, looping over items; the grid size
+    // is the largest one not above the SM count that is coprime to the
+    // number of query blocks per head (see item_of).
     const int64_t nbh = (int64_t)a.nb * a.heads;
     const int64_t nqb = (a.tq + 2 * kQT - 1) / (2 * kQT);
-    const int sms = sm_count(dev);
-    int64_t grid, items;
-    int persist;
-    if (sms > 0 && nbh >= sms) {
-        persist = 1;
-        grid = sms;
-        items = (nbh + sms - 1) / sms * nqb * sms;
-    } else {
-        persist = 0;
-        items = nbh * nqb;
-        grid = items;
-    }
-    if (items > 0x7fffffff || nbh > 0x7fffffff) return WIDEK_ERR_UNSUPPORTED;
+    const int64_t items = nbh * nqb;
+    if (items > 0x7fffffff) return WIDEK_ERR_UNSUPPORTED;
+    int64_t grid = std::min<int64_t>(items, std::max(1, sm_count(dev)));
+    while (grid > 1 && std::gcd(grid, nqb) != 1) --grid;
     const float sl2 = a.scale * 1.4426950408889634f;
-    kern<<<(unsigned)grid, kThreads, Smem::TOTAL, st>>>(q, k, v, o, a.heads, (int)nbh, (int)items, persist, a.tq,
-                                                        a.tk, a.causal, sl2, device_error_ptr());
+    kern<<<(unsigned)grid, kThreads, Smem::TOTAL, st>>>(q, k, v, o, a.heads, (int)items, a.tq, a.tk, a.causal,
+                                                        sl2, device_error_ptr());
     return check_launch("widek_attention_fwd (tcgen05)");
 }
 
