@@ -293,19 +293,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 constexpr int kPairStages = 6;
 
+template <bool TMA_STORE>
 struct PairSmem {
     static constexpr uint32_t A_BYTES = 128 * BK * 2;
     static constexpr uint32_t B_BYTES = 128 * BK * 2;
     static constexpr uint32_t RING = kPairStages * (A_BYTES + B_BYTES);
-    static constexpr uint32_t TOTAL = 1024 + RING + 8 * (2 * kPairStages + 5) + 16;
+    static constexpr uint32_t OUT_CHUNK = 128 * 32 * 2;
+    static constexpr uint32_t OUT_BYTES = TMA_STORE ? 2 * OUT_CHUNK : 0;
+    static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + 8 * (2 * kPairStages + 5) + 16;
 };
 
-template <typename T>
+template <typename T, bool TMA_STORE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     linear_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                          const T* __restrict__ bias, T* __restrict__ y, int n_models, int M, int K, int O, int act,
-                          int vec_store, int* err) {
-    using S = PairSmem;
+                          const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias, T* __restrict__ y,
+                          int n_models, int M, int K, int O, int act, int vec_store, int* err) {
+    using S = PairSmem<TMA_STORE>;
     constexpr int BN2 = 256;                 // N per pair tile (and per CTA accumulator)
     constexpr uint32_t IDESC = idesc_f16(256, BN2, std::is_same<T, __nv_bfloat16>::value);
     constexpr uint32_t TMEM_COLS = 2 * BN2;
@@ -315,7 +318,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * S::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING);
+    uint8_t* sOut = smem + S::RING;     // [2][128 rows][64 B], 64-byte swizzled (TMA store source)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::OUT_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -348,6 +352,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tm_x);
         tma_prefetch_desc(&tm_w);
+        if (TMA_STORE) tma_prefetch_desc(&tm_y);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -434,9 +439,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_wait(done, 0, &never);
         }
     } else {
-        // Epilogue: warps 2..5 of each CTA own TMEM lane quarters (warp % 4).
+        // Epilogue: warps 2..5 of each CTA own TMEM lane quarters (warp % 4);
+        // as in linear_tc_kernel, the bias comes in by shuffles and, with
+        // TMA_STORE, each 128 x 32 chunk leaves through shared memory and
+        // one TMA store.
         const int q = warp & 3;
+        const int ep_tid = threadIdx.x - 64;
         const uint32_t leader_tempty0 = map_to_rank(smem_addr(&tempty[0]), 0);
+        int oc = 0;
         int local = 0;
         for (int tile = pair; tile < tiles; tile += npairs, ++local) {
             const int mt = tile % mt_count;
@@ -451,7 +461,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int row = mt * 256 + (int)rank * 128 + q * 32 + lane;
+            const int rloc = q * 32 + lane;
+            const int row0 = mt * 256 + (int)rank * 128;
+            const int row = row0 + rloc;
             const bool row_ok = row < M;
             T* yrow = y + ((int64_t)model * M + (row_ok ? row : 0)) * O;
             const T* brow = bias ? bias + (int64_t)model * O : nullptr;
@@ -461,20 +473,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (col0 >= O) break;  // warp-uniform
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN2 + c) + ((uint32_t)(q * 32) << 16), r);
+                const float my_bias = (brow && col0 + lane < O) ? to_f<T>(brow[col0 + lane]) : 0.f;
                 tmem_ld_wait();
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                if (brow) {
+                for (int j = 0; j < 32; ++j)
+                    v[j] = apply_act(__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j), act);
+                if (TMA_STORE) {
+                    // Rows past M of the last tile are clipped by the store;
+                    // a 256-row tile never starts past M (row0 < M).
+                    uint8_t* buf = sOut + (oc & 1) * S::OUT_CHUNK;
+                    if (ep_tid == 0) bulk_wait_read1();
+                    epi_bar_sync();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (col0 + j < O) v[j] += to_f<T>(brow[col0 + j]);
-                }
-                if (act != WIDEK_ACT_NONE) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], act);
-                }
-                if (row_ok) {
+                    for (int j = 0; j < 4; ++j) {
+                        const int phys = j ^ ((rloc >> 1) & 3);
+                        store16<T>(reinterpret_cast<T*>(buf + rloc * 64 + phys * 16), v + 8 * j);
+                    }
+                    fence_proxy_async_smem();
+                    epi_bar_sync();
+                    if (ep_tid == 0 && row0 < M) {
+                        tma_store_3d(&tm_y, buf, col0, row0, model);
+                        bulk_commit();
+                    }
+                    ++oc;
+                } else if (row_ok) {
                     if (vec_store && col0 + 32 <= O) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 8) store16<T>(yrow + col0 + j, v + j);
@@ -488,6 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive_remote(leader_tempty0 + acc * 8);
         }
+        if (TMA_STORE && ep_tid == 0) bulk_wait0();
     }
 
     tc_fence_before();
@@ -558,7 +582,6 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
 template <typename T>
 int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
                    cudaStream_t st) {
-    using S = PairSmem;
     CUtensorMap tx, tw;
     {
         const uint64_t dims[3] = {(uint64_t)k, (uint64_t)m, (uint64_t)n};
@@ -574,20 +597,34 @@ int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64
         int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    auto kern = linear_tc_pair_kernel<T>;
-    static bool attr_done[64] = {false};
-    const int dev = current_device();
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
-            return set_error(WIDEK_ERR_CUDA, "linear: cannot reserve %u bytes of shared memory", S::TOTAL);
-        attr_done[dev] = true;
+    const int vec_store = (o % 8 == 0) && aligned16(y);
+    CUtensorMap ty;
+    memset(&ty, 0, sizeof(ty));
+    if (vec_store) {
+        const uint64_t dims[3] = {(uint64_t)o, (uint64_t)m, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)o * 2, (uint64_t)m * o * 2};
+        const uint32_t box[3] = {32, 128, 1};
+        int rc = encode_tmap_tiled(&ty, tmap_dtype<T>(), 3, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
     }
+    const int dev = current_device();
     const int64_t tiles = n * ((m + 255) / 256) * ((o + 255) / 256);
     const int pairs = (int)std::min<int64_t>(tiles, sm_count(dev) / 2);
-    const int vec_store = (o % 8 == 0) && aligned16(y);
-    kern<<<2 * pairs, kThreads, S::TOTAL, st>>>(tx, tw, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
-                                                device_error_ptr());
-    return check_launch("widek_linear_fwd (tcgen05 pair)");
+    auto launch = [&](auto kern, uint32_t smem_bytes, bool& attr_done) -> int {
+        if (!attr_done) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes) !=
+                cudaSuccess)
+                return set_error(WIDEK_ERR_CUDA, "linear: cannot reserve %u bytes of shared memory", smem_bytes);
+            attr_done = true;
+        }
+        kern<<<2 * pairs, kThreads, smem_bytes, st>>>(tx, tw, ty, bias, y, (int)n, (int)m, (int)k, (int)o, act,
+                                                       vec_store, device_error_ptr());
+        return check_launch("widek_linear_fwd (tcgen05 pair)");
+    };
+    static bool attr_store[64] = {false}, attr_plain[64] = {false};
+    const int d = (dev >= 0 && dev < 64) ? dev : 0;
+    if (vec_store) return launch(linear_tc_pair_kernel<T, true>, PairSmem<true>::TOTAL, attr_store[d]);
+    return launch(linear_tc_pair_kernel<T, false>, PairSmem<false>::TOTAL, attr_plain[d]);
 }
 
 
