@@ -555,6 +555,7 @@ def run_b200(args):
     _native.load()
     _native.check(_native.lib().widek_linear_set_variant(args.linear_variant), "widek_linear_set_variant")
     _native.check(_native.lib().widek_attention_set_variant(args.attn_variant), "widek_attention_set_variant")
+    _native.check(_native.lib().widek_conv_set_variant(args.conv_variant), "widek_conv_set_variant")
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     wl = make_workload(args.workload, args.models)
@@ -657,6 +658,8 @@ def run_b200(args):
         cfg["gather"] = bool(gather)
         cfg["cuda_graph"] = bool(args.graph)
         cfg["linear_variant"] = "CTA-pair tiles" if args.linear_variant == 2 else "single-CTA tiles"
+        if args.workload == "cfg3":
+            cfg["conv_variant"] = "per-tap A tiles" if args.conv_variant == 1 else "halo-reuse A tiles"
         if args.workload == "cfg5":
             cfg["attention_variant"] = ("warp-level MMA" if args.attn_variant == 1 else
                                         "tcgen05/TMEM" + (f", {args.attn_variant - 10}/4 exp2 pairs on FMA"
@@ -723,6 +726,8 @@ def main():
     ap.add_argument("--attn-variant", type=int, default=0,
                     help="attention core: 0 tcgen05/TMEM kernel (default exponential split), 1 warp-level MMA "
                          "kernel, 10/11/12 tcgen05 with 0/1/2 of every 4 exponential pairs on the FMA pipe")
+    ap.add_argument("--conv-variant", type=int, default=0,
+                    help="tensor-core conv: 0 halo-reuse kernel where it applies, 1 per-tap kernel only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

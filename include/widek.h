@@ -277,6 +277,12 @@ WIDEK_API int widek_conv_fwd(const void* x, const void* w, const void* w_packed,
                              void* workspace, size_t workspace_bytes, const int64_t* geom, int act,
                              int residual_first, int dtype, void* stream);
 
+/* Kernel choice for widek_conv_fwd's tensor-core path: 0 = halo-reuse kernel
+ * where it applies (64-channel output tiles, output width a multiple of 8),
+ * else the per-tap kernel (default); 1 = per-tap kernel only. Process-wide;
+ * for tests and measurements. No reference counterpart. */
+WIDEK_API int widek_conv_set_variant(int variant);
+
 /* ---- WideAttention -------------------------------------------------------- */
 
 #define WIDEK_MASK_NONE 0

@@ -20,6 +20,10 @@
 //     writes NCHW directly (for a fixed output channel a warp stores 32
 //     consecutive pixels) and can fuse bias, a per-channel scale/shift
 //     (folded BatchNorm), an activation and a residual add.
+//   * with 64-channel output tiles and a tile width that is a multiple of 8,
+//     conv_halo_kernel loads each input region once per tile (kw subtiles
+//     covering the kh taps of each column offset) instead of once per tap,
+//     and keeps the output tile's weights resident in shared memory.
 // CUDA-core path (everything else, including fp32): direct convolution, one
 // output element per thread, fp32 accumulation.
 #include <cstring>
@@ -484,6 +488,358 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 implicit GEMM with halo reuse (stride 1, 64-channel output tiles)
+//
+// The per-tap kernel above reloads its whole A tile from L2 for each of the
+// kh*kw taps. Here a tile of TW x TH output pixels (TW a multiple of 8,
+// TH = 128 / TW) loads, per 64-channel input block, kw subtiles of
+// TH + (kh-1)*dh input rows x TW pixels (one per horizontal tap offset,
+// 128-byte swizzled like the per-tap boxes). For tap (ky, kx) the A operand is
+// subtile kx starting ky*dh input rows further down: the 128 rows of A are
+// consecutive 128-byte rows of the subtile, at an offset that is a multiple
+// of 8 rows (1 KB), so the standard K-major SW128 descriptor applies. The
+// weights of the current (model, 64-channel output tile) stay resident in
+// shared memory; each CTA works through a contiguous range of tiles (all
+// tiles of a model are adjacent), so they are reloaded only when the range
+// crosses into the next model or output tile.
+// ---------------------------------------------------------------------------
+constexpr int kHaloMaxStages = 8;
+constexpr int HBN = 64;
+
+struct ConvHaloGeom {
+    int n, batch, cout, ho, wo, th, tw, tiles_h, tiles_w, nt_count;
+    int kh, kw, cblocks, ph, pw, dh, dw;
+    int stages;             // ring depth, one subtile per stage
+    uint32_t sub_bytes;     // (th + (kh-1)*dh) * tw * 128: one subtile
+    uint32_t w_bytes;       // kh * kw * cblocks * HBN * 128: weights of one output tile
+    int64_t tiles;
+};
+
+// Output tile buffers: one without a residual; with a TMA-loaded residual,
+// two buffers that each receive a residual tile (requested by the producer
+// warp two tiles ahead), are updated in place by the epilogue (same
+// [channel][pixel] index) and are stored from.
+template <bool RES_TMA>
+struct HaloSmem {
+    static constexpr uint32_t TILE = HBN * BM * 2;
+    static constexpr uint32_t BUFS = RES_TMA ? 2 : 1;
+    static constexpr uint32_t BARS = 8 * (2 * kHaloMaxStages + 11) + 16;
+    static uint32_t fixed(uint32_t w_bytes) { return 1024 + w_bytes + BUFS * TILE + BARS; }
+};
+
+// Issues the MMAs of one input subtile (column offset kx, channel block cb):
+// for each kernel row ky, 4 MMAs (K = 16 each) over the 64 channels. At
+// N = 64 the tensor core consumes an MMA faster than the issuing thread can
+// build one, so the descriptors are formed once per stage and advanced by
+// constants (the start-address field counts 16-byte units; smem addresses
+// stay below 2^18, so adding never carries out of the field), and with
+// compile-time KH the loop unrolls completely.
+template <int KH>
+__device__ __forceinline__ void halo_issue_subtile(uint32_t d_tmem, uint64_t a_desc, uint64_t w_desc,
+                                                   uint32_t row_step16, uint32_t tap_stride16, uint32_t idesc,
+                                                   bool first_group, int kh_runtime) {
+    const int kh = KH > 0 ? KH : kh_runtime;
+#pragma unroll
+    for (int ky = 0; ky < (KH > 0 ? KH : 8); ++ky) {
+        if (KH == 0 && ky >= kh) break;
+        const uint64_t ad = a_desc + (uint64_t)(ky * row_step16);
+        const uint64_t bd = w_desc + (uint64_t)(ky * tap_stride16);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+            umma_f16_ss(d_tmem, ad + 2 * k, bd + 2 * k, idesc, !(first_group && ky == 0 && k == 0));
+    }
+}
+
+template <typename T, bool RES_TMA, int KH, int KW>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
+                     ConvHaloGeom g, ConvEpi e, int* err) {
+    using S = HaloSmem<RES_TMA>;
+    constexpr uint32_t IDESC = idesc_f16(BM, HBN, std::is_same<T, __nv_bfloat16>::value);
+    constexpr uint32_t TMEM_COLS = 2 * HBN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sW = smem;                                    // [kb][HBN rows][128 B]
+    T* sBuf = reinterpret_cast<T*>(sW + g.w_bytes);        // [BUFS][HBN][BM]
+    uint8_t* sA = reinterpret_cast<uint8_t*>(sBuf) + S::BUFS * S::TILE;   // [stage][rows][tw][128 B]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sA + g.stages * g.sub_bytes);
+    uint64_t* empty = full + kHaloMaxStages;
+    uint64_t* w_full = empty + kHaloMaxStages;
+    uint64_t* w_empty = w_full + 1;
+    uint64_t* tfull = w_empty + 1;        // [2]
+    uint64_t* tempty = tfull + 2;         // [2]
+    uint64_t* done = tempty + 2;
+    uint64_t* res_full = done + 1;        // [2]
+    uint64_t* res_empty = res_full + 2;   // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt_count = g.tiles_h * g.tiles_w;
+    const int stages = g.stages;
+    const int64_t per_cta = (g.tiles + gridDim.x - 1) / gridDim.x;
+    const int64_t t_begin = (int64_t)blockIdx.x * per_cta;
+    const int64_t t_end = t_begin + per_cta < g.tiles ? t_begin + per_cta : g.tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(w_full, 1);
+        mbar_init(w_empty, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4 * 32);
+            mbar_init(&res_full[a], 1);
+            mbar_init(&res_empty[a], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_y);
+        if (RES_TMA) tma_prefetch_desc(&tm_r);
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // tile -> (model, n-tile, image-in-batch, m-tile); m-tile fastest. The
+    // launcher keeps the tile count below 2^31, so 32-bit division suffices.
+    auto decode = [&](int64_t tile64, int& model, int& nt, int& b, int& mt) {
+        uint32_t tile = (uint32_t)tile64;
+        mt = (int)(tile % (uint32_t)mt_count); tile /= (uint32_t)mt_count;
+        b = (int)(tile % (uint32_t)g.batch); tile /= (uint32_t)g.batch;
+        nt = (int)(tile % (uint32_t)g.nt_count);
+        model = (int)(tile / (uint32_t)g.nt_count);
+    };
+
+    if (warp == 0) {
+        // TMA producer: weights when the (model, output tile) changes; per
+        // tile its residual (two tiles ahead of the epilogue's use), then per
+        // input-channel block and column offset kx one subtile per stage.
+        const uint64_t pol_x = l2_policy_evict_normal();
+        const uint64_t pol_w = l2_policy_evict_last();
+        int s = 0, issued = 0, wl = 0, local = 0, res_issued = 0;
+        uint32_t ph = 0;
+        int64_t cur = -1;
+        bool ok = true;
+        for (int64_t tile = t_begin; tile < t_end && ok; ++tile, ++local) {
+            int model, nt, b, mt;
+            decode(tile, model, nt, b, mt);
+            const int64_t key = (int64_t)model * g.nt_count + nt;
+            if (key != cur) {
+                // Previous weights: every MMA that reads them has completed.
+                if (wl > 0 && !mbar_wait(w_empty, (uint32_t)((wl - 1) & 1), abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(w_full, g.w_bytes);
+                    for (int kb = 0; kb < g.kh * g.kw * g.cblocks; ++kb)
+                        tma_load_3d(sW + kb * (HBN * 128), &tm_w, w_full, kb * BK, nt * HBN, model, pol_w);
+                }
+                __syncwarp();
+                ++wl;
+                cur = key;
+            }
+            const int ho0 = (mt / g.tiles_w) * g.th;
+            const int wo0 = (mt % g.tiles_w) * g.tw;
+            const int img = model * g.batch + b;
+            if (RES_TMA) {
+                // Buffer local % 2 held tile local-2's output: its store has
+                // been read out (the epilogue releases it).
+                const int rb = local & 1;
+                if (local >= 2 && !mbar_wait(&res_empty[rb], (uint32_t)(((local - 2) >> 1) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&res_full[rb], S::TILE);
+                    tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, img,
+                                l2_policy_evict_first());
+                }
+                __syncwarp();
+                ++res_issued;
+            }
+            for (int cb = 0; cb < g.cblocks && ok; ++cb) {
+                for (int kx = 0; kx < g.kw; ++kx) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&full[s], g.sub_bytes);
+                        tma_load_4d(sA + s * g.sub_bytes, &tm_x, &full[s], cb * BK, wo0 - g.pw + kx * g.dw,
+                                    ho0 - g.ph, img, pol_x);
+                    }
+                    __syncwarp();
+                    ++issued;
+                    if (++s == stages) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+        }
+        if (!ok || *abort_flag) {
+            // Copies in flight land before the CTA's shared memory is released.
+            const volatile int never = 0;
+            if (wl > 0) mbar_wait(w_full, (uint32_t)((wl - 1) & 1), &never);
+            const int inflight = issued < stages ? issued : stages;
+            for (int j = 1; j <= inflight; ++j) {
+                const int idx = issued - j;
+                mbar_wait(&full[idx % stages], (uint32_t)((idx / stages) & 1), &never);
+            }
+            for (int j = 1; j <= 2; ++j) {
+                const int idx = res_issued - j;
+                if (idx >= 0) mbar_wait(&res_full[idx & 1], (uint32_t)((idx >> 1) & 1), &never);
+            }
+        }
+    } else if (warp == 1) {
+        // MMA issuer: one thread waits, fences and issues (no warp-wide
+        // polling or __syncwarp between MMA groups, which measured ~35 %
+        // slower issue); the other lanes wait at the end.
+        if (lane == 0) {
+            int s = 0, local = 0, wl = 0;
+            uint32_t ph = 0;
+            int64_t cur = -1;
+            bool ok = true;
+            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
+            const uint64_t w_desc0 = sdesc_kmajor_sw128(smem_addr(sW));
+            // ky*dh input rows further down in a subtile; one kernel row further in the weights
+            const uint32_t row_step16 = (uint32_t)(g.dh * g.tw * 128) >> 4;
+            const uint32_t tap_stride16 = (uint32_t)((KW > 0 ? KW : g.kw) * g.cblocks * HBN * 128) >> 4;
+            for (int64_t tile = t_begin; tile < t_end && ok; ++tile, ++local) {
+                int model, nt, b, mt;
+                decode(tile, model, nt, b, mt);
+                const int64_t key = (int64_t)model * g.nt_count + nt;
+                if (key != cur) {
+                    if (wl > 0) umma_commit(w_empty);
+                    if (!mbar_wait(w_full, (uint32_t)(wl & 1), abort_flag)) { ok = false; break; }
+                    ++wl;
+                    cur = key;
+                }
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * HBN;
+                const int kw = KW > 0 ? KW : g.kw;
+                for (int cb = 0; cb < g.cblocks && ok; ++cb) {
+                    for (int kx = 0; kx < kw; ++kx) {
+                        if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint64_t a_desc = a_desc0 + (uint64_t)((s * g.sub_bytes) >> 4);
+                        const uint64_t w_desc = w_desc0 + (uint64_t)(((kx * g.cblocks + cb) * (HBN * 128)) >> 4);
+                        halo_issue_subtile<KH>(d_tmem, a_desc, w_desc, row_step16, tap_stride16, IDESC,
+                                               (cb | kx) == 0, g.kh);
+                        umma_commit(&empty[s]);
+                        if (++s == g.stages) { s = 0; ph ^= 1; }
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+            }
+            // Every MMA issued by this thread completes before TMEM is freed.
+            umma_commit(done);
+            const volatile int never = 0;
+            mbar_wait(done, 0, &never);
+        }
+        __syncwarp();
+    } else {
+        // Epilogue (as conv_tc_kernel with a TMA store): warps 2..5, TMEM lane
+        // quarter q = warp % 4; per 32-channel chunk the per-channel
+        // parameters arrive by shuffles. With a residual, tile i's residual
+        // is in buffer i % 2; the output overwrites it in place and is stored
+        // from there.
+        const int q = warp & 3;
+        const int ep_tid = threadIdx.x - 64;
+        const T* bias = static_cast<const T*>(e.bias);
+        const T* scale = static_cast<const T*>(e.scale);
+        const T* shift = static_cast<const T*>(e.shift);
+        const bool res = RES_TMA && e.residual != nullptr;
+        int local = 0;
+        for (int64_t tile = t_begin; tile < t_end; ++tile, ++local) {
+            int model, nt, b, mt;
+            decode(tile, model, nt, b, mt);
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            const int buf = RES_TMA ? (local & 1) : 0;
+            T* sOut = sBuf + buf * (HBN * BM);
+            const int r = q * 32 + lane;
+            const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
+            const int64_t img = (int64_t)model * g.batch + b;
+            // The previous tile's store has read its buffer out: release that
+            // buffer to the producer (it takes the residual two tiles on) or,
+            // without a residual, reuse the single buffer.
+            if (ep_tid == 0) {
+                bulk_wait_read0();
+                if (RES_TMA && local >= 1) mbar_arrive(&res_empty[buf ^ 1]);
+            }
+            epi_bar_sync();
+            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            if (RES_TMA && !mbar_wait(&res_full[buf], (uint32_t)((local >> 1) & 1), abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
+                break;
+            }
+#pragma unroll 1
+            for (int c = 0; c < HBN; c += 32) {
+                const int co0 = nt * HBN + c;
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * HBN + c) + ((uint32_t)(q * 32) << 16), v);
+                const int64_t my_ch = (int64_t)model * g.cout + co0 + lane;
+                const float pb = bias ? to_f<T>(bias[my_ch]) : 0.f;
+                const float ps = scale ? to_f<T>(scale[my_ch]) : 1.f;
+                const float pt = shift ? to_f<T>(shift[my_ch]) : 0.f;
+                // The chunk's 32 residual values are read before any of its
+                // outputs is written over them.
+                float rv[32];
+                if (res) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) rv[j] = to_f<T>(sOut[(c + j) * BM + r]);
+                }
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float val = (__uint_as_float(v[j]) + __shfl_sync(0xffffffffu, pb, j)) *
+                                    __shfl_sync(0xffffffffu, ps, j) +
+                                __shfl_sync(0xffffffffu, pt, j);
+                    if (res && e.residual_first) val += rv[j];
+                    val = apply_act(val, e.act);
+                    if (res && !e.residual_first) val += rv[j];
+                    sOut[(c + j) * BM + r] = from_f<T>(val);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            fence_proxy_async_smem();
+            epi_bar_sync();
+            if (ep_tid == 0) {
+                tma_store_4d(&tm_y, sOut, wo0, ho0, nt * HBN, (int)img);
+                bulk_commit();
+            }
+        }
+        if (ep_tid == 0) bulk_wait0();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
 template <typename T>
 CUtensorMapDataType tmap_dt() {
     return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -557,6 +913,93 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
     return check_launch("widek_conv_fwd (tcgen05)");
 }
 
+// 0: halo-reuse kernel where it applies, else the per-tap kernel (default);
+// 1: per-tap kernel only. Set with widek_conv_set_variant (measurements).
+int g_conv_variant = 0;
+
+// Halo-reuse geometry for a stride-1 conv with 64-channel output tiles, or
+// false when it does not fit (tile width, box limits, shared memory).
+bool halo_geometry(const ConvGeom& cg, bool res_tma, ConvHaloGeom& g, uint32_t& smem) {
+    if (cg.cout % HBN != 0 || cg.ow % 8 != 0 || cg.ow < 8) return false;
+    const int tw = cg.ow >= 16 ? 16 : 8;
+    const int th = BM / tw;
+    const int rows = th + (cg.kh - 1) * cg.dh;
+    if (rows > 256) return false;
+    g = ConvHaloGeom{};
+    g.n = cg.n; g.batch = cg.batch; g.cout = cg.cout; g.ho = cg.oh; g.wo = cg.ow;
+    g.tw = tw; g.th = th;
+    g.tiles_h = (cg.oh + th - 1) / th;
+    g.tiles_w = (cg.ow + tw - 1) / tw;
+    g.nt_count = cg.cout / HBN;
+    g.kh = cg.kh; g.kw = cg.kw; g.cblocks = cg.cin / BK;
+    g.ph = cg.ph; g.pw = cg.pw; g.dh = cg.dh; g.dw = cg.dw;
+    g.sub_bytes = (uint32_t)rows * tw * 128;
+    if ((uint64_t)cg.kh * cg.kw * g.cblocks > 64) return false;
+    g.w_bytes = (uint32_t)(cg.kh * cg.kw * g.cblocks) * HBN * 128;
+    g.tiles = (int64_t)g.n * g.nt_count * g.batch * g.tiles_h * g.tiles_w;
+    if (g.tiles > 0x7fffffff) return false;
+    const uint32_t fixed = res_tma ? HaloSmem<true>::fixed(g.w_bytes) : HaloSmem<false>::fixed(g.w_bytes);
+    if (fixed >= 232448) return false;
+    g.stages = (int)std::min<uint32_t>(kHaloMaxStages, (232448 - fixed) / g.sub_bytes);
+    if (g.stages < 2) return false;
+    smem = fixed + (uint32_t)g.stages * g.sub_bytes;
+    return true;
+}
+
+template <typename T, bool RES_TMA>
+int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const ConvHaloGeom& g, uint32_t smem,
+                     const ConvEpi& e, cudaStream_t st) {
+    const int64_t nb = (int64_t)cg.n * cg.batch;
+    CUtensorMap tx, tw_map, ty_map, tr_map;
+    {
+        const uint64_t dims[4] = {(uint64_t)cg.cin, (uint64_t)cg.w, (uint64_t)cg.h, (uint64_t)nb};
+        const uint64_t strides[3] = {(uint64_t)cg.cin * 2, (uint64_t)cg.w * cg.cin * 2,
+                                     (uint64_t)cg.h * cg.w * cg.cin * 2};
+        const uint32_t box[4] = {BK, (uint32_t)g.tw, g.sub_bytes / ((uint32_t)g.tw * 128), 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dt<T>(), 4, x_nhwc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t k = (uint64_t)cg.kh * cg.kw * cg.cin;
+        const uint64_t dims[3] = {k, (uint64_t)cg.cout, (uint64_t)cg.n};
+        const uint64_t strides[2] = {k * 2, (uint64_t)cg.cout * k * 2};
+        const uint32_t box[3] = {BK, HBN, 1};
+        int rc = encode_tmap_tiled(&tw_map, tmap_dt<T>(), 3, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)nb};
+        const uint64_t strides[3] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2,
+                                     (uint64_t)cg.cout * cg.oh * cg.ow * 2};
+        const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, (uint32_t)HBN, 1};
+        int rc = encode_tmap_tiled(&ty_map, tmap_dt<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+        memset(&tr_map, 0, sizeof(tr_map));
+        if (RES_TMA) {
+            rc = encode_tmap_tiled(&tr_map, tmap_dt<T>(), 4, e.residual, dims, strides, box,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (rc) return rc;
+        }
+    }
+    const bool k33 = cg.kh == 3 && cg.kw == 3, k11 = cg.kh == 1 && cg.kw == 1;
+    auto kern = k33 ? conv_halo_kernel<T, RES_TMA, 3, 3>
+                    : (k11 ? conv_halo_kernel<T, RES_TMA, 1, 1> : conv_halo_kernel<T, RES_TMA, 0, 0>);
+    // The dynamic shared memory size varies with the geometry: raise the
+    // kernel's limit whenever a larger size is needed.
+    static uint32_t attr_bytes[64][3] = {};
+    const int dev = current_device();
+    const int d = (dev >= 0 && dev < 64) ? dev : 0;
+    const int spec = k33 ? 0 : (k11 ? 1 : 2);
+    if (attr_bytes[d][spec] < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "conv: cannot reserve %u bytes of shared memory", smem);
+        attr_bytes[d][spec] = smem;
+    }
+    const int grid = (int)std::min<int64_t>(g.tiles, sm_count(dev));
+    kern<<<grid, kThreads, smem, st>>>(tx, tw_map, ty_map, tr_map, g, e, device_error_ptr());
+    return check_launch("widek_conv_fwd (tcgen05 halo)");
+}
+
 bool tc_eligible(const ConvGeom& g, int dtype) {
     return (dtype == WIDEK_BF16 || dtype == WIDEK_F16) && g.d == 1 && g.kd == 1 && g.sh == 1 && g.sw == 1 &&
            g.cin % 64 == 0 && g.cout % 16 == 0 && g.cout <= 4096 && g.h <= 65536 && g.w <= 65536;
@@ -602,6 +1045,14 @@ struct ConvLaunch {
                     while (tw < g.ow && tw < BM) tw <<= 1;
                     const bool store_ok = tw >= 8 && g.ow % 8 == 0 && aligned16(yp);
                     const bool res_tma = store_ok && e.residual && aligned16(e.residual);
+                    ConvHaloGeom hg;
+                    uint32_t hsmem = 0;
+                    // The halo kernel takes a residual only through its TMA path.
+                    if (g_conv_variant == 0 && store_ok && (!e.residual || res_tma) &&
+                        halo_geometry(g, res_tma, hg, hsmem)) {
+                        if (res_tma) return launch_conv_halo<T, true>(xs, wpp, yp, g, hg, hsmem, e, st);
+                        return launch_conv_halo<T, false>(xs, wpp, yp, g, hg, hsmem, e, st);
+                    }
                     if (g.cout <= 64) {
                         if (res_tma && g.cout == 64) return launch_conv_tc<T, 64, 8, true, true>(xs, wpp, yp, g, e, st);
                         if (store_ok && g.cout == 64) return launch_conv_tc<T, 64, 8, true>(xs, wpp, yp, g, e, st);
@@ -630,6 +1081,12 @@ struct ConvLaunch {
 }  // namespace widek
 
 extern "C" {
+
+int widek_conv_set_variant(int variant) {
+    if (variant < 0 || variant > 1) return widek::set_error(WIDEK_ERR_INVALID, "conv: unknown variant %d", variant);
+    widek::g_conv_variant = variant;
+    return WIDEK_OK;
+}
 
 int widek_conv_pack_weight(const void* w, void* wp, int64_t rows, int64_t cin, int64_t taps, int64_t elem_bytes,
                            void* stream) {

@@ -122,6 +122,39 @@ __global__ void swap01_kernel(const U* __restrict__ src, U* __restrict__ dst, in
     }
 }
 
+// Same permutation for long rows: a job is one chunk of kRowChunk units of
+// one destination row; the index arithmetic is per job, and each thread keeps
+// kRowUnroll independent loads in flight.
+constexpr int kRowUnroll = 4;
+constexpr int kRowThreads = 256;
+constexpr int64_t kRowChunk = (int64_t)kRowThreads * kRowUnroll;
+
+template <typename U>
+__global__ void __launch_bounds__(kRowThreads) swap01_rows_kernel(const U* __restrict__ src, U* __restrict__ dst,
+                                                                  int64_t a, int64_t b, int64_t row_units) {
+    const int64_t chunks = (row_units + kRowChunk - 1) / kRowChunk;
+    const int64_t jobs = a * b * chunks;
+    for (int64_t job = blockIdx.x; job < jobs; job += gridDim.x) {
+        const int64_t drow = job / chunks;
+        const int64_t c0 = (job - drow * chunks) * kRowChunk;
+        const int64_t j = drow / a;
+        const int64_t i = drow - j * a;
+        const U* s = src + (i * b + j) * row_units;
+        U* d = dst + drow * row_units;
+        U v[kRowUnroll];
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; ++u) {
+            const int64_t k = c0 + u * kRowThreads + threadIdx.x;
+            if (k < row_units) v[u] = s[k];
+        }
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; ++u) {
+            const int64_t k = c0 + u * kRowThreads + threadIdx.x;
+            if (k < row_units) d[k] = v[u];
+        }
+    }
+}
+
 constexpr int kPackMax = 64;
 struct PackPtrs {
     const void* p[kPackMax];
@@ -175,7 +208,14 @@ int widek_swap01(const void* src, void* dst, int64_t a, int64_t b, int64_t inner
     if (!src || !dst) return set_error(WIDEK_ERR_INVALID, "swap01: null pointer");
     cudaStream_t st = (cudaStream_t)stream;
     const uintptr_t align = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | (uintptr_t)inner_bytes;
-    if ((align & 15) == 0) {
+    if ((align & 15) == 0 && inner_bytes / 16 >= kRowThreads) {
+        // Long rows of 16-byte units: row-chunked copy.
+        const int64_t ru = inner_bytes / 16;
+        const int64_t jobs = a * b * ((ru + kRowChunk - 1) / kRowChunk);
+        const int grid = (int)std::min<int64_t>(jobs, (int64_t)sm_count(current_device()) * 8);
+        swap01_rows_kernel<uint4><<<grid, kRowThreads, 0, st>>>(static_cast<const uint4*>(src),
+                                                                 static_cast<uint4*>(dst), a, b, ru);
+    } else if ((align & 15) == 0) {
         const int64_t ru = inner_bytes / 16;
         swap01_kernel<uint4><<<grid_for(a * b * ru, 256), 256, 0, st>>>(static_cast<const uint4*>(src),
                                                                        static_cast<uint4*>(dst), a, b, ru);

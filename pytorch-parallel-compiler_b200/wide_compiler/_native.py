@@ -47,6 +47,7 @@ SIGNATURES = {
     "widek_linear_fwd_simt": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
     "widek_linear_set_variant": [_int],
     "widek_attention_set_variant": [_int],
+    "widek_conv_set_variant": [_int],
     "widek_layernorm_fwd": [_c_void_p] * 4 + [_i64] * 3 + [_dbl, _int, _c_void_p],
     "widek_swap01": [_c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p],
     "widek_pack": [ctypes.POINTER(_c_void_p), _i64, _c_void_p, _i64, _i64, _c_void_p],
