@@ -182,11 +182,14 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, c
 }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// S = Q K^T for one 128-row tile: 4 MMAs over the 64-wide head dim.
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_q, uint32_t a_k, uint32_t idesc) {
+// S = Q K^T for one 128-row tile: 4 MMAs over the 64-wide head dim. The
+// descriptors are formed once and advanced by constants (the start-address
+// field counts 16-byte units and smem addresses stay below 2^18, so the add
+// never carries out of the field): the issuing thread's work between MMAs
+// is what limits small MMAs.
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc, uint32_t idesc) {
 #pragma unroll
-    for (int kk = 0; kk < kHD / 16; ++kk)
-        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a_q + kk * 32), sdesc_kmajor_sw128(a_k + kk * 32), idesc, kk != 0);
+    for (int kk = 0; kk < kHD / 16; ++kk) umma_f16_ss(d_tmem, q_desc + 2 * kk, k_desc + 2 * kk, idesc, kk != 0);
 }
 // O (+)= P V: 8 MMAs over the 128 keys; P from TMEM (8 columns of packed
 // pairs per 16 keys), V MN-major with 16 key rows (2 KB) per MMA.
@@ -199,10 +202,10 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t t_p, uint32_t a_v, uint32_t idesc, bool accum) {
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t t_p, uint64_t v_desc, uint32_t idesc, bool accum) {
 #pragma unroll
     for (int kk = 0; kk < kKT / 16; ++kk)
-        umma_f16_ts(d_tmem, t_p + kk * 8, sdesc_mnmajor_sw128(a_v + kk * 16 * 128), idesc, accum || kk != 0);
+        umma_f16_ts(d_tmem, t_p + kk * 8, v_desc + (uint64_t)kk * (16 * 128 / 16), idesc, accum || kk != 0);
 }
 
 // Work item w -> (batch*head index, query block of 256 rows): the query
@@ -385,7 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // first P V (which overwrites O) waits for that epilogue (o_free).
         // ------------------------------------------------------------------
         const int i = warp - kMmaWarp;
-        const uint32_t aK = smem_addr(sK), aV = smem_addr(sV);
+        const uint64_t k_desc0 = sdesc_kmajor_sw128(smem_addr(sK));
+        const uint64_t v_desc0 = sdesc_mnmajor_sw128(smem_addr(sV));
         const uint32_t dS = tmem_base + i * kKT, dO = tmem_base + 2 * kKT + i * kHD;
         const uint32_t tP = tmem_base + 2 * kKT + 2 * kHD + i * (kKT / 2);
         int kc = 0, vc = 0, u = 0;      // running K tiles, V tiles, items
@@ -400,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n = ntile[i];
             const int nmax = max(ntile[0], ntile[1]);
             const int qs = u & 1;
-            const uint32_t aQ = smem_addr(sQ) + (2 * qs + i) * Smem::Q_BYTES;
+            const uint64_t q_desc = sdesc_kmajor_sw128(smem_addr(sQ) + (2 * qs + i) * Smem::Q_BYTES);
             ok = mbar_wait_warp(&q_full[qs], (uint32_t)((u >> 1) & 1), abort_flag);
             for (int j = -1; j < nmax && ok; ++j) {
                 // S(j+1) of this tile, then P V for tile j.
@@ -414,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!ok) break;
                         tc_fence_after();
                         if (lane == 0) {
-                            issue_qk(dS, aQ, aK + s1 * Smem::KV_BYTES, IDESC_S);
+                            issue_qk(dS, q_desc, k_desc0 + (uint64_t)((s1 * Smem::KV_BYTES) >> 4), IDESC_S);
                             umma_commit(&s_full[i]);
                         }
                     }
@@ -433,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!ok) break;
                         tc_fence_after();
                         if (lane == 0) {
-                            issue_pv(dO, tP, aV + sv * Smem::KV_BYTES, IDESC_PV, j > 0);
+                            issue_pv(dO, tP, v_desc0 + (uint64_t)((sv * Smem::KV_BYTES) >> 4), IDESC_PV, j > 0);
                             umma_commit(&o_full[i]);
                         }
                     }
