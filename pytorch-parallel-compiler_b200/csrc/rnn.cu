@@ -16,6 +16,10 @@
 //      through distributed shared memory; one hardware cluster barrier
 //      (barrier.cluster arrive.release / wait.acquire) publishes it.
 // h is double-buffered so a single barrier per step orders reads and writes.
+// The cluster is as large as all models' clusters allow on the GPU at once
+// (up to 8 CTAs), resident weights are stored four k at a time so that the
+// mat-vec reads 16-byte words of W and h, and the next step's input-gate
+// values are loaded into registers one step ahead.
 // When the weight slice does not fit in shared memory for any cluster size,
 // the kernel reads W_hh rows from global memory (L2) instead.
 #include <cooperative_groups.h>
@@ -62,10 +66,15 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     // global row of local row lr = g * U + j
     auto grow = [&](int lr) { return (lr / U) * H + q * U + (lr % U); };
 
+    // Resident weights: [H/4][R][4] (four consecutive k of a row in one
+    // 16-byte word) when H % 4 == 0, else k-major [H][R].
+    const bool vec4 = a.w_in_smem && (H % 4 == 0);
     if (a.w_in_smem) {
         for (int i = threadIdx.x; i < R * H; i += blockDim.x) {
             const int lr = i / H, k = i % H;
-            Ws[(size_t)k * R + lr] = to_f<T>(w[(size_t)grow(lr) * H + k]);
+            const float v = to_f<T>(w[(size_t)grow(lr) * H + k]);
+            if (vec4) Ws[((size_t)(k >> 2) * R + lr) * 4 + (k & 3)] = v;
+            else Ws[(size_t)k * R + lr] = v;
         }
     }
     for (int i = threadIdx.x; i < B * H; i += blockDim.x) {
@@ -79,23 +88,60 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     }
     cluster.sync();
 
+    // Input-projection gates of the next step, prefetched into registers one
+    // step ahead when every (b, j) pair has its own thread (i = b*U + j);
+    // otherwise the gate loop reads them directly.
+    const int bu = B * U;
+    const bool pre = bu <= (int)blockDim.x;
+    float gx_next[4] = {0.f, 0.f, 0.f, 0.f};
+    auto load_gx = [&](int i, int t, float (&v)[4]) {
+        const int b = i / U, j = i % U;
+        const T* gxr = gx + ((size_t)b * a.T + t) * G * H + q * U + j;
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi)
+            if (gi < G) v[gi] = to_f<T>(gxr[(size_t)gi * H]);
+    };
+    if (pre && (int)threadIdx.x < bu && a.T > 0) load_gx(threadIdx.x, 0, gx_next);
+
     for (int t = 0; t < a.T; ++t) {
         const float* hc = hbuf + (size_t)(t & 1) * B * H;
         float* hn_local = hbuf + (size_t)((t + 1) & 1) * B * H;
+        float gx_cur[4] = {gx_next[0], gx_next[1], gx_next[2], gx_next[3]};
+        if (pre && (int)threadIdx.x < bu && t + 1 < a.T) load_gx(threadIdx.x, t + 1, gx_next);
         // 1. recurrent mat-vec: rows x batch
         for (int lr = threadIdx.x; lr < R; lr += blockDim.x) {
             const float bias = bh ? to_f<T>(bh[grow(lr)]) : 0.f;
-            for (int b0 = 0; b0 < B; b0 += 8) {
-                float acc[8];
+            for (int b0 = 0; b0 < B; b0 += 4) {
+                float acc[4];
 #pragma unroll
-                for (int bb = 0; bb < 8; ++bb) acc[bb] = bias;
-                const int nb = B - b0 < 8 ? B - b0 : 8;
-                if (a.w_in_smem) {
+                for (int bb = 0; bb < 4; ++bb) acc[bb] = bias;
+                const int nb = B - b0 < 4 ? B - b0 : 4;
+                if (vec4) {
+                    // 16-byte weight words (conflict-free across the warp) and
+                    // 16-byte broadcasts of four h values per batch row.
+                    const float4* W4 = reinterpret_cast<const float4*>(Ws);
+#pragma unroll 2
+                    for (int k4 = 0; k4 < H / 4; ++k4) {
+                        const float4 wv = W4[(size_t)k4 * R + lr];
+#pragma unroll
+                        for (int bb = 0; bb < 4; ++bb) {
+                            if (bb < nb) {
+                                const float4 hv = reinterpret_cast<const float4*>(hc + (size_t)(b0 + bb) * H)[k4];
+                                float s = acc[bb];
+                                s = fmaf(wv.x, hv.x, s);
+                                s = fmaf(wv.y, hv.y, s);
+                                s = fmaf(wv.z, hv.z, s);
+                                s = fmaf(wv.w, hv.w, s);
+                                acc[bb] = s;
+                            }
+                        }
+                    }
+                } else if (a.w_in_smem) {
 #pragma unroll 4
                     for (int k = 0; k < H; ++k) {
                         const float wv = Ws[(size_t)k * R + lr];
 #pragma unroll
-                        for (int bb = 0; bb < 8; ++bb)
+                        for (int bb = 0; bb < 4; ++bb)
                             if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
                     }
                 } else {
@@ -104,33 +150,33 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
                     for (int k = 0; k < H; ++k) {
                         const float wv = to_f<T>(wr[k]);
 #pragma unroll
-                        for (int bb = 0; bb < 8; ++bb)
+                        for (int bb = 0; bb < 4; ++bb)
                             if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
                     }
                 }
 #pragma unroll
-                for (int bb = 0; bb < 8; ++bb)
+                for (int bb = 0; bb < 4; ++bb)
                     if (bb < nb) gates[(size_t)(b0 + bb) * R + lr] = acc[bb];
             }
         }
         __syncthreads();
-        // 2. gate math for (b, j)
+        // 2. gate math for (b, j); blockDim.x >= B*U (launcher)
         for (int i = threadIdx.x; i < B * U; i += blockDim.x) {
             const int b = i / U, j = i % U;
             const int ju = q * U + j;                            // global hidden unit
-            const T* gxr = gx + ((size_t)b * a.T + t) * G * H;
             const float* gr = gates + (size_t)b * R;
+            if (!pre) load_gx(i, t, gx_cur);
             float hnew;
             if (!LSTM) {
-                const float r = sigmoidf_(to_f<T>(gxr[ju]) + gr[j]);
-                const float z = sigmoidf_(to_f<T>(gxr[H + ju]) + gr[U + j]);
-                const float nn = tanhf(to_f<T>(gxr[2 * H + ju]) + r * gr[2 * U + j]);
+                const float r = sigmoidf_(gx_cur[0] + gr[j]);
+                const float z = sigmoidf_(gx_cur[1] + gr[U + j]);
+                const float nn = tanhf(gx_cur[2] + r * gr[2 * U + j]);
                 hnew = (1.f - z) * nn + z * hc[(size_t)b * H + ju];
             } else {
-                const float ig = sigmoidf_(to_f<T>(gxr[ju]) + gr[j]);
-                const float fg = sigmoidf_(to_f<T>(gxr[H + ju]) + gr[U + j]);
-                const float gg = tanhf(to_f<T>(gxr[2 * H + ju]) + gr[2 * U + j]);
-                const float og = sigmoidf_(to_f<T>(gxr[3 * H + ju]) + gr[3 * U + j]);
+                const float ig = sigmoidf_(gx_cur[0] + gr[j]);
+                const float fg = sigmoidf_(gx_cur[1] + gr[U + j]);
+                const float gg = tanhf(gx_cur[2] + gr[2 * U + j]);
+                const float og = sigmoidf_(gx_cur[3] + gr[3 * U + j]);
                 const float c = fg * cst[i] + ig * gg;
                 cst[i] = c;
                 hnew = og * tanhf(c);
@@ -171,10 +217,19 @@ size_t rnn_smem(int B, int H, int G, int cl, bool w_in_smem) {
 
 template <typename T, bool LSTM>
 int launch_rnn(RnnArgs a, int64_t n, cudaStream_t st) {
-    // Pick the smallest cluster (1..8 CTAs, H divisible) whose weight slice fits.
+    // Cluster of 1..8 CTAs per model (H divisible by it): the largest one for
+    // which all models' clusters fit on the GPU at once (more SMs per model,
+    // a shorter mat-vec per step), else the smallest whose weight slice fits
+    // in shared memory; failing that, weights are read from global memory.
+    const int sms = sm_count(current_device());
     int cl = 0;
     bool resident = false;
+    for (int c : {8, 4, 2, 1}) {
+        if (a.H % c || (int64_t)c * n > sms) continue;
+        if (rnn_smem(a.batch, a.H, a.G, c, true) <= kMaxSmem) { cl = c; resident = true; break; }
+    }
     for (int c : {1, 2, 4, 8}) {
+        if (cl) break;
         if (a.H % c) continue;
         if (rnn_smem(a.batch, a.H, a.G, c, true) <= kMaxSmem) { cl = c; resident = true; break; }
     }
@@ -195,7 +250,7 @@ int launch_rnn(RnnArgs a, int64_t n, cudaStream_t st) {
     int threads = ((rows + 31) / 32) * 32;
     const int pairs = a.batch * (a.H / cl);
     if (threads < pairs) threads = ((pairs + 31) / 32) * 32;
-    if (threads > 1024) threads = 1024;
+    if (threads > 1024) threads = 1024;     // the gate loop strides when pairs > 1024
     if (threads < 128) threads = 128;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(n * cl));
