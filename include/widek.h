@@ -277,6 +277,39 @@ WIDEK_API int widek_conv_fwd(const void* x, const void* w, const void* w_packed,
                              void* workspace, size_t workspace_bytes, const int64_t* geom, int act,
                              int residual_first, int dtype, void* stream);
 
+/* Tensor layouts for widek_conv_fwd_ex (N models, batch B, C channels,
+ * spatial S):
+ *   WIDEK_LAYOUT_NFIRST  [N][B][C][S]   the N-first layout of the wide primitives
+ *   WIDEK_LAYOUT_PACKED  [B][N*C][S]    the packed layout at a TracedWideModel
+ *                                       boundary (ensemble_util pack_inputs)
+ *   WIDEK_LAYOUT_CLAST   [N][B][S][C]   channels-last (tensor-core path only) */
+#define WIDEK_LAYOUT_NFIRST 0
+#define WIDEK_LAYOUT_PACKED 1
+#define WIDEK_LAYOUT_CLAST 2
+
+/* widek_conv_fwd with explicit layouts of x (in_layout), y (out_layout) and
+ * the residual (res_layout: NFIRST or PACKED). Reading a packed input fuses
+ * the boundary unpack into the channels-last staging; a channels-last input
+ * skips the staging; packed and channels-last outputs (and a packed
+ * residual) are written / read by the halo-reuse kernel's TMA maps, so a
+ * chain of convolutions needs no separate pack, unpack or transpose.
+ * Returns WIDEK_ERR_UNSUPPORTED, launching nothing, when the combination
+ * cannot be served for this geometry (the caller then uses the N-first
+ * layouts). No reference counterpart: the reference materialises the
+ * N-first tensors between ops (wide_compiler/core/traced_wide.py:463-469,
+ * :531-532). */
+WIDEK_API int widek_conv_fwd_ex(const void* x, const void* w, const void* w_packed, const void* bias,
+                                const void* scale, const void* shift, const void* residual, void* y,
+                                void* workspace, size_t workspace_bytes, const int64_t* geom, int act,
+                                int residual_first, int in_layout, int out_layout, int res_layout,
+                                int dtype, void* stream);
+
+/* 1 if widek_conv_fwd_ex would run this geometry/dtype/layout combination
+ * (assuming 16-byte aligned device pointers and a large enough workspace),
+ * else 0. Launches nothing. */
+WIDEK_API int widek_conv_layouts_supported(const int64_t* geom, int dtype, int in_layout, int out_layout,
+                                           int res_layout, int has_residual);
+
 /* Kernel choice for widek_conv_fwd's tensor-core path: 0 = halo-reuse kernel
  * where it applies (64-channel output tiles, output width a multiple of 8),
  * else the per-tap kernel (default); 1 = per-tap kernel only. Process-wide;

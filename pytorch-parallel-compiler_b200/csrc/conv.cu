@@ -231,6 +231,13 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
                  "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                  : "memory");
 }
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3,
+                                             int c4) {
+    asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -511,6 +518,7 @@ struct ConvHaloGeom {
     int n, batch, cout, ho, wo, th, tw, tiles_h, tiles_w, nt_count;
     int kh, kw, cblocks, ph, pw, dh, dw;
     int stages;             // ring depth, one subtile per stage
+    int out5, res5;         // output / residual in the packed [b][n*c][h][w] layout (5-D maps)
     uint32_t sub_bytes;     // (th + (kh-1)*dh) * tw * 128: one subtile
     uint32_t w_bytes;       // kh * kw * cblocks * HBN * 128: weights of one output tile
     int64_t tiles;
@@ -551,7 +559,7 @@ __device__ __forceinline__ void halo_issue_subtile(uint32_t d_tmem, uint64_t a_d
     }
 }
 
-template <typename T, bool RES_TMA, int KH, int KW>
+template <typename T, bool RES_TMA, int KH, int KW, bool OUT_CL>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
@@ -658,8 +666,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&res_full[rb], S::TILE);
-                    tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, img,
-                                l2_policy_evict_first());
+                    if (g.res5)
+                        tma_load_5d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, b, model,
+                                    l2_policy_evict_first());
+                    else
+                        tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, img,
+                                    l2_policy_evict_first());
                 }
                 __syncwarp();
                 ++res_issued;
@@ -810,6 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; ++j) rv[j] = to_f<T>(sOut[(c + j) * BM + r]);
                 }
                 tmem_ld_wait();
+                float ov[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     float val = (__uint_as_float(v[j]) + __shfl_sync(0xffffffffu, pb, j)) *
@@ -818,7 +831,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (res && e.residual_first) val += rv[j];
                     val = apply_act(val, e.act);
                     if (res && !e.residual_first) val += rv[j];
-                    sOut[(c + j) * BM + r] = from_f<T>(val);
+                    ov[j] = val;
+                }
+                if (OUT_CL) {
+                    // channels-last staging: pixel r's 64 channels form one
+                    // 128-byte row, 16-byte unit u stored at u ^ (r % 8)
+                    // (the 128-byte swizzle the TMA store reads).
+                    uint8_t* row = reinterpret_cast<uint8_t*>(sOut) + r * 128;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        store16<T>(reinterpret_cast<T*>(row + ((((c >> 3) + u) ^ (r & 7)) << 4)), ov + 8 * u);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sOut[(c + j) * BM + r] = from_f<T>(ov[j]);
                 }
             }
             tc_fence_before();
@@ -826,7 +851,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async_smem();
             epi_bar_sync();
             if (ep_tid == 0) {
-                tma_store_4d(&tm_y, sOut, wo0, ho0, nt * HBN, (int)img);
+                if (OUT_CL)
+                    tma_store_4d(&tm_y, sOut, nt * HBN, wo0, ho0, (int)img);
+                else if (g.out5)
+                    tma_store_5d(&tm_y, sOut, wo0, ho0, nt * HBN, b, model);
+                else
+                    tma_store_4d(&tm_y, sOut, wo0, ho0, nt * HBN, (int)img);
                 bulk_commit();
             }
         }
@@ -946,9 +976,36 @@ bool halo_geometry(const ConvGeom& cg, bool res_tma, ConvHaloGeom& g, uint32_t& 
     return true;
 }
 
-template <typename T, bool RES_TMA>
-int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const ConvHaloGeom& g, uint32_t smem,
-                     const ConvEpi& e, cudaStream_t st) {
+// Output / residual tensor maps by layout (WIDEK_LAYOUT_*): N-first NCHW
+// [n*b][c][h][w] as 4-D {W, H, C, image}; packed [b][n*c][h][w] as 5-D
+// {W, H, C, b, n}; channels-last [n*b][h][w][c] as 4-D {C, W, H, image} with
+// a 64-channel, 128-byte-swizzled box.
+template <typename T>
+int halo_out_map(CUtensorMap* m, const void* base, const ConvGeom& cg, const ConvHaloGeom& g, int layout) {
+    const uint64_t nb = (uint64_t)cg.n * cg.batch, sp = (uint64_t)cg.oh * cg.ow;
+    if (layout == WIDEK_LAYOUT_CLAST) {
+        const uint64_t dims[4] = {(uint64_t)cg.cout, (uint64_t)cg.ow, (uint64_t)cg.oh, nb};
+        const uint64_t strides[3] = {(uint64_t)cg.cout * 2, (uint64_t)cg.ow * cg.cout * 2, sp * cg.cout * 2};
+        const uint32_t box[4] = {HBN, (uint32_t)g.tw, (uint32_t)g.th, 1};
+        return encode_tmap_tiled(m, tmap_dt<T>(), 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (layout == WIDEK_LAYOUT_PACKED) {
+        const uint64_t dims[5] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)cg.batch,
+                                  (uint64_t)cg.n};
+        const uint64_t strides[4] = {(uint64_t)cg.ow * 2, sp * 2, (uint64_t)cg.n * cg.cout * sp * 2,
+                                     (uint64_t)cg.cout * sp * 2};
+        const uint32_t box[5] = {(uint32_t)g.tw, (uint32_t)g.th, HBN, 1, 1};
+        return encode_tmap_tiled(m, tmap_dt<T>(), 5, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, nb};
+    const uint64_t strides[3] = {(uint64_t)cg.ow * 2, sp * 2, (uint64_t)cg.cout * sp * 2};
+    const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, HBN, 1};
+    return encode_tmap_tiled(m, tmap_dt<T>(), 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+template <typename T, bool RES_TMA, bool OUT_CL>
+int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, ConvHaloGeom g, uint32_t smem,
+                     const ConvEpi& e, int out_layout, int res_layout, cudaStream_t st) {
     const int64_t nb = (int64_t)cg.n * cg.batch;
     CUtensorMap tx, tw_map, ty_map, tr_map;
     {
@@ -967,23 +1024,18 @@ int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, con
         int rc = encode_tmap_tiled(&tw_map, tmap_dt<T>(), 3, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    {
-        const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)nb};
-        const uint64_t strides[3] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2,
-                                     (uint64_t)cg.cout * cg.oh * cg.ow * 2};
-        const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, (uint32_t)HBN, 1};
-        int rc = encode_tmap_tiled(&ty_map, tmap_dt<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    int rc = halo_out_map<T>(&ty_map, y, cg, g, out_layout);
+    if (rc) return rc;
+    memset(&tr_map, 0, sizeof(tr_map));
+    if (RES_TMA) {
+        rc = halo_out_map<T>(&tr_map, e.residual, cg, g, res_layout);
         if (rc) return rc;
-        memset(&tr_map, 0, sizeof(tr_map));
-        if (RES_TMA) {
-            rc = encode_tmap_tiled(&tr_map, tmap_dt<T>(), 4, e.residual, dims, strides, box,
-                                   CU_TENSOR_MAP_SWIZZLE_NONE);
-            if (rc) return rc;
-        }
     }
+    g.out5 = out_layout == WIDEK_LAYOUT_PACKED;
+    g.res5 = RES_TMA && res_layout == WIDEK_LAYOUT_PACKED;
     const bool k33 = cg.kh == 3 && cg.kw == 3, k11 = cg.kh == 1 && cg.kw == 1;
-    auto kern = k33 ? conv_halo_kernel<T, RES_TMA, 3, 3>
-                    : (k11 ? conv_halo_kernel<T, RES_TMA, 1, 1> : conv_halo_kernel<T, RES_TMA, 0, 0>);
+    auto kern = k33 ? conv_halo_kernel<T, RES_TMA, 3, 3, OUT_CL>
+                    : (k11 ? conv_halo_kernel<T, RES_TMA, 1, 1, OUT_CL> : conv_halo_kernel<T, RES_TMA, 0, 0, OUT_CL>);
     // The dynamic shared memory size varies with the geometry: raise the
     // kernel's limit whenever a larger size is needed.
     static uint32_t attr_bytes[64][3] = {};
@@ -1012,46 +1064,80 @@ struct ConvLaunch {
     ConvGeom g;
     ConvEpi e;
     int dtype;
-    int64_t packed_b;     // > 0: x is channel-packed [batch][n][cin][...] (tensor-core path only)
+    int in_layout, out_layout, res_layout;   // WIDEK_LAYOUT_*
+    bool query;           // decide only: WIDEK_OK if the call would run, else WIDEK_ERR_UNSUPPORTED
     cudaStream_t st;
+
+    // In query mode pointers are absent: treat them as 16-byte aligned (as
+    // every caching-allocator block is) and the workspace as large enough.
+    bool al(const void* p) const { return query || aligned16(p); }
+    int unsupported(const char* why) const {
+        return query ? WIDEK_ERR_UNSUPPORTED : set_error(WIDEK_ERR_UNSUPPORTED, "conv: %s", why);
+    }
+
     template <typename T>
     int run() {
-        if (wp && tc_eligible(g, dtype)) {
+        const bool std_layouts = in_layout == WIDEK_LAYOUT_NFIRST && out_layout == WIDEK_LAYOUT_NFIRST &&
+                                 res_layout == WIDEK_LAYOUT_NFIRST;
+        if ((wp || query) && tc_eligible(g, dtype)) {
             if constexpr (!std::is_same<T, float>::value) {
                 const int64_t nb = (int64_t)g.n * g.batch;
-                const size_t need = (size_t)nb * g.cin * g.h * g.w * sizeof(T);
-                if (ws && ws_bytes >= need && aligned16(ws) && aligned16(wp)) {
-                    const int64_t p = (int64_t)g.h * g.w;
-                    if (p % 64 == 0 && aligned16(x)) {
-                        const int64_t jobs = nb * (g.cin / 64) * (p / 64);
-                        const int blocks = (int)std::min<int64_t>(jobs, (int64_t)sm_count(current_device()) * 8);
-                        nchw_to_nhwc_vec_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint16_t*>(x),
-                                                                        static_cast<uint16_t*>(ws), nb, g.cin, p,
-                                                                        packed_b, g.n);
-                    } else {
-                        dim3 grid((unsigned)((p + 31) / 32), (unsigned)((g.cin + 31) / 32),
-                                  (unsigned)std::min<int64_t>(nb, 65535));
-                        nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(static_cast<const T*>(x),
-                                                                             static_cast<T*>(ws), nb, g.cin, p);
-                    }
-                    int rc = check_launch("widek_conv_fwd (nhwc staging)");
-                    if (rc) return rc;
-                    const T* xs = static_cast<const T*>(ws);
-                    const T* wpp = static_cast<const T*>(wp);
-                    T* yp = static_cast<T*>(y);
+                const int64_t p = (int64_t)g.h * g.w;
+                const size_t need = (size_t)nb * g.cin * p * sizeof(T);
+                const bool cl_in = in_layout == WIDEK_LAYOUT_CLAST;
+                const bool ws_ok = query || (ws && ws_bytes >= need && aligned16(ws));
+                if (cl_in || ws_ok) {
+                    if (!al(wp)) return unsupported("packed weights not 16-byte aligned");
+                    const bool vec_staging = p % 64 == 0 && al(x);
+                    if (!cl_in && in_layout == WIDEK_LAYOUT_PACKED && !vec_staging)
+                        return unsupported("packed input needs 64-pixel multiples and 16-byte alignment");
+                    if (cl_in && !al(x)) return unsupported("channels-last input not 16-byte aligned");
                     // TMA store of the output tile: box width = tile width (>= 8 elements,
-                    // 16-byte multiple), rows 16-byte aligned, whole BN-channel tiles.
+                    // 16-byte multiple), rows 16-byte aligned, whole channel tiles.
                     int tw = 1;
                     while (tw < g.ow && tw < BM) tw <<= 1;
-                    const bool store_ok = tw >= 8 && g.ow % 8 == 0 && aligned16(yp);
-                    const bool res_tma = store_ok && e.residual && aligned16(e.residual);
+                    const bool store_ok = tw >= 8 && g.ow % 8 == 0 && al(y);
+                    const bool res_tma = store_ok && e.residual && al(e.residual);
                     ConvHaloGeom hg;
                     uint32_t hsmem = 0;
-                    // The halo kernel takes a residual only through its TMA path.
-                    if (g_conv_variant == 0 && store_ok && (!e.residual || res_tma) &&
-                        halo_geometry(g, res_tma, hg, hsmem)) {
-                        if (res_tma) return launch_conv_halo<T, true>(xs, wpp, yp, g, hg, hsmem, e, st);
-                        return launch_conv_halo<T, false>(xs, wpp, yp, g, hg, hsmem, e, st);
+                    // The halo kernel takes a residual only through its TMA
+                    // path, and not with a channels-last output.
+                    const bool halo = g_conv_variant == 0 && store_ok && (!e.residual || res_tma) &&
+                                      !(e.residual && out_layout == WIDEK_LAYOUT_CLAST) &&
+                                      halo_geometry(g, res_tma, hg, hsmem);
+                    // The per-tap kernels read any input layout (staged or
+                    // channels-last) but write and add in the N-first layout.
+                    if (!halo && (out_layout != WIDEK_LAYOUT_NFIRST || res_layout != WIDEK_LAYOUT_NFIRST))
+                        return unsupported("output/residual layout needs the halo kernel, which does not apply");
+                    if (query) return WIDEK_OK;
+                    const T* xs = static_cast<const T*>(cl_in ? x : ws);
+                    if (!cl_in) {
+                        const int64_t packed_b = in_layout == WIDEK_LAYOUT_PACKED ? g.batch : 0;
+                        if (vec_staging) {
+                            const int64_t jobs = nb * (g.cin / 64) * (p / 64);
+                            const int blocks = (int)std::min<int64_t>(jobs, (int64_t)sm_count(current_device()) * 8);
+                            nchw_to_nhwc_vec_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint16_t*>(x),
+                                                                            static_cast<uint16_t*>(ws), nb, g.cin, p,
+                                                                            packed_b, g.n);
+                        } else {
+                            dim3 grid((unsigned)((p + 31) / 32), (unsigned)((g.cin + 31) / 32),
+                                      (unsigned)std::min<int64_t>(nb, 65535));
+                            nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(static_cast<const T*>(x),
+                                                                                 static_cast<T*>(ws), nb, g.cin, p);
+                        }
+                        int rc = check_launch("widek_conv_fwd (nhwc staging)");
+                        if (rc) return rc;
+                    }
+                    const T* wpp = static_cast<const T*>(wp);
+                    T* yp = static_cast<T*>(y);
+                    if (halo) {
+                        const bool ocl = out_layout == WIDEK_LAYOUT_CLAST;
+                        if (res_tma) return launch_conv_halo<T, true, false>(xs, wpp, yp, g, hg, hsmem, e, out_layout,
+                                                                            res_layout, st);
+                        if (ocl) return launch_conv_halo<T, false, true>(xs, wpp, yp, g, hg, hsmem, e, out_layout,
+                                                                        res_layout, st);
+                        return launch_conv_halo<T, false, false>(xs, wpp, yp, g, hg, hsmem, e, out_layout,
+                                                                res_layout, st);
                     }
                     if (g.cout <= 64) {
                         if (res_tma && g.cout == 64) return launch_conv_tc<T, 64, 8, true, true>(xs, wpp, yp, g, e, st);
@@ -1069,6 +1155,8 @@ struct ConvLaunch {
                 }
             }
         }
+        if (!std_layouts) return unsupported("non-default layouts need the tensor-core path");
+        if (query) return WIDEK_OK;
         const int64_t total = (int64_t)g.n * g.batch * g.cout * g.od * g.oh * g.ow;
         conv_direct_kernel<T><<<grid_cap(total, 256), 256, 0, st>>>(static_cast<const T*>(x),
                                                                     static_cast<const T*>(w), static_cast<T*>(y),
@@ -1076,6 +1164,26 @@ struct ConvLaunch {
         return check_launch("widek_conv_fwd (direct)");
     }
 };
+
+// Geometry array -> ConvGeom with validation (shared by the entry points).
+int parse_geom(const int64_t* geom, ConvGeom& g) {
+    if (!geom) return set_error(WIDEK_ERR_INVALID, "conv: null geometry");
+    g = ConvGeom{};
+    int* f = &g.n;
+    for (int i = 0; i < 22; ++i) {
+        if (geom[i] < 0 || geom[i] > 0x7fffffff) return set_error(WIDEK_ERR_INVALID, "conv: geometry[%d] out of range", i);
+        f[i] = (int)geom[i];
+    }
+    if (g.kd < 1 || g.kh < 1 || g.kw < 1 || g.sd < 1 || g.sh < 1 || g.sw < 1 || g.dd < 1 || g.dh < 1 || g.dw < 1)
+        return set_error(WIDEK_ERR_INVALID, "conv: kernel/stride/dilation must be >= 1");
+    auto outsz = [](int in, int p, int d, int k, int s) { return (in + 2 * p - d * (k - 1) - 1) / s + 1; };
+    if (g.od != outsz(g.d, g.pd, g.dd, g.kd, g.sd) || g.oh != outsz(g.h, g.ph, g.dh, g.kh, g.sh) ||
+        g.ow != outsz(g.w, g.pw, g.dw, g.kw, g.sw))
+        return set_error(WIDEK_ERR_INVALID, "conv: output size does not match input/kernel/stride/padding");
+    return WIDEK_OK;
+}
+
+bool layout_ok(int l) { return l == WIDEK_LAYOUT_NFIRST || l == WIDEK_LAYOUT_PACKED || l == WIDEK_LAYOUT_CLAST; }
 
 }  // namespace
 }  // namespace widek
@@ -1111,29 +1219,46 @@ size_t widek_conv_workspace(int64_t n, int64_t batch, int64_t cin, int64_t d, in
     return (size_t)(n * batch * cin * d * h * w) * widek::dtype_size(dtype);
 }
 
-int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const void* bias, const void* scale,
-                   const void* shift, const void* residual, void* y, void* workspace, size_t workspace_bytes,
-                   const int64_t* geom, int act, int residual_first, int dtype, void* stream) {
+int widek_conv_fwd_ex(const void* x, const void* w, const void* w_packed, const void* bias, const void* scale,
+                      const void* shift, const void* residual, void* y, void* workspace, size_t workspace_bytes,
+                      const int64_t* geom, int act, int residual_first, int in_layout, int out_layout,
+                      int res_layout, int dtype, void* stream) {
     using namespace widek;
-    if (!geom) return set_error(WIDEK_ERR_INVALID, "conv: null geometry");
-    ConvGeom g{};
-    int* f = &g.n;
-    for (int i = 0; i < 22; ++i) {
-        if (geom[i] < 0 || geom[i] > 0x7fffffff) return set_error(WIDEK_ERR_INVALID, "conv: geometry[%d] out of range", i);
-        f[i] = (int)geom[i];
-    }
-    if (g.kd < 1 || g.kh < 1 || g.kw < 1 || g.sd < 1 || g.sh < 1 || g.sw < 1 || g.dd < 1 || g.dh < 1 || g.dw < 1)
-        return set_error(WIDEK_ERR_INVALID, "conv: kernel/stride/dilation must be >= 1");
-    auto outsz = [](int in, int p, int d, int k, int s) { return (in + 2 * p - d * (k - 1) - 1) / s + 1; };
-    if (g.od != outsz(g.d, g.pd, g.dd, g.kd, g.sd) || g.oh != outsz(g.h, g.ph, g.dh, g.kh, g.sh) ||
-        g.ow != outsz(g.w, g.pw, g.dw, g.kw, g.sw))
-        return set_error(WIDEK_ERR_INVALID, "conv: output size does not match input/kernel/stride/padding");
+    ConvGeom g;
+    int rc = parse_geom(geom, g);
+    if (rc) return rc;
     if (act < WIDEK_ACT_NONE || act > WIDEK_ACT_GELU) return set_error(WIDEK_ERR_INVALID, "conv: bad activation");
+    if (!layout_ok(in_layout) || !layout_ok(out_layout) || !layout_ok(res_layout) ||
+        res_layout == WIDEK_LAYOUT_CLAST)
+        return set_error(WIDEK_ERR_INVALID, "conv: bad layout code");
     if ((int64_t)g.n * g.batch * g.cout * g.od * g.oh * g.ow == 0) return WIDEK_OK;
     if (!x || !w || !y) return set_error(WIDEK_ERR_INVALID, "conv: null pointer");
     ConvEpi e{bias, scale, shift, residual, act, residual_first};
-    ConvLaunch L{x, w, w_packed, y, workspace, workspace_bytes, g, e, dtype, 0, (cudaStream_t)stream};
+    ConvLaunch L{x, w, w_packed, y, workspace, workspace_bytes, g, e, dtype, in_layout, out_layout, res_layout,
+                 false, (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
+}
+
+int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const void* bias, const void* scale,
+                   const void* shift, const void* residual, void* y, void* workspace, size_t workspace_bytes,
+                   const int64_t* geom, int act, int residual_first, int dtype, void* stream) {
+    return widek_conv_fwd_ex(x, w, w_packed, bias, scale, shift, residual, y, workspace, workspace_bytes, geom, act,
+                             residual_first, WIDEK_LAYOUT_NFIRST, WIDEK_LAYOUT_NFIRST, WIDEK_LAYOUT_NFIRST, dtype,
+                             stream);
+}
+
+int widek_conv_layouts_supported(const int64_t* geom, int dtype, int in_layout, int out_layout, int res_layout,
+                                 int has_residual) {
+    using namespace widek;
+    ConvGeom g;
+    if (parse_geom(geom, g)) return 0;
+    if (!layout_ok(in_layout) || !layout_ok(out_layout) || !layout_ok(res_layout) || res_layout == WIDEK_LAYOUT_CLAST)
+        return 0;
+    static const int dummy = 0;
+    ConvEpi e{nullptr, nullptr, nullptr, has_residual ? &dummy : nullptr, 0, 0};
+    ConvLaunch L{nullptr, nullptr, nullptr, nullptr, nullptr, 0, g, e, dtype, in_layout, out_layout, res_layout,
+                 true, nullptr};
+    return dispatch_dtype(dtype, L) == WIDEK_OK ? 1 : 0;
 }
 
 }  // extern "C"

@@ -64,6 +64,8 @@ SIGNATURES = {
     "widek_conv_pack_weight": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p],
     "widek_conv_workspace": [_i64] * 6 + [_int],
     "widek_conv_fwd": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64), _int, _int, _int, _c_void_p],
+    "widek_conv_fwd_ex": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64)] + [_int] * 6 + [_c_void_p],
+    "widek_conv_layouts_supported": [ctypes.POINTER(_i64)] + [_int] * 5,
     "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
 }

@@ -240,6 +240,18 @@ _UNARY_METHODS = {'relu': 'relu', 'sigmoid': 'sigmoid', 'tanh': 'tanh'}
 # TracedWideModel
 # ---------------------------------------------------------------------------
 
+class _Laid:
+    """A value kept in a layout other than N-first until a consumer needs the
+    N-first tensor: the packed model input [B, N*C, *S] (fused conv groups
+    read it directly), the packed model output written by the last fused
+    conv, or a channels-last conv output consumed only by the next fused
+    conv. `std` caches the N-first tensor once it has been made."""
+    __slots__ = ('t', 'layout', 'std')
+
+    def __init__(self, t: Tensor, layout: int):
+        self.t, self.layout, self.std = t, layout, None
+
+
 class TracedWideModel(nn.Module):
     """N models fused into one stage graph built from an FX trace."""
 
@@ -432,43 +444,137 @@ class TracedWideModel(nn.Module):
                             tail = after
                 groups[tail] = g
                 folded.update(g['nodes'][:-1])
-        return {'groups': groups, 'folded': folded}
+        by_head = {g['head']: g for g in groups.values()}
+        return {'groups': groups, 'folded': folded, 'consumers': cons, 'by_head': by_head}
+
+    def _group_ready(self, g: Dict[str, Any], values: Dict[str, Any]) -> bool:
+        """Whether a fused group can run now (eval-mode BatchNorm with
+        running statistics, CUDA input, residual available)."""
+        x = values.get(self._node_args[g['head']][0])
+        t = x.t if isinstance(x, _Laid) else x
+        if not isinstance(t, Tensor) or not t.is_cuda:
+            return False
+        if g['kind'] == 'linear':
+            return True
+        bn_mod = self.stages[g['bn'].replace('.', '_')].op
+        if bn_mod.training or bn_mod.running_mean is None or bn_mod.running_var is None:
+            return False
+        if g['residual'] is not None:
+            r = values.get(g['residual'])
+            r = r.t if isinstance(r, _Laid) else r
+            if not isinstance(r, Tensor) or r.dtype != t.dtype or r.device != t.device:
+                return False
+        return True
+
+    def _conv_params(self, op):
+        if isinstance(op, WideConv2d):
+            return op.grouped_conv.weight, op.grouped_conv.bias, op.stride, op.padding, op.dilation
+        w, b = op._params()
+        return w, b, (op.stride,), (op.padding,), (op.dilation,)
+
+    def _next_conv_group(self, g: Dict[str, Any]) -> Optional[Dict[str, Any]]:
+        """The fused conv group whose input is g's output, when that group
+        is the output's only consumer."""
+        tail = g['nodes'][-1]
+        cons = self._fusion.get('consumers', {}).get(tail, [])
+        if len(cons) != 1:
+            return None
+        head_group = self._fusion.get('by_head', {}).get(cons[0])
+        if head_group is None or head_group['kind'] != 'conv':
+            return None
+        if self._node_args[head_group['head']][0] != tail or head_group['residual'] == tail:
+            return None
+        return head_group
 
     def _run_group(self, g: Dict[str, Any], values: Dict[str, Any]):
         """Executes a fused group; returns None when it cannot run fused
-        (e.g. BatchNorm in training mode), in which case the nodes run one by one."""
+        (e.g. BatchNorm in training mode), in which case the nodes run one by
+        one. Conv groups read and write the packed / channels-last layouts
+        where that saves a pack, unpack or transpose (see _Laid)."""
         from .. import ops
+        if not self._group_ready(g, values):
+            return None
         head = g['head']
-        x = values.get(self._node_args[head][0])
-        if not isinstance(x, Tensor) or not x.is_cuda:
-            return None
         op = self.stages[head.replace('.', '_')]
+        xv = values.get(self._node_args[head][0])
         if g['kind'] == 'linear':
-            return ops.linear(x, op.weight, op.bias, act=g['act'])
+            return ops.linear(self._std(xv), op.weight, op.bias, act=g['act'])
         bn_mod = self.stages[g['bn'].replace('.', '_')].op
-        if bn_mod.training or bn_mod.running_mean is None or bn_mod.running_var is None:
-            return None
-        res = values.get(g['residual']) if g['residual'] is not None else None
-        if g['residual'] is not None and not isinstance(res, Tensor):
-            return None
         scale, shift = _bn_fold(bn_mod)
-        if isinstance(op, WideConv2d):
-            w, b = op.grouped_conv.weight, op.grouped_conv.bias
-            st, pd, dl = op.stride, op.padding, op.dilation
-        else:
-            w, b = op._params()
-            st, pd, dl = (op.stride,), (op.padding,), (op.dilation,)
-        if res is not None and (res.dtype != x.dtype or res.device != x.device):
-            return None
-        y = ops.conv_nd(x, w, b, op.n, st, pd, dl, scale=scale.to(x.dtype), shift=shift.to(x.dtype),
-                        residual=res, act=g['act'], residual_first=g['residual_first'])
+        w, b, st, pd, dl = self._conv_params(op)
+        rv = values.get(g['residual']) if g['residual'] is not None else None
+        t = xv.t if isinstance(xv, _Laid) else xv
+        scale, shift = scale.to(t.dtype), shift.to(t.dtype)
+        kw = dict(scale=scale, shift=shift, act=g['act'], residual_first=g['residual_first'])
+        in_l = xv.layout if isinstance(xv, _Laid) else ops.LAYOUT_NFIRST
+        res_l = rv.layout if isinstance(rv, _Laid) else ops.LAYOUT_NFIRST
+        res_t = rv.t if isinstance(rv, _Laid) else rv
+        # Output layout: packed when this group produces the model output,
+        # channels-last when the only consumer is a fused conv group that can
+        # read it (checked for its geometry), else N-first.
+        out_l = ops.LAYOUT_NFIRST
+        tail = g['nodes'][-1]
+        nxt = self._next_conv_group(g)
+        if tail == self._output_name and self._fusion.get('consumers', {}).get(tail) == ['<output>']:
+            out_l = ops.LAYOUT_PACKED
+        elif nxt is not None and self._group_ready(nxt, {**values, self._node_args[nxt['head']][0]: t}) \
+                and self._clast_ok(nxt, op, t, in_l, w, st, pd, dl):
+            # (the next group's readiness is judged with this group's output
+            # standing in for its input; its residual must already exist)
+            out_l = ops.LAYOUT_CLAST
+        tries = [(in_l, out_l, res_l)]
+        if out_l != ops.LAYOUT_NFIRST:
+            tries.append((in_l, ops.LAYOUT_NFIRST, res_l))
+        for il, ol, rl in tries:
+            y = ops.conv_nd(t, w, b, op.n, st, pd, dl, residual=res_t, in_layout=il, out_layout=ol,
+                            res_layout=rl, **kw)
+            if y is not None:
+                return _Laid(y, ol) if ol != ops.LAYOUT_NFIRST else y
+        # Fall back to N-first tensors everywhere.
+        xs = self._std(xv)
+        res = self._std(rv) if rv is not None else None
+        y = ops.conv_nd(xs, w, b, op.n, st, pd, dl, residual=res, **kw)
         if res is not None and y.shape != res.shape:
             return None
         return y
 
+    def _clast_ok(self, nxt: Dict[str, Any], op, t: Tensor, in_l: int, w, st, pd, dl) -> bool:
+        """Whether the next conv group can read this group's output in the
+        channels-last layout (its geometry, dtype and output layouts)."""
+        import ctypes
+        from .. import _native as N
+        from .. import ops
+        op2 = self.stages[nxt['head'].replace('.', '_')]
+        w2, _, st2, pd2, dl2 = self._conv_params(op2)
+        n = op.n
+        if in_l == ops.LAYOUT_PACKED:
+            batch, sp = t.shape[0], tuple(t.shape[2:])
+        elif in_l == ops.LAYOUT_CLAST:
+            batch, sp = t.shape[1], tuple(t.shape[2:-1])
+        else:
+            batch, sp = t.shape[1], tuple(t.shape[3:])
+        nd = len(sp)
+        if nd not in (1, 2) or w2.dim() != nd + 2:
+            return False
+        cout = w.shape[0] // n
+        pad3 = lambda v, fill: (fill,) * (3 - nd) + tuple(v)
+        ks, st_, pd_, dl_ = pad3(w.shape[2:], 1), pad3(st, 1), pad3(pd, 0), pad3(dl, 1)
+        sp3 = pad3(sp, 1)
+        osp = tuple((sp3[i] + 2 * pd_[i] - dl_[i] * (ks[i] - 1) - 1) // st_[i] + 1 for i in range(3))
+        cout2 = w2.shape[0] // op2.n
+        ks2, st2_, pd2_, dl2_ = pad3(w2.shape[2:], 1), pad3(st2, 1), pad3(pd2, 0), pad3(dl2, 1)
+        osp2 = tuple((osp[i] + 2 * pd2_[i] - dl2_[i] * (ks2[i] - 1) - 1) // st2_[i] + 1 for i in range(3))
+        if min(osp2) <= 0 or op2.n != n or w2.shape[1] != cout:
+            return False
+        geom = (ctypes.c_int64 * 22)(n, batch, cout, cout2, *osp, *ks2, *st2_, *pd2_, *dl2_, *osp2)
+        has_res = 1 if nxt['residual'] is not None else 0
+        return bool(N.lib().widek_conv_layouts_supported(geom, N.dtype_code(t), ops.LAYOUT_CLAST,
+                                                         ops.LAYOUT_NFIRST, ops.LAYOUT_NFIRST, has_res))
+
     def _run_stages(self, x: Tensor) -> Any:
         if self._fusion is None:
-            self._fusion = self._build_fusion_plan() if self.fuse else {'groups': {}, 'folded': set()}
+            self._fusion = self._build_fusion_plan() if self.fuse else {'groups': {}, 'folded': set(),
+                                                                        'consumers': {}, 'by_head': {}}
         groups, folded = self._fusion['groups'], self._fusion['folded']
         values: Dict[str, Any] = {self._input_name: x}
         for name in self._attr_names:
@@ -494,17 +600,39 @@ class TracedWideModel(nn.Module):
             values[name] = self._run_node(name, values)
         return values[self._output_name]
 
+    def _std(self, v: Any) -> Any:
+        """The N-first tensor of a value (materialised once for _Laid)."""
+        if not isinstance(v, _Laid):
+            return v
+        if v.std is None:
+            from ..ops import LAYOUT_PACKED
+            if v.layout != LAYOUT_PACKED:
+                raise RuntimeError("TracedWideModel: internal channels-last value reached a non-conv consumer")
+            v.std = self._unpack(v.t)
+        return v.std
+
     def _run_node(self, name: str, values: Dict[str, Any]) -> Any:
         op = self.stages[name.replace('.', '_')]
-        args = [values[a] if isinstance(a, str) and a in values else a for a in self._node_args[name]]
-        kwargs = {k: (values[v] if isinstance(v, str) and v in values else v)
+        args = [self._std(values[a]) if isinstance(a, str) and a in values else a for a in self._node_args[name]]
+        kwargs = {k: (self._std(values[v]) if isinstance(v, str) and v in values else v)
                   for k, v in self._node_kwargs.get(name, {}).items()}
         return op(*args, **kwargs)
 
     def forward(self, x: Tensor) -> Tensor:
-        out = self._run_stages(self._unpack(x))
+        from ..ops import LAYOUT_PACKED
+        if self.fuse and x.is_cuda:
+            b, nc = x.shape[0], x.shape[1]
+            if nc % self.n != 0:
+                raise ValueError(f"input dim 1 ({nc}) is not a multiple of N={self.n}")
+            out = self._run_stages(_Laid(x, LAYOUT_PACKED))
+        else:
+            out = self._run_stages(self._unpack(x))
         if isinstance(out, tuple):
             out = out[0]
+        if isinstance(out, _Laid):
+            if out.layout == LAYOUT_PACKED:
+                return out.t           # the last fused conv wrote the packed output
+            out = self._std(out)
         return self._pack(out)
 
     def summary(self) -> str:

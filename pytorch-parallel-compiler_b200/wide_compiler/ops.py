@@ -419,23 +419,43 @@ def _packed_weight(weight: Tensor, rows: int, cin: int, taps: int, dev) -> Tenso
     return wp
 
 
+LAYOUT_NFIRST, LAYOUT_PACKED, LAYOUT_CLAST = 0, 1, 2
+
+
 def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, padding, dilation,
             scale: Optional[Tensor] = None, shift: Optional[Tensor] = None, residual: Optional[Tensor] = None,
-            act: int = ACT_NONE, residual_first: bool = False) -> Tensor:
-    """N independent convolutions on x [N, B, Cin, *S] (1-3 spatial dims) with
-    weight [N*Cout, Cin, *K]; returns [N, B, Cout, *S']. Optional fused
-    epilogue: per-channel scale/shift ([N*Cout]), activation, residual."""
+            act: int = ACT_NONE, residual_first: bool = False, in_layout: int = LAYOUT_NFIRST,
+            out_layout: int = LAYOUT_NFIRST, res_layout: int = LAYOUT_NFIRST) -> Optional[Tensor]:
+    """N independent convolutions with weight [N*Cout, Cin, *K] (1-3 spatial
+    dims). x is [N, B, Cin, *S] (LAYOUT_NFIRST), [B, N*Cin, *S] (LAYOUT_PACKED,
+    the TracedWideModel boundary layout) or [N, B, *S, Cin] (LAYOUT_CLAST); the
+    result uses out_layout likewise, and the optional residual res_layout
+    (NFIRST or PACKED). Optional fused epilogue: per-channel scale/shift
+    ([N*Cout]), activation, residual. With non-default layouts the call
+    returns None when the library cannot serve the combination for this
+    geometry (nothing is launched); the default layouts always run."""
     dev = N.require_cuda(x, weight, bias, scale, shift, residual, what="WideConv")
     _same_dtype("WideConv", weight, x, bias, scale, shift, residual)
-    nd = x.dim() - 3
+    if in_layout == LAYOUT_PACKED:
+        batch, cin, sp_in = x.shape[0], x.shape[1] // n, tuple(x.shape[2:])
+        if x.shape[1] % n != 0:
+            raise ValueError(f"WideConv: packed input {tuple(x.shape)} is not N={n} channel groups")
+    elif in_layout == LAYOUT_CLAST:
+        nn_, batch, cin, sp_in = x.shape[0], x.shape[1], x.shape[-1], tuple(x.shape[2:-1])
+        if nn_ != n:
+            raise ValueError(f"WideConv: channels-last input {tuple(x.shape)} is not N={n} models")
+    else:
+        nn_, batch, cin, sp_in = x.shape[0], x.shape[1], x.shape[2], tuple(x.shape[3:])
+        if nn_ != n:
+            raise ValueError(f"WideConv: input {tuple(x.shape)} does not match weight {tuple(weight.shape)} for N={n}")
+    nd = len(sp_in)
     if nd not in (1, 2, 3) or weight.dim() != nd + 2:
         raise ValueError(f"WideConv: input {tuple(x.shape)} / weight {tuple(weight.shape)} rank mismatch")
-    nn_, batch, cin = x.shape[:3]
-    if nn_ != n or weight.shape[0] % n != 0 or weight.shape[1] != cin:
+    if weight.shape[0] % n != 0 or weight.shape[1] != cin:
         raise ValueError(f"WideConv: input {tuple(x.shape)} does not match weight {tuple(weight.shape)} for N={n}")
     cout = weight.shape[0] // n
     pad3 = lambda v, fill: (fill,) * (3 - nd) + tuple(v)
-    sp = pad3(x.shape[3:], 1)
+    sp = pad3(sp_in, 1)
     ks = pad3(weight.shape[2:], 1)
     st = pad3(stride, 1)
     pd = pad3(padding, 0)
@@ -443,21 +463,34 @@ def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, p
     out_sp = tuple((sp[i] + 2 * pd[i] - dl[i] * (ks[i] - 1) - 1) // st[i] + 1 for i in range(3))
     if min(out_sp) <= 0:
         raise ValueError(f"WideConv: output size {out_sp} is not positive")
-    y = torch.empty((n, batch, cout, *out_sp[3 - nd:]), device=dev, dtype=x.dtype)
-    xd = _dense(x)
+    osp = out_sp[3 - nd:]
     geom = (ctypes.c_int64 * 22)(n, batch, cin, cout, *sp, *ks, *st, *pd, *dl, *out_sp)
+    default = in_layout == out_layout == res_layout == LAYOUT_NFIRST
+    if not default and not N.lib().widek_conv_layouts_supported(geom, N.dtype_code(x), in_layout, out_layout,
+                                                                  res_layout, 1 if residual is not None else 0):
+        return None
+    if out_layout == LAYOUT_PACKED:
+        y = torch.empty((batch, n * cout, *osp), device=dev, dtype=x.dtype)
+    elif out_layout == LAYOUT_CLAST:
+        y = torch.empty((n, batch, *osp, cout), device=dev, dtype=x.dtype)
+    else:
+        y = torch.empty((n, batch, cout, *osp), device=dev, dtype=x.dtype)
+    xd = _dense(x)
     wp = ws = None
     tc = (x.dtype in (torch.bfloat16, torch.float16) and nd in (1, 2) and st == (1, 1, 1) and cin % 64 == 0
           and cout % 16 == 0)
     if tc:
         taps = ks[0] * ks[1] * ks[2]
         wp = _packed_weight(weight, n * cout, cin, taps, dev)
-        ws = torch.empty(int(N.lib().widek_conv_workspace(n, batch, cin, *sp, N.dtype_code(x))) // x.element_size(),
-                         device=dev, dtype=x.dtype)
+        if in_layout != LAYOUT_CLAST:
+            ws = torch.empty(int(N.lib().widek_conv_workspace(n, batch, cin, *sp, N.dtype_code(x))) //
+                             x.element_size(), device=dev, dtype=x.dtype)
     with _guard(dev):
-        rc = N.lib().widek_conv_fwd(xd.data_ptr(), _dense(weight).data_ptr(), N.ptr(wp), N.ptr(bias), N.ptr(scale),
-                                    N.ptr(shift), N.ptr(_dense(residual) if residual is not None else None),
-                                    y.data_ptr(), N.ptr(ws), 0 if ws is None else ws.numel() * ws.element_size(),
-                                    geom, act, 1 if residual_first else 0, N.dtype_code(x), N.stream_ptr(dev))
+        rc = N.lib().widek_conv_fwd_ex(xd.data_ptr(), _dense(weight).data_ptr(), N.ptr(wp), N.ptr(bias),
+                                       N.ptr(scale), N.ptr(shift),
+                                       N.ptr(_dense(residual) if residual is not None else None),
+                                       y.data_ptr(), N.ptr(ws), 0 if ws is None else ws.numel() * ws.element_size(),
+                                       geom, act, 1 if residual_first else 0, in_layout, out_layout, res_layout,
+                                       N.dtype_code(x), N.stream_ptr(dev))
     N.check(rc, "widek_conv_fwd")
     return y
