@@ -148,7 +148,6 @@ class Workload:
     dtype = "bf16"
     bound = "hbm"            # roofline of the dominant kernel(s)
     peak_key = "hbm"
-    launches_per_step = 1
 
     def forward(self, x):
         return self.module(x)
@@ -222,7 +221,6 @@ class _MLP(nn.Module):
 class MlpCfg1(Workload):
     name = "cfg1"
     dtype = "fp32"
-    launches_per_step = 5
 
     def __init__(self, n=100, b=32):
         self.n, self.b = n, b
@@ -283,7 +281,6 @@ class ResBlockCfg3(Workload):
     name = "cfg3"
     bound = "tensor"
     peak_key = "tensor_sustained"
-    launches_per_step = 9
 
     def torch_reference_step(self):
         """The reference's GPU op sequence for this graph (wide_conv2d.py:169-194
@@ -319,7 +316,8 @@ class ResBlockCfg3(Workload):
     def config(self):
         return {"workload": f"cfg3 TracedWideModel of N={self.n} ResBlocks (Conv3x3 {self.c}->{self.c} pad 1, BN "
                             f"eval, ReLU, Conv3x3, BN, + identity), B={self.b}, {self.hw}x{self.hw}, bf16",
-                "l2": "inputs larger than L2 (419 MB activation per step), no flush"}
+                "l2": f"inputs larger than L2 ({self.n * self.b * self.c * self.hw * self.hw * 2 / 1e6:.0f} MB "
+                      f"activation per step), no flush"}
 
     def setup(self, dev, seed):
         import wide_compiler as wc
@@ -361,7 +359,6 @@ class ResBlockCfg3(Workload):
 
 class RnnCfg4(Workload):
     dtype = "fp32"
-    launches_per_step = 2
 
     def __init__(self, kind, n=32, b=4, t=32, i=64, h=128):
         self.kind, self.n, self.b, self.t, self.i, self.h = kind, n, b, t, i, h
@@ -414,7 +411,6 @@ class AttnCfg5(Workload):
     name = "cfg5"
     bound = "tensor"
     peak_key = "tensor_sustained"
-    launches_per_step = 4
 
     def torch_reference_step(self):
         """The reference's GPU op sequence (wide_attention.py:178-238 einsum
@@ -496,7 +492,7 @@ def make_workload(name, models=None):
     if name == "cfg1":
         return MlpCfg1()
     if name == "cfg3":
-        return ResBlockCfg3()
+        return ResBlockCfg3(n=models or 100)
     if name == "cfg4gru":
         return RnnCfg4("gru")
     if name == "cfg4lstm":
@@ -577,6 +573,7 @@ def run_b200(args):
 
     run = step
     graph = None
+    graph_launches = 0
     if args.graph:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
@@ -585,8 +582,10 @@ def run_b200(args):
                 step()
         torch.cuda.current_stream(dev).wait_stream(side)
         graph = torch.cuda.CUDAGraph()
+        n0 = _native.lib().widek_launch_count()
         with torch.cuda.graph(graph):
             step()
+        graph_launches = _native.lib().widek_launch_count() - n0   # kernels in one replay
         run = graph.replay
 
     clocks = ClockSampler(local)
@@ -597,10 +596,15 @@ def run_b200(args):
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    launches0 = _native.lib().widek_launch_count()
     e0.record(stream)
     for _ in range(args.steps):
         run()
     e1.record(stream)
+    # Our kernels launched in the timed region: counted by the library at
+    # every launch (a graph replay runs the kernels counted at capture).
+    gpu_launches = (graph_launches * args.steps if graph is not None
+                    else _native.lib().widek_launch_count() - launches0)
     barrier()
     ms = e0.elapsed_time(e1) / args.steps
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -697,7 +701,7 @@ def run_b200(args):
                     "d2h_bytes_per_step": y_host[0].numel() * y_host[0].element_size(),
                     "steps": e2e_steps, "ms_per_step": ms_e2e,
                     "pipelined": "upload, forward and download on separate streams, double-buffered"},
-            "gpu_launches": args.steps * wl.launches_per_step,
+            "gpu_launches": gpu_launches,
             "roofline": roof,
             "clocks": clk,
             "device_error": dev_err,

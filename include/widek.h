@@ -277,6 +277,11 @@ WIDEK_API int widek_conv_fwd(const void* x, const void* w, const void* w_packed,
                              void* workspace, size_t workspace_bytes, const int64_t* geom, int act,
                              int residual_first, int dtype, void* stream);
 
+/* Number of kernels the library has launched in this process (all entry
+ * points; a launch captured into a CUDA graph counts once, at capture). For
+ * measurements. No reference counterpart. */
+WIDEK_API long long widek_launch_count(void);
+
 /* Tensor layouts for widek_conv_fwd_ex (N models, batch B, C channels,
  * spatial S):
  *   WIDEK_LAYOUT_NFIRST  [N][B][C][S]   the N-first layout of the wide primitives

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -28,7 +29,14 @@ int set_error(int code, const char* fmt, ...) {
     return code;
 }
 
+// Kernel launches issued by the library (every launch path ends in
+// check_launch); read with widek_launch_count.
+static std::atomic<long long> g_launches{0};
+
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
 int check_launch(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return set_error(WIDEK_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -129,3 +137,5 @@ int encode_tmap_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
 }
 
 }  // namespace widek
+
+extern "C" long long widek_launch_count(void) { return widek::launch_count(); }

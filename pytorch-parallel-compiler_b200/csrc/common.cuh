@@ -18,7 +18,8 @@ namespace widek {
 // Host-side error state (thread-local message, returned codes).
 // ---------------------------------------------------------------------------
 int set_error(int code, const char* fmt, ...);
-int check_launch(const char* what);          // cudaGetLastError -> code
+int check_launch(const char* what);          // counts the launch; cudaGetLastError -> code
+long long launch_count();                    // launches so far (process-wide)
 int sm_count(int device);                    // cached multiprocessor count
 int current_device();
 

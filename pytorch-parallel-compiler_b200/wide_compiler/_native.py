@@ -48,6 +48,7 @@ SIGNATURES = {
     "widek_linear_set_variant": [_int],
     "widek_attention_set_variant": [_int],
     "widek_conv_set_variant": [_int],
+    "widek_launch_count": [],
     "widek_layernorm_fwd": [_c_void_p] * 4 + [_i64] * 3 + [_dbl, _int, _c_void_p],
     "widek_swap01": [_c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p],
     "widek_pack": [ctypes.POINTER(_c_void_p), _i64, _c_void_p, _i64, _i64, _c_void_p],
@@ -69,7 +70,8 @@ SIGNATURES = {
     "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
 }
-RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t, "widek_conv_workspace": ctypes.c_size_t}
+RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t, "widek_conv_workspace": ctypes.c_size_t,
+            "widek_launch_count": ctypes.c_longlong}
 
 
 class WideKernelError(RuntimeError):
