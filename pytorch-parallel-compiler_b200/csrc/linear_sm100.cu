@@ -154,48 +154,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------
-        // MMA issuer (one elected thread issues, the warp tracks phases)
+        // MMA issuer: one thread waits, fences and issues, with descriptors
+        // formed once and advanced by constants (the start-address field
+        // counts 16-byte units and smem addresses stay below 2^18, so the
+        // add never carries out of it); the other lanes wait at the end.
+        // Warp-wide polling and per-MMA descriptor arithmetic measurably
+        // slow the issue of back-to-back MMAs.
         // ------------------------------------------------------------------
-        int s = 0;
-        uint32_t ph = 0;
-        bool ok = true;
-        int local = 0;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
-            const int acc = local & 1;
-            const uint32_t aph = (local >> 1) & 1;
-            if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + acc * BN;
-            for (int kb = 0; kb < kb_count; ++kb) {
-                if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int local = 0;
+            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
+            const uint64_t b_desc0 = sdesc_kmajor_sw128(smem_addr(sB));
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a0 = smem_addr(sA + s * S::A_BYTES);
-                    const uint32_t b0 = smem_addr(sB + s * S::B_BYTES);
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = a_desc0 + (uint64_t)((s * S::A_BYTES) >> 4);
+                    const uint64_t bd = b_desc0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        // 16 elements = 32 bytes further along the swizzled row.
-                        umma_f16_ss(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32), IDESC,
-                                    (kb | k) != 0);
-                    }
+                    for (int k = 0; k < BK / 16; ++k)   // 16 elements = 32 bytes along the swizzled row
+                        umma_f16_ss(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
                     umma_commit(&empty[s]);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
                 }
-                __syncwarp();
-                if (++s == STAGES) { s = 0; ph ^= 1; }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);
             }
-            if (!ok) break;
-            if (lane == 0) umma_commit(&tfull[acc]);
-            __syncwarp();
+            if (!ok) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            }
+            // Drain: every MMA this thread issued completes before TMEM is freed.
+            umma_commit(done);
+            const volatile int never = 0;
+            mbar_wait(done, 0, &never);
         }
-        if (!ok) {
-            *abort_flag = 1;
-            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
-        }
-        // Drain: every MMA this thread issued completes before TMEM is freed.
-        if (lane == 0) umma_commit(done);
         __syncwarp();
-        const volatile int never = 0;
-        mbar_wait(done, 0, &never);
     } else {
         // ------------------------------------------------------------------
         // Epilogue: warps 2..5 own TMEM lane quarters (warp % 4). Per
