@@ -401,11 +401,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             while (globaltimer_ns() - t0 < 1000000ull) { }
         }
     } else if (warp == 1) {
-        if (rank == 0) {
-            // MMA issuer (leader only)
+        if (rank == 0 && lane == 0) {
+            // MMA issuer (leader CTA, one thread; descriptors formed once)
             int s = 0, local = 0;
             uint32_t ph = 0;
             bool ok = true;
+            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
+            const uint64_t b_desc0 = sdesc_kmajor_sw128(smem_addr(sB));
             for (int tile = pair; tile < tiles && ok; tile += npairs, ++local) {
                 const int acc = local & 1;
                 const uint32_t aph = (local >> 1) & 1;
@@ -415,31 +417,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < kb_count; ++kb) {
                     if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t a0 = smem_addr(sA + s * S::A_BYTES);
-                        const uint32_t b0 = smem_addr(sB + s * S::B_BYTES);
+                    const uint64_t ad = a_desc0 + (uint64_t)((s * S::A_BYTES) >> 4);
+                    const uint64_t bd = b_desc0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            umma_f16_ss_pair(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(b0 + k * 32),
-                                             IDESC, (kb | k) != 0);
-                        umma_commit_pair_multicast(&empty[s], 0x3);
-                    }
-                    __syncwarp();
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_f16_ss_pair(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+                    umma_commit_pair_multicast(&empty[s], 0x3);
                     if (++s == STAGES) { s = 0; ph ^= 1; }
                 }
                 if (!ok) break;
-                if (lane == 0) umma_commit_pair_multicast(&tfull[acc], 0x3);
-                __syncwarp();
+                umma_commit_pair_multicast(&tfull[acc], 0x3);
             }
             if (!ok) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
             }
-            if (lane == 0) umma_commit_pair_multicast(done, 0x1);
-            __syncwarp();
+            umma_commit_pair_multicast(done, 0x1);
             const volatile int never = 0;
             mbar_wait(done, 0, &never);
         }
+        __syncwarp();
     } else {
         // Epilogue: warps 2..5 of each CTA own TMEM lane quarters (warp % 4);
         // as in linear_tc_kernel, the bias comes in by shuffles and, with
