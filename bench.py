@@ -221,6 +221,7 @@ class _MLP(nn.Module):
 class MlpCfg1(Workload):
     name = "cfg1"
     dtype = "fp32"
+    bound = "fp32"           # one fused chain launch of CUDA-core fp32 FMAs
 
     def __init__(self, n=100, b=32):
         self.n, self.b = n, b
@@ -675,6 +676,17 @@ def run_b200(args):
                     "frac": achieved / pk["hbm"], "peak_kind": f"{pk['kind']} HBM copy",
                     "traffic": wl.traffic(), "algorithmic_bytes": wl.alg_bytes(),
                     "tflops": wl.alg_flops() / (ms * 1e-3) / 1e12}
+        elif wl.bound == "fp32":
+            # CUDA-core fp32 FMA pipe: no measured figure exists for it, so the
+            # nominal rate at the maximum SM clock is the denominator.
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            peak = sms * 128 * 2 * 1965e6 / 1e12
+            achieved = wl.alg_flops() / (ms * 1e-3) / 1e12
+            roof = {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak,
+                    "peak_kind": f"nominal fp32 FFMA ({sms} SMs x 128 lanes x 2 x 1965 MHz)",
+                    "traffic": wl.traffic(), "algorithmic_flops": wl.alg_flops(),
+                    "gbs": wl.alg_bytes() / (ms * 1e-3) / 1e9}
         else:
             achieved = wl.alg_flops() / (ms * 1e-3) / 1e12
             peak = pk[wl.peak_key]

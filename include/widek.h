@@ -93,6 +93,32 @@ WIDEK_API int widek_linear_fwd_simt(const void* x, const void* w, const void* bi
  * No counterpart in the reference. */
 WIDEK_API int widek_linear_set_variant(int variant);
 
+/* A chain of wide Linear layers with activations, one launch:
+ *   h_0 = x;  h_{l+1}[i] = act_l(h_l[i] @ weights[l][i]^T + biases[l][i])
+ * for every model i in [0, n), l in [0, layers); y = h_layers.
+ *   weights[l]: [n, dims[l+1], dims[l]]; biases[l]: [n, dims[l+1]] or NULL;
+ *   dims: layers + 1 widths; acts: layers WIDEK_ACT_* codes;
+ *   x: [n, batch, dims[0]] (in_layout NFIRST) or [batch, n*dims[0]] (PACKED);
+ *   y: [n, batch, dims[layers]] (out_layout NFIRST) or [batch, n*dims[layers]].
+ * One CTA per model keeps the activations and one layer's weights in shared
+ * memory; fp32 arithmetic, each layer's output rounded to the storage dtype
+ * as a layer-by-layer run stores it. Returns WIDEK_ERR_UNSUPPORTED (launching
+ * nothing) when the chain does not fit (widek_mlp_chain_supported says in
+ * advance). Replaces, for a TracedWideModel whose graph is such a chain, the
+ * boundary unpack, the per-node WideLinear (wide_compiler/core/primitives/
+ * wide_linear.py:165-168) and activation calls, and the boundary pack
+ * (wide_compiler/core/traced_wide.py:450-532). */
+WIDEK_API int widek_mlp_chain_fwd(const void* x, void* y, const void* const* weights,
+                                  const void* const* biases, const int64_t* dims, const int* acts,
+                                  int layers, int64_t n, int64_t batch, int in_layout, int out_layout,
+                                  int dtype, void* stream);
+
+/* 1 if widek_mlp_chain_fwd would run this chain (1..8 layers, widths
+ * 1..4096, batch <= 4096, activations and one layer's weights within one
+ * SM's shared memory), else 0. Launches nothing. */
+WIDEK_API int widek_mlp_chain_supported(const int64_t* dims, const int* acts, int layers, int64_t n,
+                                        int64_t batch, int dtype);
+
 /* ---- WideLayerNorm ----------------------------------------------------- */
 
 /* Per-row LayerNorm over the last dim d with per-model affine:

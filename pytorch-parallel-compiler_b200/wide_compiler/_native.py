@@ -67,6 +67,10 @@ SIGNATURES = {
     "widek_conv_fwd": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64), _int, _int, _int, _c_void_p],
     "widek_conv_fwd_ex": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64)] + [_int] * 6 + [_c_void_p],
     "widek_conv_layouts_supported": [ctypes.POINTER(_i64)] + [_int] * 5,
+    "widek_mlp_chain_fwd": [_c_void_p, _c_void_p, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
+                            ctypes.POINTER(_i64), ctypes.POINTER(_int), _int, _i64, _i64, _int, _int, _int,
+                            _c_void_p],
+    "widek_mlp_chain_supported": [ctypes.POINTER(_i64), ctypes.POINTER(_int), _int, _i64, _i64, _int],
     "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
 }
@@ -123,6 +127,11 @@ def check(rc: int, what: str) -> None:
     raise WideKernelError(msg)
 
 
+def launch_count() -> int:
+    """Kernel launches the library has issued in this process."""
+    return int(lib().widek_launch_count())
+
+
 def device_error() -> int:
     """Synchronizes, returns and clears the device-side error word."""
     code = ctypes.c_int(0)
@@ -137,7 +146,15 @@ def dtype_code(t: torch.Tensor) -> int:
         raise TypeError(f"wide_compiler kernels support float32/bfloat16/float16, got {t.dtype}") from None
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """Handle of torch's current stream on `device` (the raw query when torch
+    has it: no Stream object is built per launch)."""
+    if _raw_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 

@@ -37,6 +37,11 @@ from .primitives import (WideAttention, WideBatchNorm1d, WideBatchNorm2d, WideCo
                          WideEmbedding, WideGroupNorm, WideGRU, WideInstanceNorm1d, WideInstanceNorm2d,
                          WideLayerNorm, WideLinear, WideLSTM)
 
+# A chain of small Linears runs as one launch (one CTA per model, CUDA-core
+# FMAs) up to this many multiply-adds for bf16/f16 (4x for fp32, whose
+# per-layer path is CUDA-core too); above it the per-layer tcgen05 GEMMs win.
+CHAIN_MAX_MACS = 1 << 25
+
 WIDE_BUILDERS: Dict[str, Callable[[List[nn.Module]], nn.Module]] = {
     'Linear': WideLinear.from_modules,
     'Conv1d': WideConv1d.from_modules,
@@ -444,8 +449,94 @@ class TracedWideModel(nn.Module):
                             tail = after
                 groups[tail] = g
                 folded.update(g['nodes'][:-1])
+        self._plan_linear_chains(groups, folded, cons, op_of)
         by_head = {g['head']: g for g in groups.values()}
         return {'groups': groups, 'folded': folded, 'consumers': cons, 'by_head': by_head}
+
+    def _plan_linear_chains(self, groups, folded, cons, op_of) -> None:
+        """Merges runs of WideLinear[+act] segments, each the only consumer
+        of the previous one's output, into 'chain' groups (one libwidek
+        launch for the whole run, boundary pack/unpack fused when the run
+        starts at the model input or ends at the model output). A chain has
+        two or more layers, or one layer that touches the model boundary."""
+        lin_groups = {g['head']: (list(g['nodes']), tail, g['act'])
+                      for tail, g in groups.items() if g['kind'] == 'linear'}
+        segs = {}          # head -> (nodes, tail, act)
+        for name in self._execution_order:
+            if name not in self.stage_info or not isinstance(op_of(name), WideLinear) \
+                    or len(self._node_args[name]) != 1 or self._node_kwargs.get(name):
+                continue
+            if name in lin_groups:
+                segs[name] = lin_groups[name]
+            elif name not in folded:
+                segs[name] = ([name], name, 0)
+        seg_by_tail = {s[1]: h for h, s in segs.items()}
+
+        def next_seg(tail):
+            c = cons.get(tail, [])
+            if len(c) == 1 and c[0] in segs and self._node_args[c[0]][0] == tail:
+                return c[0]
+            return None
+
+        for head in [h for h in self._execution_order if h in segs]:
+            src = self._node_args[head][0]
+            if src in seg_by_tail and next_seg(src) == head:
+                continue           # inside the chain that starts further up
+            layers, acts, nodes = [], [], []
+            cur = head
+            while cur is not None:
+                seg_nodes, tail, act = segs[cur]
+                layers.append(cur)
+                acts.append(act)
+                nodes.extend(seg_nodes)
+                cur = next_seg(tail)
+            tail = nodes[-1]
+            boundary = self._node_args[head][0] == self._input_name or \
+                (tail == self._output_name and cons.get(tail) == ['<output>'])
+            if len(layers) < 2 and not boundary:
+                continue
+            for t in [t for t, g in groups.items() if g['kind'] == 'linear' and g['head'] in layers]:
+                del groups[t]
+            groups[tail] = {'kind': 'chain', 'nodes': nodes, 'head': head, 'layers': layers, 'acts': acts}
+            folded.update(nodes[:-1])
+
+    def _run_chain(self, g: Dict[str, Any], xv: Any):
+        """A 'chain' group: one widek_mlp_chain_fwd launch when the chain fits
+        the kernel (and is small enough that one CTA per model beats the
+        per-layer tensor-core GEMMs), else one fused Linear+act per layer."""
+        from .. import ops
+        mods = g.get('mods')
+        if mods is None:
+            mods = g['mods'] = [self.stages[name.replace('.', '_')] for name in g['layers']]
+        ws = [m.weight for m in mods]
+        bs = [m.bias for m in mods]
+        n = mods[0].n
+        t = xv.t if isinstance(xv, _Laid) else xv
+        packed_in = isinstance(xv, _Laid) and xv.layout == ops.LAYOUT_PACKED
+        tail = g['nodes'][-1]
+        at_output = tail == self._output_name and self._fusion['consumers'].get(tail) == ['<output>']
+        if packed_in and t.dim() == 2:
+            x_in, in_l, batch_shape = t, ops.LAYOUT_PACKED, (t.shape[0],)
+        else:
+            x_in = self._std(xv)
+            batch_shape = tuple(x_in.shape[1:-1])
+            x_in, in_l = x_in.reshape(n, -1, x_in.shape[-1]), ops.LAYOUT_NFIRST
+        rows = 1
+        for s in batch_shape:
+            rows *= s
+        macs = n * rows * sum(w.shape[1] * w.shape[2] for w in ws)
+        limit = CHAIN_MAX_MACS * (4 if t.dtype == torch.float32 else 1)
+        if x_in.dtype == ws[0].dtype and macs <= limit:
+            out_l = ops.LAYOUT_PACKED if at_output and len(batch_shape) == 1 else ops.LAYOUT_NFIRST
+            y = ops.mlp_chain(x_in, ws, bs, g['acts'], n, in_layout=in_l, out_layout=out_l)
+            if y is not None:
+                if out_l == ops.LAYOUT_PACKED:
+                    return _Laid(y, out_l)
+                return y.reshape(n, *batch_shape, y.shape[-1])
+        h = self._std(xv)
+        for w, b, act in zip(ws, bs, g['acts']):
+            h = ops.linear(h, w, b, act=act)
+        return h
 
     def _group_ready(self, g: Dict[str, Any], values: Dict[str, Any]) -> bool:
         """Whether a fused group can run now (eval-mode BatchNorm with
@@ -454,7 +545,7 @@ class TracedWideModel(nn.Module):
         t = x.t if isinstance(x, _Laid) else x
         if not isinstance(t, Tensor) or not t.is_cuda:
             return False
-        if g['kind'] == 'linear':
+        if g['kind'] in ('linear', 'chain'):
             return True
         bn_mod = self.stages[g['bn'].replace('.', '_')].op
         if bn_mod.training or bn_mod.running_mean is None or bn_mod.running_var is None:
@@ -499,6 +590,8 @@ class TracedWideModel(nn.Module):
         xv = values.get(self._node_args[head][0])
         if g['kind'] == 'linear':
             return ops.linear(self._std(xv), op.weight, op.bias, act=g['act'])
+        if g['kind'] == 'chain':
+            return self._run_chain(g, xv)
         bn_mod = self.stages[g['bn'].replace('.', '_')].op
         scale, shift = _bn_fold(bn_mod)
         w, b, st, pd, dl = self._conv_params(op)

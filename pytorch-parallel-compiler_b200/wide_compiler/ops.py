@@ -69,6 +69,67 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
     return y
 
 
+_CHAIN_MEMO: dict = {}
+
+
+def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Tensor]], acts: Sequence[int],
+              n: int, in_layout: int = 0, out_layout: int = 0) -> Optional[Tensor]:
+    """A chain of wide Linears with activations in one launch:
+    h = act_l(h @ weights[l][i]^T + biases[l][i]) per model i.
+
+    weights[l]: [N, D_{l+1}, D_l]; x: [N, B, D_0] (in_layout 0, N-first) or
+    [B, N*D_0] (in_layout 1, packed); the result is [N, B, D_L] or
+    [B, N*D_L] per out_layout. Returns None, launching nothing, when the
+    chain does not fit the one-CTA-per-model kernel. The argument arrays and
+    the fit query are memoised per (pointers, shapes, layouts, dtype)."""
+    layers = len(weights)
+    if not 1 <= layers <= 8 or len(biases) != layers or len(acts) != layers:
+        return None
+    wd = [w if w.is_contiguous() else w.contiguous() for w in weights]
+    bd = [b if b is None or b.is_contiguous() else b.contiguous() for b in biases]
+    batch = x.shape[0] if in_layout == 1 else (x.shape[1] if x.dim() == 3 else -1)
+    key = (tuple(w.data_ptr() for w in wd), tuple(0 if b is None else b.data_ptr() for b in bd),
+           tuple(tuple(w.shape) for w in wd), tuple(acts), n, batch, tuple(x.shape), in_layout, out_layout,
+           x.dtype, x.device)
+    plan = _CHAIN_MEMO.get(key)
+    if plan is None:
+        dev = N.require_cuda(x, *weights, *biases, what="WideLinear chain")
+        _same_dtype("WideLinear chain", weights[0], x, *weights, *biases)
+        dims = [weights[0].shape[2]] + [w.shape[1] for w in weights]
+        for l, w in enumerate(weights):
+            if w.dim() != 3 or w.shape[0] != n or w.shape[2] != dims[l]:
+                raise ValueError(f"WideLinear chain: weight {l} {tuple(w.shape)} does not follow width {dims[l]}")
+            b = biases[l]
+            if b is not None and tuple(b.shape) != (n, dims[l + 1]):
+                raise ValueError(f"WideLinear chain: bias {l} {tuple(b.shape)} is not [{n}, {dims[l + 1]}]")
+        if in_layout == 1:
+            if x.dim() != 2 or x.shape[1] != n * dims[0]:
+                raise ValueError(f"WideLinear chain: packed input {tuple(x.shape)} is not [B, {n}*{dims[0]}]")
+        elif x.dim() != 3 or x.shape[0] != n or x.shape[2] != dims[0]:
+            raise ValueError(f"WideLinear chain: input {tuple(x.shape)} is not [{n}, B, {dims[0]}]")
+        c_dims = (ctypes.c_int64 * (layers + 1))(*dims)
+        c_acts = (ctypes.c_int * layers)(*acts)
+        code = N.dtype_code(x)
+        ok = bool(N.lib().widek_mlp_chain_supported(c_dims, c_acts, layers, n, batch, code))
+        c_w = (ctypes.c_void_p * layers)(*[w.data_ptr() for w in wd])
+        c_b = (ctypes.c_void_p * layers)(*[N.ptr(b) for b in bd])
+        out_shape = (batch, n * dims[-1]) if out_layout == 1 else (n, batch, dims[-1])
+        plan = (ok, c_dims, c_acts, c_w, c_b, code, out_shape, dev)
+        if len(_CHAIN_MEMO) > 256:
+            _CHAIN_MEMO.clear()
+        _CHAIN_MEMO[key] = plan
+    ok, c_dims, c_acts, c_w, c_b, code, out_shape, dev = plan
+    if not ok:
+        return None
+    xd = x if x.is_contiguous() else x.contiguous()
+    y = torch.empty(out_shape, device=dev, dtype=x.dtype)
+    with _guard(dev):
+        rc = N.lib().widek_mlp_chain_fwd(xd.data_ptr(), y.data_ptr(), c_w, c_b, c_dims, c_acts, layers, n, batch,
+                                         in_layout, out_layout, code, N.stream_ptr(dev))
+    N.check(rc, "widek_mlp_chain_fwd")
+    return y
+
+
 # ---------------------------------------------------------------------------
 # WideLayerNorm
 # ---------------------------------------------------------------------------

@@ -71,3 +71,24 @@ def test_binding_argument_counts_match_header():
     counts = _header_param_counts()
     for name, argtypes in _native.SIGNATURES.items():
         assert len(argtypes) == counts[name], f"{name}: binding has {len(argtypes)} args, header {counts[name]}"
+
+
+def test_mlp_chain_argument_checks():
+    """widek_mlp_chain_fwd / _supported reject bad chains before any CUDA
+    call; the size query answers on the host."""
+    from wide_compiler import _native as N
+    lib = N.load()
+    I64, INT = ctypes.c_int64, ctypes.c_int
+    dims = (I64 * 3)(64, 128, 64)
+    acts = (INT * 2)(1, 0)
+    assert lib.widek_mlp_chain_fwd(None, None, None, None, dims, acts, 0, 1, 1, 0, 0, N.F32, None) == N.WIDEK_ERR_INVALID
+    assert lib.widek_mlp_chain_fwd(None, None, None, None, dims, acts, 2, 1, 1, 3, 0, N.F32, None) == N.WIDEK_ERR_INVALID
+    bad = (INT * 2)(1, 7)
+    assert lib.widek_mlp_chain_fwd(None, None, None, None, dims, bad, 2, 1, 1, 0, 0, N.F32, None) == N.WIDEK_ERR_INVALID
+    assert lib.widek_mlp_chain_supported(dims, bad, 2, 1, 1, N.F32) == 0
+    assert "activation" in N.last_error()
+    assert lib.widek_mlp_chain_supported(dims, acts, 2, 100, 32, N.F32) == 1
+    wide = (I64 * 2)(512, 512)          # 1 MB of fp32 weights: does not fit on chip
+    assert lib.widek_mlp_chain_supported(wide, acts, 1, 1, 4, N.F32) == 0
+    zero = (I64 * 2)(0, 8)
+    assert lib.widek_mlp_chain_supported(zero, acts, 1, 1, 4, N.F32) == 0

@@ -197,7 +197,11 @@ class _ResBlockT(nn.Module):
 def test_fusion_plan_structure():
     mlp = wc.TracedWideModel.from_models([_MLP() for _ in range(3)], torch.randn(2, 8))
     plan = mlp._build_fusion_plan()
-    assert list(plan['groups']) == ['relu'] and plan['groups']['relu']['kind'] == 'linear'
+    # Linear -> ReLU -> Linear is one chain group (one launch, packed in/out)
+    g = plan['groups']
+    assert list(g) == ['fc2'] and g['fc2']['kind'] == 'chain'
+    assert g['fc2']['layers'] == ['fc1', 'fc2'] and g['fc2']['acts'] == [1, 0]
+    assert plan['folded'] == {'fc1', 'relu'}
     rb = wc.TracedWideModel.from_models([_ResBlockT() for _ in range(2)], torch.randn(1, 4, 6, 6))
     plan = rb._build_fusion_plan()
     kinds = {k: (g['kind'], g['act'], g['residual']) for k, g in plan['groups'].items()}
