@@ -240,6 +240,7 @@ __device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -512,6 +513,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // crosses into the next model or output tile.
 // ---------------------------------------------------------------------------
 constexpr int kHaloMaxStages = 8;
+constexpr int kHaloEpiWarps = 4;
+constexpr int kHaloThreads = 224;   // TMA warp, MMA warp, 4 epilogue warps, second MMA warp
 constexpr int HBN = 64;
 
 struct ConvHaloGeom {
@@ -524,16 +527,19 @@ struct ConvHaloGeom {
     int64_t tiles;
 };
 
-// Output tile buffers: one without a residual; with a TMA-loaded residual,
-// two buffers that each receive a residual tile (requested by the producer
-// warp two tiles ahead), are updated in place by the epilogue (same
-// [channel][pixel] index) and are stored from.
+// Two output tile buffers, used by alternate tiles, so that a tile's
+// epilogue only waits for the store issued two tiles earlier. With a
+// TMA-loaded residual each buffer first receives the tile's residual
+// (requested by the epilogue's elected thread one tile ahead, once the
+// buffer's previous store has read it out), which the epilogue updates in
+// place (same [channel][pixel] index) before the store.
 template <bool RES_TMA>
 struct HaloSmem {
     static constexpr uint32_t TILE = HBN * BM * 2;
-    static constexpr uint32_t BUFS = RES_TMA ? 2 : 1;
-    static constexpr uint32_t BARS = 8 * (2 * kHaloMaxStages + 11) + 16;
-    static uint32_t fixed(uint32_t w_bytes) { return 1024 + w_bytes + BUFS * TILE + BARS; }
+    static constexpr uint32_t BUFS = 2;
+    static constexpr uint32_t BARS = 8 * (2 * kHaloMaxStages + 12) + 16;
+    static constexpr uint32_t PARAMS = HBN * 8;      // per-channel (scale, offset) of the current output tile
+    static uint32_t fixed(uint32_t w_bytes) { return 1024 + w_bytes + BUFS * TILE + BARS + PARAMS; }
 };
 
 // Issues the MMAs of one input subtile (column offset kx, channel block cb):
@@ -560,7 +566,7 @@ __device__ __forceinline__ void halo_issue_subtile(uint32_t d_tmem, uint64_t a_d
 }
 
 template <typename T, bool RES_TMA, int KH, int KW, bool OUT_CL>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
                      ConvHaloGeom g, ConvEpi e, int* err) {
@@ -578,11 +584,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* w_empty = w_full + 1;
     uint64_t* tfull = w_empty + 1;        // [2]
     uint64_t* tempty = tfull + 2;         // [2]
-    uint64_t* done = tempty + 2;
-    uint64_t* res_full = done + 1;        // [2]
-    uint64_t* res_empty = res_full + 2;   // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_empty + 2);
+    uint64_t* done = tempty + 2;          // [2], one per MMA issuer
+    uint64_t* res_full = done + 2;        // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float2* sPar = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(full) + S::BARS);   // [HBN]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt_count = g.tiles_h * g.tiles_w;
@@ -594,14 +600,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(w_full, 1);
-        mbar_init(w_empty, 1);
+        mbar_init(w_empty, 2);            // both MMA issuers release the weights
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4 * 32);
+            mbar_init(&tempty[a], kHaloEpiWarps * 32);
             mbar_init(&res_full[a], 1);
-            mbar_init(&res_empty[a], 1);
         }
-        mbar_init(done, 1);
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -628,12 +634,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     if (warp == 0) {
-        // TMA producer: weights when the (model, output tile) changes; per
-        // tile its residual (two tiles ahead of the epilogue's use), then per
-        // input-channel block and column offset kx one subtile per stage.
+        // TMA producer: weights when the (model, output tile) changes, then
+        // per input-channel block and column offset kx one subtile per stage
+        // (the residual tiles are requested by the epilogue).
         const uint64_t pol_x = l2_policy_evict_normal();
         const uint64_t pol_w = l2_policy_evict_last();
-        int s = 0, issued = 0, wl = 0, local = 0, res_issued = 0;
+        int s = 0, issued = 0, wl = 0, local = 0;
         uint32_t ph = 0;
         int64_t cur = -1;
         bool ok = true;
@@ -656,26 +662,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ho0 = (mt / g.tiles_w) * g.th;
             const int wo0 = (mt % g.tiles_w) * g.tw;
             const int img = model * g.batch + b;
-            if (RES_TMA) {
-                // Buffer local % 2 held tile local-2's output: its store has
-                // been read out (the epilogue releases it).
-                const int rb = local & 1;
-                if (local >= 2 && !mbar_wait(&res_empty[rb], (uint32_t)(((local - 2) >> 1) & 1), abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&res_full[rb], S::TILE);
-                    if (g.res5)
-                        tma_load_5d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, b, model,
-                                    l2_policy_evict_first());
-                    else
-                        tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, img,
-                                    l2_policy_evict_first());
-                }
-                __syncwarp();
-                ++res_issued;
-            }
             for (int cb = 0; cb < g.cblocks && ok; ++cb) {
                 for (int kx = 0; kx < g.kw; ++kx) {
                     if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
@@ -703,26 +689,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int idx = issued - j;
                 mbar_wait(&full[idx % stages], (uint32_t)((idx / stages) & 1), &never);
             }
-            for (int j = 1; j <= 2; ++j) {
-                const int idx = res_issued - j;
-                if (idx >= 0) mbar_wait(&res_full[idx & 1], (uint32_t)((idx >> 1) & 1), &never);
-            }
         }
-    } else if (warp == 1) {
-        // MMA issuer: one thread waits, fences and issues (no warp-wide
-        // polling or __syncwarp between MMA groups, which measured ~35 %
-        // slower issue); the other lanes wait at the end.
+    } else if (warp == 1 || warp == kHaloThreads / 32 - 1) {
+        // Two MMA issuers (one thread each, in warps 1 and 6): issuer i takes
+        // the CTA's tiles with local index = i (mod 2) into accumulator i, so
+        // one tile's MMAs go out while the other's are still being issued:
+        // a single thread sustains ~60 cycles per M128-N64-K16 MMA, two reach
+        // the ~48-cycle shared-memory operand bound. Both walk every tile to
+        // keep the subtile ring position and to release the weights (w_empty
+        // counts both) whenever the (model, output tile) changes.
+        const int me = warp == 1 ? 0 : 1;
         if (lane == 0) {
-            int s = 0, local = 0, wl = 0;
-            uint32_t ph = 0;
+            int wl = 0;
             int64_t cur = -1;
+            uint32_t ring = 0;            // subtiles of all earlier tiles
             bool ok = true;
             const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
             const uint64_t w_desc0 = sdesc_kmajor_sw128(smem_addr(sW));
             // ky*dh input rows further down in a subtile; one kernel row further in the weights
             const uint32_t row_step16 = (uint32_t)(g.dh * g.tw * 128) >> 4;
             const uint32_t tap_stride16 = (uint32_t)((KW > 0 ? KW : g.kw) * g.cblocks * HBN * 128) >> 4;
-            for (int64_t tile = t_begin; tile < t_end && ok; ++tile, ++local) {
+            const int kw = KW > 0 ? KW : g.kw;
+            const uint32_t per_tile = (uint32_t)(g.cblocks * kw);
+            int local = 0;
+            for (int64_t tile = t_begin; tile < t_end && ok; ++tile, ++local, ring += per_tile) {
                 int model, nt, b, mt;
                 decode(tile, model, nt, b, mt);
                 const int64_t key = (int64_t)model * g.nt_count + nt;
@@ -732,66 +722,102 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++wl;
                     cur = key;
                 }
-                const int acc = local & 1;
+                if ((local & 1) != me) continue;
                 const uint32_t aph = (local >> 1) & 1;
-                if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(&tempty[me], aph ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * HBN;
-                const int kw = KW > 0 ? KW : g.kw;
+                const uint32_t d_tmem = tmem_base + me * HBN;
+                uint32_t c = ring;
                 for (int cb = 0; cb < g.cblocks && ok; ++cb) {
-                    for (int kx = 0; kx < kw; ++kx) {
-                        if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    for (int kx = 0; kx < kw; ++kx, ++c) {
+                        const uint32_t s = c % (uint32_t)g.stages;
+                        if (!mbar_wait(&full[s], (c / (uint32_t)g.stages) & 1, abort_flag)) { ok = false; break; }
                         tc_fence_after();
                         const uint64_t a_desc = a_desc0 + (uint64_t)((s * g.sub_bytes) >> 4);
                         const uint64_t w_desc = w_desc0 + (uint64_t)(((kx * g.cblocks + cb) * (HBN * 128)) >> 4);
                         halo_issue_subtile<KH>(d_tmem, a_desc, w_desc, row_step16, tap_stride16, IDESC,
                                                (cb | kx) == 0, g.kh);
                         umma_commit(&empty[s]);
-                        if (++s == g.stages) { s = 0; ph ^= 1; }
                     }
                 }
                 if (!ok) break;
-                umma_commit(&tfull[acc]);
+                umma_commit(&tfull[me]);
             }
             if (!ok) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
             }
             // Every MMA issued by this thread completes before TMEM is freed.
-            umma_commit(done);
+            umma_commit(&done[me]);
             const volatile int never = 0;
-            mbar_wait(done, 0, &never);
+            mbar_wait(&done[me], 0, &never);
         }
         __syncwarp();
     } else {
         // Epilogue (as conv_tc_kernel with a TMA store): warps 2..5, TMEM lane
-        // quarter q = warp % 4; per 32-channel chunk the per-channel
-        // parameters arrive by shuffles. With a residual, tile i's residual
-        // is in buffer i % 2; the output overwrites it in place and is stored
-        // from there.
+        // quarter q = warp % 4. Bias and the folded BatchNorm become one
+        // (scale, offset) pair per channel, staged in shared memory when the
+        // (model, output tile) changes and read as a broadcast per value.
+        // Tile i uses buffer i % 2; with a residual that buffer holds the
+        // tile's residual, which the output overwrites in place.
         const int q = warp & 3;
         const int ep_tid = threadIdx.x - 64;
         const T* bias = static_cast<const T*>(e.bias);
         const T* scale = static_cast<const T*>(e.scale);
         const T* shift = static_cast<const T*>(e.shift);
         const bool res = RES_TMA && e.residual != nullptr;
+        int64_t par_key = -1;
+        int res_issued = 0;
+        // Residual tile of `tile` into buffer `rb` (elected thread only).
+        auto load_residual = [&](int64_t tile, int rb) {
+            int model, nt, b, mt;
+            decode(tile, model, nt, b, mt);
+            const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
+            mbar_arrive_expect_tx(&res_full[rb], S::TILE);
+            if (g.res5)
+                tma_load_5d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, b, model,
+                            l2_policy_evict_first());
+            else
+                tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN,
+                            model * g.batch + b, l2_policy_evict_first());
+            ++res_issued;
+        };
+        if (RES_TMA && ep_tid == 0 && t_begin < t_end) load_residual(t_begin, 0);
         int local = 0;
         for (int64_t tile = t_begin; tile < t_end; ++tile, ++local) {
             int model, nt, b, mt;
             decode(tile, model, nt, b, mt);
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
-            const int buf = RES_TMA ? (local & 1) : 0;
+            const int buf = local & 1;
             T* sOut = sBuf + buf * (HBN * BM);
             const int r = q * 32 + lane;
             const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
             const int64_t img = (int64_t)model * g.batch + b;
-            // The previous tile's store has read its buffer out: release that
-            // buffer to the producer (it takes the residual two tiles on) or,
-            // without a residual, reuse the single buffer.
+            // Without a residual: the store issued two tiles ago (from this
+            // tile's buffer) has read it out.
             if (ep_tid == 0) {
-                bulk_wait_read0();
-                if (RES_TMA && local >= 1) mbar_arrive(&res_empty[buf ^ 1]);
+                if (RES_TMA) {
+                    // The previous tile's store has read buffer buf ^ 1 out:
+                    // the next tile's residual goes there, a whole tile
+                    // ahead of its use.
+                    bulk_wait_read0();
+                    if (tile + 1 < t_end) load_residual(tile + 1, buf ^ 1);
+                } else {
+                    bulk_wait_read1();
+                }
+            }
+            const int64_t key = (int64_t)model * g.nt_count + nt;
+            if (key != par_key) {
+                // every read of the previous pairs finished before the last tile's second barrier
+                if (ep_tid < HBN) {
+                    const int64_t ch = (int64_t)model * g.cout + nt * HBN + ep_tid;
+                    const float pb = bias ? to_f<T>(bias[ch]) : 0.f;
+                    const float ps = scale ? to_f<T>(scale[ch]) : 1.f;
+                    const float pt = shift ? to_f<T>(shift[ch]) : 0.f;
+                    sPar[ep_tid] = make_float2(ps, pb * ps + pt);
+                }
+                par_key = key;
             }
             epi_bar_sync();
             if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
@@ -807,13 +833,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll 1
             for (int c = 0; c < HBN; c += 32) {
-                const int co0 = nt * HBN + c;
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * HBN + c) + ((uint32_t)(q * 32) << 16), v);
-                const int64_t my_ch = (int64_t)model * g.cout + co0 + lane;
-                const float pb = bias ? to_f<T>(bias[my_ch]) : 0.f;
-                const float ps = scale ? to_f<T>(scale[my_ch]) : 1.f;
-                const float pt = shift ? to_f<T>(shift[my_ch]) : 0.f;
                 // The chunk's 32 residual values are read before any of its
                 // outputs is written over them.
                 float rv[32];
@@ -825,9 +846,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float ov[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    float val = (__uint_as_float(v[j]) + __shfl_sync(0xffffffffu, pb, j)) *
-                                    __shfl_sync(0xffffffffu, ps, j) +
-                                __shfl_sync(0xffffffffu, pt, j);
+                    const float2 par = sPar[c + j];
+                    float val = fmaf(__uint_as_float(v[j]), par.x, par.y);
                     if (res && e.residual_first) val += rv[j];
                     val = apply_act(val, e.act);
                     if (res && !e.residual_first) val += rv[j];
@@ -860,7 +880,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bulk_commit();
             }
         }
-        if (ep_tid == 0) bulk_wait0();
+        if (ep_tid == 0) {
+            bulk_wait0();
+            if (RES_TMA && *abort_flag) {
+                // residual copies in flight land before the CTA's shared memory is released
+                const volatile int never = 0;
+                for (int j = 1; j <= 2; ++j) {
+                    const int idx = res_issued - j;
+                    if (idx >= 0) mbar_wait(&res_full[idx & 1], (uint32_t)((idx >> 1) & 1), &never);
+                }
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -1048,7 +1078,7 @@ int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, Con
         attr_bytes[d][spec] = smem;
     }
     const int grid = (int)std::min<int64_t>(g.tiles, sm_count(dev));
-    kern<<<grid, kThreads, smem, st>>>(tx, tw_map, ty_map, tr_map, g, e, device_error_ptr());
+    kern<<<grid, kHaloThreads, smem, st>>>(tx, tw_map, ty_map, tr_map, g, e, device_error_ptr());
     return check_launch("widek_conv_fwd (tcgen05 halo)");
 }
 

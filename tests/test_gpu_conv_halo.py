@@ -71,8 +71,8 @@ def test_conv_halo_fused_epilogue(residual_first):
     sc = (torch.rand(n * c, generator=gen) + 0.5).to(torch.bfloat16)
     sh = (torch.randn(n * c, generator=gen) * 0.1).to(torch.bfloat16)
     res = torch.randn(n, b, c, hw, hw, generator=gen).to(torch.bfloat16)
-    y = _run(0, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), scale=sc.to(DEV), shift=sh.to(DEV),
-             residual=res.to(DEV), act=ops.ACT_RELU, residual_first=residual_first)
+    y = _run(0, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), scale=sc.to(DEV),
+             shift=sh.to(DEV), residual=res.to(DEV), act=ops.ACT_RELU, residual_first=residual_first)
     v = O.conv_nd(x, w, bb, n, (1, 1), (1, 1), (1, 1)) * sc.double().view(n, 1, c, 1, 1) + \
         sh.double().view(n, 1, c, 1, 1)
     if residual_first:
@@ -96,4 +96,22 @@ def test_conv_halo_many_models_weight_reloads():
     for m in (0, n - 1):
         ref = O.conv_nd(x[m:m + 1], w[m * c:(m + 1) * c], bb[m * c:(m + 1) * c], 1, (1, 1), (1, 1), (1, 1))
         assert_lowp_close(y0[m:m + 1], ref)
+    no_device_error()
+
+
+@pytest.mark.parametrize("ow", [8, 16, 24, 40])
+def test_conv_halo_packed_residual_edges(ow):
+    """The halo kernel's TMA-stored packed output and TMA-loaded packed
+    residual at ragged tile edges (rows past the image, a half-used
+    16-pixel tile width)."""
+    n, b, c, oh = 3, 2, 64, 19
+    x, w, bb = _case(n, b, c, c, (oh, ow), 3, seed=ow)
+    gen = torch.Generator().manual_seed(ow + 1)
+    res = torch.randn(n, b, c, oh, ow, generator=gen).to(torch.bfloat16)
+    pk = lambda t: t.transpose(0, 1).reshape(b, n * c, oh, ow).contiguous()
+    y = _run(0, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), residual=pk(res).to(DEV),
+             out_layout=ops.LAYOUT_PACKED, res_layout=ops.LAYOUT_PACKED)
+    assert y is not None and y.shape == (b, n * c, oh, ow)
+    ref = O.conv_nd(x, w, bb, n, (1, 1), (1, 1), (1, 1)) + res.double()
+    assert_lowp_close(y.reshape(b, n, c, oh, ow).transpose(0, 1), ref)
     no_device_error()
