@@ -22,8 +22,10 @@ class WideConfig:
     """Configuration for building a wide model.
 
     n: number of fused models (None: taken from the model list).
-    compile / compile_mode / compile_backend / compile_options: wrap the
-        result in torch.compile with these settings.
+    compile: wrap the result in the CUDA-graph executor
+        (``core.graphed.GraphedWideModel``); compile_mode / compile_backend /
+        compile_options are validated and recorded (every mode gets the
+        same executor; no torch.compile).
     precision, allow_tf32: recorded for compatibility (the kernels compute in
         fp32 whatever the storage dtype).
     validate / validate_rtol / validate_atol: compare the wide model against

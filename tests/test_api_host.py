@@ -210,3 +210,21 @@ def test_fusion_plan_structure():
     rb2 = wc.TracedWideModel.from_models([_ResBlockT(post_relu=True) for _ in range(2)], torch.randn(1, 4, 6, 6))
     g = rb2._build_fusion_plan()['groups']
     assert g['relu_1']['residual'] == 'x' and g['relu_1']['residual_first'] and g['relu_1']['act'] == 1
+
+
+def test_compile_flag_gives_graph_executor():
+    """compile=True (the reference's torch.compile switch, api.py:137-147)
+    returns the CUDA-graph executor, which forwards attribute access to the
+    TracedWideModel and keeps its parameters under '_orig_mod.' as
+    torch.compile's wrapper does; CPU inputs take the eager path and fail
+    loudly in the kernels."""
+    from wide_compiler.core.graphed import GraphedWideModel
+    models = [_MLP() for _ in range(3)]
+    g = wc.compile(models, torch.randn(2, 8), compile_model=True)
+    assert isinstance(g, GraphedWideModel)
+    assert g.n == 3 and 'fc1' in g.stages
+    assert all(k.startswith('_orig_mod.') for k in g.state_dict())
+    b = wc.WideBuilder(models).with_sample(torch.randn(2, 8)).compile().build()
+    assert isinstance(b, GraphedWideModel)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        g(torch.randn(2, 24))
