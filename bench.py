@@ -789,7 +789,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    return run_b200(args)
+    # An inference benchmark: autograd is off, so the fused kernels and the
+    # CUDA-graph executor serve every forward (as they do under no_grad for a user).
+    with torch.no_grad():
+        return run_b200(args)
 
 
 if __name__ == "__main__":

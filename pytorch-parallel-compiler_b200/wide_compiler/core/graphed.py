@@ -23,7 +23,10 @@ one CUDA graph per input signature and replays it:
   overwrites; ``clone()`` it to keep it.
 * Inputs larger than ``max_input_bytes`` (default 32 MiB) run eagerly:
   at that size the kernels, not the launches, set the time. CPU inputs also
-  run eagerly (and fail loudly in the kernels, as the eager model does).
+  run eagerly (and fail loudly in the kernels, as the eager model does), and
+  so do calls whose result autograd needs (grad mode on and a parameter or
+  the input requiring grad): replays are for inference (``torch.no_grad()``
+  / ``torch.inference_mode()``).
 """
 from __future__ import annotations
 
@@ -93,6 +96,8 @@ class GraphedWideModel(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         if not isinstance(x, Tensor) or not x.is_cuda or x.numel() * x.element_size() > self.max_input_bytes:
             return self._orig_mod(x)
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            return self._orig_mod(x)           # autograd wants the result: no graph replay
         key = self._signature(x)
         rec = self._graphs.get(key)
         if rec is None or not rec.current():

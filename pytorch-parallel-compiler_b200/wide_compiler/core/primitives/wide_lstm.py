@@ -78,7 +78,13 @@ class WideLSTM(nn.Module):
                 self.bias_hh.zero_()
 
     def _blocks(self) -> Tuple[Tensor, Tensor]:
-        """Diagonal blocks [N, 4H, I] and [N, 4H, H], cached on parameter versions."""
+        """Diagonal blocks [N, 4H, I] and [N, 4H, H], cached on parameter
+        versions (built afresh, differentiably, when autograd needs them)."""
+        if torch.is_grad_enabled() and (self.weight_ih.requires_grad or self.weight_hh.requires_grad):
+            n, h, i = self.n, self.hidden_size, self.input_size
+            idx = torch.arange(n, device=self.weight_ih.device)
+            return (self.weight_ih.view(n, 4 * h, n, i)[idx, :, idx, :],
+                    self.weight_hh.view(n, 4 * h, n, h)[idx, :, idx, :])
         key = (self.weight_ih._version, self.weight_hh._version, self.weight_ih.data_ptr(),
                self.weight_hh.data_ptr(), self.weight_ih.dtype, self.weight_ih.device)
         if self._block_cache is None or self._block_cache[0] != key:

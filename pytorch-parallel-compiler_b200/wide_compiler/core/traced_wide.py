@@ -664,11 +664,11 @@ class TracedWideModel(nn.Module):
         return bool(N.lib().widek_conv_layouts_supported(geom, N.dtype_code(t), ops.LAYOUT_CLAST,
                                                          ops.LAYOUT_NFIRST, ops.LAYOUT_NFIRST, has_res))
 
-    def _run_stages(self, x: Tensor) -> Any:
+    def _run_stages(self, x: Tensor, fused: bool = True) -> Any:
         if self._fusion is None:
             self._fusion = self._build_fusion_plan() if self.fuse else {'groups': {}, 'folded': set(),
                                                                         'consumers': {}, 'by_head': {}}
-        groups, folded = self._fusion['groups'], self._fusion['folded']
+        groups, folded = (self._fusion['groups'], self._fusion['folded']) if fused else ({}, set())
         values: Dict[str, Any] = {self._input_name: x}
         for name in self._attr_names:
             buf = f"_attr_{name.replace('.', '_')}"
@@ -711,8 +711,21 @@ class TracedWideModel(nn.Module):
                   for k, v in self._node_kwargs.get(name, {}).items()}
         return op(*args, **kwargs)
 
+    def _needs_grad(self, x: Tensor) -> bool:
+        """Autograd wants this call's result: the fused group kernels have no
+        gradient formulation, so such a call runs node by node, each wide op
+        differentiable on its own."""
+        if not torch.is_grad_enabled():
+            return False
+        return x.requires_grad or any(p.requires_grad for p in self.parameters())
+
     def forward(self, x: Tensor) -> Tensor:
         from ..ops import LAYOUT_PACKED
+        if self._needs_grad(x):
+            out = self._run_stages(self._unpack(x), fused=False)
+            if isinstance(out, tuple):
+                out = out[0]
+            return self._pack(self._std(out))
         if self.fuse and x.is_cuda:
             b, nc = x.shape[0], x.shape[1]
             if nc % self.n != 0:

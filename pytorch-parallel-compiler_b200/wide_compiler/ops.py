@@ -15,6 +15,7 @@ import ctypes
 import torch
 from torch import Tensor
 
+from . import _autograd as _AG
 from . import _native as N
 
 ACT_NONE, ACT_RELU, ACT_GELU = N.ACT_NONE, N.ACT_RELU, N.ACT_GELU
@@ -50,6 +51,8 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
     x: [N, ..., K] (any batch dims), weight: [N, O, K], bias: [N, O] or None.
     Returns [N, ..., O].
     """
+    if _AG.needs_grad(x, weight, bias):
+        return _AG.run(linear, _AG.linear_t, x, weight, bias, act, force_simt)
     dev = N.require_cuda(x, weight, bias, what="WideLinear")
     _same_dtype("WideLinear", weight, x, bias)
     n, o, k = weight.shape
@@ -72,6 +75,15 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
 _CHAIN_MEMO: dict = {}
 
 
+def _mlp_chain_t(x, weights, biases, acts, n, in_layout=0, out_layout=0):
+    """Torch formulation of mlp_chain (gradients): per-layer WideLinear and
+    activation, with the packed boundary layout when asked."""
+    h = x.reshape(x.shape[0], n, -1).transpose(0, 1) if in_layout == 1 else x
+    for w, b, a in zip(weights, biases, acts):
+        h = _AG.linear_t(h, w, b, a)
+    return h.transpose(0, 1).reshape(h.shape[1], -1) if out_layout == 1 else h
+
+
 def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Tensor]], acts: Sequence[int],
               n: int, in_layout: int = 0, out_layout: int = 0) -> Optional[Tensor]:
     """A chain of wide Linears with activations in one launch:
@@ -82,6 +94,9 @@ def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Te
     [B, N*D_L] per out_layout. Returns None, launching nothing, when the
     chain does not fit the one-CTA-per-model kernel. The argument arrays and
     the fit query are memoised per (pointers, shapes, layouts, dtype)."""
+    if _AG.needs_grad(x, weights, biases):
+        return _AG.run(mlp_chain, _mlp_chain_t, x, list(weights), list(biases), list(acts), n, in_layout,
+                       out_layout)
     layers = len(weights)
     if not 1 <= layers <= 8 or len(biases) != layers or len(acts) != layers:
         return None
@@ -136,6 +151,8 @@ def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Te
 
 def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: float) -> Tensor:
     """LayerNorm over the last dim with per-model affine (weight/bias flat [n*d])."""
+    if _AG.needs_grad(x, weight, bias):
+        return _AG.run(layernorm, _AG.layernorm_t, x, weight, bias, n, d, eps)
     dev = N.require_cuda(x, weight, bias, what="WideLayerNorm")
     _same_dtype("WideLayerNorm", x, weight, bias)
     if x.shape[0] != n or x.shape[-1] != d:
@@ -157,6 +174,8 @@ def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: floa
 
 def swap01(x: Tensor) -> Tensor:
     """[A, B, *rest] -> [B, A, *rest] as one dense copy (rows of prod(rest))."""
+    if _AG.needs_grad(x):
+        return _AG.run(swap01, _AG.swap01_t, x)
     dev = N.require_cuda(x, what="swap01")
     xd = _dense(x)
     a, b = xd.shape[0], xd.shape[1]
@@ -171,6 +190,8 @@ def swap01(x: Tensor) -> Tensor:
 
 def pack(inputs: Sequence[Tensor]) -> Tensor:
     """Stacks N tensors [B, *F] into [B, N, *F] (one kernel, N source pointers)."""
+    if _AG.needs_grad(list(inputs)):
+        return _AG.run(pack, _AG.pack_t, list(inputs))
     dev = N.require_cuda(*inputs, what="pack")
     t0 = inputs[0]
     for t in inputs[1:]:
@@ -193,6 +214,8 @@ def pack(inputs: Sequence[Tensor]) -> Tensor:
 # ---------------------------------------------------------------------------
 
 def unary(x: Tensor, op: str) -> Tensor:
+    if _AG.needs_grad(x):
+        return _AG.run(unary, _AG.unary_t, x, op)
     dev = N.require_cuda(x, what=f"unary {op}")
     xd = _dense(x)
     y = torch.empty_like(xd)
@@ -204,6 +227,8 @@ def unary(x: Tensor, op: str) -> Tensor:
 
 
 def binary(a: Tensor, b: Tensor, op: str) -> Tensor:
+    if _AG.needs_grad(a, b):
+        return _AG.run(binary, _AG.binary_t, a, b, op)
     dev = N.require_cuda(a, b, what=f"binary {op}")
     _same_dtype(f"binary {op}", a, b)
     if a.shape != b.shape:
@@ -233,6 +258,9 @@ def batchnorm(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias: Optiona
     """Per-(model, channel) batch normalization on [N, B, C, *S]; weight, bias
     and running stats flat [N*C]. With use_batch_stats the running stats (if
     update_running) are updated in place."""
+    if _AG.needs_grad(x, weight, bias):
+        return _AG.run(batchnorm, _AG.batchnorm_t, x, n, c, weight, bias, running_mean, running_var,
+                       use_batch_stats, update_running, momentum, eps)
     dev = N.require_cuda(x, weight, bias, running_mean, running_var, what="WideBatchNorm")
     _same_dtype("WideBatchNorm", x, weight, bias, running_mean, running_var)
     batch, l = _nbcl(x, n, c, "WideBatchNorm")
@@ -263,6 +291,8 @@ def groupnorm(x: Tensor, n: int, groups: int, weight: Optional[Tensor], bias: Op
               row_stats: bool = False):
     """GroupNorm on [N, B, C, *S] with statistics per (model, sample, group).
     With row_stats also returns fp32 (mean, biased var) of shape [N, B, groups]."""
+    if _AG.needs_grad(x, weight, bias):
+        return _AG.run(groupnorm, _AG.groupnorm_t, x, n, groups, weight, bias, eps, row_stats)
     dev = N.require_cuda(x, weight, bias, what="WideGroupNorm")
     _same_dtype("WideGroupNorm", x, weight, bias)
     if x.dim() < 3 or x.shape[0] != n:
@@ -303,6 +333,8 @@ def instancenorm_train(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias
 
 def embedding(idx: Tensor, weight: Tensor) -> Tensor:
     """[N, V, D] tables, shared integer indices of any shape -> [N, *idx.shape, D]."""
+    if _AG.needs_grad(weight):
+        return _AG.run(embedding, _AG.embedding_t, idx, weight)
     dev = N.require_cuda(idx, weight, what="WideEmbedding")
     if idx.dtype not in (torch.int64, torch.int32, torch.int16, torch.int8, torch.uint8):
         raise TypeError(f"WideEmbedding: indices must be integers, got {idx.dtype}")
@@ -338,6 +370,8 @@ def _rnn_common(x: Tensor, w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor], g
 def gru(x: Tensor, h0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor],
         b_hh: Optional[Tensor]):
     """WideGRU forward: returns (out [N, B, T, H], h_n [N, B, H])."""
+    if _AG.needs_grad(x, h0, w_ih, w_hh, b_ih, b_hh):
+        return _AG.run(gru, _AG.gru_t, x, h0, w_ih, w_hh, b_ih, b_hh)
     dev = N.require_cuda(x, h0, w_ih, w_hh, b_ih, b_hh, what="WideGRU")
     _same_dtype("WideGRU", w_ih, x, h0, w_hh, b_ih, b_hh)
     n, batch, steps, hidden, gx = _rnn_common(x, w_ih, w_hh, b_ih, 3, "WideGRU")
@@ -357,6 +391,9 @@ def gru(x: Tensor, h0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor, b_ih: Optio
 def lstm(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor,
          b_ih: Optional[Tensor], b_hh: Optional[Tensor]):
     """WideLSTM forward on dense diagonal blocks: returns (out, (h_n, c_n))."""
+    if _AG.needs_grad(x, h0, c0, w_ih, w_hh, b_ih, b_hh):
+        out, hn, cn = _AG.run(_lstm_flat, _AG.lstm_t, x, h0, c0, w_ih, w_hh, b_ih, b_hh)
+        return out, (hn, cn)
     dev = N.require_cuda(x, h0, c0, w_ih, w_hh, b_ih, b_hh, what="WideLSTM")
     _same_dtype("WideLSTM", w_ih, x, h0, c0, w_hh, b_ih, b_hh)
     n, batch, steps, hidden, gx = _rnn_common(x, w_ih, w_hh, b_ih, 4, "WideLSTM")
@@ -380,6 +417,11 @@ def lstm(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], w_ih: Tensor, w_
 # ---------------------------------------------------------------------------
 # Attention
 # ---------------------------------------------------------------------------
+
+def _lstm_flat(x, h0, c0, w_ih, w_hh, b_ih, b_hh):
+    out, (hn, cn) = lstm(x, h0, c0, w_ih, w_hh, b_ih, b_hh)
+    return out, hn, cn
+
 
 def attention_core(q: Tensor, k: Tensor, v: Tensor, nb: int, heads: int, tq: int, tk: int, head_dim: int,
                    q_stride: int, k_stride: int, v_stride: int, out: Tensor, causal: bool,
@@ -420,6 +462,10 @@ def attention_core(q: Tensor, k: Tensor, v: Tensor, nb: int, heads: int, tq: int
 
 def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool) -> Tensor:
     """WideAttention forward on N-first [N, B, T, D] tensors (see the module)."""
+    params = (mod.q_weight, mod.q_bias, mod.kv_weight, mod.kv_bias, mod.out_weight, mod.out_bias)
+    if _AG.needs_grad(query, key, value, *params):
+        kernel = lambda q, k, v, m, c, h, *p: attention(mod, q, k, v, m, c)
+        return _AG.run(kernel, _AG.attention_t, query, key, value, attn_mask, is_causal, mod.n_heads, *params)
     dev = N.require_cuda(query, key, value, mod.q_weight, what="WideAttention")
     _same_dtype("WideAttention", mod.q_weight, query, key, value)
     if is_causal and attn_mask is not None:
@@ -495,6 +541,9 @@ def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, p
     ([N*Cout]), activation, residual. With non-default layouts the call
     returns None when the library cannot serve the combination for this
     geometry (nothing is launched); the default layouts always run."""
+    if _AG.needs_grad(x, weight, bias, scale, shift, residual):
+        return _AG.run(conv_nd, _AG.conv_nd_t, x, weight, bias, n, stride, padding, dilation, scale, shift,
+                       residual, act, residual_first, in_layout, out_layout, res_layout)
     dev = N.require_cuda(x, weight, bias, scale, shift, residual, what="WideConv")
     _same_dtype("WideConv", weight, x, bias, scale, shift, residual)
     if in_layout == LAYOUT_PACKED:

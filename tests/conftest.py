@@ -24,6 +24,7 @@ for p in (PKG, ROOT, GOLDEN):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device; runs the sm_100a kernels")
+    config.addinivalue_line("markers", "grad: runs with autograd enabled (gradient tests)")
 
 
 def golden_names(kind=None):
@@ -52,3 +53,15 @@ def _no_tf32():
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     yield
+
+
+@pytest.fixture(autouse=True)
+def _inference_unless_grad(request):
+    # Forward-parity GPU tests run as inference (the fused kernels and the
+    # graph executor serve calls whose result autograd does not need); tests
+    # marked ``grad`` exercise the differentiable path.
+    if request.node.get_closest_marker("gpu") and not request.node.get_closest_marker("grad"):
+        with torch.no_grad():
+            yield
+    else:
+        yield
