@@ -644,7 +644,8 @@ def run_b200(args):
         k = i % 2
         if i >= 2:
             s_in.wait_event(ev_comp[k])          # step i-2's forward has read x_dev[k]
-            stream.wait_event(ev_out[k])         # and its result has been downloaded (a graph
+            if executor:
+                stream.wait_event(ev_out[k])     # and its result has been downloaded (a graph
                                                  # replay writes the same output tensor again)
         with torch.cuda.stream(s_in):
             x_dev[k].copy_(x_host, non_blocking=True)
