@@ -271,6 +271,14 @@ WIDEK_API int widek_lstm_recurrence(const void* gates_x, const void* w_hh, const
                                     void* c_n, int64_t n, int64_t batch, int64_t steps,
                                     int64_t hidden, int dtype, void* stream);
 
+/* Kernel choice for the recurrences: 0 = the register-resident kernel where
+ * it applies (hidden size 128, at most 128 gate rows per cluster CTA; W_hh
+ * held in registers, hidden state passed by DSMEM stores and mbarrier
+ * signals), else the shared-memory cluster kernel (default); 1 = the
+ * shared-memory cluster kernel only. Process-wide; for tests and
+ * measurements. No reference counterpart. */
+WIDEK_API int widek_rnn_set_variant(int variant);
+
 /* ---- WideConv1d / WideConv2d / WideConv3d -------------------------------- */
 
 /* Repacks conv weights [rows][cin][taps] -> [rows][taps][cin] (rows = n*cout,

@@ -17,14 +17,17 @@
 //      (barrier.cluster arrive.release / wait.acquire) publishes it.
 // h is double-buffered so a single barrier per step orders reads and writes.
 // The cluster is as large as all models' clusters allow on the GPU at once
-// (up to 8 CTAs), resident weights are stored four k at a time so that the
-// mat-vec reads 16-byte words of W and h, and the next step's input-gate
-// values are loaded into registers one step ahead.
+// (up to 8 CTAs); with resident weights the mat-vec splits each row's k
+// range over S consecutive lanes (16-byte words of W and h, partial sums
+// combined by shuffles), so S*R threads share the work with short
+// dependency chains; the next step's input-gate values are loaded into
+// registers one step ahead.
 // When the weight slice does not fit in shared memory for any cluster size,
 // the kernel reads W_hh rows from global memory (L2) instead.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -43,6 +46,7 @@ struct RnnArgs {
     void* hn;            // [n, batch, H]
     void* cn;            // [n, batch, H] or null (LSTM)
     int batch, T, H, G, cl, w_in_smem;
+    int kparts;          // threads sharing one row's dot products (split k, vec4 path)
 };
 
 template <typename T, bool LSTM>
@@ -66,14 +70,14 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     // global row of local row lr = g * U + j
     auto grow = [&](int lr) { return (lr / U) * H + q * U + (lr % U); };
 
-    // Resident weights: [H/4][R][4] (four consecutive k of a row in one
-    // 16-byte word) when H % 4 == 0, else k-major [H][R].
+    // Resident weights: row-major [R][H] (16-byte words of four k) for the
+    // split-k mat-vec when H % 4 == 0, else k-major [H][R].
     const bool vec4 = a.w_in_smem && (H % 4 == 0);
     if (a.w_in_smem) {
         for (int i = threadIdx.x; i < R * H; i += blockDim.x) {
             const int lr = i / H, k = i % H;
             const float v = to_f<T>(w[(size_t)grow(lr) * H + k]);
-            if (vec4) Ws[((size_t)(k >> 2) * R + lr) * 4 + (k & 3)] = v;
+            if (vec4) Ws[(size_t)lr * H + k] = v;
             else Ws[(size_t)k * R + lr] = v;
         }
     }
@@ -109,54 +113,76 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
         float gx_cur[4] = {gx_next[0], gx_next[1], gx_next[2], gx_next[3]};
         if (pre && (int)threadIdx.x < bu && t + 1 < a.T) load_gx(threadIdx.x, t + 1, gx_next);
         // 1. recurrent mat-vec: rows x batch
-        for (int lr = threadIdx.x; lr < R; lr += blockDim.x) {
-            const float bias = bh ? to_f<T>(bh[grow(lr)]) : 0.f;
+        if (vec4) {
+            // Split k: S = kparts consecutive lanes share a row; lane part p
+            // takes the 16-byte words k4 = i*S + p, so a quarter-warp reads
+            // contiguous 128-byte runs of W and of each h row; partial sums
+            // meet by shuffles. S*R threads, many warps per SM, short chains.
+            const int S = a.kparts;
+            const int lr = threadIdx.x / S, p = threadIdx.x % S;
+            const int KS = (H >> 2) / S;
+            const bool live = lr < R;
+            const float4* W4 = reinterpret_cast<const float4*>(Ws) + (size_t)(live ? lr : 0) * (H >> 2);
+            const float bias = (live && bh) ? to_f<T>(bh[grow(lr)]) : 0.f;
             for (int b0 = 0; b0 < B; b0 += 4) {
-                float acc[4];
-#pragma unroll
-                for (int bb = 0; bb < 4; ++bb) acc[bb] = bias;
                 const int nb = B - b0 < 4 ? B - b0 : 4;
-                if (vec4) {
-                    // 16-byte weight words (conflict-free across the warp) and
-                    // 16-byte broadcasts of four h values per batch row.
-                    const float4* W4 = reinterpret_cast<const float4*>(Ws);
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                const float4* H4 = reinterpret_cast<const float4*>(hc + (size_t)b0 * H);
+                const int h4 = H >> 2;
 #pragma unroll 2
-                    for (int k4 = 0; k4 < H / 4; ++k4) {
-                        const float4 wv = W4[(size_t)k4 * R + lr];
+                for (int i = 0; i < KS; ++i) {
+                    const int k4 = i * S + p;
+                    const float4 wv = W4[k4];
 #pragma unroll
-                        for (int bb = 0; bb < 4; ++bb) {
-                            if (bb < nb) {
-                                const float4 hv = reinterpret_cast<const float4*>(hc + (size_t)(b0 + bb) * H)[k4];
-                                float s = acc[bb];
-                                s = fmaf(wv.x, hv.x, s);
-                                s = fmaf(wv.y, hv.y, s);
-                                s = fmaf(wv.z, hv.z, s);
-                                s = fmaf(wv.w, hv.w, s);
-                                acc[bb] = s;
-                            }
-                        }
-                    }
-                } else if (a.w_in_smem) {
-#pragma unroll 4
-                    for (int k = 0; k < H; ++k) {
-                        const float wv = Ws[(size_t)k * R + lr];
-#pragma unroll
-                        for (int bb = 0; bb < 4; ++bb)
-                            if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
-                    }
-                } else {
-                    const T* wr = w + (size_t)grow(lr) * H;
-#pragma unroll 4
-                    for (int k = 0; k < H; ++k) {
-                        const float wv = to_f<T>(wr[k]);
-#pragma unroll
-                        for (int bb = 0; bb < 4; ++bb)
-                            if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
+                    for (int bb = 0; bb < 4; ++bb) {
+                        const float4 hv = H4[(bb < nb ? bb : 0) * h4 + k4];
+                        float s2 = acc[bb];
+                        s2 = fmaf(wv.x, hv.x, s2);
+                        s2 = fmaf(wv.y, hv.y, s2);
+                        s2 = fmaf(wv.z, hv.z, s2);
+                        s2 = fmaf(wv.w, hv.w, s2);
+                        acc[bb] = s2;
                     }
                 }
 #pragma unroll
                 for (int bb = 0; bb < 4; ++bb)
-                    if (bb < nb) gates[(size_t)(b0 + bb) * R + lr] = acc[bb];
+                    for (int off = S >> 1; off > 0; off >>= 1) acc[bb] += __shfl_xor_sync(0xffffffffu, acc[bb], off);
+                if (live && p == 0) {
+#pragma unroll
+                    for (int bb = 0; bb < 4; ++bb)
+                        if (bb < nb) gates[(size_t)(b0 + bb) * R + lr] = acc[bb] + bias;
+                }
+            }
+        } else {
+            for (int lr = threadIdx.x; lr < R; lr += blockDim.x) {
+                const float bias = bh ? to_f<T>(bh[grow(lr)]) : 0.f;
+                for (int b0 = 0; b0 < B; b0 += 4) {
+                    float acc[4];
+#pragma unroll
+                    for (int bb = 0; bb < 4; ++bb) acc[bb] = bias;
+                    const int nb = B - b0 < 4 ? B - b0 : 4;
+                    if (a.w_in_smem) {
+#pragma unroll 4
+                        for (int k = 0; k < H; ++k) {
+                            const float wv = Ws[(size_t)k * R + lr];
+#pragma unroll
+                            for (int bb = 0; bb < 4; ++bb)
+                                if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
+                        }
+                    } else {
+                        const T* wr = w + (size_t)grow(lr) * H;
+#pragma unroll 4
+                        for (int k = 0; k < H; ++k) {
+                            const float wv = to_f<T>(wr[k]);
+#pragma unroll
+                            for (int bb = 0; bb < 4; ++bb)
+                                if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
+                        }
+                    }
+#pragma unroll
+                    for (int bb = 0; bb < 4; ++bb)
+                        if (bb < nb) gates[(size_t)(b0 + bb) * R + lr] = acc[bb];
+                }
             }
         }
         __syncthreads();
@@ -207,6 +233,263 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     cluster.sync();
 }
 
+// ---------------------------------------------------------------------------
+// Register-resident variant (small hidden sizes, e.g. H = 128): W_hh lives in
+// registers for all T steps and the hidden state moves by signals instead of
+// a cluster-wide barrier.
+//
+// 256 threads per CTA; lane part p = tid % 8 of row group g = tid / 8 holds
+// the 16-byte words k4 = i*8 + p (i < KS = H/32) of rows g + 32r (r < RPT),
+// so each step's mat-vec reads only h from shared memory (one 16-byte word
+// per k-slice and batch row) and reduces the 8 partial sums by shuffles.
+// The new h slice goes into every cluster CTA's next buffer by DSMEM stores,
+// each followed by a release-arrive on that CTA's "full" mbarrier of the
+// buffer; a CTA starts step t once its buffer for h_t has all
+// cl * B * U arrivals (acquire at cluster scope). A two-deep buffer ring is
+// enough: a CTA writes h_{t+2} into a peer only after receiving that peer's
+// h_{t+1}, which the peer produced after its step-t mat-vec finished
+// reading the buffer. Every wait is bounded (device error + abort flag).
+// ---------------------------------------------------------------------------
+constexpr int kRegThreads = 256;
+constexpr int kRegParts = 8;
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    const uint32_t addr = sm100::smem_addr(bar);
+    auto try_once = [&]() {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        return ok != 0;
+    };
+    if (try_once()) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (try_once()) return true;
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+template <typename T, bool LSTM, int RPT, int KS>
+__global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int* err) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int q = (int)cluster.block_rank();
+    const int cl = a.cl;
+    const int model = blockIdx.x / cl;
+    const int H = a.H, G = a.G, B = a.batch, U = H / cl, R = G * U;
+
+    extern __shared__ __align__(16) float rsm[];
+    float* hbuf = rsm;                                         // [2][B][H]
+    float* gates = hbuf + 2 * (size_t)B * H;                   // [B][R]
+    float* cst = gates + (size_t)B * R;                        // [B][U] (LSTM)
+    uint64_t* full = reinterpret_cast<uint64_t*>(cst + (((size_t)B * U + 1) & ~(size_t)1));   // [2]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
+
+    const T* gx = static_cast<const T*>(a.gx) + (size_t)model * B * a.T * G * H;
+    const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * G * H * H;
+    const T* bh = a.b_hh ? static_cast<const T*>(a.b_hh) + (size_t)model * G * H : nullptr;
+    T* out = static_cast<T*>(a.out) + (size_t)model * B * a.T * H;
+    auto grow = [&](int lr) { return (lr / U) * H + q * U + (lr % U); };
+
+    const int tid = threadIdx.x, grp = tid / kRegParts, p = tid % kRegParts;
+    // This thread's W words and row biases, for all steps.
+    float4 wr[RPT][KS];
+    float brow[RPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const int lr = grp + 32 * r;
+        const bool ok = lr < R;
+        const T* wrow = w + (size_t)(ok ? grow(lr) : 0) * H;
+#pragma unroll
+        for (int i = 0; i < KS; ++i) {
+            const int k = 4 * (i * kRegParts + p);
+            wr[r][i] = ok ? make_float4(to_f<T>(wrow[k]), to_f<T>(wrow[k + 1]), to_f<T>(wrow[k + 2]),
+                                        to_f<T>(wrow[k + 3]))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        brow[r] = (ok && bh) ? to_f<T>(bh[grow(lr)]) : 0.f;
+    }
+    for (int i = tid; i < B * H; i += blockDim.x)
+        hbuf[i] = a.h0 ? to_f<T>(static_cast<const T*>(a.h0)[(size_t)model * B * H + i]) : 0.f;
+    if (LSTM) {
+        for (int i = tid; i < B * U; i += blockDim.x) {
+            const int b = i / U, j = i % U;
+            cst[i] = a.c0 ? to_f<T>(static_cast<const T*>(a.c0)[((size_t)model * B + b) * H + q * U + j]) : 0.f;
+        }
+    }
+    if (tid == 0) {
+        sm100::mbar_init(&full[0], (uint32_t)(cl * B * U));
+        sm100::mbar_init(&full[1], (uint32_t)(cl * B * U));
+        *abort_flag = 0;
+        sm100::mbar_init_fence();
+    }
+    cluster.sync();
+    const uint32_t full0 = sm100::smem_addr(&full[0]);
+
+    const int bu = B * U;
+    const bool pre = bu <= (int)blockDim.x;
+    float gx_next[4] = {0.f, 0.f, 0.f, 0.f};
+    auto load_gx = [&](int i, int t, float (&v)[4]) {
+        const int b = i / U, j = i % U;
+        const T* gxr = gx + ((size_t)b * a.T + t) * G * H + q * U + j;
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi)
+            if (gi < G) v[gi] = to_f<T>(gxr[(size_t)gi * H]);
+    };
+    if (pre && tid < bu && a.T > 0) load_gx(tid, 0, gx_next);
+
+    bool ok = true;
+    for (int t = 0; t < a.T; ++t) {
+        // One thread waits for h_t (all cl * B * U arrivals); the barrier
+        // then releases the CTA, and every thread sees the same verdict.
+        if (t > 0 && tid == 0 && !mbar_wait_cluster(&full[t & 1], (uint32_t)(((t - 1) >> 1) & 1), abort_flag))
+            *abort_flag = 1;
+        __syncthreads();     // h_t complete; the previous step's gate reads are done
+        if (*abort_flag) {
+            ok = false;
+            break;
+        }
+        const float* hc = hbuf + (size_t)(t & 1) * B * H;
+        const int nxt = (t + 1) & 1;
+        float gx_cur[4] = {gx_next[0], gx_next[1], gx_next[2], gx_next[3]};
+        if (pre && tid < bu && t + 1 < a.T) load_gx(tid, t + 1, gx_next);
+        // 1. mat-vec from registers: per batch row, RPT rows x this lane's k-slice
+        const float4* H4 = reinterpret_cast<const float4*>(hc);
+        for (int b = 0; b < B; ++b) {
+            float acc[RPT];
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) acc[r] = 0.f;
+#pragma unroll
+            for (int i = 0; i < KS; ++i) {
+                const float4 hv = H4[(size_t)b * (H >> 2) + i * kRegParts + p];
+#pragma unroll
+                for (int r = 0; r < RPT; ++r) {
+                    float s2 = acc[r];
+                    s2 = fmaf(wr[r][i].x, hv.x, s2);
+                    s2 = fmaf(wr[r][i].y, hv.y, s2);
+                    s2 = fmaf(wr[r][i].z, hv.z, s2);
+                    s2 = fmaf(wr[r][i].w, hv.w, s2);
+                    acc[r] = s2;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) {
+#pragma unroll
+                for (int off = kRegParts / 2; off > 0; off >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+                const int lr = grp + 32 * r;
+                if (p == 0 && lr < R) gates[(size_t)b * R + lr] = acc[r] + brow[r];
+            }
+        }
+        __syncthreads();
+        // 2. gate math for (b, j); 3. publish h into every cluster CTA
+        for (int i = tid; i < bu; i += blockDim.x) {
+            const int b = i / U, j = i % U;
+            const int ju = q * U + j;
+            const float* gr = gates + (size_t)b * R;
+            if (!pre) load_gx(i, t, gx_cur);
+            float hnew;
+            if (!LSTM) {
+                const float r = sigmoidf_(gx_cur[0] + gr[j]);
+                const float z = sigmoidf_(gx_cur[1] + gr[U + j]);
+                const float nn = tanhf(gx_cur[2] + r * gr[2 * U + j]);
+                hnew = (1.f - z) * nn + z * hc[(size_t)b * H + ju];
+            } else {
+                const float ig = sigmoidf_(gx_cur[0] + gr[j]);
+                const float fg = sigmoidf_(gx_cur[1] + gr[U + j]);
+                const float gg = tanhf(gx_cur[2] + gr[2 * U + j]);
+                const float og = sigmoidf_(gx_cur[3] + gr[3 * U + j]);
+                const float c = fg * cst[i] + ig * gg;
+                cst[i] = c;
+                hnew = og * tanhf(c);
+            }
+            const T hs = from_f<T>(hnew);
+            const float hv = to_f<T>(hs);
+            out[((size_t)b * a.T + t) * H + ju] = hs;
+            float* hdst = hbuf + (size_t)nxt * B * H + (size_t)b * H + ju;
+            for (int r = 0; r < cl; ++r) {
+                *cluster.map_shared_rank(hdst, r) = hv;
+                sm100::mbar_arrive_remote(sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8);
+            }
+        }
+    }
+    // h_T (written by every CTA of the cluster into this CTA's buffer T % 2)
+    if (ok && a.T > 0 && tid == 0 &&
+        !mbar_wait_cluster(&full[a.T & 1], (uint32_t)(((a.T - 1) >> 1) & 1), abort_flag))
+        *abort_flag = 1;
+    __syncthreads();
+    if (tid == 0 && *abort_flag) raise_device_error(err, DEV_ERR_RNN_TIMEOUT);
+    const float* hl = hbuf + (size_t)(a.T & 1) * B * H;
+    for (int i = tid; i < bu; i += blockDim.x) {
+        const int b = i / U, j = i % U;
+        const int ju = q * U + j;
+        static_cast<T*>(a.hn)[((size_t)model * B + b) * H + ju] = from_f<T>(hl[(size_t)b * H + ju]);
+        if (LSTM && a.cn) static_cast<T*>(a.cn)[((size_t)model * B + b) * H + ju] = from_f<T>(cst[i]);
+    }
+    // No CTA may exit while a peer can still write into or read its shared memory.
+    cluster.sync();
+}
+
+size_t rnn_reg_smem(int B, int H, int G, int cl) {
+    const int U = H / cl, R = G * U;
+    const size_t f = 2 * (size_t)B * H + (size_t)B * R + (((size_t)B * U + 1) & ~(size_t)1);
+    return f * sizeof(float) + 2 * sizeof(uint64_t) + 16;
+}
+
+template <typename T, bool LSTM, int RPT>
+int launch_rnn_reg_k(const RnnArgs& a, int64_t n, size_t smem, cudaStream_t st) {
+    auto kern = rnn_reg_kernel<T, LSTM, RPT, 4>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return set_error(WIDEK_ERR_CUDA, "rnn: cannot reserve %zu bytes of shared memory", smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(n * a.cl));
+    cfg.blockDim = dim3(kRegThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, device_error_ptr());
+    if (e != cudaSuccess) return set_error(WIDEK_ERR_CUDA, "rnn: launch failed: %s", cudaGetErrorString(e));
+    return check_launch("widek_rnn_fwd (register-resident)");
+}
+
+// The register-resident kernel when H = 128 (KS = 4 words of k per lane part)
+// and a cluster of cl CTAs leaves at most 128 gate rows per CTA (RPT <= 4).
+template <typename T, bool LSTM>
+int try_rnn_reg(RnnArgs a, int64_t n, cudaStream_t st, bool& used) {
+    used = false;
+    if (a.H != 128 || a.batch > 64) return WIDEK_OK;
+    const int sms = sm_count(current_device());
+    int cl = 0;
+    for (int c : {8, 4, 2, 1}) {
+        if (a.H % c || (int64_t)c * n > sms) continue;
+        if (a.G * (a.H / c) <= 32 * 4) { cl = c; break; }
+    }
+    if (!cl) return WIDEK_OK;
+    a.cl = cl;
+    const int rpt = (a.G * (a.H / cl) + 31) / 32;
+    const size_t smem = rnn_reg_smem(a.batch, a.H, a.G, cl);
+    if (smem > 227 * 1024) return WIDEK_OK;
+    used = true;
+    switch (rpt) {
+        case 1: return launch_rnn_reg_k<T, LSTM, 1>(a, n, smem, st);
+        case 2: return launch_rnn_reg_k<T, LSTM, 2>(a, n, smem, st);
+        case 3: return launch_rnn_reg_k<T, LSTM, 3>(a, n, smem, st);
+        default: return launch_rnn_reg_k<T, LSTM, 4>(a, n, smem, st);
+    }
+}
+
 constexpr size_t kMaxSmem = 227 * 1024;
 
 size_t rnn_smem(int B, int H, int G, int cl, bool w_in_smem) {
@@ -215,8 +498,17 @@ size_t rnn_smem(int B, int H, int G, int cl, bool w_in_smem) {
     return f * sizeof(float);
 }
 
+// 0: the register-resident kernel where it applies (default); 1: the
+// shared-memory cluster kernel only. Set with widek_rnn_set_variant.
+int g_rnn_variant = 0;
+
 template <typename T, bool LSTM>
 int launch_rnn(RnnArgs a, int64_t n, cudaStream_t st) {
+    if (g_rnn_variant == 0) {
+        bool used = false;
+        const int rc = try_rnn_reg<T, LSTM>(a, n, st, used);
+        if (used) return rc;
+    }
     // Cluster of 1..8 CTAs per model (H divisible by it): the largest one for
     // which all models' clusters fit on the GPU at once (more SMs per model,
     // a shorter mat-vec per step), else the smallest whose weight slice fits
@@ -247,7 +539,15 @@ int launch_rnn(RnnArgs a, int64_t n, cudaStream_t st) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(WIDEK_ERR_CUDA, "rnn: cannot reserve %zu bytes of shared memory", smem);
     const int rows = a.G * (a.H / cl);
-    int threads = ((rows + 31) / 32) * 32;
+    // Split-k factor of the resident vec4 mat-vec: the largest S in {8, 4, 2, 1}
+    // dividing H/4 with S*rows <= 1024 threads (S = 1 keeps one row per thread).
+    a.kparts = 1;
+    if (resident && a.H % 4 == 0) {
+        for (int sp : {8, 4, 2}) {
+            if ((a.H / 4) % sp == 0 && sp * rows <= 1024) { a.kparts = sp; break; }
+        }
+    }
+    int threads = ((rows * a.kparts + 31) / 32) * 32;
     const int pairs = a.batch * (a.H / cl);
     if (threads < pairs) threads = ((pairs + 31) / 32) * 32;
     if (threads > 1024) threads = 1024;     // the gate loop strides when pairs > 1024
@@ -290,7 +590,7 @@ int rnn_entry(bool lstm, const void* gates_x, const void* w_hh, const void* b_hh
     if (n == 0 || batch == 0 || hidden == 0) return WIDEK_OK;
     if (!w_hh || !h_n || (steps > 0 && (!gates_x || !out)))
         return set_error(WIDEK_ERR_INVALID, "rnn: null pointer");
-    RnnArgs a{gates_x, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps, (int)hidden, lstm ? 4 : 3, 1, 1};
+    RnnArgs a{gates_x, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps, (int)hidden, lstm ? 4 : 3, 1, 1, 1};
     RnnLaunch L{a, n, lstm, (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
 }
@@ -299,6 +599,12 @@ int rnn_entry(bool lstm, const void* gates_x, const void* w_hh, const void* b_hh
 }  // namespace widek
 
 extern "C" {
+
+int widek_rnn_set_variant(int variant) {
+    if (variant < 0 || variant > 1) return widek::set_error(WIDEK_ERR_INVALID, "rnn: unknown variant %d", variant);
+    widek::g_rnn_variant = variant;
+    return WIDEK_OK;
+}
 
 int widek_gru_recurrence(const void* gates_x, const void* w_hh, const void* b_hh, const void* h0, void* out,
                          void* h_n, int64_t n, int64_t batch, int64_t steps, int64_t hidden, int dtype,

@@ -48,6 +48,7 @@ SIGNATURES = {
     "widek_linear_set_variant": [_int],
     "widek_attention_set_variant": [_int],
     "widek_conv_set_variant": [_int],
+    "widek_rnn_set_variant": [_int],
     "widek_launch_count": [],
     "widek_layernorm_fwd": [_c_void_p] * 4 + [_i64] * 3 + [_dbl, _int, _c_void_p],
     "widek_swap01": [_c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p],

@@ -106,3 +106,37 @@ def test_rnn_zero_steps():
                     bhh.to(DEV))
     assert y.shape == (2, 3, 0, 8)
     torch.testing.assert_close(hn.cpu(), h0)
+
+
+@pytest.fixture(params=[0, 1], ids=["register-resident", "smem-cluster"])
+def rnn_variant(request):
+    from wide_compiler import _native as N
+    N.check(N.lib().widek_rnn_set_variant(request.param), "widek_rnn_set_variant")
+    yield request.param
+    N.lib().widek_rnn_set_variant(0)
+
+
+@pytest.mark.parametrize("n,b,t", [(32, 4, 32), (1, 1, 5), (5, 8, 9), (2, 40, 3), (100, 2, 4)])
+@pytest.mark.parametrize("kind", ["gru", "lstm"])
+def test_rnn_h128_both_kernels(rnn_variant, kind, n, b, t):
+    """Hidden size 128, where the register-resident kernel applies (cluster
+    sizes 8/4/2 by N; N=100 leaves one CTA per model and takes the
+    shared-memory kernel); batch 40 makes the gate loop stride; both kernels
+    against the oracle."""
+    i, h = 24, 128
+    g = 3 if kind == "gru" else 4
+    wih, whh, bih, bhh = _rnn_params(n, i, h, g, torch.float32, n * 11 + b + t + g)
+    x = torch.randn(n, b, t, i, generator=torch.Generator().manual_seed(b + t))
+    h0 = torch.randn(n, b, h, generator=torch.Generator().manual_seed(n)) * 0.5
+    if kind == "gru":
+        y, hn = ops.gru(x.to(DEV), h0.to(DEV), wih.to(DEV), whh.to(DEV), bih.to(DEV), bhh.to(DEV))
+        ry, rh = O.gru(x, h0, wih, whh, bih, bhh)
+    else:
+        c0 = torch.randn(n, b, h, generator=torch.Generator().manual_seed(n + 1)) * 0.5
+        y, (hn, cn) = ops.lstm(x.to(DEV), h0.to(DEV), c0.to(DEV), wih.to(DEV), whh.to(DEV), bih.to(DEV),
+                               bhh.to(DEV))
+        ry, (rh, rc) = O.lstm(x, h0, c0, wih, whh, bih, bhh)
+        assert_fp32_close(cn, rc)
+    assert_fp32_close(y, ry)
+    assert_fp32_close(hn, rh)
+    no_device_error()
