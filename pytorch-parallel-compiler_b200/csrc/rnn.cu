@@ -243,9 +243,9 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
 // so each step's mat-vec reads only h from shared memory (one 16-byte word
 // per k-slice and batch row) and reduces the 8 partial sums by shuffles.
 // The new h slice goes into every cluster CTA's next buffer by DSMEM stores,
-// each followed by a release-arrive on that CTA's "full" mbarrier of the
-// buffer; a CTA starts step t once its buffer for h_t has all
-// cl * B * U arrivals (acquire at cluster scope). A two-deep buffer ring is
+// each group of lanes followed by release-arrives on that CTA's "full"
+// mbarrier of the buffer; a CTA starts step t once its buffer for h_t has
+// all 32 arrivals (acquire at cluster scope). A two-deep buffer ring is
 // enough: a CTA writes h_{t+2} into a peer only after receiving that peer's
 // h_{t+1}, which the peer produced after its step-t mat-vec finished
 // reading the buffer. Every wait is bounded (device error + abort flag).
@@ -289,7 +289,8 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
     float* hbuf = rsm;                                         // [2][B][H]
     float* gates = hbuf + 2 * (size_t)B * H;                   // [B][R]
     float* cst = gates + (size_t)B * R;                        // [B][U] (LSTM)
-    uint64_t* full = reinterpret_cast<uint64_t*>(cst + (((size_t)B * U + 1) & ~(size_t)1));   // [2]
+    float* hstage = cst + (((size_t)B * U + 3) & ~(size_t)3);  // [B][U]: this CTA's new h slice
+    uint64_t* full = reinterpret_cast<uint64_t*>(hstage + (((size_t)B * U + 3) & ~(size_t)3));   // [2]
     volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
 
     const T* gx = static_cast<const T*>(a.gx) + (size_t)model * B * a.T * G * H;
@@ -324,9 +325,12 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             cst[i] = a.c0 ? to_f<T>(static_cast<const T*>(a.c0)[((size_t)model * B + b) * H + q * U + j]) : 0.f;
         }
     }
+    // 16-byte chunks of the h slice; warp 0 publishes them (32 arrivals per
+    // barrier phase: 32 / cl lanes of each of the cl CTAs).
+    const int nchunk = (B * U) / 4;
     if (tid == 0) {
-        sm100::mbar_init(&full[0], (uint32_t)(cl * B * U));
-        sm100::mbar_init(&full[1], (uint32_t)(cl * B * U));
+        sm100::mbar_init(&full[0], 32u);
+        sm100::mbar_init(&full[1], 32u);
         *abort_flag = 0;
         sm100::mbar_init_fence();
     }
@@ -347,7 +351,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
 
     bool ok = true;
     for (int t = 0; t < a.T; ++t) {
-        // One thread waits for h_t (all cl * B * U arrivals); the barrier
+        // One thread waits for h_t (all 32 arrivals); the barrier
         // then releases the CTA, and every thread sees the same verdict.
         if (t > 0 && tid == 0 && !mbar_wait_cluster(&full[t & 1], (uint32_t)(((t - 1) >> 1) & 1), abort_flag))
             *abort_flag = 1;
@@ -360,31 +364,49 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
         const int nxt = (t + 1) & 1;
         float gx_cur[4] = {gx_next[0], gx_next[1], gx_next[2], gx_next[3]};
         if (pre && tid < bu && t + 1 < a.T) load_gx(tid, t + 1, gx_next);
-        // 1. mat-vec from registers: per batch row, RPT rows x this lane's k-slice
+        // 1. mat-vec from registers: four batch rows at a time (their loads,
+        // FMA chains and shuffle trees interleave), RPT rows x this lane's
+        // k-slice
         const float4* H4 = reinterpret_cast<const float4*>(hc);
-        for (int b = 0; b < B; ++b) {
-            float acc[RPT];
+        for (int b0 = 0; b0 < B; b0 += 4) {
+            const int nb = B - b0 < 4 ? B - b0 : 4;
+            float acc[4][RPT];
 #pragma unroll
-            for (int r = 0; r < RPT; ++r) acc[r] = 0.f;
+            for (int bb = 0; bb < 4; ++bb)
+#pragma unroll
+                for (int r = 0; r < RPT; ++r) acc[bb][r] = 0.f;
 #pragma unroll
             for (int i = 0; i < KS; ++i) {
-                const float4 hv = H4[(size_t)b * (H >> 2) + i * kRegParts + p];
+                float4 hv[4];
 #pragma unroll
-                for (int r = 0; r < RPT; ++r) {
-                    float s2 = acc[r];
-                    s2 = fmaf(wr[r][i].x, hv.x, s2);
-                    s2 = fmaf(wr[r][i].y, hv.y, s2);
-                    s2 = fmaf(wr[r][i].z, hv.z, s2);
-                    s2 = fmaf(wr[r][i].w, hv.w, s2);
-                    acc[r] = s2;
-                }
+                for (int bb = 0; bb < 4; ++bb)
+                    hv[bb] = H4[(size_t)(b0 + (bb < nb ? bb : 0)) * (H >> 2) + i * kRegParts + p];
+#pragma unroll
+                for (int bb = 0; bb < 4; ++bb)
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        float s2 = acc[bb][r];
+                        s2 = fmaf(wr[r][i].x, hv[bb].x, s2);
+                        s2 = fmaf(wr[r][i].y, hv[bb].y, s2);
+                        s2 = fmaf(wr[r][i].z, hv[bb].z, s2);
+                        s2 = fmaf(wr[r][i].w, hv[bb].w, s2);
+                        acc[bb][r] = s2;
+                    }
             }
 #pragma unroll
-            for (int r = 0; r < RPT; ++r) {
+            for (int off = kRegParts / 2; off > 0; off >>= 1)
 #pragma unroll
-                for (int off = kRegParts / 2; off > 0; off >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
-                const int lr = grp + 32 * r;
-                if (p == 0 && lr < R) gates[(size_t)b * R + lr] = acc[r] + brow[r];
+                for (int bb = 0; bb < 4; ++bb)
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) acc[bb][r] += __shfl_xor_sync(0xffffffffu, acc[bb][r], off);
+            if (p == 0) {
+#pragma unroll
+                for (int bb = 0; bb < 4; ++bb)
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        const int lr = grp + 32 * r;
+                        if (bb < nb && lr < R) gates[(size_t)(b0 + bb) * R + lr] = acc[bb][r] + brow[r];
+                    }
             }
         }
         __syncthreads();
@@ -410,13 +432,25 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
                 hnew = og * tanhf(c);
             }
             const T hs = from_f<T>(hnew);
-            const float hv = to_f<T>(hs);
+            hstage[i] = to_f<T>(hs);
             out[((size_t)b * a.T + t) * H + ju] = hs;
-            float* hdst = hbuf + (size_t)nxt * B * H + (size_t)b * H + ju;
-            for (int r = 0; r < cl; ++r) {
-                *cluster.map_shared_rank(hdst, r) = hv;
-                sm100::mbar_arrive_remote(sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8);
+        }
+        __syncthreads();
+        // 3. warp 0 publishes the slice: lane group g = lane / (32 / cl)
+        // sends the 16-byte chunks of this CTA's new h slice to cluster CTA g
+        // (DSMEM stores), then each lane release-arrives once on that CTA's
+        // "full" barrier: the groups' releases proceed in parallel, and
+        // every barrier receives 32 / cl arrivals from each of the cl CTAs.
+        if (tid < 32) {
+            const int per = 32 / cl;
+            const int r = tid / per, sub = tid % per;
+            float* hnext = hbuf + (size_t)nxt * B * H;
+            for (int c = sub; c < nchunk; c += per) {
+                const int b = (4 * c) / U, j = (4 * c) % U;
+                const float4 v = reinterpret_cast<const float4*>(hstage)[c];
+                *reinterpret_cast<float4*>(cluster.map_shared_rank(hnext + (size_t)b * H + q * U + j, r)) = v;
             }
+            sm100::mbar_arrive_remote(sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8);
         }
     }
     // h_T (written by every CTA of the cluster into this CTA's buffer T % 2)
@@ -438,7 +472,8 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
 
 size_t rnn_reg_smem(int B, int H, int G, int cl) {
     const int U = H / cl, R = G * U;
-    const size_t f = 2 * (size_t)B * H + (size_t)B * R + (((size_t)B * U + 1) & ~(size_t)1);
+    const size_t bu4 = ((size_t)B * U + 3) & ~(size_t)3;
+    const size_t f = 2 * (size_t)B * H + (size_t)B * R + 2 * bu4;
     return f * sizeof(float) + 2 * sizeof(uint64_t) + 16;
 }
 
