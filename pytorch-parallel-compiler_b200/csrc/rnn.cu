@@ -242,16 +242,17 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
 // the 16-byte words k4 = i*8 + p (i < KS = H/32) of rows g + 32r (r < RPT),
 // so each step's mat-vec reads only h from shared memory (one 16-byte word
 // per k-slice and batch row) and reduces the 8 partial sums by shuffles.
-// The new h slice goes into every cluster CTA's next buffer by DSMEM stores,
-// each group of lanes followed by release-arrives on that CTA's "full"
-// mbarrier of the buffer; a CTA starts step t once its buffer for h_t has
-// all 32 arrivals (acquire at cluster scope). A two-deep buffer ring is
+// The new h slice goes into every cluster CTA's next buffer by asynchronous
+// DSMEM stores (st.async) that complete their bytes on that CTA's "full"
+// mbarrier of the buffer; a CTA posts the B*H*4 bytes it expects for h_{t+1}
+// at the start of step t and starts step t+1 once they have all landed. A two-deep buffer ring is
 // enough: a CTA writes h_{t+2} into a peer only after receiving that peer's
 // h_{t+1}, which the peer produced after its step-t mat-vec finished
 // reading the buffer. Every wait is bounded (device error + abort flag).
 // ---------------------------------------------------------------------------
 constexpr int kRegThreads = 256;
 constexpr int kRegParts = 8;
+constexpr int kPublishers = 128;    // threads that send the h slice (kPublishers / cl per destination)
 
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort) {
     const uint32_t addr = sm100::smem_addr(bar);
@@ -325,12 +326,13 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             cst[i] = a.c0 ? to_f<T>(static_cast<const T*>(a.c0)[((size_t)model * B + b) * H + q * U + j]) : 0.f;
         }
     }
-    // 16-byte chunks of the h slice; warp 0 publishes them (32 arrivals per
-    // barrier phase: 32 / cl lanes of each of the cl CTAs).
+    // 16-byte chunks of the h slice; warps 0-3 publish them. Each "full"
+    // phase has one arrival (this CTA's expect_tx of the B*H*4 bytes that
+    // the cl CTAs' asynchronous stores complete).
     const int nchunk = (B * U) / 4;
     if (tid == 0) {
-        sm100::mbar_init(&full[0], 32u);
-        sm100::mbar_init(&full[1], 32u);
+        sm100::mbar_init(&full[0], 1u);
+        sm100::mbar_init(&full[1], 1u);
         *abort_flag = 0;
         sm100::mbar_init_fence();
     }
@@ -350,8 +352,9 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
     if (pre && tid < bu && a.T > 0) load_gx(tid, 0, gx_next);
 
     bool ok = true;
+    int posted = 0;          // last h index whose bytes this CTA expects
     for (int t = 0; t < a.T; ++t) {
-        // One thread waits for h_t (all 32 arrivals); the barrier
+        // One thread waits for h_t (all B*H*4 bytes landed); the barrier
         // then releases the CTA, and every thread sees the same verdict.
         if (t > 0 && tid == 0 && !mbar_wait_cluster(&full[t & 1], (uint32_t)(((t - 1) >> 1) & 1), abort_flag))
             *abort_flag = 1;
@@ -360,6 +363,11 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             ok = false;
             break;
         }
+        // The buffer that receives h_{t+1}: its previous phase (h_{t-1})
+        // completed before step t-1, and no CTA can send h_{t+1} before it
+        // has this CTA's h_t.
+        if (tid == 0) sm100::mbar_arrive_expect_tx(&full[(t + 1) & 1], (uint32_t)(B * H * 4));
+        posted = t + 1;
         const float* hc = hbuf + (size_t)(t & 1) * B * H;
         const int nxt = (t + 1) & 1;
         float gx_cur[4] = {gx_next[0], gx_next[1], gx_next[2], gx_next[3]};
@@ -436,21 +444,24 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             out[((size_t)b * a.T + t) * H + ju] = hs;
         }
         __syncthreads();
-        // 3. warp 0 publishes the slice: lane group g = lane / (32 / cl)
+        // 3. warps 0-3 publish the slice: thread group g = tid / (128 / cl)
         // sends the 16-byte chunks of this CTA's new h slice to cluster CTA g
-        // (DSMEM stores), then each lane release-arrives once on that CTA's
-        // "full" barrier: the groups' releases proceed in parallel, and
-        // every barrier receives 32 / cl arrivals from each of the cl CTAs.
-        if (tid < 32) {
-            const int per = 32 / cl;
+        // as asynchronous DSMEM stores that complete bytes on that CTA's
+        // "full" mbarrier (no fence, no per-thread release).
+        if (tid < kPublishers) {
+            const int per = kPublishers / cl;
             const int r = tid / per, sub = tid % per;
             float* hnext = hbuf + (size_t)nxt * B * H;
+            const uint32_t rbar = sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8;
             for (int c = sub; c < nchunk; c += per) {
                 const int b = (4 * c) / U, j = (4 * c) % U;
                 const float4 v = reinterpret_cast<const float4*>(hstage)[c];
-                *reinterpret_cast<float4*>(cluster.map_shared_rank(hnext + (size_t)b * H + q * U + j, r)) = v;
+                const uint32_t dst = sm100::map_to_rank(sm100::smem_addr(hnext + (size_t)b * H + q * U + j), (uint32_t)r);
+                asm volatile(
+                    "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                    ::"r"(dst), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+                    : "memory");
             }
-            sm100::mbar_arrive_remote(sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8);
         }
     }
     // h_T (written by every CTA of the cluster into this CTA's buffer T % 2)
@@ -458,7 +469,13 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
         !mbar_wait_cluster(&full[a.T & 1], (uint32_t)(((a.T - 1) >> 1) & 1), abort_flag))
         *abort_flag = 1;
     __syncthreads();
-    if (tid == 0 && *abort_flag) raise_device_error(err, DEV_ERR_RNN_TIMEOUT);
+    if (tid == 0 && *abort_flag) {
+        raise_device_error(err, DEV_ERR_RNN_TIMEOUT);
+        // Stores other CTAs may still have in flight into the phase this CTA
+        // posted last land (bounded wait) before its shared memory goes away.
+        const volatile int never = 0;
+        if (posted > 0) mbar_wait_cluster(&full[posted & 1], (uint32_t)(((posted - 1) >> 1) & 1), &never);
+    }
     const float* hl = hbuf + (size_t)(a.T & 1) * B * H;
     for (int i = tid; i < bu; i += blockDim.x) {
         const int b = i / U, j = i % U;
