@@ -378,11 +378,10 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
         const float4* H4 = reinterpret_cast<const float4*>(hc);
         for (int b0 = 0; b0 < B; b0 += 4) {
             const int nb = B - b0 < 4 ? B - b0 : 4;
-            float acc[4][RPT];
+            // v[bb*4 + r]: batch row b0+bb, gate row grp + 32r (rows past RPT stay 0)
+            float v[16];
 #pragma unroll
-            for (int bb = 0; bb < 4; ++bb)
-#pragma unroll
-                for (int r = 0; r < RPT; ++r) acc[bb][r] = 0.f;
+            for (int k = 0; k < 16; ++k) v[k] = 0.f;
 #pragma unroll
             for (int i = 0; i < KS; ++i) {
                 float4 hv[4];
@@ -393,28 +392,53 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
                 for (int bb = 0; bb < 4; ++bb)
 #pragma unroll
                     for (int r = 0; r < RPT; ++r) {
-                        float s2 = acc[bb][r];
+                        float s2 = v[bb * 4 + r];
                         s2 = fmaf(wr[r][i].x, hv[bb].x, s2);
                         s2 = fmaf(wr[r][i].y, hv[bb].y, s2);
                         s2 = fmaf(wr[r][i].z, hv[bb].z, s2);
                         s2 = fmaf(wr[r][i].w, hv[bb].w, s2);
-                        acc[bb][r] = s2;
+                        v[bb * 4 + r] = s2;
                     }
             }
+            // Recursive halving over the 8 lanes of the row group: each level
+            // keeps the half of the values selected by one bit of the lane
+            // part and adds the partner's copy of it (8 + 4 + 2 shuffles for
+            // 16 sums); lane part p ends with values 2p and 2p + 1.
+            float v8[8], v4[4], v2[2];
+            {
+                const bool hb = (p >> 2) & 1;
 #pragma unroll
-            for (int off = kRegParts / 2; off > 0; off >>= 1)
+                for (int k = 0; k < 8; ++k) {
+                    const float send = hb ? v[k] : v[k + 8], keep = hb ? v[k + 8] : v[k];
+                    v8[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                }
+            }
+            {
+                const bool hb = (p >> 1) & 1;
 #pragma unroll
-                for (int bb = 0; bb < 4; ++bb)
+                for (int k = 0; k < 4; ++k) {
+                    const float send = hb ? v8[k] : v8[k + 4], keep = hb ? v8[k + 4] : v8[k];
+                    v4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+                }
+            }
+            {
+                const bool hb = p & 1;
 #pragma unroll
-                    for (int r = 0; r < RPT; ++r) acc[bb][r] += __shfl_xor_sync(0xffffffffu, acc[bb][r], off);
-            if (p == 0) {
+                for (int k = 0; k < 2; ++k) {
+                    const float send = hb ? v4[k] : v4[k + 2], keep = hb ? v4[k + 2] : v4[k];
+                    v2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+                }
+            }
 #pragma unroll
-                for (int bb = 0; bb < 4; ++bb)
+            for (int k = 0; k < 2; ++k) {
+                const int idx = 2 * p + k, bb = idx >> 2, r = idx & 3;
+                const int lr = grp + 32 * r;
+                if (r < RPT && bb < nb && lr < R) {
+                    float bias = brow[0];
 #pragma unroll
-                    for (int r = 0; r < RPT; ++r) {
-                        const int lr = grp + 32 * r;
-                        if (bb < nb && lr < R) gates[(size_t)(b0 + bb) * R + lr] = acc[bb][r] + brow[r];
-                    }
+                    for (int rr = 1; rr < RPT; ++rr) bias = r == rr ? brow[rr] : bias;
+                    gates[(size_t)(b0 + bb) * R + lr] = v2[k] + bias;
+                }
             }
         }
         __syncthreads();
