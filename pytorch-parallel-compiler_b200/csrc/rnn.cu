@@ -35,6 +35,12 @@ namespace widek {
 namespace {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
+// Short-latency forms for the register-resident kernel's critical path: the
+// exponential intrinsic and an approximate divide for the logistic, and tanh
+// from the identity tanh(x) = 2 * sigmoid(2x) - 1 (absolute error ~1e-7 near
+// 0, far inside the fp32 contract's 1e-4).
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+__device__ __forceinline__ float tanh_fast(float x) { return 2.f * sigmoid_fast(2.f * x) - 1.f; }
 
 struct RnnArgs {
     const void* gx;      // [n, batch, T, G*H]
@@ -450,18 +456,18 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             if (!pre) load_gx(i, t, gx_cur);
             float hnew;
             if (!LSTM) {
-                const float r = sigmoidf_(gx_cur[0] + gr[j]);
-                const float z = sigmoidf_(gx_cur[1] + gr[U + j]);
-                const float nn = tanhf(gx_cur[2] + r * gr[2 * U + j]);
+                const float r = sigmoid_fast(gx_cur[0] + gr[j]);
+                const float z = sigmoid_fast(gx_cur[1] + gr[U + j]);
+                const float nn = tanh_fast(gx_cur[2] + r * gr[2 * U + j]);
                 hnew = (1.f - z) * nn + z * hc[(size_t)b * H + ju];
             } else {
-                const float ig = sigmoidf_(gx_cur[0] + gr[j]);
-                const float fg = sigmoidf_(gx_cur[1] + gr[U + j]);
-                const float gg = tanhf(gx_cur[2] + gr[2 * U + j]);
-                const float og = sigmoidf_(gx_cur[3] + gr[3 * U + j]);
+                const float ig = sigmoid_fast(gx_cur[0] + gr[j]);
+                const float fg = sigmoid_fast(gx_cur[1] + gr[U + j]);
+                const float gg = tanh_fast(gx_cur[2] + gr[2 * U + j]);
+                const float og = sigmoid_fast(gx_cur[3] + gr[3 * U + j]);
                 const float c = fg * cst[i] + ig * gg;
                 cst[i] = c;
-                hnew = og * tanhf(c);
+                hnew = og * tanh_fast(c);
             }
             const T hs = from_f<T>(hnew);
             hstage[i] = to_f<T>(hs);
