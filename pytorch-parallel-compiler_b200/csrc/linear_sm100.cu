@@ -32,16 +32,18 @@ using namespace sm100;
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;       // CTA-pair kernel: TMA warp, MMA warp, 4 epilogue warps
+constexpr int kGemmThreads = 320;   // single-CTA kernel: TMA warp, MMA warp, 2 x 4 epilogue warps
 
 template <int BN, int STAGES, bool TMA_STORE = false>
 struct GemmSmem {
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t RING = STAGES * (A_BYTES + B_BYTES);
-    // Output staging for the TMA store: two buffers of 128 rows x 32 columns.
+    // Output staging for the TMA store: per epilogue warpgroup two buffers of
+    // 128 rows x 32 columns.
     static constexpr uint32_t OUT_CHUNK = BM * 32 * 2;
-    static constexpr uint32_t OUT_BYTES = TMA_STORE ? 2 * OUT_CHUNK : 0;
+    static constexpr uint32_t OUT_BYTES = TMA_STORE ? 4 * OUT_CHUNK : 0;
     static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 4 + 1) + 16;
     static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + BAR_BYTES;  // 1024: alignment slack
 };
@@ -57,9 +59,11 @@ __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of one 128-thread epilogue warpgroup (ids 1 and 2).
+__device__ __forceinline__ void wg_bar_sync(int wg) { asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory"); }
 
 template <typename T, int BN, int STAGES, bool TMA_STORE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias, T* __restrict__ y,
                      int n_models, int M, int K, int O, int act, int vec_store, int l2_hints, int* err) {
@@ -94,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4 * 32);
+            mbar_init(&tempty[a], 8 * 32);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -200,15 +204,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ------------------------------------------------------------------
-        // Epilogue: warps 2..5 own TMEM lane quarters (warp % 4). Per
-        // 32-column chunk: lane j fetches bias[col0 + j] once (broadcast by
-        // shuffles); with TMA_STORE the chunk (128 rows x 64 B) is staged in
-        // shared memory (64-byte swizzle, double-buffered) and written by one
-        // TMA store, so the SM issues full-line writes instead of 16-byte
-        // pieces scattered over 32 rows per instruction.
+        // Epilogue: two warpgroups (warps 2..5 and 6..9), each warp owning
+        // the TMEM lane quarter warp % 4; warpgroup g finishes the column
+        // half [g*BN/2, (g+1)*BN/2) of the tile, so the two halves drain in
+        // parallel. Per 32-column chunk: lane j fetches bias[col0 + j] once
+        // (broadcast by shuffles); with TMA_STORE the chunk (128 rows x 64 B)
+        // is staged in the warpgroup's shared memory (64-byte swizzle,
+        // double-buffered) and written by one TMA store, so the SM issues
+        // full-line writes instead of 16-byte pieces scattered over 32 rows
+        // per instruction.
         // ------------------------------------------------------------------
         const int q = warp & 3;
-        const int ep_tid = threadIdx.x - 64;
+        const int wg = (warp - 2) >> 2;
+        const int ep_tid = threadIdx.x - 64 - 128 * wg;
+        uint8_t* sOutW = sOut + wg * 2 * S::OUT_CHUNK;
         int local = 0;
         int oc = 0;                               // chunks stored so far (buffer parity)
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
@@ -230,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             T* yrow = y + ((int64_t)model * M + (row_ok ? row : 0)) * O;
             const T* brow = bias ? bias + (int64_t)model * O : nullptr;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = wg * (BN / 2); c < (wg + 1) * (BN / 2); c += 32) {
                 const int col0 = nt * BN + c;
                 if (col0 >= O) break;  // warp-uniform
                 uint32_t r[32];
@@ -242,16 +251,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 32; ++j)
                     v[j] = apply_act(__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j), act);
                 if (TMA_STORE) {
-                    uint8_t* buf = sOut + (oc & 1) * S::OUT_CHUNK;
+                    uint8_t* buf = sOutW + (oc & 1) * S::OUT_CHUNK;
                     if (ep_tid == 0) bulk_wait_read1();       // the store that used this buffer has read it
-                    epi_bar_sync();
+                    wg_bar_sync(wg);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int phys = j ^ ((rloc >> 1) & 3);
                         store16<T>(reinterpret_cast<T*>(buf + rloc * 64 + phys * 16), v + 8 * j);
                     }
                     fence_proxy_async_smem();
-                    epi_bar_sync();
+                    wg_bar_sync(wg);
                     if (ep_tid == 0) {
                         tma_store_3d(&tm_y, buf, col0, mt * BM, model);
                         bulk_commit();
@@ -573,7 +582,7 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
     const int64_t tiles = n * ((m + BM - 1) / BM) * ((o + BN - 1) / BN);
     const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
     const int vec_store = (o % 8 == 0) && aligned16(y);
-    kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw, ty, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
+    kern<<<grid, kGemmThreads, S::TOTAL, st>>>(tx, tw, ty, bias, y, (int)n, (int)m, (int)k, (int)o, act, vec_store,
                                            g_linear_variant == 4 ? 0 : 1, device_error_ptr());
     return check_launch("widek_linear_fwd (tcgen05)");
 }
