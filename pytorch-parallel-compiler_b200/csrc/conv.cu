@@ -27,6 +27,7 @@
 // CUDA-core path (everything else, including fp32): direct convolution, one
 // output element per thread, fp32 accumulation.
 #include <cstring>
+#include <type_traits>
 
 #include "sm100_ptx.cuh"
 
@@ -527,6 +528,25 @@ struct ConvHaloGeom {
     int64_t tiles;
 };
 
+// Activations of the halo epilogues. GELU (erf) is out of line so that the
+// unrolled loops do not carry one copy of erff per value. The channels-last
+// epilogue fixes the activation at compile time (one copy of its loop per
+// activation, picked once per tile); the N-first / packed epilogue keeps the
+// runtime test, which measured faster there (its shared-memory accesses
+// then spread out instead of competing in bursts with the MMA operand reads).
+__device__ __noinline__ float conv_gelu(float v) { return gelu_erf(v); }
+template <int ACT>
+__device__ __forceinline__ float conv_act(float v) {
+    if constexpr (ACT == WIDEK_ACT_RELU) return v > 0.f ? v : 0.f;
+    else if constexpr (ACT == WIDEK_ACT_GELU) return conv_gelu(v);
+    else return v;
+}
+__device__ __forceinline__ float conv_act_rt(float v, int act) {
+    if (act == WIDEK_ACT_RELU) return v > 0.f ? v : 0.f;
+    if (act == WIDEK_ACT_GELU) return conv_gelu(v);
+    return v;
+}
+
 // Two output tile buffers, used by alternate tiles, so that a tile's
 // epilogue only waits for the store issued two tiles earlier. With a
 // TMA-loaded residual each buffer first receives the tile's residual
@@ -768,6 +788,13 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         const bool res = RES_TMA && e.residual != nullptr;
         int64_t par_key = -1;
         int res_issued = 0;
+        // Channels-last output: threads t and t + 16 of a warp share a pixel
+        // (the 16x32bx2 TMEM read), t < 16 taking channels [0, 32) and
+        // t >= 16 channels [32, 64); the lane's 32 channels' (scale, offset)
+        // pairs stay in registers. The N-first / packed output reads them
+        // from shared memory.
+        const int ch_half = lane >> 4;
+        float ps[OUT_CL ? HBN / 2 : 1], po[OUT_CL ? HBN / 2 : 1];
         // Residual tile of `tile` into buffer `rb` (elected thread only).
         auto load_residual = [&](int64_t tile, int rb) {
             int model, nt, b, mt;
@@ -791,7 +818,6 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             const uint32_t aph = (local >> 1) & 1;
             const int buf = local & 1;
             T* sOut = sBuf + buf * (HBN * BM);
-            const int r = q * 32 + lane;
             const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
             const int64_t img = (int64_t)model * g.batch + b;
             // Without a residual: the store issued two tiles ago (from this
@@ -808,18 +834,27 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 }
             }
             const int64_t key = (int64_t)model * g.nt_count + nt;
-            if (key != par_key) {
+            const bool fresh = key != par_key;
+            if (fresh) {
                 // every read of the previous pairs finished before the last tile's second barrier
                 if (ep_tid < HBN) {
                     const int64_t ch = (int64_t)model * g.cout + nt * HBN + ep_tid;
                     const float pb = bias ? to_f<T>(bias[ch]) : 0.f;
-                    const float ps = scale ? to_f<T>(scale[ch]) : 1.f;
+                    const float sc = scale ? to_f<T>(scale[ch]) : 1.f;
                     const float pt = shift ? to_f<T>(shift[ch]) : 0.f;
-                    sPar[ep_tid] = make_float2(ps, pb * ps + pt);
+                    sPar[ep_tid] = make_float2(sc, pb * sc + pt);
                 }
                 par_key = key;
             }
             epi_bar_sync();
+            if (OUT_CL && fresh) {
+#pragma unroll
+                for (int m = 0; m < (OUT_CL ? HBN / 2 : 0); ++m) {
+                    const float2 pp = sPar[32 * ch_half + m];
+                    ps[m] = pp.x;
+                    po[m] = pp.y;
+                }
+            }
             if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
@@ -831,37 +866,60 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
                 break;
             }
+            if constexpr (OUT_CL) {
+                auto epilogue = [&](auto act_c) {
+                    constexpr int ACT = decltype(act_c)::value;
+#pragma unroll
+                    for (int hs = 0; hs < 2; ++hs) {
+                        // pixels q*32 + 16*hs + (lane % 16)
+                        uint32_t v[32];
+                        tmem_ld_16x32bx2_x32_split32(
+                            tmem_base + (uint32_t)(acc * HBN) + ((uint32_t)(q * 32 + 16 * hs) << 16), v);
+                        tmem_ld_wait();
+                        float ov[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) ov[j] = conv_act<ACT>(fmaf(__uint_as_float(v[j]), ps[j], po[j]));
+                        // channels-last staging: pixel p's 64 channels form
+                        // one 128-byte row, 16-byte unit u stored at
+                        // u ^ (p % 8) (the 128-byte swizzle the TMA store reads).
+                        const int px = q * 32 + 16 * hs + (lane & 15);
+                        uint8_t* row = reinterpret_cast<uint8_t*>(sOut) + px * 128;
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            store16<T>(reinterpret_cast<T*>(row + (((4 * ch_half + u) ^ (px & 7)) << 4)),
+                                       ov + 8 * u);
+                    }
+                };
+                if (e.act == WIDEK_ACT_RELU)
+                    epilogue(std::integral_constant<int, WIDEK_ACT_RELU>{});
+                else if (e.act == WIDEK_ACT_GELU)
+                    epilogue(std::integral_constant<int, WIDEK_ACT_GELU>{});
+                else
+                    epilogue(std::integral_constant<int, WIDEK_ACT_NONE>{});
+            } else {
+                const int r = q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < HBN; c += 32) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * HBN + c) + ((uint32_t)(q * 32) << 16), v);
-                // The chunk's 32 residual values are read before any of its
-                // outputs is written over them.
-                float rv[32];
-                if (res) {
+                for (int c = 0; c < HBN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * HBN + c) + ((uint32_t)(q * 32) << 16), v);
+                    // The chunk's 32 residual values are read before any of
+                    // its outputs is written over them.
+                    float rv[32];
+                    if (res) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) rv[j] = to_f<T>(sOut[(c + j) * BM + r]);
-                }
-                tmem_ld_wait();
-                float ov[32];
+                        for (int j = 0; j < 32; ++j) rv[j] = to_f<T>(sOut[(c + j) * BM + r]);
+                    }
+                    tmem_ld_wait();
+                    float ov[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float2 par = sPar[c + j];
-                    float val = fmaf(__uint_as_float(v[j]), par.x, par.y);
-                    if (res && e.residual_first) val += rv[j];
-                    val = apply_act(val, e.act);
-                    if (res && !e.residual_first) val += rv[j];
-                    ov[j] = val;
-                }
-                if (OUT_CL) {
-                    // channels-last staging: pixel r's 64 channels form one
-                    // 128-byte row, 16-byte unit u stored at u ^ (r % 8)
-                    // (the 128-byte swizzle the TMA store reads).
-                    uint8_t* row = reinterpret_cast<uint8_t*>(sOut) + r * 128;
-#pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        store16<T>(reinterpret_cast<T*>(row + ((((c >> 3) + u) ^ (r & 7)) << 4)), ov + 8 * u);
-                } else {
+                    for (int j = 0; j < 32; ++j) {
+                        const float2 par = sPar[c + j];
+                        float val = fmaf(__uint_as_float(v[j]), par.x, par.y);
+                        if (res && e.residual_first) val += rv[j];
+                        val = conv_act_rt(val, e.act);
+                        if (res && !e.residual_first) val += rv[j];
+                        ov[j] = val;
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) sOut[(c + j) * BM + r] = from_f<T>(ov[j]);
                 }
