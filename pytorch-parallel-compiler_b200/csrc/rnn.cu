@@ -249,16 +249,17 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
 // so each step's mat-vec reads only h from shared memory (one 16-byte word
 // per k-slice and batch row) and reduces the 8 partial sums by shuffles.
 // The new h slice goes into every cluster CTA's next buffer by asynchronous
-// DSMEM stores (st.async) that complete their bytes on that CTA's "full"
+// DSMEM stores (st.async, sent by the lanes of the gate math as soon as a
+// 16-byte chunk is complete) that complete their bytes on that CTA's "full"
 // mbarrier of the buffer; a CTA posts the B*H*4 bytes it expects for h_{t+1}
-// at the start of step t and starts step t+1 once they have all landed. A two-deep buffer ring is
-// enough: a CTA writes h_{t+2} into a peer only after receiving that peer's
-// h_{t+1}, which the peer produced after its step-t mat-vec finished
-// reading the buffer. Every wait is bounded (device error + abort flag).
+// at the start of step t and starts step t+1 once they have all landed. A
+// two-deep buffer ring is enough: a CTA writes h_{t+2} into a peer only
+// after receiving all of that peer's h_{t+1}, whose chunks the peer sent
+// after its step-t reads of the buffer (mat-vec and gate math) had returned.
+// Every wait is bounded (device error + abort flag).
 // ---------------------------------------------------------------------------
 constexpr int kRegThreads = 256;
 constexpr int kRegParts = 8;
-constexpr int kPublishers = 128;    // threads that send the h slice (kPublishers / cl per destination)
 
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort) {
     const uint32_t addr = sm100::smem_addr(bar);
@@ -296,8 +297,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
     float* hbuf = rsm;                                         // [2][B][H]
     float* gates = hbuf + 2 * (size_t)B * H;                   // [B][R]
     float* cst = gates + (size_t)B * R;                        // [B][U] (LSTM)
-    float* hstage = cst + (((size_t)B * U + 3) & ~(size_t)3);  // [B][U]: this CTA's new h slice
-    uint64_t* full = reinterpret_cast<uint64_t*>(hstage + (((size_t)B * U + 3) & ~(size_t)3));   // [2]
+    uint64_t* full = reinterpret_cast<uint64_t*>(cst + (((size_t)B * U + 3) & ~(size_t)3));   // [2]
     volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
 
     const T* gx = static_cast<const T*>(a.gx) + (size_t)model * B * a.T * G * H;
@@ -332,10 +332,9 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             cst[i] = a.c0 ? to_f<T>(static_cast<const T*>(a.c0)[((size_t)model * B + b) * H + q * U + j]) : 0.f;
         }
     }
-    // 16-byte chunks of the h slice; warps 0-3 publish them. Each "full"
-    // phase has one arrival (this CTA's expect_tx of the B*H*4 bytes that
-    // the cl CTAs' asynchronous stores complete).
-    const int nchunk = (B * U) / 4;
+    // Each "full" phase has one arrival (this CTA's expect_tx of the B*H*4
+    // bytes that the cl CTAs' asynchronous stores of 16-byte h chunks
+    // complete).
     if (tid == 0) {
         sm100::mbar_init(&full[0], 1u);
         sm100::mbar_init(&full[1], 1u);
@@ -448,49 +447,60 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
             }
         }
         __syncthreads();
-        // 2. gate math for (b, j); 3. publish h into every cluster CTA
-        for (int i = tid; i < bu; i += blockDim.x) {
-            const int b = i / U, j = i % U;
-            const int ju = q * U + j;
-            const float* gr = gates + (size_t)b * R;
-            if (!pre) load_gx(i, t, gx_cur);
-            float hnew;
-            if (!LSTM) {
-                const float r = sigmoid_fast(gx_cur[0] + gr[j]);
-                const float z = sigmoid_fast(gx_cur[1] + gr[U + j]);
-                const float nn = tanh_fast(gx_cur[2] + r * gr[2 * U + j]);
-                hnew = (1.f - z) * nn + z * hc[(size_t)b * H + ju];
-            } else {
-                const float ig = sigmoid_fast(gx_cur[0] + gr[j]);
-                const float fg = sigmoid_fast(gx_cur[1] + gr[U + j]);
-                const float gg = tanh_fast(gx_cur[2] + gr[2 * U + j]);
-                const float og = sigmoid_fast(gx_cur[3] + gr[3 * U + j]);
-                const float c = fg * cst[i] + ig * gg;
-                cst[i] = c;
-                hnew = og * tanh_fast(c);
+        // 2. gate math for (b, j), then 3. publish: lanes 4m..4m+3 hold one
+        // 16-byte chunk of the new h slice (4 consecutive j of one batch row;
+        // U % 4 == 0, so a chunk never straddles rows or the end), gather it
+        // by shuffles, and lane 4m+k sends it to cluster ranks k, k+4, ... as
+        // asynchronous DSMEM stores that complete bytes on that CTA's "full"
+        // mbarrier. No barrier separates the gate math from the publish:
+        // the h_{t+1} chunks overwrite a peer's h_{t-1} buffer, and this CTA
+        // reaches this point only with the peer's whole h_t, whose last chunk
+        // the peer sent after its last read of h_{t-1} (a lane's loads are
+        // consumed before its stores issue).
+        float* hnext = hbuf + (size_t)nxt * B * H;
+        const int lane = tid & 31;
+        for (int base = 0; base < bu; base += (int)blockDim.x) {
+            const int i = base + tid;
+            const bool on = i < bu;     // the same for the 4 lanes of a chunk
+            float hval = 0.f;
+            if (on) {
+                const int b = i / U, j = i % U;
+                const int ju = q * U + j;
+                const float* gr = gates + (size_t)b * R;
+                if (!pre) load_gx(i, t, gx_cur);
+                float hnew;
+                if (!LSTM) {
+                    const float r = sigmoid_fast(gx_cur[0] + gr[j]);
+                    const float z = sigmoid_fast(gx_cur[1] + gr[U + j]);
+                    const float nn = tanh_fast(gx_cur[2] + r * gr[2 * U + j]);
+                    hnew = (1.f - z) * nn + z * hc[(size_t)b * H + ju];
+                } else {
+                    const float ig = sigmoid_fast(gx_cur[0] + gr[j]);
+                    const float fg = sigmoid_fast(gx_cur[1] + gr[U + j]);
+                    const float gg = tanh_fast(gx_cur[2] + gr[2 * U + j]);
+                    const float og = sigmoid_fast(gx_cur[3] + gr[3 * U + j]);
+                    const float c = fg * cst[i] + ig * gg;
+                    cst[i] = c;
+                    hnew = og * tanh_fast(c);
+                }
+                const T hs = from_f<T>(hnew);
+                hval = to_f<T>(hs);
+                out[((size_t)b * a.T + t) * H + ju] = hs;
             }
-            const T hs = from_f<T>(hnew);
-            hstage[i] = to_f<T>(hs);
-            out[((size_t)b * a.T + t) * H + ju] = hs;
-        }
-        __syncthreads();
-        // 3. warps 0-3 publish the slice: thread group g = tid / (128 / cl)
-        // sends the 16-byte chunks of this CTA's new h slice to cluster CTA g
-        // as asynchronous DSMEM stores that complete bytes on that CTA's
-        // "full" mbarrier (no fence, no per-thread release).
-        if (tid < kPublishers) {
-            const int per = kPublishers / cl;
-            const int r = tid / per, sub = tid % per;
-            float* hnext = hbuf + (size_t)nxt * B * H;
-            const uint32_t rbar = sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8;
-            for (int c = sub; c < nchunk; c += per) {
-                const int b = (4 * c) / U, j = (4 * c) % U;
-                const float4 v = reinterpret_cast<const float4*>(hstage)[c];
-                const uint32_t dst = sm100::map_to_rank(sm100::smem_addr(hnext + (size_t)b * H + q * U + j), (uint32_t)r);
-                asm volatile(
-                    "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-                    ::"r"(dst), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
-                    : "memory");
+            const int g0 = lane & ~3;
+            const float v0 = __shfl_sync(0xffffffffu, hval, g0), v1 = __shfl_sync(0xffffffffu, hval, g0 + 1),
+                        v2 = __shfl_sync(0xffffffffu, hval, g0 + 2), v3 = __shfl_sync(0xffffffffu, hval, g0 + 3);
+            if (on) {
+                const int c0 = i & ~3, b = c0 / U, j = c0 % U;
+                const uint32_t src = sm100::smem_addr(hnext + (size_t)b * H + q * U + j);
+                for (int r = lane & 3; r < cl; r += 4) {
+                    const uint32_t dst = sm100::map_to_rank(src, (uint32_t)r);
+                    const uint32_t rbar = sm100::map_to_rank(full0, (uint32_t)r) + nxt * 8;
+                    asm volatile(
+                        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                        ::"r"(dst), "f"(v0), "f"(v1), "f"(v2), "f"(v3), "r"(rbar)
+                        : "memory");
+                }
             }
         }
     }
@@ -520,7 +530,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
 size_t rnn_reg_smem(int B, int H, int G, int cl) {
     const int U = H / cl, R = G * U;
     const size_t bu4 = ((size_t)B * U + 3) & ~(size_t)3;
-    const size_t f = 2 * (size_t)B * H + (size_t)B * R + 2 * bu4;
+    const size_t f = 2 * (size_t)B * H + (size_t)B * R + bu4;
     return f * sizeof(float) + 2 * sizeof(uint64_t) + 16;
 }
 
