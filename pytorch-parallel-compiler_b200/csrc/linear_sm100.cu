@@ -28,6 +28,21 @@
 namespace widek {
 namespace {
 
+// Activation over one 32-value epilogue chunk: one uniform test per chunk,
+// so the per-value loops carry no branch (a branch or call per value keeps
+// the compiler from scheduling the shuffles, adds and stores across it);
+// GELU (erf) is an out-of-line call.
+__device__ __noinline__ float gemm_gelu(float v) { return gelu_erf(v); }
+__device__ __forceinline__ void act_chunk(float (&v)[32], int act) {
+    if (act == WIDEK_ACT_RELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.f ? v[j] : 0.f;
+    } else if (act == WIDEK_ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gemm_gelu(v[j]);
+    }
+}
+
 using namespace sm100;
 
 constexpr int BM = 128;
@@ -248,8 +263,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 tmem_ld_wait();
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    v[j] = apply_act(__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j), act);
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j);
+                act_chunk(v, act);
                 if (TMA_STORE) {
                     uint8_t* buf = sOutW + (oc & 1) * S::OUT_CHUNK;
                     if (ep_tid == 0) bulk_wait_read1();       // the store that used this buffer has read it
@@ -485,8 +500,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tmem_ld_wait();
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    v[j] = apply_act(__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j), act);
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j);
+                act_chunk(v, act);
                 if (TMA_STORE) {
                     // Rows past M of the last tile are clipped by the store;
                     // a 256-row tile never starts past M (row0 < M).

@@ -190,6 +190,9 @@ __device__ __forceinline__ void chain_load_layer(const ChainArgs& a, int l, int 
     }
 }
 
+// GELU (erf) out of line, so that the unrolled tiles stay small.
+__device__ __noinline__ float chain_gelu(float v) { return gelu_erf(v); }
+
 // One layer for this CTA's rows: nxt[r][o] = act(cur[r] . W[o] + bias[o]).
 // A warp tile is 16 rows x 8U outputs; lane = 8 * rg + g computes rows
 // rg + 4i (i < 4) and outputs g + 8j (j < U). Each float4 load of a k step
@@ -249,6 +252,18 @@ __device__ __forceinline__ void chain_layer(const ChainArgs& a, int l, const flo
 #pragma unroll
                 for (int j = 0; j < U; ++j) acc[i][j] = fmaf(xv[i].w, wv[j].w, acc[i][j]);
         }
+        // activation: one uniform test per tile, branch-free per value
+        if (act == WIDEK_ACT_RELU) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < U; ++j) acc[i][j] = acc[i][j] > 0.f ? acc[i][j] : 0.f;
+        } else if (act == WIDEK_ACT_GELU) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < U; ++j) acc[i][j] = chain_gelu(acc[i][j]);
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int r = b0 + 4 * i;
@@ -257,7 +272,7 @@ __device__ __forceinline__ void chain_layer(const ChainArgs& a, int l, const flo
             for (int j = 0; j < U; ++j) {
                 const int o = o0 + 8 * j;
                 if (o < dout)
-                    nxt[r * as + o] = to_f<T>(from_f<T>(apply_act(acc[i][j], act)));
+                    nxt[r * as + o] = to_f<T>(from_f<T>(acc[i][j]));
                 else if (o < dout4)
                     nxt[r * as + o] = 0.f;     // zero padding read by the next layer's k loop
             }
