@@ -593,11 +593,10 @@ class TracedWideModel(nn.Module):
         if g['kind'] == 'chain':
             return self._run_chain(g, xv)
         bn_mod = self.stages[g['bn'].replace('.', '_')].op
-        scale, shift = _bn_fold(bn_mod)
         w, b, st, pd, dl = self._conv_params(op)
         rv = values.get(g['residual']) if g['residual'] is not None else None
         t = xv.t if isinstance(xv, _Laid) else xv
-        scale, shift = scale.to(t.dtype), shift.to(t.dtype)
+        scale, shift = self._folded_bn(bn_mod, t.dtype)
         kw = dict(scale=scale, shift=shift, act=g['act'], residual_first=g['residual_first'])
         in_l = xv.layout if isinstance(xv, _Laid) else ops.LAYOUT_NFIRST
         res_l = rv.layout if isinstance(rv, _Laid) else ops.LAYOUT_NFIRST
@@ -630,6 +629,36 @@ class TracedWideModel(nn.Module):
         if res is not None and y.shape != res.shape:
             return None
         return y
+
+    def _folded_bn(self, bn_mod: nn.Module, dtype: torch.dtype):
+        """The eval-mode BatchNorm as (scale, shift) in `dtype`, kept from one
+        forward to the next (folding it costs about six small device
+        launches per conv group). The entry holds the module's four tensors
+        and their version counters, so replacing a tensor or changing it in
+        place (``copy_``, an optimizer step, training-mode statistics)
+        recomputes it. Nothing is cached while a CUDA graph is being
+        captured, so that a recorded graph folds the module's tensors on
+        every replay, nor for inference-mode tensors (no version counter)."""
+        tensors = (bn_mod.running_mean, bn_mod.running_var, bn_mod.weight, bn_mod.bias)
+
+        def fold():
+            scale, shift = _bn_fold(bn_mod)
+            return scale.to(dtype), shift.to(dtype)
+
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            return fold()
+        try:
+            versions = tuple(None if x is None else x._version for x in tensors)
+        except RuntimeError:
+            return fold()
+        cache = self.__dict__.setdefault('_bn_fold_cache', {})
+        hit = cache.get(id(bn_mod))
+        if (hit is not None and hit[0] == (dtype, float(bn_mod.eps), versions)
+                and all(a is b for a, b in zip(hit[1], tensors))):
+            return hit[2]
+        folded = fold()
+        cache[id(bn_mod)] = ((dtype, float(bn_mod.eps), versions), tensors, folded)
+        return folded
 
     def _clast_ok(self, nxt: Dict[str, Any], op, t: Tensor, in_l: int, w, st, pd, dl) -> bool:
         """Whether the next conv group can read this group's output in the

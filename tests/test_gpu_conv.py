@@ -183,6 +183,39 @@ def test_traced_resblock_fused_matches_unfused_bf16(post_relu):
     assert_lowp_close(y_fused, ref.double(), rtol=5e-2)
 
 
+def test_traced_fused_bn_follows_in_place_changes():
+    """The fused conv groups keep the folded BatchNorm between forwards; an
+    in-place change of its statistics or affine parameters, or a replaced
+    tensor, must show in the next forward."""
+    torch.manual_seed(4)
+    n, c = 2, 64
+    models = [_RB(c, False).to(DEV, torch.bfloat16).eval() for _ in range(n)]
+    wide = wc.compile(models, torch.randn(2, c, 16, 16, device=DEV, dtype=torch.bfloat16)).eval()
+    x = torch.randn(2, n * c, 16, 16, device=DEV).to(torch.bfloat16)
+
+    def ref():                                    # the N modules in fp32 (converted in place)
+        xs = wc.unpack(x, n)
+        return torch.cat([models[i].float()(xs[i].float()) for i in range(n)], dim=1).double()
+
+    with torch.no_grad():
+        assert_lowp_close(wide(x), ref(), rtol=5e-2)
+        assert wide._fusion['groups'], "expected fused groups"
+        wide(x)                                   # second forward: folded values reused
+        bn = wide.stages['bn1'].op
+        bn.running_mean.add_(0.5)                 # in place
+        bn.weight.mul_(1.5)
+        for i, m in enumerate(models):            # the same change in the references
+            m.bn1.running_mean.copy_(bn.running_mean[i * c:(i + 1) * c].to(torch.bfloat16))
+            m.bn1.weight.copy_(bn.weight[i * c:(i + 1) * c].to(torch.bfloat16))
+        assert_lowp_close(wide(x), ref(), rtol=5e-2)
+        bn2 = wide.stages['bn2'].op
+        bn2.running_var = bn2.running_var * 2.0   # replaced tensor
+        for i, m in enumerate(models):
+            m.bn2.running_var.copy_(bn2.running_var[i * c:(i + 1) * c].to(torch.bfloat16))
+        assert_lowp_close(wide(x), ref(), rtol=5e-2)
+    no_device_error()
+
+
 def test_traced_fusion_falls_back_in_training_mode():
     torch.manual_seed(3)
     models = [_RB(8, False).to(DEV) for _ in range(2)]
