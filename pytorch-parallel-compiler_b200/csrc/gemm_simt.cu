@@ -4,7 +4,9 @@
 // reference's tolerance is defined with TF32 off) and any bf16/f16 problem the
 // tensor-core kernel cannot take (k not a multiple of 8, unaligned pointers).
 // Classic shared-memory tiling: a CTA computes a BM x BN output tile of one
-// model; each thread owns a TM x TN register tile.
+// model; each thread owns TM consecutive rows and TN columns strided by
+// BN / TN (so that a warp's B-tile reads are consecutive words: no bank
+// conflict, and its output stores are coalesced).
 #include "common.cuh"
 
 namespace widek {
@@ -51,7 +53,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
 #pragma unroll
             for (int i = 0; i < TM; ++i) a[i] = As[kk][ty * TM + i];
 #pragma unroll
-            for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tx * TN + j];
+            for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tx + (BN / TN) * j];
 #pragma unroll
             for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         if (gm >= M) continue;
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
-            const int go = o0 + tx * TN + j;
+            const int go = o0 + tx + (BN / TN) * j;
             if (go >= O) continue;
             float v = acc[i][j];
             if (bias) v += to_f<T>(bias[(int64_t)model * O + go]);
