@@ -1,37 +1,43 @@
 """Benchmark of the wide forward path on B200 (one JSON line on rank 0).
 
-Default workload (the headline config that fits one
-GPU): WideLinear, N=64 models per GPU, in=1024, out=4096, B=256 rows per
-model, bf16 weights/activations (W ~ N(0, 1/1024), bias zeros, x ~ N(0, 1)),
-fp32 accumulation. A step is one wide forward over the whole batch: one
-launch of the tcgen05 grouped-GEMM kernel (bias fused in its epilogue).
+Headline workload: cfg3, the largest of the reference's configurations that
+fits one GPU: a TracedWideModel of N=100 ResBlocks (Conv3x3 64->64, BatchNorm
+eval, ReLU, Conv3x3, BatchNorm, + identity), B=32, 32x32, bf16, packed input
+[32, 6400, 32, 32]. A step is one wide forward over the whole batch. Every
+other configuration (cfg1 MLP, cfg2 WideLinear, cfg4 GRU/LSTM, cfg5
+attention+LN) and four memory-bound norm workloads are measured in the same
+run and reported under "configs" with the same keys.
 
-  value   samples/s = N*B*world / t_step, t_step from CUDA events over K
-          back-to-back steps with inputs resident in HBM (705 MB touched per
-          step, far above the 126 MB L2, so no flush is needed); max over ranks.
-  e2e     same metric through the public API (the module's __call__) with the
-          step's input copied host->device from pinned memory and the output
-          copied device->host inside the timed region.
-  roofline  dominant kernel's algorithmic bytes (or FLOPs) per launch / mean
-          launch time (CUDA events on the launching stream) vs the measured
-          peak in MEASURED_PEAKS.json.
-  cpu_baseline  the reference's arithmetic (its torch op sequence in the
-          config dtype) on the host cores, on a bounded sample.
+  value   samples/s = N*B / t_step; t_step from CUDA events over K
+          back-to-back steps with inputs resident in HBM; max over ranks.
+  e2e     the same metric through the public API call with the step's input
+          copied host->device from pinned memory and the output copied back
+          inside the timed region (upload, forward and download pipelined on
+          three streams, double-buffered).
+  roofline  the dominant kernel (the library entry point with the most device
+          time per step): its algorithmic FLOPs or bytes per launch over its
+          mean launch time, both from CUDA events around each launch inside
+          the timed region (a CUDA-graph replay counts as one launch), against
+          the measured peak in MEASURED_PEAKS.json.
+  cpu_baseline  the reference's op sequence (its torch arithmetic in the
+          configuration's dtype) for the whole workload, all N models, on the
+          host cores; rank 0, one GPU only.
 
-Other BASELINE configs (``--workload cfg1|cfg3|cfg4gru|cfg4lstm|cfg5``) print
-the same line for that config; ``--graph`` replays the step from a CUDA graph.
-
-Multi-GPU (torchrun, one process per GPU, NCCL): each rank runs its own set of
-models (weak scaling; the N models are independent, no collective is on the
-data path). ``--gather`` adds the optional output all-gather to every step.
+Multi-GPU (torchrun, one process per GPU, NCCL): the N models of each
+configuration are split into contiguous slices, one per rank (strong scaling:
+the total work is fixed; ``--weak`` gives every rank all N). No collective is
+on the data path; ``--gather`` adds the optional output all-gather to every
+step.
 
 ``--impl reference`` times the reference's CPU implementation of the path
-(the oracle's restatement of its torch op sequence) on rank 0 only.
+(the oracle's restatement of its torch op sequence) on rank 0 only, for the
+same configurations, each step one full forward of the whole workload.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -48,10 +54,16 @@ import torch.nn as nn  # noqa: E402
 import torch.nn.functional as F  # noqa: E402
 
 METRIC = "wide-forward samples/s (N·B/s) at 1/2/4/8 B200; % of TC/HBM roofline"
+HEADLINE = "cfg3"
+ORDER = ["cfg3", "cfg1", "cfg2", "cfg4gru", "cfg4lstm", "cfg5", "bn2d_eval", "bn2d_train", "gn", "ln"]
 
-# DRAM traffic (read + write bytes) per launch of linear_tc_kernel measured by
-# ncu on a 16-model capture scaled to 64 models; see profiles/linear_tc_cfg2.md.
-NCU_TRAFFIC_BYTES_CFG2 = 593_080_000
+# DRAM traffic (read + write bytes) per launch of the dominant kernel, from
+# one ncu capture of a reduced case scaled to the full launch by the units it
+# processes (traffic grows in proportion): None where no capture exists.
+NCU_TRAFFIC_PER_LAUNCH = {
+    # linear_tc_kernel: 148.27 MB over a 16-model cfg2 launch, x4 for 64 models
+    "cfg2": 593_080_000,
+}
 
 
 def peaks():
@@ -90,9 +102,12 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark(self):
+        return len(self.lines)
+
     def stop(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -100,9 +115,13 @@ class ClockSampler:
             self.proc.kill()
         if self._t:
             self._t.join(timeout=2)
+
+    def summary(self, start=0, end=None):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[start:end]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -126,6 +145,8 @@ def dist_env():
 
 
 def _timed_cpu(fn, seconds):
+    """Runs fn once untimed, then repeatedly until `seconds` have passed
+    (at least once); returns (reps, elapsed)."""
     fn()
     t0 = time.perf_counter()
     reps = 0
@@ -137,75 +158,108 @@ def _timed_cpu(fn, seconds):
             return reps, el
 
 
+def shard_range(n, world, rank):
+    from wide_compiler.parallel import shard_range as sr
+    return sr(n, world, rank)
+
+
 # ---------------------------------------------------------------------------
-# Workloads
+# Workloads. Each builds models [lo, hi) of its deterministic set of N models
+# (model j is initialised from seed + j, so any split of N across ranks runs
+# the same models) and that slice's resident input.
 # ---------------------------------------------------------------------------
 
 class Workload:
-    """One BASELINE config: builds the wide module and resident inputs on a
-    device, knows its per-step samples, algorithmic work and roofline."""
     name = ""
     dtype = "bf16"
-    bound = "hbm"            # roofline of the dominant kernel(s)
+    bound = "hbm"            # roofline of the dominant kernel: hbm | tensor | fp32
     peak_key = "hbm"
+    graph = False            # capture the step in a CUDA graph in the bench
+    n_total = 1
+    b = 1
 
-    def forward(self, x):
+    def setup(self, dev, lo, hi, seed):
+        raise NotImplementedError
+
+    def step(self, x):
         return self.module(x)
 
-    def traffic(self):
-        return None
+    def samples(self, n_models):
+        return n_models * self.b
+
+    def work(self, n_models):
+        """{entry point: algorithmic FLOPs (tensor / fp32 bound) or bytes (hbm
+        bound) per step} for n_models models."""
+        raise NotImplementedError
+
+    def traffic(self, n_models):
+        t = NCU_TRAFFIC_PER_LAUNCH.get(self.name)
+        return None if t is None else int(t * n_models / self.n_total)
+
+    def config(self):
+        raise NotImplementedError
+
+    def cpu_workload(self):
+        """(fn, samples per call, description): one full forward of the whole
+        workload (all N models) with the reference's op sequence on the host."""
+        raise NotImplementedError
+
+
+def _gen(seed):
+    return torch.Generator().manual_seed(seed)
 
 
 class LinearCfg2(Workload):
     name = "cfg2"
 
+    def __init__(self, n=64, b=256, i=1024, o=4096):
+        self.n_total, self.b, self.i, self.o = n, b, i, o
+
+    def _bytes(self, n):
+        return 2 * (n * self.o * self.i + n * self.b * self.i + n * self.b * self.o + n * self.o)
+
+    def work(self, n):
+        return {"widek_linear_fwd": self._bytes(n)}
+
+    def flops(self, n):
+        return 2 * n * self.b * self.i * self.o
+
+    def config(self):
+        return {"workload": f"cfg2 WideLinear N={self.n_total}, in={self.i}, out={self.o}, B={self.b} rows per "
+                            f"model, bf16, fp32 accumulate, bias fused; W ~ N(0, 1/in), bias 0, x ~ N(0, 1)",
+                "models": self.n_total, "rows_per_model": self.b,
+                "l2": "inputs larger than L2 (705 MB touched per step), no flush"}
+
+    def setup(self, dev, lo, hi, seed):
+        import wide_compiler as wc
+        n = hi - lo
+        lin = wc.WideLinear(n, self.i, self.o, bias=True).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            for k, j in enumerate(range(lo, hi)):
+                g = torch.Generator(device=dev).manual_seed(seed + j)
+                lin.weight[k].copy_(torch.randn(self.o, self.i, device=dev, generator=g) / self.i ** 0.5)
+            lin.bias.zero_()
+        self.module = lin
+        self.x = torch.empty(n, self.b, self.i, device=dev, dtype=torch.bfloat16)
+        for k, j in enumerate(range(lo, hi)):
+            g = torch.Generator(device=dev).manual_seed(seed + 100_000 + j)
+            self.x[k].copy_(torch.randn(self.b, self.i, device=dev, generator=g))
+
     def torch_reference_step(self):
-        """The reference's own GPU op sequence (wide_linear.py:162-171:
-        einsum 'noi,nbi->nbo' + bias, cuBLAS through torch) on the same inputs."""
+        """The reference's GPU op sequence (wide_linear.py:162-171: einsum
+        'noi,nbi->nbo' + bias, cuBLAS through torch) on the same inputs."""
         w, b, x = self.module.weight, self.module.bias, self.x
         return lambda: torch.einsum('noi,nbi->nbo', w, x) + b.unsqueeze(1)
 
-    def __init__(self, n=64, b=256, i=1024, o=4096):
-        self.n, self.b, self.i, self.o = n, b, i, o
-
-    def samples(self):
-        return self.n * self.b
-
-    def alg_bytes(self):
-        return 2 * (self.n * self.o * self.i + self.n * self.b * self.i + self.n * self.b * self.o + self.n * self.o)
-
-    def alg_flops(self):
-        return 2 * self.n * self.b * self.i * self.o
-
-    def traffic(self):
-        return int(NCU_TRAFFIC_BYTES_CFG2 * self.n / 64)
-
-    def config(self):
-        return {"workload": f"WideLinear cfg2: N={self.n} models/GPU, in={self.i}, out={self.o}, B={self.b}, "
-                            f"bf16, fp32 accumulate, bias fused",
-                "models_per_gpu": self.n, "rows_per_model": self.b, "in_features": self.i,
-                "out_features": self.o, "l2": "inputs larger than L2 (705 MB touched per step), no flush"}
-
-    def setup(self, dev, seed):
-        import wide_compiler as wc
-        g = torch.Generator(device=dev).manual_seed(seed)
-        lin = wc.WideLinear(self.n, self.i, self.o, bias=True).to(dev, torch.bfloat16)
-        with torch.no_grad():
-            lin.weight.copy_(torch.randn(self.n, self.o, self.i, device=dev, generator=g) / self.i ** 0.5)
-            lin.bias.zero_()
-        self.module = lin
-        self.x = torch.randn(self.n, self.b, self.i, device=dev, generator=g).to(torch.bfloat16)
-
-    def cpu_sample(self, seconds):
+    def cpu_workload(self):
         from oracle import wide_oracle as O
-        n_s = 2
-        g = torch.Generator().manual_seed(0)
-        w = (torch.randn(n_s, self.o, self.i, generator=g) / 32).to(torch.bfloat16)
-        b = torch.zeros(n_s, self.o, dtype=torch.bfloat16)
-        x = torch.randn(n_s, self.b, self.i, generator=g).to(torch.bfloat16)
-        reps, el = _timed_cpu(lambda: O.linear_ref_dtype(x, w, b), seconds)
-        return reps * n_s * self.b / el, (f"{reps} reps x {n_s} of the {self.n} models (B={self.b}, "
-                                          f"{self.i}->{self.o}, bf16) in {el:.1f} s, torch CPU einsum+bias")
+        g = _gen(0)
+        n = self.n_total
+        w = (torch.randn(n, self.o, self.i, generator=g) / 32).to(torch.bfloat16)
+        b = torch.zeros(n, self.o, dtype=torch.bfloat16)
+        x = torch.randn(n, self.b, self.i, generator=g).to(torch.bfloat16)
+        return (lambda: O.linear_ref_dtype(x, w, b)), n * self.b, \
+            f"one full cfg2 forward per rep (all {n} models, B={self.b}), torch CPU einsum + bias in bf16"
 
 
 class _MLP(nn.Module):
@@ -218,51 +272,68 @@ class _MLP(nn.Module):
         return self.fc2(F.relu(self.fc1(x)))
 
 
-class MlpCfg1(Workload):
+class _Traced(Workload):
+    """A TracedWideModel workload through the multi-GPU wrapper (this rank's
+    slice of the models; packed input [B, n_local*C, ...])."""
+    compile_model = False
+
+    def build(self, dev, dtype, models, sample, per_model_inputs):
+        """models: all N (host); this rank's slice is fused and moved to dev."""
+        import wide_compiler as wc
+        from wide_compiler import parallel
+        world, rank = self._world_rank
+        self.module = parallel.ShardedWideModel(models, sample, rank=rank, world=world,
+                                                gather=self._gather, compile_model=self.compile_model)
+        self.module.to(dev, dtype).eval()
+        self.x = wc.pack([t.to(dev, dtype) for t in per_model_inputs])
+
+
+class MlpCfg1(_Traced):
     name = "cfg1"
     dtype = "fp32"
-    bound = "fp32"           # one fused chain launch of CUDA-core fp32 FMAs
+    bound = "fp32"
+    compile_model = True      # the library's CUDA-graph executor (compile=True)
 
     def __init__(self, n=100, b=32):
-        self.n, self.b = n, b
+        self.n_total, self.b = n, b
 
-    def samples(self):
-        return self.n * self.b
+    def flops(self, n):
+        return 2 * n * self.b * (64 * 128 + 128 * 64)
 
-    def alg_flops(self):
-        return 2 * self.n * self.b * (64 * 128 + 128 * 64)
-
-    def alg_bytes(self):
-        # whole-model compulsory bytes: x, W1, b1, W2, b2, y (fp32)
-        return 4 * self.n * (self.b * 64 + 128 * 64 + 128 + 64 * 128 + 64 + self.b * 64)
+    def work(self, n):
+        return {"graph replay": self.flops(n)}
 
     def config(self):
-        return {"workload": f"cfg1 TracedWideModel of N={self.n} MLPs (Linear 64->128, ReLU, Linear 128->64), "
-                            f"fp32, B={self.b}, packed input [{self.b}, {self.n * 64}]",
+        return {"workload": f"cfg1 TracedWideModel of N={self.n_total} MLPs (Linear 64->128, ReLU, Linear "
+                            f"128->64), fp32 (TF32 off), B={self.b}, packed input [{self.b}, {self.n_total * 64}], "
+                            f"compile=True (CUDA-graph executor)",
+                "models": self.n_total, "rows_per_model": self.b,
                 "l2": "small working set (8 MB) stays in L2 between steps"}
 
-    def setup(self, dev, seed):
-        import wide_compiler as wc
-        torch.manual_seed(seed)
-        models = [_MLP().to(dev) for _ in range(self.n)]
-        self.module = wc.compile(models, torch.randn(self.b, 64, device=dev))
-        self.x = torch.randn(self.b, self.n * 64, device=dev)
+    def setup(self, dev, lo, hi, seed):
+        models, xs = [], []
+        for j in range(self.n_total):
+            torch.manual_seed(seed + j)
+            models.append(_MLP())
+        for j in range(lo, hi):
+            xs.append(torch.randn(self.b, 64, generator=_gen(seed + 100_000 + j)))
+        self.build(dev, torch.float32, models, torch.randn(self.b, 64), xs)
 
-    def cpu_sample(self, seconds):
+    def cpu_workload(self):
         from oracle import wide_oracle as O
-        g = torch.Generator().manual_seed(0)
-        w1 = torch.randn(self.n, 128, 64, generator=g) / 8
-        b1 = torch.zeros(self.n, 128)
-        w2 = torch.randn(self.n, 64, 128, generator=g) / 11
-        b2 = torch.zeros(self.n, 64)
-        x = torch.randn(self.b, self.n * 64, generator=g)
+        g = _gen(0)
+        n = self.n_total
+        w1 = torch.randn(n, 128, 64, generator=g) / 8
+        b1 = torch.zeros(n, 128)
+        w2 = torch.randn(n, 64, 128, generator=g) / 11
+        b2 = torch.zeros(n, 64)
+        x = torch.randn(self.b, n * 64, generator=g)
 
         def run():
-            xn = x.view(self.b, self.n, 64).movedim(1, 0).contiguous()
+            xn = x.view(self.b, n, 64).movedim(1, 0).contiguous()
             y = O.mlp2_ref_dtype(xn, w1, b1, w2, b2)
             return y.movedim(0, 1).reshape(self.b, -1)
-        reps, el = _timed_cpu(run, seconds)
-        return reps * self.samples() / el, f"{reps} full cfg1 forwards in {el:.1f} s (fp32, torch CPU)"
+        return run, n * self.b, f"one full cfg1 forward per rep (all {n} MLPs, B={self.b}), fp32, torch CPU"
 
 
 class _ResBlock(nn.Module):
@@ -278,22 +349,59 @@ class _ResBlock(nn.Module):
         return self.bn2(self.conv2(h)) + x
 
 
-class ResBlockCfg3(Workload):
+def resblock_model(c, seed):
+    """One cfg3 ResBlock: default conv init from `seed`, BatchNorm in eval with
+    running_mean ~ N(0, 1), running_var ~ U(0.5, 2), weight ~ U(0.5, 1.5),
+    bias ~ N(0, 0.1)."""
+    torch.manual_seed(seed)
+    m = _ResBlock(c)
+    with torch.no_grad():
+        for bn in (m.bn1, m.bn2):
+            bn.running_mean.normal_(0, 1)
+            bn.running_var.uniform_(0.5, 2.0)
+            bn.weight.uniform_(0.5, 1.5)
+            bn.bias.normal_(0, 0.1)
+    return m.eval()
+
+
+class ResBlockCfg3(_Traced):
     name = "cfg3"
     bound = "tensor"
     peak_key = "tensor_sustained"
 
+    def __init__(self, n=100, b=32, c=64, hw=32):
+        self.n_total, self.b, self.c, self.hw = n, b, c, hw
+
+    def flops(self, n):
+        return 2 * 2 * n * self.b * self.hw * self.hw * self.c * self.c * 9
+
+    def work(self, n):
+        return {"widek_conv_fwd_ex": self.flops(n)}
+
+    def config(self):
+        return {"workload": f"cfg3 TracedWideModel of N={self.n_total} ResBlocks (Conv3x3 {self.c}->{self.c} pad 1, "
+                            f"BatchNorm eval, ReLU, Conv3x3, BatchNorm, + identity), B={self.b}, {self.hw}x{self.hw}, "
+                            f"bf16, packed input [{self.b}, {self.n_total * self.c}, {self.hw}, {self.hw}]",
+                "models": self.n_total, "rows_per_model": self.b,
+                "l2": f"inputs larger than L2 ({self.n_total * self.b * self.c * self.hw * self.hw * 2 / 1e6:.0f} MB "
+                      f"activation per step), no flush"}
+
+    def setup(self, dev, lo, hi, seed):
+        models = [resblock_model(self.c, seed + j) for j in range(self.n_total)]
+        xs = [torch.randn(self.b, self.c, self.hw, self.hw, generator=_gen(seed + 100_000 + j))
+              for j in range(lo, hi)]
+        self.build(dev, torch.bfloat16, models, torch.randn(2, self.c, self.hw, self.hw), xs)
+
     def torch_reference_step(self):
         """The reference's GPU op sequence for this graph (wide_conv2d.py:169-194
-        permute + grouped conv, wide_batchnorm_2d.py:53-72 permute + BN,
-        F.relu, + identity) with the same parameters, through torch (cuDNN)."""
-        n, c, hw = self.n, self.c, self.hw
-        st = self.module.stages
+        grouped conv, wide_batchnorm_2d.py:53-72 BN, F.relu, + identity) with
+        the same parameters on the packed input, through torch (cuDNN)."""
+        st = self.module.local.stages
+        n = self.module.n_local
         conv1, bn1, conv2, bn2 = st['conv1'].grouped_conv, st['bn1'].op, st['conv2'].grouped_conv, st['bn2'].op
-        x = self.x                                    # packed [B, N*C, H, W]
+        x = self.x
 
         def run():
-            b = x.shape[0]
             h = F.batch_norm(F.conv2d(x, conv1.weight, conv1.bias, padding=1, groups=n), bn1.running_mean,
                              bn1.running_var, bn1.weight, bn1.bias, False, 0.0, bn1.eps)
             h = F.relu(h)
@@ -302,110 +410,79 @@ class ResBlockCfg3(Workload):
             return y + x
         return run
 
-    def __init__(self, n=100, b=32, c=64, hw=32):
-        self.n, self.b, self.c, self.hw = n, b, c, hw
-
-    def samples(self):
-        return self.n * self.b
-
-    def alg_flops(self):
-        return 2 * 2 * self.n * self.b * self.hw * self.hw * self.c * self.c * 9
-
-    def alg_bytes(self):
-        return 2 * 2 * self.n * self.b * self.c * self.hw * self.hw   # fused block: x in, y out (bf16)
-
-    def config(self):
-        return {"workload": f"cfg3 TracedWideModel of N={self.n} ResBlocks (Conv3x3 {self.c}->{self.c} pad 1, BN "
-                            f"eval, ReLU, Conv3x3, BN, + identity), B={self.b}, {self.hw}x{self.hw}, bf16",
-                "l2": f"inputs larger than L2 ({self.n * self.b * self.c * self.hw * self.hw * 2 / 1e6:.0f} MB "
-                      f"activation per step), no flush"}
-
-    def setup(self, dev, seed):
-        import wide_compiler as wc
-        torch.manual_seed(seed)
-        models = []
-        for _ in range(self.n):
-            m = _ResBlock(self.c)
-            with torch.no_grad():
-                for bn in (m.bn1, m.bn2):
-                    bn.running_mean.normal_(0, 1)
-                    bn.running_var.uniform_(0.5, 2.0)
-                    bn.weight.uniform_(0.5, 1.5)
-                    bn.bias.normal_(0, 0.1)
-            models.append(m.to(dev, torch.bfloat16).eval())
-        self.module = wc.compile(models, torch.randn(2, self.c, self.hw, self.hw, device=dev,
-                                                     dtype=torch.bfloat16)).eval()
-        self.x = torch.randn(self.b, self.n * self.c, self.hw, self.hw, device=dev).to(torch.bfloat16)
-
-    def cpu_sample(self, seconds):
+    def cpu_workload(self):
         from oracle import wide_oracle as O
-        n_s, c = 1, self.c
-        g = torch.Generator().manual_seed(0)
+        n, c = self.n_total, self.c
+        g = _gen(0)
         bf = torch.bfloat16
 
         def mk(*s, sc=1.0):
             return (torch.randn(*s, generator=g) * sc).to(bf)
 
         def bn():
-            return {'running_mean': mk(n_s * c), 'running_var': (torch.rand(n_s * c, generator=g) + 0.5).to(bf),
-                    'weight': (torch.rand(n_s * c, generator=g) + 0.5).to(bf), 'bias': mk(n_s * c, sc=0.1)}
-        c1w, c2w = mk(n_s * c, c, 3, 3, sc=1 / 24), mk(n_s * c, c, 3, 3, sc=1 / 24)
-        c1b, c2b = mk(n_s * c, sc=0.1), mk(n_s * c, sc=0.1)
+            return {'running_mean': mk(n * c), 'running_var': (torch.rand(n * c, generator=g) * 1.5 + 0.5).to(bf),
+                    'weight': (torch.rand(n * c, generator=g) + 0.5).to(bf), 'bias': mk(n * c, sc=0.1)}
+        c1w, c2w = mk(n * c, c, 3, 3, sc=1 / 24), mk(n * c, c, 3, 3, sc=1 / 24)
+        c1b, c2b = mk(n * c, sc=0.1), mk(n * c, sc=0.1)
         bn1, bn2 = bn(), bn()
-        x = mk(n_s, self.b, c, self.hw, self.hw)
-        reps, el = _timed_cpu(lambda: O.resblock_ref_dtype(x, c1w, c1b, bn1, c2w, c2b, bn2), seconds)
-        return reps * n_s * self.b / el, (f"{reps} reps x {n_s} of the {self.n} ResBlocks (B={self.b}, bf16) in "
-                                          f"{el:.1f} s, torch CPU grouped conv + BN")
+        x = mk(n, self.b, c, self.hw, self.hw)
+        return (lambda: O.resblock_ref_dtype(x, c1w, c1b, bn1, c2w, c2b, bn2)), n * self.b, \
+            (f"one full cfg3 forward per rep (all {n} ResBlocks, B={self.b}), bf16, torch CPU grouped conv + BN "
+             f"(groups=N, as the reference)")
 
 
 class RnnCfg4(Workload):
     dtype = "fp32"
+    bound = "fp32"
+    graph = True
 
     def __init__(self, kind, n=32, b=4, t=32, i=64, h=128):
-        self.kind, self.n, self.b, self.t, self.i, self.h = kind, n, b, t, i, h
+        self.kind, self.n_total, self.b, self.t, self.i, self.h = kind, n, b, t, i, h
         self.name = f"cfg4{kind}"
         self.g = 3 if kind == "gru" else 4
 
-    def samples(self):
-        return self.n * self.b
+    def flops(self, n):
+        return 2 * n * self.b * self.t * self.g * self.h * (self.i + self.h)
 
-    def alg_flops(self):
-        return 2 * self.n * self.b * self.t * self.g * self.h * (self.i + self.h)
-
-    def alg_bytes(self):
-        return 4 * self.n * (self.b * self.t * (self.i + self.h) + self.g * self.h * (self.i + self.h)
-                             + 2 * self.g * self.h)
+    def work(self, n):
+        return {"graph replay": self.flops(n)}
 
     def config(self):
-        return {"workload": f"cfg4 Wide{self.kind.upper()} N={self.n}, input {self.i}, hidden {self.h}, B={self.b}, "
-                            f"T={self.t}, fp32 (TF32 off)",
+        return {"workload": f"cfg4 Wide{self.kind.upper()} N={self.n_total}, input {self.i}, hidden {self.h}, "
+                            f"B={self.b}, T={self.t}, fp32 (TF32 off), U(+-1/sqrt(H)) init, step replayed from a "
+                            f"CUDA graph",
+                "models": self.n_total, "rows_per_model": self.b,
                 "l2": "small working set stays in L2 between steps"}
 
-    def setup(self, dev, seed):
+    def setup(self, dev, lo, hi, seed):
         import wide_compiler as wc
-        torch.manual_seed(seed)
         cls = nn.GRU if self.kind == "gru" else nn.LSTM
-        mods = [cls(self.i, self.h, batch_first=True) for _ in range(self.n)]
+        mods = []
+        for j in range(lo, hi):
+            torch.manual_seed(seed + j)
+            mods.append(cls(self.i, self.h, batch_first=True))
         wcls = wc.WideGRU if self.kind == "gru" else wc.WideLSTM
         self.module = wcls.from_modules(mods).to(dev)
-        self.x = torch.randn(self.n, self.b, self.t, self.i, device=dev)
+        self.x = torch.stack([torch.randn(self.b, self.t, self.i, generator=_gen(seed + 100_000 + j))
+                              for j in range(lo, hi)]).to(dev)
 
-    def forward(self, x):
+    def step(self, x):
         return self.module(x)[0]
 
-    def cpu_sample(self, seconds):
+    def cpu_workload(self):
         from oracle import wide_oracle as O
-        g = torch.Generator().manual_seed(0)
+        g = _gen(0)
+        n = self.n_total
         s = 1 / self.h ** 0.5
 
         def u(*shape):
             return (torch.rand(*shape, generator=g) * 2 - 1) * s
-        wih, whh = u(self.n, self.g * self.h, self.i), u(self.n, self.g * self.h, self.h)
-        bih, bhh = u(self.n, self.g * self.h), u(self.n, self.g * self.h)
-        x = torch.randn(self.n, self.b, self.t, self.i, generator=g)
+        wih, whh = u(n, self.g * self.h, self.i), u(n, self.g * self.h, self.h)
+        bih, bhh = u(n, self.g * self.h), u(n, self.g * self.h)
+        x = torch.randn(n, self.b, self.t, self.i, generator=g)
         fn = O.gru_ref_dtype if self.kind == "gru" else O.lstm_ref_dtype
-        reps, el = _timed_cpu(lambda: fn(x, wih, whh, bih, bhh), seconds)
-        return reps * self.samples() / el, f"{reps} full cfg4 {self.kind} forwards in {el:.1f} s (fp32, torch CPU)"
+        return (lambda: fn(x, wih, whh, bih, bhh)), n * self.b, \
+            f"one full cfg4 {self.kind} forward per rep (all {n} models), fp32, torch CPU"
 
 
 class AttnCfg5(Workload):
@@ -413,12 +490,51 @@ class AttnCfg5(Workload):
     bound = "tensor"
     peak_key = "tensor_sustained"
 
+    def __init__(self, n=16, b=8, t=1024, d=512, heads=8):
+        self.n_total, self.b, self.t, self.d, self.heads = n, b, t, d, heads
+
+    def work(self, n):
+        core = 2 * 2 * n * self.b * self.heads * (self.t * (self.t + 1) // 2) * (self.d // self.heads)
+        proj = 2 * n * self.b * self.t * self.d * self.d * 4
+        return {"widek_attention_fwd": core, "widek_linear_fwd": proj}
+
+    def flops(self, n):
+        return sum(self.work(n).values())
+
+    def config(self):
+        return {"workload": f"cfg5 WideAttention N={self.n_total}, d_model={self.d}, {self.heads} heads, causal "
+                            f"self-attention, B={self.b}, T={self.t}, bf16, weights ~ N(0, 0.02), followed by "
+                            f"WideLayerNorm({self.d})",
+                "models": self.n_total, "rows_per_model": self.b,
+                "l2": "inputs larger than L2 (134 MB activation, ~0.5 GB of intermediates per step), no flush"}
+
+    def setup(self, dev, lo, hi, seed):
+        import wide_compiler as wc
+        n = hi - lo
+        a = wc.WideAttention(n, self.d, self.heads)
+        with torch.no_grad():
+            for k, j in enumerate(range(lo, hi)):
+                g = _gen(seed + j)
+                for p in (a.q_weight, a.kv_weight, a.out_weight):
+                    p[k].copy_(torch.randn(p[k].shape, generator=g) * 0.02)
+            a.q_bias.zero_()
+            a.kv_bias.zero_()
+            a.out_bias.zero_()
+        self.attn = a.to(dev, torch.bfloat16).eval()
+        self.ln = wc.WideLayerNorm(n, self.d).to(dev, torch.bfloat16)
+        self.module = self.attn
+        self.x = torch.stack([torch.randn(self.b, self.t, self.d, generator=_gen(seed + 100_000 + j))
+                              for j in range(lo, hi)]).to(dev, torch.bfloat16)
+
+    def step(self, x):
+        return self.ln(self.attn(x, is_causal=True))
+
     def torch_reference_step(self):
         """The reference's GPU op sequence (wide_attention.py:178-238 einsum
         projections, head split, SDPA causal, merge, out projection;
         wide_layernorm.py:41-67) with the same parameters, through torch."""
         a, ln, x = self.attn, self.ln, self.x
-        n, d, hd = self.n, self.d, self.heads
+        n, d, hd = a.n, self.d, self.heads
 
         def run():
             _, b, t, _ = x.shape
@@ -434,109 +550,454 @@ class AttnCfg5(Workload):
             return (y - mean) / torch.sqrt(var + ln.eps) * ln.weight.view(n, 1, 1, d) + ln.bias.view(n, 1, 1, d)
         return run
 
-    def __init__(self, n=16, b=8, t=1024, d=512, heads=8):
-        self.n, self.b, self.t, self.d, self.heads = n, b, t, d, heads
+    def cpu_workload(self):
+        from oracle import wide_oracle as O
+        n = self.n_total
+        g = _gen(0)
+        bf = torch.bfloat16
+        wq = (torch.randn(n, self.d, self.d, generator=g) * 0.02).to(bf)
+        wkv = (torch.randn(n, 2 * self.d, self.d, generator=g) * 0.02).to(bf)
+        wo = (torch.randn(n, self.d, self.d, generator=g) * 0.02).to(bf)
+        lw, lb = torch.ones(n * self.d, dtype=bf), torch.zeros(n * self.d, dtype=bf)
+        x = torch.randn(n, self.b, self.t, self.d, generator=g).to(bf)
+        return (lambda: O.attention_ln_ref_dtype(x, wq, wkv, wo, self.heads, lw, lb)), n * self.b, \
+            f"one full cfg5 forward per rep (all {n} models, B={self.b}, T={self.t}), bf16, torch CPU einsum + " \
+            f"SDPA + LN"
 
-    def samples(self):
-        return self.n * self.b
 
-    def alg_flops(self):
-        proj = 2 * self.n * self.b * self.t * self.d * self.d * 4
-        core = 2 * 2 * self.n * self.b * self.heads * (self.t * self.t // 2) * (self.d // self.heads)
-        return proj + core
+class _Norm(Workload):
+    """A wide norm over a working set far above L2."""
 
-    def alg_bytes(self):
-        act = self.n * self.b * self.t * self.d * 2
-        return act * 2 + 4 * self.n * self.d * self.d * 2 + act * 2     # x, y, weights, LN read + write
+    def _act_bytes(self, n):
+        return n * self.rows * self.elem * 2
+
+    def samples(self, n):
+        return n * self.b
+
+
+class BatchNormWl(_Norm):
+    def __init__(self, training, n=100, b=32, c=64, hw=32):
+        self.training = training
+        self.name = "bn2d_train" if training else "bn2d_eval"
+        self.n_total, self.b, self.c, self.hw = n, b, c, hw
+
+    def work(self, n):
+        act = n * self.b * self.c * self.hw * self.hw * 2
+        entry = "widek_batchnorm_train_fwd" if self.training else "widek_batchnorm_fwd"
+        return {entry: 2 * act}        # compulsory: read x once, write y once (bf16)
 
     def config(self):
-        return {"workload": f"cfg5 WideAttention N={self.n}, d_model={self.d}, {self.heads} heads, causal, "
-                            f"B={self.b}, T={self.t}, bf16, followed by WideLayerNorm({self.d})",
-                "l2": "inputs larger than L2 (134 MB activation, ~0.5 GB of intermediates per step), no flush"}
+        mode = ("training mode (batch statistics, running-stat update)" if self.training
+                else "eval mode (running statistics)")
+        return {"workload": f"WideBatchNorm2d N={self.n_total}, C={self.c}, B={self.b}, {self.hw}x{self.hw}, bf16, "
+                            f"{mode}; the cfg3 BatchNorm shape, 419 MB in + 419 MB out",
+                "models": self.n_total, "rows_per_model": self.b,
+                "l2": "input larger than L2 (419 MB), no flush"}
 
-    def setup(self, dev, seed):
+    def setup(self, dev, lo, hi, seed):
         import wide_compiler as wc
-        torch.manual_seed(seed)
-        a = wc.WideAttention(self.n, self.d, self.heads)
+        n = hi - lo
+        m = wc.WideBatchNorm2d(n, self.c).to(dev, torch.bfloat16)
+        g = _gen(seed + lo)
         with torch.no_grad():
-            for p in (a.q_weight, a.kv_weight, a.out_weight):
-                p.normal_(0, 0.02)
-            a.q_bias.zero_()
-            a.kv_bias.zero_()
-            a.out_bias.zero_()
-        self.attn = a.to(dev, torch.bfloat16).eval()
-        self.ln = wc.WideLayerNorm(self.n, self.d).to(dev, torch.bfloat16)
-        self.module = self.attn
-        self.x = torch.randn(self.n, self.b, self.t, self.d, device=dev).to(torch.bfloat16)
+            m.op.running_mean.copy_(torch.randn(n * self.c, generator=g))
+            m.op.running_var.copy_(torch.rand(n * self.c, generator=g) * 1.5 + 0.5)
+            m.op.weight.copy_(torch.rand(n * self.c, generator=g) + 0.5)
+            m.op.bias.copy_(torch.randn(n * self.c, generator=g) * 0.1)
+        self.module = m.train(self.training)
+        self.x = torch.randn(n, self.b, self.c, self.hw, self.hw, device=dev,
+                             generator=torch.Generator(device=dev).manual_seed(seed + lo)).to(torch.bfloat16)
 
-    def forward(self, x):
-        return self.ln(self.attn(x, is_causal=True))
-
-    def cpu_sample(self, seconds):
+    def cpu_workload(self):
         from oracle import wide_oracle as O
-        n_s = 1
-        g = torch.Generator().manual_seed(0)
+        n, c = self.n_total, self.c
+        g = _gen(0)
         bf = torch.bfloat16
-        wq = (torch.randn(n_s, self.d, self.d, generator=g) * 0.02).to(bf)
-        wkv = (torch.randn(n_s, 2 * self.d, self.d, generator=g) * 0.02).to(bf)
-        wo = (torch.randn(n_s, self.d, self.d, generator=g) * 0.02).to(bf)
-        lw, lb = torch.ones(n_s * self.d, dtype=bf), torch.zeros(n_s * self.d, dtype=bf)
-        x = torch.randn(n_s, self.b, self.t, self.d, generator=g).to(bf)
-        reps, el = _timed_cpu(lambda: O.attention_ln_ref_dtype(x, wq, wkv, wo, self.heads, lw, lb), seconds)
-        return reps * n_s * self.b / el, (f"{reps} reps x {n_s} of the {self.n} models (B={self.b}, T={self.t}, "
-                                          f"bf16) in {el:.1f} s, torch CPU einsum + SDPA + LN")
+        x = torch.randn(n, self.b, c, self.hw, self.hw, generator=g).to(bf)
+        rm, rv = torch.zeros(n * c, dtype=bf), torch.ones(n * c, dtype=bf)
+        w, bb = torch.ones(n * c, dtype=bf), torch.zeros(n * c, dtype=bf)
+        return (lambda: O.batchnorm2d_ref_dtype(x, rm, rv, w, bb, self.training)), n * self.b, \
+            f"one full pass per rep (all {n} models), bf16, torch CPU permute + batch_norm + permute"
 
 
-def make_workload(name, models=None):
-    if name == "cfg2":
-        return LinearCfg2(n=models or 64)
-    if name == "cfg1":
-        return MlpCfg1()
-    if name == "cfg3":
-        return ResBlockCfg3(n=models or 100)
-    if name == "cfg4gru":
-        return RnnCfg4("gru")
-    if name == "cfg4lstm":
-        return RnnCfg4("lstm")
-    if name == "cfg5":
-        return AttnCfg5()
-    raise ValueError(name)
+class GroupNormWl(_Norm):
+    name = "gn"
+
+    def __init__(self, n=100, b=32, c=64, groups=8, hw=32):
+        self.n_total, self.b, self.c, self.groups, self.hw = n, b, c, groups, hw
+
+    def work(self, n):
+        return {"widek_groupnorm_fwd": 2 * n * self.b * self.c * self.hw * self.hw * 2}
+
+    def config(self):
+        return {"workload": f"WideGroupNorm N={self.n_total}, {self.groups} groups of C={self.c}, B={self.b}, "
+                            f"{self.hw}x{self.hw}, bf16, affine; 419 MB in + 419 MB out",
+                "models": self.n_total, "rows_per_model": self.b, "l2": "input larger than L2 (419 MB), no flush"}
+
+    def setup(self, dev, lo, hi, seed):
+        import wide_compiler as wc
+        n = hi - lo
+        m = wc.WideGroupNorm(n, self.groups, self.c).to(dev, torch.bfloat16)
+        g = _gen(seed + lo)
+        with torch.no_grad():
+            m.norm.weight.copy_(torch.rand(n * self.c, generator=g) + 0.5)
+            m.norm.bias.copy_(torch.randn(n * self.c, generator=g) * 0.1)
+        self.module = m
+        self.x = torch.randn(n, self.b, self.c, self.hw, self.hw, device=dev,
+                             generator=torch.Generator(device=dev).manual_seed(seed + lo)).to(torch.bfloat16)
+
+    def cpu_workload(self):
+        from oracle import wide_oracle as O
+        n, c = self.n_total, self.c
+        g = _gen(0)
+        bf = torch.bfloat16
+        x = torch.randn(n, self.b, c, self.hw, self.hw, generator=g).to(bf)
+        w, bb = torch.ones(n * c, dtype=bf), torch.zeros(n * c, dtype=bf)
+        return (lambda: O.groupnorm_ref_dtype(x, self.groups, w, bb)), n * self.b, \
+            f"one full pass per rep (all {n} models), bf16, torch CPU permute + group_norm + permute"
+
+
+class LayerNormWl(_Norm):
+    name = "ln"
+
+    def __init__(self, n=16, b=32, t=1024, d=512):
+        self.n_total, self.b, self.t, self.d = n, b, t, d
+
+    def work(self, n):
+        return {"widek_layernorm_fwd": 2 * n * self.b * self.t * self.d * 2}
+
+    def config(self):
+        return {"workload": f"WideLayerNorm N={self.n_total}, d={self.d}, B={self.b}, T={self.t}, bf16 (the cfg5 "
+                            f"LayerNorm at 4x its batch: 537 MB in + 537 MB out)",
+                "models": self.n_total, "rows_per_model": self.b, "l2": "input larger than L2 (537 MB), no flush"}
+
+    def setup(self, dev, lo, hi, seed):
+        import wide_compiler as wc
+        n = hi - lo
+        m = wc.WideLayerNorm(n, self.d).to(dev, torch.bfloat16)
+        g = _gen(seed + lo)
+        with torch.no_grad():
+            m.weight.copy_(torch.rand(n * self.d, generator=g) + 0.5)
+            m.bias.copy_(torch.randn(n * self.d, generator=g) * 0.1)
+        self.module = m
+        self.x = torch.randn(n, self.b, self.t, self.d, device=dev,
+                             generator=torch.Generator(device=dev).manual_seed(seed + lo)).to(torch.bfloat16)
+
+    def cpu_workload(self):
+        from oracle import wide_oracle as O
+        n = self.n_total
+        g = _gen(0)
+        bf = torch.bfloat16
+        x = torch.randn(n, self.b, self.t, self.d, generator=g).to(bf)
+        w, bb = torch.ones(n * self.d, dtype=bf), torch.zeros(n * self.d, dtype=bf)
+        return (lambda: O.layernorm_ref_dtype(x, w, bb, n, self.d)), n * self.b, \
+            f"one full pass per rep (all {n} models), bf16, torch CPU mean/var/normalize/affine"
+
+
+def make_workload(name):
+    return {
+        "cfg1": lambda: MlpCfg1(), "cfg2": lambda: LinearCfg2(), "cfg3": lambda: ResBlockCfg3(),
+        "cfg4gru": lambda: RnnCfg4("gru"), "cfg4lstm": lambda: RnnCfg4("lstm"), "cfg5": lambda: AttnCfg5(),
+        "bn2d_eval": lambda: BatchNormWl(False), "bn2d_train": lambda: BatchNormWl(True),
+        "gn": lambda: GroupNormWl(), "ln": lambda: LayerNormWl(),
+    }[name]()
 
 
 # ---------------------------------------------------------------------------
-# Arms
+# Reference arm
 # ---------------------------------------------------------------------------
+
+def _cpu_line(wl, steps, warmup, step_seconds):
+    """Median samples/s over `steps` steps, each as many whole-workload
+    forwards as fill `step_seconds` (at least one), after `warmup` forwards."""
+    fn, samples, desc = wl.cpu_workload()
+    for _ in range(warmup):
+        fn()
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ts = time.perf_counter()
+        reps = 0
+        while True:
+            fn()
+            reps += 1
+            el = time.perf_counter() - ts
+            if el >= step_seconds:
+                break
+        vals.append(reps * samples / el)
+    wall = time.perf_counter() - t0
+    return statistics.median(vals), wall, desc
+
 
 def run_reference(args):
-    """The reference's CPU path for the chosen workload, rank 0 only; each
-    step is one bounded sample of the workload."""
+    """The reference's CPU path for the same configurations, rank 0 only;
+    each step is at least `--ref-step-seconds` of full forwards of the whole
+    workload (all N models)."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    wl = make_workload(args.workload, args.models)
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    per_step_s = max(0.0, args.ref_step_seconds)
-    for _ in range(args.warmup):
-        wl.cpu_sample(per_step_s)
-    vals, desc = [], ""
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        v, desc = wl.cpu_sample(per_step_s)
-        vals.append(v)
-    el = time.perf_counter() - t0
-    value = statistics.median(vals)
+    names = _workload_names(args)
+    head = make_workload(names[0])
+    value, wall, desc = _cpu_line(head, args.steps, args.warmup, args.ref_step_seconds)
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * el / max(args.steps, 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-        "config": wl.config(), "impl": "reference",
+        "warmup": args.warmup, "ms_per_step": 1e3 * wall / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": head.dtype,
+        "data": "synthetic", "config": head.config(), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-                         "sample": f"median over steps; last step: {desc}"},
+                         "sample": f"median over steps of >= {args.ref_step_seconds} s each; {desc}"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    subs = {}
+    for name in names[1:]:
+        wl = make_workload(name)
+        v, w2, d2 = _cpu_line(wl, args.ref_sub_steps, 1, args.ref_step_seconds)
+        subs[name] = {"value": v, "unit": "samples/s", "ms_per_step": 1e3 * w2 / max(args.ref_sub_steps, 1),
+                      "dtype": wl.dtype, "config": wl.config(),
+                      "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "port",
+                                       "sample": d2}}
+    if subs:
+        line["configs"] = subs
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+def _workload_names(args):
+    if args.workload == "all":
+        return list(ORDER)
+    return [args.workload]
+
+
+class _Ctx:
+    def __init__(self, args, world, rank, local, dev, pg):
+        self.args, self.world, self.rank, self.local, self.dev, self.pg = args, world, rank, local, dev, pg
+
+    def barrier(self):
+        if self.pg:
+            torch.distributed.barrier(device_ids=[self.local])
+        torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, v):
+        t = torch.tensor([v], device=self.dev, dtype=torch.float64)
+        if self.pg:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+
+def _runner(wl, x, dev):
+    """Callable running one step on input buffer x (a CUDA-graph replay for
+    workloads captured in the bench) and the number of our kernels one call
+    launches when it is a replay."""
+    from wide_compiler import _native as N
+    if not wl.graph:
+        return (lambda: wl.step(x)), None
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            wl.step(x)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    n0 = N.launch_count()
+    with torch.cuda.graph(g):
+        out = wl.step(x)
+    launches = N.launch_count() - n0
+
+    def replay():
+        g.replay()
+        return out
+    replay.graph = g
+    return replay, launches
+
+
+def _gather_fn(wl, ctx):
+    if not (ctx.args.gather and ctx.world > 1):
+        return None
+    from wide_compiler import parallel
+    if isinstance(wl, _Traced):
+        return None                          # ShardedWideModel gathers inside its forward
+    return lambda y: parallel.gather_outputs(y, wl.n_total)
+
+
+def measure(name, ctx, clocks):
+    from wide_compiler import _native as N
+    args = ctx.args
+    wl = make_workload(name)
+    if args.weak:
+        lo, hi = 0, wl.n_total
+        wl._world_rank = (1, 0)
+    else:
+        lo, hi = shard_range(wl.n_total, ctx.world, ctx.rank)
+        wl._world_rank = (ctx.world, ctx.rank)
+    wl._gather = bool(args.gather and ctx.world > 1 and not args.weak)
+    n_local = hi - lo
+    wl.setup(ctx.dev, lo, hi, seed=args.seed)
+    x = wl.x
+    gather = _gather_fn(wl, ctx) if not args.weak else None
+    run0, replay_launches = _runner(wl, x, ctx.dev)
+
+    def step():
+        y = run0()
+        if gather is not None:
+            y = gather(y)
+        return y
+
+    steps = args.steps if name == HEADLINE or args.workload != "all" else args.sub_steps
+    for _ in range(max(args.warmup, 3)):
+        step()
+    ctx.barrier()
+    stream = torch.cuda.current_stream(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mark0 = clocks.mark()
+    launches0 = N.launch_count()
+    with N.LaunchTimer() as timer:
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+    ctx.barrier()
+    launches = N.launch_count() - launches0
+    gpu_launches = launches + (replay_launches or 0) * steps
+    ms_local = e0.elapsed_time(e1) / steps
+    ms = ctx.max_over_ranks(ms_local)
+    clk = clocks.summary(mark0, clocks.mark())
+    kern = timer.summary()
+
+    # End to end through the public call: pinned host input uploaded, forward,
+    # output downloaded, on three streams with double-buffered device inputs.
+    e2e_steps = max(1, min(steps, args.e2e_steps))
+    x_host = x.cpu().pin_memory()
+    x_dev = [torch.empty_like(x) for _ in range(2)]
+    runners = [_runner(wl, x_dev[k], ctx.dev)[0] for k in range(2)]
+    y0 = runners[0]()
+    if gather is not None:
+        y0 = gather(y0)
+    y_host = [torch.empty(y0.shape, dtype=y0.dtype).pin_memory() for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(ctx.dev), torch.cuda.Stream(ctx.dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_step(i):
+        k = i % 2
+        if i >= 2:
+            s_in.wait_event(ev_comp[k])          # step i-2's forward has read x_dev[k]
+            stream.wait_event(ev_out[k])         # and its output has been downloaded
+        with torch.cuda.stream(s_in):
+            x_dev[k].copy_(x_host, non_blocking=True)
+            ev_in[k].record(s_in)
+        stream.wait_event(ev_in[k])
+        y = runners[k]()
+        if gather is not None:
+            y = gather(y)
+        ev_comp[k].record(stream)
+        s_out.wait_event(ev_comp[k])
+        with torch.cuda.stream(s_out):
+            y_host[k].copy_(y, non_blocking=True)
+            y.record_stream(s_out)
+            ev_out[k].record(s_out)
+
+    for i in range(4):
+        e2e_step(i)
+    ctx.barrier()
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    stream.wait_stream(s_out)
+    stream.wait_stream(s_in)
+    e1.record(stream)
+    ctx.barrier()
+    ms_e2e = ctx.max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+
+    total_models = wl.n_total if not args.weak else wl.n_total * ctx.world
+    samples = wl.samples(total_models)
+    rec = {"value": samples / (ms * 1e-3), "unit": "samples/s", "ms_per_step": ms, "steps": steps,
+           "dtype": wl.dtype, "config": wl.config(),
+           "e2e": {"value": samples / (ms_e2e * 1e-3), "unit": "samples/s",
+                   "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                   "d2h_bytes_per_step": y_host[0].numel() * y_host[0].element_size(),
+                   "steps": e2e_steps, "ms_per_step": ms_e2e,
+                   "pipelined": "upload, forward and download on separate streams, double-buffered"},
+           "gpu_launches": gpu_launches, "clocks": clk,
+           "models_this_rank": n_local}
+    rec["roofline"] = _roofline(wl, n_local, ms_local, steps, kern, replay_launches)
+    rec["kernels"] = {k: {"launches_per_step": v["calls"] / steps, "mean_ms": v["mean_ms"],
+                          "ms_per_step": v["total_ms"] / steps} for k, v in kern.items()}
+
+    if ctx.rank == 0 and ctx.world == 1:
+        if hasattr(wl, "torch_reference_step") and not args.no_torch_gpu:
+            fn = wl.torch_reference_step()
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(ctx.dev)
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize(ctx.dev)
+            tms = e0.elapsed_time(e1) / steps
+            rec["torch_gpu_reference"] = {"ms_per_step": tms, "value": samples / (tms * 1e-3), "unit": "samples/s",
+                                          "note": "the reference's op sequence on this GPU via torch "
+                                                  "(cuBLAS / cuDNN / SDPA)"}
+        if not args.no_cpu_baseline:
+            torch.set_num_threads(len(os.sched_getaffinity(0)))
+            fn, cpu_samples, desc = wl.cpu_workload()
+            secs = args.cpu_seconds if name == HEADLINE else args.sub_cpu_seconds
+            reps, el = _timed_cpu(fn, secs)
+            rec["cpu_baseline"] = {"value": reps * cpu_samples / el, "unit": "samples/s",
+                                   "cores": torch.get_num_threads(), "kind": "port",
+                                   "sample": f"{reps} reps in {el:.1f} s: {desc}"}
+            del fn
+    for r in runners:
+        if hasattr(r, "graph"):
+            del r.graph
+    if hasattr(run0, "graph"):
+        del run0.graph
+    del wl, x, x_dev, runners, run0
+    torch.cuda.synchronize(ctx.dev)
+    torch.cuda.empty_cache()
+    return rec
+
+
+def _roofline(wl, n_local, ms_step, steps, kern, replay_launches):
+    pk = peaks()
+    work = wl.work(n_local)
+    if replay_launches is not None or not kern or "graph replay" in work:
+        entry = "graph replay"
+        units = sum(work.values())
+        kms = ms_step
+        per_step = 1
+    else:
+        entry = max(kern, key=lambda k: kern[k]["total_ms"])
+        if entry not in work:
+            entry = max((k for k in kern if k in work), key=lambda k: kern[k]["total_ms"], default=entry)
+        units = work.get(entry, 0)
+        kms = kern[entry]["total_ms"] / steps        # that entry's device time per step
+        per_step = kern[entry]["calls"] / steps
+    if wl.bound == "hbm":
+        achieved = units / (kms * 1e-3) / 1e9
+        peak, unit, kind = pk["hbm"], "GB/s", f"{pk['kind']} HBM copy"
+    elif wl.bound == "fp32":
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        achieved = units / (kms * 1e-3) / 1e12
+        peak, unit = sms * 128 * 2 * 1965e6 / 1e12, "TFLOP/s"
+        kind = f"nominal fp32 FFMA ({sms} SMs x 128 lanes x 2 x 1965 MHz; no measured figure exists)"
+    else:
+        achieved = units / (kms * 1e-3) / 1e12
+        peak, unit, kind = pk[wl.peak_key], "TFLOP/s", f"{pk['kind']} bf16 dense ({wl.peak_key})"
+    tr = wl.traffic(n_local)
+    scale = 1e9 if wl.bound == "hbm" else 1e12
+    step_rate = sum(work.values()) / (ms_step * 1e-3) / scale
+    return {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "peak_kind": kind, "traffic": None if tr is None else int(tr),
+            "kernel": entry, "launches_per_step": per_step, "kernel_ms_per_step": kms,
+            "algorithmic_per_step": units, "step_achieved": step_rate, "step_frac": step_rate / peak}
 
 
 def run_b200(args):
@@ -548,213 +1009,42 @@ def run_b200(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = True
-    from wide_compiler import _native
-    _native.load()
-    _native.check(_native.lib().widek_linear_set_variant(args.linear_variant), "widek_linear_set_variant")
-    _native.check(_native.lib().widek_attention_set_variant(args.attn_variant), "widek_attention_set_variant")
-    _native.check(_native.lib().widek_conv_set_variant(args.conv_variant), "widek_conv_set_variant")
+    from wide_compiler import _native as N
+    N.load()
+    N.check(N.lib().widek_linear_set_variant(args.linear_variant), "widek_linear_set_variant")
+    N.check(N.lib().widek_attention_set_variant(args.attn_variant), "widek_attention_set_variant")
+    N.check(N.lib().widek_conv_set_variant(args.conv_variant), "widek_conv_set_variant")
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
-    wl = make_workload(args.workload, args.models)
-    wl.setup(dev, seed=1234 + rank)
-    x = wl.x
-    gather = args.gather and world > 1
-
-    def step():
-        y = wl.forward(x)
-        if gather:
-            from wide_compiler import parallel
-            parallel.gather_outputs(y, y.shape[0] * world)
-        return y
-
-    def barrier():
-        if pg:
-            torch.distributed.barrier(device_ids=[local])
-        torch.cuda.synchronize(dev)
-
-    run = step
-    graph = None
-    graph_launches = 0
-    # TracedWideModel workloads run --graph through the library's own CUDA-graph
-    # executor (what compile=True gives a user), for the timed loop and e2e;
-    # the others capture the step here.
-    from wide_compiler.core.traced_wide import TracedWideModel
-    executor = bool(args.graph) and isinstance(getattr(wl, "module", None), TracedWideModel)
-    if executor:
-        from wide_compiler.core.graphed import GraphedWideModel
-        n0 = _native.lib().widek_launch_count()
-        wl.module(x)                          # one eager forward: the kernels a replay runs
-        torch.cuda.synchronize(dev)
-        graph_launches = _native.lib().widek_launch_count() - n0
-        wl.module = GraphedWideModel(wl.module)
-    elif args.graph:
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for _ in range(3):
-                step()
-        torch.cuda.current_stream(dev).wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        n0 = _native.lib().widek_launch_count()
-        with torch.cuda.graph(graph):
-            step()
-        graph_launches = _native.lib().widek_launch_count() - n0   # kernels in one replay
-        run = graph.replay
-
+    ctx = _Ctx(args, world, rank, local, dev, pg)
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(max(args.warmup, 3)):
-        run()
-    barrier()
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    launches0 = _native.lib().widek_launch_count()
-    e0.record(stream)
-    for _ in range(args.steps):
-        run()
-    e1.record(stream)
-    # Our kernels launched in the timed region: counted by the library at
-    # every launch (a graph replay runs the kernels counted at capture).
-    gpu_launches = (graph_launches * args.steps if (graph is not None or executor)
-                    else _native.lib().widek_launch_count() - launches0)
-    barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if pg:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(t.item())
-
-    # End to end through the public API: every step copies its input from
-    # pinned host memory to the device, runs the forward and copies the result
-    # back to pinned host memory. The three run on separate streams with
-    # double-buffered device inputs, so step i's upload, step i-1's forward
-    # and step i-2's download overlap as in a serving pipeline.
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    x_host = x.cpu().pin_memory()
-    y0 = wl.forward(x)
-    y_host = [torch.empty(y0.shape, dtype=y0.dtype).pin_memory() for _ in range(2)]
-    x_dev = [torch.empty_like(x) for _ in range(2)]
-    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_comp = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
-
-    def e2e_step(i):
-        k = i % 2
-        if i >= 2:
-            s_in.wait_event(ev_comp[k])          # step i-2's forward has read x_dev[k]
-            if executor:
-                stream.wait_event(ev_out[k])     # and its result has been downloaded (a graph
-                                                 # replay writes the same output tensor again)
-        with torch.cuda.stream(s_in):
-            x_dev[k].copy_(x_host, non_blocking=True)
-            ev_in[k].record(s_in)
-        stream.wait_event(ev_in[k])
-        y = wl.forward(x_dev[k])
-        if gather:
-            from wide_compiler import parallel
-            parallel.gather_outputs(y, y.shape[0] * world)
-        ev_comp[k].record(stream)
-        s_out.wait_event(ev_comp[k])
-        with torch.cuda.stream(s_out):
-            y_host[k].copy_(y, non_blocking=True)
-            y.record_stream(s_out)
-            ev_out[k].record(s_out)
-
-    for i in range(4):
-        e2e_step(i)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e0.record(stream)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    stream.wait_stream(s_out)
-    stream.wait_stream(s_in)
-    e1.record(stream)
-    barrier()
-    ms_e2e = e0.elapsed_time(e1) / e2e_steps
-    t2 = torch.tensor([ms_e2e], device=dev, dtype=torch.float64)
-    if pg:
-        torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
-    ms_e2e = float(t2.item())
-    clk = clocks.stop()
-    dev_err = _native.device_error()
-    del graph
-
+    names = _workload_names(args)
+    recs = {}
+    try:
+        for name in names:
+            recs[name] = measure(name, ctx, clocks)
+    finally:
+        clocks.stop()
+    dev_err = N.device_error()
     if rank == 0:
-        samples = wl.samples() * world
-        pk = peaks()
-        if wl.bound == "hbm":
-            achieved = wl.alg_bytes() / (ms * 1e-3) / 1e9
-            roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
-                    "frac": achieved / pk["hbm"], "peak_kind": f"{pk['kind']} HBM copy",
-                    "traffic": wl.traffic(), "algorithmic_bytes": wl.alg_bytes(),
-                    "tflops": wl.alg_flops() / (ms * 1e-3) / 1e12}
-        elif wl.bound == "fp32":
-            # CUDA-core fp32 FMA pipe: no measured figure exists for it, so the
-            # nominal rate at the maximum SM clock is the denominator.
-            sms = torch.cuda.get_device_properties(dev).multi_processor_count
-            peak = sms * 128 * 2 * 1965e6 / 1e12
-            achieved = wl.alg_flops() / (ms * 1e-3) / 1e12
-            roof = {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak,
-                    "peak_kind": f"nominal fp32 FFMA ({sms} SMs x 128 lanes x 2 x 1965 MHz)",
-                    "traffic": wl.traffic(), "algorithmic_flops": wl.alg_flops(),
-                    "gbs": wl.alg_bytes() / (ms * 1e-3) / 1e9}
-        else:
-            achieved = wl.alg_flops() / (ms * 1e-3) / 1e12
-            peak = pk[wl.peak_key]
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "peak_kind": f"{pk['kind']} bf16 dense ({wl.peak_key})",
-                    "traffic": wl.traffic(), "algorithmic_flops": wl.alg_flops(),
-                    "gbs": wl.alg_bytes() / (ms * 1e-3) / 1e9}
-        cfg = wl.config()
-        cfg["gather"] = bool(gather)
-        cfg["cuda_graph"] = ("library CUDA-graph executor (compile=True)" if executor
-                             else "step captured by the bench" if args.graph else False)
-        cfg["linear_variant"] = "CTA-pair tiles" if args.linear_variant == 2 else "single-CTA tiles"
-        if args.workload == "cfg3":
-            cfg["conv_variant"] = "per-tap A tiles" if args.conv_variant == 1 else "halo-reuse A tiles"
-        if args.workload == "cfg5":
-            cfg["attention_variant"] = ("warp-level MMA" if args.attn_variant == 1 else
-                                        "tcgen05/TMEM" + (f", {args.attn_variant - 10}/4 exp2 pairs on FMA"
-                                                          if args.attn_variant >= 10 else ""))
+        head = recs[names[0]]
         line = {
-            "metric": METRIC, "value": samples / (ms_max * 1e-3), "unit": "samples/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic", "config": cfg,
-            "e2e": {"value": samples / (ms_e2e * 1e-3), "unit": "samples/s",
-                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
-                    "d2h_bytes_per_step": y_host[0].numel() * y_host[0].element_size(),
-                    "steps": e2e_steps, "ms_per_step": ms_e2e,
-                    "pipelined": "upload, forward and download on separate streams, double-buffered"},
-            "gpu_launches": gpu_launches,
-            "roofline": roof,
-            "clocks": clk,
-            "device_error": dev_err,
+            "metric": METRIC, "value": head["value"], "unit": "samples/s", "n_gpus": world, "steps": head["steps"],
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": head["dtype"],
+            "data": "synthetic", "config": head["config"], "e2e": head["e2e"],
+            "gpu_launches": head["gpu_launches"], "roofline": head["roofline"], "clocks": head["clocks"],
         }
-        if world == 1 and hasattr(wl, "torch_reference_step"):
-            # Extra column: the reference's torch GPU path (library kernels), same device, same inputs.
-            fn = wl.torch_reference_step()
-            with torch.no_grad():
-                for _ in range(5):
-                    fn()
-                torch.cuda.synchronize(dev)
-                e0.record(stream)
-                for _ in range(args.steps):
-                    fn()
-                e1.record(stream)
-                torch.cuda.synchronize(dev)
-            tms = e0.elapsed_time(e1) / args.steps
-            line["torch_gpu_reference"] = {"ms_per_step": tms, "value": wl.samples() / (tms * 1e-3),
-                                           "unit": "samples/s",
-                                           "note": "reference op sequence on this GPU via torch (cuBLAS/cuDNN/SDPA)"}
-        if world == 1 and not args.no_cpu_baseline:
-            torch.set_num_threads(len(os.sched_getaffinity(0)))
-            v, desc = wl.cpu_sample(args.cpu_seconds)
-            line["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": torch.get_num_threads(),
-                                    "kind": "port", "sample": desc}
+        for k in ("cpu_baseline", "torch_gpu_reference", "kernels", "models_this_rank"):
+            if k in head:
+                line[k] = head[k]
+        line["parallel"] = {"ranks": world, "split": "weak: every rank runs all N models" if args.weak else
+                            "contiguous N-slices, one per rank (N fixed)", "gather": bool(args.gather and world > 1)}
+        line["variants"] = {"linear": args.linear_variant, "attention": args.attn_variant, "conv": args.conv_variant}
+        if len(names) > 1:
+            line["configs"] = {k: recs[k] for k in names[1:]}
+        line["device_error"] = dev_err
         print(json.dumps(line), flush=True)
     if pg:
         torch.distributed.barrier(device_ids=[local])
@@ -765,19 +1055,24 @@ def run_b200(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4gru", "cfg4lstm", "cfg5"])
-    ap.add_argument("--models", type=int, default=None,
-                    help="cfg2 models per GPU (default 64; smaller only for profiling captures)")
-    ap.add_argument("--e2e-steps", type=int, default=100)
-    ap.add_argument("--graph", action="store_true", help="replay each step from a CUDA graph")
-    ap.add_argument("--gather", action="store_true", help="include the optional output all-gather")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--ref-step-seconds", type=float, default=0.02,
-                    help="reference arm: minimum CPU time of one step's bounded sample")
+    ap.add_argument("--workload", default="all", choices=["all"] + ORDER,
+                    help="all: the cfg3 headline plus every other configuration under 'configs'")
+    ap.add_argument("--sub-steps", type=int, default=20, help="timed steps of each non-headline configuration")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--weak", action="store_true", help="every rank runs all N models (weak scaling)")
+    ap.add_argument("--gather", action="store_true", help="include the optional output all-gather in every step")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time for the headline")
+    ap.add_argument("--sub-cpu-seconds", type=float, default=3.0, help="CPU baseline time per other configuration")
+    ap.add_argument("--ref-step-seconds", type=float, default=1.0,
+                    help="reference arm: minimum CPU time of one step (whole-workload forwards)")
+    ap.add_argument("--ref-sub-steps", type=int, default=3,
+                    help="reference arm: steps of each non-headline configuration")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-torch-gpu", action="store_true", help="skip the torch GPU reference column")
     ap.add_argument("--linear-variant", type=int, default=0,
                     help="tensor-core GEMM tiling: 0 auto (single-CTA), 1 single-CTA tiles, 2 CTA-pair tiles")
     ap.add_argument("--attn-variant", type=int, default=0,

@@ -144,6 +144,17 @@ WIDEK_API int widek_swap01(const void* src, void* dst, int64_t a, int64_t b,
 WIDEK_API int widek_pack(const void* const* srcs, int64_t n, void* dst, int64_t b,
                int64_t inner_bytes, void* stream);
 
+/* Strided 2-D copy: rows of row_bytes bytes from src (row pitch src_pitch
+ * bytes) to dst (row pitch dst_pitch bytes); pitches >= row_bytes.
+ * Used where N is sharded over GPUs: a rank's channel slice
+ * x[:, lo*C:hi*C] of the packed [B, N*C, ...] input, and the placement of
+ * gathered rank outputs into the full packed output. No reference
+ * counterpart: the reference runs on one device
+ * (wide_compiler/core/traced_wide.py:463-469 and :527-532 are the
+ * single-device unpack / pack this slices). */
+WIDEK_API int widek_copy2d(const void* src, int64_t src_pitch, void* dst, int64_t dst_pitch,
+                           int64_t rows, int64_t row_bytes, void* stream);
+
 /* ---- elementwise glue --------------------------------------------------- */
 
 #define WIDEK_UNARY_RELU 0
@@ -211,7 +222,10 @@ WIDEK_API int widek_batchnorm_train_fwd(const void* x, void* y, const void* weig
  * address (cudaGetSymbolAddress), so make that first call before any stream
  * capture. All calls share the array: calls that overlap on the GPU race and
  * must be serialized by the caller. Nothing in the array has to start at zero
- * (every slot is written before it is read). Allocates nothing. */
+ * (every slot is written before it is read). Allocates nothing.
+ * The resolved address is kept for the life of the process: do not use this
+ * entry point across a cudaDeviceReset of a device it has run on (the array's
+ * address on that device may change). */
 WIDEK_API int widek_batchnorm_train_fwd_noalloc(const void* x, void* y, const void* weight,
                                                 const void* bias, void* running_mean,
                                                 void* running_var, float* save_mean,

@@ -404,3 +404,33 @@ def attention_ln_ref_dtype(x, q_weight, kv_weight, out_weight, heads, ln_w, ln_b
     mean = y.mean(dim=-1, keepdim=True)
     var = y.var(dim=-1, unbiased=False, keepdim=True)
     return (y - mean) / torch.sqrt(var + eps) * ln_w.view(n, 1, 1, d) + ln_b.view(n, 1, 1, d)
+
+
+def batchnorm2d_ref_dtype(x, running_mean, running_var, weight, bias, training, momentum=0.1, eps=1e-5):
+    """wide_batchnorm_2d.py:53-72 in the input dtype: permute to the
+    channel-packed [B, N*C, H, W] layout, nn.BatchNorm2d(N*C) (batch
+    statistics and the running update when training), permute back."""
+    n, b, c, h, w = x.shape
+    p = x.permute(1, 0, 2, 3, 4).reshape(b, n * c, h, w)
+    o = F.batch_norm(p, running_mean, running_var, weight, bias, training, momentum, eps)
+    return o.view(b, n, c, h, w).permute(1, 0, 2, 3, 4).contiguous()
+
+
+def groupnorm_ref_dtype(x, groups, weight, bias, eps=1e-5):
+    """wide_groupnorm.py:90-117 in the input dtype: channel-packed
+    nn.GroupNorm(N*G, N*C), then back to N-first."""
+    n, b, c = x.shape[:3]
+    sp = x.shape[3:]
+    p = x.permute(1, 0, 2, *range(3, x.dim())).reshape(b, n * c, *sp)
+    o = F.group_norm(p, n * groups, weight, bias, eps)
+    return o.view(b, n, c, *sp).permute(1, 0, 2, *range(3, x.dim())).contiguous()
+
+
+def layernorm_ref_dtype(x, weight_flat, bias_flat, n, d, eps=1e-5):
+    """wide_layernorm.py:41-67 in the input dtype (mean, biased var, divide
+    by sqrt, per-model affine)."""
+    wgt = weight_flat.view(n, *([1] * (x.dim() - 2)), d)
+    bs = bias_flat.view(n, *([1] * (x.dim() - 2)), d)
+    mean = x.mean(dim=-1, keepdim=True)
+    var = x.var(dim=-1, unbiased=False, keepdim=True)
+    return (x - mean) / torch.sqrt(var + eps) * wgt + bs

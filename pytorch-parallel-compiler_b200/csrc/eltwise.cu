@@ -155,6 +155,45 @@ __global__ void __launch_bounds__(kRowThreads) swap01_rows_kernel(const U* __res
     }
 }
 
+// Strided 2-D copy: dst[r * dst_pitch + k] = src[r * src_pitch + k] for
+// k < row_units (pitches in units of U); jobs are (row, chunk) pairs as in
+// swap01_rows_kernel.
+template <typename U>
+__global__ void __launch_bounds__(kRowThreads) copy2d_kernel(const U* __restrict__ src, int64_t src_pitch,
+                                                             U* __restrict__ dst, int64_t dst_pitch, int64_t rows,
+                                                             int64_t row_units) {
+    const int64_t chunks = (row_units + kRowChunk - 1) / kRowChunk;
+    const int64_t jobs = rows * chunks;
+    for (int64_t job = blockIdx.x; job < jobs; job += gridDim.x) {
+        const int64_t r = job / chunks;
+        const int64_t c0 = (job - r * chunks) * kRowChunk;
+        const U* s = src + r * src_pitch;
+        U* d = dst + r * dst_pitch;
+        U v[kRowUnroll];
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; ++u) {
+            const int64_t k = c0 + u * kRowThreads + threadIdx.x;
+            if (k < row_units) v[u] = s[k];
+        }
+#pragma unroll
+        for (int u = 0; u < kRowUnroll; ++u) {
+            const int64_t k = c0 + u * kRowThreads + threadIdx.x;
+            if (k < row_units) d[k] = v[u];
+        }
+    }
+}
+
+template <typename U>
+void launch_copy2d(const void* src, int64_t src_pitch, void* dst, int64_t dst_pitch, int64_t rows,
+                   int64_t row_bytes, cudaStream_t st) {
+    constexpr int64_t u = sizeof(U);
+    const int64_t ru = row_bytes / u;
+    const int64_t jobs = rows * ((ru + kRowChunk - 1) / kRowChunk);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(jobs, (int64_t)sm_count(current_device()) * 8));
+    copy2d_kernel<U><<<grid, kRowThreads, 0, st>>>(static_cast<const U*>(src), src_pitch / u, static_cast<U*>(dst),
+                                                   dst_pitch / u, rows, ru);
+}
+
 constexpr int kPackMax = 64;
 struct PackPtrs {
     const void* p[kPackMax];
@@ -232,6 +271,31 @@ int widek_swap01(const void* src, void* dst, int64_t a, int64_t b, int64_t inner
             static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), a, b, inner_bytes);
     }
     return check_launch("widek_swap01");
+}
+
+int widek_copy2d(const void* src, int64_t src_pitch, void* dst, int64_t dst_pitch, int64_t rows, int64_t row_bytes,
+                 void* stream) {
+    using namespace widek;
+    if (rows < 0 || row_bytes < 0) return set_error(WIDEK_ERR_INVALID, "copy2d: negative size");
+    if (rows == 0 || row_bytes == 0) return WIDEK_OK;
+    if (!src || !dst) return set_error(WIDEK_ERR_INVALID, "copy2d: null pointer");
+    if (src_pitch < row_bytes || dst_pitch < row_bytes)
+        return set_error(WIDEK_ERR_INVALID, "copy2d: pitch (%lld, %lld) below the row size %lld", (long long)src_pitch,
+                         (long long)dst_pitch, (long long)row_bytes);
+    cudaStream_t st = (cudaStream_t)stream;
+    const uintptr_t align = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) |
+                            (uintptr_t)src_pitch | (uintptr_t)dst_pitch | (uintptr_t)row_bytes;
+    if ((align & 15) == 0)
+        launch_copy2d<uint4>(src, src_pitch, dst, dst_pitch, rows, row_bytes, st);
+    else if ((align & 7) == 0)
+        launch_copy2d<uint2>(src, src_pitch, dst, dst_pitch, rows, row_bytes, st);
+    else if ((align & 3) == 0)
+        launch_copy2d<uint32_t>(src, src_pitch, dst, dst_pitch, rows, row_bytes, st);
+    else if ((align & 1) == 0)
+        launch_copy2d<uint16_t>(src, src_pitch, dst, dst_pitch, rows, row_bytes, st);
+    else
+        launch_copy2d<uint8_t>(src, src_pitch, dst, dst_pitch, rows, row_bytes, st);
+    return check_launch("widek_copy2d");
 }
 
 int widek_pack(const void* const* srcs, int64_t n, void* dst, int64_t b, int64_t inner_bytes, void* stream) {

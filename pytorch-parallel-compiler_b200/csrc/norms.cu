@@ -553,6 +553,11 @@ struct BnTrainNoAlloc {
         const int64_t channels = n * c;
         const int64_t cnt = batch * l;
         int chunks = bn_chunks(channels, cnt, sm_count(current_device()));
+        // bn_chunks gives more than one chunk only when channels < 4 * SMs, and
+        // then channels * chunks < channels + 4 * SMs < 8 * SMs, far below the
+        // array's 65536 (channel, chunk) pairs; with one chunk the caller's
+        // channel limit makes it fit. So this cap never binds on a real GPU;
+        // it is kept as a guard on the array bound.
         const int64_t fit = kNoAllocScratchDoubles / (2 * channels);   // >= 1 (checked by the caller)
         if (chunks > fit) chunks = (int)fit;
         dim3 grid((unsigned)channels, (unsigned)chunks);

@@ -18,6 +18,11 @@ one CUDA graph per input signature and replays it:
 * Recording happens on the first call with a signature: two eager warm-up
   runs on a side stream (they build the fusion plan and set the kernels'
   shared-memory limits), then capture. Later calls replay.
+* Tensors derived from the parameters (folded BatchNorm, repacked conv
+  weights, the fused [q; kv] projection, LSTM diagonal blocks) are rebuilt
+  inside the graph, so a replay always reads the live parameters: in-place
+  updates (``mul_``, an optimizer step, ``load_state_dict``, and writes
+  through ``.data``) are seen by the next replay without recording again.
 * Like torch.compile's 'reduce-overhead' mode, a call returns the graph's
   static output tensor, which the next replay of the same graph
   overwrites; ``clone()`` it to keep it.

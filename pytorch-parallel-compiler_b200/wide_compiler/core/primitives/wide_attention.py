@@ -21,7 +21,7 @@ from typing import List, Optional, Tuple, Union
 import torch
 from torch import Tensor, nn
 
-from ... import ops
+from ... import _derived, ops
 
 
 class AttentionStrategy(Enum):
@@ -60,7 +60,6 @@ class WideAttention(nn.Module):
             self.out_bias = nn.Parameter(torch.empty(n, d_model))
         else:
             self.register_parameter('out_bias', None)
-        self._qkv_cache = None
         self._reset_parameters()
 
     @property
@@ -80,17 +79,15 @@ class WideAttention(nn.Module):
 
     def _fused_qkv(self) -> Tuple[Tensor, Optional[Tensor]]:
         """[q; kv] weight [N, 3D, D] (and bias [N, 3D]) for self-attention,
-        rebuilt only when a parameter changed (tracked by tensor version)."""
-        key = (self.q_weight._version, self.kv_weight._version, self.q_weight.data_ptr(),
-               self.kv_weight.data_ptr(), self.q_weight.dtype,
-               None if self.q_bias is None else (self.q_bias._version, self.kv_bias._version,
-                                                 self.q_bias.data_ptr(), self.kv_bias.data_ptr()))
-        if self._qkv_cache is None or self._qkv_cache[0] != key:
+        kept between forwards while the four parameters are unchanged
+        (``wide_compiler._derived``: rebuilt after in-place updates and inside
+        every CUDA-graph capture)."""
+        def build():
             with torch.no_grad():
                 w = torch.cat([self.q_weight, self.kv_weight], dim=1).contiguous()
                 b = None if self.q_bias is None else torch.cat([self.q_bias, self.kv_bias], dim=1).contiguous()
-            self._qkv_cache = (key, w, b)
-        return self._qkv_cache[1], self._qkv_cache[2]
+            return w, b
+        return _derived.cached(self, 'qkv', (self.q_weight, self.kv_weight, self.q_bias, self.kv_bias), build)
 
     def forward(self, query: Tensor, key: Optional[Tensor] = None, value: Optional[Tensor] = None,
                 attn_mask: Optional[Tensor] = None, is_causal: bool = False,

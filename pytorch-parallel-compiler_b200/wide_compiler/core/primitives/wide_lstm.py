@@ -15,7 +15,7 @@ from typing import List, Optional, Tuple, Union
 import torch
 from torch import Tensor, nn
 
-from ... import ops
+from ... import _derived, ops
 
 
 class LSTMStrategy(Enum):
@@ -57,7 +57,6 @@ class WideLSTM(nn.Module):
         else:
             self.register_parameter('bias_ih', None)
             self.register_parameter('bias_hh', None)
-        self._block_cache = None
         self._init_weights()
 
     @property
@@ -78,25 +77,24 @@ class WideLSTM(nn.Module):
                 self.bias_hh.zero_()
 
     def _blocks(self) -> Tuple[Tensor, Tensor]:
-        """Diagonal blocks [N, 4H, I] and [N, 4H, H], cached on parameter
-        versions (built afresh, differentiably, when autograd needs them)."""
+        """Diagonal blocks [N, 4H, I] and [N, 4H, H], kept between forwards
+        while the parameters are unchanged (``wide_compiler._derived``:
+        rebuilt after in-place updates and inside every CUDA-graph capture);
+        built afresh, differentiably, when autograd needs them."""
         if torch.is_grad_enabled() and (self.weight_ih.requires_grad or self.weight_hh.requires_grad):
             n, h, i = self.n, self.hidden_size, self.input_size
             idx = torch.arange(n, device=self.weight_ih.device)
             return (self.weight_ih.view(n, 4 * h, n, i)[idx, :, idx, :],
                     self.weight_hh.view(n, 4 * h, n, h)[idx, :, idx, :])
-        key = (self.weight_ih._version, self.weight_hh._version, self.weight_ih.data_ptr(),
-               self.weight_hh.data_ptr(), self.weight_ih.dtype, self.weight_ih.device)
-        if self._block_cache is None or self._block_cache[0] != key:
+
+        def build():
             n, h, i = self.n, self.hidden_size, self.input_size
             with torch.no_grad():
                 wih = self.weight_ih.view(n, 4 * h, n, i)
                 whh = self.weight_hh.view(n, 4 * h, n, h)
                 idx = torch.arange(n, device=self.weight_ih.device)
-                bih = wih[idx, :, idx, :].contiguous()       # [N, 4H, I]
-                bhh = whh[idx, :, idx, :].contiguous()       # [N, 4H, H]
-            self._block_cache = (key, bih, bhh)
-        return self._block_cache[1], self._block_cache[2]
+                return wih[idx, :, idx, :].contiguous(), whh[idx, :, idx, :].contiguous()   # [N, 4H, I], [N, 4H, H]
+        return _derived.cached(self, 'blocks', (self.weight_ih, self.weight_hh), build)
 
     def forward(self, x: Tensor, hx: Optional[Tuple[Tensor, Tensor]] = None
                 ) -> Tuple[Tensor, Tuple[Tensor, Tensor]]:

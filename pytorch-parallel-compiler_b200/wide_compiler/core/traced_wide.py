@@ -31,7 +31,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 from torch import Tensor
 
-from .. import ops
+from .. import _derived, ops
 from .ensemble_util import pack_inputs, unpack_outputs  # noqa: F401  (re-exported API)
 from .primitives import (WideAttention, WideBatchNorm1d, WideBatchNorm2d, WideConv1d, WideConv2d, WideConv3d,
                          WideEmbedding, WideGroupNorm, WideGRU, WideInstanceNorm1d, WideInstanceNorm2d,
@@ -633,32 +633,29 @@ class TracedWideModel(nn.Module):
     def _folded_bn(self, bn_mod: nn.Module, dtype: torch.dtype):
         """The eval-mode BatchNorm as (scale, shift) in `dtype`, kept from one
         forward to the next (folding it costs about six small device
-        launches per conv group). The entry holds the module's four tensors
-        and their version counters, so replacing a tensor or changing it in
-        place (``copy_``, an optimizer step, training-mode statistics)
-        recomputes it. Nothing is cached while a CUDA graph is being
-        captured, so that a recorded graph folds the module's tensors on
-        every replay, nor for inference-mode tensors (no version counter)."""
+        launches per conv group). The entry is keyed on the module's four
+        tensors (identity, storage, version) and eps
+        (``wide_compiler._derived``), so replacing a tensor or changing it
+        in place (``copy_``, an optimizer step, ``load_state_dict``,
+        training-mode statistics) recomputes it; during CUDA-graph capture
+        the fold is recorded into the graph, so replays fold the live
+        tensors. In-place writes through ``.data`` leave the version
+        unchanged: call ``invalidate_caches()`` after them."""
         tensors = (bn_mod.running_mean, bn_mod.running_var, bn_mod.weight, bn_mod.bias)
 
         def fold():
             scale, shift = _bn_fold(bn_mod)
             return scale.to(dtype), shift.to(dtype)
 
-        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
-            return fold()
-        try:
-            versions = tuple(None if x is None else x._version for x in tensors)
-        except RuntimeError:
-            return fold()
-        cache = self.__dict__.setdefault('_bn_fold_cache', {})
-        hit = cache.get(id(bn_mod))
-        if (hit is not None and hit[0] == (dtype, float(bn_mod.eps), versions)
-                and all(a is b for a, b in zip(hit[1], tensors))):
-            return hit[2]
-        folded = fold()
-        cache[id(bn_mod)] = ((dtype, float(bn_mod.eps), versions), tensors, folded)
-        return folded
+        return _derived.cached(bn_mod, ('bn_fold', dtype), tensors, fold, extra=float(bn_mod.eps))
+
+    def invalidate_caches(self) -> None:
+        """Drops every tensor derived from the parameters (folded BatchNorm,
+        repacked conv weights, fused attention projections, LSTM blocks);
+        the next forward rebuilds them. Needed only after in-place writes
+        through ``.data`` (``p.data.copy_(...)``), which do not bump the
+        version counters the caches are keyed on."""
+        _derived.invalidate_caches(self)
 
     def _clast_ok(self, nxt: Dict[str, Any], op, t: Tensor, in_l: int, w, st, pd, dl) -> bool:
         """Whether the next conv group can read this group's output in the

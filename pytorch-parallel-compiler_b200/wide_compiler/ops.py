@@ -16,6 +16,7 @@ import torch
 from torch import Tensor
 
 from . import _autograd as _AG
+from . import _derived
 from . import _native as N
 
 ACT_NONE, ACT_RELU, ACT_GELU = N.ACT_NONE, N.ACT_RELU, N.ACT_GELU
@@ -506,24 +507,19 @@ def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optiona
 # ---------------------------------------------------------------------------
 
 def _packed_weight(weight: Tensor, rows: int, cin: int, taps: int, dev) -> Tensor:
-    """[rows, cin, taps] -> [rows, taps, cin] for the tensor-core conv, cached
-    on the weight tensor object and rebuilt when its version, storage or dtype
-    changes."""
-    key = (weight._version, weight.data_ptr(), weight.dtype, tuple(weight.shape))
-    hit = getattr(weight, '_widek_packed', None)
-    if hit is not None and hit[0] == key:
-        return hit[1]
-    wd = _dense(weight.detach())
-    wp = torch.empty(rows, taps, cin, device=dev, dtype=weight.dtype)
-    with _guard(dev):
-        rc = N.lib().widek_conv_pack_weight(wd.data_ptr(), wp.data_ptr(), rows, cin, taps, wd.element_size(),
-                                            N.stream_ptr(dev))
-    N.check(rc, "widek_conv_pack_weight")
-    try:
-        weight._widek_packed = (key, wp)
-    except (AttributeError, RuntimeError):
-        pass
-    return wp
+    """[rows, cin, taps] -> [rows, taps, cin] for the tensor-core conv, kept
+    on the weight tensor between forwards (see ``_derived``: rebuilt when its
+    version, storage, dtype or shape changes, and inside every CUDA-graph
+    capture)."""
+    def build():
+        wd = _dense(weight.detach())
+        wp = torch.empty(rows, taps, cin, device=dev, dtype=weight.dtype)
+        with _guard(dev):
+            rc = N.lib().widek_conv_pack_weight(wd.data_ptr(), wp.data_ptr(), rows, cin, taps, wd.element_size(),
+                                                N.stream_ptr(dev))
+        N.check(rc, "widek_conv_pack_weight")
+        return wp
+    return _derived.cached(weight, 'conv_packed', (weight,), build, extra=(rows, cin, taps))
 
 
 LAYOUT_NFIRST, LAYOUT_PACKED, LAYOUT_CLAST = 0, 1, 2

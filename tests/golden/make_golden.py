@@ -265,5 +265,6 @@ if __name__ == '__main__':
     ap.add_argument('--root', default=refimport.DEFAULT_ROOT)
     a = ap.parse_args()
     if not refimport.available(a.root):
-        sys.exit(f"reference not found under {a.root}")
+        sys.exit(f"reference not found under {a.root!r}: pass --root or set WIDE_REFERENCE_ROOT to the "
+                 "checkout that holds wide_compiler/")
     make_all(a.root)

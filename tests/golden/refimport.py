@@ -8,12 +8,14 @@ import importlib.util
 import os
 import sys
 
-DEFAULT_ROOT = os.environ.get("WIDE_REFERENCE_ROOT", "/root/reference")
+# The reference checkout's root directory (the one holding wide_compiler/),
+# given by the environment; there is no built-in default.
+DEFAULT_ROOT = os.environ.get("WIDE_REFERENCE_ROOT", "")
 ALIAS = "ref_wide_compiler"
 
 
 def available(root: str = DEFAULT_ROOT) -> bool:
-    return os.path.exists(os.path.join(root, "wide_compiler", "__init__.py"))
+    return bool(root) and os.path.exists(os.path.join(root, "wide_compiler", "__init__.py"))
 
 
 def load(root: str = DEFAULT_ROOT):

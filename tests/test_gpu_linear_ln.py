@@ -148,20 +148,35 @@ def test_binary(op):
                                          ((2, 3, 5), torch.bfloat16), ((100, 32, 64), torch.float32)])
 def test_swap01_and_pack(shape, dtype):
     x = torch.randn(*shape).to(dtype)
+    # byte-moving kernels: bit-exact
     y = ops.swap01(x.to(DEV))
-    torch.testing.assert_close(y.cpu(), x.transpose(0, 1).contiguous())
+    assert torch.equal(y.cpu(), x.transpose(0, 1).contiguous())
     inputs = [torch.randn(*shape[1:]).to(dtype) for _ in range(shape[0])]
     packed = wc.pack([t.to(DEV) for t in inputs])
-    torch.testing.assert_close(packed.cpu(), O.pack_inputs(inputs).to(dtype))
+    assert torch.equal(packed.cpu(), O.pack_inputs(inputs).to(dtype))
     outs = wc.unpack(packed, shape[0])
     for a, b in zip(outs, inputs):
-        torch.testing.assert_close(a.cpu(), b)
+        assert torch.equal(a.cpu(), b)
 
 
 def test_pack_many_sources():
     inputs = [torch.randn(3, 8) for _ in range(150)]   # more than one launch of 64 pointers
     packed = wc.pack([t.to(DEV) for t in inputs])
-    torch.testing.assert_close(packed.cpu(), O.pack_inputs(inputs))
+    assert torch.equal(packed.cpu(), O.pack_inputs(inputs))
+
+
+@pytest.mark.parametrize("shape", [(32, 6400, 32, 32), (7, 3, 5, 1, 9)])
+def test_swap01_large_and_odd_bit_exact(shape):
+    """The boundary transpose at cfg3's size (419 MB bf16) and at an odd
+    shape whose rows are not 16-byte multiples."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    b, nc = shape[0], shape[1]
+    x = torch.randn(*shape, device=DEV, generator=g).to(torch.bfloat16)
+    n = 100 if nc == 6400 else 3
+    xv = x.view(b, n, nc // n, *shape[2:])
+    y = ops.swap01(xv)
+    assert torch.equal(y, xv.transpose(0, 1).contiguous())
+    assert torch.equal(ops.swap01(y), xv)
 
 
 def test_traced_mlp_golden():

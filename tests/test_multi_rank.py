@@ -45,7 +45,12 @@ def _worker(rank, world, port, n_total, fail_rank, result_path):
         if rank == fail_rank:
             raise RuntimeError("injected failure before the collective")
         got = parallel.gather_outputs(full[a:b] * 1.0, n_total)
-        torch.save({"ok": bool(torch.equal(got, full))}, f"{result_path}.{rank}")
+        # channel-packed outputs [B, n_local*F, S] -> [B, N*F, S]
+        bsz, f, sp = 3, 2, 5
+        packed_full = torch.arange(bsz * n_total * f * sp, dtype=torch.float32).view(bsz, n_total * f, sp)
+        got_p = parallel.gather_packed(packed_full[:, a * f:b * f].contiguous(), n_total)
+        ok = bool(torch.equal(got, full)) and bool(torch.equal(got_p, packed_full))
+        torch.save({"ok": ok}, f"{result_path}.{rank}")
     except Exception as e:  # report on the host, never on a device
         torch.save({"ok": False, "error": repr(e)}, f"{result_path}.{rank}")
     finally:
@@ -72,6 +77,7 @@ def _run(world, n_total, fail_rank, tmp_path):
 
 @pytest.mark.parametrize("n_total", [4, 5])
 def test_gather_outputs_gloo_world2(tmp_path, n_total):
+    """Even (4) and ragged (5) splits of N-first and channel-packed outputs."""
     res = _run(2, n_total, -1, tmp_path)
     assert all(r["ok"] for r in res), res
 
@@ -80,3 +86,18 @@ def test_failed_rank_is_detected_not_hung(tmp_path):
     res = _run(2, 6, 1, tmp_path)
     assert not res[1]["ok"] and "injected" in res[1]["error"]
     assert not res[0]["ok"] and "error" in res[0]      # rank 0's collective errored (timeout / peer closed)
+
+
+def test_copy_rows_slices_a_rank_s_channels():
+    """The strided copy that cuts one rank's channel range out of the full
+    packed input (the CPU form of the device kernel's addressing)."""
+    n_total, c, bsz, sp = 7, 3, 4, 6
+    x = torch.randn(bsz, n_total * c, sp)
+    for world in (2, 3):
+        for rank in range(world):
+            lo, hi = parallel.shard_range(n_total, world, rank)
+            inner = c * sp
+            out = torch.empty(bsz, (hi - lo) * c, sp)
+            parallel.copy_rows(x.view(bsz, -1)[:, lo * inner:], n_total * inner * 4, out, (hi - lo) * inner * 4,
+                               bsz, (hi - lo) * inner * 4)
+            assert torch.equal(out, x[:, lo * c:hi * c])

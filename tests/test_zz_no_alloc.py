@@ -70,8 +70,9 @@ def test_noalloc_matches_workspace_entry_point_two_calls(dtype):
 
 
 def test_noalloc_saved_statistics_and_many_chunks():
-    """Few channels with many elements: the chunk count is capped by the fixed
-    scratch; saved mean / inverse std match the batch statistics."""
+    """Few channels with many elements, so the reduction is split into many
+    chunks per channel (their partial sums all live in the fixed array);
+    saved mean / inverse std match the batch statistics."""
     lib = N.load()
     n, bsz, c, l = 2, 64, 3, 4096
     x = torch.randn(n, bsz, c, l, device=DEV) * 2 + 1
