@@ -694,7 +694,14 @@ class LayerNormWl(_Norm):
             f"one full pass per rep (all {n} models), bf16, torch CPU mean/var/normalize/affine"
 
 
-def make_workload(name):
+def make_workload(name, models=None):
+    wl = _make_workload(name)
+    if models:
+        wl.n_total = models
+    return wl
+
+
+def _make_workload(name):
     return {
         "cfg1": lambda: MlpCfg1(), "cfg2": lambda: LinearCfg2(), "cfg3": lambda: ResBlockCfg3(),
         "cfg4gru": lambda: RnnCfg4("gru"), "cfg4lstm": lambda: RnnCfg4("lstm"), "cfg5": lambda: AttnCfg5(),
@@ -739,7 +746,7 @@ def run_reference(args):
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
     names = _workload_names(args)
-    head = make_workload(names[0])
+    head = make_workload(names[0], args.models)
     value, wall, desc = _cpu_line(head, args.steps, args.warmup, args.ref_step_seconds)
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -828,7 +835,7 @@ def _gather_fn(wl, ctx):
 def measure(name, ctx, clocks):
     from wide_compiler import _native as N
     args = ctx.args
-    wl = make_workload(name)
+    wl = make_workload(name, args.models)
     if args.weak:
         lo, hi = 0, wl.n_total
         wl._world_rank = (1, 0)
@@ -852,9 +859,18 @@ def measure(name, ctx, clocks):
     for _ in range(max(args.warmup, 3)):
         step()
     ctx.barrier()
+    # Clock window: untimed steps for --clock-window seconds right before the
+    # timed region, so that the 100 ms nvidia-smi samples see the GPU under
+    # this workload's load even when the timed region itself is a few ms.
+    mark0 = clocks.mark()
+    t_cw = time.perf_counter()
+    while time.perf_counter() - t_cw < args.clock_window:
+        for _ in range(8):
+            step()
+        torch.cuda.synchronize(ctx.dev)
+    ctx.barrier()
     stream = torch.cuda.current_stream(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    mark0 = clocks.mark()
     launches0 = N.launch_count()
     with N.LaunchTimer() as timer:
         e0.record(stream)
@@ -866,7 +882,6 @@ def measure(name, ctx, clocks):
     gpu_launches = launches + (replay_launches or 0) * steps
     ms_local = e0.elapsed_time(e1) / steps
     ms = ctx.max_over_ranks(ms_local)
-    clk = clocks.summary(mark0, clocks.mark())
     kern = timer.summary()
 
     # End to end through the public call: pinned host input uploaded, forward,
@@ -914,6 +929,9 @@ def measure(name, ctx, clocks):
     e1.record(stream)
     ctx.barrier()
     ms_e2e = ctx.max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    clk = clocks.summary(mark0, clocks.mark())
+    clk["window"] = (f"nvidia-smi samples every 100 ms over {args.clock_window:.1f} s of untimed steps just "
+                     f"before the timed region, the timed region and the e2e loop")
 
     total_models = wl.n_total if not args.weak else wl.n_total * ctx.world
     samples = wl.samples(total_models)
@@ -1061,7 +1079,11 @@ def main():
     ap.add_argument("--workload", default="all", choices=["all"] + ORDER,
                     help="all: the cfg3 headline plus every other configuration under 'configs'")
     ap.add_argument("--sub-steps", type=int, default=20, help="timed steps of each non-headline configuration")
+    ap.add_argument("--models", type=int, default=None,
+                    help="override the number of models N (reduced cases for profiling captures only)")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--clock-window", type=float, default=0.5,
+                    help="seconds of untimed steps before each timed region while clocks are sampled")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--weak", action="store_true", help="every rank runs all N models (weak scaling)")
     ap.add_argument("--gather", action="store_true", help="include the optional output all-gather in every step")

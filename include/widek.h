@@ -357,6 +357,18 @@ WIDEK_API int widek_conv_fwd_ex(const void* x, const void* w, const void* w_pack
                                 int residual_first, int in_layout, int out_layout, int res_layout,
                                 int dtype, void* stream);
 
+/* Which kernel widek_conv_fwd_ex would run for this geometry, dtype and
+ * layouts (pointers assumed 16-byte aligned, workspace large enough):
+ * WIDEK_CONV_PATH_DIRECT (CUDA cores), _TAPS (tcgen05 per-tap implicit GEMM
+ * on channels-last input), _HALO (tcgen05 halo-reuse on channels-last
+ * input), or -1 when the combination is not served. Launches nothing.
+ * No counterpart in the reference (a query for tests and planners). */
+#define WIDEK_CONV_PATH_DIRECT 0
+#define WIDEK_CONV_PATH_TAPS 1
+#define WIDEK_CONV_PATH_HALO 2
+WIDEK_API int widek_conv_path(const int64_t* geom, int dtype, int in_layout, int out_layout,
+                              int res_layout, int has_residual);
+
 /* 1 if widek_conv_fwd_ex would run this geometry/dtype/layout combination
  * (assuming 16-byte aligned device pointers and a large enough workspace),
  * else 0. Launches nothing. */

@@ -585,6 +585,61 @@ __device__ __forceinline__ void halo_issue_subtile(uint32_t d_tmem, uint64_t a_d
     }
 }
 
+// 16 TMEM lanes x 8 consecutive 32-bit columns, 8 times along the columns
+// (64 columns): thread t receives, for column group k, r[4k], r[4k+1] from
+// lane (base + t/4), columns 8k + 2(t%4) and + 1, and r[4k+2], r[4k+3] from
+// lane (base + 8 + t/4), the same columns.
+__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x8.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+          "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+// Four 8x8 16-bit matrices whose rows (16 bytes each) start at the addresses
+// given by lanes 8i..8i+7 for matrix i, transposed: register i of thread t
+// holds the matrix's elements (row 2(t%4), column t/4) and (row 2(t%4)+1,
+// column t/4), low half first. stmatrix...trans is the inverse.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&v)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void stsm_x4_trans(uint32_t addr, const uint32_t (&v)[4]) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3])
+                 : "memory");
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+
 template <typename T, bool RES_TMA, int KH, int KW, bool OUT_CL>
 __global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -794,7 +849,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         // pairs stay in registers. The N-first / packed output reads them
         // from shared memory.
         const int ch_half = lane >> 4;
-        float ps[OUT_CL ? HBN / 2 : 1], po[OUT_CL ? HBN / 2 : 1];
+        // N-first / packed output: the lane's 16 channels are 8k + 2(lane%4) + {0, 1}
+        // (the 16x256b TMEM read), their pairs likewise held in registers.
+        float ps[HBN / 2], po[HBN / 2];
         // Residual tile of `tile` into buffer `rb` (elected thread only).
         auto load_residual = [&](int64_t tile, int rb) {
             int model, nt, b, mt;
@@ -802,10 +859,10 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             const int ho0 = (mt / g.tiles_w) * g.th, wo0 = (mt % g.tiles_w) * g.tw;
             mbar_arrive_expect_tx(&res_full[rb], S::TILE);
             if (g.res5)
-                tma_load_5d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN, b, model,
+                tma_load_5d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, nt * HBN, ho0, b, model,
                             l2_policy_evict_first());
             else
-                tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, ho0, nt * HBN,
+                tma_load_4d(sBuf + rb * (HBN * BM), &tm_r, &res_full[rb], wo0, nt * HBN, ho0,
                             model * g.batch + b, l2_policy_evict_first());
             ++res_issued;
         };
@@ -847,10 +904,10 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 par_key = key;
             }
             epi_bar_sync();
-            if (OUT_CL && fresh) {
+            if (fresh) {
 #pragma unroll
-                for (int m = 0; m < (OUT_CL ? HBN / 2 : 0); ++m) {
-                    const float2 pp = sPar[32 * ch_half + m];
+                for (int m = 0; m < HBN / 2; ++m) {
+                    const float2 pp = OUT_CL ? sPar[32 * ch_half + m] : sPar[8 * (m >> 1) + 2 * (lane & 3) + (m & 1)];
                     ps[m] = pp.x;
                     po[m] = pp.y;
                 }
@@ -897,32 +954,90 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 else
                     epilogue(std::integral_constant<int, WIDEK_ACT_NONE>{});
             } else {
-                const int r = q * 32 + lane;
+                // N-first / packed output through [row][channel][column]
+                // staging (TMA box {tw, 64, th}; 32-byte swizzle for tw = 16):
+                // per half warp of TMEM lanes (16 pixels = pixel groups g0,
+                // g1 of 8) the 16x256b read gives each thread 2 channels of
+                // one pixel per group and column block, which is the
+                // fragment of an 8x8 transposed ldmatrix / stmatrix, so the
+                // residual is read and the output written 16 bytes per row.
+                const uint32_t buf_addr = smem_addr(sOut);
+                const int mi = lane >> 3, ri = lane & 7;     // this lane's matrix and row in an x4 access
+                // The activation and the residual order are fixed per loop copy
+                // (picked once per tile): the unrolled body then has no
+                // per-value branches, which keeps it small in the
+                // instruction cache next to the MMA and TMA roles.
+                auto epilogue = [&](auto act_c, auto rf_c) {
+                    constexpr int ACT = decltype(act_c)::value;
+                    constexpr bool RF = decltype(rf_c)::value;
 #pragma unroll 1
-                for (int c = 0; c < HBN; c += 32) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * HBN + c) + ((uint32_t)(q * 32) << 16), v);
-                    // The chunk's 32 residual values are read before any of
-                    // its outputs is written over them.
-                    float rv[32];
-                    if (res) {
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t v[32];
+                        tmem_ld_16x256b_x8(tmem_base + (uint32_t)(acc * HBN) + ((uint32_t)(q * 32 + 16 * h) << 16), v);
+                        // row address of matrix mi = (group mi & 1, column block 2*jj + (mi >> 1))
+                        const int pix = q * 32 + 16 * h + 8 * (mi & 1);   // first pixel of the group
+                        const int py = pix / g.tw, px = pix - py * g.tw;
+                        const uint32_t row0 = (uint32_t)(((py * HBN + 8 * (mi >> 1) + ri) * g.tw + px) * 2);
+                        const uint32_t swz = g.tw == 16 ? 1u : 0u;
+                        uint32_t rv[16];
+                        if constexpr (RES_TMA) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) rv[j] = to_f<T>(sOut[(c + j) * BM + r]);
+                            for (int jj = 0; jj < 4; ++jj) {
+                                uint32_t o = row0 + (uint32_t)(16 * jj * g.tw * 2);
+                                o ^= (((o >> 7) & 1u) << 4) * swz;
+                                uint32_t t4[4];
+                                ldsm_x4_trans(buf_addr + o, t4);
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) rv[4 * jj + u] = t4[u];
+                            }
+                        }
+                        tmem_ld_wait();
+                        uint32_t ov[16];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            // column block k: registers 4k..4k+3 = (g0: ch lo, hi), (g1: ch lo, hi);
+                            // x4 matrices per jj: (g0, 2jj), (g1, 2jj), (g0, 2jj+1), (g1, 2jj+1)
+#pragma unroll
+                            for (int gi = 0; gi < 2; ++gi) {
+                                float a0 = fmaf(__uint_as_float(v[4 * k + 2 * gi]), ps[2 * k], po[2 * k]);
+                                float a1 = fmaf(__uint_as_float(v[4 * k + 2 * gi + 1]), ps[2 * k + 1], po[2 * k + 1]);
+                                const int slot = 4 * (k >> 1) + 2 * (k & 1) + gi;
+                                if constexpr (RES_TMA && RF) {
+                                    const float2 r2 = unpack2<T>(rv[slot]);
+                                    a0 += r2.x;
+                                    a1 += r2.y;
+                                }
+                                a0 = conv_act<ACT>(a0);
+                                a1 = conv_act<ACT>(a1);
+                                if constexpr (RES_TMA && !RF) {
+                                    const float2 r2 = unpack2<T>(rv[slot]);
+                                    a0 += r2.x;
+                                    a1 += r2.y;
+                                }
+                                ov[slot] = pack2<T>(a0, a1);
+                            }
+                        }
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            uint32_t o = row0 + (uint32_t)(16 * jj * g.tw * 2);
+                            o ^= (((o >> 7) & 1u) << 4) * swz;
+                            const uint32_t t4[4] = {ov[4 * jj], ov[4 * jj + 1], ov[4 * jj + 2], ov[4 * jj + 3]};
+                            stsm_x4_trans(buf_addr + o, t4);
+                        }
                     }
-                    tmem_ld_wait();
-                    float ov[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float2 par = sPar[c + j];
-                        float val = fmaf(__uint_as_float(v[j]), par.x, par.y);
-                        if (res && e.residual_first) val += rv[j];
-                        val = conv_act_rt(val, e.act);
-                        if (res && !e.residual_first) val += rv[j];
-                        ov[j] = val;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) sOut[(c + j) * BM + r] = from_f<T>(ov[j]);
-                }
+                };
+                auto with_act = [&](auto rf_c) {
+                    if (e.act == WIDEK_ACT_RELU)
+                        epilogue(std::integral_constant<int, WIDEK_ACT_RELU>{}, rf_c);
+                    else if (e.act == WIDEK_ACT_GELU)
+                        epilogue(std::integral_constant<int, WIDEK_ACT_GELU>{}, rf_c);
+                    else
+                        epilogue(std::integral_constant<int, WIDEK_ACT_NONE>{}, rf_c);
+                };
+                if (RES_TMA && e.residual_first)
+                    with_act(std::true_type{});
+                else
+                    with_act(std::false_type{});
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
@@ -932,9 +1047,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 if (OUT_CL)
                     tma_store_4d(&tm_y, sOut, nt * HBN, wo0, ho0, (int)img);
                 else if (g.out5)
-                    tma_store_5d(&tm_y, sOut, wo0, ho0, nt * HBN, b, model);
+                    tma_store_5d(&tm_y, sOut, wo0, nt * HBN, ho0, b, model);
                 else
-                    tma_store_4d(&tm_y, sOut, wo0, ho0, nt * HBN, (int)img);
+                    tma_store_4d(&tm_y, sOut, wo0, nt * HBN, ho0, (int)img);
                 bulk_commit();
             }
         }
@@ -1077,18 +1192,23 @@ int halo_out_map(CUtensorMap* m, const void* base, const ConvGeom& cg, const Con
         const uint32_t box[4] = {HBN, (uint32_t)g.tw, (uint32_t)g.th, 1};
         return encode_tmap_tiled(m, tmap_dt<T>(), 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     }
+    // NCHW-family layouts: dims ordered {W, C, H, ...} so that a box lands in
+    // shared memory as [row][channel][column]; rows of 32 bytes (tw = 16)
+    // are 32-byte swizzled, which spreads the epilogue's 8-channel matrix
+    // rows over all banks.
+    const CUtensorMapSwizzle swz = g.tw == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
     if (layout == WIDEK_LAYOUT_PACKED) {
-        const uint64_t dims[5] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)cg.batch,
+        const uint64_t dims[5] = {(uint64_t)cg.ow, (uint64_t)cg.cout, (uint64_t)cg.oh, (uint64_t)cg.batch,
                                   (uint64_t)cg.n};
-        const uint64_t strides[4] = {(uint64_t)cg.ow * 2, sp * 2, (uint64_t)cg.n * cg.cout * sp * 2,
+        const uint64_t strides[4] = {sp * 2, (uint64_t)cg.ow * 2, (uint64_t)cg.n * cg.cout * sp * 2,
                                      (uint64_t)cg.cout * sp * 2};
-        const uint32_t box[5] = {(uint32_t)g.tw, (uint32_t)g.th, HBN, 1, 1};
-        return encode_tmap_tiled(m, tmap_dt<T>(), 5, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        const uint32_t box[5] = {(uint32_t)g.tw, HBN, (uint32_t)g.th, 1, 1};
+        return encode_tmap_tiled(m, tmap_dt<T>(), 5, base, dims, strides, box, swz);
     }
-    const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, nb};
-    const uint64_t strides[3] = {(uint64_t)cg.ow * 2, sp * 2, (uint64_t)cg.cout * sp * 2};
-    const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, HBN, 1};
-    return encode_tmap_tiled(m, tmap_dt<T>(), 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.cout, (uint64_t)cg.oh, nb};
+    const uint64_t strides[3] = {sp * 2, (uint64_t)cg.ow * 2, (uint64_t)cg.cout * sp * 2};
+    const uint32_t box[4] = {(uint32_t)g.tw, HBN, (uint32_t)g.th, 1};
+    return encode_tmap_tiled(m, tmap_dt<T>(), 4, base, dims, strides, box, swz);
 }
 
 template <typename T, bool RES_TMA, bool OUT_CL>
@@ -1155,6 +1275,7 @@ struct ConvLaunch {
     int in_layout, out_layout, res_layout;   // WIDEK_LAYOUT_*
     bool query;           // decide only: WIDEK_OK if the call would run, else WIDEK_ERR_UNSUPPORTED
     cudaStream_t st;
+    int path = -1;        // set in query mode: WIDEK_CONV_PATH_*
 
     // In query mode pointers are absent: treat them as 16-byte aligned (as
     // every caching-allocator block is) and the workspace as large enough.
@@ -1197,7 +1318,7 @@ struct ConvLaunch {
                     // channels-last) but write and add in the N-first layout.
                     if (!halo && (out_layout != WIDEK_LAYOUT_NFIRST || res_layout != WIDEK_LAYOUT_NFIRST))
                         return unsupported("output/residual layout needs the halo kernel, which does not apply");
-                    if (query) return WIDEK_OK;
+                    if (query) { path = halo ? WIDEK_CONV_PATH_HALO : WIDEK_CONV_PATH_TAPS; return WIDEK_OK; }
                     const T* xs = static_cast<const T*>(cl_in ? x : ws);
                     if (!cl_in) {
                         const int64_t packed_b = in_layout == WIDEK_LAYOUT_PACKED ? g.batch : 0;
@@ -1244,7 +1365,7 @@ struct ConvLaunch {
             }
         }
         if (!std_layouts) return unsupported("non-default layouts need the tensor-core path");
-        if (query) return WIDEK_OK;
+        if (query) { path = WIDEK_CONV_PATH_DIRECT; return WIDEK_OK; }
         const int64_t total = (int64_t)g.n * g.batch * g.cout * g.od * g.oh * g.ow;
         conv_direct_kernel<T><<<grid_cap(total, 256), 256, 0, st>>>(static_cast<const T*>(x),
                                                                     static_cast<const T*>(w), static_cast<T*>(y),
@@ -1333,6 +1454,20 @@ int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const voi
     return widek_conv_fwd_ex(x, w, w_packed, bias, scale, shift, residual, y, workspace, workspace_bytes, geom, act,
                              residual_first, WIDEK_LAYOUT_NFIRST, WIDEK_LAYOUT_NFIRST, WIDEK_LAYOUT_NFIRST, dtype,
                              stream);
+}
+
+int widek_conv_path(const int64_t* geom, int dtype, int in_layout, int out_layout, int res_layout,
+                    int has_residual) {
+    using namespace widek;
+    ConvGeom g;
+    if (parse_geom(geom, g)) return -1;
+    if (!layout_ok(in_layout) || !layout_ok(out_layout) || !layout_ok(res_layout) || res_layout == WIDEK_LAYOUT_CLAST)
+        return -1;
+    static const int dummy = 0;
+    ConvEpi e{nullptr, nullptr, nullptr, has_residual ? &dummy : nullptr, 0, 0};
+    ConvLaunch L{nullptr, nullptr, nullptr, nullptr, nullptr, 0, g, e, dtype, in_layout, out_layout, res_layout,
+                 true, nullptr};
+    return dispatch_dtype(dtype, L) == WIDEK_OK ? L.path : -1;
 }
 
 int widek_conv_layouts_supported(const int64_t* geom, int dtype, int in_layout, int out_layout, int res_layout,

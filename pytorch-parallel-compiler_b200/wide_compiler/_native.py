@@ -69,6 +69,7 @@ SIGNATURES = {
     "widek_conv_fwd": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64), _int, _int, _int, _c_void_p],
     "widek_conv_fwd_ex": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64)] + [_int] * 6 + [_c_void_p],
     "widek_conv_layouts_supported": [ctypes.POINTER(_i64)] + [_int] * 5,
+    "widek_conv_path": [ctypes.POINTER(_i64)] + [_int] * 5,
     "widek_mlp_chain_fwd": [_c_void_p, _c_void_p, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
                             ctypes.POINTER(_i64), ctypes.POINTER(_int), _int, _i64, _i64, _int, _int, _int,
                             _c_void_p],

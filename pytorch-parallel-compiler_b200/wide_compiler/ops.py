@@ -523,6 +523,37 @@ def _packed_weight(weight: Tensor, rows: int, cin: int, taps: int, dev) -> Tenso
 
 
 LAYOUT_NFIRST, LAYOUT_PACKED, LAYOUT_CLAST = 0, 1, 2
+CONV_PATH_DIRECT, CONV_PATH_TAPS, CONV_PATH_HALO = 0, 1, 2
+
+
+def conv_geometry(n, batch, cin, cout, sp_in, kernel, stride, padding, dilation):
+    """The 22-entry geometry array of the conv entry points (spatial values
+    padded to 3-D) and the padded input spatial, kernel, stride and the
+    output spatial of the given rank."""
+    nd = len(sp_in)
+    pad3 = lambda v, fill: (fill,) * (3 - nd) + tuple(v)
+    sp = pad3(sp_in, 1)
+    ks = pad3(kernel, 1)
+    st = pad3(stride, 1)
+    pd = pad3(padding, 0)
+    dl = pad3(dilation, 1)
+    out_sp = tuple((sp[i] + 2 * pd[i] - dl[i] * (ks[i] - 1) - 1) // st[i] + 1 for i in range(3))
+    if min(out_sp) <= 0:
+        raise ValueError(f"WideConv: output size {out_sp} is not positive")
+    geom = (ctypes.c_int64 * 22)(n, batch, cin, cout, *sp, *ks, *st, *pd, *dl, *out_sp)
+    return geom, sp, ks, st, out_sp[3 - nd:]
+
+
+def conv_path(n, batch, cin, cout, sp_in, kernel, stride, padding, dilation, dtype: torch.dtype,
+              in_layout: int = LAYOUT_NFIRST, out_layout: int = LAYOUT_NFIRST, res_layout: int = LAYOUT_NFIRST,
+              has_residual: bool = False) -> int:
+    """Which kernel the library would run for this conv (CONV_PATH_*), or -1
+    when the layout combination is not served. Launches nothing."""
+    geom = conv_geometry(n, batch, cin, cout, sp_in, kernel, stride, padding, dilation)[0]
+    code = N._DTYPE_CODES.get(dtype)
+    if code is None:
+        return -1
+    return int(N.lib().widek_conv_path(geom, code, in_layout, out_layout, res_layout, 1 if has_residual else 0))
 
 
 def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, padding, dilation,
@@ -560,17 +591,7 @@ def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, p
     if weight.shape[0] % n != 0 or weight.shape[1] != cin:
         raise ValueError(f"WideConv: input {tuple(x.shape)} does not match weight {tuple(weight.shape)} for N={n}")
     cout = weight.shape[0] // n
-    pad3 = lambda v, fill: (fill,) * (3 - nd) + tuple(v)
-    sp = pad3(sp_in, 1)
-    ks = pad3(weight.shape[2:], 1)
-    st = pad3(stride, 1)
-    pd = pad3(padding, 0)
-    dl = pad3(dilation, 1)
-    out_sp = tuple((sp[i] + 2 * pd[i] - dl[i] * (ks[i] - 1) - 1) // st[i] + 1 for i in range(3))
-    if min(out_sp) <= 0:
-        raise ValueError(f"WideConv: output size {out_sp} is not positive")
-    osp = out_sp[3 - nd:]
-    geom = (ctypes.c_int64 * 22)(n, batch, cin, cout, *sp, *ks, *st, *pd, *dl, *out_sp)
+    geom, sp, ks, st, osp = conv_geometry(n, batch, cin, cout, sp_in, weight.shape[2:], stride, padding, dilation)
     default = in_layout == out_layout == res_layout == LAYOUT_NFIRST
     if not default and not N.lib().widek_conv_layouts_supported(geom, N.dtype_code(x), in_layout, out_layout,
                                                                   res_layout, 1 if residual is not None else 0):
