@@ -285,6 +285,37 @@ WIDEK_API int widek_lstm_recurrence(const void* gates_x, const void* w_hh, const
                                     void* c_n, int64_t n, int64_t batch, int64_t steps,
                                     int64_t hidden, int dtype, void* stream);
 
+/* Whole GRU / LSTM forward in one call: the input projection
+ * x @ W_ih^T + b_ih into the caller's workspace (CUDA-core grouped GEMM,
+ * fp32 arithmetic), then the recurrence, with both weights addressed by
+ * stride so that no re-laid-out copy is needed:
+ *   x: [n, batch, steps, input]; out: [n, batch, steps, hidden];
+ *   h0 (and c0 for LSTM): [n, batch, hidden] or NULL; h_n, c_n likewise;
+ *   b_ih, b_hh: [n, G*hidden] or NULL (G = 3 for GRU r,z,n; 4 for LSTM i,f,g,o);
+ *   model i's W_ih [G*hidden, input] block starts at w_ih + i*w_strides[0]
+ *   with rows w_strides[1] elements apart, its W_hh [G*hidden, hidden] block
+ *   at w_hh + i*w_strides[2], rows w_strides[3] apart (w_strides NULL =
+ *   dense [n, G*hidden, ...]). The strides let WideLSTM pass its
+ *   block-diagonal [n*4H, n*I] / [n*4H, n*H] parameters as they are.
+ *   workspace: widek_rnn_workspace(...) bytes (the projected gates).
+ * Replaces: wide_compiler/core/primitives/wide_gru.py:148-213 and
+ * wide_lstm.py:158-234 (block extraction :184-199, input projection
+ * :168 / :190, the per-step loop). */
+WIDEK_API int widek_gru_fwd(const void* x, const void* w_ih, const void* w_hh, const void* b_ih,
+                            const void* b_hh, const void* h0, void* out, void* h_n,
+                            const int64_t* w_strides, void* workspace, size_t workspace_bytes,
+                            int64_t n, int64_t batch, int64_t steps, int64_t input, int64_t hidden,
+                            int dtype, void* stream);
+WIDEK_API int widek_lstm_fwd(const void* x, const void* w_ih, const void* w_hh, const void* b_ih,
+                             const void* b_hh, const void* h0, const void* c0, void* out, void* h_n,
+                             void* c_n, const int64_t* w_strides, void* workspace,
+                             size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps,
+                             int64_t input, int64_t hidden, int dtype, void* stream);
+
+/* Workspace bytes of widek_gru_fwd (lstm = 0) / widek_lstm_fwd (lstm = 1). */
+WIDEK_API size_t widek_rnn_workspace(int lstm, int64_t n, int64_t batch, int64_t steps, int64_t hidden,
+                                     int dtype);
+
 /* Kernel choice for the recurrences: 0 = the register-resident kernel where
  * it applies (hidden size 128, at most 128 gate rows per cluster CTA; W_hh
  * held in registers, hidden state passed by DSMEM stores and mbarrier

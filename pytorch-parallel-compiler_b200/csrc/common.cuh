@@ -35,6 +35,12 @@ int encode_tmap_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
 // device address (per device, resolved once) as an ordinary argument.
 int* device_error_ptr();
 
+// CUDA-core grouped GEMM with a strided weight: y[i] = act(x[i] @ W_i^T +
+// bias[i]) where W_i is the [o, k] matrix at w + i*w_ms with rows w_rs
+// elements apart; x [n, m, k], y [n, m, o] dense (gemm_simt.cu).
+int linear_simt_strided(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m, int64_t k,
+                        int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st);
+
 __device__ __forceinline__ void raise_device_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }

@@ -15,7 +15,7 @@ namespace {
 template <typename T, int BM, int BN, int BK, int TM, int TN>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     gemm_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
-                     T* __restrict__ y, int M, int K, int O, int act) {
+                     T* __restrict__ y, int M, int K, int O, int act, int64_t w_ms, int64_t w_rs) {
     constexpr int NT = (BM / TM) * (BN / TN);
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
@@ -23,7 +23,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     const int m0 = blockIdx.y * BM;
     const int o0 = blockIdx.x * BN;
     x += (int64_t)model * M * K;
-    w += (int64_t)model * O * K;
+    w += (int64_t)model * w_ms;
     y += (int64_t)model * M * O;
     const int tid = threadIdx.x;
     const int tx = tid % (BN / TN);
@@ -44,7 +44,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         for (int i = tid; i < BN * BK; i += NT) {
             const int r = i / BK, c = i % BK;
             const int go = o0 + r, gk = k0 + c;
-            Bs[c][r] = (go < O && gk < K) ? to_f<T>(w[(int64_t)go * K + gk]) : 0.f;
+            Bs[c][r] = (go < O && gk < K) ? to_f<T>(w[(int64_t)go * w_rs + gk]) : 0.f;
         }
         __syncthreads();
 #pragma unroll
@@ -82,6 +82,7 @@ struct SimtLaunch {
     int64_t n, m, k, o;
     int act;
     cudaStream_t st;
+    int64_t w_ms, w_rs;     // weight model / row strides (elements)
 
     template <typename T>
     int run() {
@@ -94,17 +95,25 @@ struct SimtLaunch {
         T* yp = static_cast<T*>(y);
         if (m <= 32) {
             dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 31) / 32), (unsigned)n);
-            gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act);
+            gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs);
         } else {
             dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)n);
             if (grid.y > 65535) return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): m too large");
-            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act);
+            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs);
         }
         return check_launch("widek_linear_fwd_simt");
     }
 };
 
 }  // namespace
+
+int linear_simt_strided(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m, int64_t k,
+                        int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st) {
+    if (n == 0 || m == 0 || o == 0) return WIDEK_OK;
+    SimtLaunch L{x, w, bias, y, n, m, k, o, act, st, w_ms, w_rs};
+    return dispatch_dtype(dtype, L);
+}
+
 }  // namespace widek
 
 extern "C" int widek_linear_fwd_simt(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m,
@@ -115,6 +124,6 @@ extern "C" int widek_linear_fwd_simt(const void* x, const void* w, const void* b
     if (n == 0 || m == 0 || o == 0) return WIDEK_OK;
     if (!x && k > 0) return set_error(WIDEK_ERR_INVALID, "linear: null x");
     if (!y) return set_error(WIDEK_ERR_INVALID, "linear: null y");
-    SimtLaunch L{x, w, bias, y, n, m, k, o, act, (cudaStream_t)stream};
+    SimtLaunch L{x, w, bias, y, n, m, k, o, act, (cudaStream_t)stream, o * k, k};
     return dispatch_dtype(dtype, L);
 }

@@ -44,7 +44,7 @@ __device__ __forceinline__ float tanh_fast(float x) { return 2.f * sigmoid_fast(
 
 struct RnnArgs {
     const void* gx;      // [n, batch, T, G*H]
-    const void* w_hh;    // [n, G*H, H]
+    const void* w_hh;    // model i's [G*H, H] block at w_hh + i*whh_ms, rows whh_rs apart
     const void* b_hh;    // [n, G*H] or null
     const void* h0;      // [n, batch, H] or null
     const void* c0;      // [n, batch, H] or null (LSTM)
@@ -53,6 +53,7 @@ struct RnnArgs {
     void* cn;            // [n, batch, H] or null (LSTM)
     int batch, T, H, G, cl, w_in_smem;
     int kparts;          // threads sharing one row's dot products (split k, vec4 path)
+    int64_t whh_ms, whh_rs;   // W_hh model / row strides (elements)
 };
 
 template <typename T, bool LSTM>
@@ -69,7 +70,8 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     float* cst = gates + (size_t)B * R;                       // [B][U] (LSTM)
 
     const T* gx = static_cast<const T*>(a.gx) + (size_t)model * B * a.T * G * H;
-    const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * G * H * H;
+    const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * a.whh_ms;
+    const int64_t wrs = a.whh_rs;
     const T* bh = a.b_hh ? static_cast<const T*>(a.b_hh) + (size_t)model * G * H : nullptr;
     T* out = static_cast<T*>(a.out) + (size_t)model * B * a.T * H;
 
@@ -82,7 +84,7 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     if (a.w_in_smem) {
         for (int i = threadIdx.x; i < R * H; i += blockDim.x) {
             const int lr = i / H, k = i % H;
-            const float v = to_f<T>(w[(size_t)grow(lr) * H + k]);
+            const float v = to_f<T>(w[(size_t)grow(lr) * wrs + k]);
             if (vec4) Ws[(size_t)lr * H + k] = v;
             else Ws[(size_t)k * R + lr] = v;
         }
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
                                 if (bb < nb) acc[bb] = fmaf(wv, hc[(size_t)(b0 + bb) * H + k], acc[bb]);
                         }
                     } else {
-                        const T* wr = w + (size_t)grow(lr) * H;
+                        const T* wr = w + (size_t)grow(lr) * wrs;
 #pragma unroll 4
                         for (int k = 0; k < H; ++k) {
                             const float wv = to_f<T>(wr[k]);
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
     volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
 
     const T* gx = static_cast<const T*>(a.gx) + (size_t)model * B * a.T * G * H;
-    const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * G * H * H;
+    const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * a.whh_ms;
     const T* bh = a.b_hh ? static_cast<const T*>(a.b_hh) + (size_t)model * G * H : nullptr;
     T* out = static_cast<T*>(a.out) + (size_t)model * B * a.T * H;
     auto grow = [&](int lr) { return (lr / U) * H + q * U + (lr % U); };
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
     for (int r = 0; r < RPT; ++r) {
         const int lr = grp + 32 * r;
         const bool ok = lr < R;
-        const T* wrow = w + (size_t)(ok ? grow(lr) : 0) * H;
+        const T* wrow = w + (size_t)(ok ? grow(lr) : 0) * a.whh_rs;
 #pragma unroll
         for (int i = 0; i < KS; ++i) {
             const int k = 4 * (i * kRegParts + p);
@@ -531,7 +533,7 @@ size_t rnn_reg_smem(int B, int H, int G, int cl) {
     const int U = H / cl, R = G * U;
     const size_t bu4 = ((size_t)B * U + 3) & ~(size_t)3;
     const size_t f = 2 * (size_t)B * H + (size_t)B * R + bu4;
-    return f * sizeof(float) + 2 * sizeof(uint64_t) + 16;
+    return f * sizeof(float) + 4 * sizeof(uint64_t);
 }
 
 template <typename T, bool LSTM, int RPT>
@@ -682,7 +684,44 @@ int rnn_entry(bool lstm, const void* gates_x, const void* w_hh, const void* b_hh
     if (n == 0 || batch == 0 || hidden == 0) return WIDEK_OK;
     if (!w_hh || !h_n || (steps > 0 && (!gates_x || !out)))
         return set_error(WIDEK_ERR_INVALID, "rnn: null pointer");
-    RnnArgs a{gates_x, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps, (int)hidden, lstm ? 4 : 3, 1, 1, 1};
+    const int g = lstm ? 4 : 3;
+    RnnArgs a{gates_x, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps, (int)hidden, g, 1, 1, 1,
+              (int64_t)g * hidden * hidden, hidden};
+    RnnLaunch L{a, n, lstm, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+// Whole forward: the input projection (CUDA-core grouped GEMM reading W_ih by
+// stride) into the caller's workspace, then the recurrence (W_hh by stride).
+int rnn_fwd_entry(bool lstm, const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
+                  const void* h0, const void* c0, void* out, void* h_n, void* c_n, const int64_t* wstrides,
+                  void* workspace, size_t ws_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input,
+                  int64_t hidden, int dtype, void* stream) {
+    if (n < 0 || batch < 0 || steps < 0 || hidden < 0 || input < 0)
+        return set_error(WIDEK_ERR_INVALID, "rnn: negative size");
+    if (batch > 1024 || hidden > 4096 || steps > 0x7fffffff || n > 65535)
+        return set_error(WIDEK_ERR_UNSUPPORTED, "rnn: batch=%lld hidden=%lld outside the supported range",
+                         (long long)batch, (long long)hidden);
+    if (n == 0 || batch == 0 || hidden == 0) return WIDEK_OK;
+    if (!w_hh || !h_n || (steps > 0 && (!x || !out || !w_ih))) return set_error(WIDEK_ERR_INVALID, "rnn: null pointer");
+    const int g = lstm ? 4 : 3;
+    const int64_t ims = wstrides ? wstrides[0] : (int64_t)g * hidden * input;
+    const int64_t irs = wstrides ? wstrides[1] : input;
+    const int64_t hms = wstrides ? wstrides[2] : (int64_t)g * hidden * hidden;
+    const int64_t hrs = wstrides ? wstrides[3] : hidden;
+    if (ims < 0 || irs < input || hms < 0 || hrs < hidden)
+        return set_error(WIDEK_ERR_INVALID, "rnn: weight strides (%lld, %lld, %lld, %lld) overlap the rows",
+                         (long long)ims, (long long)irs, (long long)hms, (long long)hrs);
+    const size_t need = (size_t)(n * batch * steps * g * hidden) * dtype_size(dtype);
+    if (steps > 0 && (!workspace || ws_bytes < need))
+        return set_error(WIDEK_ERR_INVALID, "rnn: workspace of %zu bytes needed, %zu given", need, ws_bytes);
+    if (steps > 0) {
+        const int rc = linear_simt_strided(x, w_ih, b_ih, workspace, n, batch * steps, input, g * hidden, ims, irs,
+                                           dtype, WIDEK_ACT_NONE, (cudaStream_t)stream);
+        if (rc) return rc;
+    }
+    RnnArgs a{steps > 0 ? workspace : nullptr, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps,
+              (int)hidden, g, 1, 1, 1, hms, hrs};
     RnnLaunch L{a, n, lstm, (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
 }
@@ -710,6 +749,27 @@ int widek_lstm_recurrence(const void* gates_x, const void* w_hh, const void* b_h
                           int dtype, void* stream) {
     return widek::rnn_entry(true, gates_x, w_hh, b_hh, h0, c0, out, h_n, c_n, n, batch, steps, hidden, dtype,
                             stream);
+}
+
+size_t widek_rnn_workspace(int lstm, int64_t n, int64_t batch, int64_t steps, int64_t hidden, int dtype) {
+    if (n < 0 || batch < 0 || steps < 0 || hidden < 0) return 0;
+    return (size_t)(n * batch * steps * (lstm ? 4 : 3) * hidden) * widek::dtype_size(dtype);
+}
+
+int widek_gru_fwd(const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
+                  const void* h0, void* out, void* h_n, const int64_t* w_strides, void* workspace,
+                  size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input, int64_t hidden,
+                  int dtype, void* stream) {
+    return widek::rnn_fwd_entry(false, x, w_ih, w_hh, b_ih, b_hh, h0, nullptr, out, h_n, nullptr, w_strides,
+                                workspace, workspace_bytes, n, batch, steps, input, hidden, dtype, stream);
+}
+
+int widek_lstm_fwd(const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
+                   const void* h0, const void* c0, void* out, void* h_n, void* c_n, const int64_t* w_strides,
+                   void* workspace, size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input,
+                   int64_t hidden, int dtype, void* stream) {
+    return widek::rnn_fwd_entry(true, x, w_ih, w_hh, b_ih, b_hh, h0, c0, out, h_n, c_n, w_strides, workspace,
+                                workspace_bytes, n, batch, steps, input, hidden, dtype, stream);
 }
 
 }  // extern "C"

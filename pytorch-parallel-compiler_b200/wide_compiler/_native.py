@@ -64,6 +64,11 @@ SIGNATURES = {
     "widek_embedding_fwd": [_c_void_p] * 3 + [_i64] * 4 + [_int, _c_void_p],
     "widek_gru_recurrence": [_c_void_p] * 6 + [_i64] * 4 + [_int, _c_void_p],
     "widek_lstm_recurrence": [_c_void_p] * 8 + [_i64] * 4 + [_int, _c_void_p],
+    "widek_gru_fwd": [_c_void_p] * 8 + [ctypes.POINTER(_i64), _c_void_p, ctypes.c_size_t] + [_i64] * 5
+                     + [_int, _c_void_p],
+    "widek_lstm_fwd": [_c_void_p] * 10 + [ctypes.POINTER(_i64), _c_void_p, ctypes.c_size_t] + [_i64] * 5
+                      + [_int, _c_void_p],
+    "widek_rnn_workspace": [_int] + [_i64] * 4 + [_int],
     "widek_conv_pack_weight": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p],
     "widek_conv_workspace": [_i64] * 6 + [_int],
     "widek_conv_fwd": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64), _int, _int, _int, _c_void_p],
@@ -78,6 +83,7 @@ SIGNATURES = {
                                                           _int, _c_void_p],
 }
 RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t, "widek_conv_workspace": ctypes.c_size_t,
+            "widek_rnn_workspace": ctypes.c_size_t,
             "widek_launch_count": ctypes.c_longlong}
 
 

@@ -98,11 +98,16 @@ class WideLSTM(nn.Module):
 
     def forward(self, x: Tensor, hx: Optional[Tuple[Tensor, Tensor]] = None
                 ) -> Tuple[Tensor, Tuple[Tensor, Tensor]]:
-        wih, whh = self._blocks()
         n, h = self.n, self.hidden_size
         bih = self.bias_ih.view(n, 4 * h) if self.bias else None
         bhh = self.bias_hh.view(n, 4 * h) if self.bias else None
         h0, c0 = (hx[0], hx[1]) if hx is not None else (None, None)
+        # Without autograd the kernels read the block-diagonal parameters in
+        # place (by stride); the differentiable path uses the diagonal blocks.
+        y = ops.lstm_blockdiag(x, h0, c0, self.weight_ih, self.weight_hh, bih, bhh, n, h)
+        if y is not None:
+            return y
+        wih, whh = self._blocks()
         return ops.lstm(x, h0, c0, wih, whh, bih, bhh)
 
     @classmethod

@@ -354,18 +354,48 @@ def embedding(idx: Tensor, weight: Tensor) -> Tensor:
 # Recurrent layers
 # ---------------------------------------------------------------------------
 
-def _rnn_common(x: Tensor, w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor], gates: int, what: str):
+def _rnn_check(x: Tensor, w_ih: Tensor, w_hh: Tensor, gates: int, what: str):
     if x.dim() != 4:
         raise ValueError(f"{what}: input must be [N, B, T, I], got {tuple(x.shape)}")
     n, batch, steps, i = x.shape
-    if w_ih.shape[0] != n or w_ih.shape[2] != i:
+    if w_ih.dim() != 3 or w_ih.shape[0] != n or w_ih.shape[2] != i:
         raise ValueError(f"{what}: weight_ih {tuple(w_ih.shape)} does not match input {tuple(x.shape)}")
     hidden = w_hh.shape[2]
-    if w_hh.shape != (n, gates * hidden, hidden):
+    if w_hh.shape != (n, gates * hidden, hidden) or w_ih.shape[1] != gates * hidden:
         raise ValueError(f"{what}: weight_hh {tuple(w_hh.shape)} is not [N, {gates}H, H]")
-    # Input projection for all steps at once: [N, B, T, G*H] (bias b_ih fused).
-    gx = linear(x, w_ih, b_ih) if steps > 0 else None
-    return n, batch, steps, hidden, gx
+    return n, batch, steps, hidden
+
+
+def _rnn_fwd(lstm: bool, x: Tensor, h0, c0, w_ih: Tensor, w_hh: Tensor, b_ih, b_hh, strides, n: int, hidden: int):
+    """One library call for the whole forward: the input projection (reading
+    W_ih by (model, row) strides, into a workspace) and the recurrence
+    (W_hh by strides)."""
+    dev = x.device
+    _, batch, steps, inp = x.shape
+    out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
+    hn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
+    cn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype) if lstm else None
+    code = N.dtype_code(x)
+    ws_bytes = int(N.lib().widek_rnn_workspace(1 if lstm else 0, n, batch, steps, hidden, code))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    c_strides = (ctypes.c_int64 * 4)(*strides)
+    xd = _dense(x)
+    with _guard(dev):
+        if lstm:
+            rc = N.lib().widek_lstm_fwd(xd.data_ptr(), w_ih.data_ptr(), w_hh.data_ptr(), N.ptr(b_ih), N.ptr(b_hh),
+                                        N.ptr(h0), N.ptr(c0), out.data_ptr(), hn.data_ptr(), cn.data_ptr(),
+                                        c_strides, ws.data_ptr(), ws.numel(), n, batch, steps, inp, hidden, code,
+                                        N.stream_ptr(dev))
+        else:
+            rc = N.lib().widek_gru_fwd(xd.data_ptr(), w_ih.data_ptr(), w_hh.data_ptr(), N.ptr(b_ih), N.ptr(b_hh),
+                                       N.ptr(h0), out.data_ptr(), hn.data_ptr(), c_strides, ws.data_ptr(), ws.numel(),
+                                       n, batch, steps, inp, hidden, code, N.stream_ptr(dev))
+    N.check(rc, "widek_lstm_fwd" if lstm else "widek_gru_fwd")
+    return out, hn, cn
+
+
+def _opt_dense(t: Optional[Tensor]) -> Optional[Tensor]:
+    return None if t is None else _dense(t)
 
 
 def gru(x: Tensor, h0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor],
@@ -373,45 +403,61 @@ def gru(x: Tensor, h0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor, b_ih: Optio
     """WideGRU forward: returns (out [N, B, T, H], h_n [N, B, H])."""
     if _AG.needs_grad(x, h0, w_ih, w_hh, b_ih, b_hh):
         return _AG.run(gru, _AG.gru_t, x, h0, w_ih, w_hh, b_ih, b_hh)
-    dev = N.require_cuda(x, h0, w_ih, w_hh, b_ih, b_hh, what="WideGRU")
+    N.require_cuda(x, h0, w_ih, w_hh, b_ih, b_hh, what="WideGRU")
     _same_dtype("WideGRU", w_ih, x, h0, w_hh, b_ih, b_hh)
-    n, batch, steps, hidden, gx = _rnn_common(x, w_ih, w_hh, b_ih, 3, "WideGRU")
+    n, batch, steps, hidden = _rnn_check(x, w_ih, w_hh, 3, "WideGRU")
     if h0 is not None and tuple(h0.shape) != (n, batch, hidden):
         raise ValueError(f"WideGRU: h_0 must be [N, B, H] = {(n, batch, hidden)}, got {tuple(h0.shape)}")
-    out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
-    hn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
-    h0d = _dense(h0) if h0 is not None else None
-    with _guard(dev):
-        rc = N.lib().widek_gru_recurrence(N.ptr(gx), _dense(w_hh).data_ptr(), N.ptr(_dense(b_hh) if b_hh is not None else None),
-                                          N.ptr(h0d), out.data_ptr(), hn.data_ptr(), n, batch, steps, hidden,
-                                          N.dtype_code(x), N.stream_ptr(dev))
-    N.check(rc, "widek_gru_recurrence")
+    wi, wh = _dense(w_ih), _dense(w_hh)
+    strides = (wi.shape[1] * wi.shape[2], wi.shape[2], wh.shape[1] * wh.shape[2], wh.shape[2])
+    out, hn, _ = _rnn_fwd(False, x, _opt_dense(h0), None, wi, wh, _opt_dense(b_ih), _opt_dense(b_hh), strides, n,
+                          hidden)
     return out, hn
+
+
+def lstm_blockdiag(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], weight_ih: Tensor, weight_hh: Tensor,
+                   b_ih: Optional[Tensor], b_hh: Optional[Tensor], n: int, hidden: int):
+    """WideLSTM forward straight from the block-diagonal module parameters
+    weight_ih [n*4H, n*I] and weight_hh [n*4H, n*H] (model i's block read by
+    stride, no extracted copy), biases [n, 4H]: (out, (h_n, c_n)). Returns
+    None (launching nothing) when autograd needs the result."""
+    if _AG.needs_grad(x, h0, c0, weight_ih, weight_hh, b_ih, b_hh):
+        return None
+    N.require_cuda(x, h0, c0, weight_ih, weight_hh, b_ih, b_hh, what="WideLSTM")
+    _same_dtype("WideLSTM", weight_ih, x, h0, c0, weight_hh, b_ih, b_hh)
+    if x.dim() != 4 or x.shape[0] != n:
+        raise ValueError(f"WideLSTM: input must be [N={n}, B, T, I], got {tuple(x.shape)}")
+    inp, batch = x.shape[3], x.shape[1]
+    if tuple(weight_ih.shape) != (n * 4 * hidden, n * inp) or tuple(weight_hh.shape) != (n * 4 * hidden, n * hidden):
+        raise ValueError(f"WideLSTM: block-diagonal weights {tuple(weight_ih.shape)} / {tuple(weight_hh.shape)} do "
+                         f"not match N={n}, I={inp}, H={hidden}")
+    for name, t in (("h_0", h0), ("c_0", c0)):
+        if t is not None and tuple(t.shape) != (n, batch, hidden):
+            raise ValueError(f"WideLSTM: {name} must be [N, B, H] = {(n, batch, hidden)}, got {tuple(t.shape)}")
+    wi, wh = _dense(weight_ih), _dense(weight_hh)
+    strides = (4 * hidden * n * inp + inp, n * inp, 4 * hidden * n * hidden + hidden, n * hidden)
+    out, hn, cn = _rnn_fwd(True, x, _opt_dense(h0), _opt_dense(c0), wi, wh, _opt_dense(b_ih), _opt_dense(b_hh),
+                           strides, n, hidden)
+    return out, (hn, cn)
 
 
 def lstm(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor,
          b_ih: Optional[Tensor], b_hh: Optional[Tensor]):
-    """WideLSTM forward on dense diagonal blocks: returns (out, (h_n, c_n))."""
+    """WideLSTM forward on dense diagonal blocks w_ih [N, 4H, I],
+    w_hh [N, 4H, H]: returns (out, (h_n, c_n))."""
     if _AG.needs_grad(x, h0, c0, w_ih, w_hh, b_ih, b_hh):
         out, hn, cn = _AG.run(_lstm_flat, _AG.lstm_t, x, h0, c0, w_ih, w_hh, b_ih, b_hh)
         return out, (hn, cn)
-    dev = N.require_cuda(x, h0, c0, w_ih, w_hh, b_ih, b_hh, what="WideLSTM")
+    N.require_cuda(x, h0, c0, w_ih, w_hh, b_ih, b_hh, what="WideLSTM")
     _same_dtype("WideLSTM", w_ih, x, h0, c0, w_hh, b_ih, b_hh)
-    n, batch, steps, hidden, gx = _rnn_common(x, w_ih, w_hh, b_ih, 4, "WideLSTM")
+    n, batch, steps, hidden = _rnn_check(x, w_ih, w_hh, 4, "WideLSTM")
     for name, t in (("h_0", h0), ("c_0", c0)):
         if t is not None and tuple(t.shape) != (n, batch, hidden):
             raise ValueError(f"WideLSTM: {name} must be [N, B, H] = {(n, batch, hidden)}, got {tuple(t.shape)}")
-    out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
-    hn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
-    cn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
-    with _guard(dev):
-        rc = N.lib().widek_lstm_recurrence(N.ptr(gx), _dense(w_hh).data_ptr(),
-                                           N.ptr(_dense(b_hh) if b_hh is not None else None),
-                                           N.ptr(_dense(h0) if h0 is not None else None),
-                                           N.ptr(_dense(c0) if c0 is not None else None), out.data_ptr(),
-                                           hn.data_ptr(), cn.data_ptr(), n, batch, steps, hidden, N.dtype_code(x),
-                                           N.stream_ptr(dev))
-    N.check(rc, "widek_lstm_recurrence")
+    wi, wh = _dense(w_ih), _dense(w_hh)
+    strides = (wi.shape[1] * wi.shape[2], wi.shape[2], wh.shape[1] * wh.shape[2], wh.shape[2])
+    out, hn, cn = _rnn_fwd(True, x, _opt_dense(h0), _opt_dense(c0), wi, wh, _opt_dense(b_ih), _opt_dense(b_hh),
+                           strides, n, hidden)
     return out, (hn, cn)
 
 

@@ -140,3 +140,95 @@ def test_rnn_h128_both_kernels(rnn_variant, kind, n, b, t):
     assert_fp32_close(y, ry)
     assert_fp32_close(hn, rh)
     no_device_error()
+
+
+# ---------------------------------------------------------------------------
+# One-call GRU / LSTM forward (projection with strided W_ih, then the
+# recurrence with strided W_hh): WideLSTM passes its block-diagonal
+# parameters as they are
+# ---------------------------------------------------------------------------
+
+def _blockdiag(blocks):
+    """[N, R, C] dense blocks -> the [N*R, N*C] block-diagonal module layout."""
+    n, r, c = blocks.shape
+    out = torch.zeros(n * r, n * c, dtype=blocks.dtype)
+    for k in range(n):
+        out[k * r:(k + 1) * r, k * c:(k + 1) * c] = blocks[k]
+    return out
+
+
+@pytest.mark.parametrize("n,b,t,i,h,bias,dtype", [
+    (32, 4, 32, 64, 128, True, torch.float32),     # cfg4
+    (5, 3, 9, 20, 128, True, torch.float32),
+    (2, 1, 1, 4, 128, False, torch.float32),
+    (7, 17, 6, 128, 128, True, torch.float32),
+    (3, 5, 4, 12, 40, True, torch.float32),        # shared-memory cluster kernel
+    (4, 4, 16, 32, 128, True, torch.bfloat16),
+])
+def test_blockdiag_lstm_and_gru_match_oracle(n, b, t, i, h, bias, dtype):
+    close = assert_fp32_close if dtype == torch.float32 else assert_lowp_close
+    gen = torch.Generator().manual_seed(n * 13 + b + t + i)
+    x = torch.randn(n, b, t, i, generator=gen).to(dtype)
+    h0 = (torch.randn(n, b, h, generator=gen) * 0.5).to(dtype)
+    c0 = (torch.randn(n, b, h, generator=gen) * 0.5).to(dtype)
+    dv = lambda v: None if v is None else v.to(DEV)
+    wih, whh, bih, bhh = _rnn_params(n, i, h, 3, dtype, n + i)
+    if not bias:
+        bih = bhh = None
+    y, hn = ops.gru(x.to(DEV), h0.to(DEV), wih.to(DEV), whh.to(DEV), dv(bih), dv(bhh))
+    ry, rh = O.gru(x, h0, wih, whh, bih, bhh)
+    close(y, ry)
+    close(hn, rh)
+    wih, whh, bih, bhh = _rnn_params(n, i, h, 4, dtype, n + i + 1)
+    if not bias:
+        bih = bhh = None
+    y, (hn, cn) = ops.lstm_blockdiag(x.to(DEV), h0.to(DEV), c0.to(DEV), _blockdiag(wih).to(DEV),
+                                     _blockdiag(whh).to(DEV), dv(bih), dv(bhh), n, h)
+    ry, (rh, rc) = O.lstm(x, h0, c0, wih, whh, bih, bhh)
+    close(y, ry)
+    close(hn, rh)
+    close(cn, rc)
+    no_device_error()
+
+
+def test_one_call_matches_projection_then_recurrence():
+    """widek_gru_fwd against the two separate entry points (grouped GEMM for
+    the projection, then widek_gru_recurrence) on the same inputs."""
+    from wide_compiler import _native as N
+    n, b, t, i, h = 6, 5, 12, 48, 128
+    wih, whh, bih, bhh = (v.to(DEV) for v in _rnn_params(n, i, h, 3, torch.float32, 77))
+    x = torch.randn(n, b, t, i, generator=torch.Generator().manual_seed(3)).to(DEV)
+    y1, h1 = ops.gru(x, None, wih, whh, bih, bhh)
+    gx = ops.linear(x, wih, bih)
+    y2 = torch.empty_like(y1)
+    h2 = torch.empty_like(h1)
+    N.check(N.lib().widek_gru_recurrence(gx.data_ptr(), whh.data_ptr(), bhh.data_ptr(), None, y2.data_ptr(),
+                                         h2.data_ptr(), n, b, t, h, N.F32, N.stream_ptr(x.device)),
+            "widek_gru_recurrence")
+    assert_fp32_close(y1, y2)
+    assert_fp32_close(h1, h2)
+    no_device_error()
+
+
+def test_wide_lstm_module_reads_block_diagonal_in_place():
+    """WideLSTM's forward reads its block-diagonal parameters in place (no
+    extracted blocks are cached) and follows an in-place update."""
+    torch.manual_seed(5)
+    lstms = [torch.nn.LSTM(16, 128, batch_first=True) for _ in range(3)]
+    wl = wc.WideLSTM.from_modules(lstms).to(DEV)
+    x = torch.randn(3, 2, 7, 16, device=DEV)
+    y, _ = wl(x)
+    assert not getattr(wl, '_widek_derived', None), "no derived blocks on the inference path"
+    ry, _ = lstms[1](x[1].cpu())
+    assert_fp32_close(y[1], ry.detach())
+    with torch.no_grad():
+        wl.weight_hh.mul_(0.5)
+        for m in lstms:
+            m.weight_hh_l0.mul_(0.5)
+    y, (hn, cn) = wl(x)
+    ry, (rh, rc) = lstms[2](x[2].cpu())
+    assert_fp32_close(y[2], ry.detach())
+    assert_fp32_close(cn[2], rc[0].detach())
+    y0, (h0n, c0n) = wl(torch.empty(3, 2, 0, 16, device=DEV))
+    assert y0.shape == (3, 2, 0, 128) and float(h0n.abs().max()) == 0.0
+    no_device_error()
