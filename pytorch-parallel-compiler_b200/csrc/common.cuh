@@ -52,6 +52,7 @@ enum DeviceError : int {
     DEV_ERR_RNN_TIMEOUT = 102,    // recurrent kernel cluster wait ran out
     DEV_ERR_ATTN_TIMEOUT = 103,
     DEV_ERR_CONV_TIMEOUT = 104,
+    DEV_ERR_NORM_TIMEOUT = 105,   // BatchNorm ring wait ran out
     DEV_ERR_INDEX = 110,          // an index input was out of range (skipped)
 };
 

@@ -6,8 +6,10 @@
 // [n * c], channel index n_i * c + c_i, exactly the inner nn.BatchNorm(N*C) /
 // nn.GroupNorm(N*G, N*C) parameter order of the reference.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace widek {
 namespace {
@@ -51,6 +53,332 @@ __global__ void bn_eval_kernel(const T* __restrict__ x, T* __restrict__ y, const
             y[e] = from_f<T>(to_f<T>(x[e]) * sc + sh);
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// BatchNorm with batch statistics (train mode), one pass over HBM when a
+// channel's batch*l elements fit in the registers of one CTA (up to 512
+// threads x NV 16-byte vectors: 32 K bf16 / 16 K fp32 elements, e.g. the
+// cfg3 shape's 32 x 32x32 per channel). One CTA per channel loads them all
+// (16-byte coalesced loads, NV in flight per thread), takes the exact
+// two-pass mean and biased variance from the registers, updates the running
+// statistics and writes the normalised values: x is read once and y written
+// once. Larger channels take the two-kernel split reduction below.
+// ---------------------------------------------------------------------------
+constexpr int kBnRegThreads = 512;
+
+__device__ __forceinline__ float bn_block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();                      // red may still be read by the previous call
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
+
+template <typename T, int NV, bool VEC>
+__global__ void __launch_bounds__(kBnRegThreads, 3) bn_train_reg_kernel(
+    const T* __restrict__ x, T* __restrict__ y, const T* __restrict__ w, const T* __restrict__ b,
+    T* __restrict__ rm, T* __restrict__ rv, float* __restrict__ save_mean, float* __restrict__ save_invstd,
+    int64_t batch, int64_t c, int64_t l, float momentum, float eps) {
+    constexpr int V = VEC ? 16 / (int)sizeof(T) : 1;
+    using Raw = typename std::conditional<VEC, uint4, T>::type;   // kept raw: 4 registers per 16 bytes
+    __shared__ float red[kBnRegThreads / 32];
+    const int64_t ch = blockIdx.x;
+    const int64_t ni = ch / c, ci = ch % c;
+    const uint32_t cnt = (uint32_t)(batch * l);       // <= 32 K elements on this path
+    const uint32_t nv = cnt / V;                      // l % V == 0 on the vector path
+    const uint32_t ll = (uint32_t)l;
+    const T* xc = x + (ni * batch * c + ci) * l;      // batch row bi of the channel at + bi * c * l
+    T* yc = y + (ni * batch * c + ci) * l;
+    const int64_t row_stride = c * l;
+    auto offset = [&](uint32_t j) {
+        const uint32_t e = j * V, bi = e / ll;
+        return (int64_t)bi * row_stride + (e - bi * ll);
+    };
+    auto unpack = [&](const Raw& r, float (&f)[V]) {
+        const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+        for (int u = 0; u < V; ++u) f[u] = to_f<T>(e[u]);
+    };
+    Raw raw[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const uint32_t j = threadIdx.x + (uint32_t)k * blockDim.x;
+        if (j < nv) raw[k] = *reinterpret_cast<const Raw*>(xc + offset(j));
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        if (threadIdx.x + (uint32_t)k * blockDim.x < nv) {
+            float f[V];
+            unpack(raw[k], f);
+#pragma unroll
+            for (int u = 0; u < V; ++u) s += f[u];
+        }
+    }
+    const float mean = bn_block_sum(s, red) / (float)cnt;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        if (threadIdx.x + (uint32_t)k * blockDim.x < nv) {
+            float f[V];
+            unpack(raw[k], f);
+#pragma unroll
+            for (int u = 0; u < V; ++u) {
+                const float d = f[u] - mean;
+                q = fmaf(d, d, q);
+            }
+        }
+    }
+    const float var = bn_block_sum(q, red) / (float)cnt;
+    const float invstd = rsqrtf(var + eps);
+    const float g = w ? to_f<T>(w[ch]) : 1.f;
+    const float bb = b ? to_f<T>(b[ch]) : 0.f;
+    const float sc = g * invstd, sh = bb - mean * sc;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const uint32_t j = threadIdx.x + (uint32_t)k * blockDim.x;
+        if (j < nv) {
+            float f[V];
+            unpack(raw[k], f);
+            Raw o;
+            T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+            for (int u = 0; u < V; ++u) oe[u] = from_f<T>(fmaf(f[u], sc, sh));
+            *reinterpret_cast<Raw*>(yc + offset(j)) = o;
+        }
+    }
+    if (threadIdx.x == 0) {
+        if (rm) rm[ch] = from_f<T>((1.f - momentum) * to_f<T>(rm[ch]) + momentum * mean);
+        if (rv) {
+            const float unbiased = cnt > 1 ? var * ((float)cnt / (float)(cnt - 1)) : var;
+            rv[ch] = from_f<T>((1.f - momentum) * to_f<T>(rv[ch]) + momentum * unbiased);
+        }
+        if (save_mean) save_mean[ch] = mean;
+        if (save_invstd) save_invstd[ch] = invstd;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Training-mode BatchNorm as a persistent stream (the main path for channels
+// of up to 64 KB whose rows are 16-byte multiples, e.g. cfg3's 32 x 32x32
+// bf16 = 64 KB per channel): one CTA per SM walks the channels
+// blockIdx.x, blockIdx.x + gridDim.x, ... through a ring of three 64 KB
+// shared-memory buffers. Thread 0 brings channel k+2 in with one bulk copy
+// per batch row (completing on the buffer's mbarrier) and writes channel k
+// out with bulk stores from the same buffer, while the CTA computes channel
+// k's exact two-pass statistics and normalises it in place; so loads,
+// stores and arithmetic of neighbouring channels overlap and HBM sees one
+// read of x and one write of y. Every wait is bounded.
+// ---------------------------------------------------------------------------
+constexpr int kBnRingThreads = 256;
+constexpr int kBnRing = 3;
+constexpr uint32_t kBnRingBytes = 64 * 1024;
+
+template <typename T>
+__global__ void __launch_bounds__(kBnRingThreads, 1) bn_train_ring_kernel(
+    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ w,
+    const T* __restrict__ b, T* __restrict__ rm, T* __restrict__ rv, float* __restrict__ save_mean,
+    float* __restrict__ save_invstd, int64_t channels, int64_t batch, int64_t c, int64_t l, float momentum,
+    float eps, int* err) {
+    constexpr int V = 16 / (int)sizeof(T);
+    extern __shared__ __align__(128) uint8_t bn_smem[];
+    __shared__ float red[kBnRingThreads / 32];
+    __shared__ uint64_t full[kBnRing];
+    __shared__ int abort_flag;
+    const int64_t cnt = batch * l;
+    const uint32_t ch_bytes = (uint32_t)(cnt * sizeof(T));
+    const int nvec = (int)(cnt / V);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBnRing; ++s) sm100::mbar_init(&full[s], 1);
+        abort_flag = 0;
+        sm100::mbar_init_fence();
+    }
+    __syncthreads();
+    const uint64_t pol = sm100::l2_policy_evict_first();
+    if (threadIdx.x == 0) {
+        sm100::tma_prefetch_desc(&tm_x);
+        sm100::tma_prefetch_desc(&tm_y);
+    }
+    int issued = 0;                                   // loads issued (thread 0)
+    // One TMA box {l0, l1, batch, 1, 1} moves a whole channel ([batch][l] in
+    // shared memory).
+    auto issue_load = [&](int kk) {
+        const int64_t ch = blockIdx.x + (int64_t)kk * gridDim.x;
+        if (ch >= channels) return;
+        const int ni = (int)(ch / c), ci = (int)(ch % c);
+        uint64_t* bar = &full[kk % kBnRing];
+        sm100::mbar_arrive_expect_tx(bar, ch_bytes);
+        sm100::tma_load_5d(bn_smem + (size_t)(kk % kBnRing) * kBnRingBytes, &tm_x, bar, 0, 0, 0, ci, ni, pol);
+        ++issued;
+    };
+    if (threadIdx.x == 0) {
+        issue_load(0);
+        issue_load(1);
+    }
+    for (int kk = 0;; ++kk) {
+        const int64_t ch = blockIdx.x + (int64_t)kk * gridDim.x;
+        if (ch >= channels) break;
+        const int slot = kk % kBnRing;
+        T* buf = reinterpret_cast<T*>(bn_smem + (size_t)slot * kBnRingBytes);
+        // Every thread waits (bounded); the verdict is made uniform before
+        // anyone leaves, since the loop body holds CTA-wide barriers.
+        const bool ok = sm100::mbar_wait(&full[slot], (uint32_t)((kk / kBnRing) & 1), &abort_flag);
+        if (__syncthreads_or(ok ? 0 : 1)) {
+            if (threadIdx.x == 0) {
+                abort_flag = 1;
+                raise_device_error(err, DEV_ERR_NORM_TIMEOUT);
+            }
+            break;
+        }
+        float s = 0.f;
+        for (int v = threadIdx.x; v < nvec; v += kBnRingThreads) {
+            float f[V];
+            load16<T>(buf + (size_t)v * V, f);
+#pragma unroll
+            for (int u = 0; u < V; ++u) s += f[u];
+        }
+        const float mean = bn_block_sum(s, red) / (float)cnt;
+        float q = 0.f;
+        for (int v = threadIdx.x; v < nvec; v += kBnRingThreads) {
+            float f[V];
+            load16<T>(buf + (size_t)v * V, f);
+#pragma unroll
+            for (int u = 0; u < V; ++u) {
+                const float d = f[u] - mean;
+                q = fmaf(d, d, q);
+            }
+        }
+        const float var = bn_block_sum(q, red) / (float)cnt;
+        const float invstd = rsqrtf(var + eps);
+        const float g = w ? to_f<T>(w[ch]) : 1.f;
+        const float bb = b ? to_f<T>(b[ch]) : 0.f;
+        const float sc = g * invstd, sh = bb - mean * sc;
+        for (int v = threadIdx.x; v < nvec; v += kBnRingThreads) {
+            float f[V];
+            load16<T>(buf + (size_t)v * V, f);
+#pragma unroll
+            for (int u = 0; u < V; ++u) f[u] = fmaf(f[u], sc, sh);
+            store16<T>(buf + (size_t)v * V, f);
+        }
+        sm100::fence_async_shared();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            sm100::tma_store_5d(&tm_y, buf, 0, 0, 0, (int)(ch % c), (int)(ch / c));
+            sm100::bulk_commit_group();
+            if (rm) rm[ch] = from_f<T>((1.f - momentum) * to_f<T>(rm[ch]) + momentum * mean);
+            if (rv) {
+                const float unbiased = cnt > 1 ? var * ((float)cnt / (float)(cnt - 1)) : var;
+                rv[ch] = from_f<T>((1.f - momentum) * to_f<T>(rv[ch]) + momentum * unbiased);
+            }
+            if (save_mean) save_mean[ch] = mean;
+            if (save_invstd) save_invstd[ch] = invstd;
+            // The buffer of channel kk+2 held channel kk-1: its stores (the
+            // group before this one) have read it out.
+            sm100::bulk_wait_group_read<1>();
+            issue_load(kk + 2);
+        }
+    }
+    if (threadIdx.x == 0) {
+        if (abort_flag) {
+            // loads in flight land before the shared memory is released
+            const volatile int never = 0;
+            for (int j = 0; j < issued; ++j) {
+                const int idx = issued - 1 - j;
+                if (j >= kBnRing) break;
+                sm100::mbar_wait(&full[idx % kBnRing], (uint32_t)((idx / kBnRing) & 1), &never);
+            }
+        }
+        sm100::bulk_wait_group_all();
+    }
+    __syncthreads();
+}
+
+// Launches the one-pass kernel when the channel fits; `launched` says whether it did.
+template <typename T>
+int bn_train_reg(const void* x, void* y, const void* w, const void* b, void* rm, void* rv, float* save_mean,
+                 float* save_invstd, int64_t n, int64_t batch, int64_t c, int64_t l, float momentum, float eps,
+                 cudaStream_t st, bool& launched) {
+    launched = false;
+    const int64_t channels = n * c, cnt = batch * l;
+    constexpr int VV = 16 / (int)sizeof(T);
+    // Persistent ring: whole rows move by bulk copies (16-byte multiples of
+    // at least 128 bytes, aligned), a channel fits one 64 KB buffer.
+    // Row split l = l0 * l1 with l0 <= 256 elements of a 16-byte multiple
+    // (the TMA box inner dimension), l1 <= 256.
+    int64_t l0 = 0;
+    for (int64_t d = std::min<int64_t>(l, 256); d >= 1; --d) {
+        if (l % d == 0 && (d * (int64_t)sizeof(T)) % 16 == 0 && l / d <= 256) { l0 = d; break; }
+    }
+    if (l0 > 0 && batch <= 256 && cnt * (int64_t)sizeof(T) <= (int64_t)kBnRingBytes && aligned16(x) &&
+        aligned16(y) && n <= 0x7fffffff && c <= 0x7fffffff) {
+        CUtensorMap tx, ty;
+        const uint64_t es = sizeof(T);
+        const uint64_t dims[5] = {(uint64_t)l0, (uint64_t)(l / l0), (uint64_t)batch, (uint64_t)c, (uint64_t)n};
+        const uint64_t strides[4] = {(uint64_t)l0 * es, (uint64_t)(c * l) * es, (uint64_t)l * es,
+                                     (uint64_t)(batch * c * l) * es};
+        const uint32_t box[5] = {(uint32_t)l0, (uint32_t)(l / l0), (uint32_t)batch, 1, 1};
+        const CUtensorMapDataType dt = sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : (std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+        int rc = encode_tmap_tiled(&tx, dt, 5, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+        rc = encode_tmap_tiled(&ty, dt, 5, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+        const uint32_t smem = kBnRing * kBnRingBytes;
+        static bool attr_done[64] = {false};
+        const int dev = current_device();
+        if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+            if (cudaFuncSetAttribute(bn_train_ring_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem) != cudaSuccess)
+                return set_error(WIDEK_ERR_CUDA, "batchnorm: cannot reserve %u bytes of shared memory", smem);
+            attr_done[dev] = true;
+        }
+        const int grid = (int)std::min<int64_t>(channels, sm_count(dev));
+        bn_train_ring_kernel<T><<<grid, kBnRingThreads, smem, st>>>(
+            tx, ty, (const T*)w, (const T*)b, (T*)rm, (T*)rv, save_mean, save_invstd, channels, batch, c, l, momentum,
+            eps, device_error_ptr());
+        launched = true;
+        return check_launch("widek_batchnorm_train_fwd (persistent ring)");
+    }
+    const bool vec = l % VV == 0 && aligned16(x) && aligned16(y);
+    const int64_t nv = vec ? cnt / VV : cnt;
+    int nvpt = 0;
+    for (int k : {1, 2, 4, 8}) {
+        if (nv <= (int64_t)k * kBnRegThreads) { nvpt = k; break; }
+    }
+    if (!nvpt || channels > 0x7fffffff) return WIDEK_OK;
+    int threads = (int)(((nv + nvpt - 1) / nvpt + 31) / 32 * 32);
+    if (threads < 32) threads = 32;
+    const dim3 grid((unsigned)channels);
+    const T* xp = static_cast<const T*>(x);
+    T* yp = static_cast<T*>(y);
+#define WIDEK_BN_REG(NVPT, VEC)                                                                                  \
+    bn_train_reg_kernel<T, NVPT, VEC><<<grid, threads, 0, st>>>(xp, yp, (const T*)w, (const T*)b, (T*)rm,       \
+                                                                (T*)rv, save_mean, save_invstd, batch, c, l,    \
+                                                                momentum, eps)
+    if (vec) {
+        switch (nvpt) {
+            case 1: WIDEK_BN_REG(1, true); break;
+            case 2: WIDEK_BN_REG(2, true); break;
+            case 4: WIDEK_BN_REG(4, true); break;
+            default: WIDEK_BN_REG(8, true); break;
+        }
+    } else {
+        switch (nvpt) {
+            case 1: WIDEK_BN_REG(1, false); break;
+            case 2: WIDEK_BN_REG(2, false); break;
+            case 4: WIDEK_BN_REG(4, false); break;
+            default: WIDEK_BN_REG(8, false); break;
+        }
+    }
+#undef WIDEK_BN_REG
+    launched = true;
+    return check_launch("widek_batchnorm_train_fwd (one pass)");
 }
 
 // ---------------------------------------------------------------------------
@@ -359,6 +687,10 @@ struct BnTrain {
     int run() {
         const int64_t channels = n * c;
         const int64_t cnt = batch * l;
+        bool done = false;
+        const int rc0 = bn_train_reg<T>(x, y, w, b, rm, rv, save_mean, save_invstd, n, batch, c, l, momentum, eps, st,
+                                        done);
+        if (done || rc0) return rc0;
         const int chunks = bn_chunks(channels, cnt, sm_count(current_device()));
         const size_t need = (size_t)channels * chunks * 2 * sizeof(double);
         if (!ws || ws_bytes < need)
@@ -552,6 +884,10 @@ struct BnTrainNoAlloc {
     int run() {
         const int64_t channels = n * c;
         const int64_t cnt = batch * l;
+        bool done = false;
+        const int rc0 = bn_train_reg<T>(x, y, w, b, rm, rv, save_mean, save_invstd, n, batch, c, l, momentum, eps, st,
+                                        done);
+        if (done || rc0) return rc0;
         int chunks = bn_chunks(channels, cnt, sm_count(current_device()));
         // bn_chunks gives more than one chunk only when channels < 4 * SMs, and
         // then channels * chunks < channels + 4 * SMs < 8 * SMs, far below the

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import bench
-from gpu_util import FP32_TOL, LOWP_RTOL, no_device_error
+from gpu_util import FP32_TOL, LOWP_RTOL, assert_lowp_close, no_device_error
 from oracle import wide_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -72,4 +72,42 @@ def test_cfg1_bench_path_matches_oracle(graphed):
     ref = O.mlp2(wl.x.cpu(), wl.n_total, st['fc1'].weight.detach().cpu(), st['fc1'].bias.detach().cpu(),
                  st['fc2'].weight.detach().cpu(), st['fc2'].bias.detach().cpu())
     torch.testing.assert_close(y.double().cpu(), ref, **FP32_TOL)
+    no_device_error()
+
+
+@pytest.mark.parametrize("name", ["bn2d_train", "bn2d_eval", "gn", "ln"])
+def test_norm_workloads_match_oracle(name):
+    """The memory-bound norm workloads bench.py times, at full size (419 MB
+    / 537 MB inputs), checked against the oracle on three sampled models
+    (training-mode BatchNorm also through its running-statistics update)."""
+    wl = _workload(name)
+    m = wl.module
+    before = None
+    if name == "bn2d_train":
+        before = (m.op.running_mean.detach().cpu().clone(), m.op.running_var.detach().cpu().clone())
+    y = wl.step(wl.x)
+    torch.cuda.synchronize()
+    n = wl.n_total
+    for i in (0, n // 2, n - 1):
+        xi = wl.x[i:i + 1].cpu()
+        if name.startswith("bn2d"):
+            c = wl.c
+            sl = slice(i * c, (i + 1) * c)
+            rm0 = before[0][sl] if before else m.op.running_mean[sl].detach().cpu()
+            rv0 = before[1][sl] if before else m.op.running_var[sl].detach().cpu()
+            ref, new_rm, new_rv = O.batchnorm(xi, 1, c, m.op.weight[sl].detach().cpu(), m.op.bias[sl].detach().cpu(),
+                                              rm0, rv0, name == "bn2d_train", momentum=0.1)
+            if name == "bn2d_train":
+                assert_lowp_close(m.op.running_mean[sl], new_rm)
+                assert_lowp_close(m.op.running_var[sl], new_rv)
+        elif name == "gn":
+            c = wl.c
+            sl = slice(i * c, (i + 1) * c)
+            ref = O.groupnorm(xi, 1, wl.groups, m.norm.weight[sl].detach().cpu(), m.norm.bias[sl].detach().cpu(),
+                              m.norm.eps)
+        else:
+            d = wl.d
+            sl = slice(i * d, (i + 1) * d)
+            ref = O.layernorm(xi, m.weight[sl].detach().cpu(), m.bias[sl].detach().cpu(), 1, d, m.eps)
+        assert_lowp_close(y[i:i + 1], ref)
     no_device_error()

@@ -57,7 +57,9 @@ def test_batchnorm_eval_random(shape, dtype):
     (assert_fp32_close if dtype == torch.float32 else assert_lowp_close)(y, ref)
 
 
-@pytest.mark.parametrize("shape", [(2, 64, 3, 33, 17), (3, 32, 8, 64, 64), (4, 6, 10), (1, 1000, 4, 50)])
+@pytest.mark.parametrize("shape", [(2, 64, 3, 33, 17), (3, 32, 8, 64, 64), (4, 6, 10), (1, 1000, 4, 50),
+                                   # one-pass kernel: 16-byte vectors (up to 8 per thread), scalars
+                                   (4, 32, 8, 32, 32), (3, 16, 5, 16, 16), (5, 3, 4, 8), (2, 7, 3, 5, 3)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_batchnorm_train_random(shape, dtype):
     gen = torch.Generator().manual_seed(sum(shape) + 1)
