@@ -66,6 +66,23 @@ WIDEK_API int widek_last_error(char* buf, size_t len);
  * *code (0 = none) and clears it. Returns WIDEK_OK or WIDEK_ERR_CUDA. */
 WIDEK_API int widek_device_error(int* code);
 
+/* Device error word codes (widek_device_error). */
+#define WIDEK_DEV_ERR_GEMM_TIMEOUT 101  /* tcgen05 GEMM pipeline wait ran out */
+#define WIDEK_DEV_ERR_RNN_TIMEOUT 102   /* recurrent kernel cluster wait ran out */
+#define WIDEK_DEV_ERR_ATTN_TIMEOUT 103  /* attention pipeline wait ran out */
+#define WIDEK_DEV_ERR_CONV_TIMEOUT 104  /* conv pipeline wait ran out */
+#define WIDEK_DEV_ERR_NORM_TIMEOUT 105  /* BatchNorm ring wait ran out */
+#define WIDEK_DEV_ERR_WAIT_PROBE 106    /* widek_test_bounded_wait ran out, as it must */
+#define WIDEK_DEV_ERR_INDEX 110         /* an index input was out of range (skipped) */
+
+/* Test hook for the failure path: launches one kernel that waits, for at
+ * most limit_ns nanoseconds (0 < limit_ns <= 1 s), on an mbarrier that
+ * nothing arrives at; the wait runs out, the kernel records
+ * WIDEK_DEV_ERR_WAIT_PROBE in the device error word and returns, exactly as
+ * the library's other bounded waits do. No fault, no trap; the context stays
+ * usable. No counterpart in the reference. */
+WIDEK_API int widek_test_bounded_wait(uint64_t limit_ns, void* stream);
+
 /* ---- WideLinear -------------------------------------------------------- */
 
 /* y[i] = act(x[i] @ w[i]^T + bias[i]) for every model i in [0, n).

@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace widek {
 
@@ -139,3 +140,37 @@ int encode_tmap_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
 }  // namespace widek
 
 extern "C" long long widek_launch_count(void) { return widek::launch_count(); }
+
+// ---------------------------------------------------------------------------
+// Failure-path probe: a kernel whose mbarrier wait can never be satisfied
+// (nothing arrives at the barrier) gives up after limit_ns, records
+// DEV_ERR_WAIT_PROBE in the device error word and returns, as every bounded
+// wait of the library does. Lets a test check, without any fault, that a
+// wait that runs out ends the kernel and leaves the context usable.
+// ---------------------------------------------------------------------------
+namespace widek {
+namespace {
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns, int* err) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bar, 1);
+        abort_flag = 0;
+        sm100::mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !sm100::mbar_wait_ns(&bar, 0, &abort_flag, limit_ns))
+        raise_device_error(err, DEV_ERR_WAIT_PROBE);
+    __syncthreads();
+}
+}  // namespace
+}  // namespace widek
+
+extern "C" int widek_test_bounded_wait(uint64_t limit_ns, void* stream) {
+    using namespace widek;
+    if (limit_ns == 0 || limit_ns > 1000000000ull)
+        return set_error(WIDEK_ERR_INVALID, "widek_test_bounded_wait: limit %llu ns outside (0, 1 s]",
+                         (unsigned long long)limit_ns);
+    bounded_wait_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(limit_ns, device_error_ptr());
+    return check_launch("widek_test_bounded_wait");
+}

@@ -53,6 +53,7 @@ enum DeviceError : int {
     DEV_ERR_ATTN_TIMEOUT = 103,
     DEV_ERR_CONV_TIMEOUT = 104,
     DEV_ERR_NORM_TIMEOUT = 105,   // BatchNorm ring wait ran out
+    DEV_ERR_WAIT_PROBE = 106,     // widek_test_bounded_wait: its wait ran out (expected)
     DEV_ERR_INDEX = 110,          // an index input was out of range (skipped)
 };
 

@@ -42,7 +42,8 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity)
 // Waits for the phase with the given parity to complete. Returns false if the
 // wait ran past kWaitLimitNs or *abort became non-zero (another role of the
 // same CTA gave up), so that the caller can leave its loop in order.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, const volatile int* abort,
+                                             uint64_t limit_ns) {
     const uint32_t a = smem_addr(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -51,8 +52,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(a, parity)) return true;
         if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    return mbar_wait_ns(bar, parity, abort, kWaitLimitNs);
 }
 
 // ---- TMA ------------------------------------------------------------------

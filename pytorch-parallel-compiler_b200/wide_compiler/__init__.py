@@ -13,6 +13,7 @@ The reference's benchmark subsystem is not shipped; as in the reference when
 that subsystem is unavailable, the benchmark names are None.
 """
 from .api import compile, WideBuilder, pack, unpack
+from . import _torch_ops  # noqa: F401  (registers the torch.library operators widek::*)
 from .core.config import WideConfig, get_default_config, set_default_config
 from .core.registry import register, unregister, get_registry, list_registered
 from .core.traced_wide import TracedWideModel, FunctionalOp, BinaryOp, print_trace

@@ -28,6 +28,10 @@ WIDEK_ERR_UNSUPPORTED = -2
 WIDEK_ERR_CUDA = -3
 WIDEK_ERR_TIMEOUT = -4
 
+# device error word codes (include/widek.h WIDEK_DEV_ERR_*)
+DEV_ERR_GEMM_TIMEOUT, DEV_ERR_RNN_TIMEOUT, DEV_ERR_ATTN_TIMEOUT = 101, 102, 103
+DEV_ERR_CONV_TIMEOUT, DEV_ERR_NORM_TIMEOUT, DEV_ERR_WAIT_PROBE, DEV_ERR_INDEX = 104, 105, 106, 110
+
 F32, BF16, F16 = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_GELU = 0, 1, 2
 
@@ -43,6 +47,7 @@ SIGNATURES = {
     "widek_version": [],
     "widek_last_error": [ctypes.c_char_p, ctypes.c_size_t],
     "widek_device_error": [ctypes.POINTER(ctypes.c_int)],
+    "widek_test_bounded_wait": [ctypes.c_uint64, _c_void_p],
     "widek_linear_fwd": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
     "widek_linear_fwd_simt": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
     "widek_linear_set_variant": [_int],

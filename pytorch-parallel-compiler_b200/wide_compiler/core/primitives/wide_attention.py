@@ -21,7 +21,7 @@ from typing import List, Optional, Tuple, Union
 import torch
 from torch import Tensor, nn
 
-from ... import _derived, ops
+from ... import ops
 
 
 class AttentionStrategy(Enum):
@@ -79,15 +79,8 @@ class WideAttention(nn.Module):
 
     def _fused_qkv(self) -> Tuple[Tensor, Optional[Tensor]]:
         """[q; kv] weight [N, 3D, D] (and bias [N, 3D]) for self-attention,
-        kept between forwards while the four parameters are unchanged
-        (``wide_compiler._derived``: rebuilt after in-place updates and inside
-        every CUDA-graph capture)."""
-        def build():
-            with torch.no_grad():
-                w = torch.cat([self.q_weight, self.kv_weight], dim=1).contiguous()
-                b = None if self.q_bias is None else torch.cat([self.q_bias, self.kv_bias], dim=1).contiguous()
-            return w, b
-        return _derived.cached(self, 'qkv', (self.q_weight, self.kv_weight, self.q_bias, self.kv_bias), build)
+        kept between forwards while the four parameters are unchanged."""
+        return ops.fused_qkv(self.q_weight, self.kv_weight, self.q_bias, self.kv_bias)
 
     def forward(self, query: Tensor, key: Optional[Tensor] = None, value: Optional[Tensor] = None,
                 attn_mask: Optional[Tensor] = None, is_causal: bool = False,

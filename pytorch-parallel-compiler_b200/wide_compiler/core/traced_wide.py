@@ -747,7 +747,9 @@ class TracedWideModel(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         from ..ops import LAYOUT_PACKED
-        if self._needs_grad(x):
+        # Under autograd, and while dynamo traces (torch.compile), the stages
+        # run one by one on the differentiable / torch.library operators.
+        if self._needs_grad(x) or torch.compiler.is_compiling():
             out = self._run_stages(self._unpack(x), fused=False)
             if isinstance(out, tuple):
                 out = out[0]

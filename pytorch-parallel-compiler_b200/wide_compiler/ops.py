@@ -25,6 +25,13 @@ UNARY_CODES = {"relu": 0, "gelu": 1, "sigmoid": 2, "tanh": 3, "silu": 4}
 BINARY_CODES = {"add": 0, "mul": 1, "sub": 2, "div": 3}
 
 
+def _compiling() -> bool:
+    """Dynamo is tracing: the wide ops go through their torch.library
+    operators (``_torch_ops``), which it can trace, instead of the ctypes
+    calls, which it cannot."""
+    return torch.compiler.is_compiling()
+
+
 def _guard(dev: torch.device):
     if dev.index is None or dev.index == torch.cuda.current_device():
         return contextlib.nullcontext()
@@ -52,6 +59,8 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
     x: [N, ..., K] (any batch dims), weight: [N, O, K], bias: [N, O] or None.
     Returns [N, ..., O].
     """
+    if _compiling() and not force_simt:
+        return torch.ops.widek.linear(x, weight, bias, act)
     if _AG.needs_grad(x, weight, bias):
         return _AG.run(linear, _AG.linear_t, x, weight, bias, act, force_simt)
     dev = N.require_cuda(x, weight, bias, what="WideLinear")
@@ -152,6 +161,8 @@ def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Te
 
 def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: float) -> Tensor:
     """LayerNorm over the last dim with per-model affine (weight/bias flat [n*d])."""
+    if _compiling():
+        return torch.ops.widek.layernorm(x, weight, bias, n, d, eps)
     if _AG.needs_grad(x, weight, bias):
         return _AG.run(layernorm, _AG.layernorm_t, x, weight, bias, n, d, eps)
     dev = N.require_cuda(x, weight, bias, what="WideLayerNorm")
@@ -175,6 +186,8 @@ def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: floa
 
 def swap01(x: Tensor) -> Tensor:
     """[A, B, *rest] -> [B, A, *rest] as one dense copy (rows of prod(rest))."""
+    if _compiling():
+        return torch.ops.widek.swap01(x)
     if _AG.needs_grad(x):
         return _AG.run(swap01, _AG.swap01_t, x)
     dev = N.require_cuda(x, what="swap01")
@@ -215,6 +228,8 @@ def pack(inputs: Sequence[Tensor]) -> Tensor:
 # ---------------------------------------------------------------------------
 
 def unary(x: Tensor, op: str) -> Tensor:
+    if _compiling():
+        return torch.ops.widek.unary(x, op)
     if _AG.needs_grad(x):
         return _AG.run(unary, _AG.unary_t, x, op)
     dev = N.require_cuda(x, what=f"unary {op}")
@@ -228,6 +243,8 @@ def unary(x: Tensor, op: str) -> Tensor:
 
 
 def binary(a: Tensor, b: Tensor, op: str) -> Tensor:
+    if _compiling():
+        return torch.ops.widek.binary(a, b, op)
     if _AG.needs_grad(a, b):
         return _AG.run(binary, _AG.binary_t, a, b, op)
     dev = N.require_cuda(a, b, what=f"binary {op}")
@@ -259,6 +276,9 @@ def batchnorm(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias: Optiona
     """Per-(model, channel) batch normalization on [N, B, C, *S]; weight, bias
     and running stats flat [N*C]. With use_batch_stats the running stats (if
     update_running) are updated in place."""
+    if _compiling():
+        return torch.ops.widek.batchnorm(x, n, c, weight, bias, running_mean, running_var, use_batch_stats,
+                                         update_running, momentum, eps)
     if _AG.needs_grad(x, weight, bias):
         return _AG.run(batchnorm, _AG.batchnorm_t, x, n, c, weight, bias, running_mean, running_var,
                        use_batch_stats, update_running, momentum, eps)
@@ -292,6 +312,8 @@ def groupnorm(x: Tensor, n: int, groups: int, weight: Optional[Tensor], bias: Op
               row_stats: bool = False):
     """GroupNorm on [N, B, C, *S] with statistics per (model, sample, group).
     With row_stats also returns fp32 (mean, biased var) of shape [N, B, groups]."""
+    if _compiling() and not row_stats:
+        return torch.ops.widek.groupnorm(x, n, groups, weight, bias, eps)
     if _AG.needs_grad(x, weight, bias):
         return _AG.run(groupnorm, _AG.groupnorm_t, x, n, groups, weight, bias, eps, row_stats)
     dev = N.require_cuda(x, weight, bias, what="WideGroupNorm")
@@ -334,6 +356,8 @@ def instancenorm_train(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias
 
 def embedding(idx: Tensor, weight: Tensor) -> Tensor:
     """[N, V, D] tables, shared integer indices of any shape -> [N, *idx.shape, D]."""
+    if _compiling():
+        return torch.ops.widek.embedding(idx, weight)
     if _AG.needs_grad(weight):
         return _AG.run(embedding, _AG.embedding_t, idx, weight)
     dev = N.require_cuda(idx, weight, what="WideEmbedding")
@@ -401,6 +425,8 @@ def _opt_dense(t: Optional[Tensor]) -> Optional[Tensor]:
 def gru(x: Tensor, h0: Optional[Tensor], w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor],
         b_hh: Optional[Tensor]):
     """WideGRU forward: returns (out [N, B, T, H], h_n [N, B, H])."""
+    if _compiling():
+        return torch.ops.widek.gru(x, h0, w_ih, w_hh, b_ih, b_hh)
     if _AG.needs_grad(x, h0, w_ih, w_hh, b_ih, b_hh):
         return _AG.run(gru, _AG.gru_t, x, h0, w_ih, w_hh, b_ih, b_hh)
     N.require_cuda(x, h0, w_ih, w_hh, b_ih, b_hh, what="WideGRU")
@@ -421,6 +447,9 @@ def lstm_blockdiag(x: Tensor, h0: Optional[Tensor], c0: Optional[Tensor], weight
     weight_ih [n*4H, n*I] and weight_hh [n*4H, n*H] (model i's block read by
     stride, no extracted copy), biases [n, 4H]: (out, (h_n, c_n)). Returns
     None (launching nothing) when autograd needs the result."""
+    if _compiling():
+        out, hn, cn = torch.ops.widek.lstm(x, h0, c0, weight_ih, weight_hh, b_ih, b_hh, n, hidden)
+        return out, (hn, cn)
     if _AG.needs_grad(x, h0, c0, weight_ih, weight_hh, b_ih, b_hh):
         return None
     N.require_cuda(x, h0, c0, weight_ih, weight_hh, b_ih, b_hh, what="WideLSTM")
@@ -507,18 +536,41 @@ def attention_core(q: Tensor, k: Tensor, v: Tensor, nb: int, heads: int, tq: int
     return out
 
 
-def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool) -> Tensor:
-    """WideAttention forward on N-first [N, B, T, D] tensors (see the module)."""
-    params = (mod.q_weight, mod.q_bias, mod.kv_weight, mod.kv_bias, mod.out_weight, mod.out_bias)
+def fused_qkv(q_weight: Tensor, kv_weight: Tensor, q_bias: Optional[Tensor],
+              kv_bias: Optional[Tensor]):
+    """[q; kv] weight [N, 3D, D] (and bias [N, 3D]) for self-attention, kept
+    on q_weight between calls while the four parameters are unchanged
+    (``_derived``: rebuilt after in-place updates and inside every CUDA-graph
+    capture)."""
+    def build():
+        with torch.no_grad():
+            w = torch.cat([q_weight, kv_weight], dim=1).contiguous()
+            b = None if q_bias is None else torch.cat([q_bias, kv_bias], dim=1).contiguous()
+        return w, b
+    return _derived.cached(q_weight, 'qkv', (q_weight, kv_weight, q_bias, kv_bias), build)
+
+
+def attention_tensors(query: Tensor, key: Tensor, value: Tensor, q_weight: Tensor, q_bias: Optional[Tensor],
+                      kv_weight: Tensor, kv_bias: Optional[Tensor], out_weight: Tensor, out_bias: Optional[Tensor],
+                      n_heads: int, attn_mask: Optional[Tensor], is_causal: bool, self_attn: bool) -> Tensor:
+    """WideAttention forward on N-first [N, B, T, D] tensors from its
+    parameters: q_weight [N, D, D], kv_weight [N, 2D, D] (k rows then v rows),
+    out_weight [N, D, D], biases [N, D] / [N, 2D]; self_attn: key and value
+    are the query (one fused [q; kv] projection)."""
+    if _compiling():
+        return torch.ops.widek.attention(query, key, value, q_weight, q_bias, kv_weight, kv_bias, out_weight,
+                                         out_bias, n_heads, attn_mask, is_causal, self_attn)
+    params = (q_weight, q_bias, kv_weight, kv_bias, out_weight, out_bias)
     if _AG.needs_grad(query, key, value, *params):
-        kernel = lambda q, k, v, m, c, h, *p: attention(mod, q, k, v, m, c)
-        return _AG.run(kernel, _AG.attention_t, query, key, value, attn_mask, is_causal, mod.n_heads, *params)
-    dev = N.require_cuda(query, key, value, mod.q_weight, what="WideAttention")
-    _same_dtype("WideAttention", mod.q_weight, query, key, value)
+        kernel = lambda q, k, v, m, c, h, *p: attention_tensors(q, k, v, *p, h, m, c, self_attn)
+        return _AG.run(kernel, _AG.attention_t, query, key, value, attn_mask, is_causal, n_heads, *params)
+    dev = N.require_cuda(query, key, value, q_weight, what="WideAttention")
+    _same_dtype("WideAttention", q_weight, query, key, value)
     if is_causal and attn_mask is not None:
         raise RuntimeError("WideAttention: an explicit attn_mask cannot be combined with is_causal=True "
                            "(same rule as scaled_dot_product_attention)")
-    n, d, heads = mod.n, mod.d_model, mod.n_heads
+    n, d = q_weight.shape[0], q_weight.shape[1]
+    heads = n_heads
     dh = d // heads
     if query.dim() != 4 or query.shape[0] != n or query.shape[3] != d:
         raise ValueError(f"WideAttention: query must be [N={n}, B, T, D={d}], got {tuple(query.shape)}")
@@ -526,26 +578,33 @@ def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optiona
     tk = key.shape[2]
     if key.shape[:2] != (n, b) or value.shape[:3] != key.shape[:3]:
         raise ValueError("WideAttention: key/value shapes do not match the query")
-    if key is query and value is query:
-        w, bias = mod._fused_qkv()
+    if self_attn:
+        w, bias = fused_qkv(q_weight, kv_weight, q_bias, kv_bias)
         qkv = linear(query, w, bias)                       # [N, B, T, 3D]
         flat = qkv.view(-1)
         q_t, k_t, v_t = flat, flat[d:], flat[2 * d:]
         sq = sk = sv = 3 * d
     elif value is key:
-        q_t = linear(query, mod.q_weight, mod.q_bias).view(-1)
-        kv = linear(key, mod.kv_weight, mod.kv_bias).view(-1)   # [N, B, Tk, 2D]
+        q_t = linear(query, q_weight, q_bias).view(-1)
+        kv = linear(key, kv_weight, kv_bias).view(-1)      # [N, B, Tk, 2D]
         k_t, v_t = kv, kv[d:]
         sq, sk, sv = d, 2 * d, 2 * d
     else:
-        kb = mod.kv_bias
-        q_t = linear(query, mod.q_weight, mod.q_bias).view(-1)
-        k_t = linear(key, mod.kv_weight[:, :d], None if kb is None else kb[:, :d]).view(-1)
-        v_t = linear(value, mod.kv_weight[:, d:], None if kb is None else kb[:, d:]).view(-1)
+        kb = kv_bias
+        q_t = linear(query, q_weight, q_bias).view(-1)
+        k_t = linear(key, kv_weight[:, :d], None if kb is None else kb[:, :d]).view(-1)
+        v_t = linear(value, kv_weight[:, d:], None if kb is None else kb[:, d:]).view(-1)
         sq = sk = sv = d
     o = torch.empty(n, b, tq, d, device=dev, dtype=query.dtype)
     attention_core(q_t, k_t, v_t, n * b, heads, tq, tk, dh, sq, sk, sv, o, is_causal, attn_mask)
-    return linear(o, mod.out_weight, mod.out_bias)
+    return linear(o, out_weight, out_bias)
+
+
+def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool) -> Tensor:
+    """WideAttention forward on N-first [N, B, T, D] tensors (see the module)."""
+    return attention_tensors(query, key, value, mod.q_weight, mod.q_bias, mod.kv_weight, mod.kv_bias,
+                             mod.out_weight, mod.out_bias, mod.n_heads, attn_mask, is_causal,
+                             key is query and value is query)
 
 
 # ---------------------------------------------------------------------------
@@ -614,6 +673,9 @@ def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, p
     ([N*Cout]), activation, residual. With non-default layouts the call
     returns None when the library cannot serve the combination for this
     geometry (nothing is launched); the default layouts always run."""
+    if _compiling() and scale is None and shift is None and residual is None and act == ACT_NONE \
+            and in_layout == out_layout == res_layout == LAYOUT_NFIRST:
+        return torch.ops.widek.conv(x, weight, bias, n, list(stride), list(padding), list(dilation))
     if _AG.needs_grad(x, weight, bias, scale, shift, residual):
         return _AG.run(conv_nd, _AG.conv_nd_t, x, weight, bias, n, stride, padding, dilation, scale, shift,
                        residual, act, residual_first, in_layout, out_layout, res_layout)

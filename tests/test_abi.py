@@ -92,3 +92,13 @@ def test_mlp_chain_argument_checks():
     assert lib.widek_mlp_chain_supported(wide, acts, 1, 1, 4, N.F32) == 0
     zero = (I64 * 2)(0, 8)
     assert lib.widek_mlp_chain_supported(zero, acts, 1, 1, 4, N.F32) == 0
+
+
+def test_bounded_wait_probe_rejects_bad_limits():
+    """Argument checks of the failure-path probe run on the host (nothing is
+    launched), so they need no GPU."""
+    from wide_compiler import _native as N
+    lib = N.load()
+    assert lib.widek_test_bounded_wait(0, None) == N.WIDEK_ERR_INVALID
+    assert lib.widek_test_bounded_wait(2_000_000_000, None) == N.WIDEK_ERR_INVALID
+    assert "limit" in N.last_error()
