@@ -283,7 +283,8 @@ class _Traced(Workload):
         from wide_compiler import parallel
         world, rank = self._world_rank
         self.module = parallel.ShardedWideModel(models, sample, rank=rank, world=world,
-                                                gather=self._gather, compile_model=self.compile_model)
+                                                gather=self._gather, compile_model=self.compile_model,
+                                                gather_chunks=getattr(self, '_gather_chunks', 1))
         self.module.to(dev, dtype).eval()
         self.x = wc.pack([t.to(dev, dtype) for t in per_model_inputs])
 
@@ -843,6 +844,7 @@ def measure(name, ctx, clocks):
         lo, hi = shard_range(wl.n_total, ctx.world, ctx.rank)
         wl._world_rank = (ctx.world, ctx.rank)
     wl._gather = bool(args.gather and ctx.world > 1 and not args.weak)
+    wl._gather_chunks = args.gather_chunks
     n_local = hi - lo
     wl.setup(ctx.dev, lo, hi, seed=args.seed)
     x = wl.x
@@ -856,18 +858,25 @@ def measure(name, ctx, clocks):
         return y
 
     steps = args.steps if name == HEADLINE or args.workload != "all" else args.sub_steps
-    for _ in range(max(args.warmup, 3)):
+    warm = max(args.warmup, 3)
+    torch.cuda.synchronize(ctx.dev)
+    t_w = time.perf_counter()
+    for _ in range(warm):
         step()
+    torch.cuda.synchronize(ctx.dev)
+    t_step = (time.perf_counter() - t_w) / warm
     ctx.barrier()
-    # Clock window: untimed steps for --clock-window seconds right before the
-    # timed region, so that the 100 ms nvidia-smi samples see the GPU under
-    # this workload's load even when the timed region itself is a few ms.
+    # Clock window: untimed steps for about --clock-window seconds right
+    # before the timed region, so that the 100 ms nvidia-smi samples see the
+    # GPU under this workload's load even when the timed region itself is a
+    # few ms. The step count is agreed over the ranks (max), since a step may
+    # hold a collective and every rank must issue the same ones.
     mark0 = clocks.mark()
-    t_cw = time.perf_counter()
-    while time.perf_counter() - t_cw < args.clock_window:
-        for _ in range(8):
-            step()
-        torch.cuda.synchronize(ctx.dev)
+    n_cw = int(ctx.max_over_ranks(min(100000, math.ceil(args.clock_window / max(t_step, 1e-6)))))
+    for i in range(n_cw):
+        step()
+        if i % 8 == 7:
+            torch.cuda.synchronize(ctx.dev)
     ctx.barrier()
     stream = torch.cuda.current_stream(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1058,7 +1067,8 @@ def run_b200(args):
             if k in head:
                 line[k] = head[k]
         line["parallel"] = {"ranks": world, "split": "weak: every rank runs all N models" if args.weak else
-                            "contiguous N-slices, one per rank (N fixed)", "gather": bool(args.gather and world > 1)}
+                            "contiguous N-slices, one per rank (N fixed)", "gather": bool(args.gather and world > 1),
+                            "gather_chunks": args.gather_chunks if args.gather and world > 1 else None}
         line["variants"] = {"linear": args.linear_variant, "attention": args.attn_variant, "conv": args.conv_variant}
         if len(names) > 1:
             line["configs"] = {k: recs[k] for k in names[1:]}
@@ -1087,6 +1097,9 @@ def main():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--weak", action="store_true", help="every rank runs all N models (weak scaling)")
     ap.add_argument("--gather", action="store_true", help="include the optional output all-gather in every step")
+    ap.add_argument("--gather-chunks", type=int, default=1,
+                    help="with --gather on TracedWideModel workloads: batch slices whose gathers overlap the "
+                         "next slice's forward")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time for the headline")
     ap.add_argument("--sub-cpu-seconds", type=float, default=3.0, help="CPU baseline time per other configuration")
     ap.add_argument("--ref-step-seconds", type=float, default=1.0,

@@ -102,10 +102,24 @@ WIDEK_API int widek_linear_fwd_simt(const void* x, const void* w, const void* bi
                           int64_t n, int64_t m, int64_t k, int64_t o,
                           int dtype, int act, void* stream);
 
+/* widek_linear_fwd with the rows of x (in_layout) and y (out_layout) in
+ * WIDEK_LAYOUT_NFIRST ([n, m, *]) or WIDEK_LAYOUT_PACKED, the
+ * TracedWideModel boundary layout [B, n*T, *] with m = B*T and
+ * rows_per_block = T (model i's row b*T + t at (b*n + i)*T + t). The tensor
+ * maps read and write the packed rows in place, so a graph whose first or
+ * last stage is a Linear on [B, T, features] inputs needs no unpack / pack
+ * copy. The tensor-core kernel takes packed rows when T is a multiple or a
+ * divisor of 128; other T run on the CUDA-core kernel.
+ * Replaces: wide_compiler/core/traced_wide.py:463-469 / :527-532 around
+ * wide_linear.py:165-168. */
+WIDEK_API int widek_linear_fwd_ex(const void* x, const void* w, const void* bias, void* y,
+                                  int64_t n, int64_t m, int64_t k, int64_t o, int64_t rows_per_block,
+                                  int in_layout, int out_layout, int dtype, int act, void* stream);
+
 /* Selects the tensor-core tiling of widek_linear_fwd for this process:
  * 0 = automatic (single-CTA 128xBN tiles), 1 = single-CTA tiles,
- * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128,
- * 3 = single-CTA 128x128 tiles (6-stage ring), 4 = as 1 without L2 hints.
+ * 3 = single-CTA 128x128 tiles (6-stage ring), 4 = as 1 without L2 hints,
+ * 5 = direct global stores instead of the TMA store (2 is not a variant).
  * A measurement knob (process-wide, not synchronized with running calls).
  * No counterpart in the reference. */
 WIDEK_API int widek_linear_set_variant(int variant);
@@ -145,6 +159,17 @@ WIDEK_API int widek_mlp_chain_supported(const int64_t* dims, const int* acts, in
 WIDEK_API int widek_layernorm_fwd(const void* x, const void* w, const void* b, void* y,
                         int64_t n, int64_t rows_per_model, int64_t d,
                         double eps, int dtype, void* stream);
+
+/* widek_layernorm_fwd on rows laid out [outer][n][inner][d]: row r uses the
+ * affine of model (r / inner) % n. outer = 1, inner = rows_per_model is the
+ * N-first layout; the packed TracedWideModel boundary layout [B, n*T, d]
+ * (and [B, n*d], T = 1) is outer = B, inner = T, so a graph whose first or
+ * last stage is a LayerNorm needs no unpack / pack copy.
+ * Replaces: wide_compiler/core/traced_wide.py:463-469 / :527-532 (the
+ * unpack / pack around wide_layernorm.py:62-65). */
+WIDEK_API int widek_layernorm_fwd_ex(const void* x, const void* w, const void* b, void* y, int64_t n,
+                                     int64_t outer, int64_t inner, int64_t d, double eps, int dtype,
+                                     void* stream);
 
 /* ---- layout boundary (pack / unpack) ----------------------------------- */
 
@@ -329,6 +354,26 @@ WIDEK_API int widek_lstm_fwd(const void* x, const void* w_ih, const void* w_hh, 
                              size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps,
                              int64_t input, int64_t hidden, int dtype, void* stream);
 
+/* widek_gru_fwd / widek_lstm_fwd with explicit layouts of x (in_layout) and
+ * out (out_layout), each WIDEK_LAYOUT_NFIRST ([n, batch, steps, *]) or
+ * WIDEK_LAYOUT_PACKED (the TracedWideModel boundary layout [batch,
+ * n*steps, *]): the projection reads a packed input in place and the
+ * recurrence writes a packed output directly (h_n / c_n stay N-first), so a
+ * graph that starts or ends with the recurrent layer needs no unpack / pack
+ * copy. Replaces: wide_compiler/core/traced_wide.py:463-469 / :527-532
+ * around wide_gru.py:148-213, wide_lstm.py:158-234. */
+WIDEK_API int widek_gru_fwd_ex(const void* x, const void* w_ih, const void* w_hh, const void* b_ih,
+                               const void* b_hh, const void* h0, void* out, void* h_n,
+                               const int64_t* w_strides, void* workspace, size_t workspace_bytes,
+                               int64_t n, int64_t batch, int64_t steps, int64_t input, int64_t hidden,
+                               int in_layout, int out_layout, int dtype, void* stream);
+WIDEK_API int widek_lstm_fwd_ex(const void* x, const void* w_ih, const void* w_hh, const void* b_ih,
+                                const void* b_hh, const void* h0, const void* c0, void* out, void* h_n,
+                                void* c_n, const int64_t* w_strides, void* workspace,
+                                size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps,
+                                int64_t input, int64_t hidden, int in_layout, int out_layout, int dtype,
+                                void* stream);
+
 /* Workspace bytes of widek_gru_fwd (lstm = 0) / widek_lstm_fwd (lstm = 1). */
 WIDEK_API size_t widek_rnn_workspace(int lstm, int64_t n, int64_t batch, int64_t steps, int64_t hidden,
                                      int dtype);
@@ -343,13 +388,21 @@ WIDEK_API int widek_rnn_set_variant(int variant);
 
 /* ---- WideConv1d / WideConv2d / WideConv3d -------------------------------- */
 
-/* Repacks conv weights [rows][cin][taps] -> [rows][taps][cin] (rows = n*cout,
- * taps = kd*kh*kw) for the tensor-core path; elem_bytes 2 or 4. */
+/* Repacks conv weights [rows][cin][taps] -> [rows][taps][cin_p] (rows =
+ * n*cout, taps = kd*kh*kw, cin_p = cin rounded up to a multiple of 64, the
+ * extra channels of every tap zero) for the tensor-core path; elem_bytes 2
+ * or 4. w_packed holds widek_conv_packed_weight_elems(rows, cin, taps)
+ * elements. */
 WIDEK_API int widek_conv_pack_weight(const void* w, void* w_packed, int64_t rows, int64_t cin,
                                      int64_t taps, int64_t elem_bytes, void* stream);
 
+/* Elements of widek_conv_pack_weight's output: rows * taps * cin_p (-1 for a
+ * negative size). */
+WIDEK_API int64_t widek_conv_packed_weight_elems(int64_t rows, int64_t cin, int64_t taps);
+
 /* Bytes of the channels-last staging workspace widek_conv_fwd uses on the
- * tensor-core path (n*batch*cin*d*h*w elements). */
+ * tensor-core path (n*batch*cin_s*d*h*w elements, cin_s = cin rounded up to
+ * a multiple of 8). */
 WIDEK_API size_t widek_conv_workspace(int64_t n, int64_t batch, int64_t cin, int64_t d, int64_t h,
                                       int64_t w, int dtype);
 
@@ -362,10 +415,13 @@ WIDEK_API size_t widek_conv_workspace(int64_t n, int64_t batch, int64_t cin, int
  *   v = acc + bias[ch]; v *= scale[ch]; v += shift[ch];
  *   residual_first ? v = act(v + residual) : v = act(v) + residual
  * (each term skipped when its pointer is NULL).
- * bf16/f16 2-D/1-D convs with stride 1, cin % 64 == 0 and cout % 16 == 0 run
- * on the tcgen05 implicit-GEMM kernel when w_packed (from
+ * bf16/f16 convs of any rank, channel counts and dilation, with H and W
+ * strides up to 8 (and an output tile whose input box fits 256 elements per
+ * dimension: tile width x stride along W, 128 / tile width x stride along
+ * H), run on the tcgen05 implicit-GEMM kernels when w_packed (from
  * widek_conv_pack_weight) and a workspace of widek_conv_workspace() bytes
- * are given; everything else runs a CUDA-core direct convolution.
+ * are given; fp32 and everything else runs a CUDA-core direct convolution
+ * (widek_conv_path tells which).
  * Replaces: wide_compiler/core/primitives/wide_conv2d.py:169-194 (permute
  * copies + grouped F.conv2d), wide_conv1d.py:118-135, wide_conv3d.py:102-125. */
 WIDEK_API int widek_conv_fwd(const void* x, const void* w, const void* w_packed, const void* bias,

@@ -118,7 +118,7 @@ std::once_flag g_encode_once;
 
 int encode_tmap_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                       const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                      CUtensorMapSwizzle swizzle) {
+                      CUtensorMapSwizzle swizzle, const uint32_t* elem_strides) {
     std::call_once(g_encode_once, []() {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -128,6 +128,8 @@ int encode_tmap_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
     });
     if (!g_encode_tiled) return set_error(WIDEK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (elem_strides)
+        for (int i = 1; i < rank && i < 5; ++i) estr[i] = elem_strides[i];
     CUresult r = g_encode_tiled(map, dtype, (cuuint32_t)rank, const_cast<void*>(base),
                                 reinterpret_cast<const cuuint64_t*>(dims),
                                 reinterpret_cast<const cuuint64_t*>(strides_bytes),

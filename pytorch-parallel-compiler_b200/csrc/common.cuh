@@ -25,9 +25,12 @@ int current_device();
 
 // Encodes a tiled TMA descriptor (dims/strides innermost first; strides are
 // for dims 1..rank-1, in bytes). Out-of-range box elements read as zero.
+// elem_strides (optional, rank entries, each 1..8; entry 0 is ignored): the
+// traversal step per dimension; a box of boxDim[i] elements then delivers
+// ceil(boxDim[i] / elem_strides[i]) elements, densely packed in shared memory.
 int encode_tmap_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                       const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                      CUtensorMapSwizzle swizzle);
+                      CUtensorMapSwizzle swizzle, const uint32_t* elem_strides = nullptr);
 
 // Device-side error word: kernels that give up on a bounded wait, or that
 // detect an out-of-contract index, record a code there instead of trapping.
@@ -38,8 +41,15 @@ int* device_error_ptr();
 // CUDA-core grouped GEMM with a strided weight: y[i] = act(x[i] @ W_i^T +
 // bias[i]) where W_i is the [o, k] matrix at w + i*w_ms with rows w_rs
 // elements apart; x [n, m, k], y [n, m, o] dense (gemm_simt.cu).
+// Optionally x is strided too: row r of model i at
+// x + i*x_ms + (r / x_rpb)*x_bs + (r % x_rpb)*k (x_ms < 0: dense [n, m, k]),
+// which reads the packed [B, n*T, k] boundary layout (x_ms = T*k,
+// x_bs = n*T*k, x_rpb = T) in place; y likewise with y_ms / y_bs and the
+// same row blocks (y_ms < 0: dense [n, m, o]).
 int linear_simt_strided(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m, int64_t k,
-                        int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st);
+                        int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st,
+                        int64_t x_ms = -1, int64_t x_bs = 0, int64_t x_rpb = 0, int64_t y_ms = -1,
+                        int64_t y_bs = 0);
 
 __device__ __forceinline__ void raise_device_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);

@@ -39,26 +39,29 @@ using namespace sm100;
 // ---------------------------------------------------------------------------
 // Layout helpers
 // ---------------------------------------------------------------------------
-// [nb][c][p] -> [nb][p][c], 32x32 tiles through shared memory (any c, p).
+// [nb][c][p] -> [nb][p][c_dst], 32x32 tiles through shared memory (any c,
+// p; c_dst >= c, channels c .. c_dst-1 written as zeros, so that a channel
+// count that is not a multiple of 8 gets 16-byte pixel rows for the TMA).
 template <typename T>
-__global__ void nchw_to_nhwc_kernel(const T* __restrict__ src, T* __restrict__ dst, int64_t nb, int c, int64_t p) {
+__global__ void nchw_to_nhwc_kernel(const T* __restrict__ src, T* __restrict__ dst, int64_t nb, int c, int64_t p,
+                                    int c_dst) {
     __shared__ T tile[32][33];
     const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
     const int64_t p0 = (int64_t)blockIdx.x * 32;
     const int c0 = blockIdx.y * 32;
     for (int64_t img = blockIdx.z; img < nb; img += gridDim.z) {
         const T* s = src + img * c * p;
-        T* d = dst + img * c * p;
+        T* d = dst + img * c_dst * p;
         for (int r = ty; r < 32; r += 8) {
             const int cc = c0 + r;
             const int64_t pp = p0 + tx;
-            if (cc < c && pp < p) tile[r][tx] = s[(int64_t)cc * p + pp];
+            tile[r][tx] = cc < c && pp < p ? s[(int64_t)cc * p + pp] : from_f<T>(0.f);
         }
         __syncthreads();
         for (int r = ty; r < 32; r += 8) {
             const int64_t pp = p0 + r;
             const int cc = c0 + tx;
-            if (cc < c && pp < p) d[pp * c + cc] = tile[tx][r];
+            if (cc < c_dst && pp < p) d[pp * c_dst + cc] = tile[tx][r];
         }
         __syncthreads();
     }
@@ -113,18 +116,19 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_vec_kernel(const uint16_t* _
     }
 }
 
-// w [rows][cin][taps] -> wp [rows][taps][cin]
+// w [rows][cin][taps] -> wp [rows][taps][cin_p] (cin_p >= cin; channels
+// cin .. cin_p-1 of every tap are zeros)
 template <typename U>
 __global__ void pack_weight_kernel(const U* __restrict__ w, U* __restrict__ wp, int64_t rows, int64_t cin,
-                                   int64_t taps) {
-    const int64_t total = rows * cin * taps;
+                                   int64_t taps, int64_t cin_p) {
+    const int64_t total = rows * cin_p * taps;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int64_t r = i / (cin * taps);
-        const int64_t rem = i - r * cin * taps;
-        const int64_t t = rem / cin;
-        const int64_t ci = rem - t * cin;
-        wp[i] = w[(r * cin + ci) * taps + t];
+        const int64_t r = i / (cin_p * taps);
+        const int64_t rem = i - r * cin_p * taps;
+        const int64_t t = rem / cin_p;
+        const int64_t ci = rem - t * cin_p;
+        wp[i] = ci < cin ? w[(r * cin + ci) * taps + t] : U(0);
     }
 }
 
@@ -247,10 +251,20 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct ConvTcGeom {
-    int n, batch, cout, ho, wo, th, tw, tiles_h, tiles_w, nt_count;
-    int kh, kw, cblocks, ph, pw, dh, dw;
+    int n, batch, cout, od, ho, wo, th, tw, tiles_h, tiles_w, nt_count;
+    int kd, kh, kw, cblocks;
+    int pd, ph, pw, sd, sh, sw, dd, dh, dw;
 };
 
+// Per-tap implicit GEMM, any spatial rank (1-D and 2-D are 3-D with unit
+// depth), stride, dilation and channel count. The channels-last input is
+// read through a 5-D map {C, W, H, D, image} whose W and H traversal steps
+// are the conv strides, so that one box {64, tw*sw, th*sh, 1, 1} delivers
+// the tw x th output pixels' input pixels of one tap densely, at
+// coordinates (c0, wo0*sw - pw + kx*dw, ho0*sh - ph + ky*dh,
+// oz*sd - pd + kz*dd, image). Channels beyond the input's (the last 64-block
+// of a channel count that is not a multiple of 64) arrive as zeros (TMA
+// out-of-range fill); the packed weights carry zeros there too.
 template <typename T, int BN, int STAGES, bool TMA_STORE, bool RES_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -276,8 +290,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt_count = g.tiles_h * g.tiles_w;
-    const int kb_count = g.kh * g.kw * g.cblocks;
-    const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * mt_count;
+    const int taps_hw = g.kh * g.kw;
+    const int kb_count = g.kd * taps_hw * g.cblocks;
+    const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * g.od * mt_count;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -299,9 +314,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    // tile -> (model, n-tile, image-in-batch, m-tile); m-tile fastest.
-    auto decode = [&](int64_t tile, int& model, int& nt, int& b, int& mt) {
+    // tile -> (model, n-tile, image-in-batch, output depth, m-tile); m-tile fastest.
+    auto decode = [&](int64_t tile, int& model, int& nt, int& b, int& oz, int& mt) {
         mt = (int)(tile % mt_count); tile /= mt_count;
+        oz = (int)(tile % g.od); tile /= g.od;
         b = (int)(tile % g.batch); tile /= g.batch;
         nt = (int)(tile % g.nt_count);
         model = (int)(tile / g.nt_count);
@@ -314,20 +330,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t ph = 0;
         bool ok = true;
         for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-            int model, nt, b, mt;
-            decode(tile, model, nt, b, mt);
-            const int ho0 = (mt / g.tiles_w) * g.th;
-            const int wo0 = (mt % g.tiles_w) * g.tw;
+            int model, nt, b, oz, mt;
+            decode(tile, model, nt, b, oz, mt);
+            const int hy = (mt / g.tiles_w) * g.th * g.sh - g.ph;
+            const int wx = (mt % g.tiles_w) * g.tw * g.sw - g.pw;
+            const int dz = oz * g.sd - g.pd;
             const int img = model * g.batch + b;
             for (int kb = 0; kb < kb_count; ++kb) {
                 const int cb = kb % g.cblocks;
                 const int tap = kb / g.cblocks;
-                const int ky = tap / g.kw, kx = tap % g.kw;
+                const int kz = tap / taps_hw, kyx = tap - kz * taps_hw;
+                const int ky = kyx / g.kw, kx = kyx - ky * g.kw;
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
-                    tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], cb * BK, wo0 - g.pw + kx * g.dw,
-                                ho0 - g.ph + ky * g.dh, img, pol_x);
+                    tma_load_5d(sA + s * S::A_BYTES, &tm_x, &full[s], cb * BK, wx + kx * g.dw, hy + ky * g.dh,
+                                dz + kz * g.dd, img, pol_x);
                     tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, nt * BN, model, pol_w);
                 }
                 __syncwarp();
@@ -389,15 +407,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // broadcast with shuffles.
         const int q = warp & 3;
         const int ep_tid = threadIdx.x - 64;            // 0..127
-        const int64_t osp = (int64_t)g.ho * g.wo;
+        const int64_t osp = (int64_t)g.od * g.ho * g.wo;
         const T* bias = static_cast<const T*>(e.bias);
         const T* scale = static_cast<const T*>(e.scale);
         const T* shift = static_cast<const T*>(e.shift);
         const T* res = static_cast<const T*>(e.residual);
         int local = 0;
         for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-            int model, nt, b, mt;
-            decode(tile, model, nt, b, mt);
+            int model, nt, b, oz, mt;
+            decode(tile, model, nt, b, oz, mt);
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
             const int r = q * 32 + lane;                 // pixel within the tile
@@ -406,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int wo = wo0 + r % g.tw;
             const bool pix_ok = ho < g.ho && wo < g.wo;
             const int64_t img = (int64_t)model * g.batch + b;
-            const int64_t pix = (int64_t)ho * g.wo + wo;
+            const int64_t pix = ((int64_t)oz * g.ho + ho) * g.wo + wo;
             if (TMA_STORE) {
                 // The previous tile's store must have finished reading sOut and
                 // every thread must be done with the previous sRes; then the
@@ -416,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 epi_bar_sync();
                 if (RES_TMA && ep_tid == 0) {
                     mbar_arrive_expect_tx(res_bar, S::STAGE_RES);
-                    tma_load_4d(sRes, &tm_r, res_bar, wo0, ho0, nt * BN, (int)img, l2_policy_evict_first());
+                    tma_load_5d(sRes, &tm_r, res_bar, wo0, ho0, oz, nt * BN, (int)img, l2_policy_evict_first());
                 }
             }
             if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
@@ -481,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ep_tid == 0) {
                     const int cvalid = g.cout - nt * BN;
                     if (cvalid >= BN) {
-                        tma_store_4d(&tm_y, sOut, wo0, ho0, nt * BN, (int)img);
+                        tma_store_5d(&tm_y, sOut, wo0, ho0, oz, nt * BN, (int)img);
                     }
                     bulk_commit();
                 }
@@ -1078,57 +1096,75 @@ CUtensorMapDataType tmap_dt() {
     return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
+// Channel stride of the staged channels-last input: the channel count
+// rounded up to 8 (16-byte pixel rows, which the TMA needs); the staging
+// writes zeros into the extra channels.
+inline int staged_channels(int cin) { return (cin + 7) & ~7; }
+// Channels per tap of the packed weights: rounded up to the 64-channel block.
+inline int packed_channels(int cin) { return (cin + BK - 1) / BK * BK; }
+
+// Output tile of the per-tap kernel: tw x th pixels of one output depth
+// slice, tw a power of two covering the row (at most 128) and th = 128 / tw.
+// The input box spans tile * stride elements per dimension, at most 256.
+bool tc_tile(const ConvGeom& cg, int& tw, int& th) {
+    tw = 1;
+    while (tw < cg.ow && tw < BM) tw <<= 1;
+    while (tw > 1 && tw * cg.sw > 256) tw >>= 1;
+    th = BM / tw;
+    return tw * cg.sw <= 256 && th * cg.sh <= 256;
+}
+
 template <typename T, int BN, int STAGES, bool TMA_STORE, bool RES_TMA = false>
 int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const ConvEpi& e, cudaStream_t st) {
     using S = ConvSmem<BN, STAGES, RES_TMA>;
     ConvTcGeom g{};
-    g.n = cg.n; g.batch = cg.batch; g.cout = cg.cout; g.ho = cg.oh; g.wo = cg.ow;
-    int tw = 1;
-    while (tw < cg.ow && tw < BM) tw <<= 1;
-    g.tw = tw;
-    g.th = BM / tw;
+    g.n = cg.n; g.batch = cg.batch; g.cout = cg.cout; g.od = cg.od; g.ho = cg.oh; g.wo = cg.ow;
+    if (!tc_tile(cg, g.tw, g.th)) return set_error(WIDEK_ERR_UNSUPPORTED, "conv: no tensor-core tile for this stride");
     g.tiles_h = (cg.oh + g.th - 1) / g.th;
     g.tiles_w = (cg.ow + g.tw - 1) / g.tw;
     g.nt_count = (cg.cout + BN - 1) / BN;
-    g.kh = cg.kh; g.kw = cg.kw; g.cblocks = cg.cin / BK;
-    g.ph = cg.ph; g.pw = cg.pw; g.dh = cg.dh; g.dw = cg.dw;
+    g.kd = cg.kd; g.kh = cg.kh; g.kw = cg.kw;
+    const int cin_s = staged_channels(cg.cin), cin_p = packed_channels(cg.cin);
+    g.cblocks = cin_p / BK;
+    g.pd = cg.pd; g.ph = cg.ph; g.pw = cg.pw;
+    g.sd = cg.sd; g.sh = cg.sh; g.sw = cg.sw;
+    g.dd = cg.dd; g.dh = cg.dh; g.dw = cg.dw;
     const int64_t nb = (int64_t)cg.n * cg.batch;
     CUtensorMap tx, tw_map;
     {
-        const uint64_t dims[4] = {(uint64_t)cg.cin, (uint64_t)cg.w, (uint64_t)cg.h, (uint64_t)nb};
-        const uint64_t strides[3] = {(uint64_t)cg.cin * 2, (uint64_t)cg.w * cg.cin * 2,
-                                     (uint64_t)cg.h * cg.w * cg.cin * 2};
-        const uint32_t box[4] = {BK, (uint32_t)g.tw, (uint32_t)g.th, 1};
-        int rc = encode_tmap_tiled(&tx, tmap_dt<T>(), 4, x_nhwc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        const uint64_t row = (uint64_t)cin_s * 2;
+        const uint64_t dims[5] = {(uint64_t)cin_s, (uint64_t)cg.w, (uint64_t)cg.h, (uint64_t)cg.d, (uint64_t)nb};
+        const uint64_t strides[4] = {row, row * cg.w, row * cg.w * cg.h, row * cg.w * cg.h * cg.d};
+        const uint32_t box[5] = {BK, (uint32_t)(g.tw * cg.sw), (uint32_t)(g.th * cg.sh), 1, 1};
+        const uint32_t estr[5] = {1, (uint32_t)cg.sw, (uint32_t)cg.sh, 1, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dt<T>(), 5, x_nhwc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, estr);
         if (rc) return rc;
     }
     {
-        const uint64_t k = (uint64_t)cg.kh * cg.kw * cg.cin;
+        const uint64_t k = (uint64_t)cg.kd * cg.kh * cg.kw * cin_p;
         const uint64_t dims[3] = {k, (uint64_t)cg.cout, (uint64_t)cg.n};
         const uint64_t strides[2] = {k * 2, (uint64_t)cg.cout * k * 2};
         const uint32_t box[3] = {BK, BN, 1};
         int rc = encode_tmap_tiled(&tw_map, tmap_dt<T>(), 3, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
+    // NCDHW output / residual per image: dims {W, H, D, C, image}; box = one
+    // tile of BN channels of one depth slice ([channel][row][column] in
+    // shared memory).
+    const uint64_t osp = (uint64_t)cg.od * cg.oh * cg.ow;
+    const uint64_t odims[5] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.od, (uint64_t)cg.cout, (uint64_t)nb};
+    const uint64_t ostrides[4] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2, osp * 2, (uint64_t)cg.cout * osp * 2};
+    const uint32_t obox[5] = {(uint32_t)g.tw, (uint32_t)g.th, 1, (uint32_t)BN, 1};
     CUtensorMap ty_map;
     memset(&ty_map, 0, sizeof(ty_map));
     if (TMA_STORE) {
-        // NCHW output per image: dims {W, H, C, image}; box = one tile of BN channels
-        const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)nb};
-        const uint64_t strides[3] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2,
-                                     (uint64_t)cg.cout * cg.oh * cg.ow * 2};
-        const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, (uint32_t)BN, 1};
-        int rc = encode_tmap_tiled(&ty_map, tmap_dt<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        int rc = encode_tmap_tiled(&ty_map, tmap_dt<T>(), 5, y, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
     CUtensorMap tr_map;
     memset(&tr_map, 0, sizeof(tr_map));
     if (RES_TMA) {
-        const uint64_t dims[4] = {(uint64_t)cg.ow, (uint64_t)cg.oh, (uint64_t)cg.cout, (uint64_t)nb};
-        const uint64_t strides[3] = {(uint64_t)cg.ow * 2, (uint64_t)cg.oh * cg.ow * 2,
-                                     (uint64_t)cg.cout * cg.oh * cg.ow * 2};
-        const uint32_t box[4] = {(uint32_t)g.tw, (uint32_t)g.th, (uint32_t)BN, 1};
-        int rc = encode_tmap_tiled(&tr_map, tmap_dt<T>(), 4, e.residual, dims, strides, box,
+        int rc = encode_tmap_tiled(&tr_map, tmap_dt<T>(), 5, e.residual, odims, ostrides, obox,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
@@ -1140,7 +1176,7 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
             return set_error(WIDEK_ERR_CUDA, "conv: cannot reserve %u bytes of shared memory", S::TOTAL);
         attr_done[dev] = true;
     }
-    const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * g.tiles_h * g.tiles_w;
+    const int64_t tiles = (int64_t)g.n * g.nt_count * g.batch * g.od * g.tiles_h * g.tiles_w;
     const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
     kern<<<grid, kThreads, S::TOTAL, st>>>(tx, tw_map, ty_map, tr_map, y, g, e, device_error_ptr());
     return check_launch("widek_conv_fwd (tcgen05)");
@@ -1153,6 +1189,7 @@ int g_conv_variant = 0;
 // Halo-reuse geometry for a stride-1 conv with 64-channel output tiles, or
 // false when it does not fit (tile width, box limits, shared memory).
 bool halo_geometry(const ConvGeom& cg, bool res_tma, ConvHaloGeom& g, uint32_t& smem) {
+    if (cg.d != 1 || cg.kd != 1 || cg.sh != 1 || cg.sw != 1 || cg.cin % BK != 0) return false;
     if (cg.cout % HBN != 0 || cg.ow % 8 != 0 || cg.ow < 8) return false;
     const int tw = cg.ow >= 16 ? 16 : 8;
     const int th = BM / tw;
@@ -1260,9 +1297,13 @@ int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, Con
     return check_launch("widek_conv_fwd (tcgen05 halo)");
 }
 
+// The tensor-core path takes bf16/f16 convs of any rank, channel count and
+// dilation with strides up to 8 along H and W (the TMA traversal-step limit)
+// whose output tile fits the 256-element input box.
 bool tc_eligible(const ConvGeom& g, int dtype) {
-    return (dtype == WIDEK_BF16 || dtype == WIDEK_F16) && g.d == 1 && g.kd == 1 && g.sh == 1 && g.sw == 1 &&
-           g.cin % 64 == 0 && g.cout % 16 == 0 && g.cout <= 4096 && g.h <= 65536 && g.w <= 65536;
+    int tw, th;
+    return (dtype == WIDEK_BF16 || dtype == WIDEK_F16) && g.sh <= 8 && g.sw <= 8 && g.cout <= 4096 &&
+           g.d <= 65536 && g.h <= 65536 && g.w <= 65536 && tc_tile(g, tw, th);
 }
 
 struct ConvLaunch {
@@ -1291,20 +1332,22 @@ struct ConvLaunch {
         if ((wp || query) && tc_eligible(g, dtype)) {
             if constexpr (!std::is_same<T, float>::value) {
                 const int64_t nb = (int64_t)g.n * g.batch;
-                const int64_t p = (int64_t)g.h * g.w;
-                const size_t need = (size_t)nb * g.cin * p * sizeof(T);
+                const int64_t p = (int64_t)g.d * g.h * g.w;
+                const int cin_s = staged_channels(g.cin);
+                const size_t need = (size_t)nb * cin_s * p * sizeof(T);
                 const bool cl_in = in_layout == WIDEK_LAYOUT_CLAST;
                 const bool ws_ok = query || (ws && ws_bytes >= need && aligned16(ws));
                 if (cl_in || ws_ok) {
                     if (!al(wp)) return unsupported("packed weights not 16-byte aligned");
-                    const bool vec_staging = p % 64 == 0 && al(x);
+                    const bool vec_staging = g.cin % 64 == 0 && p % 64 == 0 && al(x);
                     if (!cl_in && in_layout == WIDEK_LAYOUT_PACKED && !vec_staging)
-                        return unsupported("packed input needs 64-pixel multiples and 16-byte alignment");
-                    if (cl_in && !al(x)) return unsupported("channels-last input not 16-byte aligned");
+                        return unsupported("packed input needs 64-channel and 64-pixel multiples and 16-byte alignment");
+                    if (cl_in && (!al(x) || g.cin != cin_s))
+                        return unsupported("channels-last input needs 16-byte alignment and a multiple of 8 channels");
                     // TMA store of the output tile: box width = tile width (>= 8 elements,
                     // 16-byte multiple), rows 16-byte aligned, whole channel tiles.
-                    int tw = 1;
-                    while (tw < g.ow && tw < BM) tw <<= 1;
+                    int tw, th;
+                    tc_tile(g, tw, th);
                     const bool store_ok = tw >= 8 && g.ow % 8 == 0 && al(y);
                     const bool res_tma = store_ok && e.residual && al(e.residual);
                     ConvHaloGeom hg;
@@ -1329,10 +1372,10 @@ struct ConvLaunch {
                                                                             static_cast<uint16_t*>(ws), nb, g.cin, p,
                                                                             packed_b, g.n);
                         } else {
-                            dim3 grid((unsigned)((p + 31) / 32), (unsigned)((g.cin + 31) / 32),
+                            dim3 grid((unsigned)((p + 31) / 32), (unsigned)((cin_s + 31) / 32),
                                       (unsigned)std::min<int64_t>(nb, 65535));
-                            nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(static_cast<const T*>(x),
-                                                                                 static_cast<T*>(ws), nb, g.cin, p);
+                            nchw_to_nhwc_kernel<T><<<grid, dim3(32, 8), 0, st>>>(
+                                static_cast<const T*>(x), static_cast<T*>(ws), nb, g.cin, p, cin_s);
                         }
                         int rc = check_launch("widek_conv_fwd (nhwc staging)");
                         if (rc) return rc;
@@ -1412,20 +1455,27 @@ int widek_conv_pack_weight(const void* w, void* wp, int64_t rows, int64_t cin, i
     if (rows * cin * taps == 0) return WIDEK_OK;
     if (!w || !wp) return set_error(WIDEK_ERR_INVALID, "conv_pack_weight: null pointer");
     cudaStream_t st = (cudaStream_t)stream;
-    const int64_t total = rows * cin * taps;
+    const int64_t cin_p = (cin + BK - 1) / BK * BK;
+    const int64_t total = rows * cin_p * taps;
     if (elem_bytes == 2)
         pack_weight_kernel<uint16_t><<<grid_cap(total, 256), 256, 0, st>>>(
-            static_cast<const uint16_t*>(w), static_cast<uint16_t*>(wp), rows, cin, taps);
+            static_cast<const uint16_t*>(w), static_cast<uint16_t*>(wp), rows, cin, taps, cin_p);
     else if (elem_bytes == 4)
         pack_weight_kernel<uint32_t><<<grid_cap(total, 256), 256, 0, st>>>(
-            static_cast<const uint32_t*>(w), static_cast<uint32_t*>(wp), rows, cin, taps);
+            static_cast<const uint32_t*>(w), static_cast<uint32_t*>(wp), rows, cin, taps, cin_p);
     else
         return set_error(WIDEK_ERR_INVALID, "conv_pack_weight: element size %lld", (long long)elem_bytes);
     return check_launch("widek_conv_pack_weight");
 }
 
 size_t widek_conv_workspace(int64_t n, int64_t batch, int64_t cin, int64_t d, int64_t h, int64_t w, int dtype) {
-    return (size_t)(n * batch * cin * d * h * w) * widek::dtype_size(dtype);
+    const int64_t cin_s = (cin + 7) / 8 * 8;
+    return (size_t)(n * batch * cin_s * d * h * w) * widek::dtype_size(dtype);
+}
+
+int64_t widek_conv_packed_weight_elems(int64_t rows, int64_t cin, int64_t taps) {
+    if (rows < 0 || cin < 0 || taps < 0) return -1;
+    return rows * taps * ((cin + widek::BK - 1) / widek::BK * widek::BK);
 }
 
 int widek_conv_fwd_ex(const void* x, const void* w, const void* w_packed, const void* bias, const void* scale,

@@ -15,16 +15,17 @@ namespace {
 template <typename T, int BM, int BN, int BK, int TM, int TN>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     gemm_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
-                     T* __restrict__ y, int M, int K, int O, int act, int64_t w_ms, int64_t w_rs) {
+                     T* __restrict__ y, int M, int K, int O, int act, int64_t w_ms, int64_t w_rs, int64_t x_ms,
+                     int64_t x_bs, int x_rpb, int64_t y_ms, int64_t y_bs) {
     constexpr int NT = (BM / TM) * (BN / TN);
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
     const int model = blockIdx.z;
     const int m0 = blockIdx.y * BM;
     const int o0 = blockIdx.x * BN;
-    x += (int64_t)model * M * K;
+    x += (int64_t)model * x_ms;
     w += (int64_t)model * w_ms;
-    y += (int64_t)model * M * O;
+    y += (int64_t)model * y_ms;
     const int tid = threadIdx.x;
     const int tx = tid % (BN / TN);
     const int ty = tid / (BN / TN);
@@ -39,7 +40,8 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         for (int i = tid; i < BM * BK; i += NT) {
             const int r = i / BK, c = i % BK;
             const int gm = m0 + r, gk = k0 + c;
-            As[c][r] = (gm < M && gk < K) ? to_f<T>(x[(int64_t)gm * K + gk]) : 0.f;
+            As[c][r] = (gm < M && gk < K) ? to_f<T>(x[(int64_t)(gm / x_rpb) * x_bs + (int64_t)(gm % x_rpb) * K + gk])
+                                          : 0.f;
         }
         for (int i = tid; i < BN * BK; i += NT) {
             const int r = i / BK, c = i % BK;
@@ -71,7 +73,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
             if (go >= O) continue;
             float v = acc[i][j];
             if (bias) v += to_f<T>(bias[(int64_t)model * O + go]);
-            y[(int64_t)gm * O + go] = from_f<T>(apply_act(v, act));
+            y[(int64_t)(gm / x_rpb) * y_bs + (int64_t)(gm % x_rpb) * O + go] = from_f<T>(apply_act(v, act));
         }
     }
 }
@@ -83,6 +85,8 @@ struct SimtLaunch {
     int act;
     cudaStream_t st;
     int64_t w_ms, w_rs;     // weight model / row strides (elements)
+    int64_t x_ms = -1, x_bs = 0, x_rpb = 0;   // strided x (x_ms < 0: dense)
+    int64_t y_ms = -1, y_bs = 0;              // strided y (y_ms < 0: dense)
 
     template <typename T>
     int run() {
@@ -93,13 +97,23 @@ struct SimtLaunch {
         const T* wp = static_cast<const T*>(w);
         const T* bp = static_cast<const T*>(b);
         T* yp = static_cast<T*>(y);
+        const int64_t xms = x_ms < 0 ? m * k : x_ms;
+        const int64_t xbs = x_ms < 0 ? 0 : x_bs;
+        const int64_t xrpb = x_ms < 0 ? m : x_rpb;
+        // y rows use the same row blocks as x (dense x: one block of m rows)
+        const int64_t yms = y_ms < 0 ? m * o : y_ms;
+        const int64_t ybs = y_ms < 0 ? (xrpb == m ? 0 : xrpb * o) : y_bs;
+        if (xrpb <= 0 || xrpb > 0x7fffffff) return set_error(WIDEK_ERR_INVALID, "linear (simt): bad row block %lld",
+                                                             (long long)xrpb);
         if (m <= 32) {
             dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 31) / 32), (unsigned)n);
-            gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs);
+            gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
+                                                                    (int)xrpb, yms, ybs);
         } else {
             dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)n);
             if (grid.y > 65535) return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): m too large");
-            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs);
+            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
+                                                                    (int)xrpb, yms, ybs);
         }
         return check_launch("widek_linear_fwd_simt");
     }
@@ -108,9 +122,10 @@ struct SimtLaunch {
 }  // namespace
 
 int linear_simt_strided(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m, int64_t k,
-                        int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st) {
+                        int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st, int64_t x_ms,
+                        int64_t x_bs, int64_t x_rpb, int64_t y_ms, int64_t y_bs) {
     if (n == 0 || m == 0 || o == 0) return WIDEK_OK;
-    SimtLaunch L{x, w, bias, y, n, m, k, o, act, st, w_ms, w_rs};
+    SimtLaunch L{x, w, bias, y, n, m, k, o, act, st, w_ms, w_rs, x_ms, x_bs, x_rpb, y_ms, y_bs};
     return dispatch_dtype(dtype, L);
 }
 

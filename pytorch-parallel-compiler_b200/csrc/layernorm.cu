@@ -1,7 +1,10 @@
 // WideLayerNorm forward: one HBM pass, statistics in fp32.
 //
-// Layout: x, y are [n, rows_per_model, d] (N-first, rows contiguous); the
-// per-model affine w, b are [n, d]. Row r belongs to model r / rows_per_model.
+// Layout: x, y are [outer][n][inner][d] rows (contiguous); the per-model
+// affine w, b are [n, d]. Row r belongs to model (r / inner) % n. The
+// N-first layout [n, rows_per_model, d] is outer = 1, inner = rows_per_model;
+// the packed TracedWideModel boundary layout [B, n*T, d] is outer = B,
+// inner = T, so LayerNorm runs on either without a layout change.
 //
 // Fast path: one warp per row, the row held in registers as 16-byte vectors
 // (mean and the biased variance are two exact passes over registers, so the
@@ -15,7 +18,7 @@ namespace {
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) layernorm_warp_kernel(
     const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
-    T* __restrict__ y, int64_t rows, int64_t rows_per_model, int d, float eps) {
+    T* __restrict__ y, int64_t rows, int64_t inner, int64_t n, int d, float eps) {
     constexpr int VEC = 16 / sizeof(T);
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -48,7 +51,7 @@ __global__ void __launch_bounds__(256) layernorm_warp_kernel(
     }
     const float var = warp_sum(q) / (float)d;
     const float rstd = rsqrtf(var + eps);
-    const int64_t model = row / rows_per_model;
+    const int64_t model = (row / inner) % n;
     const T* wr = w + model * d;
     const T* br = b + model * d;
     T* yr = y + row * d;
@@ -70,7 +73,7 @@ __global__ void __launch_bounds__(256) layernorm_warp_kernel(
 template <typename T>
 __global__ void __launch_bounds__(256) layernorm_block_kernel(
     const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
-    T* __restrict__ y, int64_t rows_per_model, int d, float eps) {
+    T* __restrict__ y, int64_t inner, int64_t n, int d, float eps) {
     __shared__ float red[32];
     const int64_t row = blockIdx.x;
     const T* xr = x + row * d;
@@ -102,7 +105,7 @@ __global__ void __launch_bounds__(256) layernorm_block_kernel(
     }
     __syncthreads();
     const float rstd = rsqrtf(red[0] / (float)d + eps);
-    const int64_t model = row / rows_per_model;
+    const int64_t model = (row / inner) % n;
     const T* wr = w + model * d;
     const T* br = b + model * d;
     T* yr = y + row * d;
@@ -113,14 +116,14 @@ __global__ void __launch_bounds__(256) layernorm_block_kernel(
 struct LayerNormLaunch {
     const void *x, *w, *b;
     void* y;
-    int64_t n, rpm, d;
+    int64_t n, outer, inner, d;
     float eps;
     cudaStream_t st;
 
     template <typename T>
     int run() {
         constexpr int VEC = 16 / sizeof(T);
-        const int64_t rows = n * rpm;
+        const int64_t rows = outer * n * inner;
         if (rows == 0 || d == 0) return WIDEK_OK;
         const bool vec_ok = (d % VEC == 0) && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
         const int64_t per_lane = (d / VEC + 31) / 32;
@@ -134,16 +137,16 @@ struct LayerNormLaunch {
             if (blocks > 0x7fffffff) return set_error(WIDEK_ERR_INVALID, "layernorm: too many rows");
             dim3 grid((unsigned)blocks), block(32 * warps);
             if (per_lane <= 1)
-                layernorm_warp_kernel<T, 1><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, rpm, (int)d, eps);
+                layernorm_warp_kernel<T, 1><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, inner, n, (int)d, eps);
             else if (per_lane <= 2)
-                layernorm_warp_kernel<T, 2><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, rpm, (int)d, eps);
+                layernorm_warp_kernel<T, 2><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, inner, n, (int)d, eps);
             else if (per_lane <= 4)
-                layernorm_warp_kernel<T, 4><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, rpm, (int)d, eps);
+                layernorm_warp_kernel<T, 4><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, inner, n, (int)d, eps);
             else
-                layernorm_warp_kernel<T, 8><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, rpm, (int)d, eps);
+                layernorm_warp_kernel<T, 8><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, inner, n, (int)d, eps);
         } else {
             if (rows > 0x7fffffff) return set_error(WIDEK_ERR_INVALID, "layernorm: too many rows");
-            layernorm_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, wp, bp, yp, rpm, (int)d, eps);
+            layernorm_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, wp, bp, yp, inner, n, (int)d, eps);
         }
         return check_launch("widek_layernorm_fwd");
     }
@@ -152,15 +155,21 @@ struct LayerNormLaunch {
 }  // namespace
 }  // namespace widek
 
+extern "C" int widek_layernorm_fwd_ex(const void* x, const void* w, const void* b, void* y, int64_t n,
+                                      int64_t outer, int64_t inner, int64_t d, double eps, int dtype,
+                                      void* stream) {
+    using namespace widek;
+    if (n < 0 || outer < 0 || inner < 0 || d < 0 || d > (1 << 30))
+        return set_error(WIDEK_ERR_INVALID, "layernorm: bad sizes n=%lld outer=%lld inner=%lld d=%lld",
+                         (long long)n, (long long)outer, (long long)inner, (long long)d);
+    if (n * outer * inner * d > 0 && (!x || !w || !b || !y))
+        return set_error(WIDEK_ERR_INVALID, "layernorm: null pointer");
+    LayerNormLaunch L{x, w, b, y, n, outer, inner, d, (float)eps, (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
 extern "C" int widek_layernorm_fwd(const void* x, const void* w, const void* b, void* y,
                                    int64_t n, int64_t rows_per_model, int64_t d,
                                    double eps, int dtype, void* stream) {
-    using namespace widek;
-    if (n < 0 || rows_per_model < 0 || d < 0 || d > (1 << 30))
-        return set_error(WIDEK_ERR_INVALID, "layernorm: bad sizes n=%lld rows=%lld d=%lld",
-                         (long long)n, (long long)rows_per_model, (long long)d);
-    if (n * rows_per_model * d > 0 && (!x || !w || !b || !y))
-        return set_error(WIDEK_ERR_INVALID, "layernorm: null pointer");
-    LayerNormLaunch L{x, w, b, y, n, rows_per_model, d, (float)eps, (cudaStream_t)stream};
-    return dispatch_dtype(dtype, L);
+    return widek_layernorm_fwd_ex(x, w, b, y, n, 1, rows_per_model, d, eps, dtype, stream);
 }

@@ -48,12 +48,14 @@ struct RnnArgs {
     const void* b_hh;    // [n, G*H] or null
     const void* h0;      // [n, batch, H] or null
     const void* c0;      // [n, batch, H] or null (LSTM)
-    void* out;           // [n, batch, T, H]
+    void* out;           // [n, batch, T, H] (or packed, see out_ms / out_bs)
     void* hn;            // [n, batch, H]
     void* cn;            // [n, batch, H] or null (LSTM)
     int batch, T, H, G, cl, w_in_smem;
     int kparts;          // threads sharing one row's dot products (split k, vec4 path)
     int64_t whh_ms, whh_rs;   // W_hh model / row strides (elements)
+    int64_t out_ms, out_bs;   // out model / batch strides (elements): N-first [n, batch, T, H] is
+                              // (batch*T*H, T*H), the packed [batch, n*T, H] layout (T*H, n*T*H)
 };
 
 template <typename T, bool LSTM>
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
     const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * a.whh_ms;
     const int64_t wrs = a.whh_rs;
     const T* bh = a.b_hh ? static_cast<const T*>(a.b_hh) + (size_t)model * G * H : nullptr;
-    T* out = static_cast<T*>(a.out) + (size_t)model * B * a.T * H;
+    T* out = static_cast<T*>(a.out) + (size_t)model * a.out_ms;
 
     // global row of local row lr = g * U + j
     auto grow = [&](int lr) { return (lr / U) * H + q * U + (lr % U); };
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
             // value the reference would hold in a tensor of that dtype.
             const T hs = from_f<T>(hnew);
             const float hv = to_f<T>(hs);
-            out[((size_t)b * a.T + t) * H + ju] = hs;
+            out[(size_t)b * a.out_bs + (size_t)t * H + ju] = hs;
             // 3. publish into every cluster CTA's next buffer (DSMEM)
             for (int r = 0; r < a.cl; ++r) {
                 float* dst = cluster.map_shared_rank(hn_local, r);
@@ -305,7 +307,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
     const T* gx = static_cast<const T*>(a.gx) + (size_t)model * B * a.T * G * H;
     const T* w = static_cast<const T*>(a.w_hh) + (size_t)model * a.whh_ms;
     const T* bh = a.b_hh ? static_cast<const T*>(a.b_hh) + (size_t)model * G * H : nullptr;
-    T* out = static_cast<T*>(a.out) + (size_t)model * B * a.T * H;
+    T* out = static_cast<T*>(a.out) + (size_t)model * a.out_ms;
     auto grow = [&](int lr) { return (lr / U) * H + q * U + (lr % U); };
 
     const int tid = threadIdx.x, grp = tid / kRegParts, p = tid % kRegParts;
@@ -487,7 +489,7 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
                 }
                 const T hs = from_f<T>(hnew);
                 hval = to_f<T>(hs);
-                out[((size_t)b * a.T + t) * H + ju] = hs;
+                out[(size_t)b * a.out_bs + (size_t)t * H + ju] = hs;
             }
             const int g0 = lane & ~3;
             const float v0 = __shfl_sync(0xffffffffu, hval, g0), v1 = __shfl_sync(0xffffffffu, hval, g0 + 1),
@@ -686,7 +688,7 @@ int rnn_entry(bool lstm, const void* gates_x, const void* w_hh, const void* b_hh
         return set_error(WIDEK_ERR_INVALID, "rnn: null pointer");
     const int g = lstm ? 4 : 3;
     RnnArgs a{gates_x, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps, (int)hidden, g, 1, 1, 1,
-              (int64_t)g * hidden * hidden, hidden};
+              (int64_t)g * hidden * hidden, hidden, batch * steps * hidden, steps * hidden};
     RnnLaunch L{a, n, lstm, (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
 }
@@ -696,9 +698,12 @@ int rnn_entry(bool lstm, const void* gates_x, const void* w_hh, const void* b_hh
 int rnn_fwd_entry(bool lstm, const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
                   const void* h0, const void* c0, void* out, void* h_n, void* c_n, const int64_t* wstrides,
                   void* workspace, size_t ws_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input,
-                  int64_t hidden, int dtype, void* stream) {
+                  int64_t hidden, int in_layout, int out_layout, int dtype, void* stream) {
     if (n < 0 || batch < 0 || steps < 0 || hidden < 0 || input < 0)
         return set_error(WIDEK_ERR_INVALID, "rnn: negative size");
+    if ((in_layout != WIDEK_LAYOUT_NFIRST && in_layout != WIDEK_LAYOUT_PACKED) ||
+        (out_layout != WIDEK_LAYOUT_NFIRST && out_layout != WIDEK_LAYOUT_PACKED))
+        return set_error(WIDEK_ERR_INVALID, "rnn: layouts must be N-first or packed");
     if (batch > 1024 || hidden > 4096 || steps > 0x7fffffff || n > 65535)
         return set_error(WIDEK_ERR_UNSUPPORTED, "rnn: batch=%lld hidden=%lld outside the supported range",
                          (long long)batch, (long long)hidden);
@@ -716,12 +721,19 @@ int rnn_fwd_entry(bool lstm, const void* x, const void* w_ih, const void* w_hh, 
     if (steps > 0 && (!workspace || ws_bytes < need))
         return set_error(WIDEK_ERR_INVALID, "rnn: workspace of %zu bytes needed, %zu given", need, ws_bytes);
     if (steps > 0) {
+        // x rows (b, t) of model i: N-first at i*batch*T*I + (b*T + t)*I,
+        // packed [batch, n*T, I] at (b*n + i)*T*I + t*I
+        const bool pin = in_layout == WIDEK_LAYOUT_PACKED;
         const int rc = linear_simt_strided(x, w_ih, b_ih, workspace, n, batch * steps, input, g * hidden, ims, irs,
-                                           dtype, WIDEK_ACT_NONE, (cudaStream_t)stream);
+                                           dtype, WIDEK_ACT_NONE, (cudaStream_t)stream,
+                                           pin ? steps * input : batch * steps * input,
+                                           pin ? n * steps * input : steps * input, steps);
         if (rc) return rc;
     }
+    const bool pout = out_layout == WIDEK_LAYOUT_PACKED;
     RnnArgs a{steps > 0 ? workspace : nullptr, w_hh, b_hh, h0, c0, out, h_n, c_n, (int)batch, (int)steps,
-              (int)hidden, g, 1, 1, 1, hms, hrs};
+              (int)hidden, g, 1, 1, 1, hms, hrs, pout ? steps * hidden : batch * steps * hidden,
+              pout ? n * steps * hidden : steps * hidden};
     RnnLaunch L{a, n, lstm, (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
 }
@@ -756,20 +768,38 @@ size_t widek_rnn_workspace(int lstm, int64_t n, int64_t batch, int64_t steps, in
     return (size_t)(n * batch * steps * (lstm ? 4 : 3) * hidden) * widek::dtype_size(dtype);
 }
 
+int widek_gru_fwd_ex(const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
+                     const void* h0, void* out, void* h_n, const int64_t* w_strides, void* workspace,
+                     size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input, int64_t hidden,
+                     int in_layout, int out_layout, int dtype, void* stream) {
+    return widek::rnn_fwd_entry(false, x, w_ih, w_hh, b_ih, b_hh, h0, nullptr, out, h_n, nullptr, w_strides,
+                                workspace, workspace_bytes, n, batch, steps, input, hidden, in_layout, out_layout,
+                                dtype, stream);
+}
+
+int widek_lstm_fwd_ex(const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
+                      const void* h0, const void* c0, void* out, void* h_n, void* c_n, const int64_t* w_strides,
+                      void* workspace, size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps,
+                      int64_t input, int64_t hidden, int in_layout, int out_layout, int dtype, void* stream) {
+    return widek::rnn_fwd_entry(true, x, w_ih, w_hh, b_ih, b_hh, h0, c0, out, h_n, c_n, w_strides, workspace,
+                                workspace_bytes, n, batch, steps, input, hidden, in_layout, out_layout, dtype,
+                                stream);
+}
+
 int widek_gru_fwd(const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
                   const void* h0, void* out, void* h_n, const int64_t* w_strides, void* workspace,
                   size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input, int64_t hidden,
                   int dtype, void* stream) {
-    return widek::rnn_fwd_entry(false, x, w_ih, w_hh, b_ih, b_hh, h0, nullptr, out, h_n, nullptr, w_strides,
-                                workspace, workspace_bytes, n, batch, steps, input, hidden, dtype, stream);
+    return widek_gru_fwd_ex(x, w_ih, w_hh, b_ih, b_hh, h0, out, h_n, w_strides, workspace, workspace_bytes, n, batch,
+                            steps, input, hidden, WIDEK_LAYOUT_NFIRST, WIDEK_LAYOUT_NFIRST, dtype, stream);
 }
 
 int widek_lstm_fwd(const void* x, const void* w_ih, const void* w_hh, const void* b_ih, const void* b_hh,
                    const void* h0, const void* c0, void* out, void* h_n, void* c_n, const int64_t* w_strides,
                    void* workspace, size_t workspace_bytes, int64_t n, int64_t batch, int64_t steps, int64_t input,
                    int64_t hidden, int dtype, void* stream) {
-    return widek::rnn_fwd_entry(true, x, w_ih, w_hh, b_ih, b_hh, h0, c0, out, h_n, c_n, w_strides, workspace,
-                                workspace_bytes, n, batch, steps, input, hidden, dtype, stream);
+    return widek_lstm_fwd_ex(x, w_ih, w_hh, b_ih, b_hh, h0, c0, out, h_n, c_n, w_strides, workspace, workspace_bytes,
+                             n, batch, steps, input, hidden, WIDEK_LAYOUT_NFIRST, WIDEK_LAYOUT_NFIRST, dtype, stream);
 }
 
 }  // extern "C"

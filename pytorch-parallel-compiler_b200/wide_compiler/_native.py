@@ -49,6 +49,7 @@ SIGNATURES = {
     "widek_device_error": [ctypes.POINTER(ctypes.c_int)],
     "widek_test_bounded_wait": [ctypes.c_uint64, _c_void_p],
     "widek_linear_fwd": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
+    "widek_linear_fwd_ex": [_c_void_p] * 4 + [_i64] * 5 + [_int] * 4 + [_c_void_p],
     "widek_linear_fwd_simt": [_c_void_p] * 4 + [_i64] * 4 + [_int, _int, _c_void_p],
     "widek_linear_set_variant": [_int],
     "widek_attention_set_variant": [_int],
@@ -56,6 +57,7 @@ SIGNATURES = {
     "widek_rnn_set_variant": [_int],
     "widek_launch_count": [],
     "widek_layernorm_fwd": [_c_void_p] * 4 + [_i64] * 3 + [_dbl, _int, _c_void_p],
+    "widek_layernorm_fwd_ex": [_c_void_p] * 4 + [_i64] * 4 + [_dbl, _int, _c_void_p],
     "widek_swap01": [_c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p],
     "widek_pack": [ctypes.POINTER(_c_void_p), _i64, _c_void_p, _i64, _i64, _c_void_p],
     "widek_copy2d": [_c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p],
@@ -73,9 +75,14 @@ SIGNATURES = {
                      + [_int, _c_void_p],
     "widek_lstm_fwd": [_c_void_p] * 10 + [ctypes.POINTER(_i64), _c_void_p, ctypes.c_size_t] + [_i64] * 5
                       + [_int, _c_void_p],
+    "widek_gru_fwd_ex": [_c_void_p] * 8 + [ctypes.POINTER(_i64), _c_void_p, ctypes.c_size_t] + [_i64] * 5
+                        + [_int] * 3 + [_c_void_p],
+    "widek_lstm_fwd_ex": [_c_void_p] * 10 + [ctypes.POINTER(_i64), _c_void_p, ctypes.c_size_t] + [_i64] * 5
+                         + [_int] * 3 + [_c_void_p],
     "widek_rnn_workspace": [_int] + [_i64] * 4 + [_int],
     "widek_conv_pack_weight": [_c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p],
     "widek_conv_workspace": [_i64] * 6 + [_int],
+    "widek_conv_packed_weight_elems": [_i64] * 3,
     "widek_conv_fwd": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64), _int, _int, _int, _c_void_p],
     "widek_conv_fwd_ex": [_c_void_p] * 9 + [ctypes.c_size_t, ctypes.POINTER(_i64)] + [_int] * 6 + [_c_void_p],
     "widek_conv_layouts_supported": [ctypes.POINTER(_i64)] + [_int] * 5,
@@ -88,7 +95,7 @@ SIGNATURES = {
                                                           _int, _c_void_p],
 }
 RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t, "widek_conv_workspace": ctypes.c_size_t,
-            "widek_rnn_workspace": ctypes.c_size_t,
+            "widek_rnn_workspace": ctypes.c_size_t, "widek_conv_packed_weight_elems": _i64,
             "widek_launch_count": ctypes.c_longlong}
 
 

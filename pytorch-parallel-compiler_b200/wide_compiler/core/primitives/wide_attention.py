@@ -96,6 +96,21 @@ class WideAttention(nn.Module):
         out = ops.attention(self, query, key, value, attn_mask, is_causal)
         return (out, None) if mha_mode else out
 
+    def forward_packed(self, query: Tensor, key=None, value=None, attn_mask=None, is_causal: bool = False,
+                       need_weights: bool = False):
+        """Self-attention on the packed boundary layout [B, N*T, D]: the fused
+        QKV projection reads the packed rows in place and the output
+        projection writes them packed (used by TracedWideModel); other forms
+        (cross-attention, masks) decline."""
+        mha_mode = key is not None
+        if (key is not None and key is not query) or (value is not None and value is not query) \
+                or attn_mask is not None or (self.training and self.dropout > 0.0):
+            return None
+        if query.dim() != 3 or query.shape[1] % self.n != 0 or query.shape[2] != self.d_model:
+            return None
+        out = ops.attention_packed(self, query, is_causal)
+        return (out, None) if mha_mode else out
+
     @classmethod
     def from_modules(cls, modules: List[nn.MultiheadAttention],
                      strategy: Union[str, AttentionStrategy] = 'auto') -> 'WideAttention':

@@ -27,6 +27,13 @@ class WideBatchNorm1d(nn.Module):
             raise ValueError(f"WideBatchNorm1d expects [N, B, C] or [N, B, C, L], got {tuple(x.shape)}")
         return wide_batchnorm_forward(x, self.op, self.n, self.num_features)
 
+    def forward_packed(self, x: Tensor):
+        """The same BatchNorm on the packed boundary layout [B, N*C] or
+        [B, N*C, L], run as one model of N*C channels (see WideBatchNorm2d)."""
+        if x.dim() not in (2, 3):
+            return None
+        return wide_batchnorm_forward(x.unsqueeze(0), self.op, 1, self.n * self.num_features).squeeze(0)
+
     @classmethod
     def from_modules(cls, modules: List[nn.BatchNorm1d]) -> 'WideBatchNorm1d':
         return _bn_from_modules(cls, modules)

@@ -29,6 +29,15 @@ class WideBatchNorm2d(nn.Module):
             raise ValueError(f"WideBatchNorm2d expects [N, B, C, H, W], got {tuple(x.shape)}")
         return wide_batchnorm_forward(x, self.op, self.n, self.num_features)
 
+    def forward_packed(self, x: Tensor):
+        """The same BatchNorm on the packed boundary layout [B, N*C, H, W]:
+        there the (model, channel) pairs are the N*C channels of one
+        BatchNorm2d (same parameter order), so it runs as one model of N*C
+        channels, result in that layout (used by TracedWideModel)."""
+        if x.dim() != 4:
+            return None
+        return wide_batchnorm_forward(x.unsqueeze(0), self.op, 1, self.n * self.num_features).squeeze(0)
+
     @classmethod
     def from_modules(cls, modules: List[nn.BatchNorm2d]) -> 'WideBatchNorm2d':
         return _bn_from_modules(cls, modules)

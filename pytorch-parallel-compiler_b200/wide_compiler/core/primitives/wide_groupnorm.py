@@ -59,6 +59,16 @@ class WideGroupNorm(nn.Module):
         w, b = self._affine()
         return ops.groupnorm(x, self.n, self.num_groups, w, b, self.eps)
 
+    def forward_packed(self, x: Tensor):
+        """The same GroupNorm on the packed boundary layout [B, N*C, *S]: each
+        (model, group) is a run of C/G consecutive channels there, so it is
+        one GroupNorm of N*G groups over N*C channels, result in that layout
+        (used by TracedWideModel)."""
+        if x.dim() < 2:
+            return None
+        w, b = self._affine()
+        return ops.groupnorm(x.unsqueeze(0), 1, self.n * self.num_groups, w, b, self.eps).squeeze(0)
+
     @classmethod
     def from_modules(cls, modules: List[nn.GroupNorm],
                      strategy: Union[str, GroupNormStrategy] = 'auto') -> 'WideGroupNorm':

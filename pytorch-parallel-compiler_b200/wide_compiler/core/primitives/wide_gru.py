@@ -71,6 +71,14 @@ class WideGRU(nn.Module):
     def forward(self, x: Tensor, h_0: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
         return ops.gru(x, h_0, self.weight_ih, self.weight_hh, self.bias_ih, self.bias_hh)
 
+    def forward_packed(self, x: Tensor, h_0=None):
+        """The same GRU on the packed boundary layout [B, N*T, I]: the kernels
+        read the packed input and write the packed output [B, N*T, H] in
+        place; h_n stays [N, B, H] (used by TracedWideModel)."""
+        if h_0 is not None or x.dim() != 3:
+            return None
+        return ops.gru_packed(x, self.weight_ih, self.weight_hh, self.bias_ih, self.bias_hh)
+
     @classmethod
     def from_modules(cls, modules: List[nn.GRU], strategy: Union[str, GRUStrategy] = 'auto') -> 'WideGRU':
         t = modules[0]

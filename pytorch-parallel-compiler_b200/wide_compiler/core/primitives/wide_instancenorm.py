@@ -66,17 +66,28 @@ class _WideInstanceNorm(nn.Module):
         if x.dim() != 3 + self._spatial_dims:
             raise ValueError(f"{type(self).__name__} expects {3 + self._spatial_dims}-D N-first input, "
                              f"got {tuple(x.shape)}")
+        return self._run(x, self.n, self.num_features)
+
+    def forward_packed(self, x: Tensor):
+        """The same InstanceNorm on the packed boundary layout [B, N*C, *S]
+        (one model of N*C channels there: the parameters and statistics are
+        per (model, channel) either way), result in that layout (used by
+        TracedWideModel)."""
+        if x.dim() != 2 + self._spatial_dims:
+            return None
+        return self._run(x.unsqueeze(0), 1, self.n * self.num_features).squeeze(0)
+
+    def _run(self, x: Tensor, n: int, c: int) -> Tensor:
         w, b = (self._cat('weight'), self._cat('bias')) if self.affine else (None, None)
         if self.track_running_stats and not self.training:
-            return ops.batchnorm(x, self.n, self.num_features, w, b, self._cat('running_mean'),
-                                 self._cat('running_var'), use_batch_stats=False, update_running=False,
-                                 momentum=0.0, eps=self.eps)
+            return ops.batchnorm(x, n, c, w, b, self._cat('running_mean'), self._cat('running_var'),
+                                 use_batch_stats=False, update_running=False, momentum=0.0, eps=self.eps)
         if self.track_running_stats and self.training:
             if not self._use_fused:
                 raise NotImplementedError("running-stat update for the sequential InstanceNorm layout")
-            return ops.instancenorm_train(x, self.n, self.num_features, w, b, self.norm.running_mean,
-                                          self.norm.running_var, self.momentum, self.eps)
-        return ops.groupnorm(x, self.n, self.num_features, w, b, self.eps)
+            return ops.instancenorm_train(x, n, c, w, b, self.norm.running_mean, self.norm.running_var,
+                                          self.momentum, self.eps)
+        return ops.groupnorm(x, n, c, w, b, self.eps)
 
     @classmethod
     def from_modules(cls, modules, strategy: Union[str, InstanceNormStrategy] = 'auto'):

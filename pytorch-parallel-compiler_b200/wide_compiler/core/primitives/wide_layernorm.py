@@ -29,6 +29,11 @@ class WideLayerNorm(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         return ops.layernorm(x, self.weight, self.bias, self.n, self.normalized_shape, self.eps)
 
+    def forward_packed(self, x: Tensor) -> Tensor:
+        """The same LayerNorm on the packed boundary layout [B, N*T, ..., D]
+        (or [B, N*D]), result in that layout (used by TracedWideModel)."""
+        return ops.layernorm_packed(x, self.weight, self.bias, self.n, self.normalized_shape, self.eps)
+
     @classmethod
     def from_modules(cls, modules: List[nn.LayerNorm]) -> 'WideLayerNorm':
         t = modules[0]

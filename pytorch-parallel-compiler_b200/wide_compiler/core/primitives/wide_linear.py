@@ -83,6 +83,20 @@ class WideLinear(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         return ops.linear(x, self.weight, self.bias)
 
+    def forward_packed(self, x: Tensor):
+        """The same Linear on the packed boundary layout [B, N*T, K] (or
+        [B, N*K]): the kernel reads and writes the packed rows in place,
+        result [B, N*T, O] (or [B, N*O]); used by TracedWideModel."""
+        if x.dim() == 2:
+            if x.shape[1] != self.n * self.in_features:
+                return None
+            y = ops.linear_layout(x.view(x.shape[0], self.n, self.in_features), self.weight, self.bias,
+                                  ops.ACT_NONE, True, True)
+            return y.view(x.shape[0], self.n * self.out_features)
+        if x.dim() != 3 or x.shape[1] % self.n != 0:
+            return None
+        return ops.linear_layout(x, self.weight, self.bias, ops.ACT_NONE, True, True)
+
     @classmethod
     def from_modules(cls, modules: List[nn.Linear], strategy: Union[str, LinearStrategy] = 'auto') -> 'WideLinear':
         t = modules[0]

@@ -110,6 +110,16 @@ class WideLSTM(nn.Module):
         wih, whh = self._blocks()
         return ops.lstm(x, h0, c0, wih, whh, bih, bhh)
 
+    def forward_packed(self, x: Tensor, hx=None):
+        """The same LSTM on the packed boundary layout [B, N*T, I] (packed
+        output [B, N*T, H]; h_n, c_n stay [N, B, H]), used by TracedWideModel."""
+        if hx is not None or x.dim() != 3:
+            return None
+        n, h = self.n, self.hidden_size
+        bih = self.bias_ih.view(n, 4 * h) if self.bias else None
+        bhh = self.bias_hh.view(n, 4 * h) if self.bias else None
+        return ops.lstm_blockdiag_packed(x, self.weight_ih, self.weight_hh, bih, bhh, n, h)
+
     @classmethod
     def from_modules(cls, modules: List[nn.LSTM], strategy: Union[str, LSTMStrategy] = 'auto') -> 'WideLSTM':
         t = modules[0]

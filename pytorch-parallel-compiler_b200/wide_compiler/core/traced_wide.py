@@ -134,6 +134,13 @@ class FunctionalOp(nn.Module):
             return ops.unary(args[0], self.unary)
         return self.fn(*args, **kwargs)
 
+    def forward_packed(self, *args, **kwargs):
+        """Elementwise activations give the same values in any layout, so they
+        run on the packed boundary layout as is; other functions decline."""
+        if self.unary is not None and len(args) == 1 and _kernel_tensor(args[0]) and self._plain(kwargs):
+            return ops.unary(args[0], self.unary)
+        return None
+
     def _plain(self, kwargs) -> bool:
         if not kwargs:
             return True
@@ -169,6 +176,18 @@ class BinaryOp(nn.Module):
                 and a.dtype == b.dtype and a.device == b.device):
             return ops.binary(a, b, self.op)
         return _BINARY_TORCH[self.op](a, b)
+
+    def forward_packed(self, a, b):
+        """On the packed boundary layout: two packed operands of one shape
+        (elementwise, so layout-independent), or a packed operand and a Python
+        number; anything that broadcasts declines."""
+        if self.op == 'matmul':
+            return None
+        if isinstance(a, Tensor) and isinstance(b, Tensor):
+            return self.forward(a, b) if a.shape == b.shape else None
+        if isinstance(a, (int, float)) or isinstance(b, (int, float)):
+            return _BINARY_TORCH[self.op](a, b)
+        return None
 
     def __repr__(self):
         return f"BinaryOp({self.op})"
@@ -255,6 +274,10 @@ class _Laid:
 
     def __init__(self, t: Tensor, layout: int):
         self.t, self.layout, self.std = t, layout, None
+
+
+class _Decline:
+    """Marker: an argument that rules out the packed-layout call."""
 
 
 class TracedWideModel(nn.Module):
@@ -730,8 +753,42 @@ class TracedWideModel(nn.Module):
             v.std = self._unpack(v.t)
         return v.std
 
+    def _packed_call(self, op: nn.Module, name: str, values: Dict[str, Any]) -> Any:
+        """Runs a stage on the packed boundary layout when every tensor it
+        reads is a packed value and the stage offers ``forward_packed``
+        (norms, elementwise glue, recurrent and attention layers): the result
+        stays packed, so neither the unpack before it nor, at the graph's end,
+        the pack after it is needed. None when the stage declines."""
+        fp = getattr(op, 'forward_packed', None)
+        if fp is None:
+            return None
+        from ..ops import LAYOUT_PACKED
+
+        def resolve(a):
+            v = values[a] if isinstance(a, str) and a in values else a
+            if isinstance(v, _Laid):
+                return v.t if v.layout == LAYOUT_PACKED else _Decline
+            if isinstance(v, (Tensor, tuple, list, dict)):
+                return _Decline
+            return v
+        args = [resolve(a) for a in self._node_args[name]]
+        kwargs = {k: resolve(v) for k, v in self._node_kwargs.get(name, {}).items()}
+        if any(a is _Decline for a in args) or any(v is _Decline for v in kwargs.values()):
+            return None
+        if not any(isinstance(a, Tensor) for a in args):
+            return None
+        out = fp(*args, **kwargs)
+        if out is None:
+            return None
+        if isinstance(out, tuple):
+            return (_Laid(out[0], LAYOUT_PACKED),) + tuple(out[1:])
+        return _Laid(out, LAYOUT_PACKED)
+
     def _run_node(self, name: str, values: Dict[str, Any]) -> Any:
         op = self.stages[name.replace('.', '_')]
+        packed = self._packed_call(op, name, values)
+        if packed is not None:
+            return packed
         args = [self._std(values[a]) if isinstance(a, str) and a in values else a for a in self._node_args[name]]
         kwargs = {k: (self._std(values[v]) if isinstance(v, str) and v in values else v)
                   for k, v in self._node_kwargs.get(name, {}).items()}

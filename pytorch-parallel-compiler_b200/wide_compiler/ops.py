@@ -82,6 +82,33 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
     return y
 
 
+def linear_layout(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int, in_packed: bool,
+                  out_packed: bool) -> Tensor:
+    """WideLinear with the packed boundary layout on either side: x is
+    [B, N*T, K] when ``in_packed`` (else N-first [N, B, T, K]), the result
+    [B, N*T, O] when ``out_packed`` (else [N, B, T, O]). The kernels read and
+    write the packed rows in place (widek_linear_fwd_ex); equal to unpacking,
+    ``linear`` and packing (traced_wide.py:463-469, :527-532)."""
+    dev = N.require_cuda(x, weight, bias, what="WideLinear")
+    _same_dtype("WideLinear", weight, x, bias)
+    n, o, k = weight.shape
+    if x.dim() != (3 if in_packed else 4) or x.shape[-1] != k or (in_packed and x.shape[1] % n != 0) \
+            or (not in_packed and x.shape[0] != n):
+        raise ValueError(f"WideLinear: input {tuple(x.shape)} does not match weight {tuple(weight.shape)} "
+                         f"({'packed' if in_packed else 'N-first'})")
+    b, t = (x.shape[0], x.shape[1] // n) if in_packed else (x.shape[1], x.shape[2])
+    y = torch.empty((b, n * t, o) if out_packed else (n, b, t, o), device=dev, dtype=weight.dtype)
+    xd, wd = _dense(x), _dense(weight)
+    bd = _dense(bias) if bias is not None else None
+    with _guard(dev):
+        rc = N.lib().widek_linear_fwd_ex(xd.data_ptr(), wd.data_ptr(), N.ptr(bd), y.data_ptr(), n, b * t, k, o, t,
+                                         LAYOUT_PACKED if in_packed else LAYOUT_NFIRST,
+                                         LAYOUT_PACKED if out_packed else LAYOUT_NFIRST, N.dtype_code(weight), act,
+                                         N.stream_ptr(dev))
+    N.check(rc, "widek_linear_fwd_ex")
+    return y
+
+
 _CHAIN_MEMO: dict = {}
 
 
@@ -177,6 +204,31 @@ def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: floa
                                          y.data_ptr(), n, rows, d, float(eps), N.dtype_code(x),
                                          N.stream_ptr(dev))
     N.check(rc, "widek_layernorm_fwd")
+    return y
+
+
+def layernorm_packed(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: float) -> Tensor:
+    """LayerNorm of N models on the packed boundary layout: x [B, N*T, ..., D]
+    (or [B, N*D]) -> same layout, model i's affine applied to its rows
+    (widek_layernorm_fwd_ex, outer = B). Equals packing the LayerNorm of the
+    unpacked N-first tensor (traced_wide.py:463-469, :527-532)."""
+    dev = N.require_cuda(x, weight, bias, what="WideLayerNorm")
+    _same_dtype("WideLayerNorm", x, weight, bias)
+    if x.dim() == 2:
+        ok = x.shape[1] == n * d
+    else:
+        ok = x.dim() > 2 and x.shape[-1] == d and x.shape[1] % n == 0
+    if not ok:
+        raise ValueError(f"WideLayerNorm: packed input {tuple(x.shape)} does not hold N={n} models of D={d}")
+    xd = _dense(x)
+    outer = xd.shape[0]
+    inner = xd.numel() // (outer * n * d) if outer * n * d > 0 else 0
+    y = torch.empty_like(xd)
+    with _guard(dev):
+        rc = N.lib().widek_layernorm_fwd_ex(xd.data_ptr(), _dense(weight).data_ptr(), _dense(bias).data_ptr(),
+                                            y.data_ptr(), n, outer, inner, d, float(eps), N.dtype_code(x),
+                                            N.stream_ptr(dev))
+    N.check(rc, "widek_layernorm_fwd_ex")
     return y
 
 
@@ -390,13 +442,20 @@ def _rnn_check(x: Tensor, w_ih: Tensor, w_hh: Tensor, gates: int, what: str):
     return n, batch, steps, hidden
 
 
-def _rnn_fwd(lstm: bool, x: Tensor, h0, c0, w_ih: Tensor, w_hh: Tensor, b_ih, b_hh, strides, n: int, hidden: int):
+def _rnn_fwd(lstm: bool, x: Tensor, h0, c0, w_ih: Tensor, w_hh: Tensor, b_ih, b_hh, strides, n: int, hidden: int,
+             packed: bool = False):
     """One library call for the whole forward: the input projection (reading
     W_ih by (model, row) strides, into a workspace) and the recurrence
-    (W_hh by strides)."""
+    (W_hh by strides). With ``packed`` x is the boundary layout
+    [B, N*T, I] and out is written as [B, N*T, H]."""
     dev = x.device
-    _, batch, steps, inp = x.shape
-    out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
+    if packed:
+        batch, steps, inp = x.shape[0], x.shape[1] // n, x.shape[2]
+        out = torch.empty(batch, n * steps, hidden, device=dev, dtype=x.dtype)
+    else:
+        _, batch, steps, inp = x.shape
+        out = torch.empty(n, batch, steps, hidden, device=dev, dtype=x.dtype)
+    lay = LAYOUT_PACKED if packed else LAYOUT_NFIRST
     hn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype)
     cn = torch.empty(n, batch, hidden, device=dev, dtype=x.dtype) if lstm else None
     code = N.dtype_code(x)
@@ -406,16 +465,58 @@ def _rnn_fwd(lstm: bool, x: Tensor, h0, c0, w_ih: Tensor, w_hh: Tensor, b_ih, b_
     xd = _dense(x)
     with _guard(dev):
         if lstm:
-            rc = N.lib().widek_lstm_fwd(xd.data_ptr(), w_ih.data_ptr(), w_hh.data_ptr(), N.ptr(b_ih), N.ptr(b_hh),
-                                        N.ptr(h0), N.ptr(c0), out.data_ptr(), hn.data_ptr(), cn.data_ptr(),
-                                        c_strides, ws.data_ptr(), ws.numel(), n, batch, steps, inp, hidden, code,
-                                        N.stream_ptr(dev))
+            rc = N.lib().widek_lstm_fwd_ex(xd.data_ptr(), w_ih.data_ptr(), w_hh.data_ptr(), N.ptr(b_ih),
+                                           N.ptr(b_hh), N.ptr(h0), N.ptr(c0), out.data_ptr(), hn.data_ptr(),
+                                           cn.data_ptr(), c_strides, ws.data_ptr(), ws.numel(), n, batch, steps, inp,
+                                           hidden, lay, lay, code, N.stream_ptr(dev))
         else:
-            rc = N.lib().widek_gru_fwd(xd.data_ptr(), w_ih.data_ptr(), w_hh.data_ptr(), N.ptr(b_ih), N.ptr(b_hh),
-                                       N.ptr(h0), out.data_ptr(), hn.data_ptr(), c_strides, ws.data_ptr(), ws.numel(),
-                                       n, batch, steps, inp, hidden, code, N.stream_ptr(dev))
-    N.check(rc, "widek_lstm_fwd" if lstm else "widek_gru_fwd")
+            rc = N.lib().widek_gru_fwd_ex(xd.data_ptr(), w_ih.data_ptr(), w_hh.data_ptr(), N.ptr(b_ih), N.ptr(b_hh),
+                                          N.ptr(h0), out.data_ptr(), hn.data_ptr(), c_strides, ws.data_ptr(),
+                                          ws.numel(), n, batch, steps, inp, hidden, lay, lay, code,
+                                          N.stream_ptr(dev))
+    N.check(rc, "widek_lstm_fwd_ex" if lstm else "widek_gru_fwd_ex")
     return out, hn, cn
+
+
+def _packed_rnn_check(x: Tensor, n: int, what: str) -> None:
+    if x.dim() != 3 or x.shape[1] % n != 0:
+        raise ValueError(f"{what}: packed input must be [B, N*T, I] with N={n}, got {tuple(x.shape)}")
+
+
+def gru_packed(x: Tensor, w_ih: Tensor, w_hh: Tensor, b_ih: Optional[Tensor], b_hh: Optional[Tensor]):
+    """WideGRU forward on the packed boundary layout, zero initial state:
+    x [B, N*T, I] -> (out [B, N*T, H] packed, h_n [N, B, H]), equal to
+    packing the output of ``gru`` on the unpacked input."""
+    N.require_cuda(x, w_ih, w_hh, b_ih, b_hh, what="WideGRU")
+    _same_dtype("WideGRU", w_ih, x, w_hh, b_ih, b_hh)
+    n = w_ih.shape[0]
+    _packed_rnn_check(x, n, "WideGRU")
+    hidden = w_hh.shape[2]
+    if w_ih.shape[2] != x.shape[2] or tuple(w_hh.shape) != (n, 3 * hidden, hidden):
+        raise ValueError(f"WideGRU: weights {tuple(w_ih.shape)} / {tuple(w_hh.shape)} do not match {tuple(x.shape)}")
+    wi, wh = _dense(w_ih), _dense(w_hh)
+    strides = (wi.shape[1] * wi.shape[2], wi.shape[2], wh.shape[1] * wh.shape[2], wh.shape[2])
+    out, hn, _ = _rnn_fwd(False, x, None, None, wi, wh, _opt_dense(b_ih), _opt_dense(b_hh), strides, n, hidden,
+                          packed=True)
+    return out, hn
+
+
+def lstm_blockdiag_packed(x: Tensor, weight_ih: Tensor, weight_hh: Tensor, b_ih: Optional[Tensor],
+                          b_hh: Optional[Tensor], n: int, hidden: int):
+    """WideLSTM forward (block-diagonal parameters, zero initial state) on the
+    packed boundary layout: x [B, N*T, I] -> (out [B, N*T, H], (h_n, c_n))."""
+    N.require_cuda(x, weight_ih, weight_hh, b_ih, b_hh, what="WideLSTM")
+    _same_dtype("WideLSTM", weight_ih, x, weight_hh, b_ih, b_hh)
+    _packed_rnn_check(x, n, "WideLSTM")
+    inp = x.shape[2]
+    if tuple(weight_ih.shape) != (n * 4 * hidden, n * inp) or tuple(weight_hh.shape) != (n * 4 * hidden, n * hidden):
+        raise ValueError(f"WideLSTM: block-diagonal weights {tuple(weight_ih.shape)} / {tuple(weight_hh.shape)} do "
+                         f"not match N={n}, I={inp}, H={hidden}")
+    wi, wh = _dense(weight_ih), _dense(weight_hh)
+    strides = (4 * hidden * n * inp + inp, n * inp, 4 * hidden * n * hidden + hidden, n * hidden)
+    out, hn, cn = _rnn_fwd(True, x, None, None, wi, wh, _opt_dense(b_ih), _opt_dense(b_hh), strides, n, hidden,
+                           packed=True)
+    return out, (hn, cn)
 
 
 def _opt_dense(t: Optional[Tensor]) -> Optional[Tensor]:
@@ -600,6 +701,27 @@ def attention_tensors(query: Tensor, key: Tensor, value: Tensor, q_weight: Tenso
     return linear(o, out_weight, out_bias)
 
 
+def attention_packed(mod, x: Tensor, is_causal: bool) -> Tensor:
+    """WideAttention self-attention on the packed boundary layout: x
+    [B, N*T, D] -> [B, N*T, D], the fused QKV projection reading the packed
+    rows in place and the output projection writing them packed; equal to
+    unpacking, ``attention_tensors`` and packing (traced_wide.py:463-469,
+    :527-532 around wide_attention.py:178-238)."""
+    n, d = mod.q_weight.shape[0], mod.q_weight.shape[1]
+    heads = mod.n_heads
+    if x.dim() != 3 or x.shape[1] % n != 0 or x.shape[2] != d:
+        raise ValueError(f"WideAttention: packed input must be [B, N*T, D={d}] with N={n}, got {tuple(x.shape)}")
+    dev = N.require_cuda(x, mod.q_weight, what="WideAttention")
+    b, t = x.shape[0], x.shape[1] // n
+    w, bias = fused_qkv(mod.q_weight, mod.kv_weight, mod.q_bias, mod.kv_bias)
+    qkv = linear_layout(x, w, bias, ACT_NONE, True, False)      # [N, B, T, 3D]
+    flat = qkv.view(-1)
+    o = torch.empty(n, b, t, d, device=dev, dtype=x.dtype)
+    attention_core(flat, flat[d:], flat[2 * d:], n * b, heads, t, t, d // heads, 3 * d, 3 * d, 3 * d, o, is_causal,
+                   None)
+    return linear_layout(o, mod.out_weight, mod.out_bias, ACT_NONE, False, True)
+
+
 def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool) -> Tensor:
     """WideAttention forward on N-first [N, B, T, D] tensors (see the module)."""
     return attention_tensors(query, key, value, mod.q_weight, mod.q_bias, mod.kv_weight, mod.kv_bias,
@@ -612,13 +734,14 @@ def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optiona
 # ---------------------------------------------------------------------------
 
 def _packed_weight(weight: Tensor, rows: int, cin: int, taps: int, dev) -> Tensor:
-    """[rows, cin, taps] -> [rows, taps, cin] for the tensor-core conv, kept
-    on the weight tensor between forwards (see ``_derived``: rebuilt when its
-    version, storage, dtype or shape changes, and inside every CUDA-graph
-    capture)."""
+    """[rows, cin, taps] -> [rows, taps, cin_p] (cin_p = cin rounded up to 64,
+    zero-filled) for the tensor-core conv, kept on the weight tensor between
+    forwards (see ``_derived``: rebuilt when its version, storage, dtype or
+    shape changes, and inside every CUDA-graph capture)."""
     def build():
         wd = _dense(weight.detach())
-        wp = torch.empty(rows, taps, cin, device=dev, dtype=weight.dtype)
+        elems = int(N.lib().widek_conv_packed_weight_elems(rows, cin, taps))
+        wp = torch.empty(elems, device=dev, dtype=weight.dtype)
         with _guard(dev):
             rc = N.lib().widek_conv_pack_weight(wd.data_ptr(), wp.data_ptr(), rows, cin, taps, wd.element_size(),
                                                 N.stream_ptr(dev))
@@ -647,6 +770,26 @@ def conv_geometry(n, batch, cin, cout, sp_in, kernel, stride, padding, dilation)
         raise ValueError(f"WideConv: output size {out_sp} is not positive")
     geom = (ctypes.c_int64 * 22)(n, batch, cin, cout, *sp, *ks, *st, *pd, *dl, *out_sp)
     return geom, sp, ks, st, out_sp[3 - nd:]
+
+
+_TC_PATH_CACHE: dict = {}
+
+
+def _tensor_core_path(geom, dtype_code: int, in_layout: int, out_layout: int, res_layout: int,
+                      has_residual: bool) -> bool:
+    """Whether the library runs this conv on a tensor-core kernel (which then
+    needs the packed weights and, for a non-channels-last input, the staging
+    workspace). The library's own decision (widek_conv_path), memoised."""
+    key = (tuple(geom), dtype_code, in_layout, out_layout, res_layout, has_residual)
+    hit = _TC_PATH_CACHE.get(key)
+    if hit is None:
+        path = int(N.lib().widek_conv_path(geom, dtype_code, in_layout, out_layout, res_layout,
+                                           1 if has_residual else 0))
+        hit = path in (CONV_PATH_TAPS, CONV_PATH_HALO)
+        if len(_TC_PATH_CACHE) > 4096:
+            _TC_PATH_CACHE.clear()
+        _TC_PATH_CACHE[key] = hit
+    return hit
 
 
 def conv_path(n, batch, cin, cout, sp_in, kernel, stride, padding, dilation, dtype: torch.dtype,
@@ -712,9 +855,7 @@ def conv_nd(x: Tensor, weight: Tensor, bias: Optional[Tensor], n: int, stride, p
         y = torch.empty((n, batch, cout, *osp), device=dev, dtype=x.dtype)
     xd = _dense(x)
     wp = ws = None
-    tc = (x.dtype in (torch.bfloat16, torch.float16) and nd in (1, 2) and st == (1, 1, 1) and cin % 64 == 0
-          and cout % 16 == 0)
-    if tc:
+    if _tensor_core_path(geom, N.dtype_code(x), in_layout, out_layout, res_layout, residual is not None):
         taps = ks[0] * ks[1] * ks[2]
         wp = _packed_weight(weight, n * cout, cin, taps, dev)
         if in_layout != LAYOUT_CLAST:

@@ -92,11 +92,12 @@ def gather_outputs(local: Tensor, n_total: int, group=None, out: Optional[Tensor
     return out
 
 
-def gather_packed(local: Tensor, n_total: int, group=None) -> Tensor:
-    """All-gathers channel-packed outputs ``[B, n_local*F, *S]`` into
-    ``[B, n_total*F, *S]`` on every rank (rank r's models at channels
-    ``[lo_r*F, hi_r*F)``)."""
-    rank, world, _ = _group_ranks(group)
+def _start_gather_packed(local: Tensor, n_total: int, group=None):
+    """Issues the collectives of ``gather_packed`` asynchronously and returns
+    ``place(full)``, which waits for them (on the device: the current stream
+    waits, the host does not block) and writes every rank's rows into the
+    packed result ``full`` [B, n_total*F, *S] (one strided copy per rank)."""
+    rank, world, globals_ = _group_ranks(group)
     a, b = shard_range(n_total, world, rank)
     n_local = b - a
     bsz = local.shape[0]
@@ -114,22 +115,39 @@ def gather_packed(local: Tensor, n_total: int, group=None) -> Tensor:
         offs.append(offs[-1] + sz)
     flat = torch.empty(sum(sizes), dtype=local.dtype, device=local.device)
     mine = local.contiguous().reshape(-1)
+    works = []
     if len(set(sizes)) == 1 and hasattr(dist, "all_gather_into_tensor") and dist.get_backend(group) != "gloo":
-        dist.all_gather_into_tensor(flat, mine, group=group)
+        works.append(dist.all_gather_into_tensor(flat, mine, group=group, async_op=True))
     else:
-        _, _, globals_ = _group_ranks(group)
         flat[offs[rank]:offs[rank] + sizes[rank]].copy_(mine)
         for r in range(world):
             if sizes[r]:
-                dist.broadcast(flat[offs[r]:offs[r] + sizes[r]], src=globals_[r], group=group)
-    full = torch.empty((bsz, n_total * f, *local.shape[2:]), dtype=local.dtype, device=local.device)
-    es = local.element_size()
-    for r, (ra, rb) in enumerate(blocks):
-        if rb == ra:
-            continue
-        row = (rb - ra) * inner * es
-        copy_rows(flat[offs[r]:offs[r] + sizes[r]], row, full.view(bsz, n_total * inner)[:, ra * inner:],
-                  n_total * inner * es, bsz, row)
+                works.append(dist.broadcast(flat[offs[r]:offs[r] + sizes[r]], src=globals_[r], group=group,
+                                            async_op=True))
+
+    def place(full: Tensor) -> None:
+        for w in works:
+            w.wait()
+        es = local.element_size()
+        for r, (ra, rb) in enumerate(blocks):
+            if rb == ra:
+                continue
+            row = (rb - ra) * inner * es
+            copy_rows(flat[offs[r]:offs[r] + sizes[r]], row, full.view(bsz, n_total * inner)[:, ra * inner:],
+                      n_total * inner * es, bsz, row)
+    return place
+
+
+def gather_packed(local: Tensor, n_total: int, group=None) -> Tensor:
+    """All-gathers channel-packed outputs ``[B, n_local*F, *S]`` into
+    ``[B, n_total*F, *S]`` on every rank (rank r's models at channels
+    ``[lo_r*F, hi_r*F)``)."""
+    place = _start_gather_packed(local, n_total, group)
+    _, world, _ = _group_ranks(group)
+    a, b = shard_range(n_total, world, _group_ranks(group)[0])
+    f = local.shape[1] // (b - a)
+    full = torch.empty((local.shape[0], n_total * f, *local.shape[2:]), dtype=local.dtype, device=local.device)
+    place(full)
     return full
 
 
@@ -165,11 +183,23 @@ class ShardedWideModel(nn.Module):
     copy; it returns this rank's packed output ``[B, n_local*F, ...]`` or,
     with ``gather=True``, the full packed output ``[B, N*F, ...]`` on every
     rank (``gather_packed``: the only collective).
+
+    ``gather_chunks=k`` (> 1) overlaps that gather with the forward: the
+    batch runs as k consecutive slices (contiguous in the packed layout, so
+    no copy), each slice's gather is issued asynchronously as soon as its
+    forward has been queued, and runs on NCCL's stream while the next slice
+    computes; the rows land in the result after the last forward. Used only
+    when the result cannot depend on the batch split: no BatchNorm in
+    training mode.
     """
 
     def __init__(self, models: Sequence[nn.Module], sample_input: Tensor, rank: Optional[int] = None,
-                 world: Optional[int] = None, group=None, gather: bool = False, compile_model: bool = False):
+                 world: Optional[int] = None, group=None, gather: bool = False, compile_model: bool = False,
+                 gather_chunks: int = 1):
         super().__init__()
+        if gather_chunks < 1:
+            raise ValueError(f"gather_chunks must be >= 1, got {gather_chunks}")
+        self.gather_chunks = gather_chunks
         from .api import compile as wide_compile
         self.group = group
         self.rank = dist.get_rank(group) if rank is None else rank
@@ -204,11 +234,27 @@ class ShardedWideModel(nn.Module):
                   self.n_local * inner * es, x.shape[0], self.n_local * inner * es)
         return out
 
+    def _batch_split_ok(self) -> bool:
+        return not any(isinstance(m, nn.modules.batchnorm._BatchNorm) and m.training for m in self.local.modules())
+
     def forward(self, x: Tensor) -> Tensor:
-        y = self.local(self.local_input(x))
-        if self.gather and self.world > 1:
-            return gather_packed(y, self.n_total, group=self.group)
-        return y
+        xl = self.local_input(x)
+        if not (self.gather and self.world > 1):
+            return self.local(xl)
+        k = min(self.gather_chunks, xl.shape[0])
+        if k <= 1 or not self._batch_split_ok():
+            return gather_packed(self.local(xl), self.n_total, group=self.group)
+        places, full = [], None
+        for c in range(k):
+            b0, b1 = shard_range(xl.shape[0], k, c)
+            y = self.local(xl[b0:b1])
+            if full is None:
+                f = y.shape[1] // self.n_local
+                full = torch.empty((xl.shape[0], self.n_total * f, *y.shape[2:]), dtype=y.dtype, device=y.device)
+            places.append((b0, b1, _start_gather_packed(y, self.n_total, self.group)))
+        for b0, b1, place in places:
+            place(full[b0:b1])
+        return full
 
 
 __all__ = ['shard_range', 'shard_models', 'gather_outputs', 'gather_packed', 'copy_rows', 'ShardedWideModel']

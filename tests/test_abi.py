@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "widek.h")
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"WIDEK_API\s+(?:int|size_t|long long)\s+(widek_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"WIDEK_API\s+(?:int|int64_t|size_t|long long)\s+(widek_\w+)\s*\(", text)))
 
 
 def test_header_declares_entry_points():
@@ -60,7 +60,7 @@ def test_zero_sized_calls_are_noops():
 def _header_param_counts():
     text = open(HEADER).read()
     out = {}
-    for m in re.finditer(r"WIDEK_API\s+(?:int|size_t|long long)\s+(widek_\w+)\s*\(([^)]*)\)", text, re.S):
+    for m in re.finditer(r"WIDEK_API\s+(?:int|int64_t|size_t|long long)\s+(widek_\w+)\s*\(([^)]*)\)", text, re.S):
         params = m.group(2).strip()
         out[m.group(1)] = 0 if params in ("", "void") else len(params.split(","))
     return out

@@ -54,12 +54,13 @@ def test_conv_tensor_core(n, b, cin, cout, sp, k, p, d, dtype):
     (2, 2, 3, 8, (9, 11), 3, 2, 1, 1, torch.float32),
     (2, 2, 5, 4, (4, 5, 6), 3, 1, 1, 1, torch.float32),
     (2, 1, 4, 6, (33,), 4, 3, 2, 2, torch.float32),
-    (2, 2, 3, 8, (9, 11), 3, 1, 1, 1, torch.bfloat16),      # cin % 64 != 0 -> CUDA cores
-    (2, 2, 64, 64, (9, 11), 3, 2, 1, 1, torch.bfloat16),    # stride 2 -> CUDA cores
+    (2, 2, 64, 64, (40, 41), 3, 9, 1, 1, torch.bfloat16),   # stride > 8 (TMA step limit) -> CUDA cores
 ])
 def test_conv_direct(n, b, cin, cout, sp, k, s, p, d, dtype):
     x, w, bb = _conv_case(n, b, cin, cout, sp, k, dtype, k + s + cin)
     nd = len(sp)
+    assert ops.conv_path(n, b, cin, cout, sp, (k,) * nd, (s,) * nd, (p,) * nd, (d,) * nd, dtype) == \
+        ops.CONV_PATH_DIRECT
     y = ops.conv_nd(x.to(DEV), w.to(DEV), bb.to(DEV), n, (s,) * nd, (p,) * nd, (d,) * nd)
     ref = O.conv_nd(x, w, bb, n, (s,) * nd, (p,) * nd, (d,) * nd)
     (assert_fp32_close if dtype == torch.float32 else assert_lowp_close)(y, ref)

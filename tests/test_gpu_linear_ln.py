@@ -205,22 +205,34 @@ def test_traced_mlp_golden():
     no_device_error()
 
 
-@pytest.mark.parametrize("n,m,k,o", [(2, 256, 1024, 512), (3, 300, 200, 264), (1, 129, 64, 136), (4, 512, 256, 1024)])
-def test_linear_pair_tiles_match_single_cta(n, m, k, o):
-    """CTA-pair (cta_group::2) tiles vs single-CTA tiles vs the oracle."""
-    from wide_compiler import _native
-    x, w, b = _rand_linear(n, m, k, o, torch.bfloat16, seed=m + o)
-    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
-    lib = _native.lib()
-    try:
-        _native.check(lib.widek_linear_set_variant(1), "variant")
-        y1 = ops.linear(xd, wd, bd)
-        _native.check(lib.widek_linear_set_variant(2), "variant")
-        y2 = ops.linear(xd, wd, bd)
-    finally:
-        lib.widek_linear_set_variant(0)
-    ref = O.linear(x, w, b)
-    assert_lowp_close(y1, ref)
-    assert_lowp_close(y2, ref)
-    torch.testing.assert_close(y1.float(), y2.float(), rtol=1e-2, atol=1e-2)
+@pytest.mark.parametrize("n,b,t,k,o,dtype", [
+    (3, 4, 32, 64, 96, torch.bfloat16),      # T divides 128: box of 4 row blocks
+    (2, 2, 256, 128, 64, torch.bfloat16),    # T a multiple of 128
+    (4, 128, 1, 64, 200, torch.float16),     # T = 1 ([B, N*K] rows)
+    (2, 3, 50, 64, 64, torch.bfloat16),      # T neither: CUDA-core kernel
+    (2, 3, 16, 24, 40, torch.float32),       # fp32: CUDA-core kernel
+])
+@pytest.mark.parametrize("inp,outp", [(True, True), (True, False), (False, True)])
+def test_linear_packed_rows(n, b, t, k, o, dtype, inp, outp):
+    """widek_linear_fwd_ex on the packed boundary layout [B, N*T, K] (in,
+    out or both) equals unpack -> linear -> pack, bit for bit against the
+    N-first kernel call on the same inputs."""
+    g = torch.Generator().manual_seed(n * 100 + t)
+    x = torch.randn(n, b, t, k, generator=g).to(dtype)
+    w = (torch.randn(n, o, k, generator=g) / k ** 0.5).to(dtype)
+    bias = (torch.randn(n, o, generator=g) * 0.1).to(dtype)
+    xd, wd, bd = x.to(DEV), w.to(DEV), bias.to(DEV)
+    xin = O.nfirst_to_packed(x).reshape(b, n * t, k).contiguous().to(DEV) if inp else xd
+    y = ops.linear_layout(xin, wd, bd, ops.ACT_NONE, inp, outp)
+    ref = ops.linear(xd, wd, bd)
+    if outp:
+        ref = O.nfirst_to_packed(ref).reshape(b, n * t, o).to(DEV)
+    assert y.shape == ref.shape
+    if dtype == torch.float32 or t % 128 == 0 or 128 % t == 0:
+        assert torch.equal(y, ref)          # same kernel, same tiles: bit-identical
+    else:
+        assert_lowp_close(y, ref.double())  # packed rows on the CUDA-core kernel
+    if dtype == torch.float32:
+        assert_fp32_close(ref if not outp else y, O.linear(x, w, bias) if not outp else
+                          O.nfirst_to_packed(O.linear(x, w, bias)).reshape(b, n * t, o))
     no_device_error()

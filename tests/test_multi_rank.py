@@ -49,7 +49,18 @@ def _worker(rank, world, port, n_total, fail_rank, result_path):
         bsz, f, sp = 3, 2, 5
         packed_full = torch.arange(bsz * n_total * f * sp, dtype=torch.float32).view(bsz, n_total * f, sp)
         got_p = parallel.gather_packed(packed_full[:, a * f:b * f].contiguous(), n_total)
-        ok = bool(torch.equal(got, full)) and bool(torch.equal(got_p, packed_full))
+        # the overlapped form ShardedWideModel(gather_chunks=2) uses: two batch
+        # slices gathered asynchronously, then placed into slices of the result
+        chunked = torch.empty_like(packed_full)
+        places = []
+        for c in range(2):
+            b0, b1 = parallel.shard_range(bsz, 2, c)
+            places.append((b0, b1, parallel._start_gather_packed(packed_full[b0:b1, a * f:b * f].contiguous(),
+                                                                  n_total)))
+        for b0, b1, place in places:
+            place(chunked[b0:b1])
+        ok = bool(torch.equal(got, full)) and bool(torch.equal(got_p, packed_full)) and \
+            bool(torch.equal(chunked, packed_full))
         torch.save({"ok": ok}, f"{result_path}.{rank}")
     except Exception as e:  # report on the host, never on a device
         torch.save({"ok": False, "error": repr(e)}, f"{result_path}.{rank}")
