@@ -29,6 +29,17 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     const int tid = threadIdx.x;
     const int tx = tid % (BN / TN);
     const int ty = tid / (BN / TN);
+    // Row offsets (elements) of the x rows this thread loads (the same rows
+    // in every k tile) and of the y rows it stores: block-strided rows
+    // (row r at (r / x_rpb)*x_bs + (r % x_rpb)*K), one division per row
+    // instead of per element.
+    constexpr int LOADS = (BM * BK + NT - 1) / NT;
+    int64_t xoff[LOADS];
+#pragma unroll
+    for (int j = 0; j < LOADS; ++j) {
+        const int gm = m0 + (tid + j * NT) / BK;
+        xoff[j] = gm < M ? (int64_t)(gm / x_rpb) * x_bs + (int64_t)(gm % x_rpb) * K : 0;
+    }
 
     float acc[TM][TN];
 #pragma unroll
@@ -37,11 +48,14 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
     for (int k0 = 0; k0 < K; k0 += BK) {
-        for (int i = tid; i < BM * BK; i += NT) {
-            const int r = i / BK, c = i % BK;
-            const int gm = m0 + r, gk = k0 + c;
-            As[c][r] = (gm < M && gk < K) ? to_f<T>(x[(int64_t)(gm / x_rpb) * x_bs + (int64_t)(gm % x_rpb) * K + gk])
-                                          : 0.f;
+#pragma unroll
+        for (int j = 0; j < LOADS; ++j) {
+            const int i = tid + j * NT;
+            if (i < BM * BK) {
+                const int r = i / BK, c = i % BK;
+                const int gm = m0 + r, gk = k0 + c;
+                As[c][r] = (gm < M && gk < K) ? to_f<T>(x[xoff[j] + gk]) : 0.f;
+            }
         }
         for (int i = tid; i < BN * BK; i += NT) {
             const int r = i / BK, c = i % BK;
@@ -67,13 +81,14 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     for (int i = 0; i < TM; ++i) {
         const int gm = m0 + ty * TM + i;
         if (gm >= M) continue;
+        T* yrow = y + (int64_t)(gm / x_rpb) * y_bs + (int64_t)(gm % x_rpb) * O;
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
             const int go = o0 + tx + (BN / TN) * j;
             if (go >= O) continue;
             float v = acc[i][j];
             if (bias) v += to_f<T>(bias[(int64_t)model * O + go]);
-            y[(int64_t)(gm / x_rpb) * y_bs + (int64_t)(gm % x_rpb) * O + go] = from_f<T>(apply_act(v, act));
+            yrow[go] = from_f<T>(apply_act(v, act));
         }
     }
 }

@@ -15,6 +15,19 @@
 namespace widek {
 namespace {
 
+// Model of a row: (row / inner) % n, with 32-bit division when the values
+// fit (a 64-bit division is a long instruction sequence on the critical path
+// to the affine loads) and no modulo in the N-first layout (quotient < n).
+__device__ __forceinline__ int64_t model_of_row(int64_t row, int64_t inner, int64_t n) {
+    int64_t q;
+    if (((uint64_t)row | (uint64_t)inner) <= 0xffffffffull)
+        q = (int64_t)((uint32_t)row / (uint32_t)inner);
+    else
+        q = row / inner;
+    if (q >= n) q = (n <= 0xffffffffll && q <= 0xffffffffll) ? (int64_t)((uint32_t)q % (uint32_t)n) : q % n;
+    return q;
+}
+
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) layernorm_warp_kernel(
     const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
@@ -51,7 +64,7 @@ __global__ void __launch_bounds__(256) layernorm_warp_kernel(
     }
     const float var = warp_sum(q) / (float)d;
     const float rstd = rsqrtf(var + eps);
-    const int64_t model = (row / inner) % n;
+    const int64_t model = model_of_row(row, inner, n);
     const T* wr = w + model * d;
     const T* br = b + model * d;
     T* yr = y + row * d;
@@ -105,7 +118,7 @@ __global__ void __launch_bounds__(256) layernorm_block_kernel(
     }
     __syncthreads();
     const float rstd = rsqrtf(red[0] / (float)d + eps);
-    const int64_t model = (row / inner) % n;
+    const int64_t model = model_of_row(row, inner, n);
     const T* wr = w + model * d;
     const T* br = b + model * d;
     T* yr = y + row * d;

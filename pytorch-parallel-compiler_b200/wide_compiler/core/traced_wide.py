@@ -538,6 +538,15 @@ class TracedWideModel(nn.Module):
         packed_in = isinstance(xv, _Laid) and xv.layout == ops.LAYOUT_PACKED
         tail = g['nodes'][-1]
         at_output = tail == self._output_name and self._fusion['consumers'].get(tail) == ['<output>']
+        if packed_in and t.dim() == 3 and t.shape[1] % n == 0:
+            # packed [B, N*T, K] rows: the per-layer GEMMs read the packed
+            # input and write the packed output in place (no unpack / pack)
+            h, in_p = t, True
+            for i, (w, b, act) in enumerate(zip(ws, bs, g['acts'])):
+                out_p = at_output and i == len(ws) - 1
+                h = ops.linear_layout(h, w, b, act, in_p, out_p) if (in_p or out_p) else ops.linear(h, w, b, act=act)
+                in_p = False
+            return _Laid(h, ops.LAYOUT_PACKED) if at_output else h
         if packed_in and t.dim() == 2:
             x_in, in_l, batch_shape = t, ops.LAYOUT_PACKED, (t.shape[0],)
         else:

@@ -33,7 +33,7 @@ def swap_calls(monkeypatch):
 
 
 def _run(models, sample, inputs):
-    wide = TracedWideModel.from_models(models, sample)
+    wide = TracedWideModel.from_models(models, sample).eval()
     out = wide(O.pack_inputs(inputs).to(DEV))
     with torch.no_grad():
         outs = [m(x) for m, x in zip(models, inputs)]
@@ -220,7 +220,7 @@ def test_packed_boundary_matches_unfused_bitwise(case, swap_calls):
     inputs = [torch.randn(*shape, generator=g).to(DEV, torch.bfloat16) for _ in range(n)]
     packed = O.pack_inputs(inputs).to(DEV)
     with torch.no_grad():
-        wide = TracedWideModel.from_models(models, inputs[0])
+        wide = TracedWideModel.from_models(models, inputs[0]).eval()
         fused = wide(packed)
         assert swap_calls == [], f"{case}: unpack/pack copies {swap_calls}"
         wide.fuse = False
