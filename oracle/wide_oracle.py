@@ -289,7 +289,7 @@ def nfirst_to_packed(x: Tensor) -> Tensor:
 
 
 # ---------------------------------------------------------------------------
-# The BASELINE model graphs, composed from the functions above
+# The benchmark model graphs, composed from the functions above
 # ---------------------------------------------------------------------------
 def mlp2(x_packed: Tensor, n: int, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor) -> Tensor:
     """TracedWideModel of N two-layer MLPs (Linear -> ReLU -> Linear),

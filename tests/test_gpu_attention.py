@@ -98,7 +98,7 @@ def test_attention_fp32_modules_match_torch_mha():
 
 
 def test_attention_cfg5_full_size_sampled():
-    """BASELINE cfg5: N=16, B=8, T=1024, d=512, 8 heads, causal, bf16; the
+    """Benchmark configuration cfg5: N=16, B=8, T=1024, d=512, 8 heads, causal, bf16; the
     oracle checks two (model, batch) slices."""
     n, b, t, d, h = 16, 8, 1024, 512, 8
     torch.manual_seed(5)

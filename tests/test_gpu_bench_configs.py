@@ -1,4 +1,4 @@
-"""GPU parity at the BASELINE sizes, on the exact modules and inputs bench.py
+"""GPU parity at the benchmark sizes, on the exact modules and inputs bench.py
 times (its workload builders): the cfg3 ResBlock TracedWideModel (fused halo
 conv chain with the folded BatchNorm and the residual, packed input and
 output) and the cfg1 MLP TracedWideModel (one chain launch, eager and under

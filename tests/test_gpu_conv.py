@@ -99,7 +99,7 @@ def test_conv_modules_and_weight_cache():
 
 
 def test_conv_cfg3_full_size_sampled():
-    """BASELINE cfg3 conv: N=100, B=32, 64->64, 3x3 pad 1, 32x32, bf16."""
+    """Benchmark configuration cfg3 conv: N=100, B=32, 64->64, 3x3 pad 1, 32x32, bf16."""
     n, b, c = 100, 32, 64
     g = torch.Generator(device=DEV).manual_seed(3)
     x = torch.randn(n, b, c, 32, 32, device=DEV, generator=g).to(torch.bfloat16)

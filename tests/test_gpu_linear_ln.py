@@ -82,7 +82,7 @@ def test_linear_tc_matches_simt():
 
 
 def test_linear_cfg2_full_size_sampled():
-    """BASELINE cfg2 (N=64, 1024->4096, B=256, bf16) at full size; the oracle
+    """Benchmark configuration cfg2 (N=64, 1024->4096, B=256, bf16) at full size; the oracle
     checks a sample of models and rows, a checksum covers every output."""
     n, m, k, o = 64, 256, 1024, 4096
     g = torch.Generator(device=DEV).manual_seed(1)

@@ -46,7 +46,7 @@ def _check(y, ref, dtype):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("in_l,out_l", [(0, 0), (1, 1), (1, 0), (0, 1)])
 def test_cfg1_shape_layouts(dtype, in_l, out_l):
-    """The BASELINE MLP (64 -> 128, ReLU, -> 64), every layout pair."""
+    """The benchmark cfg1 MLP (64 -> 128, ReLU, -> 64), every layout pair."""
     n, b, dims, acts = 7, 32, [64, 128, 64], [ops.ACT_RELU, ops.ACT_NONE]
     ws, bs = _chain(n, dims, dtype, seed=1)
     x = torch.randn(n, b, dims[0], generator=torch.Generator().manual_seed(2)).to(dtype)

@@ -80,7 +80,7 @@ def test_rnn_bf16_and_no_bias():
 
 
 def test_rnn_modules_from_torch_cfg4():
-    """BASELINE cfg4 through the public modules built from nn.GRU / nn.LSTM."""
+    """Benchmark configuration cfg4 through the public modules built from nn.GRU / nn.LSTM."""
     torch.manual_seed(0)
     grus = [torch.nn.GRU(64, 128, batch_first=True) for _ in range(32)]
     lstms = [torch.nn.LSTM(64, 128, batch_first=True) for _ in range(32)]
