@@ -125,9 +125,12 @@ struct SimtLaunch {
             gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
                                                                     (int)xrpb, yms, ybs);
         } else {
+            // 64x64 tiles of 64 threads with 8x8 outputs each: per k a lane
+            // reads 8 + 8 shared floats for 64 FMAs (4 FMAs per shared-memory
+            // wavefront, the FMA pipe's rate), where 4x4 tiles give 2
             dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)n);
             if (grid.y > 65535) return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): m too large");
-            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
+            gemm_simt_kernel<T, 64, 64, 16, 8, 8><<<grid, 64, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
                                                                     (int)xrpb, yms, ybs);
         }
         return check_launch("widek_linear_fwd_simt");
