@@ -480,9 +480,12 @@ WIDEK_API int widek_conv_layouts_supported(const int64_t* geom, int dtype, int i
                                            int res_layout, int has_residual);
 
 /* Kernel choice for widek_conv_fwd's tensor-core path: 0 = halo-reuse kernel
- * where it applies (64-channel output tiles, output width a multiple of 8),
- * else the per-tap kernel (default); 1 = per-tap kernel only. Process-wide;
- * for tests and measurements. No reference counterpart. */
+ * where it applies (64-channel output tiles, output width a multiple of 8;
+ * 8 x 16 pixel tiles with one shared halo buffer for channels-last outputs,
+ * 16 x 8 tiles with column-shifted subtiles otherwise), else the per-tap
+ * kernel (default); 1 = per-tap kernel only; 2 = as 0 with the shared halo
+ * buffer for every output layout. Process-wide; for tests and
+ * measurements. No reference counterpart. */
 WIDEK_API int widek_conv_set_variant(int variant);
 
 /* ---- WideAttention -------------------------------------------------------- */

@@ -541,7 +541,9 @@ struct ConvHaloGeom {
     int kh, kw, cblocks, ph, pw, dh, dw;
     int stages;             // ring depth, one subtile per stage
     int out5, res5;         // output / residual in the packed [b][n*c][h][w] layout (5-D maps)
-    uint32_t sub_bytes;     // (th + (kh-1)*dh) * tw * 128: one subtile
+    int shared;             // one halo buffer per (tile, channel block) for all kw column offsets
+    int pitch;              // pixels per buffer row in shared mode (a multiple of 8)
+    uint32_t sub_bytes;     // (th + (kh-1)*dh) * (shared ? pitch : tw) * 128: one subtile / buffer
     uint32_t w_bytes;       // kh * kw * cblocks * HBN * 128: weights of one output tile
     int64_t tiles;
 };
@@ -755,8 +757,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             const int ho0 = (mt / g.tiles_w) * g.th;
             const int wo0 = (mt % g.tiles_w) * g.tw;
             const int img = model * g.batch + b;
+            const int loads = g.shared ? 1 : g.kw;
             for (int cb = 0; cb < g.cblocks && ok; ++cb) {
-                for (int kx = 0; kx < g.kw; ++kx) {
+                for (int kx = 0; kx < loads; ++kx) {
                     if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
                     if (lane == 0) {
                         mbar_arrive_expect_tx(&full[s], g.sub_bytes);
@@ -803,7 +806,17 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             const uint32_t row_step16 = (uint32_t)(g.dh * g.tw * 128) >> 4;
             const uint32_t tap_stride16 = (uint32_t)((KW > 0 ? KW : g.kw) * g.cblocks * HBN * 128) >> 4;
             const int kw = KW > 0 ? KW : g.kw;
-            const uint32_t per_tile = (uint32_t)(g.cblocks * kw);
+            const int kh = KH > 0 ? KH : g.kh;
+            const uint32_t per_tile = (uint32_t)(g.cblocks * (g.shared ? 1 : kw));
+            // Shared mode: A rows are (tile row, pixel) at a pitch of g.pitch
+            // pixels, so the 8-row core groups are g.pitch*128 bytes apart
+            // (a multiple of 1024); tap (ky, kx) starts ky*dh*pitch + kx*dw
+            // rows into the buffer. The start need not be 1024-aligned: the
+            // tensor core takes each row's 128-byte swizzle phase from its
+            // shared-memory address, as the TMA wrote it (checked against
+            // the oracle on B200; the descriptor's base-offset field stays 0).
+            const uint64_t a_desc_sh = (a_desc0 & ~((uint64_t)0x3FFF << 32)) |
+                                       ((uint64_t)(((uint32_t)g.pitch * 128u) >> 4) << 32);
             int local = 0;
             for (int64_t tile = t_begin; tile < t_end && ok; ++tile, ++local, ring += per_tile) {
                 int model, nt, b, mt;
@@ -821,6 +834,33 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + me * HBN;
                 uint32_t c = ring;
+                if (g.shared) {
+                    for (int cb = 0; cb < g.cblocks && ok; ++cb, ++c) {
+                        const uint32_t s = c % (uint32_t)g.stages;
+                        if (!mbar_wait(&full[s], (c / (uint32_t)g.stages) & 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint64_t a_stage = a_desc_sh + (uint64_t)((s * g.sub_bytes) >> 4);
+#pragma unroll 1
+                        for (int ky = 0; ky < kh; ++ky) {
+#pragma unroll
+                            for (int kx = 0; kx < (KW > 0 ? KW : 8); ++kx) {
+                                if (KW == 0 && kx >= kw) break;
+                                const uint32_t off = (uint32_t)(ky * g.dh * g.pitch + kx * g.dw);
+                                const uint64_t ad = a_stage + (uint64_t)(off * 8u);
+                                const uint64_t bd = w_desc0 + (uint64_t)((((ky * kw + kx) * g.cblocks + cb) *
+                                                                          (HBN * 128)) >> 4);
+#pragma unroll
+                                for (int k = 0; k < BK / 16; ++k)
+                                    umma_f16_ss(d_tmem, ad + 2 * k, bd + 2 * k, IDESC,
+                                                !(cb == 0 && ky == 0 && kx == 0 && k == 0));
+                            }
+                        }
+                        umma_commit(&empty[s]);
+                    }
+                    if (!ok) break;
+                    umma_commit(&tfull[me]);
+                    continue;
+                }
                 for (int cb = 0; cb < g.cblocks && ok; ++cb) {
                     for (int kx = 0; kx < kw; ++kx, ++c) {
                         const uint32_t s = c % (uint32_t)g.stages;
@@ -1183,19 +1223,32 @@ int launch_conv_tc(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, const
 }
 
 // 0: halo-reuse kernel where it applies, else the per-tap kernel (default);
-// 1: per-tap kernel only. Set with widek_conv_set_variant (measurements).
+// 1: per-tap kernel only; 2: halo kernel with one shared halo buffer per
+// tile (8 x 16 pixel tiles) for every output layout (variant 0 uses it for
+// channels-last outputs only). Set with widek_conv_set_variant (measurements).
 int g_conv_variant = 0;
 
 // Halo-reuse geometry for a stride-1 conv with 64-channel output tiles, or
 // false when it does not fit (tile width, box limits, shared memory).
-bool halo_geometry(const ConvGeom& cg, bool res_tma, ConvHaloGeom& g, uint32_t& smem) {
+bool halo_geometry(const ConvGeom& cg, bool res_tma, bool cl_out, ConvHaloGeom& g, uint32_t& smem) {
     if (cg.d != 1 || cg.kd != 1 || cg.sh != 1 || cg.sw != 1 || cg.cin % BK != 0) return false;
     if (cg.cout % HBN != 0 || cg.ow % 8 != 0 || cg.ow < 8) return false;
-    const int tw = cg.ow >= 16 ? 16 : 8;
+    // Shared halo buffer: 8 x 16 pixel tiles, one buffer of (16 + (kh-1)*dh)
+    // rows x pitch pixels per channel block serving every tap (36 KB per
+    // tile at 3x3 instead of three 20 KB column-shifted subtiles). Used for
+    // channels-last outputs (128-byte output rows; on cfg3's conv1 283 vs
+    // 292 us), and for every output with variant 2; the N-first / packed
+    // outputs keep 16 x 8 tiles, whose 32-byte output rows make full sectors
+    // (with 8-pixel tiles cfg3's conv2 went 331 -> 426 us).
+    const int pitch = (8 + (cg.kw - 1) * cg.dw + 7) / 8 * 8;
+    const bool shared = (g_conv_variant == 2 || (g_conv_variant == 0 && cl_out)) && pitch <= 256;
+    const int tw = shared ? 8 : (cg.ow >= 16 ? 16 : 8);
     const int th = BM / tw;
     const int rows = th + (cg.kh - 1) * cg.dh;
     if (rows > 256) return false;
     g = ConvHaloGeom{};
+    g.shared = shared ? 1 : 0;
+    g.pitch = pitch;
     g.n = cg.n; g.batch = cg.batch; g.cout = cg.cout; g.ho = cg.oh; g.wo = cg.ow;
     g.tw = tw; g.th = th;
     g.tiles_h = (cg.oh + th - 1) / th;
@@ -1203,7 +1256,7 @@ bool halo_geometry(const ConvGeom& cg, bool res_tma, ConvHaloGeom& g, uint32_t& 
     g.nt_count = cg.cout / HBN;
     g.kh = cg.kh; g.kw = cg.kw; g.cblocks = cg.cin / BK;
     g.ph = cg.ph; g.pw = cg.pw; g.dh = cg.dh; g.dw = cg.dw;
-    g.sub_bytes = (uint32_t)rows * tw * 128;
+    g.sub_bytes = (uint32_t)rows * (shared ? pitch : tw) * 128;
     if ((uint64_t)cg.kh * cg.kw * g.cblocks > 64) return false;
     g.w_bytes = (uint32_t)(cg.kh * cg.kw * g.cblocks) * HBN * 128;
     g.tiles = (int64_t)g.n * g.nt_count * g.batch * g.tiles_h * g.tiles_w;
@@ -1257,7 +1310,8 @@ int launch_conv_halo(const T* x_nhwc, const T* wp, T* y, const ConvGeom& cg, Con
         const uint64_t dims[4] = {(uint64_t)cg.cin, (uint64_t)cg.w, (uint64_t)cg.h, (uint64_t)nb};
         const uint64_t strides[3] = {(uint64_t)cg.cin * 2, (uint64_t)cg.w * cg.cin * 2,
                                      (uint64_t)cg.h * cg.w * cg.cin * 2};
-        const uint32_t box[4] = {BK, (uint32_t)g.tw, g.sub_bytes / ((uint32_t)g.tw * 128), 1};
+        const uint32_t bw = (uint32_t)(g.shared ? g.pitch : g.tw);
+        const uint32_t box[4] = {BK, bw, g.sub_bytes / (bw * 128), 1};
         int rc = encode_tmap_tiled(&tx, tmap_dt<T>(), 4, x_nhwc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
@@ -1354,9 +1408,9 @@ struct ConvLaunch {
                     uint32_t hsmem = 0;
                     // The halo kernel takes a residual only through its TMA
                     // path, and not with a channels-last output.
-                    const bool halo = g_conv_variant == 0 && store_ok && (!e.residual || res_tma) &&
+                    const bool halo = g_conv_variant != 1 && store_ok && (!e.residual || res_tma) &&
                                       !(e.residual && out_layout == WIDEK_LAYOUT_CLAST) &&
-                                      halo_geometry(g, res_tma, hg, hsmem);
+                                      halo_geometry(g, res_tma, out_layout == WIDEK_LAYOUT_CLAST, hg, hsmem);
                     // The per-tap kernels read any input layout (staged or
                     // channels-last) but write and add in the N-first layout.
                     if (!halo && (out_layout != WIDEK_LAYOUT_NFIRST || res_layout != WIDEK_LAYOUT_NFIRST))
@@ -1443,7 +1497,7 @@ bool layout_ok(int l) { return l == WIDEK_LAYOUT_NFIRST || l == WIDEK_LAYOUT_PAC
 extern "C" {
 
 int widek_conv_set_variant(int variant) {
-    if (variant < 0 || variant > 1) return widek::set_error(WIDEK_ERR_INVALID, "conv: unknown variant %d", variant);
+    if (variant < 0 || variant > 2) return widek::set_error(WIDEK_ERR_INVALID, "conv: unknown variant %d", variant);
     widek::g_conv_variant = variant;
     return WIDEK_OK;
 }

@@ -8,6 +8,7 @@
 // BN / TN (so that a warp's B-tile reads are consecutive words: no bank
 // conflict, and its output stores are coalesced).
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace widek {
 namespace {
@@ -20,6 +21,10 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     constexpr int NT = (BM / TM) * (BN / TN);
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
+    // A programmatic dependent of this kernel (the recurrence after the RNN
+    // input projection) may start its set-up now; it waits for this grid's
+    // results before reading them.
+    sm100::grid_dep_launch_dependents();
     const int model = blockIdx.z;
     const int m0 = blockIdx.y * BM;
     const int o0 = blockIdx.x * BN;
@@ -125,12 +130,9 @@ struct SimtLaunch {
             gemm_simt_kernel<T, 32, 64, 16, 2, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
                                                                     (int)xrpb, yms, ybs);
         } else {
-            // 64x64 tiles of 64 threads with 8x8 outputs each: per k a lane
-            // reads 8 + 8 shared floats for 64 FMAs (4 FMAs per shared-memory
-            // wavefront, the FMA pipe's rate), where 4x4 tiles give 2
             dim3 grid((unsigned)((o + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)n);
             if (grid.y > 65535) return set_error(WIDEK_ERR_UNSUPPORTED, "linear (simt): m too large");
-            gemm_simt_kernel<T, 64, 64, 16, 8, 8><<<grid, 64, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
+            gemm_simt_kernel<T, 64, 64, 16, 4, 4><<<grid, 256, 0, st>>>(xp, wp, bp, yp, (int)m, (int)k, (int)o, act, w_ms, w_rs, xms, xbs,
                                                                     (int)xrpb, yms, ybs);
         }
         return check_launch("widek_linear_fwd_simt");

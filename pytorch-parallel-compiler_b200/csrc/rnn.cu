@@ -115,6 +115,10 @@ __global__ void __launch_bounds__(1024) rnn_cluster_kernel(RnnArgs a) {
         for (int gi = 0; gi < 4; ++gi)
             if (gi < G) v[gi] = to_f<T>(gxr[(size_t)gi * H]);
     };
+    // The projected gates come from the kernel before this one on the
+    // stream (launched as its programmatic dependent: everything above ran
+    // while it finished).
+    sm100::grid_dep_wait();
     if (pre && (int)threadIdx.x < bu && a.T > 0) load_gx(threadIdx.x, 0, gx_next);
 
     for (int t = 0; t < a.T; ++t) {
@@ -358,6 +362,10 @@ __global__ void __launch_bounds__(kRegThreads, 1) rnn_reg_kernel(RnnArgs a, int*
         for (int gi = 0; gi < 4; ++gi)
             if (gi < G) v[gi] = to_f<T>(gxr[(size_t)gi * H]);
     };
+    // The projected gates come from the kernel before this one on the
+    // stream (launched as its programmatic dependent: the W_hh register
+    // load, the state set-up and the cluster start ran while it finished).
+    sm100::grid_dep_wait();
     if (pre && tid < bu && a.T > 0) load_gx(tid, 0, gx_next);
 
     bool ok = true;
@@ -548,13 +556,15 @@ int launch_rnn_reg_k(const RnnArgs& a, int64_t n, size_t smem, cudaStream_t st) 
     cfg.blockDim = dim3(kRegThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = a.cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, device_error_ptr());
     if (e != cudaSuccess) return set_error(WIDEK_ERR_CUDA, "rnn: launch failed: %s", cudaGetErrorString(e));
     return check_launch("widek_rnn_fwd (register-resident)");
@@ -653,13 +663,15 @@ int launch_rnn(RnnArgs a, int64_t n, cudaStream_t st) {
     cfg.blockDim = dim3((unsigned)threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) return set_error(WIDEK_ERR_CUDA, "rnn: launch failed: %s", cudaGetErrorString(e));
     return check_launch("widek_rnn_fwd");

@@ -233,6 +233,19 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool is_bf16) {
 }  // namespace sm100
 }  // namespace widek
 
+// ---- programmatic dependent launch ------------------------------------------------
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel on the stream still runs; grid_dep_wait() blocks until
+// that kernel has completed and its writes are visible (it returns at once
+// when there is no such dependency). grid_dep_launch_dependents() lets the
+// dependent kernel be scheduled before this one ends.
+namespace widek {
+namespace sm100 {
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+}  // namespace sm100
+}  // namespace widek
+
 // ---- cluster helpers -----------------------------------------------------------
 namespace widek {
 namespace sm100 {

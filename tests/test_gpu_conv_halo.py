@@ -1,6 +1,8 @@
 """GPU parity of the halo-reuse convolution kernel (variant 0, where it
-applies: 64-channel output tiles, output width a multiple of 8) and the
-per-tap kernel (variant 1) against the float64 oracle, which restates the
+applies: 64-channel output tiles, output width a multiple of 8; variant 2,
+its form with one shared halo buffer per 8 x 16 tile whose taps start at
+row offsets inside the 128-byte swizzle pattern) and the per-tap kernel
+(variant 1) against the float64 oracle, which restates the
 reference's grouped conv (wide_compiler/core/primitives/wide_conv2d.py:169-194).
 """
 import pytest
@@ -49,7 +51,7 @@ SHAPES = [
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "-".join(str(v) for v in s))
-@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("variant", [0, 1, 2])
 def test_conv_halo_vs_oracle(shape, variant):
     n, b, cin, cout, sp, k, p, d = shape
     x, w, bb = _case(n, b, cin, cout, sp, k, seed=sum(sp) + cin + k)
@@ -61,8 +63,9 @@ def test_conv_halo_vs_oracle(shape, variant):
     no_device_error()
 
 
+@pytest.mark.parametrize("variant", [0, 2])
 @pytest.mark.parametrize("residual_first", [False, True])
-def test_conv_halo_fused_epilogue(residual_first):
+def test_conv_halo_fused_epilogue(residual_first, variant):
     """Folded BatchNorm scale/shift, ReLU and a residual, as the fused
     ResBlock convs use them, on the halo kernel."""
     n, b, c, hw = 2, 3, 64, 16
@@ -71,7 +74,7 @@ def test_conv_halo_fused_epilogue(residual_first):
     sc = (torch.rand(n * c, generator=gen) + 0.5).to(torch.bfloat16)
     sh = (torch.randn(n * c, generator=gen) * 0.1).to(torch.bfloat16)
     res = torch.randn(n, b, c, hw, hw, generator=gen).to(torch.bfloat16)
-    y = _run(0, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), scale=sc.to(DEV),
+    y = _run(variant, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), scale=sc.to(DEV),
              shift=sh.to(DEV), residual=res.to(DEV), act=ops.ACT_RELU, residual_first=residual_first)
     v = O.conv_nd(x, w, bb, n, (1, 1), (1, 1), (1, 1)) * sc.double().view(n, 1, c, 1, 1) + \
         sh.double().view(n, 1, c, 1, 1)
@@ -99,8 +102,9 @@ def test_conv_halo_many_models_weight_reloads():
     no_device_error()
 
 
+@pytest.mark.parametrize("variant", [0, 2])
 @pytest.mark.parametrize("ow", [8, 16, 24, 40])
-def test_conv_halo_packed_residual_edges(ow):
+def test_conv_halo_packed_residual_edges(ow, variant):
     """The halo kernel's TMA-stored packed output and TMA-loaded packed
     residual at ragged tile edges (rows past the image, a half-used
     16-pixel tile width)."""
@@ -109,9 +113,30 @@ def test_conv_halo_packed_residual_edges(ow):
     gen = torch.Generator().manual_seed(ow + 1)
     res = torch.randn(n, b, c, oh, ow, generator=gen).to(torch.bfloat16)
     pk = lambda t: t.transpose(0, 1).reshape(b, n * c, oh, ow).contiguous()
-    y = _run(0, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), residual=pk(res).to(DEV),
+    y = _run(variant, x.to(DEV), w.to(DEV), bb.to(DEV), n, (1, 1), (1, 1), (1, 1), residual=pk(res).to(DEV),
              out_layout=ops.LAYOUT_PACKED, res_layout=ops.LAYOUT_PACKED)
     assert y is not None and y.shape == (b, n * c, oh, ow)
     ref = O.conv_nd(x, w, bb, n, (1, 1), (1, 1), (1, 1)) + res.double()
     assert_lowp_close(y.reshape(b, n, c, oh, ow).transpose(0, 1), ref)
+    no_device_error()
+
+
+@pytest.mark.parametrize("variant", [0, 2])
+def test_conv_halo_channels_last_chain(variant):
+    """conv1 -> conv2 as the fused ResBlock runs them: packed input, conv1
+    writing channels-last (the 128-byte swizzled [pixel][channel] staging),
+    conv2 reading it and adding the packed residual, packed output."""
+    n, b, c, hw = 3, 2, 64, 32
+    x, w1, b1 = _case(n, b, c, c, (hw, hw), 3, seed=41)
+    _, w2, b2 = _case(n, b, c, c, (hw, hw), 3, seed=42)
+    pk = lambda t: t.transpose(0, 1).reshape(b, n * c, hw, hw).contiguous()
+    xp = pk(x).to(DEV)
+    h = _run(variant, xp, w1.to(DEV), b1.to(DEV), n, (1, 1), (1, 1), (1, 1), act=ops.ACT_RELU,
+             in_layout=ops.LAYOUT_PACKED, out_layout=ops.LAYOUT_CLAST)
+    assert h is not None and h.shape == (n, b, hw, hw, c)
+    y = _run(variant, h, w2.to(DEV), b2.to(DEV), n, (1, 1), (1, 1), (1, 1), residual=xp,
+             in_layout=ops.LAYOUT_CLAST, out_layout=ops.LAYOUT_PACKED, res_layout=ops.LAYOUT_PACKED)
+    h_ref = torch.relu(O.conv_nd(x, w1, b1, n, (1, 1), (1, 1), (1, 1))).to(torch.bfloat16)
+    ref = O.conv_nd(h_ref, w2, b2, n, (1, 1), (1, 1), (1, 1)) + x.double()
+    assert_lowp_close(y.reshape(b, n, c, hw, hw).transpose(0, 1), ref)
     no_device_error()
