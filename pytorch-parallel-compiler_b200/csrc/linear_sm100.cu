@@ -319,11 +319,253 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair form (cta_group::2): a cluster of 2 CTAs on 2 SMs computes a
+// 256 x 256 tile. CTA r loads rows [r*128, r*128+128) of the x tile and rows
+// [r*128, r*128+128) of the w tile, so per MMA each SM reads 8 KB of operands
+// from its shared memory instead of 12 KB (and its TMA writes 32 KB per k
+// block instead of 48 KB); the leader (r = 0) issues M=256, N=256 MMAs that
+// read both CTAs' shared memory and write each CTA's 128 accumulator rows
+// into its own TMEM. Both CTAs' TMA loads count their bytes on the leader's
+// "full" barrier; the leader's commits arrive on the "empty" / "tmem full"
+// barriers of both CTAs; each CTA's two epilogue warpgroups (as in
+// linear_tc_kernel, one 128-column half each) release the accumulator on
+// the leader's "tmem empty" barrier (remote arrive).
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+
+template <bool TMA_STORE>
+struct PairSmem {
+    static constexpr uint32_t A_BYTES = 128 * BK * 2;
+    static constexpr uint32_t B_BYTES = 128 * BK * 2;
+    static constexpr uint32_t RING = kPairStages * (A_BYTES + B_BYTES);
+    static constexpr uint32_t OUT_CHUNK = 128 * 32 * 2;
+    static constexpr uint32_t OUT_BYTES = TMA_STORE ? 4 * OUT_CHUNK : 0;
+    static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + 8 * (2 * kPairStages + 5) + 16;
+};
+
+template <typename T, bool TMA_STORE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    linear_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                          const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias, T* __restrict__ y,
+                          int n_models, int M, int K, int O, int act, int vec_store, GemmRows rw, int* err) {
+    using S = PairSmem<TMA_STORE>;
+    constexpr int BN2 = 256;                 // N per pair tile (and per CTA accumulator)
+    constexpr uint32_t IDESC = idesc_f16(256, BN2, std::is_same<T, __nv_bfloat16>::value);
+    constexpr uint32_t TMEM_COLS = 2 * BN2;
+    constexpr int STAGES = kPairStages;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * S::A_BYTES;
+    uint8_t* sOut = smem + S::RING;     // [2 warpgroups][2][128 rows][64 B], 64-byte swizzled
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::OUT_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int mt_count = (M + 255) / 256;
+    const int nt_count = (O + BN2 - 1) / BN2;
+    const int kb_count = (K + BK - 1) / BK;
+    const int tiles = n_models * mt_count * nt_count;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * 8 * 32);   // both CTAs' epilogue threads
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+        if (TMA_STORE) tma_prefetch_desc(&tm_y);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();                      // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // TMA producer (both CTAs); bytes land on the leader's full barrier.
+        const uint64_t pol_x = l2_policy_evict_last();
+        const uint64_t pol_w = l2_policy_evict_first();
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int tile = pair; tile < tiles && ok; tile += npairs) {
+            const int mt = tile % mt_count;
+            const int rest = tile / mt_count;
+            const int nt = rest % nt_count;
+            const int model = rest / nt_count;
+            const int row0 = mt * 256 + (int)rank * 128;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (S::A_BYTES + S::B_BYTES));
+                    const uint32_t leader_full = map_to_rank(smem_addr(&full[s]), 0);
+                    tma_load_4d_pair(sA + s * S::A_BYTES, &tm_x, leader_full, kb * BK, row0 % rw.rpb, row0 / rw.rpb,
+                                     model, pol_x);
+                    tma_load_3d_pair(sB + s * S::B_BYTES, &tm_w, leader_full, kb * BK, nt * BN2 + (int)rank * 128,
+                                     model, pol_w);
+                }
+                __syncwarp();
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            // This CTA's copies count on the leader's barrier; give them time
+            // to land (bounded) before the CTA's shared memory is released.
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 1000000ull) { }
+        }
+    } else if (warp == 1) {
+        if (rank == 0 && lane == 0) {
+            // MMA issuer (leader CTA, one thread; descriptors formed once)
+            int s = 0, local = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
+            const uint64_t b_desc0 = sdesc_kmajor_sw128(smem_addr(sB));
+            for (int tile = pair; tile < tiles && ok; tile += npairs, ++local) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN2;
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = a_desc0 + (uint64_t)((s * S::A_BYTES) >> 4);
+                    const uint64_t bd = b_desc0 + (uint64_t)((s * S::B_BYTES) >> 4);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_f16_ss_pair(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+                    umma_commit_pair_mc(&empty[s], 0x3);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit_pair_mc(&tfull[acc], 0x3);
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            }
+            umma_commit_pair_mc(done, 0x1);
+            const volatile int never = 0;
+            mbar_wait(done, 0, &never);
+        }
+        __syncwarp();
+    } else {
+        // Epilogue: warpgroup wg (warps 2..5, 6..9) drains the column half
+        // [wg*128, wg*128+128) of this CTA's 128 accumulator rows, TMEM lane
+        // quarter q = warp % 4, as in linear_tc_kernel.
+        const int q = warp & 3;
+        const int wg = (warp - 2) >> 2;
+        const int ep_tid = threadIdx.x - 64 - 128 * wg;
+        uint8_t* sOutW = sOut + wg * 2 * S::OUT_CHUNK;
+        const uint32_t leader_tempty0 = map_to_rank(smem_addr(&tempty[0]), 0);
+        int oc = 0;
+        int local = 0;
+        for (int tile = pair; tile < tiles; tile += npairs, ++local) {
+            const int mt = tile % mt_count;
+            const int rest = tile / mt_count;
+            const int nt = rest % nt_count;
+            const int model = rest / nt_count;
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const int rloc = q * 32 + lane;
+            const int row0 = mt * 256 + (int)rank * 128;
+            const int row = row0 + rloc;
+            const bool row_ok = row < M;
+            const int rr = row_ok ? row : 0;
+            T* yrow = y + (int64_t)model * rw.y_ms + (int64_t)(rr / rw.rpb) * rw.y_bs + (int64_t)(rr % rw.rpb) * O;
+            const T* brow = bias ? bias + (int64_t)model * O : nullptr;
+#pragma unroll 1
+            for (int c = wg * (BN2 / 2); c < (wg + 1) * (BN2 / 2); c += 32) {
+                const int col0 = nt * BN2 + c;
+                if (col0 >= O) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN2 + c) + ((uint32_t)(q * 32) << 16), r);
+                const float my_bias = (brow && col0 + lane < O) ? to_f<T>(brow[col0 + lane]) : 0.f;
+                tmem_ld_wait();
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_bias, j);
+                act_chunk(v, act);
+                if (TMA_STORE) {
+                    // Rows past M of the last tile are clipped by the store;
+                    // a CTA whose 128 rows all lie past M stores nothing.
+                    uint8_t* buf = sOutW + (oc & 1) * S::OUT_CHUNK;
+                    if (ep_tid == 0) bulk_wait_read1();
+                    wg_bar_sync(wg);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int phys = j ^ ((rloc >> 1) & 3);
+                        store16<T>(reinterpret_cast<T*>(buf + rloc * 64 + phys * 16), v + 8 * j);
+                    }
+                    fence_proxy_async_smem();
+                    wg_bar_sync(wg);
+                    if (ep_tid == 0 && row0 < M) {
+                        tma_store_4d(&tm_y, buf, col0, row0 % rw.rpb, row0 / rw.rpb, model);
+                        bulk_commit();
+                    }
+                    ++oc;
+                } else if (row_ok) {
+                    if (vec_store && col0 + 32 <= O) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) store16<T>(yrow + col0 + j, v + j);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < O) yrow[col0 + j] = from_f<T>(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_remote(leader_tempty0 + acc * 8);
+        }
+        if (TMA_STORE && ep_tid == 0) bulk_wait0();
+    }
+
+    tc_fence_before();
+    cluster_sync_all();                      // no CTA leaves while its pair may still touch its smem / TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
 // Kernel selection (set with widek_linear_set_variant, for measurements):
-// 0 = automatic, 1 = single-CTA tiles (as 0), 3 = 128x128 tiles with a
-// 6-stage ring, 4 = as 1 without L2 hints, 5 = direct stores instead of the
-// TMA store. (2, CTA-pair tiles, measured slower on every shape and was
-// removed.)
+// 0 = automatic, 1 = single-CTA tiles, 2 = CTA-pair 256x256 tiles when
+// m > 128 and o > 128, 3 = 128x128 tiles with a 6-stage ring, 4 = as 1
+// without L2 hints, 5 = direct stores instead of the TMA store.
 int g_linear_variant = 0;
 
 template <typename T>
@@ -399,8 +641,61 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
 }
 
 template <typename T>
+int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
+                   const LinRows& rows, cudaStream_t st) {
+    uint32_t tb, bb;
+    if (!tile_box(rows, tb, bb)) return set_error(WIDEK_ERR_UNSUPPORTED, "linear: row blocks of %lld rows",
+                                                  (long long)rows.rpb);
+    CUtensorMap tx, tw;
+    {
+        const uint64_t dims[4] = {(uint64_t)k, (uint64_t)rows.rpb, (uint64_t)rows.nblk, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)k * 2, (uint64_t)rows.x_bs * 2, (uint64_t)rows.x_ms * 2};
+        const uint32_t box[4] = {BK, tb, bb, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dtype<T>(), 4, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[3] = {(uint64_t)k, (uint64_t)o, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)o * k * 2};
+        const uint32_t box[3] = {BK, 128, 1};
+        int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    const int vec_store = (o % 8 == 0) && aligned16(y);
+    CUtensorMap ty;
+    memset(&ty, 0, sizeof(ty));
+    if (vec_store) {
+        const uint64_t dims[4] = {(uint64_t)o, (uint64_t)rows.rpb, (uint64_t)rows.nblk, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)o * 2, (uint64_t)rows.y_bs * 2, (uint64_t)rows.y_ms * 2};
+        const uint32_t box[4] = {32, tb, bb, 1};
+        int rc = encode_tmap_tiled(&ty, tmap_dtype<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
+    }
+    const int dev = current_device();
+    const int64_t tiles = n * ((m + 255) / 256) * ((o + 255) / 256);
+    const int pairs = (int)std::min<int64_t>(tiles, sm_count(dev) / 2);
+    const GemmRows rw{(int)rows.rpb, rows.y_ms, rows.y_bs};
+    auto launch = [&](auto kern, uint32_t smem_bytes, bool& attr_done) -> int {
+        if (!attr_done) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes) !=
+                cudaSuccess)
+                return set_error(WIDEK_ERR_CUDA, "linear: cannot reserve %u bytes of shared memory", smem_bytes);
+            attr_done = true;
+        }
+        kern<<<2 * pairs, kGemmThreads, smem_bytes, st>>>(tx, tw, ty, bias, y, (int)n, (int)m, (int)k, (int)o, act,
+                                                           vec_store, rw, device_error_ptr());
+        return check_launch("widek_linear_fwd (tcgen05 pair)");
+    };
+    static bool attr_store[64] = {false}, attr_plain[64] = {false};
+    const int d = (dev >= 0 && dev < 64) ? dev : 0;
+    if (vec_store) return launch(linear_tc_pair_kernel<T, true>, PairSmem<true>::TOTAL, attr_store[d]);
+    return launch(linear_tc_pair_kernel<T, false>, PairSmem<false>::TOTAL, attr_plain[d]);
+}
+
+template <typename T>
 int linear_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
               const LinRows& r, cudaStream_t st) {
+    if (g_linear_variant == 2 && o > 128 && m > 128) return launch_tc_pair<T>(x, w, bias, y, n, m, k, o, act, r, st);
     if (g_linear_variant == 3 && o > 64) return launch_tc<T, 128, 6>(x, w, bias, y, n, m, k, o, act, r, st);
     // Output through shared memory + TMA store when the output rows are
     // 16-byte aligned (o % 8 == 0); variant 5 keeps direct stores.
@@ -443,8 +738,7 @@ int linear_entry(const void* x, const void* w, const void* bias, void* y, int64_
 }  // namespace widek
 
 extern "C" int widek_linear_set_variant(int variant) {
-    if (variant < 0 || variant > 5 || variant == 2)
-        return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
+    if (variant < 0 || variant > 5) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
     widek::g_linear_variant = variant;
     return WIDEK_OK;
 }

@@ -236,3 +236,32 @@ def test_linear_packed_rows(n, b, t, k, o, dtype, inp, outp):
         assert_fp32_close(ref if not outp else y, O.linear(x, w, bias) if not outp else
                           O.nfirst_to_packed(O.linear(x, w, bias)).reshape(b, n * t, o))
     no_device_error()
+
+
+@pytest.mark.parametrize("n,m,k,o", [(2, 256, 1024, 512), (3, 300, 200, 264), (1, 129, 64, 136), (4, 512, 256, 1024),
+                                     (2, 8192, 512, 1536)])
+def test_linear_pair_tiles_match_single_cta(n, m, k, o):
+    """CTA-pair (cta_group::2, 256x256 per pair) tiles against single-CTA
+    tiles and the oracle: the same products in the same k order, so the
+    results agree bit for bit."""
+    from wide_compiler import _native
+    x, w, b = _rand_linear(n, m, k, o, torch.bfloat16, seed=m + o)
+    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+    lib = _native.lib()
+    try:
+        _native.check(lib.widek_linear_set_variant(1), "variant")
+        y1 = ops.linear(xd, wd, bd)
+        _native.check(lib.widek_linear_set_variant(2), "variant")
+        y2 = ops.linear(xd, wd, bd)
+        y2p = None
+        if m % 32 == 0:
+            # packed [B, n*T, k] rows (T = 32, B = m / 32): 4-D row-block maps
+            xp = xd.view(n, m // 32, 32, k).transpose(0, 1).reshape(m // 32, n * 32, k).contiguous()
+            y2p = ops.linear_layout(xp, wd, bd, ops.ACT_NONE, True, False)
+    finally:
+        lib.widek_linear_set_variant(0)
+    assert torch.equal(y1, y2)
+    if y2p is not None:
+        assert torch.equal(y2p.reshape(y2.shape), y2)
+    assert_lowp_close(y1[:, :64], O.linear(x[:, :64], w, b))
+    no_device_error()
