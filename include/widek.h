@@ -118,8 +118,9 @@ WIDEK_API int widek_linear_fwd_ex(const void* x, const void* w, const void* bias
 
 /* Selects the tensor-core tiling of widek_linear_fwd for this process:
  * 0 = automatic (single-CTA 128xBN tiles), 1 = single-CTA tiles,
+ * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128,
  * 3 = single-CTA 128x128 tiles (6-stage ring), 4 = as 1 without L2 hints,
- * 5 = direct global stores instead of the TMA store (2 is not a variant).
+ * 5 = direct global stores instead of the TMA store.
  * A measurement knob (process-wide, not synchronized with running calls).
  * No counterpart in the reference. */
 WIDEK_API int widek_linear_set_variant(int variant);
@@ -513,7 +514,8 @@ WIDEK_API int widek_attention_fwd(const void* q, const void* k, const void* v, v
                                   int dtype, void* stream);
 
 /* Kernel choice for widek_attention_fwd: 0 = tcgen05/TMEM flash kernel
- * where it applies (bf16/f16, head_dim 64, no explicit mask), else the
+ * where it applies (bf16/f16, head_dim 64; causal or not, with or without
+ * an explicit bool / additive mask of any strides), else the
  * warp-level MMA or CUDA-core kernels (default); 1 = never the tcgen05
  * kernel; 10 + k (k = 0, 1, 2) = as 0, with k of every 4 column pairs of
  * exponentials computed by an FMA-pipe polynomial instead of the

@@ -20,7 +20,7 @@ struct AttnArgs {
 };
 
 // Launches the tcgen05/TMEM flash kernel (attention_sm100.cu) when the call
-// fits it (bf16/f16, head_dim 64, no explicit mask, positive scale, 16-byte
+// fits it (bf16/f16, head_dim 64, any mask kind, positive scale, 16-byte
 // aligned rows). Returns WIDEK_ERR_UNSUPPORTED without launching anything
 // when it does not, so that the caller can take another kernel.
 template <typename T>

@@ -219,11 +219,87 @@ __device__ __forceinline__ void item_of(int w, int nqb, int& bh, int& qb) {
     qb = nqb - 1 - w % nqb;
 }
 
-template <typename T, int NPOLY>
+// Explicit attention mask (wide_attention.py:223-228 passes attn_mask to
+// scaled_dot_product_attention): element (b, h, q, k) at
+// b*sb + h*sh + q*sq + k*sk of a bool (uint8: nonzero = attend) or additive
+// (T or fp32) tensor. The softmax works on raw scores s (scaled into the
+// log2 domain by sl2 = scale*log2(e) later), so an additive value m enters
+// as s + m / scale and a masked-out key as s = -inf.
+struct AttnMaskArgs {
+    const void* p;
+    int kind;                   // 1 bool, 2 additive T, 3 additive fp32
+    int vec;                    // 16-byte loads along the keys: unit key stride, 16-byte aligned rows, tk % vector == 0
+    int64_t sb, sh, sq, sk;
+    float inv_scale;
+};
+
+template <typename T>
+__device__ __forceinline__ void attn_apply_mask(const AttnMaskArgs& mk, int b, int h, int qrow, int kbase, int tk,
+                                                float (&s)[kKT]) {
+    const int64_t base = (int64_t)b * mk.sb + (int64_t)h * mk.sh + (int64_t)qrow * mk.sq;
+    if (mk.kind == 1) {
+        const uint8_t* m = static_cast<const uint8_t*>(mk.p) + base;
+        if (mk.vec) {
+#pragma unroll
+            for (int g = 0; g < kKT / 16; ++g) {
+                if (kbase + 16 * g < tk) {
+                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(m + kbase + 16 * g));
+                    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        if (((w4[e >> 2] >> (8 * (e & 3))) & 0xffu) == 0u) s[16 * g + e] = -INFINITY;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < kKT; ++c)
+                if (kbase + c < tk && m[(int64_t)(kbase + c) * mk.sk] == 0) s[c] = -INFINITY;
+        }
+        return;
+    }
+    if (mk.kind == 2) {
+        const T* m = static_cast<const T*>(mk.p) + base;
+        if (mk.vec) {
+#pragma unroll
+            for (int g = 0; g < kKT / 8; ++g) {
+                if (kbase + 8 * g < tk) {
+                    float f[8];
+                    load16<T>(m + kbase + 8 * g, f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) s[8 * g + e] = fmaf(f[e], mk.inv_scale, s[8 * g + e]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < kKT; ++c)
+                if (kbase + c < tk) s[c] = fmaf(to_f<T>(m[(int64_t)(kbase + c) * mk.sk]), mk.inv_scale, s[c]);
+        }
+        return;
+    }
+    const float* m = static_cast<const float*>(mk.p) + base;
+    if (mk.vec) {
+#pragma unroll
+        for (int g = 0; g < kKT / 4; ++g) {
+            if (kbase + 4 * g < tk) {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(m + kbase + 4 * g));
+                s[4 * g] = fmaf(f.x, mk.inv_scale, s[4 * g]);
+                s[4 * g + 1] = fmaf(f.y, mk.inv_scale, s[4 * g + 1]);
+                s[4 * g + 2] = fmaf(f.z, mk.inv_scale, s[4 * g + 2]);
+                s[4 * g + 3] = fmaf(f.w, mk.inv_scale, s[4 * g + 3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < kKT; ++c)
+            if (kbase + c < tk) s[c] = fmaf(m[(int64_t)(kbase + c) * mk.sk], mk.inv_scale, s[c]);
+    }
+}
+
+template <typename T, int NPOLY, bool MASKED>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o, int heads,
-                   int items, int tq, int tk, int causal, float sl2, int* err) {
+                   int items, int tq, int tk, int causal, float sl2, AttnMaskArgs mk, int* err) {
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr uint32_t IDESC_S = idesc_f16(kQT, kKT, kBf16);
     constexpr uint32_t IDESC_PV = idesc_f16(kQT, kHD, kBf16) | (1u << 16);   // B (V) MN-major
@@ -512,6 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 mbar_arrive(&s_free[i]);
 
+                if constexpr (MASKED) {
+                    if (qrow < tq) attn_apply_mask<T>(mk, bh / heads, bh % heads, qrow, kbase, tk, s);
+                }
                 const bool need_mask = (kbase + kKT > tk) || (causal && kbase + kKT - 1 > wrow0);
                 if (need_mask) {
                     const int lim = causal ? min(tk - kbase, qrow - kbase + 1) : tk - kbase;
@@ -678,10 +757,10 @@ int rows_map(CUtensorMap* m, const void* base, int64_t stride, int t, int nb, in
     return encode_tmap_tiled(m, tmap_dtype<T>(), 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <typename T, int NPOLY>
+template <typename T, int NPOLY, bool MASKED = false>
 int launch_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& o,
               const AttnArgs& a, cudaStream_t st) {
-    auto kern = attn_tc_kernel<T, NPOLY>;
+    auto kern = attn_tc_kernel<T, NPOLY, MASKED>;
     static bool attr_done[64] = {false};
     const int dev = current_device();
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
@@ -700,8 +779,16 @@ int launch_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, 
     int64_t grid = std::min<int64_t>(items, std::max(1, sm_count(dev)));
     while (grid > 1 && std::gcd(grid, nqb) != 1) --grid;
     const float sl2 = a.scale * 1.4426950408889634f;
+    AttnMaskArgs mk{};
+    if (MASKED) {
+        const int64_t es = a.mask_kind == 1 ? 1 : (a.mask_kind == 2 ? (int64_t)sizeof(T) : 4);
+        const int64_t vlen = 16 / es;
+        mk = AttnMaskArgs{a.mask, a.mask_kind, 0, a.ms_b, a.ms_h, a.ms_q, a.ms_k, 1.f / a.scale};
+        mk.vec = a.ms_k == 1 && aligned16(a.mask) && (a.ms_q * es) % 16 == 0 && (a.ms_h * es) % 16 == 0 &&
+                 (a.ms_b * es) % 16 == 0 && a.tk % vlen == 0;
+    }
     kern<<<(unsigned)grid, kThreads, Smem::TOTAL, st>>>(q, k, v, o, a.heads, (int)items, a.tq, a.tk, a.causal,
-                                                        sl2, device_error_ptr());
+                                                        sl2, mk, device_error_ptr());
     return check_launch("widek_attention_fwd (tcgen05)");
 }
 
@@ -713,7 +800,8 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st) {
         return WIDEK_ERR_UNSUPPORTED;
     } else {
         const int64_t width = (int64_t)a.heads * kHD;
-        const bool fits = a.dh == kHD && a.mask_kind == 0 && a.scale > 0.f && a.tk > 0 &&
+        const bool fits = a.dh == kHD && a.mask_kind >= 0 && a.mask_kind <= 3 && (a.mask_kind == 0 || a.mask) &&
+                          a.scale > 0.f && a.tk > 0 &&
                           a.sq % 8 == 0 && a.sk % 8 == 0 && a.sv % 8 == 0 && a.so % 8 == 0 &&
                           a.sq >= width && a.sk >= width && a.sv >= width && a.so >= width &&
                           aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.o);
@@ -724,6 +812,7 @@ int launch_attn_tc(const AttnArgs& a, cudaStream_t st) {
         if (!rc) rc = rows_map<T>(&tv_, a.v, a.sv, a.tk, a.nb, a.heads, kKT);
         if (!rc) rc = rows_map<T>(&to_, a.o, a.so, a.tq, a.nb, a.heads, 32);
         if (rc) return rc;
+        if (a.mask_kind != 0) return launch_tc<T, 1, true>(tq_, tk_, tv_, to_, a, st);
         switch (attn_poly_pairs()) {
             case 0: return launch_tc<T, 0>(tq_, tk_, tv_, to_, a, st);
             case 2: return launch_tc<T, 2>(tq_, tk_, tv_, to_, a, st);

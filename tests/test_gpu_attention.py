@@ -119,3 +119,57 @@ def test_attention_cfg5_full_size_sampled():
         ref = _ref(sub, xs, xs, xs, causal=True)
         assert_lowp_close(y[i:i + 1, j:j + 1], ref)
     no_device_error()
+
+
+def _kernels_run(fn):
+    """Names of the CUDA kernels ``fn`` launches (torch profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+@pytest.mark.parametrize("kind", ['bool', 'float', 'float32', 'per_head'])
+@pytest.mark.parametrize("t,causal", [(80, False), (75, False), (200, True)])
+def test_attention_masks_on_tcgen05(kind, t, causal):
+    """Explicit masks (wide_attention.py:223-228) run on the tcgen05 flash
+    kernel: bool (attend where true) and additive (bf16 or fp32) masks,
+    broadcast [T, T] or per (sample, head), vectorised (T a multiple of the
+    16-byte vector) and scalar (T = 75) mask reads, alone and with the causal
+    mask; rows whose keys are all masked give zeros, as the other kernels."""
+    n, b, d, h = 2, 2, 256, 4
+    m = _mod(n, d, h, torch.bfloat16, 21 + t)
+    x = torch.randn(n, b, t, d, device=DEV).to(torch.bfloat16)
+    g = torch.Generator(device=DEV).manual_seed(t)
+    if kind == 'bool':
+        mask = torch.rand(t, t, device=DEV, generator=g) > 0.4
+        mask[:, 0] = True
+        mask[3, :] = False                   # one query attends nothing
+    elif kind == 'float':
+        mask = torch.randn(t, t, device=DEV, generator=g).to(torch.bfloat16)
+    elif kind == 'float32':
+        mask = torch.randn(t, t, device=DEV, generator=g)
+    else:
+        mask = torch.randn(n * b, h, t, t, device=DEV, generator=g).to(torch.bfloat16)
+    names = _kernels_run(lambda: m(x, attn_mask=mask, is_causal=False) if not causal else None)
+    if not causal:
+        assert any('attn_tc_kernel' in s for s in names), names
+    y = m(x, attn_mask=mask) if not causal else None
+    if causal:
+        # is_causal with an explicit mask is rejected (SDPA's rule); the
+        # causal + mask combination is the mask with the upper triangle off
+        tri = torch.ones(t, t, device=DEV, dtype=torch.bool).tril()
+        cm = (mask & tri) if kind == 'bool' else mask.float().masked_fill(~tri, float('-inf')).to(mask.dtype)
+        y = m(x, attn_mask=cm)
+        ref = _ref(m, x, x, x, mask=cm)
+    else:
+        ref = _ref(m, x, x, x, mask=mask)
+    # a query with no attended key: zeros from the core (the oracle's
+    # softmax over only -inf gives NaN), so the module returns out_bias
+    nan_rows = torch.isnan(ref).any(dim=-1)
+    ref = torch.where(nan_rows[..., None], m.out_bias.detach().double().cpu()[:, None, None, :], ref)
+    assert_lowp_close(y, ref)
+    if kind == 'bool' and not causal:
+        assert torch.count_nonzero(y[:, :, 3].float() - m.out_bias[:, None, :].float()) == 0
+    no_device_error()
