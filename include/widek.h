@@ -88,8 +88,11 @@ WIDEK_API int widek_test_bounded_wait(uint64_t limit_ns, void* stream);
 /* y[i] = act(x[i] @ w[i]^T + bias[i]) for every model i in [0, n).
  *   x: [n, m, k], w: [n, o, k], bias: [n, o] or NULL, y: [n, m, o].
  * bf16/f16 with k % 8 == 0 and 16-byte aligned pointers run on the tcgen05
- * tensor-core kernel; every other case runs the CUDA-core kernel (fp32
- * FFMA, used for fp32 so results match fp32 arithmetic with TF32 off).
+ * tensor-core kernel. fp32 without an activation, with k % 4 == 0 and
+ * 16-byte aligned rows, runs on the tensor cores with each operand split
+ * into two bf16 parts (hi*hi + hi*lo + lo*hi accumulated in fp32: each
+ * product within ~2^-16 of the fp32 one, inside the fp32 tolerance with
+ * TF32 off); every other case runs the CUDA-core kernel (fp32 FFMA).
  * Replaces: wide_compiler/core/primitives/wide_linear.py:165
  *           (einsum 'noi,nbi->nbo') and :168 (bias add). */
 WIDEK_API int widek_linear_fwd(const void* x, const void* w, const void* bias, void* y,
@@ -120,7 +123,8 @@ WIDEK_API int widek_linear_fwd_ex(const void* x, const void* w, const void* bias
  * 0 = automatic (single-CTA 128xBN tiles), 1 = single-CTA tiles,
  * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128,
  * 3 = single-CTA 128x128 tiles (6-stage ring), 4 = as 1 without L2 hints,
- * 5 = direct global stores instead of the TMA store.
+ * 5 = direct global stores instead of the TMA store, 6 = fp32 always on the
+ * CUDA-core kernel (instead of the split-operand tensor-core kernel).
  * A measurement knob (process-wide, not synchronized with running calls).
  * No counterpart in the reference. */
 WIDEK_API int widek_linear_set_variant(int variant);

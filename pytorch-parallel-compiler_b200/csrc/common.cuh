@@ -46,6 +46,15 @@ int* device_error_ptr();
 // which reads the packed [B, n*T, k] boundary layout (x_ms = T*k,
 // x_bs = n*T*k, x_rpb = T) in place; y likewise with y_ms / y_bs and the
 // same row blocks (y_ms < 0: dense [n, m, o]).
+// fp32 grouped GEMM on the tensor cores with split bf16 operands (three
+// products per K step, gemm_f32x3.cu), same strided addressing as
+// linear_simt_strided (x_ms >= 0 required; x_rpb rows per block). Returns
+// WIDEK_ERR_UNSUPPORTED, launching nothing, when the shapes / alignment do
+// not fit it.
+int linear_f32x3_strided(const float* x, const float* w, const float* bias, float* y, int64_t n, int64_t m, int64_t k,
+                         int64_t o, int64_t w_ms, int64_t w_rs, int64_t x_ms, int64_t x_bs, int64_t x_rpb,
+                         int64_t y_ms, int64_t y_bs, cudaStream_t st);
+
 int linear_simt_strided(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m, int64_t k,
                         int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st,
                         int64_t x_ms = -1, int64_t x_bs = 0, int64_t x_rpb = 0, int64_t y_ms = -1,

@@ -565,7 +565,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 // Kernel selection (set with widek_linear_set_variant, for measurements):
 // 0 = automatic, 1 = single-CTA tiles, 2 = CTA-pair 256x256 tiles when
 // m > 128 and o > 128, 3 = 128x128 tiles with a 6-stage ring, 4 = as 1
-// without L2 hints, 5 = direct stores instead of the TMA store.
+// without L2 hints, 5 = direct stores instead of the TMA store, 6 = fp32 on
+// the CUDA-core kernel instead of the split-operand tensor-core kernel.
 int g_linear_variant = 0;
 
 template <typename T>
@@ -724,6 +725,14 @@ int linear_entry(const void* x, const void* w, const void* bias, void* y, int64_
     if (!tc_ok) {
         if (!x && k > 0) return set_error(WIDEK_ERR_INVALID, "linear: null x");
         if (!y) return set_error(WIDEK_ERR_INVALID, "linear: null y");
+        // fp32 without an activation: the split-operand tensor-core GEMM
+        // where it fits (products within ~2^-16 of fp32), else CUDA cores
+        if (dtype == WIDEK_F32 && act == WIDEK_ACT_NONE && g_linear_variant != 6) {
+            const int rc = linear_f32x3_strided(static_cast<const float*>(x), static_cast<const float*>(w),
+                                                static_cast<const float*>(bias), static_cast<float*>(y), n, m, k, o,
+                                                o * k, k, r.x_ms, r.x_bs, r.rpb, r.y_ms, r.y_bs, st);
+            if (rc != WIDEK_ERR_UNSUPPORTED) return rc;
+        }
         return linear_simt_strided(x, w, bias, y, n, m, k, o, o * k, k, dtype, act, st, r.x_ms, r.x_bs, r.rpb,
                                    r.y_ms, r.y_bs);
     }
@@ -738,7 +747,7 @@ int linear_entry(const void* x, const void* w, const void* bias, void* y, int64_
 }  // namespace widek
 
 extern "C" int widek_linear_set_variant(int variant) {
-    if (variant < 0 || variant > 5) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
+    if (variant < 0 || variant > 6) return widek::set_error(WIDEK_ERR_INVALID, "linear variant %d", variant);
     widek::g_linear_variant = variant;
     return WIDEK_OK;
 }

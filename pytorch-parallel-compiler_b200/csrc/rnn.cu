@@ -736,10 +736,20 @@ int rnn_fwd_entry(bool lstm, const void* x, const void* w_ih, const void* w_hh, 
         // x rows (b, t) of model i: N-first at i*batch*T*I + (b*T + t)*I,
         // packed [batch, n*T, I] at (b*n + i)*T*I + t*I
         const bool pin = in_layout == WIDEK_LAYOUT_PACKED;
-        const int rc = linear_simt_strided(x, w_ih, b_ih, workspace, n, batch * steps, input, g * hidden, ims, irs,
-                                           dtype, WIDEK_ACT_NONE, (cudaStream_t)stream,
-                                           pin ? steps * input : batch * steps * input,
-                                           pin ? n * steps * input : steps * input, steps);
+        const int64_t xms = pin ? steps * input : batch * steps * input;
+        const int64_t xbs = pin ? n * steps * input : steps * input;
+        const int64_t gsz = (int64_t)g * hidden;
+        // fp32: the split-operand tensor-core GEMM where it fits, else the
+        // CUDA-core kernel (both write the dense [n, batch*T, G*H] gates)
+        int rc = WIDEK_ERR_UNSUPPORTED;
+        if (dtype == WIDEK_F32)
+            rc = linear_f32x3_strided(static_cast<const float*>(x), static_cast<const float*>(w_ih),
+                                      static_cast<const float*>(b_ih), static_cast<float*>(workspace), n,
+                                      batch * steps, input, gsz, ims, irs, xms, xbs, steps, batch * steps * gsz,
+                                      steps * gsz, (cudaStream_t)stream);
+        if (rc == WIDEK_ERR_UNSUPPORTED)
+            rc = linear_simt_strided(x, w_ih, b_ih, workspace, n, batch * steps, input, gsz, ims, irs, dtype,
+                                     WIDEK_ACT_NONE, (cudaStream_t)stream, xms, xbs, steps);
         if (rc) return rc;
     }
     const bool pout = out_layout == WIDEK_LAYOUT_PACKED;

@@ -265,3 +265,30 @@ def test_linear_pair_tiles_match_single_cta(n, m, k, o):
         assert torch.equal(y2p.reshape(y2.shape), y2)
     assert_lowp_close(y1[:, :64], O.linear(x[:, :64], w, b))
     no_device_error()
+
+
+@pytest.mark.parametrize("n,m,k,o", [(3, 300, 100, 200), (2, 128, 64, 384), (4, 37, 256, 130), (1, 1000, 512, 64),
+                                     (2, 64, 102, 96)])
+def test_linear_fp32_split_tensor_core(n, m, k, o):
+    """fp32 WideLinear on the split-operand tensor-core kernel (hi/lo bf16
+    parts, three products per K step) against the fp64 oracle at the fp32
+    tolerance and against the CUDA-core kernel (linear variant 6); k = 102
+    (not a multiple of 4) takes the CUDA-core kernel."""
+    from wide_compiler import _native
+    x, w, b = _rand_linear(n, m, k, o, torch.float32, seed=m + k)
+    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+    lib = _native.lib()
+    y = ops.linear(xd, wd, bd)
+    try:
+        _native.check(lib.widek_linear_set_variant(6), "variant")
+        y_simt = ops.linear(xd, wd, bd)
+    finally:
+        lib.widek_linear_set_variant(0)
+    ref = O.linear(x, w, b)
+    assert_fp32_close(y, ref)
+    assert_fp32_close(y_simt, ref)
+    # the split products stay far inside the tolerance (each within ~2^-17
+    # of the fp32 product; the sums here are within a few 1e-5 of fp64)
+    err = (y.double().cpu() - ref).abs().max().item()
+    assert err <= 5e-5 * max(1.0, ref.abs().max().item()), err
+    no_device_error()
