@@ -77,7 +77,9 @@ def peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the GPU is busy."""
+    """Samples nvidia-smi clocks and throttle reasons while the GPU is busy.
+    nvidia-smi writes to a pseudo-terminal, so that it line-buffers and each
+    sample arrives (and is time-stamped) when it is taken."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -85,25 +87,46 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines = []
+        self.lines = []                  # (arrival time, line)
         self._t = None
+        self._fd = None
 
     def start(self):
         try:
+            import pty
+            master, slave = pty.openpty()
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdin=subprocess.DEVNULL, stdout=slave, stderr=subprocess.DEVNULL, close_fds=True)
+            os.close(slave)
+            self._fd = master
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
         except Exception:
             self.proc = None
+            return
+        # wait (bounded) for the first sample, so that a short run still has
+        # samples in its window
+        t0 = time.perf_counter()
+        while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 10.0:
+            time.sleep(0.02)
 
     def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        buf = b""
+        while True:
+            try:
+                chunk = os.read(self._fd, 4096)
+            except OSError:              # the terminal closes when nvidia-smi exits
+                break
+            if not chunk:
+                break
+            buf += chunk
+            while b"\n" in buf:
+                line, buf = buf.split(b"\n", 1)
+                self.lines.append((time.perf_counter(), line.decode(errors="replace").strip()))
 
     def mark(self):
-        return len(self.lines)
+        return time.perf_counter()
 
     def stop(self):
         if self.proc is None:
@@ -115,13 +138,20 @@ class ClockSampler:
             self.proc.kill()
         if self._t:
             self._t.join(timeout=2)
+        try:
+            os.close(self._fd)
+        except OSError:
+            pass
 
-    def summary(self, start=0, end=None):
+    def summary(self, start=0.0, end=None):
+        """Samples that arrived between the marks start and end."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines[start:end]:
+        for t, ln in list(self.lines):
+            if t < start or (end is not None and t > end):
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue

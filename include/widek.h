@@ -138,7 +138,12 @@ WIDEK_API int widek_linear_set_variant(int variant);
  *   y: [n, batch, dims[layers]] (out_layout NFIRST) or [batch, n*dims[layers]].
  * One CTA per model keeps the activations and one layer's weights in shared
  * memory; fp32 arithmetic, each layer's output rounded to the storage dtype
- * as a layer-by-layer run stores it. Returns WIDEK_ERR_UNSUPPORTED (launching
+ * as a layer-by-layer run stores it. fp32 chains whose layers are at most
+ * 128 wide and 256 deep (widths multiples of 4, 16-byte aligned tensors)
+ * with at least 2^21 multiply-adds per CTA run on tcgen05 instead: per layer D^T = W . h^T with the weights as the
+ * 128-row A operand and the batch rows as N, every fp32 operand split into
+ * bf16 hi + lo and accumulated as hi*hi + hi*lo + lo*hi in fp32 (each
+ * product within ~2^-17 of the fp32 one). Returns WIDEK_ERR_UNSUPPORTED (launching
  * nothing) when the chain does not fit (widek_mlp_chain_supported says in
  * advance). Replaces, for a TracedWideModel whose graph is such a chain, the
  * boundary unpack, the per-node WideLinear (wide_compiler/core/primitives/
@@ -154,6 +159,12 @@ WIDEK_API int widek_mlp_chain_fwd(const void* x, void* y, const void* const* wei
  * SM's shared memory), else 0. Launches nothing. */
 WIDEK_API int widek_mlp_chain_supported(const int64_t* dims, const int* acts, int layers, int64_t n,
                                         int64_t batch, int dtype);
+
+/* Kernel choice for fp32 chains: 0 = the CUDA-core kernel (default), 1 =
+ * the tcgen05 split-operand kernel wherever it fits (measured no faster at
+ * the sizes it fits). Process-wide; for tests and measurements. No
+ * reference counterpart. */
+WIDEK_API int widek_mlp_chain_set_variant(int variant);
 
 /* ---- WideLayerNorm ----------------------------------------------------- */
 

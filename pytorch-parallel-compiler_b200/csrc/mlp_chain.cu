@@ -28,7 +28,10 @@
 // (boundary unpack :467-468, one WideLinear per node with its einsum and bias
 // add wide_compiler/core/primitives/wide_linear.py:165-168, the activation
 // node, boundary pack :528-529) for chains whose weights fit on chip.
+#include <type_traits>
+
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace widek {
 namespace {
@@ -398,12 +401,337 @@ bool chain_plan(ChainArgs& a, int sms) {
     return false;
 }
 
+
+// ---------------------------------------------------------------------------
+// fp32 chains on the tensor cores (split bf16 operands)
+//
+// For fp32 chains whose layers are at most 128 wide (out) and 256 deep (in),
+// with at most 256 batch rows per CTA, each layer runs as
+//   D^T [dout x rows] = W [dout x din] . X^T
+// on tcgen05: the weights are the A operand (M = 128; rows past dout are
+// never written, and the accumulator rows they reach are dropped), the layer
+// input the B operand (N = the batch rows rounded up to 16), so a small batch
+// wastes little. Every fp32 operand is split into bf16 hi + lo parts and the
+// product accumulated in fp32 TMEM as hi*hi + hi*lo + lo*hi (three MMAs per
+// K step; each product within ~2^-17 of the fp32 one). The input rows and
+// every layer's weights arrive up front as bulk copies into an fp32 staging
+// area (one mbarrier), are split into the swizzled bf16 tiles, and the chain
+// then costs per layer one MMA round trip and one epilogue: all 8 warps read
+// the accumulator (one output feature per TMEM lane, 16 batch rows per
+// read), add the bias, apply the activation and either write the next
+// layer's split input tiles into shared memory or the result rows to global
+// memory (N-first or packed; consecutive lanes = consecutive features, so
+// the stores coalesce).
+// ---------------------------------------------------------------------------
+// Kernel choice for fp32 chains: 0 = the CUDA-core kernel (default), 1 =
+// the tensor-core kernel wherever its plan fits. At cfg1 (32 rows x
+// 64-128-64, the one size of that family whose fp32 staging plus bf16 tiles
+// fit in shared memory) it takes 11.07 us against 10.76 us for the CUDA-core
+// kernel: per CTA ~6 K cycles go to splitting the staged weights and ~2 K
+// to each MMA round trip, against the ~4 K cycles the FFMA layers save.
+// Set with widek_mlp_chain_set_variant (tests and measurements).
+int g_chain_variant = 0;
+
+constexpr int kTcThreads = 256;
+constexpr int kTcMaxRows = 256;      // batch rows per CTA (N of the MMAs)
+constexpr int kTcMaxIn = 256;        // din per layer (4 chunks of 64)
+constexpr int kTcOut = 128;          // dout per layer (M of the MMAs)
+constexpr int kTcLoadBatch = 16;
+
+struct ChainTcPlan {
+    int rows, np;                     // batch rows per CTA, N (rows rounded up to 16)
+    int kc[kChainMax];                // 64-wide K chunks per layer
+    uint32_t w_off[kChainMax];        // byte offset of layer l's hi tiles (lo tiles follow)
+    uint32_t w_bytes, x_bytes, smem;  // weights region, one activation buffer (hi + lo), total
+    uint32_t raw_w_off[kChainMax];    // fp32 staging of layer l's weights (bulk-copied) inside the raw region
+    uint32_t raw_bytes;               // fp32 staging: input rows, then every layer's weights
+    int tmem_cols;
+};
+
+__host__ __device__ inline uint32_t tc_tile_bytes(int rows) { return (uint32_t)rows * 128u; }   // [rows][64] bf16
+
+bool chain_tc_plan(const ChainArgs& a, ChainTcPlan& p) {
+    int max_kc = 0;
+    uint32_t w = 0;
+    for (int l = 0; l < a.layers; ++l) {
+        if (a.dims[l + 1] > kTcOut || a.dims[l] > kTcMaxIn || a.dims[l] % 4 != 0) return false;
+        p.kc[l] = (a.dims[l] + 63) / 64;
+        max_kc = max_kc > p.kc[l] ? max_kc : p.kc[l];
+        p.w_off[l] = w;
+        w += 2u * (uint32_t)p.kc[l] * tc_tile_bytes(kTcOut);
+    }
+    if (a.dims[a.layers] % 4 != 0) return false;
+    p.rows = a.batch < kTcMaxRows ? a.batch : kTcMaxRows;
+    p.np = (p.rows + 15) / 16 * 16;
+    p.w_bytes = w;
+    p.x_bytes = 2u * (uint32_t)max_kc * tc_tile_bytes(p.np);
+    uint32_t raw = (uint32_t)p.rows * a.dims[0] * 4;
+    for (int l = 0; l < a.layers; ++l) {
+        p.raw_w_off[l] = raw;
+        raw += (uint32_t)a.dims[l + 1] * a.dims[l] * 4;
+    }
+    p.raw_bytes = raw;
+    p.smem = 1024 + p.w_bytes + 2 * p.x_bytes + p.raw_bytes + 64;
+    int c = 32;
+    while (c < p.np) c <<= 1;
+    p.tmem_cols = c;
+    return p.smem <= (uint32_t)kChainSmemMax;
+}
+
+// Byte offset of element (r, kk) (kk < 64) in a 128-byte swizzled K-major
+// bf16 tile: row r at r*128, 16-byte chunk kk/8 at chunk ^ (r % 8).
+__device__ __forceinline__ uint32_t tc_off(int r, int kk) {
+    return (uint32_t)(r * 128 + ((((kk >> 3) ^ (r & 7)) << 4) | ((kk & 7) << 1)));
+}
+
+__device__ __forceinline__ void tc_split4(uint8_t* hi, uint8_t* lo, uint32_t off, float4 v) {
+    const float a4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t h2[2], l2[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a4[2 * q], a4[2 * q + 1]);
+        const float2 hf = __bfloat1622float2(h);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(a4[2 * q] - hf.x, a4[2 * q + 1] - hf.y);
+        h2[q] = *reinterpret_cast<const uint32_t*>(&h);
+        l2[q] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+    *reinterpret_cast<uint2*>(hi + off) = make_uint2(h2[0], h2[1]);
+    *reinterpret_cast<uint2*>(lo + off) = make_uint2(l2[0], l2[1]);
+}
+
+// Splits a [nrows][len] fp32 matrix staged densely in shared memory (row
+// stride len) into kc 64-wide chunk tiles of prow rows at dst (lo tiles after
+// the hi tiles); columns from len up to kc*64 become zeros. Rows from nrows
+// to prow are left as they are: an MMA row (weights) or column (inputs) only
+// reaches the accumulator row or column of the same index, which the
+// epilogue drops. Four float4 per thread are loaded before any is stored.
+__device__ __forceinline__ void tc_split_staged(uint8_t* dst, int kc, int prow, const float* raw, int nrows,
+                                                int len) {
+    const uint32_t tile = tc_tile_bytes(prow);
+    const int per_row = kc * 16;                 // float4 per padded row
+    const int total = nrows * per_row;
+    for (int i0 = threadIdx.x; i0 < total; i0 += 4 * kTcThreads) {
+        float4 v[4];
+        int r[4], c4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = i0 + u * kTcThreads;
+            r[u] = i / per_row;
+            c4[u] = i - r[u] * per_row;
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < total && 4 * c4[u] < len)
+                v[u] = *reinterpret_cast<const float4*>(raw + (size_t)r[u] * len + 4 * c4[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (i0 + u * kTcThreads < total) {
+                uint8_t* hi = dst + (uint32_t)(c4[u] >> 4) * tile;
+                tc_split4(hi, hi + (uint32_t)kc * tile, tc_off(r[u], (c4[u] & 15) * 4), v[u]);
+            }
+        }
+    }
+}
+
+// arr[i] for a kernel-parameter array by unrolled selects: a runtime index
+// into a parameter array would otherwise copy the array to local memory.
+template <typename T, int K>
+__device__ __forceinline__ T pick(const T (&arr)[K], int i) {
+    T v = arr[0];
+#pragma unroll
+    for (int u = 1; u < K; ++u) v = (i == u) ? arr[u] : v;
+    return v;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) mlp_chain_tc_kernel(ChainArgs a, ChainTcPlan p, int* err) {
+    using namespace sm100;
+    extern __shared__ uint8_t tc_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* wreg = sm;
+    uint8_t* const xbuf0 = sm + p.w_bytes;
+    uint8_t* const xbuf1 = xbuf0 + p.x_bytes;
+    uint8_t* rawp = sm + p.w_bytes + 2 * p.x_bytes;
+    uint64_t* done = reinterpret_cast<uint64_t*>(rawp + p.raw_bytes);
+    uint64_t* ld_bar = done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
+
+    const int model = blockIdx.x;
+    const int row0 = blockIdx.y * p.rows;
+    const int rows = min(p.rows, a.batch - row0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t n = a.n, B = a.batch;
+    const int d0 = a.dims[0];
+    const float* x = static_cast<const float*>(a.x);
+
+    if (tid == 0) {
+        mbar_init(done, 1);
+        mbar_init(ld_bar, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    // Input rows and every layer's weights as bulk copies into the fp32
+    // staging area (one copy per weight matrix; the N-first input block is
+    // contiguous, the packed input one copy per row), all in flight at once.
+    if (warp == 0) {
+        const uint64_t pol = l2_policy_evict_normal();
+        if (lane == 0) {
+            uint32_t bytes = (uint32_t)rows * d0 * 4;
+            for (int l = 0; l < a.layers; ++l) bytes += (uint32_t)pick(a.dims, l + 1) * pick(a.dims, l) * 4;
+            mbar_arrive_expect_tx(ld_bar, bytes);
+            for (int l = 0; l < a.layers; ++l) {
+                const int din = pick(a.dims, l), dout = pick(a.dims, l + 1);
+                bulk_load(rawp + pick(p.raw_w_off, l), static_cast<const float*>(pick(a.w, l)) + (size_t)model * dout * din,
+                          (uint32_t)dout * din * 4, ld_bar, pol);
+            }
+            if (!a.in_packed)
+                bulk_load(rawp, x + ((size_t)model * B + row0) * d0, (uint32_t)rows * d0 * 4, ld_bar, pol);
+        }
+        __syncwarp();
+        if (a.in_packed)
+            for (int r = lane; r < rows; r += 32)
+                bulk_load(rawp + (uint32_t)r * d0 * 4, x + ((size_t)(row0 + r) * n + model) * d0, (uint32_t)d0 * 4,
+                          ld_bar, pol);
+        tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
+        tmem_relinquish();
+    }
+    {
+        const volatile int no_abort = 0;
+        const bool got = mbar_wait(ld_bar, 0, &no_abort);
+        if (!__syncthreads_and(got)) {
+            // the copies did not land in time: report, and wait (bounded) before the CTA ends
+            if (tid == 0) raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            mbar_wait(ld_bar, 0, &no_abort);
+            tc_fence_before();
+            __syncthreads();
+            if (warp == 0) { tc_fence_after(); tmem_dealloc(*tmem_slot, (uint32_t)p.tmem_cols); }
+            return;
+        }
+    }
+    // Split into the bf16 hi / lo tiles the MMAs read.
+    tc_split_staged(xbuf0, p.kc[0], p.np, reinterpret_cast<const float*>(rawp), rows, d0);
+    for (int l = 0; l < a.layers; ++l)
+        tc_split_staged(wreg + pick(p.w_off, l), pick(p.kc, l), kTcOut, reinterpret_cast<const float*>(rawp + pick(p.raw_w_off, l)),
+                        pick(a.dims, l + 1), pick(a.dims, l));
+    fence_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t idesc = idesc_f16(kTcOut, p.np, true);
+
+    bool ok = true;
+    for (int l = 0; l < a.layers && ok; ++l) {
+        const int dout = pick(a.dims, l + 1);
+        uint8_t* xin = (l & 1) ? xbuf1 : xbuf0;
+        uint8_t* xout = (l & 1) ? xbuf0 : xbuf1;
+        const int kc = pick(p.kc, l);
+        if (tid == 0) {
+            const uint32_t wt = tc_tile_bytes(kTcOut), xt = tc_tile_bytes(p.np);
+            const uint8_t* wh = wreg + pick(p.w_off, l);
+            const uint8_t* wl = wh + (uint32_t)kc * wt;
+            const uint8_t* xh = xin;
+            const uint8_t* xl = xin + (uint32_t)kc * xt;
+            for (int c = 0; c < kc; ++c) {
+                const uint64_t dwh = sdesc_kmajor_sw128(smem_addr(wh + c * wt)), dwl = sdesc_kmajor_sw128(smem_addr(wl + c * wt));
+                const uint64_t dxh = sdesc_kmajor_sw128(smem_addr(xh + c * xt)), dxl = sdesc_kmajor_sw128(smem_addr(xl + c * xt));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    umma_f16_ss(tmem, dwh + 2 * k, dxh + 2 * k, idesc, (c | k) != 0);
+                    umma_f16_ss(tmem, dwh + 2 * k, dxl + 2 * k, idesc, 1);
+                    umma_f16_ss(tmem, dwl + 2 * k, dxh + 2 * k, idesc, 1);
+                }
+            }
+            umma_commit(done);
+        }
+        const volatile int no_abort = 0;
+        const bool got = mbar_wait(done, (uint32_t)(l & 1), &no_abort);
+        tc_fence_after();
+        if (!__syncthreads_and(got)) { ok = false; break; }
+        // Epilogue: all 8 warps; warp w reads TMEM lanes 32*(w%4).. (feature
+        // o = TMEM lane) and every other 16-column (batch row) block, from
+        // block w/4.
+        {
+            const int o = (warp & 3) * 32 + lane;
+            const bool o_ok = o < dout;
+            const float bo = (o_ok && pick(a.b, l)) ? static_cast<const float*>(pick(a.b, l))[(size_t)model * dout + o] : 0.f;
+            const int act = pick(a.act, l);
+            const bool last = l + 1 == a.layers;
+            const uint32_t xt = tc_tile_bytes(p.np);
+            const bool in_next = !last && (o >> 6) < pick(p.kc, l + 1);
+            uint8_t* oh = xout + (uint32_t)(o >> 6) * xt;
+            uint8_t* ol = xout + (uint32_t)pick(p.kc, last ? l : l + 1) * xt + (uint32_t)(o >> 6) * xt;
+            float* y = static_cast<float*>(a.y);
+#pragma unroll 1
+            for (int c0 = (warp >> 2) * 16; c0 < p.np; c0 += 32) {
+                uint32_t v[16];
+                tmem_ld_32x32b_x16(tmem + (uint32_t)c0 + ((uint32_t)((warp & 3) * 32) << 16), v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int r = c0 + j;
+                    float f = __uint_as_float(v[j]) + bo;
+                    if (act == WIDEK_ACT_RELU) f = f > 0.f ? f : 0.f;
+                    else if (act == WIDEK_ACT_GELU) f = chain_gelu(f);
+                    if (last) {
+                        if (o_ok && r < rows) {
+                            if (a.out_packed) y[((size_t)(row0 + r) * n + model) * dout + o] = f;
+                            else y[((size_t)model * B + row0 + r) * dout + o] = f;
+                        }
+                    } else if (in_next) {
+                        // next layer's input element (row r, k = o); features past dout
+                        // and rows past the batch are zeros
+                        const float fv = (o_ok && r < rows) ? f : 0.f;
+                        const __nv_bfloat16 h = __float2bfloat16_rn(fv);
+                        const __nv_bfloat16 lw = __float2bfloat16_rn(fv - __bfloat162float(h));
+                        const uint32_t off = tc_off(r, o & 63);
+                        *reinterpret_cast<__nv_bfloat16*>(oh + off) = h;
+                        *reinterpret_cast<__nv_bfloat16*>(ol + off) = lw;
+                    }
+                }
+            }
+        }
+        // The next layer's input tiles are written (generic proxy) before its MMAs read them.
+        fence_async_shared();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (!ok) raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+    }
+}
+
 struct ChainLaunch {
     ChainArgs a;
     bool query;
     cudaStream_t st;
     template <typename T>
     int run() {
+        if constexpr (std::is_same<T, float>::value) {
+            // fp32: the tensor-core chain when selected and the layers and pointers fit it
+            ChainTcPlan p{};
+            bool aligned = query || (aligned16(a.x) && aligned16(a.y));
+            for (int l = 0; l < a.layers && aligned && !query; ++l)
+                aligned = aligned16(a.w[l]) && (!a.b[l] || aligned16(a.b[l]));
+            if (g_chain_variant == 1 && aligned && chain_tc_plan(a, p)) {
+                if (query) return WIDEK_OK;
+                static bool attr_done[64] = {false};
+                const int dev = current_device();
+                if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+                    if (cudaFuncSetAttribute(mlp_chain_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kChainSmemMax) != cudaSuccess)
+                        return set_error(WIDEK_ERR_CUDA, "mlp_chain: cannot reserve shared memory");
+                    attr_done[dev] = true;
+                }
+                const unsigned blocks = (unsigned)((a.batch + p.rows - 1) / p.rows);
+                mlp_chain_tc_kernel<<<dim3((unsigned)a.n, blocks), kTcThreads, p.smem, st>>>(a, p,
+                                                                                           device_error_ptr());
+                return check_launch("widek_mlp_chain_fwd (tcgen05, split fp32)");
+            }
+        }
         if (!chain_plan(a, sm_count(current_device())))
             return query ? WIDEK_ERR_UNSUPPORTED
                          : set_error(WIDEK_ERR_UNSUPPORTED, "mlp_chain: the layers do not fit in shared memory");
@@ -480,6 +808,12 @@ extern "C" int widek_mlp_chain_fwd(const void* x, void* y, const void* const* we
                                    int in_layout, int out_layout, int dtype, void* stream) {
     return widek::chain_entry(x, y, weights, biases, dims, acts, layers, n, batch, in_layout, out_layout, dtype,
                               false, stream);
+}
+
+extern "C" int widek_mlp_chain_set_variant(int variant) {
+    if (variant < 0 || variant > 1) return widek::set_error(WIDEK_ERR_INVALID, "mlp_chain: unknown variant %d", variant);
+    widek::g_chain_variant = variant;
+    return WIDEK_OK;
 }
 
 extern "C" int widek_mlp_chain_supported(const int64_t* dims, const int* acts, int layers, int64_t n, int64_t batch,

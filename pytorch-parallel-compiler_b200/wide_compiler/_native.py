@@ -91,6 +91,7 @@ SIGNATURES = {
                             ctypes.POINTER(_i64), ctypes.POINTER(_int), _int, _i64, _i64, _int, _int, _int,
                             _c_void_p],
     "widek_mlp_chain_supported": [ctypes.POINTER(_i64), ctypes.POINTER(_int), _int, _i64, _i64, _int],
+    "widek_mlp_chain_set_variant": [_int],
     "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
 }
@@ -216,9 +217,20 @@ def check(rc: int, what: str) -> None:
     raise WideKernelError(msg)
 
 
+_replayed_launches = 0
+
+
+def note_replayed_launches(n: int) -> None:
+    """Counts n library kernels launched by replaying a recorded CUDA graph
+    (the launches were counted once when the graph was recorded)."""
+    global _replayed_launches
+    _replayed_launches += n
+
+
 def launch_count() -> int:
-    """Kernel launches the library has issued in this process."""
-    return int(lib().widek_launch_count())
+    """Kernel launches the library has issued in this process, including
+    those run by replays of the CUDA-graph executor's recorded graphs."""
+    return int(lib().widek_launch_count()) + _replayed_launches
 
 
 def device_error() -> int:

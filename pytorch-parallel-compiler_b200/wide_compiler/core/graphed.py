@@ -42,13 +42,16 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
+from .. import _native
+
 
 class _Recorded:
-    __slots__ = ('graph', 'output', 'tensors', 'ptrs')
+    __slots__ = ('graph', 'output', 'tensors', 'ptrs', 'launches')
 
-    def __init__(self, graph, output, tensors):
+    def __init__(self, graph, output, tensors, launches):
         self.graph, self.output, self.tensors = graph, output, tensors
         self.ptrs = tuple(t.data_ptr() for t in tensors)
+        self.launches = launches            # library kernels one replay runs
 
     def current(self) -> bool:
         """The parameters and buffers still live where the graph reads them."""
@@ -90,9 +93,10 @@ class GraphedWideModel(nn.Module):
         # each graph keeps a private memory pool, so graphs recorded for
         # different inputs may also be replayed on different streams
         g = torch.cuda.CUDAGraph()
+        n0 = _native.launch_count()
         with torch.cuda.graph(g):
             out = m(x)
-        return _Recorded(g, out, list(m.parameters()) + list(m.buffers()))
+        return _Recorded(g, out, list(m.parameters()) + list(m.buffers()), _native.launch_count() - n0)
 
     def reset(self) -> None:
         """Drops every recorded graph (they are recorded again on demand)."""
@@ -112,6 +116,7 @@ class GraphedWideModel(nn.Module):
             self._graphs[key] = rec
         self._graphs.move_to_end(key)
         rec.graph.replay()
+        _native.note_replayed_launches(rec.launches)
         return rec.output
 
     def extra_repr(self) -> str:

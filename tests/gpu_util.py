@@ -23,3 +23,12 @@ def assert_fp32_close(actual: torch.Tensor, expected: torch.Tensor):
 def no_device_error():
     from wide_compiler import _native
     assert _native.device_error() == 0
+
+
+def kernels_run(fn):
+    """Names of the CUDA kernels ``fn`` launches (torch profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}

@@ -6,7 +6,7 @@ import torch
 import wide_compiler as wc
 from wide_compiler import ops
 from conftest import golden_names, load_golden
-from gpu_util import assert_fp32_close, assert_lowp_close, no_device_error
+from gpu_util import assert_fp32_close, assert_lowp_close, kernels_run as _kernels_run, no_device_error
 from oracle import wide_oracle as O
 from test_api_host import _build_from_state
 
@@ -119,15 +119,6 @@ def test_attention_cfg5_full_size_sampled():
         ref = _ref(sub, xs, xs, xs, causal=True)
         assert_lowp_close(y[i:i + 1, j:j + 1], ref)
     no_device_error()
-
-
-def _kernels_run(fn):
-    """Names of the CUDA kernels ``fn`` launches (torch profiler)."""
-    from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        fn()
-        torch.cuda.synchronize()
-    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
 
 
 @pytest.mark.parametrize("kind", ['bool', 'float', 'float32', 'per_head'])

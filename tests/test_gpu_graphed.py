@@ -46,11 +46,13 @@ def test_graphed_mlp_matches_eager_and_replays():
     y0 = graphed(x)                      # records, then replays
     assert_fp32_close(y0, eager(x))
     torch.cuda.synchronize()
-    before = _native.launch_count()
+    host_before, before = _native.lib().widek_launch_count(), _native.launch_count()
     x.copy_(torch.randn(b, n * 64, device=DEV))
     y1 = graphed(x)                      # replay: same static output, new values
     torch.cuda.synchronize()
-    assert _native.launch_count() == before
+    assert _native.lib().widek_launch_count() == host_before     # no launch from the host
+    rec = next(iter(graphed._graphs.values()))
+    assert rec.launches >= 1 and _native.launch_count() == before + rec.launches   # the graph's kernels counted
     assert y1.data_ptr() == y0.data_ptr()
     assert_fp32_close(y1, eager(x))
     x2 = torch.randn(b, n * 64, device=DEV)   # another buffer: a second graph

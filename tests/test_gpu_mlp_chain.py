@@ -10,7 +10,7 @@ import torch.nn as nn
 
 import wide_compiler as wc
 from wide_compiler import _native, ops
-from gpu_util import assert_fp32_close, assert_lowp_close, no_device_error
+from gpu_util import assert_fp32_close, assert_lowp_close, kernels_run, no_device_error
 from oracle import wide_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -162,4 +162,42 @@ def test_traced_mlp_matches_per_model_modules():
     outs = wc.unpack_outputs(y, n)
     for m, xi, yi in zip(models, xs, outs):
         assert_fp32_close(yi, m.double()(xi.double()))
+    no_device_error()
+
+
+@pytest.mark.parametrize("n,b,dims,acts,bias,fits", [
+    (7, 32, [64, 128, 64], [ops.ACT_RELU, ops.ACT_NONE], True, True),             # cfg1 shape
+    (5, 16, [32, 64, 32, 8], [ops.ACT_GELU, ops.ACT_RELU, ops.ACT_NONE], True, True),  # 3 layers, narrow
+    (3, 40, [20, 128, 12], [ops.ACT_RELU, ops.ACT_NONE], False, True),       # ragged widths (K padding), no bias
+    (2, 64, [64, 64, 64], [ops.ACT_GELU, ops.ACT_GELU], True, True),         # activation on the last layer
+    (3, 300, [64, 128, 96, 32], [ops.ACT_GELU, ops.ACT_RELU, ops.ACT_NONE], True, False),   # too large: CUDA cores
+    (2, 8, [36, 128, 128, 128, 12], [ops.ACT_RELU] * 3 + [ops.ACT_NONE], True, False),
+])
+@pytest.mark.parametrize("in_l,out_l", [(0, 0), (1, 1), (0, 1)])
+def test_fp32_chain_tensor_core_vs_cuda_cores(n, b, dims, acts, bias, fits, in_l, out_l):
+    """fp32 chains on the tcgen05 split-operand kernel (chain variant 1,
+    where its plan fits in shared memory; checked by kernel name) and on the
+    CUDA-core kernel (variant 0, the default), both against the fp64 oracle
+    at the fp32 tolerance."""
+    ws, bs = _chain(n, dims, torch.float32, bias=bias, seed=b + len(dims))
+    x = torch.randn(n, b, dims[0], generator=torch.Generator().manual_seed(b)).to(torch.float32)
+    xin = (O.nfirst_to_packed(x).contiguous() if in_l == 1 else x).to(DEV)
+    wd = [w.to(DEV) for w in ws]
+    bd = [t.to(DEV) if t is not None else None for t in bs]
+    ref = _oracle(x, ws, bs, acts, torch.float32)
+    if out_l == 1:
+        ref = O.nfirst_to_packed(ref)
+    lib = _native.lib()
+    got = {}
+    try:
+        _native.check(lib.widek_mlp_chain_set_variant(1), "variant")     # tensor cores wherever they fit
+        names = kernels_run(lambda: got.__setitem__('tc', ops.mlp_chain(xin, wd, bd, acts, n, in_l, out_l)))
+        _native.check(lib.widek_mlp_chain_set_variant(0), "variant")
+        got['cc'] = ops.mlp_chain(xin, wd, bd, acts, n, in_l, out_l)
+    finally:
+        lib.widek_mlp_chain_set_variant(0)
+    assert got['tc'] is not None and got['cc'] is not None
+    assert any('mlp_chain_tc_kernel' in k for k in names) == fits, names
+    assert_fp32_close(got['tc'], ref)
+    assert_fp32_close(got['cc'], ref)
     no_device_error()
