@@ -90,9 +90,10 @@ WIDEK_API int widek_test_bounded_wait(uint64_t limit_ns, void* stream);
  * bf16/f16 with k % 8 == 0 and 16-byte aligned pointers run on the tcgen05
  * tensor-core kernel. fp32 without an activation, with k % 4 == 0 and
  * 16-byte aligned rows, runs on the tensor cores with each operand split
- * into two bf16 parts (hi*hi + hi*lo + lo*hi accumulated in fp32: each
- * product within ~2^-16 of the fp32 one, inside the fp32 tolerance with
- * TF32 off); every other case runs the CUDA-core kernel (fp32 FFMA).
+ * into three bf16 pieces (the six piece products of order >= 2^-18
+ * accumulated in fp32: each product as accurate as an fp32 multiply, so
+ * the sums match an fp32 GEMM up to accumulation order with TF32 off);
+ * every other case runs the CUDA-core kernel (fp32 FFMA).
  * Replaces: wide_compiler/core/primitives/wide_linear.py:165
  *           (einsum 'noi,nbi->nbo') and :168 (bias add). */
 WIDEK_API int widek_linear_fwd(const void* x, const void* w, const void* bias, void* y,
@@ -140,10 +141,11 @@ WIDEK_API int widek_linear_set_variant(int variant);
  * memory; fp32 arithmetic, each layer's output rounded to the storage dtype
  * as a layer-by-layer run stores it. fp32 chains whose layers are at most
  * 128 wide and 256 deep (widths multiples of 4, 16-byte aligned tensors)
- * with at least 2^21 multiply-adds per CTA run on tcgen05 instead: per layer D^T = W . h^T with the weights as the
- * 128-row A operand and the batch rows as N, every fp32 operand split into
- * bf16 hi + lo and accumulated as hi*hi + hi*lo + lo*hi in fp32 (each
- * product within ~2^-17 of the fp32 one). Returns WIDEK_ERR_UNSUPPORTED (launching
+ * can run on tcgen05 instead (widek_mlp_chain_set_variant(1)): per layer
+ * D^T = W . h^T with the weights as the 128-row A operand and the batch
+ * rows as N, every fp32 operand split into bf16 hi + lo and accumulated as
+ * hi*hi + hi*lo + lo*hi in fp32 (each product within ~2^-17 of the fp32
+ * one). Returns WIDEK_ERR_UNSUPPORTED (launching
  * nothing) when the chain does not fit (widek_mlp_chain_supported says in
  * advance). Replaces, for a TracedWideModel whose graph is such a chain, the
  * boundary unpack, the per-node WideLinear (wide_compiler/core/primitives/
@@ -538,6 +540,54 @@ WIDEK_API int widek_attention_fwd(const void* q, const void* k, const void* v, v
  * Process-wide; for tests and measurements. No reference counterpart (the
  * reference has a single torch SDPA call). */
 WIDEK_API int widek_attention_set_variant(int variant);
+
+/* ---- Backward (training) ------------------------------------------------
+ * The reference differentiates its primitives' torch forward with autograd
+ * (gradient flow tested at wide_compiler/core/primitives/wide_lstm.py:744-762);
+ * these entries compute the same gradients on the GPU. */
+
+/* y[b] = x[b]^T for x [batch, rows, cols] -> y [batch, cols, rows], any
+ * dtype (bytes are moved, not converted). */
+WIDEK_API int widek_transpose(const void* x, void* y, int64_t batch, int64_t rows, int64_t cols,
+                              int dtype, void* stream);
+
+/* Workspace bytes widek_linear_bwd needs (-1 for bad arguments). */
+WIDEK_API int64_t widek_linear_bwd_workspace(int64_t n, int64_t m, int64_t k, int64_t o, int dtype);
+
+/* Gradients of widek_linear_fwd without activation (y = x W^T + b per
+ * model; x [n, m, k], W [n, o, k], dy [n, m, o], all dense):
+ *   dx [n, m, k] = dy W,  dw [n, o, k] = dy^T x,  db [n, o] = sum_m dy.
+ * Any of dx / dw / db may be null (not computed). The two products run on
+ * widek_linear_fwd (tcgen05 for bf16/f16, split-operand tcgen05 or CUDA
+ * cores for fp32) over transposed copies of W, dy and x in the workspace;
+ * db is a column sum in fp32 (fixed summation order). Replaces the
+ * autograd of wide_compiler/core/primitives/wide_linear.py:162-171
+ * (einsum 'noi,nbi->nbo' + bias). */
+WIDEK_API int widek_linear_bwd(const void* x, const void* w, const void* dy, void* dx, void* dw,
+                               void* db, int64_t n, int64_t m, int64_t k, int64_t o, int dtype,
+                               void* workspace, int64_t workspace_bytes, void* stream);
+
+/* dpre = dy * act'(saved) elementwise over count elements: act RELU with
+ * saved = the activation's output (gradient 1 where it is > 0), act GELU
+ * (exact erf form) with saved = its input: Phi(s) + s * phi(s). Replaces the
+ * autograd of torch.relu / F.gelu after a WideLinear
+ * (wide_compiler/core/traced_wide.py:174-211). */
+WIDEK_API int widek_act_bwd(const void* dy, const void* saved, void* dpre, int64_t count, int act,
+                            int dtype, void* stream);
+
+/* Workspace bytes widek_layernorm_bwd needs (-1 for bad arguments). */
+WIDEK_API int64_t widek_layernorm_bwd_workspace(int64_t n, int64_t outer, int64_t d);
+
+/* Gradients of widek_layernorm_fwd (x, dy, dx [n, outer, d] dense; gamma
+ * flat [n*d]): dx = rstd * (g - mean(g) - x_hat * mean(g * x_hat)) with
+ * g = dy * gamma, dgamma = sum_rows dy * x_hat, dbeta = sum_rows dy (mean
+ * and rstd recomputed from x with the forward's eps; biased variance).
+ * dw / db may be null. d <= 1024. Replaces the autograd of
+ * wide_compiler/core/primitives/wide_layernorm.py:62-65. */
+WIDEK_API int widek_layernorm_bwd(const void* x, const void* w, const void* dy, void* dx,
+                                  void* dw, void* db, int64_t n, int64_t outer, int64_t d,
+                                  double eps, int dtype, void* workspace, int64_t workspace_bytes,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

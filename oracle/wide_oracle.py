@@ -83,6 +83,55 @@ def layernorm(x: Tensor, weight_flat: Tensor, bias_flat: Tensor, n: int, d: int,
 
 
 # ---------------------------------------------------------------------------
+# Gradients (the reference trains by torch autograd over the forwards above;
+# its gradient-flow test: wide_lstm.py:744-762). Explicit formulas in
+# float64, the upstream gradient dy given:
+#   WideLinear + act:  dpre = dy * act'(pre)  (ReLU: 1 where the output is
+#                      > 0; GELU: Phi(pre) + pre * phi(pre)),
+#                      dx = dpre W, dW = sum_rows dpre^T x, db = sum_rows dpre
+#   WideLayerNorm:     g = dy * gamma,
+#                      dx = rstd * (g - mean(g) - x_hat * mean(g * x_hat)),
+#                      dgamma = sum_rows dy * x_hat, dbeta = sum_rows dy
+# ---------------------------------------------------------------------------
+def linear_grads(x: Tensor, weight: Tensor, bias: Optional[Tensor], dy: Tensor, act: str = 'none'):
+    """(dx, dweight, dbias or None) of activation(linear(x, weight, bias))."""
+    x, w, b, g = _f(x), _f(weight), _f(bias), _f(dy)
+    n, o, k = w.shape
+    x2 = x.reshape(n, -1, k)
+    pre = torch.bmm(x2, w.transpose(1, 2))
+    if b is not None:
+        pre = pre + b[:, None, :]
+    g2 = g.reshape(n, -1, o)
+    if act == 'relu':
+        g2 = g2 * (pre > 0).to(D)
+    elif act == 'gelu':
+        g2 = g2 * (0.5 * (1.0 + torch.erf(pre / math.sqrt(2.0))) + pre * torch.exp(-0.5 * pre * pre)
+                   / math.sqrt(2.0 * math.pi))
+    elif act != 'none':
+        raise ValueError(act)
+    dx = torch.bmm(g2, w).reshape(x.shape)
+    dw = torch.bmm(g2.transpose(1, 2), x2)
+    db = g2.sum(dim=1) if b is not None else None
+    return dx, dw, db
+
+
+def layernorm_grads(x: Tensor, weight_flat: Tensor, dy: Tensor, n: int, d: int, eps: float):
+    """(dx, dweight_flat, dbias_flat) of layernorm(x, weight_flat, ., n, d, eps)."""
+    x, g = _f(x), _f(dy)
+    w = _f(weight_flat).view(n, *([1] * (x.dim() - 2)), d)
+    mean = x.mean(dim=-1, keepdim=True)
+    var = ((x - mean) ** 2).mean(dim=-1, keepdim=True)
+    rstd = 1.0 / torch.sqrt(var + eps)
+    xh = (x - mean) * rstd
+    gg = g * w
+    dx = rstd * (gg - gg.mean(dim=-1, keepdim=True) - xh * (gg * xh).mean(dim=-1, keepdim=True))
+    rows = tuple(range(1, x.dim() - 1))
+    dw = (g * xh).sum(dim=rows).reshape(n * d) if rows else (g * xh).reshape(n * d)
+    db = g.sum(dim=rows).reshape(n * d) if rows else g.reshape(n * d)
+    return dx, dw, db
+
+
+# ---------------------------------------------------------------------------
 # BatchNorm1d/2d — wide_batchnorm_2d.py:53-72, wide_batchnorm_1d.py:53-73
 # (inner nn.BatchNorm over N*C channels == per-(model, channel) statistics)
 # ---------------------------------------------------------------------------

@@ -2,23 +2,37 @@
 //
 //   y[i] = x[i] @ W_i^T + bias[i]   (fp32 in, fp32 out)
 //
-// Each fp32 operand a is split into two bf16 values, hi = bf16(a) and
-// lo = bf16(a - hi), so that a = hi + lo to about 2^-17 relative. The
-// product is accumulated in fp32 TMEM as hi_x*hi_w + hi_x*lo_w + lo_x*hi_w
-// (three tcgen05 kind::f16 MMAs per K step; the dropped lo*lo term is about
-// 2^-16 relative), which keeps each product within ~2^-16 of the fp32 one:
-// well inside the fp32 contract (rtol 1e-3 / atol 1e-4 with TF32 off),
-// while the CUDA-core kernel of gemm_simt.cu is bound by its shared-memory
-// wavefronts. Serves the recurrent layers' input projection (all T steps of
-// x at once), whose rows and weights come strided exactly as for
-// linear_simt_strided.
+// Each fp32 operand a is split into three bf16 pieces, a0 = bf16(a),
+// a1 = bf16(a - a0), a2 = bf16(a - a0 - a1), so that a = a0 + a1 + a2 to
+// about 2^-27 relative. The product is accumulated in fp32 TMEM from the six
+// piece products whose order is at most 2^-18 relative,
+//   x0*w0 + x0*w1 + x1*w0 + x0*w2 + x1*w1 + x2*w0
+// (six tcgen05 kind::f16 MMAs per K step; the dropped terms are below
+// 2^-26), so each product is as accurate as an fp32 multiply and the sums
+// differ from an fp32 FFMA GEMM by accumulation order only: the fp32
+// contract (rtol 1e-3 / atol 1e-4 with TF32 off) holds however long K is.
+// (Two pieces and three products leave ~2^-17 per product, which over a
+// few hundred unscaled terms, e.g. a weight gradient summed over the batch,
+// already reaches the 1e-4 absolute bound.) Serves fp32 WideLinear and the
+// recurrent layers' input projection (all T steps of x at once), whose rows
+// and weights come strided exactly as for linear_simt_strided.
 //
-// One CTA of 128 threads per (model, 128-row tile, 128-column tile): the
-// threads load their x and W tiles with coalesced 16-byte loads, split them
-// and write the four bf16 tiles into shared memory in the 128-byte swizzled
-// K-major layout (rows of 64 values); one thread issues the MMAs into a
-// 128-column TMEM accumulator; each warp then reads its 32 TMEM lanes (rows)
-// and writes them with the bias added. K runs in chunks of 64.
+// The tensor core's fp32 accumulation does not round to nearest: adding
+// into one TMEM accumulator over all of K left errors that grow with K
+// (1.1e-3 at K = 2048 with unscaled operands, against ~1e-4 for FFMA). So
+// each 64-wide K chunk accumulates afresh, x0*w0 and the five small
+// products into two separate TMEM accumulators, and the threads add both
+// into fp32 registers (round to nearest) after the chunk: the truncation
+// then acts on chunk-sized partial sums only.
+//
+// One CTA of 128 threads per (model, 128-row tile, 128-column tile), two
+// stages: the threads load the x and W tiles of chunk c with coalesced
+// 16-byte loads, split them and write the six bf16 tiles into the stage's
+// shared memory in the 128-byte swizzled K-major layout (rows of 64
+// values); one thread issues chunk c's MMAs into the stage's two 128-column
+// TMEM accumulators; while they run, every thread drains chunk c-1's
+// accumulators (its row: TMEM lane) into its registers. Epilogue: each
+// thread writes its row with the bias added.
 #include "common.cuh"
 #include "sm100_ptx.cuh"
 
@@ -32,6 +46,8 @@ constexpr int kF3K = 64;         // K per chunk (one 128-byte swizzled bf16 row)
 constexpr int kF3Threads = 128;
 constexpr int kF3Batch = 8;      // 16-byte loads of x and of W in flight per thread
 constexpr uint32_t kF3Tile = kF3Rows * kF3K * 2;     // one bf16 tile: 16 KB
+constexpr uint32_t kF3Stage = 6 * kF3Tile;             // three pieces of x and of W
+constexpr uint32_t kF3TmemCols = 4 * kF3Rows;          // per stage: x0*w0, and the small products
 
 struct F3Args {
     const float* x;
@@ -51,33 +67,43 @@ __device__ __forceinline__ uint32_t f3_off(int r, int kk) {
     return (uint32_t)(r * 128 + ((((kk >> 3) ^ (r & 7)) << 4) | ((kk & 7) << 1)));
 }
 
-// Splits four consecutive fp32 values into bf16 hi / lo parts and stores
-// them at (r, kk..kk+3) of the hi and lo tiles.
-__device__ __forceinline__ void f3_split_store(uint8_t* hi, uint8_t* lo, int r, int kk, float4 v) {
+// Splits four consecutive fp32 values into three bf16 pieces each and
+// stores them at (r, kk..kk+3) of the piece tiles t0, t1, t2.
+__device__ __forceinline__ void f3_split_store(uint8_t* t0, uint8_t* t1, uint8_t* t2, int r, int kk, float4 v) {
     const float a[4] = {v.x, v.y, v.z, v.w};
-    uint32_t h2[2], l2[2];
+    uint32_t p0[2], p1[2], p2[2];
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
         const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * p], a[2 * p + 1]);
         const float2 hf = __bfloat1622float2(h);
-        const __nv_bfloat162 l = __floats2bfloat162_rn(a[2 * p] - hf.x, a[2 * p + 1] - hf.y);
-        h2[p] = *reinterpret_cast<const uint32_t*>(&h);
-        l2[p] = *reinterpret_cast<const uint32_t*>(&l);
+        const float r0 = a[2 * p] - hf.x, r1 = a[2 * p + 1] - hf.y;          // exact in fp32
+        const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
+        const float2 mf = __bfloat1622float2(m);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);
+        p0[p] = *reinterpret_cast<const uint32_t*>(&h);
+        p1[p] = *reinterpret_cast<const uint32_t*>(&m);
+        p2[p] = *reinterpret_cast<const uint32_t*>(&l);
     }
     const uint32_t off = f3_off(r, kk);      // 4 values = 8 bytes, inside one 16-byte chunk
-    *reinterpret_cast<uint2*>(hi + off) = make_uint2(h2[0], h2[1]);
-    *reinterpret_cast<uint2*>(lo + off) = make_uint2(l2[0], l2[1]);
+    *reinterpret_cast<uint2*>(t0 + off) = make_uint2(p0[0], p0[1]);
+    *reinterpret_cast<uint2*>(t1 + off) = make_uint2(p1[0], p1[1]);
+    *reinterpret_cast<uint2*>(t2 + off) = make_uint2(p2[0], p2[1]);
 }
 
+// MULTI: K spans more than one chunk (register accumulation over chunks);
+// otherwise the single chunk's accumulators are written out directly, and
+// the kernel keeps few registers (room on the SM for a programmatic
+// dependent's CTAs).
+template <bool MULTI>
 __global__ void __launch_bounds__(kF3Threads, 1) gemm_f32x3_kernel(F3Args a, int* err) {
     extern __shared__ uint8_t f3_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(f3_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* xh = sm;
-    uint8_t* xl = sm + kF3Tile;
-    uint8_t* wh = sm + 2 * kF3Tile;
-    uint8_t* wl = sm + 3 * kF3Tile;
-    uint64_t* done = reinterpret_cast<uint64_t*>(sm + 4 * kF3Tile);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    // barriers in the first 1 KB, then one or two stages of six tiles (x
+    // pieces 0..2, then W pieces 0..2); a single-chunk call gets one stage,
+    // which leaves room on the SM for a programmatic dependent's CTAs
+    uint64_t* done = reinterpret_cast<uint64_t*>(sm);      // [2], one per stage
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
+    uint8_t* tiles = sm + 1024;
 
     // A programmatic dependent (the recurrence after the RNN input
     // projection) may start its set-up now; it waits for this grid's results.
@@ -90,25 +116,60 @@ __global__ void __launch_bounds__(kF3Threads, 1) gemm_f32x3_kernel(F3Args a, int
     const float* wm = a.w + (int64_t)model * a.w_ms;
 
     if (tid == 0) {
-        mbar_init(done, 1);
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
         mbar_init_fence();
     }
-    if (warp == 0) { tmem_alloc(tmem_slot, kF3Rows); tmem_relinquish(); }
+    if (warp == 0) { tmem_alloc(tmem_slot, kF3TmemCols); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     constexpr uint32_t IDESC = idesc_f16(kF3Rows, kF3Rows, true);
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+    // Row r = warp*32 + lane of the tile, all 128 columns, summed in fp32
+    // registers (round to nearest) over the K chunks.
+    float acc[MULTI ? kF3Rows : 1];
+#pragma unroll
+    for (int j = 0; j < (MULTI ? kF3Rows : 1); ++j) acc[j] = 0.f;
+    // Adds the accumulators of one stage (x0*w0 and the sum of the small
+    // piece products, 128 columns each) to acc.
+    auto drain = [&](int stage) {
+        if constexpr (MULTI) {
+            const uint32_t big = tmem + (uint32_t)(stage * 2 * kF3Rows) + lane_base;
+            const uint32_t small = big + kF3Rows;
+#pragma unroll
+            for (int c = 0; c < kF3Rows; c += 32) {
+                uint32_t vb[32], vs[32];
+                tmem_ld_32x32b_x32(big + (uint32_t)c, vb);
+                tmem_ld_32x32b_x32(small + (uint32_t)c, vs);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[c + j] += __uint_as_float(vb[j]) + __uint_as_float(vs[j]);
+            }
+        }
+    };
 
     bool ok = true;
+    int last_issued = 0;
+    const volatile int no_abort = 0;
     const int chunks = (a.k + kF3K - 1) / kF3K;
-    for (int ch = 0; ch < chunks; ++ch) {
+    for (int ch = 0; ch < chunks && ok; ++ch) {
+        const int st = ch & 1;
+        uint8_t* x0 = tiles + st * kF3Stage;
+        uint8_t* x1 = x0 + kF3Tile;
+        uint8_t* x2 = x0 + 2 * kF3Tile;
+        uint8_t* w0 = x0 + 3 * kF3Tile;
+        uint8_t* w1 = x0 + 4 * kF3Tile;
+        uint8_t* w2 = x0 + 5 * kF3Tile;
         const int k0 = ch * kF3K;
         // x and W tiles: 128 rows x 16 float4 each, consecutive threads on
         // consecutive 16-byte pieces of a row; rows / columns past the
         // matrix and k past K are zeros. Loads are issued in batches of
         // kF3Batch per tile before any is split and stored, so their
-        // latencies overlap.
+        // latencies overlap. The stage's previous MMAs (chunk ch - 2) were
+        // waited for before chunk ch - 1's were issued.
         constexpr int kPer = kF3Rows * (kF3K / 4) / kF3Threads;     // float4 per thread per tile
 #pragma unroll 1
         for (int j0 = 0; j0 < kPer; j0 += kF3Batch) {
@@ -131,56 +192,82 @@ __global__ void __launch_bounds__(kF3Threads, 1) gemm_f32x3_kernel(F3Args a, int
             for (int jj = 0; jj < kF3Batch; ++jj) {
                 const int i = tid + (j0 + jj) * kF3Threads;
                 const int r = i >> 4, kk = (i & 15) * 4;
-                f3_split_store(xh, xl, r, kk, xv[jj]);
-                f3_split_store(wh, wl, r, kk, wv[jj]);
+                f3_split_store(x0, x1, x2, r, kk, xv[jj]);
+                f3_split_store(w0, w1, w2, r, kk, wv[jj]);
             }
         }
-        // The tiles written by the threads become visible to the tensor core.
+        // The tiles written by the threads become visible to the tensor
+        // core; the stage's accumulators were drained (chunk ch - 2).
         fence_async_shared();
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
         if (tid == 0) {
-            const uint64_t dxh = sdesc_kmajor_sw128(smem_addr(xh)), dxl = sdesc_kmajor_sw128(smem_addr(xl));
-            const uint64_t dwh = sdesc_kmajor_sw128(smem_addr(wh)), dwl = sdesc_kmajor_sw128(smem_addr(wl));
+            const uint32_t t_big = tmem + (uint32_t)(st * 2 * kF3Rows), t_small = t_big + kF3Rows;
+            const uint64_t dx0 = sdesc_kmajor_sw128(smem_addr(x0)), dx1 = sdesc_kmajor_sw128(smem_addr(x1)),
+                           dx2 = sdesc_kmajor_sw128(smem_addr(x2));
+            const uint64_t dw0 = sdesc_kmajor_sw128(smem_addr(w0)), dw1 = sdesc_kmajor_sw128(smem_addr(w1)),
+                           dw2 = sdesc_kmajor_sw128(smem_addr(w2));
 #pragma unroll
             for (int k = 0; k < kF3K / 16; ++k) {
-                umma_f16_ss(tmem, dxh + 2 * k, dwh + 2 * k, IDESC, (ch | k) != 0);
-                umma_f16_ss(tmem, dxh + 2 * k, dwl + 2 * k, IDESC, 1);
-                umma_f16_ss(tmem, dxl + 2 * k, dwh + 2 * k, IDESC, 1);
+                umma_f16_ss(t_big, dx0 + 2 * k, dw0 + 2 * k, IDESC, k != 0);
+                umma_f16_ss(t_small, dx0 + 2 * k, dw1 + 2 * k, IDESC, k != 0);
+                umma_f16_ss(t_small, dx1 + 2 * k, dw0 + 2 * k, IDESC, 1);
+                umma_f16_ss(t_small, dx0 + 2 * k, dw2 + 2 * k, IDESC, 1);
+                umma_f16_ss(t_small, dx1 + 2 * k, dw1 + 2 * k, IDESC, 1);
+                umma_f16_ss(t_small, dx2 + 2 * k, dw0 + 2 * k, IDESC, 1);
             }
-            umma_commit(done);
+            umma_commit(&done[st]);
         }
-        // The MMAs have read the tiles (and, after the last chunk, written
-        // the accumulator) before the tiles are overwritten / TMEM is read.
-        // Every thread waits (bounded); the verdict is made uniform so that
-        // no thread leaves the loop while others reach the next barrier.
-        const volatile int no_abort = 0;
-        const bool got = mbar_wait(done, (uint32_t)(ch & 1), &no_abort);
+        last_issued = ch;
+        // While chunk ch's MMAs run, drain chunk ch - 1's accumulators (its
+        // MMAs are done once its barrier completes; every thread waits,
+        // bounded, and the verdict is made uniform).
+        if (ch > 0) {
+            const int ps = st ^ 1;
+            const bool got = mbar_wait(&done[ps], (uint32_t)(((ch - 1) >> 1) & 1), &no_abort);
+            tc_fence_after();
+            if (!__syncthreads_and(got)) { ok = false; break; }
+            drain(ps);
+            tc_fence_before();
+        }
+    }
+    if (ok) {
+        const int last = chunks - 1;
+        const bool got = mbar_wait(&done[last & 1], (uint32_t)((last >> 1) & 1), &no_abort);
         tc_fence_after();
-        if (!__syncthreads_and(got)) { ok = false; break; }
+        ok = __syncthreads_and(got);
+        if (ok && MULTI) drain(last & 1);
     }
     if (!ok) {
+        // a wait ran out: report, and give the MMAs still in flight (the
+        // last chunk issued) a bounded wait before the accumulators are freed
         raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+        mbar_wait(&done[last_issued & 1], (uint32_t)((last_issued >> 1) & 1), &no_abort);
     } else {
-        // Epilogue: warp q reads TMEM lanes 32q..32q+31 (rows), 32 columns at a time.
+        // Epilogue: thread (warp, lane) holds row warp*32 + lane.
         const int r = warp * 32 + lane;
         const int gm = m0 + r;
-        float* yr = a.y + (int64_t)model * a.y_ms + (int64_t)((gm < a.m ? gm : 0) / a.rpb) * a.y_bs +
-                    (int64_t)((gm < a.m ? gm : 0) % a.rpb) * a.o;
         const float* bm = a.bias ? a.bias + (int64_t)model * a.o : nullptr;
+        if (!MULTI) {
+            // one chunk: big + small straight from TMEM (stage 0), 16 columns at a time
+            float* yr = a.y + (int64_t)model * a.y_ms + (int64_t)((gm < a.m ? gm : 0) / a.rpb) * a.y_bs +
+                        (int64_t)((gm < a.m ? gm : 0) % a.rpb) * a.o;
 #pragma unroll 1
-        for (int c = 0; c < kF3Rows; c += 32) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + (uint32_t)c + ((uint32_t)(warp * 32) << 16), v);
-            tmem_ld_wait();
-            if (gm < a.m) {
+            for (int c = 0; c < kF3Rows; c += 16) {
+                uint32_t vb[16], vs[16];
+                tmem_ld_32x32b_x16(tmem + lane_base + (uint32_t)c, vb);
+                tmem_ld_32x32b_x16(tmem + lane_base + kF3Rows + (uint32_t)c, vs);
+                tmem_ld_wait();
+                if (gm >= a.m) continue;
                 const int go0 = o0 + c;
-                if (go0 + 32 <= a.o && (a.o & 3) == 0) {
+                if (go0 + 16 <= a.o && (a.o & 3) == 0) {
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        float4 f = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                               __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                    for (int j = 0; j < 16; j += 4) {
+                        float4 f = make_float4(__uint_as_float(vb[j]) + __uint_as_float(vs[j]),
+                                               __uint_as_float(vb[j + 1]) + __uint_as_float(vs[j + 1]),
+                                               __uint_as_float(vb[j + 2]) + __uint_as_float(vs[j + 2]),
+                                               __uint_as_float(vb[j + 3]) + __uint_as_float(vs[j + 3]));
                         if (bm) {
                             const float4 b = *reinterpret_cast<const float4*>(bm + go0 + j);
                             f.x += b.x; f.y += b.y; f.z += b.z; f.w += b.w;
@@ -188,9 +275,27 @@ __global__ void __launch_bounds__(kF3Threads, 1) gemm_f32x3_kernel(F3Args a, int
                         *reinterpret_cast<float4*>(yr + go0 + j) = f;
                     }
                 } else {
-                    for (int j = 0; j < 32; ++j)
-                        if (go0 + j < a.o) yr[go0 + j] = __uint_as_float(v[j]) + (bm ? bm[go0 + j] : 0.f);
+                    for (int j = 0; j < 16; ++j)
+                        if (go0 + j < a.o)
+                            yr[go0 + j] = __uint_as_float(vb[j]) + __uint_as_float(vs[j]) + (bm ? bm[go0 + j] : 0.f);
                 }
+            }
+        } else if (gm < a.m) {
+            float* yr = a.y + (int64_t)model * a.y_ms + (int64_t)(gm / a.rpb) * a.y_bs + (int64_t)(gm % a.rpb) * a.o;
+            if (o0 + kF3Rows <= a.o && (a.o & 3) == 0) {
+#pragma unroll
+                for (int j = 0; j < (MULTI ? kF3Rows : 0); j += 4) {
+                    float4 f = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                    if (bm) {
+                        const float4 b = *reinterpret_cast<const float4*>(bm + o0 + j);
+                        f.x += b.x; f.y += b.y; f.z += b.z; f.w += b.w;
+                    }
+                    *reinterpret_cast<float4*>(yr + o0 + j) = f;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < (MULTI ? kF3Rows : 0); ++j)
+                    if (o0 + j < a.o) yr[o0 + j] = acc[j] + (bm ? bm[o0 + j] : 0.f);
             }
         }
     }
@@ -198,7 +303,7 @@ __global__ void __launch_bounds__(kF3Threads, 1) gemm_f32x3_kernel(F3Args a, int
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kF3Rows);
+        tmem_dealloc(tmem, kF3TmemCols);
     }
 }
 
@@ -219,17 +324,23 @@ int linear_f32x3_strided(const float* x, const float* w, const float* bias, floa
     const int64_t mt = (m + kF3Rows - 1) / kF3Rows, ot = (o + kF3Rows - 1) / kF3Rows;
     if (mt > 65535 || ot > 0x7fffffff) return WIDEK_ERR_UNSUPPORTED;
     F3Args a{x, w, bias, y, (int)m, (int)k, (int)o, w_ms, w_rs, x_ms, x_bs, y_ms, y_bs, (int)x_rpb};
-    const size_t smem = 1024 + 4 * kF3Tile + 16;
+    const size_t smem_max = 2048 + 2 * kF3Stage;
+    const size_t smem = 2048 + (k > kF3K ? 2 : 1) * (size_t)kF3Stage;
     static bool attr_done[64] = {false};
     const int dev = current_device();
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        if (cudaFuncSetAttribute(gemm_f32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-            return set_error(WIDEK_ERR_CUDA, "linear (f32x3): cannot reserve %zu bytes of shared memory", smem);
+        if (cudaFuncSetAttribute(gemm_f32x3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem_max) != cudaSuccess ||
+            cudaFuncSetAttribute(gemm_f32x3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem_max) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "linear (f32x3): cannot reserve %zu bytes of shared memory", smem_max);
         attr_done[dev] = true;
     }
     dim3 grid((unsigned)ot, (unsigned)mt, (unsigned)n);
-    gemm_f32x3_kernel<<<grid, kF3Threads, smem, st>>>(a, device_error_ptr());
+    if (k > kF3K)
+        gemm_f32x3_kernel<true><<<grid, kF3Threads, smem, st>>>(a, device_error_ptr());
+    else
+        gemm_f32x3_kernel<false><<<grid, kF3Threads, smem, st>>>(a, device_error_ptr());
     return check_launch("widek_linear_fwd (fp32 split tensor-core)");
 }
 

@@ -284,3 +284,133 @@ def attention_t(query: Tensor, key: Tensor, value: Tensor, attn_mask, is_causal:
                                        is_causal=is_causal, scale=1.0 / math.sqrt(dh))
     o = o.transpose(1, 2).reshape(n, b, tq, d)
     return linear_t(o, out_weight, out_bias)
+
+
+# ---------------------------------------------------------------------------
+# Kernel-backed gradients
+#
+# WideLinear (with its fused ReLU / GELU), WideLayerNorm and the layout swap
+# have backward kernels (csrc/backward.cu): their forward runs once, on the
+# kernels, and the backward launches the gradient kernels on the saved
+# tensors instead of re-running a torch formulation.
+# ---------------------------------------------------------------------------
+_KERNEL_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
+
+class LinearFn(torch.autograd.Function):
+    """y = act(x W^T + b) per model; backward: widek_act_bwd then
+    widek_linear_bwd (dX, dW, db). ReLU keeps its output for the gradient;
+    GELU runs unfused (GEMM, then the GELU kernel) and keeps its input."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, act):
+        from . import ops
+        with torch.no_grad():
+            if act == 2:
+                pre = ops.linear(x, weight, bias, 0)
+                y, saved = ops.unary(pre, 'gelu'), pre
+            else:
+                y = ops.linear(x, weight, bias, act)
+                saved = y if act == 1 else None
+        ctx.act, ctx.has_bias = act, bias is not None
+        ctx.save_for_backward(x, weight, saved)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        x, weight, saved = ctx.saved_tensors
+        dy = dy.to(weight.dtype).contiguous()
+        if ctx.act:
+            dy = ops.act_bwd(dy, saved, ctx.act)
+        need_x, need_w, need_b = ctx.needs_input_grad[:3]
+        dx, dw, db = ops.linear_bwd(x, weight, dy, need_x, need_w, need_b and ctx.has_bias)
+        if dx is not None:
+            dx = dx.view(x.shape)
+        return dx, dw, db, None
+
+
+class LayerNormFn(torch.autograd.Function):
+    """LayerNorm with per-model affine; backward: widek_layernorm_bwd."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, n, d, eps):
+        from . import ops
+        with torch.no_grad():
+            y = ops.layernorm(x, weight, bias, n, d, eps)
+        ctx.n, ctx.d, ctx.eps, ctx.bias_shape = n, d, eps, bias.shape
+        ctx.save_for_backward(x, weight)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        x, weight = ctx.saved_tensors
+        dx, dw, db = ops.layernorm_bwd(x, weight, dy.to(x.dtype).contiguous(), ctx.n, ctx.d, ctx.eps,
+                                       ctx.needs_input_grad[1], ctx.needs_input_grad[2])
+        dw = None if dw is None else dw.view(weight.shape)
+        db = None if db is None else db.view(ctx.bias_shape)
+        return dx.view(x.shape), dw, db, None, None, None
+
+
+class Swap01Fn(torch.autograd.Function):
+    """[A, B, ...] -> [B, A, ...]; its gradient is the same swap."""
+
+    @staticmethod
+    def forward(ctx, x):
+        from . import ops
+        with torch.no_grad():
+            return ops.swap01(x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        return ops.swap01(dy.contiguous())
+
+
+class ActFn(torch.autograd.Function):
+    """ReLU / GELU glue (traced_wide.py:174-186); backward: widek_act_bwd
+    (ReLU from its output, GELU from its input)."""
+
+    @staticmethod
+    def forward(ctx, x, op):
+        from . import ops
+        with torch.no_grad():
+            y = ops.unary(x, op)
+        ctx.act = 1 if op == 'relu' else 2
+        ctx.save_for_backward(y if op == 'relu' else x)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        saved, = ctx.saved_tensors
+        return ops.act_bwd(dy.to(saved.dtype).contiguous(), saved, ctx.act).view(saved.shape), None
+
+
+def unary_grad(x: Tensor, op: str) -> Tensor:
+    from . import ops
+    if op in ('relu', 'gelu') and x.is_cuda and x.dtype in _KERNEL_DTYPES:
+        return ActFn.apply(x, op)
+    return run(ops.unary, unary_t, x, op)
+
+
+def linear_grad(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int) -> Tensor:
+    """Differentiable WideLinear: the kernel-backed Function where the
+    tensors fit it, else the recompute path."""
+    from . import ops
+    ok = (x.is_cuda and weight.dtype in _KERNEL_DTYPES and x.dtype == weight.dtype
+          and (bias is None or bias.dtype == weight.dtype) and x.dim() >= 2 and weight.dim() == 3
+          and x.shape[0] == weight.shape[0] and x.shape[-1] == weight.shape[2] and weight.shape[0] <= 65535)
+    if not ok:
+        return run(ops.linear, linear_t, x, weight, bias, act)
+    return LinearFn.apply(x, weight, bias, act)
+
+
+def layernorm_grad(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: float) -> Tensor:
+    from . import ops
+    ok = (x.is_cuda and x.dtype in _KERNEL_DTYPES and weight.dtype == x.dtype and bias.dtype == x.dtype
+          and 0 < d <= 1024 and x.dim() >= 2 and x.shape[0] == n and x.shape[-1] == d and n <= 65535)
+    if not ok:
+        return run(ops.layernorm, layernorm_t, x, weight, bias, n, d, eps)
+    return LayerNormFn.apply(x, weight, bias, n, d, eps)

@@ -94,10 +94,17 @@ SIGNATURES = {
     "widek_mlp_chain_set_variant": [_int],
     "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
+    "widek_transpose": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
+    "widek_linear_bwd_workspace": [_i64] * 4 + [_int],
+    "widek_linear_bwd": [_c_void_p] * 6 + [_i64] * 4 + [_int, _c_void_p, _i64, _c_void_p],
+    "widek_act_bwd": [_c_void_p] * 3 + [_i64, _int, _int, _c_void_p],
+    "widek_layernorm_bwd_workspace": [_i64] * 3,
+    "widek_layernorm_bwd": [_c_void_p] * 6 + [_i64] * 3 + [_dbl, _int, _c_void_p, _i64, _c_void_p],
 }
 RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t, "widek_conv_workspace": ctypes.c_size_t,
             "widek_rnn_workspace": ctypes.c_size_t, "widek_conv_packed_weight_elems": _i64,
-            "widek_launch_count": ctypes.c_longlong}
+            "widek_launch_count": ctypes.c_longlong, "widek_linear_bwd_workspace": _i64,
+            "widek_layernorm_bwd_workspace": _i64}
 
 
 class WideKernelError(RuntimeError):
@@ -138,9 +145,9 @@ def lib() -> ctypes.CDLL:
 
 
 # Entry points that launch work (everything else is a query or a setter).
-_LAUNCHING = frozenset(n for n in SIGNATURES if n.endswith(("_fwd", "_fwd_ex", "_fwd_simt", "_recurrence"))
+_LAUNCHING = frozenset(n for n in SIGNATURES if n.endswith(("_fwd", "_fwd_ex", "_fwd_simt", "_recurrence", "_bwd"))
                        or n in ("widek_swap01", "widek_pack", "widek_copy2d", "widek_unary", "widek_binary",
-                                "widek_conv_pack_weight", "widek_batchnorm_train_fwd_noalloc"))
+                                "widek_conv_pack_weight", "widek_batchnorm_train_fwd_noalloc", "widek_transpose"))
 
 _timer: Optional["LaunchTimer"] = None
 

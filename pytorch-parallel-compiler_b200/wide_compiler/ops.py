@@ -62,7 +62,9 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
     if _compiling() and not force_simt:
         return torch.ops.widek.linear(x, weight, bias, act)
     if _AG.needs_grad(x, weight, bias):
-        return _AG.run(linear, _AG.linear_t, x, weight, bias, act, force_simt)
+        if force_simt:
+            return _AG.run(linear, _AG.linear_t, x, weight, bias, act, force_simt)
+        return _AG.linear_grad(x, weight, bias, act)
     dev = N.require_cuda(x, weight, bias, what="WideLinear")
     _same_dtype("WideLinear", weight, x, bias)
     n, o, k = weight.shape
@@ -80,6 +82,62 @@ def linear(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int = ACT_NON
                 N.dtype_code(weight), act, N.stream_ptr(dev))
     N.check(rc, "widek_linear_fwd")
     return y
+
+
+def transpose(x: Tensor) -> Tensor:
+    """[batch, R, C] -> [batch, C, R] as one dense copy (widek_transpose)."""
+    dev = N.require_cuda(x, what="transpose")
+    if x.dim() != 3:
+        raise ValueError(f"transpose: expected [batch, R, C], got {tuple(x.shape)}")
+    xd = _dense(x)
+    y = torch.empty((xd.shape[0], xd.shape[2], xd.shape[1]), device=dev, dtype=x.dtype)
+    with _guard(dev):
+        rc = N.lib().widek_transpose(xd.data_ptr(), y.data_ptr(), xd.shape[0], xd.shape[1], xd.shape[2],
+                                     N.dtype_code(x), N.stream_ptr(dev))
+    N.check(rc, "widek_transpose")
+    return y
+
+
+def linear_bwd(x: Tensor, weight: Tensor, dy: Tensor, need_dx: bool = True, need_dw: bool = True,
+               need_db: bool = True):
+    """Gradients of y = x W^T + b per model (no activation): (dx, dw, db),
+    None where not asked. x [N, ..., K], weight [N, O, K], dy [N, ..., O]
+    (widek_linear_bwd; the products on the forward's grouped GEMM)."""
+    dev = N.require_cuda(x, weight, dy, what="WideLinear backward")
+    _same_dtype("WideLinear backward", weight, x, dy)
+    n, o, k = weight.shape
+    m = math.prod(x.shape[1:-1])
+    xd, wd, dyd = _dense(x), _dense(weight), _dense(dy)
+    dx = torch.empty_like(xd) if need_dx else None
+    dw = torch.empty_like(wd) if need_dw else None
+    db = torch.empty((n, o), device=dev, dtype=weight.dtype) if need_db else None
+    if not (need_dx or need_dw or need_db):
+        return None, None, None
+    code = N.dtype_code(weight)
+    ws_bytes = N.lib().widek_linear_bwd_workspace(n, m, k, o, code)
+    if ws_bytes < 0:
+        raise ValueError(f"WideLinear backward: bad sizes n={n} m={m} k={k} o={o}")
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    with _guard(dev):
+        rc = N.lib().widek_linear_bwd(xd.data_ptr(), wd.data_ptr(), dyd.data_ptr(), N.ptr(dx), N.ptr(dw), N.ptr(db),
+                                      n, m, k, o, code, ws.data_ptr(), ws_bytes, N.stream_ptr(dev))
+    N.check(rc, "widek_linear_bwd")
+    return dx, dw, db
+
+
+def act_bwd(dy: Tensor, saved: Tensor, act: int) -> Tensor:
+    """dy * act'(saved): ReLU from its output, GELU (erf) from its input."""
+    dev = N.require_cuda(dy, saved, what="activation backward")
+    _same_dtype("activation backward", dy, saved)
+    if dy.shape != saved.shape:
+        raise ValueError(f"activation backward: {tuple(dy.shape)} vs {tuple(saved.shape)}")
+    dyd, sd = _dense(dy), _dense(saved)
+    out = torch.empty_like(dyd)
+    with _guard(dev):
+        rc = N.lib().widek_act_bwd(dyd.data_ptr(), sd.data_ptr(), out.data_ptr(), dyd.numel(), act,
+                                   N.dtype_code(dy), N.stream_ptr(dev))
+    N.check(rc, "widek_act_bwd")
+    return out
 
 
 def linear_layout(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int, in_packed: bool,
@@ -112,15 +170,6 @@ def linear_layout(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int, i
 _CHAIN_MEMO: dict = {}
 
 
-def _mlp_chain_t(x, weights, biases, acts, n, in_layout=0, out_layout=0):
-    """Torch formulation of mlp_chain (gradients): per-layer WideLinear and
-    activation, with the packed boundary layout when asked."""
-    h = x.reshape(x.shape[0], n, -1).transpose(0, 1) if in_layout == 1 else x
-    for w, b, a in zip(weights, biases, acts):
-        h = _AG.linear_t(h, w, b, a)
-    return h.transpose(0, 1).reshape(h.shape[1], -1) if out_layout == 1 else h
-
-
 def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Tensor]], acts: Sequence[int],
               n: int, in_layout: int = 0, out_layout: int = 0) -> Optional[Tensor]:
     """A chain of wide Linears with activations in one launch:
@@ -132,8 +181,13 @@ def mlp_chain(x: Tensor, weights: Sequence[Tensor], biases: Sequence[Optional[Te
     chain does not fit the one-CTA-per-model kernel. The argument arrays and
     the fit query are memoised per (pointers, shapes, layouts, dtype)."""
     if _AG.needs_grad(x, weights, biases):
-        return _AG.run(mlp_chain, _mlp_chain_t, x, list(weights), list(biases), list(acts), n, in_layout,
-                       out_layout)
+        # training: layer by layer, each WideLinear with its backward kernels
+        if not 1 <= len(weights) <= 8 or len(biases) != len(weights) or len(acts) != len(weights):
+            return None
+        h = swap01(x.reshape(x.shape[0], n, -1)) if in_layout == 1 else x
+        for w, b, a in zip(weights, biases, acts):
+            h = linear(h, w, b, a)
+        return swap01(h).reshape(h.shape[1], -1) if out_layout == 1 else h
     layers = len(weights)
     if not 1 <= layers <= 8 or len(biases) != layers or len(acts) != layers:
         return None
@@ -191,7 +245,7 @@ def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: floa
     if _compiling():
         return torch.ops.widek.layernorm(x, weight, bias, n, d, eps)
     if _AG.needs_grad(x, weight, bias):
-        return _AG.run(layernorm, _AG.layernorm_t, x, weight, bias, n, d, eps)
+        return _AG.layernorm_grad(x, weight, bias, n, d, eps)
     dev = N.require_cuda(x, weight, bias, what="WideLayerNorm")
     _same_dtype("WideLayerNorm", x, weight, bias)
     if x.shape[0] != n or x.shape[-1] != d:
@@ -205,6 +259,29 @@ def layernorm(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: floa
                                          N.stream_ptr(dev))
     N.check(rc, "widek_layernorm_fwd")
     return y
+
+
+def layernorm_bwd(x: Tensor, weight: Tensor, dy: Tensor, n: int, d: int, eps: float, need_dw: bool = True,
+                  need_db: bool = True):
+    """Gradients of the per-model LayerNorm: (dx, dweight, dbias), None where
+    not asked (widek_layernorm_bwd; statistics recomputed from x)."""
+    dev = N.require_cuda(x, weight, dy, what="WideLayerNorm backward")
+    _same_dtype("WideLayerNorm backward", x, weight, dy)
+    xd, wd, dyd = _dense(x), _dense(weight), _dense(dy)
+    outer = xd.numel() // (n * d) if n * d > 0 else 0
+    dx = torch.empty_like(xd)
+    dw = torch.empty((n * d,), device=dev, dtype=weight.dtype) if need_dw else None
+    db = torch.empty((n * d,), device=dev, dtype=weight.dtype) if need_db else None
+    ws_bytes = N.lib().widek_layernorm_bwd_workspace(n, outer, d)
+    if ws_bytes < 0:
+        raise ValueError(f"WideLayerNorm backward: bad sizes n={n} rows={outer} d={d}")
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    with _guard(dev):
+        rc = N.lib().widek_layernorm_bwd(xd.data_ptr(), wd.data_ptr(), dyd.data_ptr(), dx.data_ptr(), N.ptr(dw),
+                                         N.ptr(db), n, outer, d, float(eps), N.dtype_code(x), ws.data_ptr(),
+                                         ws_bytes, N.stream_ptr(dev))
+    N.check(rc, "widek_layernorm_bwd")
+    return dx, dw, db
 
 
 def layernorm_packed(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps: float) -> Tensor:
@@ -241,7 +318,7 @@ def swap01(x: Tensor) -> Tensor:
     if _compiling():
         return torch.ops.widek.swap01(x)
     if _AG.needs_grad(x):
-        return _AG.run(swap01, _AG.swap01_t, x)
+        return _AG.Swap01Fn.apply(x)
     dev = N.require_cuda(x, what="swap01")
     xd = _dense(x)
     a, b = xd.shape[0], xd.shape[1]
@@ -283,7 +360,7 @@ def unary(x: Tensor, op: str) -> Tensor:
     if _compiling():
         return torch.ops.widek.unary(x, op)
     if _AG.needs_grad(x):
-        return _AG.run(unary, _AG.unary_t, x, op)
+        return _AG.unary_grad(x, op)
     dev = N.require_cuda(x, what=f"unary {op}")
     xd = _dense(x)
     y = torch.empty_like(xd)

@@ -10,7 +10,7 @@ Each fixture ``<case>.pt`` is a dict:
     inputs    input tensors
     outputs   reference outputs (and updated running stats where relevant)
 
-Usage:  python tests/golden/make_golden.py [--root /path/to/reference]
+Usage:  python tests/golden/make_golden.py [--root /path/to/reference] [--only forward|grads]
 The fixtures are small (a few hundred KB in total) and committed.
 """
 from __future__ import annotations
@@ -260,11 +260,65 @@ def make_all(root: str) -> None:
               {'inputs': inputs, 'packed': packed}, {'y': out})
 
 
+def make_grads(root: str) -> None:
+    """Gradient fixtures: the reference's modules differentiated by torch
+    autograd (the reference's training path; its gradient-flow test is
+    wide_lstm.py:744-762) with a seeded upstream gradient dy, i.e.
+    d(sum(y * dy)) with respect to the input and every parameter."""
+    ref = refimport.load(root)
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    # WideLinear (wide_linear.py:162-171), then an optional activation the
+    # way a traced graph applies it (torch.relu / F.gelu on the wide output)
+    for name, (n, shape, i, o, bias, act) in {
+        'grad_linear_basic': (4, (9,), 24, 40, True, 'none'),
+        'grad_linear_gelu_3d': (3, (2, 5), 16, 12, True, 'gelu'),
+        'grad_linear_relu_nobias': (2, (7,), 20, 8, False, 'relu'),
+    }.items():
+        torch.manual_seed(zlib.crc32(name.encode()) % 1000)
+        mods = [nn.Linear(i, o, bias=bias) for _ in range(n)]
+        w = ref.WideLinear.from_modules(mods, strategy='einsum')
+        x = torch.randn(n, *shape, i, requires_grad=True)
+        y = w(x)
+        y = {'none': lambda t: t, 'relu': torch.relu, 'gelu': F.gelu}[act](y)
+        dy = torch.randn_like(y)
+        (y * dy).sum().backward()
+        grads = {'x': x.grad.clone()}
+        for k, v in w.named_parameters():
+            grads[k] = v.grad.clone()
+        _save(name, 'grad_linear', {'n': n, 'in': i, 'out': o, 'bias': bias, 'act': act}, w.state_dict(),
+              {'x': x.detach(), 'dy': dy}, {'y': y.detach(), 'grads': grads})
+
+    # WideLayerNorm (wide_layernorm.py:62-65)
+    torch.manual_seed(21)
+    n, d = 3, 40
+    mods = [nn.LayerNorm(d) for _ in range(n)]
+    for m in mods:
+        with torch.no_grad():
+            m.weight.uniform_(0.5, 1.5)
+            m.bias.normal_(0, 0.1)
+    w = ref.WideLayerNorm.from_modules(mods)
+    x = (torch.randn(n, 4, 6, d) * 2 + 0.5).requires_grad_(True)
+    y = w(x)
+    dy = torch.randn_like(y)
+    (y * dy).sum().backward()
+    grads = {'x': x.grad.clone()}
+    for k, v in w.named_parameters():
+        grads[k] = v.grad.clone()
+    _save('grad_layernorm', 'grad_layernorm', {'n': n, 'd': d, 'eps': 1e-5}, w.state_dict(),
+          {'x': x.detach(), 'dy': dy}, {'y': y.detach(), 'grads': grads})
+
+
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()
     ap.add_argument('--root', default=refimport.DEFAULT_ROOT)
+    ap.add_argument('--only', choices=['forward', 'grads'], default=None,
+                    help="generate only the forward or only the gradient fixtures")
     a = ap.parse_args()
     if not refimport.available(a.root):
         sys.exit(f"reference not found under {a.root!r}: pass --root or set WIDE_REFERENCE_ROOT to the "
                  "checkout that holds wide_compiler/")
-    make_all(a.root)
+    if a.only != 'grads':
+        make_all(a.root)
+    if a.only != 'forward':
+        make_grads(a.root)

@@ -64,9 +64,9 @@ def test_config_presets_and_debug_field():
 
 def _build_from_state(g):
     k, m, s = g['kind'], g['meta'], g['state']
-    if k == 'linear':
+    if k in ('linear', 'grad_linear'):
         mod = wc.WideLinear(m['n'], m['in'], m['out'], bias=m['bias'])
-    elif k == 'layernorm':
+    elif k in ('layernorm', 'grad_layernorm'):
         mod = wc.WideLayerNorm(m['n'], m['d'], m['eps'])
     elif k == 'batchnorm':
         cls = wc.WideBatchNorm2d if m['dims'] == 5 else wc.WideBatchNorm1d

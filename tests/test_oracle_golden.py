@@ -68,21 +68,40 @@ def oracle_eval(g):
             y = O.resblock(x, n, cat('conv1.weight'), cat('conv1.bias'), bn('bn1'), cat('conv2.weight'),
                            cat('conv2.bias'), bn('bn2'))
             return {'y': O.nfirst_to_packed(y)}
+    if k == 'grad_linear':
+        y = O.activation(O.linear(inp['x'], s['weight'], s.get('bias')), m['act'])
+        dx, dw, db = O.linear_grads(inp['x'], s['weight'], s.get('bias'), inp['dy'], m['act'])
+        out = {'y': y, 'grads.x': dx, 'grads.weight': dw}
+        if db is not None:
+            out['grads.bias'] = db
+        return out
+    if k == 'grad_layernorm':
+        dx, dw, db = O.layernorm_grads(inp['x'], s['weight'], inp['dy'], m['n'], m['d'], m['eps'])
+        return {'y': O.layernorm(inp['x'], s['weight'], s['bias'], m['n'], m['d'], m['eps']),
+                'grads.x': dx, 'grads.weight': dw, 'grads.bias': db}
     raise KeyError(k)
+
+
+def _expected(g, key):
+    if key.startswith('grads.'):
+        return g['outputs']['grads'][key[len('grads.'):]]
+    return g['outputs'][key]
 
 
 @pytest.mark.parametrize("name", golden_names())
 def test_oracle_matches_reference_fixture(name):
     g = load_golden(name)
     got = oracle_eval(g)
+    if g['kind'].startswith('grad_'):
+        assert {k[len('grads.'):] for k in got if k.startswith('grads.')} == set(g['outputs']['grads'])
     for key, val in got.items():
-        _close(val, g['outputs'][key])
+        _close(val, _expected(g, key))
 
 
 def test_fixture_set_covers_every_primitive():
     kinds = {load_golden(n)['kind'] for n in golden_names()}
     assert {'linear', 'layernorm', 'batchnorm', 'groupnorm', 'instancenorm', 'embedding', 'conv', 'attention',
-            'gru', 'lstm', 'traced'} <= kinds
+            'gru', 'lstm', 'traced', 'grad_linear', 'grad_layernorm'} <= kinds
 
 
 def test_pack_roundtrip_oracle():
