@@ -56,6 +56,7 @@ import torch.nn.functional as F  # noqa: E402
 METRIC = "wide-forward samples/s (N·B/s) at 1/2/4/8 B200; % of TC/HBM roofline"
 HEADLINE = "cfg3"
 ORDER = ["cfg3", "cfg1", "cfg2", "cfg4gru", "cfg4lstm", "cfg5", "bn2d_eval", "bn2d_train", "gn", "ln"]
+TRAINING = ["cfg2train", "lntrain"]      # forward + backward steps, run only when named
 
 # DRAM traffic (read + write bytes) per launch of the dominant kernel, from
 # one ncu capture of a reduced case scaled to the full launch by the units it
@@ -725,6 +726,117 @@ class LayerNormWl(_Norm):
             f"one full pass per rep (all {n} models), bf16, torch CPU mean/var/normalize/affine"
 
 
+class LinearCfg2Train(LinearCfg2):
+    """cfg2's WideLinear trained one step: forward, then the backward kernels
+    (dX, dW, db) for a fixed upstream gradient. Not in the default set; run
+    with --workload cfg2train. The dominant entry is widek_linear_bwd, bound
+    by the tensor pipe (two GEMMs of the forward's size) plus the transposes
+    that give them K-major operands."""
+    name = "cfg2train"
+    bound = "tensor"
+    peak_key = "tensor_sustained"
+
+    def work(self, n):
+        return {"widek_linear_bwd": 2 * 2 * n * self.b * self.i * self.o,
+                "widek_linear_fwd": 2 * n * self.b * self.i * self.o}
+
+    def config(self):
+        c = super().config()
+        c["workload"] = c["workload"].replace("cfg2 WideLinear", "cfg2 WideLinear training step (forward + "
+                                              "backward: dX, dW, db for a fixed upstream gradient)")
+        return c
+
+    def setup(self, dev, lo, hi, seed):
+        super().setup(dev, lo, hi, seed)
+        g = torch.Generator(device=dev).manual_seed(seed + 7)
+        self.dy = torch.randn(hi - lo, self.b, self.o, device=dev, generator=g).to(torch.bfloat16)
+
+    def step(self, x):
+        m = self.module
+        m.weight.grad = None
+        m.bias.grad = None
+        xg = x.detach().requires_grad_(True)
+        with torch.enable_grad():
+            m(xg).backward(self.dy)
+        return xg.grad
+
+    def torch_reference_step(self):
+        """The reference's training step on this GPU: its einsum + bias
+        forward differentiated by torch autograd (cuBLAS)."""
+        w = self.module.weight.detach().requires_grad_(True)
+        b = self.module.bias.detach().requires_grad_(True)
+
+        def fn():
+            w.grad = None
+            b.grad = None
+            xg = self.x.detach().requires_grad_(True)
+            with torch.enable_grad():
+                (torch.einsum('noi,nbi->nbo', w, xg) + b.unsqueeze(1)).backward(self.dy)
+            return xg.grad
+        return fn
+
+    def cpu_workload(self):
+        n = max(1, self.n_total // 32)
+        g = _gen(0)
+        w = (torch.randn(n, self.o, self.i, generator=g) / 32).to(torch.bfloat16).requires_grad_(True)
+        b = torch.zeros(n, self.o, dtype=torch.bfloat16, requires_grad=True)
+        x = torch.randn(n, self.b, self.i, generator=g).to(torch.bfloat16).requires_grad_(True)
+        dy = torch.randn(n, self.b, self.o, generator=g).to(torch.bfloat16)
+
+        def fn():
+            for t in (w, b, x):
+                t.grad = None
+            (torch.einsum('noi,nbi->nbo', w, x) + b.unsqueeze(1)).backward(dy)
+        return fn, n * self.b, f"{n} of the {self.n_total} models per rep: torch CPU einsum + bias, autograd backward"
+
+
+class LayerNormTrain(LayerNormWl):
+    """The cfg5 LayerNorm (at 4x its batch) trained one step: forward, then
+    widek_layernorm_bwd (dX, dgamma, dbeta). Not in the default set; run with
+    --workload lntrain."""
+    name = "lntrain"
+
+    def work(self, n):
+        elems = n * self.b * self.t * self.d
+        return {"widek_layernorm_bwd": 3 * elems * 2, "widek_layernorm_fwd": 2 * elems * 2}
+
+    def config(self):
+        c = super().config()
+        c["workload"] = c["workload"].replace("WideLayerNorm", "WideLayerNorm training step (forward + backward: "
+                                              "dX, dgamma, dbeta for a fixed upstream gradient)", 1)
+        return c
+
+    def setup(self, dev, lo, hi, seed):
+        super().setup(dev, lo, hi, seed)
+        self.dy = torch.randn(self.x.shape, device=dev,
+                              generator=torch.Generator(device=dev).manual_seed(seed + 7)).to(torch.bfloat16)
+
+    def step(self, x):
+        m = self.module
+        m.weight.grad = None
+        m.bias.grad = None
+        xg = x.detach().requires_grad_(True)
+        with torch.enable_grad():
+            m(xg).backward(self.dy)
+        return xg.grad
+
+    def cpu_workload(self):
+        n = max(1, self.n_total // 16)
+        g = _gen(0)
+        bf = torch.bfloat16
+        x = torch.randn(n, self.b, self.t, self.d, generator=g).to(bf).requires_grad_(True)
+        w = torch.ones(n * self.d, dtype=bf, requires_grad=True)
+        bb = torch.zeros(n * self.d, dtype=bf, requires_grad=True)
+        dy = torch.randn(x.shape, generator=g).to(bf)
+
+        def fn():
+            for t in (x, w, bb):
+                t.grad = None
+            shape = (n, 1, 1, self.d)
+            (torch.nn.functional.layer_norm(x, (self.d,), eps=1e-5) * w.view(shape) + bb.view(shape)).backward(dy)
+        return fn, n * self.b, f"{n} of the {self.n_total} models per rep: torch CPU layer_norm + affine, autograd"
+
+
 def make_workload(name, models=None):
     wl = _make_workload(name)
     if models:
@@ -738,6 +850,7 @@ def _make_workload(name):
         "cfg4gru": lambda: RnnCfg4("gru"), "cfg4lstm": lambda: RnnCfg4("lstm"), "cfg5": lambda: AttnCfg5(),
         "bn2d_eval": lambda: BatchNormWl(False), "bn2d_train": lambda: BatchNormWl(True),
         "gn": lambda: GroupNormWl(), "ln": lambda: LayerNormWl(),
+        "cfg2train": lambda: LinearCfg2Train(), "lntrain": lambda: LayerNormTrain(),
     }[name]()
 
 
@@ -1116,8 +1229,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all"] + ORDER,
-                    help="all: the cfg3 headline plus every other configuration under 'configs'")
+    ap.add_argument("--workload", default="all", choices=["all"] + ORDER + TRAINING,
+                    help="all: the cfg3 headline plus every other configuration under 'configs'; "
+                         "cfg2train / lntrain: forward + backward steps (not part of 'all')")
     ap.add_argument("--sub-steps", type=int, default=20, help="timed steps of each non-headline configuration")
     ap.add_argument("--models", type=int, default=None,
                     help="override the number of models N (reduced cases for profiling captures only)")

@@ -32,6 +32,8 @@
 
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 namespace widek {
 namespace {
 
@@ -124,25 +126,39 @@ int launch_transpose(const void* x, void* y, int64_t batch, int64_t R, int64_t C
 constexpr int kSumThreads = 256;
 constexpr int kSumRows = 128;         // rows per partial
 
-template <typename T>
+// PAIR: two adjacent 16-bit columns per thread (one 4-byte load per row, so
+// a warp reads 128 contiguous bytes of a row, as in the fp32 case).
+template <typename T, bool PAIR>
 __global__ void __launch_bounds__(kSumThreads) colsum_part_kernel(const T* __restrict__ x, float* __restrict__ part,
                                                                    int64_t M, int64_t C, int nblk) {
+    constexpr int P = PAIR ? 2 : 1;
     const int64_t i = blockIdx.z;
     const int blk = blockIdx.y;
-    const int64_t c = (int64_t)blockIdx.x * kSumThreads + threadIdx.x;
+    const int64_t c = ((int64_t)blockIdx.x * kSumThreads + threadIdx.x) * P;
     if (c >= C) return;
     const int64_t r_end = min(M, (int64_t)(blk + 1) * kSumRows);
     const T* p = x + i * M * C + c;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    float s0[P], s1[P];
+#pragma unroll
+    for (int q = 0; q < P; ++q) s0[q] = s1[q] = 0.f;
     int64_t r = (int64_t)blk * kSumRows;
-    for (; r + 4 <= r_end; r += 4) {
-        s0 += to_f<T>(p[r * C]);
-        s1 += to_f<T>(p[(r + 1) * C]);
-        s2 += to_f<T>(p[(r + 2) * C]);
-        s3 += to_f<T>(p[(r + 3) * C]);
+    auto add = [&](float (&acc)[P], int64_t row) {
+        if constexpr (PAIR) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(p + row * C);
+            const T* e = reinterpret_cast<const T*>(&w);
+            acc[0] += to_f<T>(e[0]);
+            acc[P - 1] += to_f<T>(e[1]);
+        } else {
+            acc[0] += to_f<T>(p[row * C]);
+        }
+    };
+    for (; r + 2 <= r_end; r += 2) {
+        add(s0, r);
+        add(s1, r + 1);
     }
-    for (; r < r_end; ++r) s0 += to_f<T>(p[r * C]);
-    part[(i * nblk + blk) * C + c] = (s0 + s1) + (s2 + s3);
+    if (r < r_end) add(s0, r);
+#pragma unroll
+    for (int q = 0; q < P; ++q) part[(i * nblk + blk) * C + c + q] = s0[q] + s1[q];
 }
 
 template <typename T>
@@ -233,20 +249,37 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_bwd_kernel(const T* __re
     for (int e = 0; e < E; ++e) ag[e] = ab[e] = 0.f;
     const int64_t r_begin = (int64_t)blk * rpc;
     const int64_t r_end = min(outer, r_begin + rpc);
+    // The next row's raw bytes are loaded before the current row is
+    // reduced, so each warp keeps two rows in flight.
+    using Raw = typename std::conditional<V == 1, T, uint4>::type;
+    Raw px[CPL], pg[CPL];
+    auto load_raw = [&](int64_t row) {
+        const int64_t o = (model * outer + row) * d;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const int ch = lane + 32 * c;
+            if (ch < nch) {
+                px[c] = *reinterpret_cast<const Raw*>(x + o + (int64_t)ch * V);
+                pg[c] = *reinterpret_cast<const Raw*>(dy + o + (int64_t)ch * V);
+            }
+        }
+    };
+    if (r_begin + warp < r_end) load_raw(r_begin + warp);
     for (int64_t r = r_begin + warp; r < r_end; r += kLnWarps) {
         const int64_t off = (model * outer + r) * d;
         float xv[E], gv[E];
 #pragma unroll
         for (int c = 0; c < CPL; ++c) {
             const int ch = lane + 32 * c;
-            if (ch < nch) {
-                ln_load<T, V>(x + off + (int64_t)ch * V, xv + c * V);
-                ln_load<T, V>(dy + off + (int64_t)ch * V, gv + c * V);
-            } else {
+            const T* ex = reinterpret_cast<const T*>(&px[c]);
+            const T* eg = reinterpret_cast<const T*>(&pg[c]);
 #pragma unroll
-                for (int j = 0; j < V; ++j) xv[c * V + j] = gv[c * V + j] = 0.f;
+            for (int j = 0; j < V; ++j) {
+                xv[c * V + j] = ch < nch ? to_f<T>(ex[j]) : 0.f;
+                gv[c * V + j] = ch < nch ? to_f<T>(eg[j]) : 0.f;
             }
         }
+        if (r + kLnWarps < r_end) load_raw(r + kLnWarps);
         float s = 0.f;
 #pragma unroll
         for (int e = 0; e < E; ++e) s += xv[e];
@@ -438,8 +471,13 @@ struct ColsumLaunch {
     int run() {
         using namespace widek;
         const unsigned cx = (unsigned)((c + kSumThreads - 1) / kSumThreads);
-        colsum_part_kernel<T><<<dim3(cx, (unsigned)nblk, (unsigned)n), kSumThreads, 0, st>>>(static_cast<const T*>(x),
-                                                                                           part, m, c, nblk);
+        const bool pair = sizeof(T) == 2 && c % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 3u) == 0;
+        if (pair)
+            colsum_part_kernel<T, true><<<dim3((cx + 1) / 2, (unsigned)nblk, (unsigned)n), kSumThreads, 0, st>>>(
+                static_cast<const T*>(x), part, m, c, nblk);
+        else
+            colsum_part_kernel<T, false><<<dim3(cx, (unsigned)nblk, (unsigned)n), kSumThreads, 0, st>>>(
+                static_cast<const T*>(x), part, m, c, nblk);
         int rc = check_launch("linear_bwd (bias partial sums)");
         if (rc != WIDEK_OK) return rc;
         colsum_final_kernel<T><<<dim3(cx, (unsigned)n), kSumThreads, 0, st>>>(part, static_cast<T*>(out), c, nblk);
