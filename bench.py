@@ -91,6 +91,7 @@ class ClockSampler:
         self.lines = []                  # (arrival time, line)
         self._t = None
         self._fd = None
+        self.t_start = 0.0
 
     def start(self):
         try:
@@ -108,8 +109,8 @@ class ClockSampler:
             return
         # wait (bounded) for the first sample, so that a short run still has
         # samples in its window
-        t0 = time.perf_counter()
-        while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 10.0:
+        t0 = self.t_start = time.perf_counter()
+        while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 30.0:
             time.sleep(0.02)
 
     def _read(self):
@@ -979,6 +980,7 @@ def _gather_fn(wl, ctx):
 def measure(name, ctx, clocks):
     from wide_compiler import _native as N
     args = ctx.args
+    mark_setup = clocks.mark()
     wl = make_workload(name, args.models)
     if args.weak:
         lo, hi = 0, wl.n_total
@@ -1084,6 +1086,17 @@ def measure(name, ctx, clocks):
     clk = clocks.summary(mark0, clocks.mark())
     clk["window"] = (f"nvidia-smi samples every 100 ms over {args.clock_window:.1f} s of untimed steps just "
                      f"before the timed region, the timed region and the e2e loop")
+    if not clk.get("samples"):
+        # no sample arrived in that window: widen it to this workload's whole
+        # measurement (set-up, warm-up and the steps above), and say so
+        wide = clocks.summary(mark_setup, clocks.mark())
+        if wide.get("samples"):
+            clk = wide
+            clk["window"] = ("no nvidia-smi sample arrived during the timed steps; samples over this workload's "
+                             "whole measurement (set-up, warm-up, timed and e2e steps)")
+    clk["samples_total"] = len(clocks.lines)
+    if clocks.lines:
+        clk["first_sample_s"] = round(clocks.lines[0][0] - clocks.t_start, 3)
 
     total_models = wl.n_total if not args.weak else wl.n_total * ctx.world
     samples = wl.samples(total_models)
@@ -1236,7 +1249,7 @@ def main():
     ap.add_argument("--models", type=int, default=None,
                     help="override the number of models N (reduced cases for profiling captures only)")
     ap.add_argument("--e2e-steps", type=int, default=20)
-    ap.add_argument("--clock-window", type=float, default=0.5,
+    ap.add_argument("--clock-window", type=float, default=2.0,
                     help="seconds of untimed steps before each timed region while clocks are sampled")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--weak", action="store_true", help="every rank runs all N models (weak scaling)")
