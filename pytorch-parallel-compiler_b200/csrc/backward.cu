@@ -9,13 +9,15 @@
 //
 //   WideLinear  y[i] = x[i] W[i]^T + b[i]     (x [N, M, K], W [N, O, K])
 //     dX[i] = dY[i] W[i]          dW[i] = dY[i]^T x[i]      db[i] = sum_rows dY[i]
-//   Both products run on the forward's grouped GEMM (tcgen05 for bf16/f16,
-//   split-operand tcgen05 or CUDA cores for fp32), whose operands are
-//   K-major: dX = dY . (W^T)^T needs W^T [N, K, O]; dW = (dY^T) . (x^T)^T
-//   needs dY^T [N, O, M] and x^T [N, K, M]. Those three come from one batched
-//   transpose kernel into a caller-provided workspace; the bias gradient is
-//   a column sum (per-block partials in fp32, then one pass over the blocks,
-//   so the result does not depend on scheduling).
+//   For bf16/f16 with 16-byte rows both products run on the tcgen05 GEMM
+//   with MN-major operands read straight from W, dY and x (dX: W MN-major;
+//   dW: dY and x MN-major). Otherwise (fp32: split-operand tcgen05 or CUDA
+//   cores; ragged widths) they run on the forward's K-major GEMM:
+//   dX = dY . (W^T)^T needs W^T [N, K, O]; dW = (dY^T) . (x^T)^T needs
+//   dY^T [N, O, M] and x^T [N, K, M], from one batched transpose kernel into
+//   a caller-provided workspace. The bias gradient is a column sum
+//   (per-block partials in fp32, then one pass over the blocks, so the
+//   result does not depend on scheduling).
 //
 //   activation  dpre = dY * act'(.)   ReLU from the saved output (y > 0),
 //                                     exact-erf GELU from the saved
@@ -553,18 +555,26 @@ int widek_linear_bwd(const void* x, const void* w, const void* dy, void* dx, voi
     }
     if (!dy || (dx && !w) || (dw && !x)) return set_error(WIDEK_ERR_INVALID, "linear_bwd: null pointer");
     if (dx) {
-        // dX [n, m, k] = dY [n, m, o] . (W^T [n, k, o])^T
-        if ((rc = launch_transpose(w, ws + L.wt, n, o, k, es, st)) != WIDEK_OK) return rc;
-        if ((rc = widek_linear_fwd(dy, ws + L.wt, nullptr, dx, n, m, o, k, dtype, WIDEK_ACT_NONE, stream)) != WIDEK_OK)
-            return rc;
+        // dX [n, m, k] = dY [n, m, o] . W [n, o, k]: W read MN-major by the
+        // tcgen05 GEMM where it can, else dY . (W^T [n, k, o])^T on the
+        // forward's GEMM
+        rc = gemm_tc_mn(dy, w, dx, n, m, o, k, false, true, dtype, st);
+        if (rc == WIDEK_ERR_UNSUPPORTED) {
+            if ((rc = launch_transpose(w, ws + L.wt, n, o, k, es, st)) != WIDEK_OK) return rc;
+            rc = widek_linear_fwd(dy, ws + L.wt, nullptr, dx, n, m, o, k, dtype, WIDEK_ACT_NONE, stream);
+        }
+        if (rc != WIDEK_OK) return rc;
     }
     if (dw) {
-        // dW [n, o, k] = dY^T [n, o, m] . (x^T [n, k, m])^T
-        if ((rc = launch_transpose(dy, ws + L.dyt, n, m, o, es, st)) != WIDEK_OK) return rc;
-        if ((rc = launch_transpose(x, ws + L.xt, n, m, k, es, st)) != WIDEK_OK) return rc;
-        if ((rc = widek_linear_fwd(ws + L.dyt, ws + L.xt, nullptr, dw, n, o, m, k, dtype, WIDEK_ACT_NONE, stream)) !=
-            WIDEK_OK)
-            return rc;
+        // dW [n, o, k] = dY^T . x with both read MN-major where the tcgen05
+        // GEMM can, else dY^T [n, o, m] . (x^T [n, k, m])^T
+        rc = gemm_tc_mn(dy, x, dw, n, o, m, k, true, true, dtype, st);
+        if (rc == WIDEK_ERR_UNSUPPORTED) {
+            if ((rc = launch_transpose(dy, ws + L.dyt, n, m, o, es, st)) != WIDEK_OK) return rc;
+            if ((rc = launch_transpose(x, ws + L.xt, n, m, k, es, st)) != WIDEK_OK) return rc;
+            rc = widek_linear_fwd(ws + L.dyt, ws + L.xt, nullptr, dw, n, o, m, k, dtype, WIDEK_ACT_NONE, stream);
+        }
+        if (rc != WIDEK_OK) return rc;
     }
     if (db) {
         ColsumLaunch C{dy, db, reinterpret_cast<float*>(ws + L.part), n, m, o, L.nblk, st};

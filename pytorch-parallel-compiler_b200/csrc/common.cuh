@@ -55,6 +55,15 @@ int linear_f32x3_strided(const float* x, const float* w, const float* bias, floa
                          int64_t o, int64_t w_ms, int64_t w_rs, int64_t x_ms, int64_t x_bs, int64_t x_rpb,
                          int64_t y_ms, int64_t y_bs, cudaStream_t st);
 
+// Grouped GEMM on the tcgen05 kernel of linear_sm100.cu, y[i] = A_i . B_i
+// (bf16/f16, fp32 accumulate, dense y [n, M, N]) with either operand read
+// MN-major: A is [n, M, K] (a_mn false) or [n, K, M] (a_mn true), B is
+// [n, N, K] (b_mn false) or [n, K, N] (b_mn true). Returns
+// WIDEK_ERR_UNSUPPORTED, launching nothing, when the dtype, the extents
+// (contiguous extents multiples of 8) or the alignment do not fit.
+int gemm_tc_mn(const void* a, const void* b, void* y, int64_t n, int64_t M, int64_t K, int64_t N, bool a_mn,
+               bool b_mn, int dtype, cudaStream_t st);
+
 int linear_simt_strided(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m, int64_t k,
                         int64_t o, int64_t w_ms, int64_t w_rs, int dtype, int act, cudaStream_t st,
                         int64_t x_ms = -1, int64_t x_bs = 0, int64_t x_rpb = 0, int64_t y_ms = -1,

@@ -87,14 +87,25 @@ __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;"
 // Named barrier of one 128-thread epilogue warpgroup (ids 1 and 2).
 __device__ __forceinline__ void wg_bar_sync(int wg) { asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory"); }
 
-template <typename T, int BN, int STAGES, bool TMA_STORE>
+// A_MN / B_MN: the operand is read MN-major (its M / N index contiguous in
+// memory, one row per K index), as the backward products need: x^T-like
+// operands come straight from the untransposed tensors. An MN-major tile is
+// loaded as 64-column boxes (128 B rows, 128-byte swizzle) of BK rows each,
+// 8 KB apart; its descriptor's leading byte offset is that 8 KB (next 64
+// columns), the stride byte offset 1 KB (next 8 K rows), and a K step of 16
+// advances 16 rows (2 KB).
+template <typename T, int BN, int STAGES, bool TMA_STORE, bool A_MN = false, bool B_MN = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias, T* __restrict__ y,
                      int n_models, int M, int K, int O, int act, int vec_store, int l2_hints, GemmRows rw,
                      int* err) {
     using S = GemmSmem<BN, STAGES, TMA_STORE>;
-    constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value);
+    constexpr uint32_t IDESC = idesc_f16(BM, BN, std::is_same<T, __nv_bfloat16>::value) | (A_MN ? 1u << 15 : 0u) |
+                               (B_MN ? 1u << 16 : 0u);
+    constexpr uint32_t kMnBlock = 64 * BK * 2;        // one 64-column box of an MN-major tile
+    constexpr uint32_t A_KSTEP = A_MN ? (16 * 128) >> 4 : 2;   // descriptor units per K step of 16
+    constexpr uint32_t B_KSTEP = B_MN ? (16 * 128) >> 4 : 2;
     constexpr uint32_t TMEM_COLS = 2 * BN;
 
     extern __shared__ uint8_t smem_raw[];
@@ -163,9 +174,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
-                    tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], kb * BK, (mt * BM) % rw.rpb,
-                                (mt * BM) / rw.rpb, model, pol_x);
-                    tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, nt * BN, model, pol_w);
+                    if constexpr (A_MN) {
+#pragma unroll
+                        for (int j = 0; j < BM / 64; ++j)
+                            tma_load_3d(sA + s * S::A_BYTES + j * kMnBlock, &tm_x, &full[s], mt * BM + j * 64,
+                                        kb * BK, model, pol_x);
+                    } else {
+                        tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], kb * BK, (mt * BM) % rw.rpb,
+                                    (mt * BM) / rw.rpb, model, pol_x);
+                    }
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_3d(sB + s * S::B_BYTES + j * kMnBlock, &tm_w, &full[s], nt * BN + j * 64,
+                                        kb * BK, model, pol_w);
+                    } else {
+                        tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, nt * BN, model, pol_w);
+                    }
                 }
                 __syncwarp();
                 ++issued;
@@ -197,8 +222,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             int local = 0;
-            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
-            const uint64_t b_desc0 = sdesc_kmajor_sw128(smem_addr(sB));
+            const uint64_t a_desc0 =
+                A_MN ? sdesc_mnmajor_sw128(smem_addr(sA), kMnBlock) : sdesc_kmajor_sw128(smem_addr(sA));
+            const uint64_t b_desc0 =
+                B_MN ? sdesc_mnmajor_sw128(smem_addr(sB), kMnBlock) : sdesc_kmajor_sw128(smem_addr(sB));
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
                 const int acc = local & 1;
                 const uint32_t aph = (local >> 1) & 1;
@@ -211,8 +238,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint64_t ad = a_desc0 + (uint64_t)((s * S::A_BYTES) >> 4);
                     const uint64_t bd = b_desc0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)   // 16 elements = 32 bytes along the swizzled row
-                        umma_f16_ss(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+                    for (int k = 0; k < BK / 16; ++k)   // K-major: 32 bytes along the row; MN-major: 16 rows
+                        umma_f16_ss(d_tmem, ad + A_KSTEP * k, bd + B_KSTEP * k, IDESC, (kb | k) != 0);
                     umma_commit(&empty[s]);
                     if (++s == STAGES) { s = 0; ph ^= 1; }
                 }
@@ -641,6 +668,71 @@ int launch_tc(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m,
     return check_launch("widek_linear_fwd (tcgen05)");
 }
 
+// y[i] = A_i . B_i on linear_tc_kernel with either operand MN-major (see
+// gemm_tc_mn). The MN-major maps are 3-D {cols, K rows, model} with 64-column
+// boxes; the K-major ones are the forward's.
+template <typename T, int BN, int STAGES, bool TMA_STORE, bool A_MN, bool B_MN>
+int launch_tc_mn(const T* a, const T* b, T* y, int64_t n, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+    using S = GemmSmem<BN, STAGES, TMA_STORE>;
+    CUtensorMap ta, tb, ty;
+    memset(&ty, 0, sizeof(ty));
+    if (A_MN) {
+        const uint64_t dims[3] = {(uint64_t)M, (uint64_t)K, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)M * 2, (uint64_t)K * M * 2};
+        const uint32_t box[3] = {64, BK, 1};
+        int rc = encode_tmap_tiled(&ta, tmap_dtype<T>(), 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    } else {
+        const uint64_t dims[4] = {(uint64_t)K, (uint64_t)M, 1, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)K * 2, (uint64_t)M * K * 2, (uint64_t)M * K * 2};
+        const uint32_t box[4] = {BK, BM, 1, 1};
+        int rc = encode_tmap_tiled(&ta, tmap_dtype<T>(), 4, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    if (B_MN) {
+        const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
+        const uint32_t box[3] = {64, BK, 1};
+        int rc = encode_tmap_tiled(&tb, tmap_dtype<T>(), 3, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    } else {
+        const uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)K * 2, (uint64_t)N * K * 2};
+        const uint32_t box[3] = {BK, BN, 1};
+        int rc = encode_tmap_tiled(&tb, tmap_dtype<T>(), 3, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    if (TMA_STORE) {
+        const uint64_t dims[4] = {(uint64_t)N, (uint64_t)M, 1, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)N * 2, (uint64_t)M * N * 2, (uint64_t)M * N * 2};
+        const uint32_t box[4] = {32, BM, 1, 1};
+        int rc = encode_tmap_tiled(&ty, tmap_dtype<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
+    }
+    auto kern = linear_tc_kernel<T, BN, STAGES, TMA_STORE, A_MN, B_MN>;
+    static bool attr_done[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "gemm (MN-major): cannot reserve %u bytes of shared memory", S::TOTAL);
+        attr_done[dev] = true;
+    }
+    const int64_t tiles = n * ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
+    const int vec_store = (N % 8 == 0) && aligned16(y);
+    const GemmRows rw{(int)M, M * N, M * N};
+    kern<<<grid, kGemmThreads, S::TOTAL, st>>>(ta, tb, ty, nullptr, y, (int)n, (int)M, (int)K, (int)N,
+                                               WIDEK_ACT_NONE, vec_store, 1, rw, device_error_ptr());
+    return check_launch("gemm (tcgen05, MN-major operands)");
+}
+
+template <typename T, bool A_MN, bool B_MN>
+int gemm_tc_mn_t(const T* a, const T* b, T* y, int64_t n, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+    if (N > 128) return launch_tc_mn<T, 256, 4, true, A_MN, B_MN>(a, b, y, n, M, K, N, st);
+    if (N > 64) return launch_tc_mn<T, 128, 6, true, A_MN, B_MN>(a, b, y, n, M, K, N, st);
+    return launch_tc_mn<T, 64, 8, true, A_MN, B_MN>(a, b, y, n, M, K, N, st);
+}
+
 template <typename T>
 int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
                    const LinRows& rows, cudaStream_t st) {
@@ -744,6 +836,31 @@ int linear_entry(const void* x, const void* w, const void* bias, void* y, int64_
 }
 
 }  // namespace
+
+int gemm_tc_mn(const void* a, const void* b, void* y, int64_t n, int64_t M, int64_t K, int64_t N, bool a_mn,
+               bool b_mn, int dtype, cudaStream_t st) {
+    if (dtype != WIDEK_BF16 && dtype != WIDEK_F16) return WIDEK_ERR_UNSUPPORTED;
+    if (n <= 0 || M <= 0 || K <= 0 || N <= 0 || n > 0x7fffffff || M > 0x7fffffff || K > 0x7fffffff ||
+        N > 0x7fffffff || n * ((M + 127) / 128) * ((N + 63) / 64) > 0x7fffffff)
+        return WIDEK_ERR_UNSUPPORTED;
+    // TMA rows start on 16-byte boundaries: the contiguous extent of each
+    // operand (K when K-major, M / N when MN-major) and of y a multiple of 8
+    if ((a_mn ? M : K) % 8 != 0 || (b_mn ? N : K) % 8 != 0 || N % 8 != 0 || !aligned16(a) || !aligned16(b) ||
+        !aligned16(y))
+        return WIDEK_ERR_UNSUPPORTED;
+    auto go = [&](auto tag) -> int {
+        using T = decltype(tag);
+        const T* A = static_cast<const T*>(a);
+        const T* B = static_cast<const T*>(b);
+        T* Y = static_cast<T*>(y);
+        if (a_mn && b_mn) return gemm_tc_mn_t<T, true, true>(A, B, Y, n, M, K, N, st);
+        if (a_mn) return gemm_tc_mn_t<T, true, false>(A, B, Y, n, M, K, N, st);
+        if (b_mn) return gemm_tc_mn_t<T, false, true>(A, B, Y, n, M, K, N, st);
+        return gemm_tc_mn_t<T, false, false>(A, B, Y, n, M, K, N, st);
+    };
+    return dtype == WIDEK_BF16 ? go(__nv_bfloat16{}) : go(__half{});
+}
+
 }  // namespace widek
 
 extern "C" int widek_linear_set_variant(int variant) {

@@ -231,7 +231,22 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, A and B K-major.
+// MN-major operand tile written by TMA with 128-byte swizzling: 64 elements
+// of M (or N) per 128-byte row, one row per K index, 8-row groups 1024 bytes
+// apart (stride byte offset); the next 64 elements of M / N start lbo_bytes
+// further (leading byte offset). A K step of 16 is 16 rows (2 KB) on.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);            // start address, 16-byte units
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;  // leading byte offset: next 64-wide M / N block
+    d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: next 8 K rows
+    d |= (uint64_t)1 << 46;                            // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;                            // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A and B K-major (bit
+// 15 / 16 set by the caller for an MN-major A / B).
 // is_bf16 selects bf16 (1) or f16 (0) for both operands.
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool is_bf16) {
     return (1u << 4)                                   // D format: f32
