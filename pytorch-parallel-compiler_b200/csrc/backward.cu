@@ -126,7 +126,7 @@ int launch_transpose(const void* x, void* y, int64_t batch, int64_t R, int64_t C
 // (fp32), then out[i][c] = sum over blocks, in the storage dtype.
 // ---------------------------------------------------------------------------
 constexpr int kSumThreads = 256;
-constexpr int kSumRows = 128;         // rows per partial
+constexpr int kSumRows = 32;          // rows per partial
 
 // PAIR: two adjacent 16-bit columns per thread (one 4-byte load per row, so
 // a warp reads 128 contiguous bytes of a row, as in the fp32 case).
@@ -154,11 +154,13 @@ __global__ void __launch_bounds__(kSumThreads) colsum_part_kernel(const T* __res
             acc[0] += to_f<T>(p[row * C]);
         }
     };
-    for (; r + 2 <= r_end; r += 2) {
+    for (; r + 4 <= r_end; r += 4) {       // four independent loads in flight
         add(s0, r);
         add(s1, r + 1);
+        add(s0, r + 2);
+        add(s1, r + 3);
     }
-    if (r < r_end) add(s0, r);
+    for (; r < r_end; ++r) add(s0, r);
 #pragma unroll
     for (int q = 0; q < P; ++q) part[(i * nblk + blk) * C + c + q] = s0[q] + s1[q];
 }
@@ -355,20 +357,36 @@ __global__ void __launch_bounds__(kLnThreads) layernorm_bwd_kernel(const T* __re
 }
 
 // dgamma[i*d + j] = sum over blocks of part[i][blk][0][j] (dbeta: [1]).
+// A CTA takes 32 columns; its 8 warps sum every 8th block each (lanes on
+// consecutive columns), then warp 0 adds the 8 partial sums in order.
 template <typename T>
 __global__ void __launch_bounds__(kSumThreads) ln_param_reduce_kernel(const float* __restrict__ part, T* __restrict__ dw,
                                                                        T* __restrict__ db, int d, int nblk) {
+    __shared__ float red[2][kSumThreads / 32][32];
     const int64_t i = blockIdx.y;
-    const int j = blockIdx.x * kSumThreads + threadIdx.x;
-    if (j >= d) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j = blockIdx.x * 32 + lane;
     float sg = 0.f, sb = 0.f;
-    for (int b = 0; b < nblk; ++b) {
-        const float* p = part + ((i * nblk + b) * 2) * d;
-        sg += p[j];
-        sb += p[d + j];
+    if (j < d) {
+        for (int b = warp; b < nblk; b += kSumThreads / 32) {
+            const float* p = part + ((i * nblk + b) * 2) * d;
+            sg += p[j];
+            sb += p[d + j];
+        }
     }
-    if (dw) dw[i * d + j] = from_f<T>(sg);
-    if (db) db[i * d + j] = from_f<T>(sb);
+    red[0][warp][lane] = sg;
+    red[1][warp][lane] = sb;
+    __syncthreads();
+    if (warp == 0 && j < d) {
+        float g = 0.f, bsum = 0.f;
+#pragma unroll
+        for (int q = 0; q < kSumThreads / 32; ++q) {
+            g += red[0][q][lane];
+            bsum += red[1][q][lane];
+        }
+        if (dw) dw[i * d + j] = from_f<T>(g);
+        if (db) db[i * d + j] = from_f<T>(bsum);
+    }
 }
 
 int ln_blocks(int64_t n, int64_t outer) {
@@ -429,8 +447,8 @@ struct LnBwdLaunch {
         }
         int rc = check_launch("layernorm_bwd");
         if (rc != WIDEK_OK || (!dw && !db)) return rc;
-        ln_param_reduce_kernel<T><<<dim3((unsigned)((d + kSumThreads - 1) / kSumThreads), (unsigned)n), kSumThreads, 0,
-                                    st>>>(part, static_cast<T*>(dw), static_cast<T*>(db), d, nblk);
+        ln_param_reduce_kernel<T><<<dim3((unsigned)((d + 31) / 32), (unsigned)n), kSumThreads, 0, st>>>(
+            part, static_cast<T*>(dw), static_cast<T*>(db), d, nblk);
         return check_launch("layernorm_bwd (parameter sums)");
     }
 };
