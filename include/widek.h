@@ -120,6 +120,22 @@ WIDEK_API int widek_linear_fwd_ex(const void* x, const void* w, const void* bias
                                   int64_t n, int64_t m, int64_t k, int64_t o, int64_t rows_per_block,
                                   int in_layout, int out_layout, int dtype, int act, void* stream);
 
+/* y = LayerNorm(x @ w^T + bias) * ln_w + ln_b per model and row, in one
+ * launch: the attention output projection and the WideLayerNorm after it.
+ * Rows and layouts as widek_linear_fwd_ex (N-first or packed on either side,
+ * rows_per_block for the packed form); ln_w, ln_b: [n, o] (the flat [n*o]
+ * parameters of WideLayerNorm); bias [n, o] or NULL; biased variance with
+ * eps; statistics in fp32 from the unrounded projection. bf16/f16 with
+ * o a multiple of 16 up to 512, k a multiple of 8 and 16-byte aligned x, w
+ * and y; otherwise returns WIDEK_ERR_UNSUPPORTED, launching nothing (run
+ * widek_linear_fwd_ex and widek_layernorm_fwd_ex instead). Replaces the
+ * output projection of wide_compiler/core/primitives/wide_attention.py:233-236
+ * followed by wide_layernorm.py:62-65. */
+WIDEK_API int widek_linear_ln_fwd_ex(const void* x, const void* w, const void* bias, const void* ln_w,
+                                     const void* ln_b, void* y, int64_t n, int64_t m, int64_t k, int64_t o,
+                                     int64_t rows_per_block, int in_layout, int out_layout, double eps,
+                                     int dtype, void* stream);
+
 /* Selects the tensor-core tiling of widek_linear_fwd for this process:
  * 0 = automatic (single-CTA 128xBN tiles), 1 = single-CTA tiles,
  * 2 = CTA-pair (cta_group::2) 256x256 tiles when m > 128 and o > 128,

@@ -733,6 +733,331 @@ int gemm_tc_mn_t(const T* a, const T* b, T* y, int64_t n, int64_t M, int64_t K, 
     return launch_tc_mn<T, 64, 8, true, A_MN, B_MN>(a, b, y, n, M, K, N, st);
 }
 
+// ---------------------------------------------------------------------------
+// WideLinear with a fused LayerNorm epilogue:
+//   y[i][r] = LayerNorm(x[i][r] @ w[i]^T + bias[i]) * ln_w[i] + ln_b[i]
+// for o <= 512 output features (a multiple of 16): the attention output
+// projection followed by WideLayerNorm. A tile is 128 rows x all o columns,
+// so each row's statistics are complete in TMEM: one 512-column fp32
+// accumulator (M = 128; two MMAs of N = 256 / o - 256 per K step when
+// o > 256). Same warp roles as linear_tc_kernel; the accumulator is not
+// double-buffered (the whole TMEM), so the next tile's MMAs wait for the
+// epilogue. Epilogue: warpgroup g owns columns [256g, 256g + 256) of the
+// 128 rows (one row per thread); pass 1 sums v = acc + bias, pass 2 sums
+// (v - mean)^2 (two-pass variance, fp32), the two warpgroups adding their
+// halves through shared memory; pass 3 writes (v - mean) * rstd * ln_w +
+// ln_b through the staged TMA store. The output is rounded once, from the
+// fp32 accumulator (the unfused path rounds the projection to the storage
+// dtype before normalising).
+// ---------------------------------------------------------------------------
+constexpr int kLnBN = 512;
+constexpr int kLnStages = 2;
+
+struct GemmLnSmem {
+    static constexpr uint32_t A_BYTES = BM * BK * 2;
+    static constexpr uint32_t B_BYTES = kLnBN * BK * 2;
+    static constexpr uint32_t RING = kLnStages * (A_BYTES + B_BYTES);
+    static constexpr uint32_t OUT_CHUNK = BM * 32 * 2;
+    static constexpr uint32_t OUT_BYTES = 4 * OUT_CHUNK;
+    static constexpr uint32_t RED_BYTES = 2 * 2 * BM * 4;     // [sum | sq][warpgroup][row]
+    static constexpr uint32_t BAR_BYTES = 8 * (2 * kLnStages + 2 + 1) + 16;
+    static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + RED_BYTES + BAR_BYTES;
+};
+
+// Named barrier over the two epilogue warpgroups (256 threads).
+__device__ __forceinline__ void epi_all_sync() { asm volatile("bar.sync 3, 256;" ::: "memory"); }
+
+template <typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    linear_ln_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_y, const T* __restrict__ bias,
+                     const T* __restrict__ ln_w, const T* __restrict__ ln_b, int n_models, int M, int K, int O,
+                     float eps, GemmRows rw, int* err) {
+    using S = GemmLnSmem;
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kLnStages * S::A_BYTES;
+    uint8_t* sOut = smem + S::RING;
+    float* red = reinterpret_cast<float*>(smem + S::RING + S::OUT_BYTES);   // [2][2][BM]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::OUT_BYTES + S::RED_BYTES);
+    uint64_t* empty = full + kLnStages;
+    uint64_t* tfull = empty + kLnStages;
+    uint64_t* tempty = tfull + 1;
+    uint64_t* done = tempty + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int mt_count = (M + BM - 1) / BM;
+    const int kb_count = (K + BK - 1) / BK;
+    const int tiles = n_models * mt_count;
+    const int o_pad = (O + 15) & ~15;
+    const int n0 = o_pad < 256 ? o_pad : 256;          // first MMA's N
+    const int n1 = o_pad - n0;                         // second MMA's N (0: none)
+    // w boxes: rows [0, n0) and, when o > 256, rows [256, 512) (past o: zeros)
+    const uint32_t b_bytes = (uint32_t)n0 * BK * 2 + (n1 > 0 ? 256u * BK * 2 : 0u);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kLnStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        mbar_init(tempty, 8 * 32);
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_y);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kLnBN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // TMA producer: x tile 128 x 64, w rows [0, 256) and [256, 512) as
+        // two boxes (the second only when o > 256)
+        const uint64_t pol_x = l2_policy_evict_first();
+        const uint64_t pol_w = l2_policy_evict_last();
+        int s = 0;
+        uint32_t ph = 0;
+        int issued = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int mt = tile % mt_count;
+            const int model = tile / mt_count;
+            for (int kb = 0; kb < kb_count; ++kb) {
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], S::A_BYTES + b_bytes);
+                    tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], kb * BK, (mt * BM) % rw.rpb,
+                                (mt * BM) / rw.rpb, model, pol_x);
+                    tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, 0, model, pol_w);
+                    if (n1 > 0)
+                        tma_load_3d(sB + s * S::B_BYTES + 256 * BK * 2, &tm_w, &full[s], kb * BK, 256, model, pol_w);
+                }
+                __syncwarp();
+                ++issued;
+                if (++s == kLnStages) { s = 0; ph ^= 1; }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            const int inflight = issued < kLnStages ? issued : kLnStages;
+            for (int j = 1; j <= inflight; ++j) {
+                const int idx = issued - j;
+                const volatile int never = 0;
+                mbar_wait(&full[idx % kLnStages], (uint32_t)((idx / kLnStages) & 1), &never);
+            }
+        }
+    } else if (warp == 1) {
+        // MMA issuer (one thread)
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int local = 0;
+            const uint32_t idesc0 = idesc_f16(BM, n0, kBf16);
+            const uint32_t idesc1 = idesc_f16(BM, n1 > 0 ? n1 : 16, kBf16);
+            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
+            const uint64_t b_desc0 = sdesc_kmajor_sw128(smem_addr(sB));
+            constexpr uint64_t kB1 = (256 * BK * 2) >> 4;       // rows 256.. of the w tile
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+                if (!mbar_wait(tempty, (uint32_t)(local & 1) ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = a_desc0 + (uint64_t)((s * S::A_BYTES) >> 4);
+                    const uint64_t bd = b_desc0 + (uint64_t)((s * S::B_BYTES) >> 4);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        umma_f16_ss(tmem_base, ad + 2 * k, bd + 2 * k, idesc0, (kb | k) != 0);
+                        if (n1 > 0) umma_f16_ss(tmem_base + 256, ad + 2 * k, bd + kB1 + 2 * k, idesc1, (kb | k) != 0);
+                    }
+                    umma_commit(&empty[s]);
+                    if (++s == kLnStages) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit(tfull);
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+            }
+            umma_commit(done);
+            const volatile int never = 0;
+            mbar_wait(done, 0, &never);
+        }
+        __syncwarp();
+    } else {
+        // Epilogue: warpgroup wg = columns [256 wg, 256 wg + 256), warp
+        // quarter q = TMEM lanes (rows) 32q..32q+31.
+        const int q = warp & 3;
+        const int wg = (warp - 2) >> 2;
+        const int ep_tid = threadIdx.x - 64 - 128 * wg;
+        const int rloc = q * 32 + lane;
+        uint8_t* sOutW = sOut + wg * 2 * S::OUT_CHUNK;
+        float* red_sum = red;               // [2][BM]
+        float* red_sq = red + 2 * BM;       // [2][BM]
+        const float inv_o = 1.0f / (float)O;
+        const int c_begin = wg * 256;
+        const int c_end = (wg + 1) * 256 < O ? (wg + 1) * 256 : O;
+        int local = 0;
+        int oc = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int mt = tile % mt_count;
+            const int model = tile / mt_count;
+            if (!mbar_wait(tfull, (uint32_t)(local & 1), abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const T* brow = bias ? bias + (int64_t)model * O : nullptr;
+            const T* grow = ln_w + (int64_t)model * O;
+            const T* hrow = ln_b + (int64_t)model * O;
+            const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16);
+            // pass 1: row sums of v = acc + bias over this warpgroup's columns
+            float sum = 0.f;
+#pragma unroll 1
+            for (int c = c_begin; c < c_end; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
+                const float my_b = (brow && c + lane < O) ? to_f<T>(brow[c + lane]) : 0.f;
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (c + j < O) sum += __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_b, j);
+            }
+            red_sum[wg * BM + rloc] = sum;
+            epi_all_sync();
+            const float mean = (red_sum[rloc] + red_sum[BM + rloc]) * inv_o;
+            // pass 2: sum of squared deviations
+            float sq = 0.f;
+#pragma unroll 1
+            for (int c = c_begin; c < c_end; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
+                const float my_b = (brow && c + lane < O) ? to_f<T>(brow[c + lane]) : 0.f;
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float dv = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_b, j) - mean;
+                    if (c + j < O) sq += dv * dv;
+                }
+            }
+            red_sq[wg * BM + rloc] = sq;
+            epi_all_sync();
+            const float rstd = rsqrtf((red_sq[rloc] + red_sq[BM + rloc]) * inv_o + eps);
+            // pass 3: normalise, affine, store through the staged TMA store
+#pragma unroll 1
+            for (int c = c_begin; c < c_end; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
+                const bool in = c + lane < O;
+                const float my_b = (brow && in) ? to_f<T>(brow[c + lane]) : 0.f;
+                const float my_g = in ? to_f<T>(grow[c + lane]) : 0.f;
+                const float my_h = in ? to_f<T>(hrow[c + lane]) : 0.f;
+                tmem_ld_wait();
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float u = (__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_b, j) - mean) * rstd;
+                    v[j] = u * __shfl_sync(0xffffffffu, my_g, j) + __shfl_sync(0xffffffffu, my_h, j);
+                }
+                uint8_t* buf = sOutW + (oc & 1) * S::OUT_CHUNK;
+                if (ep_tid == 0) bulk_wait_read1();
+                wg_bar_sync(wg);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int phys = j ^ ((rloc >> 1) & 3);
+                    store16<T>(reinterpret_cast<T*>(buf + rloc * 64 + phys * 16), v + 8 * j);
+                }
+                fence_proxy_async_smem();
+                wg_bar_sync(wg);
+                if (ep_tid == 0) {
+                    tma_store_4d(&tm_y, buf, c, (mt * BM) % rw.rpb, (mt * BM) / rw.rpb, model);
+                    bulk_commit();
+                }
+                ++oc;
+            }
+            tc_fence_before();
+            mbar_arrive(tempty);
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            raise_device_error(err, DEV_ERR_GEMM_TIMEOUT);
+        }
+        if (ep_tid == 0) bulk_wait0();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kLnBN);
+    }
+}
+
+// Launches linear_ln_kernel; WIDEK_ERR_UNSUPPORTED (nothing launched) when
+// the shapes, layouts or alignment do not fit it.
+template <typename T>
+int launch_ln(const T* x, const T* w, const T* bias, const T* lnw, const T* lnb, T* y, int64_t n, int64_t m,
+              int64_t k, int64_t o, float eps, const LinRows& rows, cudaStream_t st) {
+    using S = GemmLnSmem;
+    uint32_t tb, bb;
+    if (o < 16 || o > kLnBN || o % 16 != 0 || k % 8 != 0 || k <= 0 || !aligned16(x) || !aligned16(w) ||
+        !aligned16(y) || !tile_box(rows, tb, bb) || n > 0x7fffffff || m > 0x7fffffff || k > 0x7fffffff ||
+        n * ((m + BM - 1) / BM) > 0x7fffffff)
+        return WIDEK_ERR_UNSUPPORTED;
+    CUtensorMap tx, tw, ty;
+    {
+        const uint64_t dims[4] = {(uint64_t)k, (uint64_t)rows.rpb, (uint64_t)rows.nblk, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)k * 2, (uint64_t)rows.x_bs * 2, (uint64_t)rows.x_ms * 2};
+        const uint32_t box[4] = {BK, tb, bb, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dtype<T>(), 4, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[3] = {(uint64_t)k, (uint64_t)o, (uint64_t)n};
+        const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)o * k * 2};
+        const uint32_t box[3] = {BK, (uint32_t)(o < 256 ? o : 256), 1};
+        int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[4] = {(uint64_t)o, (uint64_t)rows.rpb, (uint64_t)rows.nblk, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)o * 2, (uint64_t)rows.y_bs * 2, (uint64_t)rows.y_ms * 2};
+        const uint32_t box[4] = {32, tb, bb, 1};
+        int rc = encode_tmap_tiled(&ty, tmap_dtype<T>(), 4, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
+    }
+    auto kern = linear_ln_kernel<T>;
+    static bool attr_done[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
+            return set_error(WIDEK_ERR_CUDA, "linear + layernorm: cannot reserve %u bytes of shared memory", S::TOTAL);
+        attr_done[dev] = true;
+    }
+    const int64_t tiles = n * ((m + BM - 1) / BM);
+    const int grid = (int)std::min<int64_t>(tiles, sm_count(dev));
+    const GemmRows rw{(int)rows.rpb, rows.y_ms, rows.y_bs};
+    kern<<<grid, kGemmThreads, S::TOTAL, st>>>(tx, tw, ty, bias, lnw, lnb, (int)n, (int)m, (int)k, (int)o, eps, rw,
+                                               device_error_ptr());
+    return check_launch("widek_linear_ln_fwd (tcgen05, LayerNorm epilogue)");
+}
+
 template <typename T>
 int launch_tc_pair(const T* x, const T* w, const T* bias, T* y, int64_t n, int64_t m, int64_t k, int64_t o, int act,
                    const LinRows& rows, cudaStream_t st) {
@@ -873,6 +1198,31 @@ extern "C" int widek_linear_fwd(const void* x, const void* w, const void* bias, 
                                 int64_t k, int64_t o, int dtype, int act, void* stream) {
     using namespace widek;
     return linear_entry(x, w, bias, y, n, m, k, o, nfirst_rows(m, k, o), dtype, act, (cudaStream_t)stream);
+}
+
+extern "C" int widek_linear_ln_fwd_ex(const void* x, const void* w, const void* bias, const void* ln_w,
+                                      const void* ln_b, void* y, int64_t n, int64_t m, int64_t k, int64_t o,
+                                      int64_t rows_per_block, int in_layout, int out_layout, double eps, int dtype,
+                                      void* stream) {
+    using namespace widek;
+    const bool pin = in_layout == WIDEK_LAYOUT_PACKED, pout = out_layout == WIDEK_LAYOUT_PACKED;
+    if ((!pin && in_layout != WIDEK_LAYOUT_NFIRST) || (!pout && out_layout != WIDEK_LAYOUT_NFIRST))
+        return set_error(WIDEK_ERR_INVALID, "linear + layernorm: layouts must be N-first or packed");
+    if (n < 0 || m < 0 || k < 0 || o < 0) return set_error(WIDEK_ERR_INVALID, "linear + layernorm: negative size");
+    if (n == 0 || m == 0) return WIDEK_OK;
+    if (!x || !w || !ln_w || !ln_b || !y) return set_error(WIDEK_ERR_INVALID, "linear + layernorm: null pointer");
+    if (dtype != WIDEK_BF16 && dtype != WIDEK_F16) return WIDEK_ERR_UNSUPPORTED;
+    if ((pin || pout) && (rows_per_block <= 0 || m % rows_per_block != 0))
+        return set_error(WIDEK_ERR_INVALID, "linear + layernorm: %lld rows are not whole blocks of %lld", (long long)m,
+                         (long long)rows_per_block);
+    const int64_t t = (pin || pout) ? rows_per_block : m, nb = m / t;
+    LinRows r{t, nb, pin ? n * t * k : t * k, pin ? t * k : m * k, pout ? n * t * o : t * o, pout ? t * o : m * o};
+    if (dtype == WIDEK_BF16)
+        return launch_ln<__nv_bfloat16>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (const __nv_bfloat16*)bias,
+                                        (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, (__nv_bfloat16*)y,
+                                        n, m, k, o, (float)eps, r, (cudaStream_t)stream);
+    return launch_ln<__half>((const __half*)x, (const __half*)w, (const __half*)bias, (const __half*)ln_w,
+                             (const __half*)ln_b, (__half*)y, n, m, k, o, (float)eps, r, (cudaStream_t)stream);
 }
 
 extern "C" int widek_linear_fwd_ex(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t m,

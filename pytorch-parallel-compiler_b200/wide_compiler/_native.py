@@ -95,6 +95,7 @@ SIGNATURES = {
     "widek_attention_fwd": [_c_void_p] * 4 + [_i64] * 9 + [_int, _c_void_p, _int, ctypes.POINTER(_i64), _dbl,
                                                           _int, _c_void_p],
     "widek_transpose": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
+    "widek_linear_ln_fwd_ex": [_c_void_p] * 6 + [_i64] * 5 + [_int, _int, _dbl, _int, _c_void_p],
     "widek_linear_bwd_workspace": [_i64] * 4 + [_int],
     "widek_linear_bwd": [_c_void_p] * 6 + [_i64] * 4 + [_int, _c_void_p, _i64, _c_void_p],
     "widek_act_bwd": [_c_void_p] * 3 + [_i64, _int, _int, _c_void_p],

@@ -473,8 +473,69 @@ class TracedWideModel(nn.Module):
                 groups[tail] = g
                 folded.update(g['nodes'][:-1])
         self._plan_linear_chains(groups, folded, cons, op_of)
+        self._plan_attn_ln(groups, folded, cons, op_of)
         by_head = {g['head']: g for g in groups.values()}
         return {'groups': groups, 'folded': folded, 'consumers': cons, 'by_head': by_head}
+
+    def _plan_attn_ln(self, groups, folded, cons, op_of) -> None:
+        """Self-attention (one input, no mask) whose output is read only by a
+        WideLayerNorm of the same width: the LayerNorm runs in the output
+        projection's epilogue (attention out-projection + LN; reference
+        wide_attention.py:233-236 then wide_layernorm.py:62-65). A traced
+        nn.MultiheadAttention returns (output, weights): the output reaches
+        the LayerNorm through getitem 0, and getitems of the weights that
+        nothing reads fold into the group."""
+        order = {nm: i for i, nm in enumerate(self._execution_order)}
+        for name in self._execution_order:
+            if name not in self.stage_info or name in folded or name in groups:
+                continue
+            op = op_of(name)
+            if not isinstance(op, WideAttention):
+                continue
+            args = self._node_args[name]
+            kw = self._node_kwargs.get(name, {})
+            if not args or not isinstance(args[0], str) or any(a != args[0] for a in args):
+                continue
+            if any(k not in ('is_causal', 'need_weights') for k in kw) or \
+                    not isinstance(kw.get('is_causal', False), bool):
+                continue
+            users = cons.get(name, [])
+            path = [name]
+            if len(users) == 1 and users[0] in self.stage_info and isinstance(op_of(users[0]), WideLayerNorm):
+                ln = users[0]
+            else:
+                items: Dict[Any, List[str]] = {}
+                ok = bool(users)
+                for u in users:
+                    uo = op_of(u) if u in self.stage_info else None
+                    ua = self._node_args.get(u, ())
+                    if not (isinstance(uo, FunctionalOp) and uo.fn is operator.getitem and len(ua) == 2
+                            and ua[0] == name and not isinstance(ua[1], str) and u not in folded
+                            and not self._node_kwargs.get(u)):
+                        ok = False
+                        break
+                    items.setdefault(ua[1], []).append(u)
+                if not ok or len(items.get(0, [])) != 1:
+                    continue
+                dead = [u for key, us in items.items() if key != 0 for u in us]
+                if any(cons.get(u) for u in dead):
+                    continue
+                g0 = items[0][0]
+                nxt = cons.get(g0, [])
+                if len(nxt) != 1 or nxt[0] not in self.stage_info:
+                    continue
+                ln = nxt[0]
+                path += [g0] + dead
+            lop = op_of(ln)
+            if ln in folded or not isinstance(lop, WideLayerNorm) or len(self._node_args[ln]) != 1 \
+                    or self._node_kwargs.get(ln) or lop.n != op.n or lop.normalized_shape != op.d_model:
+                continue
+            if self._node_args[ln][0] != path[-1 if len(path) == 1 else 1]:
+                continue
+            nodes = sorted(path, key=order.get) + [ln]
+            groups[ln] = {'kind': 'attn_ln', 'nodes': nodes, 'head': name, 'ln': ln,
+                          'is_causal': bool(kw.get('is_causal', False))}
+            folded.update(nodes[:-1])
 
     def _plan_linear_chains(self, groups, folded, cons, op_of) -> None:
         """Merges runs of WideLinear[+act] segments, each the only consumer
@@ -579,6 +640,9 @@ class TracedWideModel(nn.Module):
             return False
         if g['kind'] in ('linear', 'chain'):
             return True
+        if g['kind'] == 'attn_ln':
+            op = self.stages[g['head'].replace('.', '_')]
+            return not (op.training and op.dropout > 0.0)
         bn_mod = self.stages[g['bn'].replace('.', '_')].op
         if bn_mod.training or bn_mod.running_mean is None or bn_mod.running_var is None:
             return False
@@ -624,6 +688,13 @@ class TracedWideModel(nn.Module):
             return ops.linear(self._std(xv), op.weight, op.bias, act=g['act'])
         if g['kind'] == 'chain':
             return self._run_chain(g, xv)
+        if g['kind'] == 'attn_ln':
+            ln = self.stages[g['ln'].replace('.', '_')]
+            out_ln = (ln.weight, ln.bias, ln.eps)
+            if isinstance(xv, _Laid) and xv.layout == ops.LAYOUT_PACKED and xv.t.dim() == 3:
+                return _Laid(ops.attention_packed(op, xv.t, g['is_causal'], out_ln), ops.LAYOUT_PACKED)
+            x = self._std(xv)
+            return ops.attention(op, x, x, x, None, g['is_causal'], out_ln)
         bn_mod = self.stages[g['bn'].replace('.', '_')].op
         w, b, st, pd, dl = self._conv_params(op)
         rv = values.get(g['residual']) if g['residual'] is not None else None

@@ -167,6 +167,36 @@ def linear_layout(x: Tensor, weight: Tensor, bias: Optional[Tensor], act: int, i
     return y
 
 
+def linear_ln_layout(x: Tensor, weight: Tensor, bias: Optional[Tensor], ln_weight: Tensor, ln_bias: Tensor,
+                     eps: float, in_packed: bool, out_packed: bool) -> Optional[Tensor]:
+    """LayerNorm(x @ weight^T + bias) with the per-model affine (ln_weight /
+    ln_bias flat [N*O]) in one launch (widek_linear_ln_fwd_ex): the attention
+    output projection (wide_attention.py:233-236) followed by WideLayerNorm
+    (wide_layernorm.py:62-65). Layouts as ``linear_layout``; None, launching
+    nothing, when the kernel does not take the shapes (the caller runs the
+    two ops)."""
+    dev = N.require_cuda(x, weight, bias, ln_weight, ln_bias, what="WideLinear + LayerNorm")
+    _same_dtype("WideLinear + LayerNorm", weight, x, bias, ln_weight, ln_bias)
+    n, o, k = weight.shape
+    if x.dim() != (3 if in_packed else 4) or x.shape[-1] != k or (in_packed and x.shape[1] % n != 0) \
+            or (not in_packed and x.shape[0] != n) or ln_weight.numel() != n * o or ln_bias.numel() != n * o:
+        return None
+    b, t = (x.shape[0], x.shape[1] // n) if in_packed else (x.shape[1], x.shape[2])
+    y = torch.empty((b, n * t, o) if out_packed else (n, b, t, o), device=dev, dtype=weight.dtype)
+    xd, wd = _dense(x), _dense(weight)
+    bd = _dense(bias) if bias is not None else None
+    with _guard(dev):
+        rc = N.lib().widek_linear_ln_fwd_ex(xd.data_ptr(), wd.data_ptr(), N.ptr(bd), _dense(ln_weight).data_ptr(),
+                                            _dense(ln_bias).data_ptr(), y.data_ptr(), n, b * t, k, o, t,
+                                            LAYOUT_PACKED if in_packed else LAYOUT_NFIRST,
+                                            LAYOUT_PACKED if out_packed else LAYOUT_NFIRST, float(eps),
+                                            N.dtype_code(weight), N.stream_ptr(dev))
+    if rc == N.WIDEK_ERR_UNSUPPORTED:
+        return None
+    N.check(rc, "widek_linear_ln_fwd_ex")
+    return y
+
+
 _CHAIN_MEMO: dict = {}
 
 
@@ -730,15 +760,20 @@ def fused_qkv(q_weight: Tensor, kv_weight: Tensor, q_bias: Optional[Tensor],
 
 def attention_tensors(query: Tensor, key: Tensor, value: Tensor, q_weight: Tensor, q_bias: Optional[Tensor],
                       kv_weight: Tensor, kv_bias: Optional[Tensor], out_weight: Tensor, out_bias: Optional[Tensor],
-                      n_heads: int, attn_mask: Optional[Tensor], is_causal: bool, self_attn: bool) -> Tensor:
+                      n_heads: int, attn_mask: Optional[Tensor], is_causal: bool, self_attn: bool,
+                      out_ln=None) -> Tensor:
     """WideAttention forward on N-first [N, B, T, D] tensors from its
     parameters: q_weight [N, D, D], kv_weight [N, 2D, D] (k rows then v rows),
     out_weight [N, D, D], biases [N, D] / [N, 2D]; self_attn: key and value
     are the query (one fused [q; kv] projection)."""
+    params = (q_weight, q_bias, kv_weight, kv_bias, out_weight, out_bias)
+    if out_ln is not None and (_compiling() or _AG.needs_grad(query, key, value, *params, out_ln[0], out_ln[1])):
+        # traced or differentiated: the two ops, each on its own operator
+        y = attention_tensors(query, key, value, *params, n_heads, attn_mask, is_causal, self_attn)
+        return layernorm(y, out_ln[0], out_ln[1], q_weight.shape[0], q_weight.shape[1], out_ln[2])
     if _compiling():
         return torch.ops.widek.attention(query, key, value, q_weight, q_bias, kv_weight, kv_bias, out_weight,
                                          out_bias, n_heads, attn_mask, is_causal, self_attn)
-    params = (q_weight, q_bias, kv_weight, kv_bias, out_weight, out_bias)
     if _AG.needs_grad(query, key, value, *params):
         kernel = lambda q, k, v, m, c, h, *p: attention_tensors(q, k, v, *p, h, m, c, self_attn)
         return _AG.run(kernel, _AG.attention_t, query, key, value, attn_mask, is_causal, n_heads, *params)
@@ -775,10 +810,28 @@ def attention_tensors(query: Tensor, key: Tensor, value: Tensor, q_weight: Tenso
         sq = sk = sv = d
     o = torch.empty(n, b, tq, d, device=dev, dtype=query.dtype)
     attention_core(q_t, k_t, v_t, n * b, heads, tq, tk, dh, sq, sk, sv, o, is_causal, attn_mask)
+    return _out_projection(o, out_weight, out_bias, out_ln, False)
+
+
+def _out_projection(o: Tensor, out_weight: Tensor, out_bias: Optional[Tensor], out_ln, out_packed: bool) -> Tensor:
+    """The attention output projection; with ``out_ln`` = (weight, bias, eps)
+    of a WideLayerNorm that follows it, the LayerNorm too (one launch where
+    the fused kernel takes the shapes, else the two ops)."""
+    if out_ln is not None:
+        y = linear_ln_layout(o, out_weight, out_bias, out_ln[0], out_ln[1], out_ln[2], False, out_packed)
+        if y is not None:
+            return y
+        n, d = out_weight.shape[0], out_weight.shape[1]
+        if out_packed:
+            y = linear_layout(o, out_weight, out_bias, ACT_NONE, False, True)
+            return layernorm_packed(y, out_ln[0], out_ln[1], n, d, out_ln[2])
+        return layernorm(linear(o, out_weight, out_bias), out_ln[0], out_ln[1], n, d, out_ln[2])
+    if out_packed:
+        return linear_layout(o, out_weight, out_bias, ACT_NONE, False, True)
     return linear(o, out_weight, out_bias)
 
 
-def attention_packed(mod, x: Tensor, is_causal: bool) -> Tensor:
+def attention_packed(mod, x: Tensor, is_causal: bool, out_ln=None) -> Tensor:
     """WideAttention self-attention on the packed boundary layout: x
     [B, N*T, D] -> [B, N*T, D], the fused QKV projection reading the packed
     rows in place and the output projection writing them packed; equal to
@@ -796,14 +849,17 @@ def attention_packed(mod, x: Tensor, is_causal: bool) -> Tensor:
     o = torch.empty(n, b, t, d, device=dev, dtype=x.dtype)
     attention_core(flat, flat[d:], flat[2 * d:], n * b, heads, t, t, d // heads, 3 * d, 3 * d, 3 * d, o, is_causal,
                    None)
-    return linear_layout(o, mod.out_weight, mod.out_bias, ACT_NONE, False, True)
+    return _out_projection(o, mod.out_weight, mod.out_bias, out_ln, True)
 
 
-def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool) -> Tensor:
-    """WideAttention forward on N-first [N, B, T, D] tensors (see the module)."""
+def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor], is_causal: bool,
+              out_ln=None) -> Tensor:
+    """WideAttention forward on N-first [N, B, T, D] tensors (see the module);
+    ``out_ln`` = (weight, bias, eps) of a WideLayerNorm applied to the result
+    fuses it into the output projection."""
     return attention_tensors(query, key, value, mod.q_weight, mod.q_bias, mod.kv_weight, mod.kv_bias,
                              mod.out_weight, mod.out_bias, mod.n_heads, attn_mask, is_causal,
-                             key is query and value is query)
+                             key is query and value is query, out_ln)
 
 
 # ---------------------------------------------------------------------------
