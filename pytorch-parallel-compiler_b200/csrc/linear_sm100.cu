@@ -743,26 +743,44 @@ int gemm_tc_mn_t(const T* a, const T* b, T* y, int64_t n, int64_t M, int64_t K, 
 // o > 256). Same warp roles as linear_tc_kernel; the accumulator is not
 // double-buffered (the whole TMEM), so the next tile's MMAs wait for the
 // epilogue. Epilogue: warpgroup g owns columns [256g, 256g + 256) of the
-// 128 rows (one row per thread); pass 1 sums v = acc + bias, pass 2 sums
-// (v - mean)^2 (two-pass variance, fp32), the two warpgroups adding their
-// halves through shared memory; pass 3 writes (v - mean) * rstd * ln_w +
-// ln_b through the staged TMA store. The output is rounded once, from the
+// 128 rows (one row per thread); one pass sums d = v - c and d^2 (v = acc
+// + bias, c the row's first value: a shifted one-pass variance in fp32),
+// the two warpgroups adding their halves through shared memory; a second
+// pass writes (v - mean) * rstd * ln_w + ln_b through the staged TMA store. The output is rounded once, from the
 // fp32 accumulator (the unfused path rounds the projection to the storage
 // dtype before normalising).
 // ---------------------------------------------------------------------------
 constexpr int kLnBN = 512;
-constexpr int kLnStages = 2;
+// K per stage 32 (64-byte rows, 64-byte swizzle): a stage is 8 KB of x and
+// 32 KB of w, so four stages fit beside the output staging; with 128-byte
+// rows (K = 64) a stage is 80 KB and only two fit, which left the TMA
+// latency exposed (231 against 142 us at cfg5's size).
+constexpr int kLnBK = 32;
+constexpr int kLnStages = 4;
 
 struct GemmLnSmem {
-    static constexpr uint32_t A_BYTES = BM * BK * 2;
-    static constexpr uint32_t B_BYTES = kLnBN * BK * 2;
+    static constexpr uint32_t A_BYTES = BM * kLnBK * 2;
+    static constexpr uint32_t B_BYTES = kLnBN * kLnBK * 2;
     static constexpr uint32_t RING = kLnStages * (A_BYTES + B_BYTES);
     static constexpr uint32_t OUT_CHUNK = BM * 32 * 2;
     static constexpr uint32_t OUT_BYTES = 4 * OUT_CHUNK;
     static constexpr uint32_t RED_BYTES = 2 * 2 * BM * 4;     // [sum | sq][warpgroup][row]
+    static constexpr uint32_t VEC_BYTES = 3 * kLnBN * 4;      // bias, ln_w, ln_b of the tile's model (fp32)
     static constexpr uint32_t BAR_BYTES = 8 * (2 * kLnStages + 2 + 1) + 16;
-    static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + RED_BYTES + BAR_BYTES;
+    static constexpr uint32_t TOTAL = 1024 + RING + OUT_BYTES + RED_BYTES + VEC_BYTES + BAR_BYTES;
 };
+
+// K-major operand tile with 64-byte rows and 64-byte swizzling: 8-row
+// groups 512 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);   // start address, 16-byte units
+    d |= (uint64_t)1 << 16;                   // leading byte offset (unused when swizzled)
+    d |= (uint64_t)(512 >> 4) << 32;          // stride byte offset: 8 rows * 64 B
+    d |= (uint64_t)1 << 46;                   // descriptor version for sm_100
+    d |= (uint64_t)4 << 61;                   // layout type 4 = 64-byte swizzle
+    return d;
+}
 
 // Named barrier over the two epilogue warpgroups (256 threads).
 __device__ __forceinline__ void epi_all_sync() { asm volatile("bar.sync 3, 256;" ::: "memory"); }
@@ -781,7 +799,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* sB = smem + kLnStages * S::A_BYTES;
     uint8_t* sOut = smem + S::RING;
     float* red = reinterpret_cast<float*>(smem + S::RING + S::OUT_BYTES);   // [2][2][BM]
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::OUT_BYTES + S::RED_BYTES);
+    float* vec = red + 4 * BM;                                              // [3][kLnBN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::OUT_BYTES + S::RED_BYTES + S::VEC_BYTES);
     uint64_t* empty = full + kLnStages;
     uint64_t* tfull = empty + kLnStages;
     uint64_t* tempty = tfull + 1;
@@ -792,13 +811,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int mt_count = (M + BM - 1) / BM;
-    const int kb_count = (K + BK - 1) / BK;
+    const int kb_count = (K + kLnBK - 1) / kLnBK;
     const int tiles = n_models * mt_count;
     const int o_pad = (O + 15) & ~15;
     const int n0 = o_pad < 256 ? o_pad : 256;          // first MMA's N
     const int n1 = o_pad - n0;                         // second MMA's N (0: none)
     // w boxes: rows [0, n0) and, when o > 256, rows [256, 512) (past o: zeros)
-    const uint32_t b_bytes = (uint32_t)n0 * BK * 2 + (n1 > 0 ? 256u * BK * 2 : 0u);
+    const uint32_t b_bytes = (uint32_t)n0 * kLnBK * 2 + (n1 > 0 ? 256u * kLnBK * 2 : 0u);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kLnStages; ++s) {
@@ -841,11 +860,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full[s], S::A_BYTES + b_bytes);
-                    tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], kb * BK, (mt * BM) % rw.rpb,
+                    tma_load_4d(sA + s * S::A_BYTES, &tm_x, &full[s], kb * kLnBK, (mt * BM) % rw.rpb,
                                 (mt * BM) / rw.rpb, model, pol_x);
-                    tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * BK, 0, model, pol_w);
+                    tma_load_3d(sB + s * S::B_BYTES, &tm_w, &full[s], kb * kLnBK, 0, model, pol_w);
                     if (n1 > 0)
-                        tma_load_3d(sB + s * S::B_BYTES + 256 * BK * 2, &tm_w, &full[s], kb * BK, 256, model, pol_w);
+                        tma_load_3d(sB + s * S::B_BYTES + 256 * kLnBK * 2, &tm_w, &full[s], kb * kLnBK, 256, model,
+                                    pol_w);
                 }
                 __syncwarp();
                 ++issued;
@@ -871,9 +891,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int local = 0;
             const uint32_t idesc0 = idesc_f16(BM, n0, kBf16);
             const uint32_t idesc1 = idesc_f16(BM, n1 > 0 ? n1 : 16, kBf16);
-            const uint64_t a_desc0 = sdesc_kmajor_sw128(smem_addr(sA));
-            const uint64_t b_desc0 = sdesc_kmajor_sw128(smem_addr(sB));
-            constexpr uint64_t kB1 = (256 * BK * 2) >> 4;       // rows 256.. of the w tile
+            const uint64_t a_desc0 = sdesc_kmajor_sw64(smem_addr(sA));
+            const uint64_t b_desc0 = sdesc_kmajor_sw64(smem_addr(sB));
+            constexpr uint64_t kB1 = (256 * kLnBK * 2) >> 4;    // rows 256.. of the w tile
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
                 if (!mbar_wait(tempty, (uint32_t)(local & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
@@ -883,7 +903,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint64_t ad = a_desc0 + (uint64_t)((s * S::A_BYTES) >> 4);
                     const uint64_t bd = b_desc0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
+                    for (int k = 0; k < kLnBK / 16; ++k) {   // 16 elements = 32 bytes along the 64-byte row
                         umma_f16_ss(tmem_base, ad + 2 * k, bd + 2 * k, idesc0, (kb | k) != 0);
                         if (n1 > 0) umma_f16_ss(tmem_base + 256, ad + 2 * k, bd + kB1 + 2 * k, idesc1, (kb | k) != 0);
                     }
@@ -923,57 +943,78 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int model = tile / mt_count;
             if (!mbar_wait(tfull, (uint32_t)(local & 1), abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const T* brow = bias ? bias + (int64_t)model * O : nullptr;
-            const T* grow = ln_w + (int64_t)model * O;
-            const T* hrow = ln_b + (int64_t)model * O;
-            const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16);
-            // pass 1: row sums of v = acc + bias over this warpgroup's columns
-            float sum = 0.f;
-#pragma unroll 1
-            for (int c = c_begin; c < c_end; c += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
-                const float my_b = (brow && c + lane < O) ? to_f<T>(brow[c + lane]) : 0.f;
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (c + j < O) sum += __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_b, j);
-            }
-            red_sum[wg * BM + rloc] = sum;
+            // the tile's model's bias, ln_w and ln_b as fp32 in shared memory
+            // (every epilogue thread is done with the previous tile's)
             epi_all_sync();
-            const float mean = (red_sum[rloc] + red_sum[BM + rloc]) * inv_o;
-            // pass 2: sum of squared deviations
-            float sq = 0.f;
+            for (int j = ep_tid + 128 * wg; j < O; j += 256) {
+                vec[j] = bias ? to_f<T>(bias[(int64_t)model * O + j]) : 0.f;
+                vec[kLnBN + j] = to_f<T>(ln_w[(int64_t)model * O + j]);
+                vec[2 * kLnBN + j] = to_f<T>(ln_b[(int64_t)model * O + j]);
+            }
+            epi_all_sync();
+            const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16);
+            // pass 1: sums of d = v - c and d^2 over this warpgroup's
+            // columns, v = acc + bias, shifted by the row's first value c
+            // (the same in both warpgroups) so that the one-pass variance
+            // does not cancel when the mean is large against the spread
+            const float c0 = __uint_as_float(tmem_ld_32x32b_x1(trow));
+            tmem_ld_wait();
+            const float shift = c0 + vec[0];
+            float s1 = 0.f, s2 = 0.f;
 #pragma unroll 1
             for (int c = c_begin; c < c_end; c += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
-                const float my_b = (brow && c + lane < O) ? to_f<T>(brow[c + lane]) : 0.f;
                 tmem_ld_wait();
+                if (c + 32 <= O) {
+                    const float4* vb = reinterpret_cast<const float4*>(vec + c);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float dv = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_b, j) - mean;
-                    if (c + j < O) sq += dv * dv;
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 bv = vb[j4];               // one 16-byte broadcast read
+                        const float bj[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float dv = __uint_as_float(r[4 * j4 + e]) + bj[e] - shift;
+                            s1 += dv;
+                            s2 += dv * dv;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float dv = c + j < O ? __uint_as_float(r[j]) + vec[c + j] - shift : 0.f;
+                        s1 += dv;
+                        s2 += dv * dv;
+                    }
                 }
             }
-            red_sq[wg * BM + rloc] = sq;
+            red_sum[wg * BM + rloc] = s1;
+            red_sq[wg * BM + rloc] = s2;
             epi_all_sync();
-            const float rstd = rsqrtf((red_sq[rloc] + red_sq[BM + rloc]) * inv_o + eps);
-            // pass 3: normalise, affine, store through the staged TMA store
+            const float m1 = (red_sum[rloc] + red_sum[BM + rloc]) * inv_o;      // mean of d
+            const float var = fmaxf((red_sq[rloc] + red_sq[BM + rloc]) * inv_o - m1 * m1, 0.f);
+            const float mean = shift + m1;
+            const float rstd = rsqrtf(var + eps);
+            // pass 2: normalise, affine, store through the staged TMA store
 #pragma unroll 1
             for (int c = c_begin; c < c_end; c += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
-                const bool in = c + lane < O;
-                const float my_b = (brow && in) ? to_f<T>(brow[c + lane]) : 0.f;
-                const float my_g = in ? to_f<T>(grow[c + lane]) : 0.f;
-                const float my_h = in ? to_f<T>(hrow[c + lane]) : 0.f;
                 tmem_ld_wait();
                 float v[32];
+                const float4* vb = reinterpret_cast<const float4*>(vec + c);
+                const float4* vg = reinterpret_cast<const float4*>(vec + kLnBN + c);
+                const float4* vh = reinterpret_cast<const float4*>(vec + 2 * kLnBN + c);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float u = (__uint_as_float(r[j]) + __shfl_sync(0xffffffffu, my_b, j) - mean) * rstd;
-                    v[j] = u * __shfl_sync(0xffffffffu, my_g, j) + __shfl_sync(0xffffffffu, my_h, j);
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 bv = vb[j4], gv = vg[j4], hv = vh[j4];
+                    const float bj[4] = {bv.x, bv.y, bv.z, bv.w}, gj[4] = {gv.x, gv.y, gv.z, gv.w},
+                                hj[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float u = (__uint_as_float(r[4 * j4 + e]) + bj[e] - mean) * rstd;
+                        v[4 * j4 + e] = u * gj[e] + hj[e];
+                    }
                 }
                 uint8_t* buf = sOutW + (oc & 1) * S::OUT_CHUNK;
                 if (ep_tid == 0) bulk_wait_read1();
@@ -1024,15 +1065,15 @@ int launch_ln(const T* x, const T* w, const T* bias, const T* lnw, const T* lnb,
     {
         const uint64_t dims[4] = {(uint64_t)k, (uint64_t)rows.rpb, (uint64_t)rows.nblk, (uint64_t)n};
         const uint64_t strides[3] = {(uint64_t)k * 2, (uint64_t)rows.x_bs * 2, (uint64_t)rows.x_ms * 2};
-        const uint32_t box[4] = {BK, tb, bb, 1};
-        int rc = encode_tmap_tiled(&tx, tmap_dtype<T>(), 4, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        const uint32_t box[4] = {kLnBK, tb, bb, 1};
+        int rc = encode_tmap_tiled(&tx, tmap_dtype<T>(), 4, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
         if (rc) return rc;
     }
     {
         const uint64_t dims[3] = {(uint64_t)k, (uint64_t)o, (uint64_t)n};
         const uint64_t strides[2] = {(uint64_t)k * 2, (uint64_t)o * k * 2};
-        const uint32_t box[3] = {BK, (uint32_t)(o < 256 ? o : 256), 1};
-        int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        const uint32_t box[3] = {kLnBK, (uint32_t)(o < 256 ? o : 256), 1};
+        int rc = encode_tmap_tiled(&tw, tmap_dtype<T>(), 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
         if (rc) return rc;
     }
     {
