@@ -518,7 +518,25 @@ class RnnCfg4(Workload):
             f"one full cfg4 {self.kind} forward per rep (all {n} models), fp32, torch CPU"
 
 
-class AttnCfg5(Workload):
+class _AttnLN(nn.Module):
+    """One cfg5 model: causal self-attention (nn.MultiheadAttention, batch
+    first) followed by LayerNorm."""
+
+    def __init__(self, d, heads):
+        super().__init__()
+        self.attn = nn.MultiheadAttention(d, heads, batch_first=True)
+        self.ln = nn.LayerNorm(d)
+
+    def forward(self, x):
+        a, _ = self.attn(x, x, x, need_weights=False, is_causal=True)
+        return self.ln(a)
+
+
+class AttnCfg5(_Traced):
+    """cfg5 through wide_compiler.compile: a TracedWideModel of N (attention
+    -> LayerNorm) models on the packed input [B, N*T, D]. The QKV projection
+    reads the packed rows in place, the output projection runs with the
+    LayerNorm in its epilogue and writes the packed output."""
     name = "cfg5"
     bound = "tensor"
     peak_key = "tensor_sustained"
@@ -529,48 +547,45 @@ class AttnCfg5(Workload):
     def work(self, n):
         core = 2 * 2 * n * self.b * self.heads * (self.t * (self.t + 1) // 2) * (self.d // self.heads)
         proj = 2 * n * self.b * self.t * self.d * self.d * 4
-        return {"widek_attention_fwd": core, "widek_linear_fwd": proj}
+        return {"widek_attention_fwd": core, "widek_linear_fwd_ex": proj * 3 // 4,
+                "widek_linear_ln_fwd_ex": proj // 4}
 
     def flops(self, n):
         return sum(self.work(n).values())
 
     def config(self):
-        return {"workload": f"cfg5 WideAttention N={self.n_total}, d_model={self.d}, {self.heads} heads, causal "
-                            f"self-attention, B={self.b}, T={self.t}, bf16, weights ~ N(0, 0.02), followed by "
-                            f"WideLayerNorm({self.d})",
+        return {"workload": f"cfg5 TracedWideModel of N={self.n_total} (MultiheadAttention d_model={self.d}, "
+                            f"{self.heads} heads, causal self-attention -> LayerNorm({self.d})), B={self.b}, "
+                            f"T={self.t}, bf16, weights ~ N(0, 0.02), biases 0, packed input "
+                            f"[{self.b}, {self.n_total * self.t}, {self.d}]",
                 "models": self.n_total, "rows_per_model": self.b,
                 "l2": "inputs larger than L2 (134 MB activation, ~0.5 GB of intermediates per step), no flush"}
 
     def setup(self, dev, lo, hi, seed):
-        import wide_compiler as wc
-        n = hi - lo
-        a = wc.WideAttention(n, self.d, self.heads)
-        with torch.no_grad():
-            for k, j in enumerate(range(lo, hi)):
-                g = _gen(seed + j)
-                for p in (a.q_weight, a.kv_weight, a.out_weight):
-                    p[k].copy_(torch.randn(p[k].shape, generator=g) * 0.02)
-            a.q_bias.zero_()
-            a.kv_bias.zero_()
-            a.out_bias.zero_()
-        self.attn = a.to(dev, torch.bfloat16).eval()
-        self.ln = wc.WideLayerNorm(n, self.d).to(dev, torch.bfloat16)
-        self.module = self.attn
-        self.x = torch.stack([torch.randn(self.b, self.t, self.d, generator=_gen(seed + 100_000 + j))
-                              for j in range(lo, hi)]).to(dev, torch.bfloat16)
-
-    def step(self, x):
-        return self.ln(self.attn(x, is_causal=True))
+        models = []
+        for j in range(self.n_total):
+            m = _AttnLN(self.d, self.heads)
+            g = _gen(seed + j)
+            with torch.no_grad():
+                m.attn.in_proj_weight.copy_(torch.randn(m.attn.in_proj_weight.shape, generator=g) * 0.02)
+                m.attn.out_proj.weight.copy_(torch.randn(m.attn.out_proj.weight.shape, generator=g) * 0.02)
+                m.attn.in_proj_bias.zero_()
+                m.attn.out_proj.bias.zero_()
+            models.append(m.eval())
+        xs = [torch.randn(self.b, self.t, self.d, generator=_gen(seed + 100_000 + j)) for j in range(lo, hi)]
+        self.build(dev, torch.bfloat16, models, torch.randn(2, self.t, self.d), xs)
 
     def torch_reference_step(self):
         """The reference's GPU op sequence (wide_attention.py:178-238 einsum
         projections, head split, SDPA causal, merge, out projection;
         wide_layernorm.py:41-67) with the same parameters, through torch."""
-        a, ln, x = self.attn, self.ln, self.x
+        st = self.module.local.stages
+        a, ln = st['attn'], st['ln']
         n, d, hd = a.n, self.d, self.heads
+        b, t = self.b, self.t
+        x = self.x.view(b, n, t, d).transpose(0, 1)
 
         def run():
-            _, b, t, _ = x.shape
             q = torch.einsum('nbtd,nod->nbto', x, a.q_weight) + a.q_bias.view(n, 1, 1, d)
             k = torch.einsum('nbtd,nod->nbto', x, a.kv_weight[:, :d]) + a.kv_bias[:, :d].view(n, 1, 1, d)
             v = torch.einsum('nbtd,nod->nbto', x, a.kv_weight[:, d:]) + a.kv_bias[:, d:].view(n, 1, 1, d)

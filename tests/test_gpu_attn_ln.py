@@ -132,3 +132,33 @@ def test_traced_attention_layernorm_group(n, b, t, d, heads):
     ref_unfused = wide(packed)
     assert_lowp_close(got['y'], ref_unfused.float())
     no_device_error()
+
+
+def test_cfg5_bench_graph_sampled():
+    """The cfg5 benchmark graph as bench.py builds it (TracedWideModel of
+    attention -> LayerNorm models, T = 1024, d = 512, 8 heads, causal), at 2
+    models: the fused group runs, and sampled (model, batch) outputs match
+    the oracle's attention + LayerNorm."""
+    import bench
+    wl = bench.make_workload('cfg5', 2)
+    wl._world_rank = (1, 0)
+    wl._gather = False
+    wl.setup(DEV, 0, 2, seed=1234)
+    wl.step(wl.x)
+    names = kernels_run(lambda: wl.step(wl.x))
+    assert any('linear_ln_kernel' in s for s in names), names
+    y = wl.step(wl.x)                                    # [B, 2*T, D] packed
+    st = wl.module.local.stages
+    a, ln = st['attn'], st['ln']
+    b, t, d = wl.b, wl.t, wl.d
+    xn = wl.x.view(b, 2, t, d).transpose(0, 1)           # [2, B, T, D]
+    yn = y.view(b, 2, t, d).transpose(0, 1)
+    for i, bi in [(0, 0), (1, 5)]:
+        xi = xn[i, bi][None, None].cpu()
+        sl = slice(i, i + 1)
+        ref = O.attention(xi, xi, xi, a.q_weight[sl].cpu(), a.kv_weight[sl].cpu(), a.q_bias[sl].cpu(),
+                          a.kv_bias[sl].cpu(), a.out_weight[sl].cpu(), a.out_bias[sl].cpu(), wl.heads,
+                          is_causal=True)
+        ref = O.layernorm(ref, ln.weight[i * d:(i + 1) * d].cpu(), ln.bias[i * d:(i + 1) * d].cpu(), 1, d, ln.eps)
+        assert_lowp_close(yn[i, bi], ref[0, 0])
+    no_device_error()
