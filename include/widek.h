@@ -605,6 +605,35 @@ WIDEK_API int widek_layernorm_bwd(const void* x, const void* w, const void* dy, 
                                   double eps, int dtype, void* workspace, int64_t workspace_bytes,
                                   void* stream);
 
+/* Gradients of widek_batchnorm_fwd / widek_batchnorm_train_fwd on
+ * x, dy, dx: [n, batch, c, l] dense; weight (nullable: no affine),
+ * running_mean / running_var flat [n*c]. batch_stats = 1: the statistics
+ * of the batch (recomputed from x; biased variance), dx = rstd * (g -
+ * mean(g) - x_hat * mean(g * x_hat)) with g = dy * gamma; batch_stats = 0
+ * (eval mode): the running statistics, dx = rstd * g. dw / db ([n*c],
+ * nullable) = sum of dy * x_hat / of dy per (model, channel). Replaces the
+ * autograd of wide_compiler/core/primitives/wide_batchnorm_2d.py:53-72 and
+ * wide_batchnorm_1d.py:53-73. */
+WIDEK_API int widek_batchnorm_bwd(const void* x, const void* dy, const void* weight,
+                                  const void* running_mean, const void* running_var, void* dx,
+                                  void* dw, void* db, int64_t n, int64_t batch, int64_t c,
+                                  int64_t l, int batch_stats, double eps, int dtype, void* stream);
+
+/* Workspace bytes widek_groupnorm_bwd needs (-1 for bad arguments). */
+WIDEK_API int64_t widek_groupnorm_bwd_workspace(int64_t n, int64_t batch, int64_t c);
+
+/* Gradients of widek_groupnorm_fwd (statistics per (model, sample, group),
+ * recomputed from x; per-channel affine weight [n*c], nullable): dx as for
+ * batch statistics above over each group's elements; dw / db ([n*c],
+ * nullable) summed over the batch in a fixed order. InstanceNorm is the
+ * case groups = c. Replaces the autograd of
+ * wide_compiler/core/primitives/wide_groupnorm.py:90-117 and
+ * wide_instancenorm.py:89-108. */
+WIDEK_API int widek_groupnorm_bwd(const void* x, const void* dy, const void* weight, void* dx,
+                                  void* dw, void* db, int64_t n, int64_t batch, int64_t c,
+                                  int64_t l, int64_t groups, double eps, int dtype,
+                                  void* workspace, int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -131,6 +131,57 @@ def layernorm_grads(x: Tensor, weight_flat: Tensor, dy: Tensor, n: int, d: int, 
     return dx, dw, db
 
 
+def _norm_grads(x: Tensor, g: Tensor, gamma: Tensor, dims, mean: Tensor, rstd: Tensor, batch_stats: bool):
+    """dx, and the per-element dy * x_hat, for a normalisation whose
+    statistics reduce over `dims`: with batch statistics
+    dx = rstd * (g' - mean(g') - x_hat * mean(g' * x_hat)), g' = dy * gamma;
+    with fixed (running) statistics dx = rstd * g'."""
+    xh = (x - mean) * rstd
+    gg = g * gamma
+    if batch_stats:
+        dx = rstd * (gg - gg.mean(dim=dims, keepdim=True) - xh * (gg * xh).mean(dim=dims, keepdim=True))
+    else:
+        dx = rstd * gg
+    return dx, g * xh
+
+
+def batchnorm_grads(x: Tensor, n: int, c: int, weight: Optional[Tensor], running_mean: Optional[Tensor],
+                    running_var: Optional[Tensor], dy: Tensor, batch_stats: bool, eps: float):
+    """(dx, dweight_flat or None, dbias_flat) of batchnorm on [N, B, C, *S]
+    (batch statistics: biased variance over B and S per (model, channel))."""
+    x, g = _f(x), _f(dy)
+    shape = (n, 1, c) + (1,) * (x.dim() - 3)
+    dims = tuple([1] + list(range(3, x.dim())))
+    if batch_stats:
+        mean = x.mean(dim=dims, keepdim=True)
+        var = ((x - mean) ** 2).mean(dim=dims, keepdim=True)
+    else:
+        mean, var = _f(running_mean).view(shape), _f(running_var).view(shape)
+    rstd = 1.0 / torch.sqrt(var + eps)
+    gamma = _f(weight).view(shape) if weight is not None else torch.ones(shape, dtype=D)
+    dx, gxh = _norm_grads(x, g, gamma, dims, mean, rstd, batch_stats)
+    dw = gxh.sum(dim=dims).reshape(n * c) if weight is not None else None
+    return dx, dw, g.sum(dim=dims).reshape(n * c)
+
+
+def groupnorm_grads(x: Tensor, n: int, groups: int, weight: Optional[Tensor], dy: Tensor, eps: float):
+    """(dx, dweight_flat or None, dbias_flat) of groupnorm on [N, B, C, *S]
+    (statistics per (model, sample, group))."""
+    x, g = _f(x), _f(dy)
+    b, c = x.shape[1], x.shape[2]
+    xg = x.reshape(n, b, groups, -1)
+    mean = xg.mean(dim=-1, keepdim=True)
+    var = ((xg - mean) ** 2).mean(dim=-1, keepdim=True)
+    rstd = 1.0 / torch.sqrt(var + eps)
+    cshape = (n, 1, c) + (1,) * (x.dim() - 3)
+    gamma = (_f(weight).view(cshape) if weight is not None else torch.ones(cshape, dtype=D)).expand(x.shape)
+    dxg, gxh = _norm_grads(xg, g.reshape(n, b, groups, -1), gamma.reshape(n, b, groups, -1), (-1,), mean, rstd,
+                           True)
+    rows = tuple([1] + list(range(3, x.dim())))
+    dw = gxh.reshape(x.shape).sum(dim=rows).reshape(n * c) if weight is not None else None
+    return dxg.reshape(x.shape), dw, g.sum(dim=rows).reshape(n * c)
+
+
 # ---------------------------------------------------------------------------
 # BatchNorm1d/2d — wide_batchnorm_2d.py:53-72, wide_batchnorm_1d.py:53-73
 # (inner nn.BatchNorm over N*C channels == per-(model, channel) statistics)

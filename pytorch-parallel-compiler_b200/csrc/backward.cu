@@ -456,6 +456,208 @@ struct LnBwdLaunch {
 }  // namespace
 }  // namespace widek
 
+namespace widek {
+namespace {
+
+// ---------------------------------------------------------------------------
+// BatchNorm / GroupNorm backward (InstanceNorm is GroupNorm with one channel
+// per group). x, dy, dx: [n, B, C, L] dense (L = spatial size). A segment is
+// the set of elements one statistic covers: BatchNorm (i, c): B chunks of L
+// elements, C*L apart; GroupNorm (i, b, g): cg = C/G consecutive chunks of L
+// elements. Chunk k of a segment has channel ch0 + k * chan_step.
+//   x_hat = (x - mean) * rstd, g = dy * gamma_ch, M = elements of the segment
+//   batch statistics: dx = rstd * (g - mean(g) - x_hat * mean(g * x_hat))
+//   running statistics (BatchNorm in eval mode): dx = rstd * g
+//   dgamma_ch = sum dy * x_hat, dbeta_ch = sum dy over the channel's elements
+// One CTA per segment: pass 1 accumulates sum x, sum x^2 (shifted by the
+// segment's first element), sum g and sum g * x; pass 2 (the segment again,
+// mostly from L2) writes dx and the parameter sums: per segment for
+// BatchNorm (the channel is the segment), per (segment, channel) partials
+// for GroupNorm, added over the batch by a second kernel in a fixed order.
+// ---------------------------------------------------------------------------
+constexpr int kNbThreads = 256;
+
+struct NormBwdArgs {
+    const void *x, *dy, *w, *rmean, *rvar;
+    void *dx, *dw, *db;
+    float* part;                    // GroupNorm: [n * B][C][2] (dgamma, dbeta) partials
+    int64_t n, batch, c, l;
+    int groups;                     // 0: BatchNorm
+    int batch_stats;                // BatchNorm: 1 = batch statistics, 0 = running statistics
+    float eps;
+};
+
+__device__ __forceinline__ float nb_block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();                 // red is free (a previous sum has been read)
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < kNbThreads / 32; ++q) t += red[q];
+    return t;
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kNbThreads) norm_bwd_kernel(NormBwdArgs a) {
+    __shared__ float red[kNbThreads / 32];
+    constexpr int V = VEC ? 16 / (int)sizeof(T) : 1;
+    const T* x = static_cast<const T*>(a.x);
+    const T* dy = static_cast<const T*>(a.dy);
+    const T* w = static_cast<const T*>(a.w);
+    T* dx = static_cast<T*>(a.dx);
+    const int64_t seg = blockIdx.x;
+    const bool bn = a.groups == 0;
+    int64_t base, kstride, ch0, chan_step, chunks;
+    if (bn) {
+        const int64_t i = seg / a.c, c = seg % a.c;
+        base = (i * a.batch * a.c + c) * a.l;
+        kstride = a.c * a.l;
+        ch0 = i * a.c + c;
+        chan_step = 0;
+        chunks = a.batch;
+    } else {
+        const int64_t cg = a.c / a.groups;
+        const int64_t g = seg % a.groups, ib = seg / a.groups, i = ib / a.batch;
+        base = (ib * a.c + g * cg) * a.l;
+        kstride = a.l;
+        ch0 = i * a.c + g * cg;
+        chan_step = 1;
+        chunks = cg;
+    }
+    const int64_t L = a.l, M = chunks * L;
+    const int64_t nv = L / V;               // vectors per chunk
+    const float shift = to_f<T>(x[base]);
+    auto gamma = [&](int64_t ch) { return w ? to_f<T>(w[ch]) : 1.f; };
+    // pass 1
+    float sx = 0.f, sxx = 0.f, sg = 0.f, sgx = 0.f;
+    for (int64_t k = 0; k < chunks; ++k) {
+        const int64_t off = base + k * kstride;
+        const float gm = gamma(ch0 + k * chan_step);
+        for (int64_t q = threadIdx.x; q < nv; q += kNbThreads) {
+            float xv[V], gv[V];
+            if constexpr (VEC) {
+                load16<T>(x + off + q * V, xv);
+                load16<T>(dy + off + q * V, gv);
+            } else {
+                xv[0] = to_f<T>(x[off + q]);
+                gv[0] = to_f<T>(dy[off + q]);
+            }
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                const float d = xv[e] - shift, g = gv[e] * gm;
+                sx += d;
+                sxx += d * d;
+                sg += g;
+                sgx += g * d;
+            }
+        }
+    }
+    const float inv_m = 1.0f / (float)M;
+    const float m_d = nb_block_sum(sx, red) * inv_m;              // mean of x - shift
+    const float var_b = fmaxf(nb_block_sum(sxx, red) * inv_m - m_d * m_d, 0.f);
+    const float mg = nb_block_sum(sg, red) * inv_m;                // mean of g
+    const float mgd = nb_block_sum(sgx, red) * inv_m;              // mean of g * (x - shift)
+    float mean, rstd;
+    if (bn && !a.batch_stats) {
+        mean = to_f<T>(static_cast<const T*>(a.rmean)[ch0]);
+        rstd = rsqrtf(to_f<T>(static_cast<const T*>(a.rvar)[ch0]) + a.eps);
+    } else {
+        mean = shift + m_d;
+        rstd = rsqrtf(var_b + a.eps);
+    }
+    // mean(g * x_hat) = rstd * (mean(g * (x - shift)) - (mean - shift) * mean(g))
+    const float mgxh = rstd * (mgd - (mean - shift) * mg);
+    const bool full = !(bn && !a.batch_stats);
+    // pass 2
+    float pdw = 0.f, pdb = 0.f;
+    for (int64_t k = 0; k < chunks; ++k) {
+        const int64_t off = base + k * kstride;
+        const int64_t ch = ch0 + k * chan_step;
+        const float gm = gamma(ch);
+        for (int64_t q = threadIdx.x; q < nv; q += kNbThreads) {
+            float xv[V], gv[V], o[V];
+            if constexpr (VEC) {
+                load16<T>(x + off + q * V, xv);
+                load16<T>(dy + off + q * V, gv);
+            } else {
+                xv[0] = to_f<T>(x[off + q]);
+                gv[0] = to_f<T>(dy[off + q]);
+            }
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                const float xh = (xv[e] - mean) * rstd;
+                pdw += gv[e] * xh;
+                pdb += gv[e];
+                const float g = gv[e] * gm;
+                o[e] = full ? rstd * (g - mg - xh * mgxh) : rstd * g;
+            }
+            if constexpr (VEC) store16<T>(dx + off + q * V, o);
+            else dx[off + q] = from_f<T>(o[0]);
+        }
+        if (!bn) {
+            // GroupNorm: this chunk is one channel; its partial sums
+            const float tw = nb_block_sum(pdw, red), tb = nb_block_sum(pdb, red);
+            if (threadIdx.x == 0) {
+                const int64_t ib = seg / a.groups;
+                const int64_t cl = ch - (ib / a.batch) * a.c;
+                a.part[((ib * a.c) + cl) * 2] = tw;
+                a.part[((ib * a.c) + cl) * 2 + 1] = tb;
+            }
+            pdw = pdb = 0.f;
+        }
+    }
+    if (bn) {
+        const float tw = nb_block_sum(pdw, red), tb = nb_block_sum(pdb, red);
+        if (threadIdx.x == 0) {
+            if (a.dw) static_cast<T*>(a.dw)[ch0] = from_f<T>(tw);
+            if (a.db) static_cast<T*>(a.db)[ch0] = from_f<T>(tb);
+        }
+    }
+}
+
+// GroupNorm parameter gradients: dgamma[i*C + c] = sum over b of part[i][b][c].
+template <typename T>
+__global__ void __launch_bounds__(kSumThreads) gn_param_reduce_kernel(const float* __restrict__ part, T* dw, T* db,
+                                                                       int64_t n, int64_t batch, int64_t c) {
+    const int64_t idx = (int64_t)blockIdx.x * kSumThreads + threadIdx.x;
+    if (idx >= n * c) return;
+    const int64_t i = idx / c, cl = idx % c;
+    float tw = 0.f, tb = 0.f;
+    for (int64_t b = 0; b < batch; ++b) {
+        const float* p = part + (((i * batch + b) * c) + cl) * 2;
+        tw += p[0];
+        tb += p[1];
+    }
+    if (dw) dw[idx] = from_f<T>(tw);
+    if (db) db[idx] = from_f<T>(tb);
+}
+
+struct NormBwdLaunch {
+    NormBwdArgs a;
+    cudaStream_t st;
+    template <typename T>
+    int run() {
+        constexpr int VV = 16 / sizeof(T);
+        const bool vec = a.l % VV == 0 && aligned16(a.x) && aligned16(a.dy) && aligned16(a.dx);
+        const int64_t segs = a.groups == 0 ? a.n * a.c : a.n * a.batch * a.groups;
+        if (segs > 0x7fffffff) return set_error(WIDEK_ERR_UNSUPPORTED, "norm backward: too many segments");
+        if (vec)
+            norm_bwd_kernel<T, true><<<(unsigned)segs, kNbThreads, 0, st>>>(a);
+        else
+            norm_bwd_kernel<T, false><<<(unsigned)segs, kNbThreads, 0, st>>>(a);
+        int rc = check_launch(a.groups == 0 ? "batchnorm_bwd" : "groupnorm_bwd");
+        if (rc != WIDEK_OK || a.groups == 0 || (!a.dw && !a.db)) return rc;
+        gn_param_reduce_kernel<T><<<(unsigned)((a.n * a.c + kSumThreads - 1) / kSumThreads), kSumThreads, 0, st>>>(
+            a.part, static_cast<T*>(a.dw), static_cast<T*>(a.db), a.n, a.batch, a.c);
+        return check_launch("groupnorm_bwd (parameter sums)");
+    }
+};
+
+}  // namespace
+}  // namespace widek
+
 // ---------------------------------------------------------------------------
 // C-ABI
 // ---------------------------------------------------------------------------
@@ -641,6 +843,56 @@ int widek_layernorm_bwd(const void* x, const void* w, const void* dy, void* dx, 
     }
     LnBwdLaunch L{x, w, dy, dx, dw, db, static_cast<float*>(workspace), n, outer, (int)d, (float)eps, ln_blocks(n, outer),
                   (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+int widek_batchnorm_bwd(const void* x, const void* dy, const void* weight, const void* running_mean,
+                        const void* running_var, void* dx, void* dw, void* db, int64_t n, int64_t batch, int64_t c,
+                        int64_t l, int batch_stats, double eps, int dtype, void* stream) {
+    using namespace widek;
+    if (n < 0 || batch < 0 || c < 0 || l < 0) return set_error(WIDEK_ERR_INVALID, "batchnorm_bwd: negative size");
+    if (n * c == 0) return WIDEK_OK;
+    if (batch * l == 0) return set_error(WIDEK_ERR_INVALID, "batchnorm_bwd: a channel has no elements");
+    if (!x || !dy || !dx) return set_error(WIDEK_ERR_INVALID, "batchnorm_bwd: null pointer");
+    if (!batch_stats && (!running_mean || !running_var))
+        return set_error(WIDEK_ERR_INVALID, "batchnorm_bwd: running statistics needed without batch statistics");
+    NormBwdLaunch L{NormBwdArgs{x, dy, weight, running_mean, running_var, dx, dw, db, nullptr, n, batch, c, l, 0,
+                                batch_stats ? 1 : 0, (float)eps},
+                    (cudaStream_t)stream};
+    return dispatch_dtype(dtype, L);
+}
+
+int64_t widek_groupnorm_bwd_workspace(int64_t n, int64_t batch, int64_t c) {
+    if (n < 0 || batch < 0 || c < 0) return -1;
+    return (int64_t)widek::align256((size_t)n * batch * c * 2 * sizeof(float));
+}
+
+int widek_groupnorm_bwd(const void* x, const void* dy, const void* weight, void* dx, void* dw, void* db, int64_t n,
+                        int64_t batch, int64_t c, int64_t l, int64_t groups, double eps, int dtype, void* workspace,
+                        int64_t workspace_bytes, void* stream) {
+    using namespace widek;
+    if (n < 0 || batch < 0 || c < 0 || l < 0 || groups <= 0)
+        return set_error(WIDEK_ERR_INVALID, "groupnorm_bwd: bad sizes");
+    if (c % groups != 0) return set_error(WIDEK_ERR_INVALID, "groupnorm_bwd: %lld channels in %lld groups",
+                                          (long long)c, (long long)groups);
+    const int64_t need = widek_groupnorm_bwd_workspace(n, batch, c);
+    if (workspace_bytes < need || (!workspace && need > 0))
+        return set_error(WIDEK_ERR_INVALID, "groupnorm_bwd: workspace of %lld bytes, %lld needed",
+                         (long long)workspace_bytes, (long long)need);
+    if (n * batch * c == 0) {
+        const size_t bytes = (size_t)n * c * dtype_size(dtype);
+        cudaStream_t st = (cudaStream_t)stream;
+        if (bytes && ((dw && cudaMemsetAsync(dw, 0, bytes, st) != cudaSuccess) ||
+                      (db && cudaMemsetAsync(db, 0, bytes, st) != cudaSuccess)))
+            return set_error(WIDEK_ERR_CUDA, "groupnorm_bwd: memset failed");
+        return WIDEK_OK;
+    }
+    if (l == 0) return set_error(WIDEK_ERR_INVALID, "groupnorm_bwd: empty spatial extent");
+    if (!x || !dy || !dx) return set_error(WIDEK_ERR_INVALID, "groupnorm_bwd: null pointer");
+    if (groups > 0x7fffffff) return set_error(WIDEK_ERR_UNSUPPORTED, "groupnorm_bwd: too many groups");
+    NormBwdLaunch L{NormBwdArgs{x, dy, weight, nullptr, nullptr, dx, dw, db, static_cast<float*>(workspace), n, batch,
+                                c, l, (int)groups, 1, (float)eps},
+                    (cudaStream_t)stream};
     return dispatch_dtype(dtype, L);
 }
 

@@ -414,3 +414,76 @@ def layernorm_grad(x: Tensor, weight: Tensor, bias: Tensor, n: int, d: int, eps:
     if not ok:
         return run(ops.layernorm, layernorm_t, x, weight, bias, n, d, eps)
     return LayerNormFn.apply(x, weight, bias, n, d, eps)
+
+
+class BatchNormFn(torch.autograd.Function):
+    """BatchNorm on [N, B, C, *S] (batch or running statistics); backward:
+    widek_batchnorm_bwd. Running statistics are updated once, in forward."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, n, c, running_mean, running_var, use_batch_stats, update_running, momentum,
+                eps):
+        from . import ops
+        with torch.no_grad():
+            y = ops.batchnorm(x, n, c, weight, bias, running_mean, running_var, use_batch_stats, update_running,
+                              momentum, eps)
+        ctx.n, ctx.c, ctx.eps, ctx.batch_stats = n, c, eps, use_batch_stats
+        ctx.has_w, ctx.has_b = weight is not None, bias is not None
+        stats = (running_mean.clone(), running_var.clone()) if not use_batch_stats else (None, None)
+        ctx.save_for_backward(x, weight, *stats)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        x, weight, rm, rv = ctx.saved_tensors
+        dx, dw, db = ops.batchnorm_bwd(x, dy.to(x.dtype).contiguous(), ctx.n, ctx.c, weight, rm, rv, ctx.batch_stats,
+                                       ctx.eps, ctx.needs_input_grad[1], ctx.needs_input_grad[2] and ctx.has_b)
+        return (dx.view(x.shape), None if dw is None else dw.view(weight.shape), db, None, None, None, None, None,
+                None, None, None)
+
+
+class GroupNormFn(torch.autograd.Function):
+    """GroupNorm on [N, B, C, *S] (also InstanceNorm); backward:
+    widek_groupnorm_bwd."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, n, groups, eps):
+        from . import ops
+        with torch.no_grad():
+            y = ops.groupnorm(x, n, groups, weight, bias, eps)
+        ctx.n, ctx.groups, ctx.eps, ctx.has_b = n, groups, eps, bias is not None
+        ctx.bias_shape = None if bias is None else bias.shape
+        ctx.save_for_backward(x, weight)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+        x, weight = ctx.saved_tensors
+        dx, dw, db = ops.groupnorm_bwd(x, dy.to(x.dtype).contiguous(), ctx.n, ctx.groups, weight, ctx.eps,
+                                       ctx.needs_input_grad[1], ctx.needs_input_grad[2] and ctx.has_b)
+        return (dx.view(x.shape), None if dw is None else dw.view(weight.shape),
+                None if db is None else db.view(ctx.bias_shape), None, None, None)
+
+
+def batchnorm_grad(x, n, c, weight, bias, running_mean, running_var, use_batch_stats, update_running, momentum,
+                   eps):
+    from . import ops
+    ok = (x.is_cuda and x.dtype in _KERNEL_DTYPES and x.dim() >= 3 and all(
+        t is None or t.dtype == x.dtype for t in (weight, bias, running_mean, running_var))
+        and (use_batch_stats or (running_mean is not None and running_var is not None)))
+    if not ok:
+        return run(ops.batchnorm, batchnorm_t, x, n, c, weight, bias, running_mean, running_var, use_batch_stats,
+                   update_running, momentum, eps)
+    return BatchNormFn.apply(x, weight, bias, n, c, running_mean, running_var, use_batch_stats, update_running,
+                             momentum, eps)
+
+
+def groupnorm_grad(x, n, groups, weight, bias, eps):
+    from . import ops
+    ok = (x.is_cuda and x.dtype in _KERNEL_DTYPES and x.dim() >= 3 and x.shape[2] % groups == 0
+          and all(t is None or t.dtype == x.dtype for t in (weight, bias)))
+    if not ok:
+        return run(ops.groupnorm, groupnorm_t, x, n, groups, weight, bias, eps, False)
+    return GroupNormFn.apply(x, weight, bias, n, groups, eps)

@@ -96,6 +96,9 @@ SIGNATURES = {
                                                           _int, _c_void_p],
     "widek_transpose": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
     "widek_linear_ln_fwd_ex": [_c_void_p] * 6 + [_i64] * 5 + [_int, _int, _dbl, _int, _c_void_p],
+    "widek_batchnorm_bwd": [_c_void_p] * 8 + [_i64] * 4 + [_int, _dbl, _int, _c_void_p],
+    "widek_groupnorm_bwd_workspace": [_i64] * 3,
+    "widek_groupnorm_bwd": [_c_void_p] * 6 + [_i64] * 5 + [_dbl, _int, _c_void_p, _i64, _c_void_p],
     "widek_linear_bwd_workspace": [_i64] * 4 + [_int],
     "widek_linear_bwd": [_c_void_p] * 6 + [_i64] * 4 + [_int, _c_void_p, _i64, _c_void_p],
     "widek_act_bwd": [_c_void_p] * 3 + [_i64, _int, _int, _c_void_p],
@@ -105,7 +108,7 @@ SIGNATURES = {
 RESTYPES = {"widek_batchnorm_train_workspace": ctypes.c_size_t, "widek_conv_workspace": ctypes.c_size_t,
             "widek_rnn_workspace": ctypes.c_size_t, "widek_conv_packed_weight_elems": _i64,
             "widek_launch_count": ctypes.c_longlong, "widek_linear_bwd_workspace": _i64,
-            "widek_layernorm_bwd_workspace": _i64}
+            "widek_layernorm_bwd_workspace": _i64, "widek_groupnorm_bwd_workspace": _i64}
 
 
 class WideKernelError(RuntimeError):

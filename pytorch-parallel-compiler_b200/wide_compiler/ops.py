@@ -439,8 +439,8 @@ def batchnorm(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias: Optiona
         return torch.ops.widek.batchnorm(x, n, c, weight, bias, running_mean, running_var, use_batch_stats,
                                          update_running, momentum, eps)
     if _AG.needs_grad(x, weight, bias):
-        return _AG.run(batchnorm, _AG.batchnorm_t, x, n, c, weight, bias, running_mean, running_var,
-                       use_batch_stats, update_running, momentum, eps)
+        return _AG.batchnorm_grad(x, n, c, weight, bias, running_mean, running_var, use_batch_stats,
+                                  update_running, momentum, eps)
     dev = N.require_cuda(x, weight, bias, running_mean, running_var, what="WideBatchNorm")
     _same_dtype("WideBatchNorm", x, weight, bias, running_mean, running_var)
     batch, l = _nbcl(x, n, c, "WideBatchNorm")
@@ -467,6 +467,49 @@ def batchnorm(x: Tensor, n: int, c: int, weight: Optional[Tensor], bias: Optiona
     return y
 
 
+def batchnorm_bwd(x: Tensor, dy: Tensor, n: int, c: int, weight: Optional[Tensor], running_mean: Optional[Tensor],
+                  running_var: Optional[Tensor], batch_stats: bool, eps: float, need_dw: bool = True,
+                  need_db: bool = True):
+    """Gradients of ``batchnorm``: (dx, dweight, dbias), None where not asked
+    or without affine parameters (widek_batchnorm_bwd)."""
+    dev = N.require_cuda(x, dy, weight, running_mean, running_var, what="WideBatchNorm backward")
+    _same_dtype("WideBatchNorm backward", x, dy, weight, running_mean, running_var)
+    batch, l = _nbcl(x, n, c, "WideBatchNorm backward")
+    xd, dyd = _dense(x), _dense(dy)
+    dx = torch.empty_like(xd)
+    dw = torch.empty((n * c,), device=dev, dtype=x.dtype) if need_dw and weight is not None else None
+    db = torch.empty((n * c,), device=dev, dtype=x.dtype) if need_db else None
+    with _guard(dev):
+        rc = N.lib().widek_batchnorm_bwd(xd.data_ptr(), dyd.data_ptr(), N.ptr(_opt_dense(weight)),
+                                         N.ptr(_opt_dense(running_mean)), N.ptr(_opt_dense(running_var)),
+                                         dx.data_ptr(), N.ptr(dw), N.ptr(db), n, batch, c, l, int(batch_stats),
+                                         float(eps), N.dtype_code(x), N.stream_ptr(dev))
+    N.check(rc, "widek_batchnorm_bwd")
+    return dx, dw, db
+
+
+def groupnorm_bwd(x: Tensor, dy: Tensor, n: int, groups: int, weight: Optional[Tensor], eps: float,
+                  need_dw: bool = True, need_db: bool = True):
+    """Gradients of ``groupnorm``: (dx, dweight, dbias), None where not asked
+    (widek_groupnorm_bwd; statistics recomputed from x)."""
+    dev = N.require_cuda(x, dy, weight, what="WideGroupNorm backward")
+    _same_dtype("WideGroupNorm backward", x, dy, weight)
+    batch, c = x.shape[1], x.shape[2]
+    l = math.prod(x.shape[3:])
+    xd, dyd = _dense(x), _dense(dy)
+    dx = torch.empty_like(xd)
+    dw = torch.empty((n * c,), device=dev, dtype=x.dtype) if need_dw and weight is not None else None
+    db = torch.empty((n * c,), device=dev, dtype=x.dtype) if need_db else None
+    ws_bytes = N.lib().widek_groupnorm_bwd_workspace(n, batch, c)
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    with _guard(dev):
+        rc = N.lib().widek_groupnorm_bwd(xd.data_ptr(), dyd.data_ptr(), N.ptr(_opt_dense(weight)), dx.data_ptr(),
+                                         N.ptr(dw), N.ptr(db), n, batch, c, l, groups, float(eps), N.dtype_code(x),
+                                         ws.data_ptr(), ws_bytes, N.stream_ptr(dev))
+    N.check(rc, "widek_groupnorm_bwd")
+    return dx, dw, db
+
+
 def groupnorm(x: Tensor, n: int, groups: int, weight: Optional[Tensor], bias: Optional[Tensor], eps: float,
               row_stats: bool = False):
     """GroupNorm on [N, B, C, *S] with statistics per (model, sample, group).
@@ -474,7 +517,9 @@ def groupnorm(x: Tensor, n: int, groups: int, weight: Optional[Tensor], bias: Op
     if _compiling() and not row_stats:
         return torch.ops.widek.groupnorm(x, n, groups, weight, bias, eps)
     if _AG.needs_grad(x, weight, bias):
-        return _AG.run(groupnorm, _AG.groupnorm_t, x, n, groups, weight, bias, eps, row_stats)
+        if row_stats:
+            return _AG.run(groupnorm, _AG.groupnorm_t, x, n, groups, weight, bias, eps, row_stats)
+        return _AG.groupnorm_grad(x, n, groups, weight, bias, eps)
     dev = N.require_cuda(x, weight, bias, what="WideGroupNorm")
     _same_dtype("WideGroupNorm", x, weight, bias)
     if x.dim() < 3 or x.shape[0] != n:

@@ -308,6 +308,50 @@ def make_grads(root: str) -> None:
     _save('grad_layernorm', 'grad_layernorm', {'n': n, 'd': d, 'eps': 1e-5}, w.state_dict(),
           {'x': x.detach(), 'dy': dy}, {'y': y.detach(), 'grads': grads})
 
+    # WideBatchNorm2d (wide_batchnorm_2d.py:53-72), training (batch
+    # statistics) and eval (running statistics)
+    for name, train in {'grad_bn2d_train': True, 'grad_bn2d_eval': False}.items():
+        torch.manual_seed(zlib.crc32(name.encode()) % 1000)
+        n, c = 3, 4
+        mods = [nn.BatchNorm2d(c) for _ in range(n)]
+        for m in mods:
+            with torch.no_grad():
+                m.running_mean.normal_(0, 1)
+                m.running_var.uniform_(0.5, 2.0)
+                m.weight.uniform_(0.5, 1.5)
+                m.bias.normal_(0, 0.1)
+        w = ref.WideBatchNorm2d.from_modules(mods)
+        w.train(train)
+        state0 = {k: v.clone() for k, v in w.state_dict().items()}
+        x = (torch.randn(n, 5, c, 6, 7) * 1.5 + 0.3).requires_grad_(True)
+        y = w(x)
+        dy = torch.randn_like(y)
+        (y * dy).sum().backward()
+        grads = {'x': x.grad.clone()}
+        for k, v in w.named_parameters():
+            grads[k] = v.grad.clone()
+        _save(name, 'grad_batchnorm', {'n': n, 'c': c, 'train': train, 'eps': 1e-5}, state0,
+              {'x': x.detach(), 'dy': dy}, {'y': y.detach(), 'grads': grads})
+
+    # WideGroupNorm (wide_groupnorm.py:90-117)
+    torch.manual_seed(31)
+    n, b, g, c = 3, 2, 4, 8
+    mods = [nn.GroupNorm(g, c) for _ in range(n)]
+    for m in mods:
+        with torch.no_grad():
+            m.weight.uniform_(0.5, 1.5)
+            m.bias.normal_(0, 0.1)
+    w = ref.WideGroupNorm.from_modules(mods)
+    x = (torch.randn(n, b, c, 5, 6) * 2 + 0.5).requires_grad_(True)
+    y = w(x)
+    dy = torch.randn_like(y)
+    (y * dy).sum().backward()
+    grads = {'x': x.grad.clone()}
+    for k, v in w.named_parameters():
+        grads[k] = v.grad.clone()
+    _save('grad_groupnorm', 'grad_groupnorm', {'n': n, 'groups': g, 'c': c, 'eps': 1e-5}, w.state_dict(),
+          {'x': x.detach(), 'dy': dy}, {'y': y.detach(), 'grads': grads})
+
 
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()

@@ -68,9 +68,13 @@ def _build_from_state(g):
         mod = wc.WideLinear(m['n'], m['in'], m['out'], bias=m['bias'])
     elif k in ('layernorm', 'grad_layernorm'):
         mod = wc.WideLayerNorm(m['n'], m['d'], m['eps'])
+    elif k == 'grad_batchnorm':
+        mod = wc.WideBatchNorm2d(m['n'], m['c'])
     elif k == 'batchnorm':
         cls = wc.WideBatchNorm2d if m['dims'] == 5 else wc.WideBatchNorm1d
         mod = cls(m['n'], m['c'])
+    elif k == 'grad_groupnorm':
+        mod = wc.WideGroupNorm(m['n'], m['groups'], m['c'])
     elif k == 'groupnorm':
         mod = wc.WideGroupNorm(m['n'], m['groups'], m['c'], affine=m['affine'])
     elif k == 'instancenorm':

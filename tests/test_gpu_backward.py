@@ -118,12 +118,16 @@ def test_layernorm_backward_vs_oracle(dtype, n, rows, d):
     no_device_error()
 
 
-@pytest.mark.parametrize("name", golden_names('grad_linear') + golden_names('grad_layernorm'))
+@pytest.mark.parametrize("name", golden_names('grad_linear') + golden_names('grad_layernorm')
+                         + golden_names('grad_batchnorm') + golden_names('grad_groupnorm'))
 def test_golden_gradients_through_modules(name):
     """The reference's own gradients (grad_* fixtures) reproduced through
-    this package's modules (WideLinear + activation glue, WideLayerNorm)."""
+    this package's modules (WideLinear + activation glue, WideLayerNorm,
+    WideBatchNorm2d in training and eval mode, WideGroupNorm)."""
     g = load_golden(name)
     mod = _build_from_state(g).to(DEV)
+    if g['kind'] == 'grad_batchnorm':
+        mod.train(g['meta']['train'])
     x = g['inputs']['x'].to(DEV).requires_grad_()
     y = mod(x)
     if g['kind'] == 'grad_linear' and g['meta']['act'] != 'none':
@@ -171,4 +175,59 @@ def test_traced_mlp_training_step_gradients():
         md(xi.double()).backward(dyi.double())
         for key, p in md.named_parameters():
             assert_fp32_close(grads[f'stages.{key}'][i], p.grad)
+    no_device_error()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,b,c,sp,batch_stats,affine", [
+    (3, 5, 4, (6, 7), True, True),
+    (2, 32, 64, (32, 32), True, True),        # cfg3's BatchNorm size per model (vector path)
+    (3, 4, 6, (5, 5), False, True),           # eval mode: running statistics
+    (2, 3, 5, (7,), True, False),             # 1-d, no affine, element-wise path (L = 7)
+])
+def test_batchnorm_backward_vs_oracle(dtype, n, b, c, sp, batch_stats, affine):
+    x = (torch.randn(n, b, c, *sp, generator=_g(c)) * 1.5 + 0.3).to(dtype)
+    w = torch.empty(n * c).uniform_(0.5, 1.5, generator=_g(1)).to(dtype) if affine else None
+    bb = (torch.randn(n * c, generator=_g(2)) * 0.1).to(dtype) if affine else None
+    rm = torch.randn(n * c, generator=_g(3)).to(dtype)
+    rv = torch.empty(n * c).uniform_(0.5, 2.0, generator=_g(4)).to(dtype)
+    dy = torch.randn(n, b, c, *sp, generator=_g(5)).to(dtype)
+    xg = x.to(DEV).requires_grad_()
+    wg = w.to(DEV).requires_grad_() if affine else None
+    bg = bb.to(DEV).requires_grad_() if affine else None
+    rmd, rvd = rm.to(DEV), rv.to(DEV)
+    y = ops.batchnorm(xg, n, c, wg, bg, rmd, rvd, batch_stats, False, 0.1, 1e-5)
+    names = kernels_run(lambda: y.backward(dy.to(DEV)))
+    assert any('norm_bwd_kernel' in s for s in names), names
+    rdx, rdw, rdb = O.batchnorm_grads(x, n, c, w, rm, rv, dy, batch_stats, 1e-5)
+    _close(dtype, xg.grad, rdx)
+    if affine:
+        _close(dtype, wg.grad, rdw)
+        _close(dtype, bg.grad, rdb)
+    no_device_error()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,b,c,groups,sp,affine", [
+    (3, 2, 8, 4, (5, 6), True),
+    (2, 4, 64, 32, (16, 16), True),           # vector path, two channels per group
+    (2, 3, 6, 6, (7,), False),                # InstanceNorm (one channel per group), element-wise path
+    (1, 2, 12, 1, (8, 8), True),              # one group: the whole sample
+])
+def test_groupnorm_backward_vs_oracle(dtype, n, b, c, groups, sp, affine):
+    x = (torch.randn(n, b, c, *sp, generator=_g(c + groups)) * 2 + 0.5).to(dtype)
+    w = torch.empty(n * c).uniform_(0.5, 1.5, generator=_g(1)).to(dtype) if affine else None
+    bb = (torch.randn(n * c, generator=_g(2)) * 0.1).to(dtype) if affine else None
+    dy = torch.randn(n, b, c, *sp, generator=_g(5)).to(dtype)
+    xg = x.to(DEV).requires_grad_()
+    wg = w.to(DEV).requires_grad_() if affine else None
+    bg = bb.to(DEV).requires_grad_() if affine else None
+    y = ops.groupnorm(xg, n, groups, wg, bg, 1e-5)
+    names = kernels_run(lambda: y.backward(dy.to(DEV)))
+    assert any('norm_bwd_kernel' in s for s in names), names
+    rdx, rdw, rdb = O.groupnorm_grads(x, n, groups, w, dy, 1e-5)
+    _close(dtype, xg.grad, rdx)
+    if affine:
+        _close(dtype, wg.grad, rdw)
+        _close(dtype, bg.grad, rdb)
     no_device_error()

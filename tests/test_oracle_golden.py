@@ -79,6 +79,14 @@ def oracle_eval(g):
         dx, dw, db = O.layernorm_grads(inp['x'], s['weight'], inp['dy'], m['n'], m['d'], m['eps'])
         return {'y': O.layernorm(inp['x'], s['weight'], s['bias'], m['n'], m['d'], m['eps']),
                 'grads.x': dx, 'grads.weight': dw, 'grads.bias': db}
+    if k == 'grad_batchnorm':
+        dx, dw, db = O.batchnorm_grads(inp['x'], m['n'], m['c'], s['op.weight'], s['op.running_mean'],
+                                       s['op.running_var'], inp['dy'], m['train'], m['eps'])
+        return {'grads.x': dx, 'grads.op.weight': dw, 'grads.op.bias': db}
+    if k == 'grad_groupnorm':
+        dx, dw, db = O.groupnorm_grads(inp['x'], m['n'], m['groups'], s['norm.weight'], inp['dy'], m['eps'])
+        return {'y': O.groupnorm(inp['x'], m['n'], m['groups'], s['norm.weight'], s['norm.bias'], m['eps']),
+                'grads.x': dx, 'grads.norm.weight': dw, 'grads.norm.bias': db}
     raise KeyError(k)
 
 
@@ -101,7 +109,7 @@ def test_oracle_matches_reference_fixture(name):
 def test_fixture_set_covers_every_primitive():
     kinds = {load_golden(n)['kind'] for n in golden_names()}
     assert {'linear', 'layernorm', 'batchnorm', 'groupnorm', 'instancenorm', 'embedding', 'conv', 'attention',
-            'gru', 'lstm', 'traced', 'grad_linear', 'grad_layernorm'} <= kinds
+            'gru', 'lstm', 'traced', 'grad_linear', 'grad_layernorm', 'grad_batchnorm', 'grad_groupnorm'} <= kinds
 
 
 def test_pack_roundtrip_oracle():
