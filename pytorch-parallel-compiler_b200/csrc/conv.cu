@@ -532,8 +532,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // crosses into the next model or output tile.
 // ---------------------------------------------------------------------------
 constexpr int kHaloMaxStages = 8;
-constexpr int kHaloEpiWarps = 4;
-constexpr int kHaloThreads = 224;   // TMA warp, MMA warp, 4 epilogue warps, second MMA warp
+// Two epilogue warpgroups: for N-first / packed outputs warps 2..5 take TMEM
+// lanes (pixels) 32q..32q+15 of their quarter q and warps 6..9 lanes
+// 32q+16..32q+31, so such a tile drains in half the time (its epilogue, not
+// the MMAs, bounded the tile with four warps: cfg3's conv2 352 -> 333 us).
+constexpr int kHaloEpiWarps = 8;
+constexpr int kHaloThreads = 352;   // TMA warp, MMA warp, 8 epilogue warps, second MMA warp
+__device__ __forceinline__ void halo_epi_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kHaloEpiWarps * 32) : "memory");
+}
 constexpr int HBN = 64;
 
 struct ConvHaloGeom {
@@ -887,13 +894,14 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         }
         __syncwarp();
     } else {
-        // Epilogue (as conv_tc_kernel with a TMA store): warps 2..5, TMEM lane
-        // quarter q = warp % 4. Bias and the folded BatchNorm become one
+        // Epilogue (as conv_tc_kernel with a TMA store): warps 2..9, TMEM lane
+        // quarter q = warp % 4, 16-lane half eh = (warp - 2) / 4. Bias and the folded BatchNorm become one
         // (scale, offset) pair per channel, staged in shared memory when the
         // (model, output tile) changes and read as a broadcast per value.
         // Tile i uses buffer i % 2; with a residual that buffer holds the
         // tile's residual, which the output overwrites in place.
         const int q = warp & 3;
+        const int eh = (warp - 2) >> 2;            // which 16-lane half of the quarter
         const int ep_tid = threadIdx.x - 64;
         const T* bias = static_cast<const T*>(e.bias);
         const T* scale = static_cast<const T*>(e.scale);
@@ -961,7 +969,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 }
                 par_key = key;
             }
-            epi_bar_sync();
+            halo_epi_sync();
             if (fresh) {
 #pragma unroll
                 for (int m = 0; m < HBN / 2; ++m) {
@@ -984,8 +992,12 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             if constexpr (OUT_CL) {
                 auto epilogue = [&](auto act_c) {
                     constexpr int ACT = decltype(act_c)::value;
+                    // channels-last output: the first warpgroup drains both
+                    // 16-lane halves (splitting them made conv1 slower, 279 ->
+                    // 293 us at cfg3, its MMAs being fed by the input loads);
+                    // the second only joins the barriers
 #pragma unroll
-                    for (int hs = 0; hs < 2; ++hs) {
+                    for (int hs = 0; hs < (eh == 0 ? 2 : 0); ++hs) {
                         // pixels q*32 + 16*hs + (lane % 16)
                         uint32_t v[32];
                         tmem_ld_16x32bx2_x32_split32(
@@ -1028,8 +1040,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 auto epilogue = [&](auto act_c, auto rf_c) {
                     constexpr int ACT = decltype(act_c)::value;
                     constexpr bool RF = decltype(rf_c)::value;
-#pragma unroll 1
-                    for (int h = 0; h < 2; ++h) {
+                    {
+                        const int h = eh;
                         uint32_t v[32];
                         tmem_ld_16x256b_x8(tmem_base + (uint32_t)(acc * HBN) + ((uint32_t)(q * 32 + 16 * h) << 16), v);
                         // row address of matrix mi = (group mi & 1, column block 2*jj + (mi >> 1))
@@ -1100,7 +1112,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             fence_proxy_async_smem();
-            epi_bar_sync();
+            halo_epi_sync();
             if (ep_tid == 0) {
                 if (OUT_CL)
                     tma_store_4d(&tm_y, sOut, nt * HBN, wo0, ho0, (int)img);
