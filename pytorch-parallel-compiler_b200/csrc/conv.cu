@@ -794,7 +794,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             }
         }
     } else if (warp == 1 || warp == kHaloThreads / 32 - 1) {
-        // Two MMA issuers (one thread each, in warps 1 and 6): issuer i takes
+        // Two MMA issuers (one thread each, in warps 1 and 10): issuer i takes
         // the CTA's tiles with local index = i (mod 2) into accumulator i, so
         // one tile's MMAs go out while the other's are still being issued:
         // a single thread sustains ~60 cycles per M128-N64-K16 MMA, two reach
