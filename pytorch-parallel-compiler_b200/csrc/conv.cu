@@ -978,13 +978,18 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                     po[m] = pp.y;
                 }
             }
-            if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+            // With a channels-last output the second warpgroup has no pixels
+            // to drain: it neither polls the accumulator nor the residual
+            // (polling warps take issue slots from the MMA and TMA warps),
+            // and only keeps step through the barriers and the arrival.
+            const bool idle = OUT_CL && eh == 1;
+            if (!idle && !mbar_wait(&tfull[acc], aph, abort_flag)) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
                 break;
             }
             tc_fence_after();
-            if (RES_TMA && !mbar_wait(&res_full[buf], (uint32_t)((local >> 1) & 1), abort_flag)) {
+            if (RES_TMA && !idle && !mbar_wait(&res_full[buf], (uint32_t)((local >> 1) & 1), abort_flag)) {
                 *abort_flag = 1;
                 raise_device_error(err, DEV_ERR_CONV_TIMEOUT);
                 break;
