@@ -216,6 +216,32 @@ def test_fusion_plan_structure():
     assert g['relu_1']['residual'] == 'x' and g['relu_1']['residual_first'] and g['relu_1']['act'] == 1
 
 
+class _AttnLNT(nn.Module):
+    def __init__(self, causal=False, weights=False):
+        super().__init__()
+        self.attn = nn.MultiheadAttention(16, 2, batch_first=True)
+        self.ln = nn.LayerNorm(16)
+        self.causal, self.weights = causal, weights
+
+    def forward(self, x):
+        a, w = self.attn(x, x, x, need_weights=False, is_causal=self.causal)
+        return self.ln(a) if not self.weights else (self.ln(a), w)
+
+
+def test_fusion_plan_attention_layernorm():
+    """Self-attention whose output (getitem 0) only feeds a LayerNorm of the
+    same width becomes one 'attn_ln' group (the LayerNorm runs in the output
+    projection's epilogue); the unused getitem of the weights folds in; when
+    the weights are read too, or the attention is not self-attention, the
+    pair stays unfused."""
+    m = wc.TracedWideModel.from_models([_AttnLNT(causal=True) for _ in range(2)], torch.randn(2, 8, 16))
+    g = m._build_fusion_plan()['groups']
+    assert list(g) == ['ln'] and g['ln']['kind'] == 'attn_ln' and g['ln']['is_causal']
+    assert g['ln']['nodes'][0] == 'attn' and g['ln']['nodes'][-1] == 'ln' and len(g['ln']['nodes']) == 4
+    m2 = wc.TracedWideModel.from_models([_AttnLNT(weights=True) for _ in range(2)], torch.randn(2, 8, 16))
+    assert not m2._build_fusion_plan()['groups']
+
+
 def test_compile_flag_gives_graph_executor():
     """compile=True (the reference's torch.compile switch, api.py:137-147)
     returns the CUDA-graph executor, which forwards attribute access to the
