@@ -217,29 +217,28 @@ def test_fusion_plan_structure():
 
 
 class _AttnLNT(nn.Module):
-    def __init__(self, causal=False, weights=False):
+    def __init__(self, causal=False, reuse=False):
         super().__init__()
         self.attn = nn.MultiheadAttention(16, 2, batch_first=True)
         self.ln = nn.LayerNorm(16)
-        self.causal, self.weights = causal, weights
+        self.causal, self.reuse = causal, reuse
 
     def forward(self, x):
-        a, w = self.attn(x, x, x, need_weights=False, is_causal=self.causal)
-        return self.ln(a) if not self.weights else (self.ln(a), w)
+        a, _ = self.attn(x, x, x, need_weights=False, is_causal=self.causal)
+        return self.ln(a) + a if self.reuse else self.ln(a)
 
 
 def test_fusion_plan_attention_layernorm():
     """Self-attention whose output (getitem 0) only feeds a LayerNorm of the
     same width becomes one 'attn_ln' group (the LayerNorm runs in the output
     projection's epilogue); the unused getitem of the weights folds in; when
-    the weights are read too, or the attention is not self-attention, the
-    pair stays unfused."""
+    the attention output is read elsewhere too, the pair stays unfused."""
     m = wc.TracedWideModel.from_models([_AttnLNT(causal=True) for _ in range(2)], torch.randn(2, 8, 16))
     g = m._build_fusion_plan()['groups']
     assert list(g) == ['ln'] and g['ln']['kind'] == 'attn_ln' and g['ln']['is_causal']
     assert g['ln']['nodes'][0] == 'attn' and g['ln']['nodes'][-1] == 'ln' and len(g['ln']['nodes']) == 4
-    m2 = wc.TracedWideModel.from_models([_AttnLNT(weights=True) for _ in range(2)], torch.randn(2, 8, 16))
-    assert not m2._build_fusion_plan()['groups']
+    m2 = wc.TracedWideModel.from_models([_AttnLNT(reuse=True) for _ in range(2)], torch.randn(2, 8, 16))
+    assert not any(g['kind'] == 'attn_ln' for g in m2._build_fusion_plan()['groups'].values())
 
 
 def test_compile_flag_gives_graph_executor():
