@@ -118,3 +118,45 @@ def test_pack_roundtrip_oracle():
     torch.testing.assert_close(packed, g['inputs']['packed'])
     nf = O.packed_to_nfirst(packed, g['meta']['n'])
     torch.testing.assert_close(O.nfirst_to_packed(nf), packed)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_oracle_gradient_formulas_match_autograd(seed):
+    """The oracle's explicit gradient formulas against torch autograd of the
+    primitives' torch forms (float64) on random shapes, beyond the reference
+    fixtures: WideLinear (+ ReLU / GELU), LayerNorm, BatchNorm with batch and
+    with running statistics, GroupNorm."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)
+    tol = dict(rtol=1e-9, atol=1e-10)
+    n, b, k, o = 2 + seed, 3 + seed, 5 + 2 * seed, 4 + seed
+    acts = {'none': lambda t: t, 'relu': torch.relu, 'gelu': F.gelu}
+    for act, fn in acts.items():
+        x, w, bb, dy = r(n, b, k).requires_grad_(), r(n, o, k).requires_grad_(), r(n, o).requires_grad_(), r(n, b, o)
+        fn(torch.einsum('noi,nbi->nbo', w, x) + bb[:, None, :]).backward(dy)
+        for got, want in zip(O.linear_grads(x.detach(), w.detach(), bb.detach(), dy, act), (x.grad, w.grad, bb.grad)):
+            torch.testing.assert_close(got, want, **tol)
+    d = 6 + seed
+    x, w, bb, dy = r(n, b, 2, d).requires_grad_(), r(n * d).requires_grad_(), r(n * d).requires_grad_(), r(n, b, 2, d)
+    (F.layer_norm(x, (d,), eps=1e-5) * w.view(n, 1, 1, d) + bb.view(n, 1, 1, d)).backward(dy)
+    for got, want in zip(O.layernorm_grads(x.detach(), w.detach(), dy, n, d, 1e-5), (x.grad, w.grad, bb.grad)):
+        torch.testing.assert_close(got, want, **tol)
+    c = 3
+    for stats in (True, False):
+        x, w, bb = r(n, b, c, 4, 5).requires_grad_(), r(n * c).requires_grad_(), r(n * c).requires_grad_()
+        rm, rv, dy = r(n * c), torch.rand(n * c, generator=g, dtype=torch.float64) + 0.5, r(n, b, c, 4, 5)
+        # the reference's inner nn.BatchNorm over N*C channels on [B, N*C, H, W]
+        xt = x.transpose(0, 1).reshape(b, n * c, 4, 5)
+        y = F.batch_norm(xt, rm.clone(), rv.clone(), w, bb, training=stats, momentum=0.0, eps=1e-5)
+        y.reshape(b, n, c, 4, 5).transpose(0, 1).backward(dy)
+        got = O.batchnorm_grads(x.detach(), n, c, w.detach(), rm, rv, dy, stats, 1e-5)
+        for gt, want in zip(got, (x.grad, w.grad, bb.grad)):
+            torch.testing.assert_close(gt, want, **tol)
+    groups, c = 2, 4
+    x, w, bb, dy = r(n, b, c, 3, 3).requires_grad_(), r(n * c).requires_grad_(), r(n * c).requires_grad_(), r(n, b, c, 3, 3)
+    # the reference's nn.GroupNorm(N*G, N*C) on [B, N*C, H, W]
+    xt = x.transpose(0, 1).reshape(b, n * c, 3, 3)
+    F.group_norm(xt, n * groups, w, bb, eps=1e-5).reshape(b, n, c, 3, 3).transpose(0, 1).backward(dy)
+    for got, want in zip(O.groupnorm_grads(x.detach(), n, groups, w.detach(), dy, 1e-5), (x.grad, w.grad, bb.grad)):
+        torch.testing.assert_close(got, want, **tol)
