@@ -4,9 +4,11 @@ Headline workload: cfg3, the largest of the reference's configurations that
 fits one GPU: a TracedWideModel of N=100 ResBlocks (Conv3x3 64->64, BatchNorm
 eval, ReLU, Conv3x3, BatchNorm, + identity), B=32, 32x32, bf16, packed input
 [32, 6400, 32, 32]. A step is one wide forward over the whole batch. Every
-other configuration (cfg1 MLP, cfg2 WideLinear, cfg4 GRU/LSTM, cfg5
-attention+LN) and four memory-bound norm workloads are measured in the same
-run and reported under "configs" with the same keys.
+other configuration (cfg1 MLP and cfg5 attention -> LayerNorm as
+TracedWideModels, cfg2 WideLinear, cfg4 GRU/LSTM) and four memory-bound norm
+workloads are measured in the same run and reported under "configs" with
+the same keys. Two training-step workloads (forward + backward: cfg2train,
+lntrain) run only when named with --workload.
 
   value   samples/s = N*B / t_step; t_step from CUDA events over K
           back-to-back steps with inputs resident in HBM; max over ranks.
