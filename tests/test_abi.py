@@ -102,3 +102,36 @@ def test_bounded_wait_probe_rejects_bad_limits():
     assert lib.widek_test_bounded_wait(0, None) == N.WIDEK_ERR_INVALID
     assert lib.widek_test_bounded_wait(2_000_000_000, None) == N.WIDEK_ERR_INVALID
     assert "limit" in N.last_error()
+
+
+def test_backward_and_fused_entry_argument_checks():
+    """The backward entries and the fused projection + LayerNorm reject bad
+    arguments (and accept empty problems) before any CUDA call."""
+    from wide_compiler import _native as N
+    lib = N.load()
+    P = 16                               # a stand-in pointer: never dereferenced on these paths
+    assert lib.widek_linear_bwd_workspace(-1, 1, 1, 1, N.BF16) == -1
+    ws = lib.widek_linear_bwd_workspace(2, 4, 8, 8, N.BF16)
+    assert ws > 0
+    assert lib.widek_linear_bwd(P, P, P, P, P, P, 2, 4, 8, 8, N.BF16, P, ws - 1, None) == N.WIDEK_ERR_INVALID
+    assert "workspace" in N.last_error()
+    assert lib.widek_linear_bwd(None, None, None, None, None, None, 0, 4, 8, 8, N.BF16, None, 0, None) == 0
+    assert lib.widek_act_bwd(P, P, P, 4, 0, N.BF16, None) == N.WIDEK_ERR_INVALID
+    assert lib.widek_transpose(P, P, 1, 2, 2, 9, None) == N.WIDEK_ERR_INVALID
+    assert lib.widek_layernorm_bwd_workspace(-1, 1, 1) == -1
+    assert lib.widek_layernorm_bwd(P, P, P, P, P, P, 1, 4, 2000, 1e-5, N.BF16, P, 1 << 20, None) == \
+        N.WIDEK_ERR_UNSUPPORTED
+    gws = lib.widek_groupnorm_bwd_workspace(2, 3, 8)
+    assert gws > 0
+    assert lib.widek_groupnorm_bwd(P, P, P, P, P, P, 2, 3, 5, 4, 2, 1e-5, N.BF16, P, gws, None) == \
+        N.WIDEK_ERR_INVALID                                        # 5 channels in 2 groups
+    assert lib.widek_groupnorm_bwd(P, P, P, P, P, P, 2, 3, 8, 4, 2, 1e-5, N.BF16, P, gws - 1, None) == \
+        N.WIDEK_ERR_INVALID                                        # workspace too small
+    assert lib.widek_batchnorm_bwd(P, P, P, None, None, P, P, P, 2, 3, 4, 5, 0, 1e-5, N.BF16, None) == \
+        N.WIDEK_ERR_INVALID                                        # eval mode without running statistics
+    assert lib.widek_batchnorm_bwd(None, None, None, None, None, None, None, None, 0, 3, 4, 5, 1, 1e-5, N.BF16,
+                                   None) == 0
+    assert lib.widek_linear_ln_fwd_ex(P, P, P, P, P, P, 2, 4, 8, 16, 4, 7, 0, 1e-5, N.BF16, None) == \
+        N.WIDEK_ERR_INVALID                                        # unknown layout
+    assert lib.widek_linear_ln_fwd_ex(P, P, P, P, P, P, 2, 4, 8, 16, 4, 0, 0, 1e-5, N.F32, None) == \
+        N.WIDEK_ERR_UNSUPPORTED                                    # fp32: the caller runs the two ops
