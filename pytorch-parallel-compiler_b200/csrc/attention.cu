@@ -7,8 +7,9 @@
 // h*dh), so no head-split copies exist; the output is written directly as
 // [n, b, tq, D] (head h at columns h*dh) for the output projection.
 //
-// bf16/f16, dh = 64, no explicit mask: the tcgen05/TMEM kernel of
-// attention_sm100.cu. Other bf16/f16 calls with dh in {64, 128}: a warp-level
+// bf16/f16, dh = 64, 16-byte-aligned operands with row strides a multiple of
+// 8 elements (causal and/or an explicit mask of any kind): the tcgen05/TMEM
+// kernel of attention_sm100.cu. Other bf16/f16 calls with dh in {64, 128}: a warp-level
 // tensor-core kernel here (m16n8k16 MMA, 64 or 128 query rows per CTA,
 // 64-key tiles double-buffered with cp.async, XOR-swizzled shared memory for
 // conflict-free ldmatrix). fp32 and other head sizes: a CUDA-core kernel (one
