@@ -91,9 +91,11 @@ class WideAttention(nn.Module):
         if value is None:
             value = key
         if self.training and self.dropout > 0.0:
-            raise NotImplementedError("WideAttention: attention dropout in training mode is not implemented "
-                                      "by the sm_100a kernels; call .eval() or set dropout=0")
-        out = ops.attention(self, query, key, value, attn_mask, is_causal)
+            # random attention dropout: projections on the kernels, the core
+            # on torch's SDPA with dropout_p (ops.attention_dropout)
+            out = ops.attention_dropout(self, query, key, value, attn_mask, is_causal, self.dropout)
+        else:
+            out = ops.attention(self, query, key, value, attn_mask, is_causal)
         return (out, None) if mha_mode else out
 
     def forward_packed(self, query: Tensor, key=None, value=None, attn_mask=None, is_causal: bool = False,

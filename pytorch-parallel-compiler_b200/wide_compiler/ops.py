@@ -907,6 +907,41 @@ def attention(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optiona
                              key is query and value is query, out_ln)
 
 
+def attention_dropout(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask: Optional[Tensor],
+                      is_causal: bool, dropout_p: float) -> Tensor:
+    """WideAttention in training mode with attention dropout
+    (wide_attention.py:221-228 of the reference, which passes
+    ``dropout_p = self.dropout`` to scaled_dot_product_attention while
+    training). The Q, K, V and output projections run on the WideLinear
+    kernels (with their backward kernels under autograd); the core with its
+    random mask runs on torch's ``scaled_dot_product_attention`` on the GPU,
+    whose backward reuses the mask its forward drew from torch's generator,
+    so a seeded run draws the same mask as the reference's. Rows with no
+    attended key follow SDPA here (NaN), not the kernels' zeros."""
+    import torch.nn.functional as F
+    N.require_cuda(query, key, value, mod.q_weight, what="WideAttention")
+    _same_dtype("WideAttention", mod.q_weight, query, key, value)
+    if is_causal and attn_mask is not None:
+        raise RuntimeError("WideAttention: an explicit attn_mask cannot be combined with is_causal=True "
+                           "(same rule as scaled_dot_product_attention)")
+    n, d, heads = mod.n, mod.d_model, mod.n_heads
+    dh = d // heads
+    if query.dim() != 4 or query.shape[0] != n or query.shape[3] != d:
+        raise ValueError(f"WideAttention: query must be [N={n}, B, T, D={d}], got {tuple(query.shape)}")
+    _, b, tq, _ = query.shape
+    tk = key.shape[2]
+    if key.shape[:2] != (n, b) or value.shape[:3] != key.shape[:3]:
+        raise ValueError("WideAttention: key/value shapes do not match the query")
+    kv_b = mod.kv_bias
+    q = linear(query, mod.q_weight, mod.q_bias)
+    k = linear(key, mod.kv_weight[:, :d], None if kv_b is None else kv_b[:, :d])
+    v = linear(value, mod.kv_weight[:, d:], None if kv_b is None else kv_b[:, d:])
+    heads_of = lambda t, tt: t.reshape(n * b, tt, heads, dh).transpose(1, 2)
+    o = F.scaled_dot_product_attention(heads_of(q, tq), heads_of(k, tk), heads_of(v, tk), attn_mask=attn_mask,
+                                       dropout_p=dropout_p, is_causal=is_causal, scale=1.0 / math.sqrt(dh))
+    return linear(o.transpose(1, 2).reshape(n, b, tq, d), mod.out_weight, mod.out_bias)
+
+
 # ---------------------------------------------------------------------------
 # Convolutions
 # ---------------------------------------------------------------------------

@@ -257,3 +257,66 @@ def test_compile_flag_gives_graph_executor():
     assert isinstance(b, GraphedWideModel)
     with pytest.raises(RuntimeError, match="CUDA"):
         g(torch.randn(2, 24))
+
+
+def _attention_dropout_reference(mod, query, key, value, attn_mask, is_causal):
+    """The reference's fused WideAttention forward in training mode
+    (wide_attention.py:178-238): einsum projections, head split by
+    view/permute/reshape, SDPA with dropout_p = module dropout."""
+    n, d, h = mod.n, mod.d_model, mod.n_heads
+    dh = d // h
+    _, b, tq, _ = query.shape
+    tk = key.shape[2]
+    q = torch.einsum('nbtd,nod->nbto', query, mod.q_weight) + mod.q_bias.view(n, 1, 1, d)
+    k = torch.einsum('nbtd,nod->nbto', key, mod.kv_weight[:, :d]) + mod.kv_bias[:, :d].view(n, 1, 1, d)
+    v = torch.einsum('nbtd,nod->nbto', value, mod.kv_weight[:, d:]) + mod.kv_bias[:, d:].view(n, 1, 1, d)
+    split = lambda t, tt: t.view(n, b, tt, h, dh).permute(0, 1, 3, 2, 4).reshape(n * b, h, tt, dh)
+    o = F.scaled_dot_product_attention(split(q, tq), split(k, tk), split(v, tk), attn_mask=attn_mask,
+                                       dropout_p=mod.dropout, is_causal=is_causal)
+    o = o.view(n, b, h, tq, dh).permute(0, 1, 3, 2, 4).reshape(n, b, tq, d)
+    return torch.einsum('nbtd,nod->nbto', o, mod.out_weight) + mod.out_bias.view(n, 1, 1, d)
+
+
+@pytest.mark.parametrize("case", ["self", "causal", "bool_mask", "cross"])
+def test_attention_dropout_composition(monkeypatch, case):
+    """Training-mode attention dropout: WideAttention.forward routes to
+    ops.attention_dropout, whose projections, head split, SDPA call and merge
+    reproduce the reference's forward, drawing the same dropout mask from a
+    seeded generator. The projection kernels are replaced by their torch
+    formulation here (no GPU); only the composition is under test."""
+    from wide_compiler import _native, ops
+    monkeypatch.setattr(_native, "require_cuda", lambda *t, what: torch.device("cpu"))
+    monkeypatch.setattr(ops, "linear", lambda x, w, b, act=0: torch.einsum('n...k,nok->n...o', x, w)
+                        + b.view(b.shape[0], *([1] * (x.dim() - 2)), b.shape[1]))
+    torch.manual_seed(0)
+    mod = wc.WideAttention(3, 32, 4, dropout=0.25).train()
+    with torch.no_grad():
+        for p in (mod.q_bias, mod.kv_bias, mod.out_bias):
+            p.normal_(0, 0.1)
+    query = torch.randn(3, 2, 6, 32)
+    key = value = query
+    kw = {}
+    if case == "cross":
+        key = torch.randn(3, 2, 5, 32)
+        value = torch.randn(3, 2, 5, 32)
+    if case == "causal":
+        kw = {"is_causal": True}
+    if case == "bool_mask":
+        kw = {"attn_mask": torch.rand(6, 6) > 0.3}
+    torch.manual_seed(11)
+    got = mod(query, key if case == "cross" else None, value if case == "cross" else None, **kw)
+    got = got[0] if case == "cross" else got
+    torch.manual_seed(11)
+    want = _attention_dropout_reference(mod, query, key, value, kw.get("attn_mask"), kw.get("is_causal", False))
+    torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-6)
+    torch.manual_seed(12)
+    other = mod(query, key if case == "cross" else None, value if case == "cross" else None, **kw)
+    other = other[0] if case == "cross" else other
+    assert not torch.allclose(got, other)                        # the mask is random
+    got.sum().backward()
+    for p in (mod.q_weight, mod.kv_weight, mod.out_weight, mod.q_bias, mod.kv_bias, mod.out_bias):
+        assert p.grad is not None and torch.isfinite(p.grad).all()
+    mod.eval()
+    with pytest.raises(RuntimeError, match="CUDA"):              # eval mode: the kernels, which need a GPU
+        monkeypatch.undo()
+        mod(query)
