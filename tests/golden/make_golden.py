@@ -10,7 +10,7 @@ Each fixture ``<case>.pt`` is a dict:
     inputs    input tensors
     outputs   reference outputs (and updated running stats where relevant)
 
-Usage:  python tests/golden/make_golden.py [--root /path/to/reference] [--only forward|grads]
+Usage:  python tests/golden/make_golden.py [--root /path/to/reference] [--only forward|grads|traced_seq]
 The fixtures are small (a few hundred KB in total) and committed.
 """
 from __future__ import annotations
@@ -353,16 +353,85 @@ def make_grads(root: str) -> None:
           {'x': x.detach(), 'dy': dy}, {'y': y.detach(), 'grads': grads})
 
 
+class AttnLN(nn.Module):
+    """cfg5's model, small: causal self-attention, then LayerNorm."""
+
+    def __init__(self, d=16, heads=2):
+        super().__init__()
+        self.attn = nn.MultiheadAttention(d, heads, batch_first=True)
+        self.ln = nn.LayerNorm(d)
+
+    def forward(self, x):
+        a, _ = self.attn(x, x, x, need_weights=False, is_causal=True)
+        return self.ln(a)
+
+
+class GRUOut(nn.Module):
+    def __init__(self, i=6, h=10):
+        super().__init__()
+        self.gru = nn.GRU(i, h, batch_first=True)
+
+    def forward(self, x):
+        out, _ = self.gru(x)
+        return out
+
+
+class LSTMOut(nn.Module):
+    def __init__(self, i=6, h=10):
+        super().__init__()
+        self.lstm = nn.LSTM(i, h, batch_first=True)
+
+    def forward(self, x):
+        out, _ = self.lstm(x)
+        return out
+
+
+SEQ_GRAPHS = {'traced_attn_ln': (AttnLN, 3, (2, 12, 16), {'heads': 2, 'causal': True}),
+              'traced_gru': (GRUOut, 3, (2, 5, 6), {}), 'traced_lstm': (LSTMOut, 2, (3, 4, 6), {})}
+
+
+def make_traced_seq(root: str) -> None:
+    """TracedWideModel graphs of the sequence primitives (reference
+    traced_wide.py:450-534 around wide_attention.py / wide_gru.py /
+    wide_lstm.py): attention -> getitem -> LayerNorm (cfg5's graph, causal)
+    and a recurrent layer -> getitem, on packed inputs [B, N*T, F]."""
+    ref = refimport.load(root)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for name, (cls, n, shape, extra) in SEQ_GRAPHS.items():
+        torch.manual_seed(zlib.crc32(name.encode()) % 1000)
+        models = [cls().eval() for _ in range(n)]
+        for m in models:
+            for mod in m.modules():
+                if isinstance(mod, nn.LayerNorm):
+                    with torch.no_grad():
+                        mod.weight.uniform_(0.5, 1.5)
+                        mod.bias.normal_(0, 0.1)
+                if isinstance(mod, nn.MultiheadAttention):
+                    with torch.no_grad():
+                        mod.in_proj_bias.normal_(0, 0.1)
+                        mod.out_proj.bias.normal_(0, 0.1)
+        wide = ref.TracedWideModel.from_models(models, torch.randn(*shape)).eval()
+        inputs = [torch.randn(*shape) for _ in range(n)]
+        packed = ref.pack_inputs(inputs)
+        with torch.no_grad():
+            out = wide(packed)
+        _save(name, 'traced', {'n': n, 'model': cls.__name__, **extra},
+              {f"m{k}.{key}": v for k, m in enumerate(models) for key, v in m.state_dict().items()},
+              {'inputs': inputs, 'packed': packed}, {'y': out})
+
+
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()
     ap.add_argument('--root', default=refimport.DEFAULT_ROOT)
-    ap.add_argument('--only', choices=['forward', 'grads'], default=None,
-                    help="generate only the forward or only the gradient fixtures")
+    ap.add_argument('--only', choices=['forward', 'grads', 'traced_seq'], default=None,
+                    help="generate only the forward, the gradient or the traced sequence-model fixtures")
     a = ap.parse_args()
     if not refimport.available(a.root):
         sys.exit(f"reference not found under {a.root!r}: pass --root or set WIDE_REFERENCE_ROOT to the "
                  "checkout that holds wide_compiler/")
-    if a.only != 'grads':
+    if a.only in (None, 'forward'):
         make_all(a.root)
-    if a.only != 'forward':
+    if a.only in (None, 'grads'):
         make_grads(a.root)
+    if a.only in (None, 'traced_seq'):
+        make_traced_seq(a.root)

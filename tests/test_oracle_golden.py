@@ -68,6 +68,24 @@ def oracle_eval(g):
             y = O.resblock(x, n, cat('conv1.weight'), cat('conv1.bias'), bn('bn1'), cat('conv2.weight'),
                            cat('conv2.bias'), bn('bn2'))
             return {'y': O.nfirst_to_packed(y)}
+        st = lambda key: torch.stack([s[f'm{i}.{key}'] for i in range(n)])
+        x = O.packed_to_nfirst(inp['packed'], n)
+        if m['model'] == 'AttnLN':
+            # MultiheadAttention's packed in_proj: q rows [0, D), then k and v
+            d = x.shape[-1]
+            w_in, b_in = st('attn.in_proj_weight'), st('attn.in_proj_bias')
+            y = O.attention(x, x, x, w_in[:, :d], w_in[:, d:], b_in[:, :d], b_in[:, d:],
+                            st('attn.out_proj.weight'), st('attn.out_proj.bias'), m['heads'], None, m['causal'])
+            y = O.layernorm(y, st('ln.weight').reshape(-1), st('ln.bias').reshape(-1), n, d, 1e-5)
+            return {'y': O.nfirst_to_packed(y)}
+        if m['model'] == 'GRUOut':
+            y, _ = O.gru(x, None, st('gru.weight_ih_l0'), st('gru.weight_hh_l0'), st('gru.bias_ih_l0'),
+                         st('gru.bias_hh_l0'))
+            return {'y': O.nfirst_to_packed(y)}
+        if m['model'] == 'LSTMOut':
+            y, _ = O.lstm(x, None, None, st('lstm.weight_ih_l0'), st('lstm.weight_hh_l0'), st('lstm.bias_ih_l0'),
+                          st('lstm.bias_hh_l0'))
+            return {'y': O.nfirst_to_packed(y)}
     if k == 'grad_linear':
         y = O.activation(O.linear(inp['x'], s['weight'], s.get('bias')), m['act'])
         dx, dw, db = O.linear_grads(inp['x'], s['weight'], s.get('bias'), inp['dy'], m['act'])
