@@ -937,7 +937,8 @@ def attention_dropout(mod, query: Tensor, key: Tensor, value: Tensor, attn_mask:
     k = linear(key, mod.kv_weight[:, :d], None if kv_b is None else kv_b[:, :d])
     v = linear(value, mod.kv_weight[:, d:], None if kv_b is None else kv_b[:, d:])
     heads_of = lambda t, tt: t.reshape(n * b, tt, heads, dh).transpose(1, 2)
-    o = F.scaled_dot_product_attention(heads_of(q, tq), heads_of(k, tk), heads_of(v, tk), attn_mask=attn_mask,
+    mask = None if attn_mask is None else attn_mask.to(query.device)    # as the kernel path (attention_core)
+    o = F.scaled_dot_product_attention(heads_of(q, tq), heads_of(k, tk), heads_of(v, tk), attn_mask=mask,
                                        dropout_p=dropout_p, is_causal=is_causal, scale=1.0 / math.sqrt(dh))
     return linear(o.transpose(1, 2).reshape(n, b, tq, d), mod.out_weight, mod.out_bias)
 
